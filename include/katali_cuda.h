@@ -1,0 +1,156 @@
+/* katali_cuda.h — C ABI of the B200 (sm_100a) katali_cuda plugin.
+ *
+ * libkatali_cuda.so is a drop-in for the reference's runtime-loaded CUDA plugin
+ * (katali_cuda.dll, loaded with LoadLibrary, README.md:11,313-320). The
+ * reference checkout has neither the plugin source nor this header
+ * (build-qwen3.bat:5 names the missing src/katali_cuda.c); the entry points in
+ * section 1 are reconstructed from their call sites in
+ * vendor/katali_gguf_dense/src/katali_dense_cuda.c (abbreviated KDC below),
+ * with the same names, argument order and meaning. Sections 2-5 are new.
+ *
+ * Conventions
+ *  - Every int-returning call returns KATALI_OK (0) or a KataliStatus code.
+ *    The plugin never falls back to the CPU; the caller decides (KDC:46-55).
+ *  - Pointers named *_dev / w / x / y / xq are DEVICE pointers unless the
+ *    comment says host. Weights stay in native GGUF block layout.
+ *  - Calls are not re-entrant (KDC:8-12 keeps plugin state in globals). They
+ *    run on the plugin stream (katali_cuda_set_stream). In the default
+ *    synchronous mode each compute call returns after the GPU finished, like
+ *    the reference's upload -> matvec -> download sequence; after
+ *    katali_cuda_set_async(1) compute calls only enqueue and katali_cuda_sync()
+ *    reports errors raised on the device (KATALI_ERR_TIMEOUT).
+ */
+#ifndef KATALI_CUDA_H
+#define KATALI_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum KataliStatus {
+    KATALI_OK = 0,                    /* success value tested at KDC:27-28,41,52-54 */
+    KATALI_ERR_NO_DEVICE = 1,         /* no driver / no sm_100 device */
+    KATALI_ERR_OOM = 2,
+    KATALI_ERR_BAD_ARG = 3,
+    KATALI_ERR_UNSUPPORTED_TYPE = 4,
+    KATALI_ERR_UNSUPPORTED_SHAPE = 5,
+    KATALI_ERR_TIMEOUT = 6,           /* a bounded device-side wait gave up */
+    KATALI_ERR_CUDA = 7,
+    KATALI_ERR_NCCL = 8
+} KataliStatus;
+
+/* GGUF tensor type ids used here (V/include/katali_gguf_dtype.h:20-41). */
+#define KATALI_TYPE_Q8_1 9u
+#define KATALI_TYPE_Q4_K 12u
+#define KATALI_TYPE_Q6_K 14u
+
+/* ------------------------------------------------------------------------ */
+/* 1. Entry points the reference already calls (KDC = katali_dense_cuda.c)    */
+/* ------------------------------------------------------------------------ */
+/* Nonzero when a usable sm_100 device and driver are present (KDC:19). */
+int katali_cuda_probe(void);
+/* Human-readable reason for the probe result; never NULL (KDC:19). */
+const char *katali_cuda_status(void);
+/* Device allocation owned by the caller (KDC:27-28,40). 256-byte aligned. */
+int katali_cuda_malloc(void **ptr, size_t bytes);
+/* Frees a katali_cuda_malloc pointer; NULL is a no-op (KDC:25-26,41,76-78). */
+int katali_cuda_free(void *ptr);
+/* Host -> device copy of `bytes` (KDC:41,52,65). Synchronous. */
+int katali_cuda_upload(void *dev, const void *host, size_t bytes);
+/* Device -> host copy of `bytes` (KDC:54,69). Synchronous. */
+int katali_cuda_download(void *host, const void *dev, size_t bytes);
+/* Nonzero when katali_cuda_matvec accepts this GGUF type (KDC:48,67). */
+int katali_cuda_supports_type(uint32_t ggml_type);
+/* y[rows] = W x with fp32 activations; W is a GGUF matrix, dims[0] = cols
+ * contiguous, dims[1] = rows (KDC:49-53). Q4_K and Q6_K. */
+int katali_cuda_matvec(uint32_t type, const void *w, uint64_t rows, uint64_t cols,
+                       const float *x, float *y);
+
+/* ------------------------------------------------------------------------ */
+/* 2. Streams, modes, errors                                                 */
+/* ------------------------------------------------------------------------ */
+/* Run subsequent work on `stream` (a cudaStream_t); NULL selects the plugin's
+ * own non-blocking stream. */
+int katali_cuda_set_stream(void *stream);
+/* 0 (default): compute calls synchronise before returning. 1: enqueue only. */
+int katali_cuda_set_async(int on);
+/* Wait for the plugin stream; returns and clears any device-side error. */
+int katali_cuda_sync(void);
+/* Name of a status code. */
+const char *katali_cuda_strerror(int status);
+
+/* ------------------------------------------------------------------------ */
+/* 3. Dense GEMV family                                                      */
+/* ------------------------------------------------------------------------ */
+/* n (<= 8) projections sharing one x and cols, in ONE launch; replaces the
+ * per-projection loop of katali_dense_cuda_matvec_multi (KDC:58-73) and mirrors
+ * the CPU katali_ggml_matvec_fused (V/src/gguf_dtype.c:925-985). */
+int katali_cuda_matvec_multi(int n, const uint32_t *types, const void *const *w,
+                             const uint64_t *rows, uint64_t cols, const float *x,
+                             float *const *y);
+/* Quantise n fp32 values (n % 32 == 0) to GGUF q8_1 blocks (36 B per 32). */
+int katali_cuda_quantize_q8_1(const float *x, uint64_t n, void *xq);
+/* y = W xq with q8_1 activations (the DP4A path, README.md:17). */
+int katali_cuda_matvec_q8_1(uint32_t type, const void *w, uint64_t rows, uint64_t cols,
+                            const void *xq, float *y);
+/* Encode rows x cols fp32 (device) into GGUF blocks of `type` (Q4_K, Q6_K,
+ * Q8_1) at dst. Byte-identical to the CPU encoder of the test oracle. */
+int katali_cuda_quantize_rows(uint32_t type, const float *src, uint64_t rows,
+                              uint64_t cols, void *dst);
+
+/* ------------------------------------------------------------------------ */
+/* 4. Fused MoE layer ("one GPU call per MoE layer", README.md:13,17)         */
+/* ------------------------------------------------------------------------ */
+typedef struct KataliMoe KataliMoe;
+
+/* Activation modes. */
+#define KATALI_MOE_Q8_1 0u   /* x and h quantised to q8_1, integer block dots */
+#define KATALI_MOE_F32  1u   /* fp32 activations (parity with the CPU kernels) */
+/* Descriptor flags. */
+#define KATALI_MOE_NORM_TOPK 1u  /* renormalise the top-k softmax weights */
+
+typedef struct KataliMoeDesc {
+    uint32_t n_experts;   /* <= 1024 */
+    uint32_t hidden;      /* H: gate/up cols, down rows; multiple of 256 */
+    uint32_t ffn;         /* F: gate/up rows, down cols; multiple of 256 */
+    uint32_t top_k;       /* 1..16 */
+    uint32_t gate_type, up_type, down_type;  /* Q4_K, Q4_K, Q6_K */
+    uint32_t flags;       /* KATALI_MOE_NORM_TOPK */
+    /* HOST array of 3*n_experts device pointers: gate_e, up_e, down_e for each
+     * expert e (16-byte aligned). NULL leaves every expert unset. */
+    const void *const *experts;
+} KataliMoeDesc;
+
+int katali_cuda_moe_create(const KataliMoeDesc *desc, KataliMoe **out);
+/* Point expert e at resident device copies (used by the residency tier). */
+int katali_cuda_moe_set_expert(KataliMoe *m, uint32_t e, const void *gate,
+                               const void *up, const void *down);
+int katali_cuda_moe_destroy(KataliMoe *m);
+/* One token: y[H] = sum_k w_k * down_ek(silu(gate_ek x) * up_ek x), with
+ * (e_k, w_k) the top-k of softmax(router_logits[n_experts]). One launch. */
+int katali_cuda_moe_layer(KataliMoe *m, const float *x, const float *router_logits,
+                          float *y, uint32_t mode);
+/* Same with routing given: ids[top_k] (int32), w[top_k] (fp32). */
+int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *ids,
+                                 const float *w, float *y, uint32_t mode);
+
+/* ------------------------------------------------------------------------ */
+/* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
+/* ------------------------------------------------------------------------ */
+/* Integer in-block sums of every row against q8_1 xq. Q4_K: per 32-group
+ * isum and xsum (rows x cols/32 each); Q6_K: per 16-group isum
+ * (rows x cols/16), xsum may be NULL. */
+int katali_cuda_debug_row_isums(uint32_t type, const void *w, uint64_t rows,
+                                uint64_t cols, const void *xq, int32_t *isum,
+                                int32_t *xsum);
+/* The MoE kernel's routing decision for router_logits: ids/w of top_k. */
+int katali_cuda_debug_route(KataliMoe *m, const float *router_logits, int32_t *ids,
+                            float *w);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KATALI_CUDA_H */

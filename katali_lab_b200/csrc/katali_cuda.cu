@@ -1,0 +1,445 @@
+// katali_cuda.cu — the C ABI of libkatali_cuda.so (declared in include/katali_cuda.h).
+//
+// Host side of the plugin: device probe, allocation and copies, argument
+// checks, launch of the kernels in kq_gemv.cu / kq_moe.cu on the plugin stream,
+// and error reporting. No CPU fallback: a call that cannot run on the GPU
+// returns a status code and the caller decides (the reference's caller falls
+// back to its CPU kernels, vendor/katali_gguf_dense/src/gguf_model.c:500-504).
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "katali_cuda.h"
+#include "kq_launch.h"
+
+namespace {
+
+int g_probed = -1;
+char g_status[512] = "not probed";
+int g_dev = 0;
+int g_num_sms = 148;
+int g_max_smem = 0;
+cudaStream_t g_own_stream = nullptr;
+cudaStream_t g_stream = nullptr;
+int g_async = 0;
+uint32_t *g_status_host = nullptr;  // mapped pinned word the kernels set on a device-side timeout
+uint32_t *g_status_dev = nullptr;
+
+int probe_impl() {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        snprintf(g_status, sizeof g_status, "CUDA unavailable: %s", cudaGetErrorString(e));
+        return 0;
+    }
+    if (n <= 0) {
+        snprintf(g_status, sizeof g_status, "no CUDA device");
+        return 0;
+    }
+    cudaGetDevice(&g_dev);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, g_dev) != cudaSuccess) {
+        snprintf(g_status, sizeof g_status, "cannot query device %d", g_dev);
+        return 0;
+    }
+    if (prop.major != 10 || prop.minor != 0) {
+        snprintf(g_status, sizeof g_status,
+                 "device %d (%s) is sm_%d%d; this plugin is built for sm_100a (B200)", g_dev,
+                 prop.name, prop.major, prop.minor);
+        return 0;
+    }
+    g_num_sms = prop.multiProcessorCount;
+    g_max_smem = (int)prop.sharedMemPerBlockOptin;
+    snprintf(g_status, sizeof g_status, "ok: device %d %s sm_%d%d, %d SMs, %.1f GiB", g_dev,
+             prop.name, prop.major, prop.minor, prop.multiProcessorCount,
+             prop.totalGlobalMem / 1073741824.0);
+    return 1;
+}
+
+int ensure() {
+    if (g_probed < 0) g_probed = probe_impl();
+    if (!g_probed) return KATALI_ERR_NO_DEVICE;
+    if (!g_own_stream) {
+        if (cudaStreamCreateWithFlags(&g_own_stream, cudaStreamNonBlocking) != cudaSuccess)
+            return KATALI_ERR_CUDA;
+        if (!g_stream) g_stream = g_own_stream;
+    }
+    if (!g_status_host) {
+        if (cudaHostAlloc((void **)&g_status_host, sizeof(uint32_t), cudaHostAllocMapped) !=
+            cudaSuccess)
+            return KATALI_ERR_CUDA;
+        *g_status_host = 0;
+        if (cudaHostGetDevicePointer((void **)&g_status_dev, g_status_host, 0) != cudaSuccess)
+            return KATALI_ERR_CUDA;
+    }
+    return KATALI_OK;
+}
+
+int cuda_fail(cudaError_t e) {
+    snprintf(g_status, sizeof g_status, "CUDA error: %s", cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
+}
+
+int take_device_status() {
+    const uint32_t s = *(volatile uint32_t *)g_status_host;
+    if (s) {
+        *(volatile uint32_t *)g_status_host = 0;
+        snprintf(g_status, sizeof g_status, "device-side wait timed out (bits 0x%x)", s);
+        return KATALI_ERR_TIMEOUT;
+    }
+    return KATALI_OK;
+}
+
+// After a launch: in synchronous mode wait for the stream and report errors.
+int finish(cudaError_t e) {
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (g_async) return KATALI_OK;
+    e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return take_device_status();
+}
+
+bool aligned16(const void *p) { return p && ((uintptr_t)p & 15u) == 0; }
+
+uint64_t row_bytes(uint32_t type, uint64_t cols) {
+    switch (type) {
+        case KATALI_TYPE_Q4_K: return cols % 256 ? 0 : cols / 256 * 144;
+        case KATALI_TYPE_Q6_K: return cols % 256 ? 0 : cols / 256 * 210;
+        case KATALI_TYPE_Q8_1: return cols % 32 ? 0 : cols / 32 * 36;
+        default: return 0;
+    }
+}
+
+bool gemv_type(uint32_t t) { return t == KATALI_TYPE_Q4_K || t == KATALI_TYPE_Q6_K; }
+
+// fp32-activation GEMV by default, as the reference's dense path; the q8_1
+// (DP4A) path when KATALI_CUDA_DP4A=1 (the reference's switch, README.md:17).
+int dense_mode() {
+    const char *e = getenv("KATALI_CUDA_DP4A");
+    return (e && (e[0] == '1' || e[0] == 'y' || e[0] == 'Y')) ? 0 : 2;
+}
+
+int max_cols_for_smem(int mode) {
+    // activations staged per CTA next to the weight ring (~100 KB)
+    return mode == 2 ? 24576 : 65536;
+}
+
+}  // namespace
+
+struct KataliMoe {
+    kq::MoeParams plan[2];  // per activation mode
+    int plan_ok[2];
+    std::vector<const uint8_t *> table;  // host copy of the device pointer table
+    const uint8_t **d_table;
+    float *hbuf;
+    uint32_t *sync;
+    int32_t *dbg_ids;
+    float *dbg_w;
+    int grid;
+};
+
+extern "C" {
+
+int katali_cuda_probe(void) {
+    if (g_probed < 0) g_probed = probe_impl();
+    return g_probed;
+}
+
+const char *katali_cuda_status(void) {
+    if (g_probed < 0) g_probed = probe_impl();
+    return g_status;
+}
+
+const char *katali_cuda_strerror(int s) {
+    switch (s) {
+        case KATALI_OK: return "ok";
+        case KATALI_ERR_NO_DEVICE: return "no usable sm_100 device";
+        case KATALI_ERR_OOM: return "out of device memory";
+        case KATALI_ERR_BAD_ARG: return "bad argument";
+        case KATALI_ERR_UNSUPPORTED_TYPE: return "unsupported tensor type";
+        case KATALI_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+        case KATALI_ERR_TIMEOUT: return "device-side wait timed out";
+        case KATALI_ERR_CUDA: return "CUDA error";
+        case KATALI_ERR_NCCL: return "NCCL error";
+        default: return "unknown status";
+    }
+}
+
+int katali_cuda_malloc(void **ptr, size_t bytes) {
+    if (!ptr) return KATALI_ERR_BAD_ARG;
+    *ptr = nullptr;
+    int s = ensure();
+    if (s) return s;
+    cudaError_t e = cudaMalloc(ptr, bytes ? bytes : 1);
+    if (e != cudaSuccess) {
+        *ptr = nullptr;
+        return cuda_fail(e);
+    }
+    return KATALI_OK;
+}
+
+int katali_cuda_free(void *ptr) {
+    if (!ptr) return KATALI_OK;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? KATALI_OK : cuda_fail(e);
+}
+
+int katali_cuda_upload(void *dev, const void *host, size_t bytes) {
+    if ((!dev || !host) && bytes) return KATALI_ERR_BAD_ARG;
+    int s = ensure();
+    if (s) return s;
+    cudaError_t e = cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, g_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
+    return e == cudaSuccess ? KATALI_OK : cuda_fail(e);
+}
+
+int katali_cuda_download(void *host, const void *dev, size_t bytes) {
+    if ((!dev || !host) && bytes) return KATALI_ERR_BAD_ARG;
+    int s = ensure();
+    if (s) return s;
+    cudaError_t e = cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, g_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return take_device_status();
+}
+
+int katali_cuda_supports_type(uint32_t type) { return gemv_type(type) ? 1 : 0; }
+
+int katali_cuda_set_stream(void *stream) {
+    int s = ensure();
+    if (s) return s;
+    g_stream = stream ? (cudaStream_t)stream : g_own_stream;
+    return KATALI_OK;
+}
+
+int katali_cuda_set_async(int on) {
+    g_async = on ? 1 : 0;
+    return KATALI_OK;
+}
+
+int katali_cuda_sync(void) {
+    int s = ensure();
+    if (s) return s;
+    cudaError_t e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return take_device_status();
+}
+
+static int matvec_common(int n, const uint32_t *types, const void *const *w, const uint64_t *rows,
+                         uint64_t cols, const float *x, const uint8_t *xq, float *const *y,
+                         int mode) {
+    if (n <= 0 || n > 8 || !types || !w || !rows || !y) return KATALI_ERR_BAD_ARG;
+    if (mode == 1 ? !xq : !aligned16(x)) return KATALI_ERR_BAD_ARG;
+    if (cols == 0 || cols % 256 || cols > (uint64_t)max_cols_for_smem(mode))
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    int s = ensure();
+    if (s) return s;
+    kq::GemvParams p = {};
+    p.njobs = n;
+    p.cols = (uint32_t)cols;
+    p.x = x;
+    p.xq = xq;
+    p.status = g_status_dev;
+    for (int j = 0; j < n; ++j) {
+        if (!gemv_type(types[j])) return KATALI_ERR_UNSUPPORTED_TYPE;
+        if (!aligned16(w[j]) || !y[j] || rows[j] == 0 || rows[j] > 0xFFFFFFFFull)
+            return KATALI_ERR_BAD_ARG;
+        p.job[j].w = (const uint8_t *)w[j];
+        p.job[j].y = y[j];
+        p.job[j].rows = rows[j];
+        p.job[j].type = types[j];
+        p.job[j].rb = (uint32_t)row_bytes(types[j], cols);
+    }
+    return finish(kq::launch_gemv(p, mode, g_stream));
+}
+
+int katali_cuda_matvec(uint32_t type, const void *w, uint64_t rows, uint64_t cols, const float *x,
+                       float *y) {
+    if (!gemv_type(type)) return KATALI_ERR_UNSUPPORTED_TYPE;
+    if (!x) return KATALI_ERR_BAD_ARG;
+    const void *wl[1] = {w};
+    float *yl[1] = {y};
+    return matvec_common(1, &type, wl, &rows, cols, x, nullptr, yl, dense_mode());
+}
+
+int katali_cuda_matvec_multi(int n, const uint32_t *types, const void *const *w,
+                             const uint64_t *rows, uint64_t cols, const float *x, float *const *y) {
+    if (!x) return KATALI_ERR_BAD_ARG;
+    return matvec_common(n, types, w, rows, cols, x, nullptr, y, dense_mode());
+}
+
+int katali_cuda_matvec_q8_1(uint32_t type, const void *w, uint64_t rows, uint64_t cols,
+                            const void *xq, float *y) {
+    if (!gemv_type(type)) return KATALI_ERR_UNSUPPORTED_TYPE;
+    const void *wl[1] = {w};
+    float *yl[1] = {y};
+    return matvec_common(1, &type, wl, &rows, cols, nullptr, (const uint8_t *)xq, yl, 1);
+}
+
+int katali_cuda_quantize_q8_1(const float *x, uint64_t n, void *xq) {
+    if (!x || !xq || n == 0 || n % 32) return KATALI_ERR_BAD_ARG;
+    int s = ensure();
+    if (s) return s;
+    return finish(kq::launch_quantize_q8_1(x, n, xq, g_stream));
+}
+
+int katali_cuda_quantize_rows(uint32_t type, const float *src, uint64_t rows, uint64_t cols,
+                              void *dst) {
+    if (type != KATALI_TYPE_Q4_K && type != KATALI_TYPE_Q6_K && type != KATALI_TYPE_Q8_1)
+        return KATALI_ERR_UNSUPPORTED_TYPE;
+    if (!src || !dst || rows == 0 || row_bytes(type, cols) == 0) return KATALI_ERR_BAD_ARG;
+    int s = ensure();
+    if (s) return s;
+    return finish(kq::launch_encode(type, src, rows * cols, dst, g_stream));
+}
+
+int katali_cuda_debug_row_isums(uint32_t type, const void *w, uint64_t rows, uint64_t cols,
+                                const void *xq, int32_t *isum, int32_t *xsum) {
+    if (!gemv_type(type)) return KATALI_ERR_UNSUPPORTED_TYPE;
+    if (!w || !xq || !isum || rows == 0 || cols == 0 || cols % 256) return KATALI_ERR_BAD_ARG;
+    if (type == KATALI_TYPE_Q4_K && !xsum) return KATALI_ERR_BAD_ARG;
+    int s = ensure();
+    if (s) return s;
+    return finish(kq::launch_row_isums(type, w, rows, cols, (uint32_t)row_bytes(type, cols), xq,
+                                       isum, xsum, g_stream));
+}
+
+// ---------------------------------------------------------------------------
+// MoE
+// ---------------------------------------------------------------------------
+int katali_cuda_moe_create(const KataliMoeDesc *d, KataliMoe **out) {
+    if (!d || !out) return KATALI_ERR_BAD_ARG;
+    *out = nullptr;
+    if (d->n_experts == 0 || d->n_experts > 1024 || d->top_k == 0 || d->top_k > kq::MOE_MAX_K ||
+        d->top_k > d->n_experts)
+        return KATALI_ERR_BAD_ARG;
+    if (!gemv_type(d->gate_type) || !gemv_type(d->up_type) || !gemv_type(d->down_type))
+        return KATALI_ERR_UNSUPPORTED_TYPE;
+    const uint64_t rbg = row_bytes(d->gate_type, d->hidden), rbu = row_bytes(d->up_type, d->hidden);
+    const uint64_t rbd = row_bytes(d->down_type, d->ffn);
+    if (!rbg || !rbu || !rbd || rbg % 16 || rbu % 16)
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    int s = ensure();
+    if (s) return s;
+    KataliMoe *m = new KataliMoe();
+    m->grid = g_num_sms;
+    for (int mode = 0; mode < 2; ++mode) {
+        kq::MoeParams &p = m->plan[mode];
+        p = kq::MoeParams{};
+        p.n_experts = (int)d->n_experts;
+        p.H = (int)d->hidden;
+        p.F = (int)d->ffn;
+        p.K = (int)d->top_k;
+        p.norm = (d->flags & KATALI_MOE_NORM_TOPK) ? 1 : 0;
+        p.mode = mode;
+        p.gate_type = d->gate_type;
+        p.up_type = d->up_type;
+        p.down_type = d->down_type;
+        p.rbg = (uint32_t)rbg;
+        p.rbu = (uint32_t)rbu;
+        p.rbd = (uint32_t)rbd;
+        m->plan_ok[mode] = kq::moe_plan(p, m->grid, g_max_smem) == 0;
+    }
+    m->table.assign(3 * (size_t)d->n_experts, nullptr);
+    if (d->experts) {
+        for (size_t i = 0; i < m->table.size(); ++i) {
+            if (d->experts[i] && !aligned16(d->experts[i])) {
+                delete m;
+                return KATALI_ERR_BAD_ARG;
+            }
+            m->table[i] = (const uint8_t *)d->experts[i];
+        }
+    }
+    cudaError_t e = cudaMalloc((void **)&m->d_table, m->table.size() * sizeof(void *));
+    if (e == cudaSuccess) e = cudaMalloc((void **)&m->hbuf, sizeof(float) * d->top_k * d->ffn);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&m->sync, 16);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&m->dbg_ids, 4 * kq::MOE_MAX_K);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&m->dbg_w, 4 * kq::MOE_MAX_K);
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->sync, 0, 16, g_stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->d_table, m->table.data(), m->table.size() * sizeof(void *),
+                            cudaMemcpyHostToDevice, g_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) {
+        katali_cuda_moe_destroy(m);
+        return cuda_fail(e);
+    }
+    *out = m;
+    return KATALI_OK;
+}
+
+int katali_cuda_moe_set_expert(KataliMoe *m, uint32_t e, const void *gate, const void *up,
+                               const void *down) {
+    if (!m || e >= m->table.size() / 3) return KATALI_ERR_BAD_ARG;
+    if (!aligned16(gate) || !aligned16(up) || !aligned16(down)) return KATALI_ERR_BAD_ARG;
+    m->table[3 * e] = (const uint8_t *)gate;
+    m->table[3 * e + 1] = (const uint8_t *)up;
+    m->table[3 * e + 2] = (const uint8_t *)down;
+    // Stream-ordered: calls already enqueued keep the pointers they were launched with.
+    cudaError_t err = cudaMemcpyAsync(m->d_table + 3 * e, &m->table[3 * e], 3 * sizeof(void *),
+                                      cudaMemcpyHostToDevice, g_stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(g_stream);
+    return err == cudaSuccess ? KATALI_OK : cuda_fail(err);
+}
+
+int katali_cuda_moe_destroy(KataliMoe *m) {
+    if (!m) return KATALI_OK;
+    if (g_stream) cudaStreamSynchronize(g_stream);
+    cudaFree(m->d_table);
+    cudaFree(m->hbuf);
+    cudaFree(m->sync);
+    cudaFree(m->dbg_ids);
+    cudaFree(m->dbg_w);
+    delete m;
+    return KATALI_OK;
+}
+
+static int moe_run(KataliMoe *m, const float *x, const float *logits, const int32_t *ids,
+                   const float *w, float *y, uint32_t mode, int route_only) {
+    if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
+    if (!m->plan_ok[mode]) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    for (const uint8_t *t : m->table)
+        if (!t) return KATALI_ERR_BAD_ARG;  // every expert must be resident
+    kq::MoeParams p = m->plan[mode];
+    p.experts = m->d_table;
+    p.x = x;
+    p.logits = logits;
+    p.ids = ids;
+    p.w = w;
+    p.y = y;
+    p.hbuf = m->hbuf;
+    p.sync = m->sync;
+    p.status = g_status_dev;
+    p.dbg_ids = m->dbg_ids;
+    p.dbg_w = m->dbg_w;
+    p.route_only = route_only;
+    return finish(kq::launch_moe(p, route_only ? 1 : m->grid, g_stream));
+}
+
+int katali_cuda_moe_layer(KataliMoe *m, const float *x, const float *router_logits, float *y,
+                          uint32_t mode) {
+    if (!aligned16(x) || !router_logits || !y) return KATALI_ERR_BAD_ARG;
+    return moe_run(m, x, router_logits, nullptr, nullptr, y, mode, 0);
+}
+
+int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *ids, const float *w,
+                                 float *y, uint32_t mode) {
+    if (!aligned16(x) || !ids || !w || !y) return KATALI_ERR_BAD_ARG;
+    return moe_run(m, x, nullptr, ids, w, y, mode, 0);
+}
+
+int katali_cuda_debug_route(KataliMoe *m, const float *router_logits, int32_t *ids, float *w) {
+    if (!m || !router_logits || !ids || !w) return KATALI_ERR_BAD_ARG;
+    int s = moe_run(m, nullptr, router_logits, nullptr, nullptr, nullptr,
+                    0, 1);
+    if (s) return s;
+    const int K = m->plan[0].K;
+    cudaError_t e = cudaMemcpyAsync(ids, m->dbg_ids, 4 * K, cudaMemcpyDeviceToDevice, g_stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w, m->dbg_w, 4 * K, cudaMemcpyDeviceToDevice, g_stream);
+    return finish(e);
+}
+
+}  // extern "C"

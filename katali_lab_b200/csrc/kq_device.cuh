@@ -1,0 +1,384 @@
+// kq_device.cuh — device building blocks of the katali_cuda plugin (sm_100a).
+//
+// GGUF block layouts (vendor/katali_gguf_dense/src/gguf_dtype.c, V/ below):
+//   Q4_K 144 B / 256 w: d f16 @0, dmin f16 @2, 12 B packed 6-bit scales/mins @4,
+//        128 B nibbles @16; 64-element chunk c: low nibbles of bytes 32c..32c+31
+//        are elements 64c..64c+31, high nibbles 64c+32..64c+63 (V:429-452,350-358)
+//   Q6_K 210 B / 256 w: ql[128] @0, qh[64] @128, 16 int8 scales @192, d f16 @208;
+//        element e = 128h + 32*quarter + l takes ql[64h + 32(quarter&1) + l]
+//        (low nibble for quarter<2, high otherwise) and bits 2*quarter of
+//        qh[32h + l]; value d * sc[e/16] * (q - 32) (V:487-512)
+//   q8_1  36 B / 32:  d f16 @0, s f16 @2, 32 int8 @4 (V:328-335)
+//
+// Exactness contract shared with the CPU restatement (oracle/kq_oracle.c):
+// integer block sums are exact; each per-q8-block float term is a product of
+// values exact in double, rounded once; terms are summed in double and each
+// row rounds once to float. kq_expf and the encoders use only IEEE-rounded
+// single operations (explicit __f*_rn intrinsics, so nvcc cannot contract
+// them), which makes routing weights, silu(g)*u and the q8_1 bytes
+// bit-identical to the CPU restatement.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define KQ_FULL 0xFFFFFFFFu
+
+namespace kq {
+
+constexpr int Q4K_BYTES = 144;
+constexpr int Q6K_BYTES = 210;
+constexpr int Q81_BYTES = 36;
+constexpr uint32_t T_Q8_1 = 9, T_Q4_K = 12, T_Q6_K = 14;
+
+// Bounded waits: iterations of a poll loop with a short sleep. ~2^24 polls of
+// >= 64 ns each is well above a second; a wait that runs out sets a status bit
+// and returns instead of hanging the GPU.
+constexpr uint32_t SPIN_LIMIT = 1u << 24;
+constexpr uint32_t ERR_TIMEOUT_TMA = 1u;
+constexpr uint32_t ERR_TIMEOUT_GRID = 2u;
+
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFFu)));
+}
+__device__ __forceinline__ uint16_t f2h(float f) {
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+// e^x: Cody-Waite reduction by ln2 (hi/lo split) and a degree-7 Taylor
+// polynomial for e^r, |r| <= 0.35. Same operations, in the same order, as
+// kqo_expf in the CPU restatement.
+__device__ __forceinline__ float kq_expf(float x) {
+    if (x != x) return x;
+    x = fminf(fmaxf(x, -87.0f), 88.0f);
+    const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+    float r = __fmaf_rn(-n, 0.693145751953125f, x);
+    r = __fmaf_rn(-n, 1.42860682030941723e-6f, r);
+    float p = 1.98412698412698413e-4f;
+    p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
+    p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
+    p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
+    p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const float s = __uint_as_float((uint32_t)((int)n + 127) << 23);
+    return __fmul_rn(p, s);
+}
+
+__device__ __forceinline__ float kq_silu(float x) {
+    return __fdiv_rn(x, __fadd_rn(1.0f, kq_expf(-x)));
+}
+
+// Total order for top-k: NaN lowest, -0 == +0, then by value.
+__device__ __forceinline__ uint32_t order_key(float f) {
+    if (f != f) return 0u;
+    const uint32_t u = __float_as_uint(__fadd_rn(f, 0.0f));
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(KQ_FULL, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(KQ_FULL, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk (TMA, non-tensor) copies, no multicast.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on phase `parity`; returns false (and the caller records a
+// timeout) when the limit runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (it > 64) __nanosleep(64);
+    }
+    return false;
+}
+// Global -> shared bulk copy completing on `bar`. dst/src 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+        "[%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Loads
+// ---------------------------------------------------------------------------
+// 16 bytes at a 2-byte aligned address: five aligned words, funnel-shifted.
+// Reads at most 2 bytes before and 2 after the range; callers keep that inside
+// the weight block (every Q6_K sub-range used here is).
+__device__ __forceinline__ void load16_a2(const uint8_t *p, uint32_t out[4]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+    out[0] = __funnelshift_r(w0, w1, sh);
+    out[1] = __funnelshift_r(w1, w2, sh);
+    out[2] = __funnelshift_r(w2, w3, sh);
+    out[3] = __funnelshift_r(w3, w4, sh);
+}
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t *p) {
+    return *reinterpret_cast<const uint16_t *>(p);
+}
+
+// Q4_K sub-scale and sub-min for groups 2c and 2c+1 from the 16-byte block
+// header (h.y = scale bytes 0..3, h.z = 4..7, h.w = 8..11).
+__device__ __forceinline__ void q4k_scales(const uint4 &h, int c, int &sc0, int &m0, int &sc1,
+                                           int &m1) {
+    const int j0 = 2 * c, j1 = 2 * c + 1;
+    auto byte = [](uint32_t w, int i) { return (int)((w >> (8 * i)) & 0xFFu); };
+    if (j0 < 4) {  // c = 0, 1: both groups < 4
+        sc0 = byte(h.y, j0) & 63;
+        m0 = byte(h.z, j0) & 63;
+        sc1 = byte(h.y, j1) & 63;
+        m1 = byte(h.z, j1) & 63;
+    } else {  // c = 2, 3: both groups >= 4
+        sc0 = (byte(h.w, j0 - 4) & 0x0F) | ((byte(h.y, j0 - 4) >> 6) << 4);
+        m0 = (byte(h.w, j0 - 4) >> 4) | ((byte(h.z, j0 - 4) >> 6) << 4);
+        sc1 = (byte(h.w, j1 - 4) & 0x0F) | ((byte(h.y, j1 - 4) >> 6) << 4);
+        m1 = (byte(h.w, j1 - 4) >> 4) | ((byte(h.z, j1 - 4) >> 6) << 4);
+    }
+}
+
+// Activations staged in shared memory in a split q8_1 layout: int8 values
+// contiguous (16-byte aligned), the fp16 scale of each 32-block widened to
+// float, the exact integer sum of each 32-block and of each 16-half.
+struct ActQ8 {
+    const int8_t *q;
+    const float *d;
+    const int *s32;
+    const int *s16;
+};
+
+// ---------------------------------------------------------------------------
+// Row dots, one warp per row. Each returns this lane's double partial; the
+// caller reduces across the warp (warp_sum_d) and rounds once to float.
+// ---------------------------------------------------------------------------
+// Q4_K x q8_1. Lane = (block b = lane/4 + 8i, 64-element chunk c = lane%4).
+__device__ __forceinline__ double q4k_q8_partial(const uint8_t *row, int nb, const ActQ8 &a,
+                                                 int lane) {
+    double acc = 0.0;
+    const int c = lane & 3;
+    for (int b = lane >> 2; b < nb; b += 8) {
+        const uint8_t *blk = row + Q4K_BYTES * b;
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+        const int g = 8 * b + 2 * c;
+        const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + 32 * g);
+        const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+        const uint32_t M = 0x0F0F0F0Fu;
+        int lo = 0, hi = 0;
+        lo = __dp4a((int)(w0.x & M), (int)a0.x, lo);
+        hi = __dp4a((int)((w0.x >> 4) & M), (int)a2.x, hi);
+        lo = __dp4a((int)(w0.y & M), (int)a0.y, lo);
+        hi = __dp4a((int)((w0.y >> 4) & M), (int)a2.y, hi);
+        lo = __dp4a((int)(w0.z & M), (int)a0.z, lo);
+        hi = __dp4a((int)((w0.z >> 4) & M), (int)a2.z, hi);
+        lo = __dp4a((int)(w0.w & M), (int)a0.w, lo);
+        hi = __dp4a((int)((w0.w >> 4) & M), (int)a2.w, hi);
+        lo = __dp4a((int)(w1.x & M), (int)a1.x, lo);
+        hi = __dp4a((int)((w1.x >> 4) & M), (int)a3.x, hi);
+        lo = __dp4a((int)(w1.y & M), (int)a1.y, lo);
+        hi = __dp4a((int)((w1.y >> 4) & M), (int)a3.y, hi);
+        lo = __dp4a((int)(w1.z & M), (int)a1.z, lo);
+        hi = __dp4a((int)((w1.z >> 4) & M), (int)a3.z, hi);
+        lo = __dp4a((int)(w1.w & M), (int)a1.w, lo);
+        hi = __dp4a((int)((w1.w >> 4) & M), (int)a3.w, hi);
+        int sc0, m0, sc1, m1;
+        q4k_scales(h, c, sc0, m0, sc1, m1);
+        const double d = (double)h2f(h.x), dmin = (double)h2f(h.x >> 16);
+        const double dx0 = (double)a.d[g], dx1 = (double)a.d[g + 1];
+        acc += (d * dx0) * (double)(sc0 * lo) - (dmin * dx0) * (double)(m0 * a.s32[g]);
+        acc += (d * dx1) * (double)(sc1 * hi) - (dmin * dx1) * (double)(m1 * a.s32[g + 1]);
+    }
+    return acc;
+}
+
+// Q6_K x q8_1. Lane = (block b = lane/16 + 2i, 16-element group k = lane%16);
+// lanes k and k^1 share one q8_1 block and combine their scaled sums exactly.
+__device__ __forceinline__ double q6k_q8_partial(const uint8_t *row, int nb, const ActQ8 &a,
+                                                 int lane) {
+    double acc = 0.0;
+    const int k = lane & 15, h = k >> 3, kk = k & 7, qq = kk >> 1, sub = kk & 1;
+    const int nit = (nb + 1) >> 1;
+    for (int it = 0; it < nit; ++it) {
+        const int b = (lane >> 4) + 2 * it;
+        int I = 0;
+        double dd = 0.0;
+        if (b < nb) {
+            const uint8_t *blk = row + Q6K_BYTES * b;
+            uint32_t ql[4], qh[4];
+            load16_a2(blk + 64 * h + 32 * (qq & 1) + 16 * sub, ql);
+            load16_a2(blk + 128 + 32 * h + 16 * sub, qh);
+            const int sc = (int)(int8_t)blk[192 + k];
+            const uint4 av = *reinterpret_cast<const uint4 *>(a.q + 256 * b + 16 * k);
+            const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+            const int lsh = (qq >= 2) ? 4 : 0, hsh = 2 * qq;
+            int s = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t v = ((ql[i] >> lsh) & 0x0F0F0F0Fu) |
+                                   (((qh[i] >> hsh) & 0x03030303u) << 4);
+                s = __dp4a((int)v, (int)aw[i], s);
+            }
+            I = sc * (s - 32 * a.s16[16 * b + k]);
+            dd = (double)h2f(ld_u16(blk + 208)) * (double)a.d[8 * b + (k >> 1)];
+        }
+        I += __shfl_xor_sync(KQ_FULL, I, 1);
+        if (b < nb && !(k & 1)) acc += dd * (double)I;
+    }
+    return acc;
+}
+
+// Q4_K x fp32 activations x (shared), with per-32-group sums xs.
+__device__ __forceinline__ double q4k_f32_partial(const uint8_t *row, int nb, const float *x,
+                                                  const float *xs, int lane) {
+    double acc = 0.0;
+    const int c = lane & 3;
+    for (int b = lane >> 2; b < nb; b += 8) {
+        const uint8_t *blk = row + Q4K_BYTES * b;
+        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+        const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float *xl = x + 256 * b + 64 * c;
+        float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 xa = *reinterpret_cast<const float4 *>(xl + 4 * i);
+            const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 + 4 * i);
+            const uint32_t w = ww[i];
+            lo = fmaf((float)(w & 15u), xa.x, lo);
+            hi = fmaf((float)((w >> 4) & 15u), xb.x, hi);
+            lo = fmaf((float)((w >> 8) & 15u), xa.y, lo);
+            hi = fmaf((float)((w >> 12) & 15u), xb.y, hi);
+            lo = fmaf((float)((w >> 16) & 15u), xa.z, lo);
+            hi = fmaf((float)((w >> 20) & 15u), xb.z, hi);
+            lo = fmaf((float)((w >> 24) & 15u), xa.w, lo);
+            hi = fmaf((float)(w >> 28), xb.w, hi);
+        }
+        int sc0, m0, sc1, m1;
+        q4k_scales(h, c, sc0, m0, sc1, m1);
+        const float d = h2f(h.x), dmin = h2f(h.x >> 16);
+        const int g = 8 * b + 2 * c;
+        acc += (double)(d * (float)sc0) * (double)lo - (double)(dmin * (float)m0) * (double)xs[g];
+        acc += (double)(d * (float)sc1) * (double)hi -
+               (double)(dmin * (float)m1) * (double)xs[g + 1];
+    }
+    return acc;
+}
+
+// Q6_K x fp32 activations x (shared).
+__device__ __forceinline__ double q6k_f32_partial(const uint8_t *row, int nb, const float *x,
+                                                  int lane) {
+    double acc = 0.0;
+    const int k = lane & 15, h = k >> 3, kk = k & 7, qq = kk >> 1, sub = kk & 1;
+    for (int b = lane >> 4; b < nb; b += 2) {
+        const uint8_t *blk = row + Q6K_BYTES * b;
+        uint32_t ql[4], qh[4];
+        load16_a2(blk + 64 * h + 32 * (qq & 1) + 16 * sub, ql);
+        load16_a2(blk + 128 + 32 * h + 16 * sub, qh);
+        const int sc = (int)(int8_t)blk[192 + k];
+        const float d = h2f(ld_u16(blk + 208));
+        const float *xp = x + 256 * b + 16 * k;
+        const int lsh = (qq >= 2) ? 4 : 0, hsh = 2 * qq;
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xp + 4 * i);
+            const uint32_t v =
+                ((ql[i] >> lsh) & 0x0F0F0F0Fu) | (((qh[i] >> hsh) & 0x03030303u) << 4);
+            s = fmaf((float)((int)(v & 63u) - 32), xv.x, s);
+            s = fmaf((float)((int)((v >> 8) & 63u) - 32), xv.y, s);
+            s = fmaf((float)((int)((v >> 16) & 63u) - 32), xv.z, s);
+            s = fmaf((float)((int)((v >> 24) & 63u) - 32), xv.w, s);
+        }
+        acc += (double)(d * (float)sc) * (double)s;
+    }
+    return acc;
+}
+
+// ---------------------------------------------------------------------------
+// q8_1 quantisation of one 32-element block by one warp (lane = element).
+// Writes the split shared layout; optionally the GGUF block at gblk.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void quant_block_q8(float v, int lane, int8_t *q, float *d_out,
+                                               int *s32_out, int *s16_out, uint8_t *gblk) {
+    const float av = fabsf(v);
+    const float amax = __uint_as_float(__reduce_max_sync(KQ_FULL, __float_as_uint(av)));
+    const float d = __fdiv_rn(amax, 127.0f);
+    int qi = 0;
+    if (amax != 0.0f) qi = max(-127, min(127, (int)roundf(__fdiv_rn(v, d))));
+    const int sum = __reduce_add_sync(KQ_FULL, qi);
+    const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+    q[lane] = (int8_t)qi;
+    const uint16_t dh = f2h(d);
+    if (lane == 0) {
+        *d_out = h2f(dh);
+        *s32_out = sum;
+        if (s16_out) {
+            s16_out[0] = sum_lo;
+            s16_out[1] = sum - sum_lo;
+        }
+    }
+    if (gblk) {
+        gblk[4 + lane] = (uint8_t)(int8_t)qi;
+        if (lane == 0) {
+            const uint16_t sh = f2h(__fmul_rn(d, (float)sum));
+            gblk[0] = (uint8_t)(dh & 0xFF);
+            gblk[1] = (uint8_t)(dh >> 8);
+            gblk[2] = (uint8_t)(sh & 0xFF);
+            gblk[3] = (uint8_t)(sh >> 8);
+        }
+    }
+}
+
+}  // namespace kq

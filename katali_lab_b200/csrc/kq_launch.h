@@ -1,0 +1,72 @@
+// kq_launch.h — kernel parameter blocks and host launchers (internal to the plugin).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kq {
+
+struct GemvJob {
+    const uint8_t *w;  // device matrix, native GGUF rows, 16-byte aligned
+    float *y;
+    uint64_t rows;
+    uint32_t type;
+    uint32_t rb;     // bytes per row
+    uint32_t tr;     // rows per tile (set by the launcher)
+    uint32_t tile0;  // first global tile of this job (set by the launcher)
+};
+
+struct GemvParams {
+    GemvJob job[8];
+    int njobs;
+    uint32_t total_tiles;
+    uint32_t cols;
+    uint32_t stage_bytes;
+    int nstages;
+    uint32_t act_off;
+    int use_tma;
+    const float *x;     // fp32 activations (modes 0 and 2)
+    const uint8_t *xq;  // q8_1 blocks (mode 1)
+    volatile uint32_t *status;
+};
+
+// mode 0: q8_1 activations quantised in-kernel from fp32 x; 1: from q8_1 blocks;
+// 2: fp32 activations.
+cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st);
+cudaError_t launch_quantize_q8_1(const float *x, uint64_t n, void *out, cudaStream_t st);
+cudaError_t launch_encode(uint32_t type, const float *x, uint64_t n, void *out, cudaStream_t st);
+cudaError_t launch_row_isums(uint32_t type, const void *w, uint64_t rows, uint64_t cols,
+                             uint32_t rb, const void *xq, int32_t *isum, int32_t *xsum,
+                             cudaStream_t st);
+
+constexpr int MOE_MAX_K = 16;
+constexpr int MOE_MAX_CHUNKS = 64;
+
+struct MoeParams {
+    const uint8_t *const *experts;  // device table: gate_e, up_e, down_e per expert
+    const float *x;
+    const float *logits;   // router logits (NULL when ids/w are given)
+    const int32_t *ids;    // routed variant
+    const float *w;
+    float *y;
+    float *hbuf;           // scratch: top_k * ffn floats
+    uint32_t *sync;        // scratch: grid-barrier arrive / done counters (zero between calls)
+    volatile uint32_t *status;
+    int32_t *dbg_ids;      // optional: routing decision (written by CTA 0)
+    float *dbg_w;
+    int n_experts, H, F, K, norm, mode;
+    uint32_t gate_type, up_type, down_type;
+    uint32_t rbg, rbu, rbd;
+    uint32_t rg;           // phase-B rows per aligned group (set by moe_plan)
+    int route_only;        // 1: routing decision only (check entry point)
+    // shared-memory plan (bytes), identical for every CTA
+    uint32_t chunk_units;  // max row pairs per phase-A chunk
+    uint32_t sa_bytes;     // phase-A staging capacity
+    uint32_t sb_off, sb_bytes;
+    uint32_t act_off, hact_off, misc_off, smem_bytes;
+};
+
+cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
+int moe_plan(MoeParams &p, int grid, int max_smem);
+
+}  // namespace kq

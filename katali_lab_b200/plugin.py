@@ -1,0 +1,182 @@
+"""ctypes binding of libkatali_cuda.so for tests and the benchmark.
+
+Every call goes through the plugin's C ABI (include/katali_cuda.h) exactly as
+the reference engine's C code calls katali_cuda.dll. Device buffers are torch
+CUDA tensors (torch is only used for device memory and streams here); the
+binding passes their raw pointers. A missing library raises: there is no CPU
+fallback in this package.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+from . import build as _build
+
+Q8_1, Q4_K, Q6_K = 9, 12, 14
+MOE_Q8_1, MOE_F32 = 0, 1
+MOE_NORM_TOPK = 1
+
+HEADER = os.path.join(_build.INCLUDE, "katali_cuda.h")
+
+_vp, _u32, _u64, _i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int
+
+
+class KataliError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"katali_cuda error {code}: {msg}")
+        self.code = code
+
+
+class KataliMoeDesc(C.Structure):
+    _fields_ = [("n_experts", _u32), ("hidden", _u32), ("ffn", _u32), ("top_k", _u32),
+                ("gate_type", _u32), ("up_type", _u32), ("down_type", _u32), ("flags", _u32),
+                ("experts", C.POINTER(_vp))]
+
+
+def header_symbols(path: str = HEADER) -> list[str]:
+    """Every function the public header declares."""
+    src = open(path).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(katali_cuda_\w+)\s*\(", src)))
+
+
+def _ptr(t) -> int:
+    """Device pointer of a torch tensor (or an int address)."""
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError("expected a contiguous tensor")
+    return t.data_ptr()
+
+
+class Plugin:
+    def __init__(self, path: str | None = None):
+        path = path or _build.PLUGIN
+        if not os.path.exists(path):
+            raise FileNotFoundError(
+                f"{path} is missing; build it with `python -m katali_lab_b200.build`")
+        self.path = path
+        L = C.CDLL(path)
+        self.L = L
+        sig = {
+            "katali_cuda_probe": ([], _i32),
+            "katali_cuda_status": ([], C.c_char_p),
+            "katali_cuda_strerror": ([_i32], C.c_char_p),
+            "katali_cuda_malloc": ([C.POINTER(_vp), C.c_size_t], _i32),
+            "katali_cuda_free": ([_vp], _i32),
+            "katali_cuda_upload": ([_vp, _vp, C.c_size_t], _i32),
+            "katali_cuda_download": ([_vp, _vp, C.c_size_t], _i32),
+            "katali_cuda_supports_type": ([_u32], _i32),
+            "katali_cuda_matvec": ([_u32, _vp, _u64, _u64, _vp, _vp], _i32),
+            "katali_cuda_set_stream": ([_vp], _i32),
+            "katali_cuda_set_async": ([_i32], _i32),
+            "katali_cuda_sync": ([], _i32),
+            "katali_cuda_matvec_multi": ([_i32, C.POINTER(_u32), C.POINTER(_vp), C.POINTER(_u64),
+                                          _u64, _vp, C.POINTER(_vp)], _i32),
+            "katali_cuda_quantize_q8_1": ([_vp, _u64, _vp], _i32),
+            "katali_cuda_matvec_q8_1": ([_u32, _vp, _u64, _u64, _vp, _vp], _i32),
+            "katali_cuda_quantize_rows": ([_u32, _vp, _u64, _u64, _vp], _i32),
+            "katali_cuda_moe_create": ([C.POINTER(KataliMoeDesc), C.POINTER(_vp)], _i32),
+            "katali_cuda_moe_set_expert": ([_vp, _u32, _vp, _vp, _vp], _i32),
+            "katali_cuda_moe_destroy": ([_vp], _i32),
+            "katali_cuda_moe_layer": ([_vp, _vp, _vp, _vp, _u32], _i32),
+            "katali_cuda_moe_layer_routed": ([_vp, _vp, _vp, _vp, _vp, _u32], _i32),
+            "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
+            "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),
+        }
+        for name, (args, res) in sig.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+
+    # -- basics ----------------------------------------------------------
+    def probe(self) -> bool:
+        return bool(self.L.katali_cuda_probe())
+
+    def status(self) -> str:
+        return self.L.katali_cuda_status().decode()
+
+    def check(self, rc: int) -> None:
+        if rc != 0:
+            raise KataliError(rc, f"{self.L.katali_cuda_strerror(rc).decode()} ({self.status()})")
+
+    def set_stream(self, stream) -> None:
+        """stream: a torch.cuda.Stream, a raw cudaStream_t int, or None (plugin stream)."""
+        raw = getattr(stream, "cuda_stream", stream)
+        self.check(self.L.katali_cuda_set_stream(raw or None))
+
+    def set_async(self, on: bool) -> None:
+        self.check(self.L.katali_cuda_set_async(int(on)))
+
+    def sync(self) -> None:
+        self.check(self.L.katali_cuda_sync())
+
+    # -- dense -----------------------------------------------------------
+    def matvec(self, qtype, w, rows, cols, x, y) -> None:
+        self.check(self.L.katali_cuda_matvec(qtype, _ptr(w), rows, cols, _ptr(x), _ptr(y)))
+
+    def matvec_multi(self, qtypes, ws, rows, cols, x, ys) -> None:
+        n = len(qtypes)
+        self.check(self.L.katali_cuda_matvec_multi(
+            n, (_u32 * n)(*qtypes), (_vp * n)(*[_ptr(w) for w in ws]), (_u64 * n)(*rows), cols,
+            _ptr(x), (_vp * n)(*[_ptr(y) for y in ys])))
+
+    def quantize_q8_1(self, x, n, xq) -> None:
+        self.check(self.L.katali_cuda_quantize_q8_1(_ptr(x), n, _ptr(xq)))
+
+    def matvec_q8_1(self, qtype, w, rows, cols, xq, y) -> None:
+        self.check(self.L.katali_cuda_matvec_q8_1(qtype, _ptr(w), rows, cols, _ptr(xq), _ptr(y)))
+
+    def quantize_rows(self, qtype, src, rows, cols, dst) -> None:
+        self.check(self.L.katali_cuda_quantize_rows(qtype, _ptr(src), rows, cols, _ptr(dst)))
+
+    def row_isums(self, qtype, w, rows, cols, xq, isum, xsum) -> None:
+        self.check(self.L.katali_cuda_debug_row_isums(qtype, _ptr(w), rows, cols, _ptr(xq),
+                                                       _ptr(isum), _ptr(xsum)))
+
+
+class MoeLayer:
+    """One MoE layer's expert table inside the plugin (katali_cuda_moe_*)."""
+
+    def __init__(self, plugin: Plugin, n_experts, hidden, ffn, top_k, experts, norm_topk=True,
+                 gate_type=Q4_K, up_type=Q4_K, down_type=Q6_K):
+        """experts: list of (gate_ptr, up_ptr, down_ptr) device addresses, one per expert."""
+        self.p = plugin
+        flat = (_vp * (3 * n_experts))(*[int(a) for tri in experts for a in tri])
+        self._flat = flat
+        desc = KataliMoeDesc(n_experts, hidden, ffn, top_k, gate_type, up_type, down_type,
+                             MOE_NORM_TOPK if norm_topk else 0, C.cast(flat, C.POINTER(_vp)))
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_moe_create(C.byref(desc), C.byref(h)))
+        self.h = h
+        self.top_k = top_k
+
+    def forward(self, x, logits, y, mode=MOE_Q8_1) -> None:
+        self.p.check(self.p.L.katali_cuda_moe_layer(self.h, _ptr(x), _ptr(logits), _ptr(y), mode))
+
+    def forward_routed(self, x, ids, w, y, mode=MOE_Q8_1) -> None:
+        self.p.check(self.p.L.katali_cuda_moe_layer_routed(self.h, _ptr(x), _ptr(ids), _ptr(w),
+                                                           _ptr(y), mode))
+
+    def route(self, logits, ids, w) -> None:
+        self.p.check(self.p.L.katali_cuda_debug_route(self.h, _ptr(logits), _ptr(ids), _ptr(w)))
+
+    def set_expert(self, e, gate, up, down) -> None:
+        self.p.check(self.p.L.katali_cuda_moe_set_expert(self.h, e, int(gate), int(up), int(down)))
+
+    def close(self) -> None:
+        if self.h:
+            self.p.L.katali_cuda_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
