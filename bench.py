@@ -1,0 +1,378 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized expert hot path (C2: one fused MoE layer, batch-1 decode).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one pass of the hot path over one batch of synthetic input: CALLS
+fused-MoE-layer calls, call i on layer i % LAYERS of a LAYERS-deep expert store
+(256 experts x {gate, up Q4_K 512x2048; down Q6_K 2048x512} per layer, 522 MB),
+each with its own seeded x (N(0,1), 2048) and router logits (N(0,1), 256).
+The store (16 x 522 MB = 8.4 GB) is far larger than the 126 MB L2 and each call
+reads 8 random experts of a different layer, so expert bytes come from HBM.
+
+metric = quantised expert bytes read per second (16,318,464 B per call), whole
+job; `value` is timed on the device with inputs already in HBM (CUDA graph of
+the step's launches, CUDA events); `e2e` is the same metric through the C ABI
+with host buffers: upload of the step's inputs from pinned memory, the layer
+calls, download of the outputs, each step. N > 1 GPUs run independent replicas
+(one process per GPU, weak scaling) and report the max time over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, F, E, K = 2048, 512, 256, 8
+RBG = H // 256 * 144
+RBD = F // 256 * 210
+EXPERT_BYTES = 2 * F * RBG + H * RBD          # 2,039,808
+CALL_BYTES = K * EXPERT_BYTES                  # 16,318,464 quantised expert bytes per call
+ACT_BYTES = H * 4 + E * 4 + H * 4              # x, logits in; y out (fp32)
+METRIC = "MoE-layer quant-weight GB/s vs HBM peak"
+WORKLOAD = ("C2 fused MoE layer, batch-1 decode: hidden 2048, 256 experts, expert FFN 512, "
+            "top-8 of softmax(N(0,1) logits), gate/up Q4_K, down Q6_K (N(0,0.02) weights), "
+            "x N(0,1) quantised to q8_1 on device")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--calls", type=int, default=64)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-graph", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the MoE kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "moe_kernel_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,"
+                 "clocks_event_reasons.active", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 3:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        for r in self.rows:
+            try:
+                bits = int(r[2], 16)
+            except ValueError:
+                continue
+            for b, n in REASON_BITS.items():
+                if bits & b:
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the reference's own kernels; test infrastructure under oracle/)
+# ---------------------------------------------------------------------------
+def cpu_reference_rate(layers_host, seconds: float, seed: int = 7):
+    """Time the reference's CPU kernels (composed MoE layer) with all host cores on a
+    bounded sample of the workload: as many layer calls as fit in ~`seconds`."""
+    from oracle.oracle import Ref
+    ref = Ref()
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(seed)
+    scratch = ref.moe_scratch(layers_host[0])
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        lw = layers_host[calls % len(layers_host)]
+        x = rng.normal(0, 1, H).astype(np.float32)
+        lg = rng.normal(0, 1, E).astype(np.float32)
+        ref.moe_layer(lw, x, lg, n_threads=cores, scratch=scratch)
+        calls += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and calls >= 8) or calls >= 100000:
+            break
+    ref.L.kref_moe_scratch_free(scratch)
+    gbs = calls * CALL_BYTES / el / 1e9
+    return gbs, cores, calls, el
+
+
+def host_layer_numpy(seed: int):
+    """One layer's experts encoded on the host (oracle C encoder), for the reference arm."""
+    from oracle.oracle import Port, make_moe_weights
+    return make_moe_weights(Port(), E, H, F, seed=seed, top_k=K)
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    layers = [host_layer_numpy(1000 + i) for i in range(2)]
+    for _ in range(args.warmup):
+        cpu_reference_rate(layers, 0.0)
+    rates, total_calls, total_s = [], 0, 0.0
+    per_step = max(args.cpu_seconds / max(args.steps, 1), 0.05)
+    for s in range(args.steps):
+        gbs, cores, calls, el = cpu_reference_rate(layers, per_step, seed=100 + s)
+        rates.append(gbs)
+        total_calls += calls
+        total_s += el
+    value = total_calls * CALL_BYTES / total_s / 1e9
+    sample = (f"{total_calls} layer calls over {args.steps} steps on 2 host-encoded layers "
+              f"(reference kernels: katali_ggml_matvec_fused gate/up, silu_mul_avx2, Q6_K matvec)")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * total_s / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "threads": os.cpu_count()},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(),
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import MOE_Q8_1, MoeLayer, Plugin
+    from katali_lab_b200.synth import make_expert_store
+
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    plugin.set_stream(stream)
+
+    L, T = args.layers, args.calls
+    stores = [make_expert_store(plugin, E, H, F, seed=10_000 * rank + l) for l in range(L)]
+    layers = [MoeLayer(plugin, E, H, F, K, st.pointers()) for st in stores]
+    g = torch.Generator(device="cuda").manual_seed(77 + rank)
+    xs = torch.randn((T, H), generator=g, device="cuda")
+    lgs = torch.randn((T, E), generator=g, device="cuda")
+    ys = torch.empty((T, H), device="cuda")
+    torch.cuda.synchronize()
+
+    plugin.set_async(True)
+
+    def step():
+        for i in range(T):
+            layers[i % L].forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+
+    # correctness guard: first call equals a synchronous run
+    step()
+    plugin.sync()
+
+    graph = None
+    if not args.no_graph:
+        try:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                plugin.set_stream(torch.cuda.current_stream())
+                step()
+            plugin.set_stream(stream)
+            graph = gr
+        except Exception as e:  # capture unsupported: time eager launches
+            print(f"[bench] graph capture failed ({e}); timing eager launches", file=sys.stderr)
+            plugin.set_stream(stream)
+            torch.cuda.synchronize()
+            graph = None
+
+    run = graph.replay if graph is not None else step
+    for _ in range(max(args.warmup, 3)):
+        run()
+    plugin.sync()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local_rank) as clk:
+        start.record(stream)
+        for _ in range(args.steps):
+            run()
+        end.record(stream)
+        end.synchronize()
+    barrier()
+    plugin.sync()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * args.steps * T * CALL_BYTES / (ms / 1e3) / 1e9
+    us_per_call = 1e3 * ms / (args.steps * T)
+
+    # ---- e2e through the C ABI with host buffers --------------------------
+    import ctypes as C
+    xh = torch.randn((T, H), generator=torch.Generator().manual_seed(5)).pin_memory()
+    lh = torch.randn((T, E), generator=torch.Generator().manual_seed(6)).pin_memory()
+    yh = torch.empty((T, H)).pin_memory()
+    plugin.set_async(True)
+    L_ = plugin.L
+
+    def e2e_step():
+        plugin.check(L_.katali_cuda_upload(xs.data_ptr(), xh.data_ptr(), xh.numel() * 4))
+        plugin.check(L_.katali_cuda_upload(lgs.data_ptr(), lh.data_ptr(), lh.numel() * 4))
+        for i in range(T):
+            layers[i % L].forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+        plugin.check(L_.katali_cuda_download(yh.data_ptr(), ys.data_ptr(), yh.numel() * 4))
+
+    for _ in range(2):
+        e2e_step()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    e_end.synchronize()
+    e_ms = e_start.elapsed_time(e_end)
+    if world > 1:
+        t = torch.tensor([e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_value = world * args.steps * T * CALL_BYTES / (e_ms / 1e3) / 1e9
+
+    # ---- CPU baseline (rank 0, N == 1 only) ---------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        try:
+            from oracle.oracle import MoeWeights
+            hl = [MoeWeights(st.gate.cpu().numpy(), st.up.cpu().numpy(), st.down.cpu().numpy(),
+                             H, F, K) for st in stores[:2]]
+            gbs, cores, calls, el = cpu_reference_rate(hl, args.cpu_seconds)
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                   "sample": f"{calls} layer calls ({el:.1f} s) on 2 of the benchmark's layers, "
+                             f"reference CPU kernels composed per call, {cores} threads"}
+        except Exception as e:
+            cpu = {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"unavailable: {e}"}
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = CALL_BYTES / (us_per_call * 1e-6) / 1e9
+        traffic = committed_traffic()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "calls_per_step": T, "layers_in_store": L,
+                       "store_bytes_per_gpu": L * E * EXPERT_BYTES,
+                       "l2": "inputs larger than L2: 16-layer store (8.4 GB) rotated per call",
+                       "graph": graph is not None, "parallelism": f"replicas x{world}",
+                       "us_per_layer": round(us_per_call, 3)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": f"{peak_kind} hbm_gbs",
+                         "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                         "algorithmic_bytes_per_launch": CALL_BYTES},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
+                    "d2h_bytes_per_step": yh.numel() * 4},
+            "gpu_launches": args.steps * T,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for l in layers:
+        l.close()
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

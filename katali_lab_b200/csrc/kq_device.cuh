@@ -348,7 +348,8 @@ __device__ __forceinline__ double q6k_f32_partial(const uint8_t *row, int nb, co
 
 // ---------------------------------------------------------------------------
 // q8_1 quantisation of one 32-element block by one warp (lane = element).
-// Writes the split shared layout; optionally the GGUF block at gblk.
+// Writes the split shared layout (q/d_out/s32_out may be NULL), and the GGUF
+// block at gblk when non-NULL.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void quant_block_q8(float v, int lane, int8_t *q, float *d_out,
                                                int *s32_out, int *s16_out, uint8_t *gblk) {
@@ -359,9 +360,9 @@ __device__ __forceinline__ void quant_block_q8(float v, int lane, int8_t *q, flo
     if (amax != 0.0f) qi = max(-127, min(127, (int)roundf(__fdiv_rn(v, d))));
     const int sum = __reduce_add_sync(KQ_FULL, qi);
     const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
-    q[lane] = (int8_t)qi;
+    if (q) q[lane] = (int8_t)qi;
     const uint16_t dh = f2h(d);
-    if (lane == 0) {
+    if (lane == 0 && d_out) {
         *d_out = h2f(dh);
         *s32_out = sum;
         if (s16_out) {

@@ -159,10 +159,8 @@ __global__ void quantize_q8_1_kernel(const float *x, uint64_t nblocks, uint8_t *
     const uint64_t wg = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (wg >= nblocks) return;
-    int8_t q;
-    float d;
-    int s32;
-    quant_block_q8(x[32 * wg + lane], lane, &q, &d, &s32, nullptr, out + Q81_BYTES * wg);
+    quant_block_q8(x[32 * wg + lane], lane, nullptr, nullptr, nullptr, nullptr,
+                   out + Q81_BYTES * wg);
 }
 
 // ---------------------------------------------------------------------------
@@ -372,8 +370,12 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     int grid = 2 * num_sms();
     if ((uint32_t)grid > tiles) grid = (int)tiles;
     void (*fn)(GemvParams) = mode == 0 ? gemv_kernel<0> : (mode == 1 ? gemv_kernel<1> : gemv_kernel<2>);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    static size_t set_bytes[3] = {0, 0, 0};
+    if (smem > set_bytes[mode]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        set_bytes[mode] = smem;
+    }
     fn<<<grid, GEMV_THREADS, smem, st>>>(p);
     return cudaGetLastError();
 }

@@ -364,9 +364,15 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
 }
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
-    cudaError_t e =
-        cudaFuncSetAttribute(moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem_bytes);
-    if (e != cudaSuccess) return e;
+    // Raise the dynamic shared-memory limit once per size (never during a graph capture
+    // that follows a first eager call with the same plan).
+    static uint32_t set_bytes = 0;
+    if (p.smem_bytes > set_bytes) {
+        cudaError_t e = cudaFuncSetAttribute(moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)p.smem_bytes);
+        if (e != cudaSuccess) return e;
+        set_bytes = p.smem_bytes;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(MOE_THREADS);
