@@ -91,7 +91,8 @@ const char *katali_cuda_strerror(int status);
 int katali_cuda_matvec_multi(int n, const uint32_t *types, const void *const *w,
                              const uint64_t *rows, uint64_t cols, const float *x,
                              float *const *y);
-/* Quantise n fp32 values (n % 32 == 0) to GGUF q8_1 blocks (36 B per 32). */
+/* Quantise n fp32 values (n % 32 == 0) to GGUF q8_1 blocks (36 B per 32);
+ * xq 4-byte aligned. */
 int katali_cuda_quantize_q8_1(const float *x, uint64_t n, void *xq);
 /* y = W xq with q8_1 activations (the DP4A path, README.md:17). */
 int katali_cuda_matvec_q8_1(uint32_t type, const void *w, uint64_t rows, uint64_t cols,

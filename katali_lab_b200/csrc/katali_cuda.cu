@@ -280,7 +280,7 @@ int katali_cuda_matvec_q8_1(uint32_t type, const void *w, uint64_t rows, uint64_
 }
 
 int katali_cuda_quantize_q8_1(const float *x, uint64_t n, void *xq) {
-    if (!x || !xq || n == 0 || n % 32) return KATALI_ERR_BAD_ARG;
+    if (!x || !xq || n == 0 || n % 32 || ((uintptr_t)xq & 3u)) return KATALI_ERR_BAD_ARG;
     int s = ensure();
     if (s) return s;
     return finish(kq::launch_quantize_q8_1(x, n, xq, g_stream));
@@ -291,6 +291,7 @@ int katali_cuda_quantize_rows(uint32_t type, const float *src, uint64_t rows, ui
     if (type != KATALI_TYPE_Q4_K && type != KATALI_TYPE_Q6_K && type != KATALI_TYPE_Q8_1)
         return KATALI_ERR_UNSUPPORTED_TYPE;
     if (!src || !dst || rows == 0 || row_bytes(type, cols) == 0) return KATALI_ERR_BAD_ARG;
+    if (type == KATALI_TYPE_Q8_1 && ((uintptr_t)dst & 3u)) return KATALI_ERR_BAD_ARG;
     int s = ensure();
     if (s) return s;
     return finish(kq::launch_encode(type, src, rows * cols, dst, g_stream));

@@ -349,7 +349,7 @@ __device__ __forceinline__ double q6k_f32_partial(const uint8_t *row, int nb, co
 // ---------------------------------------------------------------------------
 // q8_1 quantisation of one 32-element block by one warp (lane = element).
 // Writes the split shared layout (q/d_out/s32_out may be NULL), and the GGUF
-// block at gblk when non-NULL.
+// block at gblk (4-byte aligned) when non-NULL.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void quant_block_q8(float v, int lane, int8_t *q, float *d_out,
                                                int *s32_out, int *s16_out, uint8_t *gblk) {
@@ -370,14 +370,16 @@ __device__ __forceinline__ void quant_block_q8(float v, int lane, int8_t *q, flo
             s16_out[1] = sum - sum_lo;
         }
     }
-    if (gblk) {
-        gblk[4 + lane] = (uint8_t)(int8_t)qi;
+    if (gblk) {  // GGUF block, written as aligned 32-bit words (gblk is 4-byte aligned)
+        const uint32_t b = (uint32_t)qi & 0xFFu;
+        const uint32_t b1 = __shfl_down_sync(KQ_FULL, b, 1);
+        const uint32_t b2 = __shfl_down_sync(KQ_FULL, b, 2);
+        const uint32_t b3 = __shfl_down_sync(KQ_FULL, b, 3);
+        if ((lane & 3) == 0)
+            *reinterpret_cast<uint32_t *>(gblk + 4 + lane) = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
         if (lane == 0) {
-            const uint16_t sh = f2h(__fmul_rn(d, (float)sum));
-            gblk[0] = (uint8_t)(dh & 0xFF);
-            gblk[1] = (uint8_t)(dh >> 8);
-            gblk[2] = (uint8_t)(sh & 0xFF);
-            gblk[3] = (uint8_t)(sh >> 8);
+            const uint32_t sh = f2h(__fmul_rn(d, (float)sum));
+            *reinterpret_cast<uint32_t *>(gblk) = (uint32_t)dh | (sh << 16);
         }
     }
 }

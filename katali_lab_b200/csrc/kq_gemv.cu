@@ -352,7 +352,8 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     p.total_tiles = tiles;
     if (tiles == 0) return cudaSuccess;
     const uint32_t cols = p.cols;
-    const uint32_t act_bytes = mode == 2 ? cols * 4 + cols / 32 * 4 : cols + cols / 32 * 12 + 16;
+    // activation area: fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
+    const uint32_t act_bytes = mode == 2 ? cols * 4 + cols / 32 * 4 : cols + cols / 32 * 16;
     p.stage_bytes = stage + 16;
     p.use_tma = 1;
     int ns = (int)(98304 / p.stage_bytes);
