@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--warm", action="store_true",
+                    help="diagnostic: every call reuses layer 0 and input 0 (weights stay in L2)")
+    ap.add_argument("--trace", action="store_true",
+                    help="print the per-phase timeline of the MoE kernel to stderr")
     return ap.parse_args()
 
 
@@ -224,7 +228,8 @@ def run_ours(args, rank, world, local_rank):
 
     def step():
         for i in range(T):
-            layers[i % L].forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+            j = 0 if args.warm else i
+            layers[j % L].forward(xs[j], lgs[j], ys[i], MOE_Q8_1)
 
     # correctness guard: first call equals a synchronous run
     step()
@@ -272,6 +277,9 @@ def run_ours(args, rank, world, local_rank):
         ms = float(t.item())
     value = world * args.steps * T * CALL_BYTES / (ms / 1e3) / 1e9
     us_per_call = 1e3 * ms / (args.steps * T)
+
+    if args.trace and rank == 0:
+        print_trace(plugin, layers, xs, lgs, ys, T, L, args.warm)
 
     # ---- e2e through the C ABI with host buffers --------------------------
     import ctypes as C
@@ -348,6 +356,41 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
     for l in layers:
         l.close()
+
+
+TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first chunk in",
+               5: "gate/up done", 6: "barrier passed", 7: "phase B start", 8: "end",
+               9: "route: logits in", 10: "route: sorted", 11: "route: top-k done",
+               12: "2nd chunk in", 13: "down rows in", 14: "down rows decoded",
+               15: "phase B row0 dots"}
+
+
+def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
+    """Phase timeline of the fused MoE kernel from its %globaltimer trace (ns)."""
+    import torch
+    from katali_lab_b200 import MOE_Q8_1
+    buf = torch.zeros(1024 * 16, dtype=torch.int64, device="cuda")
+    rows = []
+    for n in range(min(T, 32)):
+        i = 0 if warm else n
+        lay = layers[i % L]
+        grid = lay.set_trace(buf)
+        lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+        plugin.sync()
+        lay.set_trace(None)
+        t = buf[:grid * 16].view(grid, 16).cpu().numpy().astype(np.int64)
+        t0 = t[:, 0].min()
+        row = [t[:, 0].max() - t0]
+        for s in range(1, 16):  # CTAs without phase-A or phase-B rows leave their slot 0
+            v = t[:, s][t[:, s] > 0]
+            row.append((v.max() - t0) if v.size else 0)
+        rows.append(row)
+    med = np.median(np.array(rows, dtype=np.float64), axis=0) / 1e3
+    print("[trace] median over calls, us after the first CTA started (max over CTAs):",
+          file=sys.stderr)
+    print(f"[trace]   last CTA start {med[0]:.2f}", file=sys.stderr)
+    for s, v in sorted(zip(range(1, 16), med[1:]), key=lambda sv: sv[1]):
+        print(f"[trace]   {TRACE_NAMES[s]:20s} {v:.2f}", file=sys.stderr)
 
 
 def main():

@@ -138,6 +138,7 @@ struct KataliMoe {
     uint32_t *sync;
     int32_t *dbg_ids;
     float *dbg_w;
+    uint64_t *trace;
     int grid;
 };
 
@@ -354,7 +355,8 @@ int katali_cuda_moe_create(const KataliMoeDesc *d, KataliMoe **out) {
             m->table[i] = (const uint8_t *)d->experts[i];
         }
     }
-    cudaError_t e = cudaMalloc((void **)&m->d_table, m->table.size() * sizeof(void *));
+    // +1 pointer: the kernel copies the table in 16-byte pairs
+    cudaError_t e = cudaMalloc((void **)&m->d_table, (m->table.size() + 1) * sizeof(void *));
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->hbuf, sizeof(float) * d->top_k * d->ffn);
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->sync, 16);
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->dbg_ids, 4 * kq::MOE_MAX_K);
@@ -417,6 +419,7 @@ static int moe_run(KataliMoe *m, const float *x, const float *logits, const int3
     p.dbg_ids = m->dbg_ids;
     p.dbg_w = m->dbg_w;
     p.route_only = route_only;
+    p.trace = route_only ? nullptr : m->trace;
     return finish(kq::launch_moe(p, route_only ? 1 : m->grid, g_stream));
 }
 
@@ -430,6 +433,13 @@ int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *id
                                  float *y, uint32_t mode) {
     if (!aligned16(x) || !ids || !w || !y) return KATALI_ERR_BAD_ARG;
     return moe_run(m, x, nullptr, ids, w, y, mode, 0);
+}
+
+int katali_cuda_debug_moe_trace(KataliMoe *m, uint64_t *trace, int *grid) {
+    if (!m) return KATALI_ERR_BAD_ARG;
+    m->trace = trace;
+    if (grid) *grid = m->grid;
+    return KATALI_OK;
 }
 
 int katali_cuda_debug_route(KataliMoe *m, const float *router_logits, int32_t *ids, float *w) {

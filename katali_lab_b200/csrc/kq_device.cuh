@@ -128,14 +128,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on phase `parity`; returns false (and the caller records a
-// timeout) when the limit runs out.
+// Bounded wait on phase `parity`: 64 quick tries, then tries spaced by a short
+// sleep (tight polling of an mbarrier slows the TMA transfers completing on it).
+// Returns false (and the caller records a timeout) when the limit runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if (it > 64) __nanosleep(64);
     }
     return false;
+}
+// Same, called by all lanes of a warp together (all lanes poll one address).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+    return mbar_wait(bar, parity);
 }
 // Global -> shared bulk copy completing on `bar`. dst/src 16-byte aligned,
 // bytes a multiple of 16.
@@ -145,6 +150,22 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
         "[%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// L2 policy for streamed weights: read once per call, so they are marked
+// evict-first and do not push code, pointer tables and activations out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes,
+                                              uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
 }
 
@@ -198,151 +219,192 @@ struct ActQ8 {
 };
 
 // ---------------------------------------------------------------------------
-// Row dots, one warp per row. Each returns this lane's double partial; the
-// caller reduces across the warp (warp_sum_d) and rounds once to float.
+// Block dots by "unit": 64 consecutive elements of a row whose bytes one lane
+// loads once and uses fully.
+//   Q4_K unit u: block b = u/4, chunk c = u%4 -> the 32 nibble bytes of chunk c,
+//                low nibbles = q8_1 block 8b+2c, high nibbles = 8b+2c+1.
+//   Q6_K unit u: block b = u/4, half h = (u/2)%2, quarter pair {qo, qo+2} with
+//                qo = u%2 -> 32 ql bytes (low nibbles quarter qo, high nibbles
+//                quarter qo+2) and the 32 qh bytes of half h;
+//                q8_1 blocks 8b+4h+qo and 8b+4h+qo+2.
+// Each unit returns the sum of its two exact per-q8-block double terms.
 // ---------------------------------------------------------------------------
-// Q4_K x q8_1. Lane = (block b = lane/4 + 8i, 64-element chunk c = lane%4).
+__device__ __forceinline__ double q4k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+    const int b = u >> 2, c = u & 3;
+    const uint8_t *blk = row + Q4K_BYTES * b;
+    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+    const int g = 8 * b + 2 * c;
+    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + 32 * g);
+    const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+    const uint32_t M = 0x0F0F0F0Fu;
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)(w0.x & M), (int)a0.x, lo);
+    hi = __dp4a((int)((w0.x >> 4) & M), (int)a2.x, hi);
+    lo = __dp4a((int)(w0.y & M), (int)a0.y, lo);
+    hi = __dp4a((int)((w0.y >> 4) & M), (int)a2.y, hi);
+    lo = __dp4a((int)(w0.z & M), (int)a0.z, lo);
+    hi = __dp4a((int)((w0.z >> 4) & M), (int)a2.z, hi);
+    lo = __dp4a((int)(w0.w & M), (int)a0.w, lo);
+    hi = __dp4a((int)((w0.w >> 4) & M), (int)a2.w, hi);
+    lo = __dp4a((int)(w1.x & M), (int)a1.x, lo);
+    hi = __dp4a((int)((w1.x >> 4) & M), (int)a3.x, hi);
+    lo = __dp4a((int)(w1.y & M), (int)a1.y, lo);
+    hi = __dp4a((int)((w1.y >> 4) & M), (int)a3.y, hi);
+    lo = __dp4a((int)(w1.z & M), (int)a1.z, lo);
+    hi = __dp4a((int)((w1.z >> 4) & M), (int)a3.z, hi);
+    lo = __dp4a((int)(w1.w & M), (int)a1.w, lo);
+    hi = __dp4a((int)((w1.w >> 4) & M), (int)a3.w, hi);
+    int sc0, m0, sc1, m1;
+    q4k_scales(h, c, sc0, m0, sc1, m1);
+    const double d = (double)h2f(h.x), dmin = (double)h2f(h.x >> 16);
+    const double dx0 = (double)a.d[g], dx1 = (double)a.d[g + 1];
+    return ((d * dx0) * (double)(sc0 * lo) - (dmin * dx0) * (double)(m0 * a.s32[g])) +
+           ((d * dx1) * (double)(sc1 * hi) - (dmin * dx1) * (double)(m1 * a.s32[g + 1]));
+}
+
+__device__ __forceinline__ double q6k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
+    const uint8_t *blk = row + Q6K_BYTES * b;
+    uint32_t ql[8], qh[8];
+    load16_a2(blk + 64 * h + 32 * qo, ql);
+    load16_a2(blk + 64 * h + 32 * qo + 16, ql + 4);
+    load16_a2(blk + 128 + 32 * h, qh);
+    load16_a2(blk + 128 + 32 * h + 16, qh + 4);
+    const int jA = 8 * b + 4 * h + qo, jB = jA + 2;
+    const uint4 *aA = reinterpret_cast<const uint4 *>(a.q + 32 * jA);
+    const uint4 *aB = reinterpret_cast<const uint4 *>(a.q + 32 * jB);
+    const uint4 xA0 = aA[0], xA1 = aA[1], xB0 = aB[0], xB1 = aB[1];
+    const uint32_t wa[8] = {xA0.x, xA0.y, xA0.z, xA0.w, xA1.x, xA1.y, xA1.z, xA1.w};
+    const uint32_t wb[8] = {xB0.x, xB0.y, xB0.z, xB0.w, xB1.x, xB1.y, xB1.z, xB1.w};
+    const int shA = 2 * qo, shB = 2 * qo + 4;
+    int sA0 = 0, sA1 = 0, sB0 = 0, sB1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
+        const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
+        sA0 = __dp4a((int)vA, (int)wa[i], sA0);
+        sB0 = __dp4a((int)vB, (int)wb[i], sB0);
+    }
+#pragma unroll
+    for (int i = 4; i < 8; ++i) {
+        const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
+        const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
+        sA1 = __dp4a((int)vA, (int)wa[i], sA1);
+        sB1 = __dp4a((int)vB, (int)wb[i], sB1);
+    }
+    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
+    const int IA = (int)sc[2 * qo] * (sA0 - 32 * a.s16[2 * jA]) +
+                   (int)sc[2 * qo + 1] * (sA1 - 32 * a.s16[2 * jA + 1]);
+    const int IB = (int)sc[2 * qo + 4] * (sB0 - 32 * a.s16[2 * jB]) +
+                   (int)sc[2 * qo + 5] * (sB1 - 32 * a.s16[2 * jB + 1]);
+    const double d = (double)h2f(ld_u16(blk + 208));
+    return (d * (double)a.d[jA]) * (double)IA + (d * (double)a.d[jB]) * (double)IB;
+}
+
+// fp32 activations x (shared) with per-32-group sums xs.
+__device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const float *x,
+                                               const float *xs) {
+    const int b = u >> 2, c = u & 3;
+    const uint8_t *blk = row + Q4K_BYTES * b;
+    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+    const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const float *xl = x + 256 * b + 64 * c;
+    float lo = 0.0f, hi = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 xa = *reinterpret_cast<const float4 *>(xl + 4 * i);
+        const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 + 4 * i);
+        const uint32_t w = ww[i];
+        lo = fmaf((float)(w & 15u), xa.x, lo);
+        hi = fmaf((float)((w >> 4) & 15u), xb.x, hi);
+        lo = fmaf((float)((w >> 8) & 15u), xa.y, lo);
+        hi = fmaf((float)((w >> 12) & 15u), xb.y, hi);
+        lo = fmaf((float)((w >> 16) & 15u), xa.z, lo);
+        hi = fmaf((float)((w >> 20) & 15u), xb.z, hi);
+        lo = fmaf((float)((w >> 24) & 15u), xa.w, lo);
+        hi = fmaf((float)(w >> 28), xb.w, hi);
+    }
+    int sc0, m0, sc1, m1;
+    q4k_scales(h, c, sc0, m0, sc1, m1);
+    const float d = h2f(h.x), dmin = h2f(h.x >> 16);
+    const int g = 8 * b + 2 * c;
+    return ((double)(d * (float)sc0) * (double)lo - (double)(dmin * (float)m0) * (double)xs[g]) +
+           ((double)(d * (float)sc1) * (double)hi - (double)(dmin * (float)m1) * (double)xs[g + 1]);
+}
+
+__device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const float *x) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
+    const uint8_t *blk = row + Q6K_BYTES * b;
+    uint32_t ql[8], qh[8];
+    load16_a2(blk + 64 * h + 32 * qo, ql);
+    load16_a2(blk + 64 * h + 32 * qo + 16, ql + 4);
+    load16_a2(blk + 128 + 32 * h, qh);
+    load16_a2(blk + 128 + 32 * h + 16, qh + 4);
+    const float *xA = x + 256 * b + 128 * h + 32 * qo, *xB = xA + 64;
+    const int shA = 2 * qo, shB = 2 * qo + 4;
+    float fA[2] = {0.0f, 0.0f}, fB[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
+        const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
+        const float4 a4 = *reinterpret_cast<const float4 *>(xA + 4 * i);
+        const float4 b4 = *reinterpret_cast<const float4 *>(xB + 4 * i);
+        float &fa = fA[i >> 2], &fb = fB[i >> 2];
+        fa = fmaf((float)((int)(vA & 63u) - 32), a4.x, fa);
+        fa = fmaf((float)((int)((vA >> 8) & 63u) - 32), a4.y, fa);
+        fa = fmaf((float)((int)((vA >> 16) & 63u) - 32), a4.z, fa);
+        fa = fmaf((float)((int)((vA >> 24) & 63u) - 32), a4.w, fa);
+        fb = fmaf((float)((int)(vB & 63u) - 32), b4.x, fb);
+        fb = fmaf((float)((int)((vB >> 8) & 63u) - 32), b4.y, fb);
+        fb = fmaf((float)((int)((vB >> 16) & 63u) - 32), b4.z, fb);
+        fb = fmaf((float)((int)((vB >> 24) & 63u) - 32), b4.w, fb);
+    }
+    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
+    const float d = h2f(ld_u16(blk + 208));
+    return ((double)(d * (float)sc[2 * qo]) * (double)fA[0] +
+            (double)(d * (float)sc[2 * qo + 1]) * (double)fA[1]) +
+           ((double)(d * (float)sc[2 * qo + 4]) * (double)fB[0] +
+            (double)(d * (float)sc[2 * qo + 5]) * (double)fB[1]);
+}
+
+template <uint32_t T>
+__device__ __forceinline__ double unit_q8(const uint8_t *row, int u, const ActQ8 &a) {
+    return T == T_Q4_K ? q4k_q8_unit(row, u, a) : q6k_q8_unit(row, u, a);
+}
+template <uint32_t T>
+__device__ __forceinline__ double unit_f32(const uint8_t *row, int u, const float *x,
+                                           const float *xs) {
+    return T == T_Q4_K ? q4k_f32_unit(row, u, x, xs) : q6k_f32_unit(row, u, x);
+}
+
+// One warp per row: this lane's double partial over units lane, lane+32, ...
+// (cols/64 units per row); the caller reduces across the warp and rounds once.
 __device__ __forceinline__ double q4k_q8_partial(const uint8_t *row, int nb, const ActQ8 &a,
                                                  int lane) {
     double acc = 0.0;
-    const int c = lane & 3;
-    for (int b = lane >> 2; b < nb; b += 8) {
-        const uint8_t *blk = row + Q4K_BYTES * b;
-        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-        const int g = 8 * b + 2 * c;
-        const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + 32 * g);
-        const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
-        const uint32_t M = 0x0F0F0F0Fu;
-        int lo = 0, hi = 0;
-        lo = __dp4a((int)(w0.x & M), (int)a0.x, lo);
-        hi = __dp4a((int)((w0.x >> 4) & M), (int)a2.x, hi);
-        lo = __dp4a((int)(w0.y & M), (int)a0.y, lo);
-        hi = __dp4a((int)((w0.y >> 4) & M), (int)a2.y, hi);
-        lo = __dp4a((int)(w0.z & M), (int)a0.z, lo);
-        hi = __dp4a((int)((w0.z >> 4) & M), (int)a2.z, hi);
-        lo = __dp4a((int)(w0.w & M), (int)a0.w, lo);
-        hi = __dp4a((int)((w0.w >> 4) & M), (int)a2.w, hi);
-        lo = __dp4a((int)(w1.x & M), (int)a1.x, lo);
-        hi = __dp4a((int)((w1.x >> 4) & M), (int)a3.x, hi);
-        lo = __dp4a((int)(w1.y & M), (int)a1.y, lo);
-        hi = __dp4a((int)((w1.y >> 4) & M), (int)a3.y, hi);
-        lo = __dp4a((int)(w1.z & M), (int)a1.z, lo);
-        hi = __dp4a((int)((w1.z >> 4) & M), (int)a3.z, hi);
-        lo = __dp4a((int)(w1.w & M), (int)a1.w, lo);
-        hi = __dp4a((int)((w1.w >> 4) & M), (int)a3.w, hi);
-        int sc0, m0, sc1, m1;
-        q4k_scales(h, c, sc0, m0, sc1, m1);
-        const double d = (double)h2f(h.x), dmin = (double)h2f(h.x >> 16);
-        const double dx0 = (double)a.d[g], dx1 = (double)a.d[g + 1];
-        acc += (d * dx0) * (double)(sc0 * lo) - (dmin * dx0) * (double)(m0 * a.s32[g]);
-        acc += (d * dx1) * (double)(sc1 * hi) - (dmin * dx1) * (double)(m1 * a.s32[g + 1]);
-    }
+    for (int u = lane; u < 4 * nb; u += 32) acc += q4k_q8_unit(row, u, a);
     return acc;
 }
-
-// Q6_K x q8_1. Lane = (block b = lane/16 + 2i, 16-element group k = lane%16);
-// lanes k and k^1 share one q8_1 block and combine their scaled sums exactly.
 __device__ __forceinline__ double q6k_q8_partial(const uint8_t *row, int nb, const ActQ8 &a,
                                                  int lane) {
     double acc = 0.0;
-    const int k = lane & 15, h = k >> 3, kk = k & 7, qq = kk >> 1, sub = kk & 1;
-    const int nit = (nb + 1) >> 1;
-    for (int it = 0; it < nit; ++it) {
-        const int b = (lane >> 4) + 2 * it;
-        int I = 0;
-        double dd = 0.0;
-        if (b < nb) {
-            const uint8_t *blk = row + Q6K_BYTES * b;
-            uint32_t ql[4], qh[4];
-            load16_a2(blk + 64 * h + 32 * (qq & 1) + 16 * sub, ql);
-            load16_a2(blk + 128 + 32 * h + 16 * sub, qh);
-            const int sc = (int)(int8_t)blk[192 + k];
-            const uint4 av = *reinterpret_cast<const uint4 *>(a.q + 256 * b + 16 * k);
-            const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-            const int lsh = (qq >= 2) ? 4 : 0, hsh = 2 * qq;
-            int s = 0;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t v = ((ql[i] >> lsh) & 0x0F0F0F0Fu) |
-                                   (((qh[i] >> hsh) & 0x03030303u) << 4);
-                s = __dp4a((int)v, (int)aw[i], s);
-            }
-            I = sc * (s - 32 * a.s16[16 * b + k]);
-            dd = (double)h2f(ld_u16(blk + 208)) * (double)a.d[8 * b + (k >> 1)];
-        }
-        I += __shfl_xor_sync(KQ_FULL, I, 1);
-        if (b < nb && !(k & 1)) acc += dd * (double)I;
-    }
+    for (int u = lane; u < 4 * nb; u += 32) acc += q6k_q8_unit(row, u, a);
     return acc;
 }
-
-// Q4_K x fp32 activations x (shared), with per-32-group sums xs.
 __device__ __forceinline__ double q4k_f32_partial(const uint8_t *row, int nb, const float *x,
                                                   const float *xs, int lane) {
     double acc = 0.0;
-    const int c = lane & 3;
-    for (int b = lane >> 2; b < nb; b += 8) {
-        const uint8_t *blk = row + Q4K_BYTES * b;
-        const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-        const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const float *xl = x + 256 * b + 64 * c;
-        float lo = 0.0f, hi = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 xa = *reinterpret_cast<const float4 *>(xl + 4 * i);
-            const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 + 4 * i);
-            const uint32_t w = ww[i];
-            lo = fmaf((float)(w & 15u), xa.x, lo);
-            hi = fmaf((float)((w >> 4) & 15u), xb.x, hi);
-            lo = fmaf((float)((w >> 8) & 15u), xa.y, lo);
-            hi = fmaf((float)((w >> 12) & 15u), xb.y, hi);
-            lo = fmaf((float)((w >> 16) & 15u), xa.z, lo);
-            hi = fmaf((float)((w >> 20) & 15u), xb.z, hi);
-            lo = fmaf((float)((w >> 24) & 15u), xa.w, lo);
-            hi = fmaf((float)(w >> 28), xb.w, hi);
-        }
-        int sc0, m0, sc1, m1;
-        q4k_scales(h, c, sc0, m0, sc1, m1);
-        const float d = h2f(h.x), dmin = h2f(h.x >> 16);
-        const int g = 8 * b + 2 * c;
-        acc += (double)(d * (float)sc0) * (double)lo - (double)(dmin * (float)m0) * (double)xs[g];
-        acc += (double)(d * (float)sc1) * (double)hi -
-               (double)(dmin * (float)m1) * (double)xs[g + 1];
-    }
+    for (int u = lane; u < 4 * nb; u += 32) acc += q4k_f32_unit(row, u, x, xs);
     return acc;
 }
-
-// Q6_K x fp32 activations x (shared).
 __device__ __forceinline__ double q6k_f32_partial(const uint8_t *row, int nb, const float *x,
                                                   int lane) {
     double acc = 0.0;
-    const int k = lane & 15, h = k >> 3, kk = k & 7, qq = kk >> 1, sub = kk & 1;
-    for (int b = lane >> 4; b < nb; b += 2) {
-        const uint8_t *blk = row + Q6K_BYTES * b;
-        uint32_t ql[4], qh[4];
-        load16_a2(blk + 64 * h + 32 * (qq & 1) + 16 * sub, ql);
-        load16_a2(blk + 128 + 32 * h + 16 * sub, qh);
-        const int sc = (int)(int8_t)blk[192 + k];
-        const float d = h2f(ld_u16(blk + 208));
-        const float *xp = x + 256 * b + 16 * k;
-        const int lsh = (qq >= 2) ? 4 : 0, hsh = 2 * qq;
-        float s = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float4 xv = *reinterpret_cast<const float4 *>(xp + 4 * i);
-            const uint32_t v =
-                ((ql[i] >> lsh) & 0x0F0F0F0Fu) | (((qh[i] >> hsh) & 0x03030303u) << 4);
-            s = fmaf((float)((int)(v & 63u) - 32), xv.x, s);
-            s = fmaf((float)((int)((v >> 8) & 63u) - 32), xv.y, s);
-            s = fmaf((float)((int)((v >> 16) & 63u) - 32), xv.z, s);
-            s = fmaf((float)((int)((v >> 24) & 63u) - 32), xv.w, s);
-        }
-        acc += (double)(d * (float)sc) * (double)s;
-    }
+    for (int u = lane; u < 4 * nb; u += 32) acc += q6k_f32_unit(row, u, x);
     return acc;
 }
 

@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     if (warp == GEMV_CW) {
         // Producer: stream this CTA's tiles through the ring.
         if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
             uint32_t i = 0;
             for (uint32_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++i) {
                 const int s = (int)(i % p.nstages);
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
                 const uint32_t bytes = nrows * J.rb;
                 if (p.use_tma && (bytes & 15u) == 0) {
                     mbar_arrive_expect_tx(&full[s], bytes);
-                    bulk_g2s(stages + (size_t)s * p.stage_bytes, J.w + r0 * J.rb, bytes, &full[s]);
+                    bulk_g2s_hint(stages + (size_t)s * p.stage_bytes, J.w + r0 * J.rb, bytes, &full[s], pol);
                 } else {
                     mbar_arrive(&full[s]);  // consumers read this tile from global
                 }
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     uint32_t i = 0, g = 0;
     for (uint32_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++i) {
         const int s = (int)(i % p.nstages);
-        if (!mbar_wait(&full[s], (i / p.nstages) & 1)) {
+        if (!mbar_wait_warp(&full[s], (i / p.nstages) & 1)) {
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
             return;
         }

@@ -41,6 +41,7 @@ cudaError_t launch_row_isums(uint32_t type, const void *w, uint64_t rows, uint64
 
 constexpr int MOE_MAX_K = 16;
 constexpr int MOE_MAX_CHUNKS = 64;
+constexpr int TRACE_SLOTS = 16;  // %globaltimer samples per CTA when tracing
 
 struct MoeParams {
     const uint8_t *const *experts;  // device table: gate_e, up_e, down_e per expert
@@ -54,6 +55,7 @@ struct MoeParams {
     volatile uint32_t *status;
     int32_t *dbg_ids;      // optional: routing decision (written by CTA 0)
     float *dbg_w;
+    uint64_t *trace;       // optional: TRACE_SLOTS timestamps per CTA
     int n_experts, H, F, K, norm, mode;
     uint32_t gate_type, up_type, down_type;
     uint32_t rbg, rbu, rbd;
@@ -64,6 +66,8 @@ struct MoeParams {
     uint32_t sa_bytes;     // phase-A staging capacity
     uint32_t sb_off, sb_bytes;
     uint32_t act_off, hact_off, misc_off, smem_bytes;
+    uint32_t dec_off, dec_row_bytes;  // decoded int8 down rows (q8_1 mode, Q6_K)
+    int dec_enabled;
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);

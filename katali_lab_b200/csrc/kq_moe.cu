@@ -4,22 +4,25 @@
 // sum; the reference ships that kernel only in binary form).
 //
 // B200 design: a persistent cooperative grid, one 16-warp CTA per SM.
-//  1. Every CTA routes redundantly (warp 0: softmax top-k over the router
-//     logits, deterministic ties) while warps 1-15 quantise x to q8_1 in shared
-//     memory.
+//  1. Every CTA routes redundantly (warp 0: top-k over the router logits held
+//     in registers, deterministic ties) while the other warps stage x in
+//     shared memory with one vector load per thread.
 //  2. Thread 0 then requests ALL of the CTA's expert bytes at once with
-//     cp.async.bulk into shared memory: its slice of the K*F gate/up row pairs
-//     (phase A, one mbarrier per chunk) and its slice of the H down rows for all
-//     K selected experts (phase B, one mbarrier). At the C2 shape (H 2048,
-//     F 512, top-8) that is ~110 KB per SM, so the whole 16.3 MB layer is in
-//     flight from the first microsecond.
-//  3. Phase A: a warp per row pair computes gate and up against q8_1(x) with
-//     DP4A, applies silu(g)*u and writes h to a small global scratch.
+//     cp.async.bulk (TMA, no multicast) into shared memory: its phase-A blocks
+//     (32 gate/up row pairs each, four 8-pair chunks with one mbarrier each)
+//     and its slice of the H down rows for all K selected experts (phase B, one
+//     mbarrier). At the C2 shape (H 2048, F 512, top-8) that is ~120 KB per
+//     SM, so the whole 16.3 MB layer is in flight from the start.
+//  3. Phase A: each warp computes two gate/up row pairs against q8_1(x) with
+//     DP4A; silu(g)*u lands in shared memory and the CTA quantises its
+//     32-value block of h to q8_1 itself, writing one 48-byte record.
 //  4. Grid barrier (one counter, bounded spin, error bit on timeout).
-//  5. Phase B: every CTA quantises h (K*F values, from L2) to q8_1, then a warp
-//     per output row dots the K down rows (already resident in shared memory)
-//     and forms sum_k w_k * down_k in a fixed order, so the output is
-//     deterministic and needs no atomics.
+//  5. Phase B: every CTA loads the K*F/32 h records (6 KB at C2) with one vector
+//     load per thread, then a warp per output row dots the K down rows
+//     (already in shared memory) and forms sum_k w_k * down_k in a fixed order:
+//     deterministic, no atomics.
+// Optional tracing: when p.trace is set, thread 0 of every CTA records
+// %globaltimer at the phase boundaries (TRACE_SLOTS per CTA).
 #include "kq_device.cuh"
 #include "kq_launch.h"
 
@@ -27,45 +30,124 @@ namespace kq {
 
 constexpr int MOE_WARPS = 16;
 constexpr int MOE_THREADS = MOE_WARPS * 32;
-
-struct Chunk {
-    uint32_t u0;   // first unit (row pair) of the chunk, global unit index
-    uint32_t n;    // units
-    uint32_t off;  // byte offset in the phase-A staging area
-    uint32_t pad;
-};
+constexpr int HB = 32;        // row pairs per phase-A block = one q8_1 block of h
+constexpr int HCH = 16;       // row pairs per TMA chunk
+constexpr int NCH = HB / HCH; // chunks per block
+constexpr int MAX_ABLK = 8;   // phase-A blocks per CTA
+constexpr int NBARS = MAX_ABLK * NCH + 1;
+constexpr int REC_BYTES = 48; // q8_1 record of h: 32 x int8, d, sum32, sum16[2]
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-
-__device__ __forceinline__ double dot_q8(uint32_t type, const uint8_t *row, int nb,
-                                         const ActQ8 &a, int lane) {
-    return type == T_Q4_K ? q4k_q8_partial(row, nb, a, lane) : q6k_q8_partial(row, nb, a, lane);
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ double dot_f32(uint32_t type, const uint8_t *row, int nb,
-                                          const float *x, const float *xs, int lane) {
-    return type == T_Q4_K ? q4k_f32_partial(row, nb, x, xs, lane)
-                          : q6k_f32_partial(row, nb, x, lane);
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace(const MoeParams &p, int slot) {
+    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * TRACE_SLOTS + slot] = globaltimer();
 }
 
 __device__ __forceinline__ void bulk_g2s_split(uint8_t *dst, const uint8_t *src, uint32_t bytes,
-                                               uint64_t *bar) {
+                                               uint64_t *bar, uint64_t pol) {
     while (bytes) {
         const uint32_t n = bytes > 32768u ? 32768u : bytes;
-        bulk_g2s(dst, src, n, bar);
+        bulk_g2s_hint(dst, src, n, bar, pol);
         dst += n;
         src += n;
         bytes -= n;
     }
 }
 
-// Softmax top-k by one warp: lane l owns logits [l*npl, (l+1)*npl). Each round
-// takes the largest remaining key; equal keys go to the lower expert id.
-__device__ void route_warp(const MoeParams &p, float *s_logits, int32_t *s_ids, float *s_w,
-                           int lane) {
+// Softmax weights of the chosen ids (lane 0 writes s_w); shared by both top-k paths.
+__device__ __forceinline__ void route_weights(const MoeParams &p, const float *lg, int npl,
+                                              int lane, int32_t *s_ids, float *s_w) {
+    const int n = p.n_experts, K = p.K;
+    const float m = __ldg(&p.logits[s_ids[0]]);
+    double S = 0.0;
+    if (!p.norm) {  // sum over all n logits (lane-owned contiguous ranges)
+        const int per = (n + 31) >> 5;
+        for (int i = 0; i < per; ++i) {
+            const int idx = lane * per + i;
+            if (idx < n) S += (double)kq_expf(__fsub_rn(lg ? lg[i] : __ldg(&p.logits[idx]), m));
+        }
+        S = warp_sum_d(S);
+    }
+    // lane t < K: e_t; every lane then sums e_0..e_{K-1} in order (the
+    // restatement's order) and lane t divides its own weight.
+    const float e = lane < K ? kq_expf(__fsub_rn(__ldg(&p.logits[s_ids[lane]]), m)) : 0.0f;
+    if (p.norm) {
+        S = 0.0;
+        for (int t = 0; t < K; ++t) S += (double)__shfl_sync(KQ_FULL, e, t);
+    }
+    if (lane < K) s_w[lane] = (float)((double)e / S);
+    __syncwarp();
+}
+
+// Composite routing key: order_key(logit) in the high word, ~id in the low word,
+// so a larger key is a larger logit or, for equal logits, a lower expert id.
+__device__ __forceinline__ uint64_t route_key(float f, int idx) {
+    return ((uint64_t)order_key(f) << 32) | (uint32_t)(~idx);
+}
+__device__ __forceinline__ void ce_desc(uint64_t &a, uint64_t &b) {
+    const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
+    a = hi;
+    b = lo;
+}
+
+// Top-k by one warp for n <= 256: lane l owns ids [8l, 8l+8), sorts its 8 keys
+// (Batcher odd-even merge network), then each round takes the warp maximum of
+// the lane heads with two redux steps and the winning lane pops its head.
+__device__ __forceinline__ void route_regs(const MoeParams &p, int lane, int32_t *s_ids,
+                                           float *s_w, bool weights) {
+    const int n = p.n_experts, K = p.K;
+    const int npl = (n + 31) >> 5;
+    uint64_t v[8];
+    if (n == 256) {  // two 16-byte loads per lane, contiguous across the warp
+        const float4 l0 = __ldg(reinterpret_cast<const float4 *>(p.logits) + 2 * lane);
+        const float4 l1 = __ldg(reinterpret_cast<const float4 *>(p.logits) + 2 * lane + 1);
+        const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = route_key(lv[i], 8 * lane + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = lane * npl + i;
+            v[i] = (i < npl && idx < n) ? route_key(__ldg(&p.logits[idx]), idx) : 0ull;
+        }
+    }
+    trace(p, 9);
+    ce_desc(v[0], v[1]); ce_desc(v[2], v[3]); ce_desc(v[4], v[5]); ce_desc(v[6], v[7]);
+    ce_desc(v[0], v[2]); ce_desc(v[1], v[3]); ce_desc(v[4], v[6]); ce_desc(v[5], v[7]);
+    ce_desc(v[1], v[2]); ce_desc(v[5], v[6]);
+    ce_desc(v[0], v[4]); ce_desc(v[1], v[5]); ce_desc(v[2], v[6]); ce_desc(v[3], v[7]);
+    ce_desc(v[2], v[4]); ce_desc(v[3], v[5]);
+    ce_desc(v[1], v[2]); ce_desc(v[3], v[4]); ce_desc(v[5], v[6]);
+    trace(p, 10);
+    for (int t = 0; t < K; ++t) {
+        const uint32_t hi = (uint32_t)(v[0] >> 32), lo = (uint32_t)v[0];
+        const uint32_t Mh = __reduce_max_sync(KQ_FULL, hi);
+        const uint32_t Ml = __reduce_max_sync(KQ_FULL, hi == Mh ? lo : 0u);
+        const bool won = (hi == Mh) && (lo == Ml) && (v[0] != 0ull);
+#pragma unroll
+        for (int i = 0; i < 7; ++i) v[i] = won ? v[i + 1] : v[i];
+        v[7] = won ? 0ull : v[7];
+        if (lane == 0) s_ids[t] = (int32_t)(~Ml);
+    }
+    __syncwarp();
+    trace(p, 11);
+    if (weights) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+}
+
+// Generic top-k for n_experts > 256: logits staged in shared memory.
+__device__ void route_smem(const MoeParams &p, float *s_logits, int32_t *s_ids, float *s_w,
+                           int lane, bool weights) {
     const int n = p.n_experts, K = p.K;
     for (int i = lane; i < n; i += 32) s_logits[i] = p.logits[i];
     __syncwarp();
@@ -92,54 +174,152 @@ __device__ void route_warp(const MoeParams &p, float *s_logits, int32_t *s_ids, 
         if (lane == 0) s_ids[t] = widx;
     }
     __syncwarp();
-    const float m = s_logits[s_ids[0]];
-    double S = 0.0;
-    if (!p.norm) {
-        for (int i = 0; i < npl; ++i) {
-            const int idx = lane * npl + i;
-            if (idx < n) S += (double)kq_expf(__fsub_rn(s_logits[idx], m));
-        }
-        S = warp_sum_d(S);
+    float lg[32];
+    for (int i = 0; i < npl; ++i) {
+        const int idx = lane * npl + i;
+        lg[i] = idx < n ? s_logits[idx] : 0.0f;
     }
-    if (lane == 0) {
-        float e[MOE_MAX_K];
-        for (int t = 0; t < K; ++t) e[t] = kq_expf(__fsub_rn(s_logits[s_ids[t]], m));
-        if (p.norm) {
-            S = 0.0;
-            for (int t = 0; t < K; ++t) S += (double)e[t];
-        }
-        for (int t = 0; t < K; ++t) s_w[t] = (float)((double)e[t] / S);
-    }
-    __syncwarp();
+    if (weights) route_weights(p, lg, npl, lane, s_ids, s_w);
 }
 
+__device__ __forceinline__ void route(const MoeParams &p, float *s_logits, int32_t *s_ids,
+                                      float *s_w, int lane, bool weights = true) {
+    if (p.n_experts <= 256) route_regs(p, lane, s_ids, s_w, weights);
+    else route_smem(p, s_logits, s_ids, s_w, lane, weights);
+}
+
+// This lane's Q4_K unit of x held in registers (phase A reuses it for every row).
+struct Q4Act {
+    uint4 a0, a1, a2, a3;
+    double dx0, dx1;
+    int xs0, xs1;
+};
+__device__ __forceinline__ Q4Act load_q4act(const ActQ8 &a, int u) {
+    const int g = 8 * (u >> 2) + 2 * (u & 3);
+    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + 32 * g);
+    return Q4Act{ap[0], ap[1], ap[2], ap[3], (double)a.d[g], (double)a.d[g + 1], a.s32[g], a.s32[g + 1]};
+}
+// q4k_q8_unit with register activations: identical terms.
+__device__ __forceinline__ double q4k_q8_unit_r(const uint8_t *row, int u, const Q4Act &A) {
+    const int b = u >> 2, c = u & 3;
+    const uint8_t *blk = row + Q4K_BYTES * b;
+    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
+    const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+    const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+    const uint32_t M = 0x0F0F0F0Fu;
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)(w0.x & M), (int)A.a0.x, lo);
+    hi = __dp4a((int)((w0.x >> 4) & M), (int)A.a2.x, hi);
+    lo = __dp4a((int)(w0.y & M), (int)A.a0.y, lo);
+    hi = __dp4a((int)((w0.y >> 4) & M), (int)A.a2.y, hi);
+    lo = __dp4a((int)(w0.z & M), (int)A.a0.z, lo);
+    hi = __dp4a((int)((w0.z >> 4) & M), (int)A.a2.z, hi);
+    lo = __dp4a((int)(w0.w & M), (int)A.a0.w, lo);
+    hi = __dp4a((int)((w0.w >> 4) & M), (int)A.a2.w, hi);
+    lo = __dp4a((int)(w1.x & M), (int)A.a1.x, lo);
+    hi = __dp4a((int)((w1.x >> 4) & M), (int)A.a3.x, hi);
+    lo = __dp4a((int)(w1.y & M), (int)A.a1.y, lo);
+    hi = __dp4a((int)((w1.y >> 4) & M), (int)A.a3.y, hi);
+    lo = __dp4a((int)(w1.z & M), (int)A.a1.z, lo);
+    hi = __dp4a((int)((w1.z >> 4) & M), (int)A.a3.z, hi);
+    lo = __dp4a((int)(w1.w & M), (int)A.a1.w, lo);
+    hi = __dp4a((int)((w1.w >> 4) & M), (int)A.a3.w, hi);
+    int sc0, m0, sc1, m1;
+    q4k_scales(h, c, sc0, m0, sc1, m1);
+    const double d = (double)h2f(h.x), dmin = (double)h2f(h.x >> 16);
+    return ((d * A.dx0) * (double)(sc0 * lo) - (dmin * A.dx0) * (double)(m0 * A.xs0)) +
+           ((d * A.dx1) * (double)(sc1 * hi) - (dmin * A.dx1) * (double)(m1 * A.xs1));
+}
+
+// Decode Q6_K unit u of a raw row (quarter pair {qo, qo+2} of half h of block b)
+// into its unsigned 6-bit values q at vals (element order), and, once per block,
+// its 16 int8 sub-scales and fp16 scale (as float).
+__device__ __forceinline__ void q6k_decode_unit(const uint8_t *row, int u, int8_t *vals,
+                                                int8_t *scales, float *dd) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
+    const uint8_t *blk = row + Q6K_BYTES * b;
+    uint32_t ql[8], qh[8];
+    load16_a2(blk + 64 * h + 32 * qo, ql);
+    load16_a2(blk + 64 * h + 32 * qo + 16, ql + 4);
+    load16_a2(blk + 128 + 32 * h, qh);
+    load16_a2(blk + 128 + 32 * h + 16, qh + 4);
+    const int shA = 2 * qo, shB = 2 * qo + 4;
+    uint32_t va[8], vb[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        va[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
+        vb[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
+    }
+    uint4 *da = reinterpret_cast<uint4 *>(vals + 256 * b + 128 * h + 32 * qo);
+    uint4 *db = reinterpret_cast<uint4 *>(vals + 256 * b + 128 * h + 32 * qo + 64);
+    da[0] = make_uint4(va[0], va[1], va[2], va[3]);
+    da[1] = make_uint4(va[4], va[5], va[6], va[7]);
+    db[0] = make_uint4(vb[0], vb[1], vb[2], vb[3]);
+    db[1] = make_uint4(vb[4], vb[5], vb[6], vb[7]);
+    if ((u & 3) == 0) {
+        uint32_t sc[4];
+        load16_a2(blk + 192, sc);
+        *reinterpret_cast<uint4 *>(scales + 16 * b) = make_uint4(sc[0], sc[1], sc[2], sc[3]);
+        dd[b] = h2f(ld_u16(blk + 208));
+    }
+}
+
+// Dot of 64 decoded elements [64u, 64u+64) of a row against q8_1 activations:
+// the same exact per-q8-block terms as q6k_q8_unit (sum (q-32)x = sum qx - 32 sum x).
+__device__ __forceinline__ double dec_q8_unit(const uint8_t *drow, int F, int u, const ActQ8 &a) {
+    const uint4 *w = reinterpret_cast<const uint4 *>(drow + 64 * u);
+    const uint4 *x = reinterpret_cast<const uint4 *>(a.q + 64 * u);
+    int s[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const uint4 wv = w[g], xv = x[g];
+        int acc = __dp4a((int)wv.x, (int)xv.x, 0);
+        acc = __dp4a((int)wv.y, (int)xv.y, acc);
+        acc = __dp4a((int)wv.z, (int)xv.z, acc);
+        s[g] = __dp4a((int)wv.w, (int)xv.w, acc);
+    }
+    const int8_t *sc = reinterpret_cast<const int8_t *>(drow + F) + 4 * u;
+    const float d = reinterpret_cast<const float *>(drow + F + F / 16)[u >> 2];
+    const int *x16 = a.s16 + 4 * u;
+    const int I0 = (int)sc[0] * (s[0] - 32 * x16[0]) + (int)sc[1] * (s[1] - 32 * x16[1]);
+    const int I1 = (int)sc[2] * (s[2] - 32 * x16[2]) + (int)sc[3] * (s[3] - 32 * x16[3]);
+    return ((double)d * (double)a.d[2 * u]) * (double)I0 +
+           ((double)d * (double)a.d[2 * u + 1]) * (double)I1;
+}
+
+template <int MODE, uint32_t DT>
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_constant__ MoeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int H = p.H, F = p.F, K = p.K;
+    trace(p, 0);
 
     uint8_t *sa = smem;
     uint8_t *sb = smem + p.sb_off;
     uint8_t *act = smem + p.act_off;
     uint8_t *hact = smem + p.hact_off;
     uint8_t *misc = smem + p.misc_off;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(misc);  // MOE_MAX_CHUNKS + 1
-    Chunk *chunks = reinterpret_cast<Chunk *>(misc + 8 * (MOE_MAX_CHUNKS + 1));
-    int32_t *s_ids = reinterpret_cast<int32_t *>(chunks + MOE_MAX_CHUNKS);
+    const uint8_t **s_tab = reinterpret_cast<const uint8_t **>(misc);  // 3 * n_experts pointers
+    uint64_t *bars = reinterpret_cast<uint64_t *>(misc + 24 * ((p.n_experts + 1) & ~1));
+    int32_t *s_ids = reinterpret_cast<int32_t *>(bars + NBARS + 1);
     float *s_w = reinterpret_cast<float *>(s_ids + MOE_MAX_K);
-    int *s_nch = reinterpret_cast<int *>(s_w + MOE_MAX_K);
-    float *s_logits = reinterpret_cast<float *>(s_nch + 4);
+    float *s_h = s_w + MOE_MAX_K;                                   // MAX_ABLK * HB floats
+    uint8_t *s_rec = reinterpret_cast<uint8_t *>(s_h + MAX_ABLK * HB);  // MAX_ABLK * REC_BYTES
+    float *s_logits = reinterpret_cast<float *>(s_rec + MAX_ABLK * REC_BYTES);
 
-    const uint32_t U = (uint32_t)K * F;
-    const uint32_t u0 = (uint32_t)((uint64_t)U * c / G), u1 = (uint32_t)((uint64_t)U * (c + 1) / G);
+    const uint32_t BA = (uint32_t)K * F / HB;  // phase-A blocks
+    const uint32_t b0 = (uint32_t)((uint64_t)BA * c / G), b1 = (uint32_t)((uint64_t)BA * (c + 1) / G);
+    const int nbA = (int)(b1 - b0);
     const uint32_t Q = (uint32_t)H / p.rg;  // phase-B row groups (16-byte aligned copies)
     const uint32_t q0 = (uint32_t)((uint64_t)Q * c / G), q1 = (uint32_t)((uint64_t)Q * (c + 1) / G);
     const uint32_t rB0 = p.rg * q0, nrB = p.rg * (q1 - q0);
+    const uint32_t rbg = p.rbg, rbu = p.rbu, rbd = p.rbd;
+    const uint32_t blk_bytes = HB * (rbg + rbu);
 
     if (p.route_only) {  // check entry point: the routing decision only
         if (warp == 0) {
-            route_warp(p, s_logits, s_ids, s_w, lane);
+            route(p, s_logits, s_ids, s_w, lane);
             if (c == 0 && lane < K) {
                 p.dbg_ids[lane] = s_ids[lane];
                 p.dbg_w[lane] = s_w[lane];
@@ -147,18 +327,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
         return;
     }
-    if (tid == 0) {
-        for (int i = 0; i <= MOE_MAX_CHUNKS; ++i) mbar_init(&bars[i], 1);
+    if (tid == 32) {  // warp 1: keep warp 0 free for routing
+        for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
 
-    // ---- 1. routing (warp 0) and x staging (warps 1..) ----------------------
-    int8_t *xq = reinterpret_cast<int8_t *>(act);
-    float *xd = reinterpret_cast<float *>(act + H);
+    // ---- 1. routing (warp 0) and x staging (all other threads) --------------
+    float *xf = reinterpret_cast<float *>(act);  // fp32 x, H floats
+    int8_t *xq = reinterpret_cast<int8_t *>(act + 4 * H);
+    float *xd = reinterpret_cast<float *>(act + 5 * H);
     int *xs32 = reinterpret_cast<int *>(xd + H / 32);
     int *xs16 = xs32 + H / 32;
-    float *xf = reinterpret_cast<float *>(act);
-    float *xfs = xf + H;
+    float *xfs = reinterpret_cast<float *>(act + 4 * H);  // fp32 mode: per-32 sums
     if (warp == 0) {
         if (p.ids) {
             if (lane < K) {
@@ -167,160 +347,242 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             }
             __syncwarp();
         } else {
-            route_warp(p, s_logits, s_ids, s_w, lane);
+            route(p, s_logits, s_ids, s_w, lane, false);  // weights after the copies are issued
         }
-    } else if (p.mode == 0) {
-        for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1)
-            quant_block_q8(__ldg(&p.x[32 * g + lane]), lane, xq + 32 * g, xd + g, xs32 + g,
-                           xs16 + 2 * g, nullptr);
+        trace(p, 1);
     } else {
         for (int i = tid - 32; i < H / 4; i += MOE_THREADS - 32)
             reinterpret_cast<float4 *>(xf)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
+        const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
+        for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
+            reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
     }
     __syncthreads();
-    if (p.mode != 0 && warp > 0) {
+    trace(p, 2);
+
+    // ---- 2. request every expert byte this CTA needs (warp 0, one copy per lane) ----
+    if (warp == 0) {
+        const uint64_t pol = l2_evict_first_policy();
+        const int nchunk = nbA * NCH;
+        const uint32_t per = nrB * rbd;
+        if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
+        if (lane == 31 && nrB) mbar_arrive_expect_tx(&bars[NBARS - 1], per * (uint32_t)K);
+        __syncwarp();
+        const int nB = nrB ? K : 0;
+        const int ncopy = 2 * nchunk + nB;
+        // Down rows first: they are decoded while the gate/up rows are still arriving.
+        for (int q0 = lane; q0 < ncopy; q0 += 32) {
+            const int q = q0 < nB ? 2 * nchunk + q0 : q0 - nB;
+            if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
+                const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
+                const uint32_t blk = b0 + a;
+                const int k = (int)(blk / (F / HB));
+                const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
+                const uint32_t rb = up ? rbu : rbg;
+                const uint8_t *src = s_tab[3 * s_ids[k] + up] + (size_t)j0 * rb;
+                uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
+                bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol);
+            } else {  // down rows [rB0, rB0 + nrB) of selected expert k
+                const int k = q - 2 * nchunk;
+                bulk_g2s_split(sb + (size_t)k * (per + 16), s_tab[3 * s_ids[k] + 2] + (size_t)rB0 * rbd,
+                               per, &bars[NBARS - 1], pol);
+            }
+        }
+        trace(p, 3);
+        if (!p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+    } else if (warp > 0) {
         for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
-            const float v = warp_sum_f(xf[32 * g + lane]);
-            if (lane == 0) xfs[g] = v;
-        }
-    }
-    // ---- 2. request every expert byte this CTA needs ------------------------
-    if (tid == 0) {
-        int nch = 0;
-        uint32_t off = 0;
-        for (uint32_t u = u0; u < u1;) {
-            const uint32_t k = u / F, j = u % F;
-            uint32_t n = u1 - u;
-            if (n > p.chunk_units) n = p.chunk_units;
-            if (n > (uint32_t)F - j) n = (uint32_t)F - j;
-            const int e = s_ids[k];
-            const uint8_t *gsrc = p.experts[3 * e] + (size_t)j * p.rbg;
-            const uint8_t *usrc = p.experts[3 * e + 1] + (size_t)j * p.rbu;
-            const uint32_t gb = n * p.rbg, ub = n * p.rbu;
-            mbar_arrive_expect_tx(&bars[nch], gb + ub);
-            bulk_g2s_split(sa + off, gsrc, gb, &bars[nch]);
-            bulk_g2s_split(sa + off + gb, usrc, ub, &bars[nch]);
-            chunks[nch] = Chunk{u, n, off, 0};
-            off += gb + ub;
-            ++nch;
-            u += n;
-        }
-        *s_nch = nch;
-        if (nrB) {
-            const uint32_t per = nrB * p.rbd;
-            mbar_arrive_expect_tx(&bars[MOE_MAX_CHUNKS], per * (uint32_t)K);
-            for (int k = 0; k < K; ++k)
-                bulk_g2s_split(sb + (size_t)k * per, p.experts[3 * s_ids[k] + 2] + (size_t)rB0 * p.rbd,
-                               per, &bars[MOE_MAX_CHUNKS]);
+            const float v = xf[32 * g + lane];
+            if (MODE == 0) {
+                quant_block_q8(v, lane, xq + 32 * g, xd + g, xs32 + g, xs16 + 2 * g, nullptr);
+            } else {
+                const float s = warp_sum_f(v);
+                if (lane == 0) xfs[g] = s;
+            }
         }
     }
     __syncthreads();
 
-    // ---- 3. phase A: gate/up row pairs -> h = silu(g) * u --------------------
+    // ---- 3. phase A: gate/up row pairs -> h = silu(g) * u, quantised per block --
     bool ok = true;
-    {
-        const int nbh = H / 256;
-        const ActQ8 ax{xq, xd, xs32, xs16};
-        int ci = 0;
-        for (uint32_t v = u0 + warp; v < u1; v += MOE_WARPS) {
-            while (v >= chunks[ci].u0 + chunks[ci].n) ++ci;
-            const Chunk ch = chunks[ci];
-            if (!mbar_wait(&bars[ci], 0)) {
-                ok = false;
-                break;
-            }
-            const uint32_t jj = v - ch.u0;
-            const uint8_t *grow = sa + ch.off + (size_t)jj * p.rbg;
-            const uint8_t *urow = sa + ch.off + (size_t)ch.n * p.rbg + (size_t)jj * p.rbu;
-            double pg, pu;
-            if (p.mode == 0) {
-                pg = dot_q8(p.gate_type, grow, nbh, ax, lane);
-                pu = dot_q8(p.up_type, urow, nbh, ax, lane);
-            } else {
-                pg = dot_f32(p.gate_type, grow, nbh, xf, xfs, lane);
-                pu = dot_f32(p.up_type, urow, nbh, xf, xfs, lane);
-            }
-            pg = warp_sum_d(pg);
-            pu = warp_sum_d(pu);
-            if (lane == 0) {
-                const float g = (float)pg, u = (float)pu;
-                p.hbuf[v] = __fmul_rn(kq_silu(g), u);  // unit v = k*F + j
-            }
+    const int nbh = H / 256;
+    const ActQ8 ax{xq, xd, xs32, xs16};
+    Q4Act xr;
+    if (MODE == 0 && nbh == 8 && nbA > 0) xr = load_q4act(ax, lane);  // this lane's unit of x
+    for (int a = 0; a < nbA; ++a) {
+        const uint8_t *base = sa + (size_t)a * blk_bytes;
+        const int p0 = warp, p1 = warp + MOE_WARPS;  // two row pairs per warp
+        ok &= mbar_wait_warp(&bars[a * NCH + p0 / HCH], 0);
+        if (a == 0) trace(p, 4);
+        ok &= mbar_wait_warp(&bars[a * NCH + p1 / HCH], 0);
+        if (a == 0) trace(p, 12);
+        const uint8_t *g0 = base + (size_t)p0 * rbg, *g1 = base + (size_t)p1 * rbg;
+        const uint8_t *u0 = base + (size_t)HB * rbg + (size_t)p0 * rbu;
+        const uint8_t *u1 = base + (size_t)HB * rbg + (size_t)p1 * rbu;
+        double pg0, pu0, pg1, pu1;
+        if (MODE == 0 && nbh == 8) {
+            pg0 = q4k_q8_unit_r(g0, lane, xr);
+            pu0 = q4k_q8_unit_r(u0, lane, xr);
+            pg1 = q4k_q8_unit_r(g1, lane, xr);
+            pu1 = q4k_q8_unit_r(u1, lane, xr);
+        } else if (MODE == 0) {
+            pg0 = q4k_q8_partial(g0, nbh, ax, lane);
+            pu0 = q4k_q8_partial(u0, nbh, ax, lane);
+            pg1 = q4k_q8_partial(g1, nbh, ax, lane);
+            pu1 = q4k_q8_partial(u1, nbh, ax, lane);
+        } else {
+            pg0 = q4k_f32_partial(g0, nbh, xf, xfs, lane);
+            pu0 = q4k_f32_partial(u0, nbh, xf, xfs, lane);
+            pg1 = q4k_f32_partial(g1, nbh, xf, xfs, lane);
+            pu1 = q4k_f32_partial(u1, nbh, xf, xfs, lane);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            pg0 += __shfl_xor_sync(KQ_FULL, pg0, o);
+            pu0 += __shfl_xor_sync(KQ_FULL, pu0, o);
+            pg1 += __shfl_xor_sync(KQ_FULL, pg1, o);
+            pu1 += __shfl_xor_sync(KQ_FULL, pu1, o);
+        }
+        if (lane == 0) {
+            s_h[a * HB + p0] = __fmul_rn(kq_silu((float)pg0), (float)pu0);
+            s_h[a * HB + p1] = __fmul_rn(kq_silu((float)pg1), (float)pu1);
         }
     }
     if (!ok && lane == 0) *p.status |= ERR_TIMEOUT_TMA;
+    trace(p, 5);
+    __syncthreads();
+    if (warp < nbA) {  // one warp per block: publish h as a q8_1 record (fp32 in mode 1)
+        const int a = warp;
+        const float v = s_h[a * HB + lane];
+        const uint32_t blk = b0 + a;
+        if (MODE == 0) {
+            uint8_t *r = s_rec + a * REC_BYTES;
+            float *md = reinterpret_cast<float *>(r + 32);
+            int *ms = reinterpret_cast<int *>(r + 36);
+            quant_block_q8(v, lane, reinterpret_cast<int8_t *>(r), md, ms, ms + 1, nullptr);
+            __syncwarp();
+            if (lane < 3)
+                reinterpret_cast<uint4 *>(p.hbuf)[3 * blk + lane] =
+                    reinterpret_cast<const uint4 *>(r)[lane];
+        } else {
+            p.hbuf[HB * blk + lane] = v;
+        }
+    }
 
-    // ---- 4. grid barrier ----------------------------------------------------
+    // ---- 4. grid barrier: arrive, decode the down rows while waiting, then wait ----
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        atomicAdd(&p.sync[0], 1u);
+        red_release_gpu_add(&p.sync[0], 1u);
+    }
+    const bool predecode = MODE == 0 && DT == T_Q6_K && p.dec_enabled && nrB != 0;
+    uint8_t *sdec = smem + p.dec_off;
+    const uint32_t drb = p.dec_row_bytes;
+    const uint32_t dstride = nrB * drb + 16;  // padded decoded expert stride
+    if (predecode) {
+        if (!mbar_wait_warp(&bars[NBARS - 1], 0)) {
+            if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
+        } else {
+            trace(p, 13);
+            const int upr = F / 64;  // units per row
+            const int total = K * (int)nrB * upr;
+            for (int t = tid; t < total; t += MOE_THREADS) {
+                const int u = t % upr, r = t / upr, kk = r / (int)nrB, rr = r - kk * (int)nrB;
+                uint8_t *drow = sdec + (size_t)kk * dstride + (size_t)rr * drb;
+                q6k_decode_unit(sb + (size_t)kk * (nrB * rbd + 16) + (size_t)rr * rbd, u,
+                                reinterpret_cast<int8_t *>(drow),
+                                reinterpret_cast<int8_t *>(drow + F),
+                                reinterpret_cast<float *>(drow + F + F / 16));
+            }
+        }
+    }
+    trace(p, 14);
+    if (tid == 0) {
         uint32_t it = 0;
         while (ld_acquire_gpu(&p.sync[0]) < G) {
             if (++it > SPIN_LIMIT) {
                 *p.status |= ERR_TIMEOUT_GRID;
                 break;
             }
-            __nanosleep(32);
+            if (it > 32) __nanosleep(20);
         }
     }
     __syncthreads();
+    trace(p, 6);
 
-    // ---- 5. phase B: quantise h, then the K down rows per output row ---------
-    int8_t *hq = reinterpret_cast<int8_t *>(hact);
-    float *hd = reinterpret_cast<float *>(hact + (size_t)K * F);
+    // ---- 5. load h for phase B ------------------------------------------------
+    int8_t *hq = reinterpret_cast<int8_t *>(hact);  // expert stride F + 16 (bank spread)
+    float *hd = reinterpret_cast<float *>(hact + (size_t)K * (F + 16));
     int *hs32 = reinterpret_cast<int *>(hd + (size_t)K * F / 32);
     int *hs16 = hs32 + (size_t)K * F / 32;
     float *hf = reinterpret_cast<float *>(hact);
     float *hfs = hf + (size_t)K * F;
-    const int nblk = K * F / 32;
-    for (int g = warp; g < nblk; g += MOE_WARPS) {
-        const float v = __ldcg(&p.hbuf[32 * g + lane]);
-        if (p.mode == 0) {
-            quant_block_q8(v, lane, hq + 32 * g, hd + g, hs32 + g, hs16 + 2 * g, nullptr);
-        } else {
-            hf[32 * g + lane] = v;
-            const float s = warp_sum_f(v);
+    if (MODE == 0) {
+        const int nrec = (int)BA;
+        for (int t = tid; t < 3 * nrec; t += MOE_THREADS) {
+            const int r = t / 3, part = t - 3 * r;
+            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.hbuf) + t);
+            if (part < 2) {
+                const int kk = r / (F / HB), jb = r - kk * (F / HB);
+                reinterpret_cast<uint4 *>(hq + (size_t)kk * (F + 16) + HB * jb)[part] = v;
+            } else {
+                hd[r] = __uint_as_float(v.x);
+                hs32[r] = (int)v.y;
+                hs16[2 * r] = (int)v.z;
+                hs16[2 * r + 1] = (int)v.w;
+            }
+        }
+    } else {
+        for (int t = tid; t < K * F / 4; t += MOE_THREADS)
+            reinterpret_cast<float4 *>(hf)[t] = __ldcg(reinterpret_cast<const float4 *>(p.hbuf) + t);
+        __syncthreads();
+        for (int g = warp; g < K * F / 32; g += MOE_WARPS) {
+            const float s = warp_sum_f(hf[32 * g + lane]);
             if (lane == 0) hfs[g] = s;
         }
     }
     __syncthreads();
 
+    // ---- 6. phase B: K down rows per output row, fixed-order weighted sum ------
     if (nrB) {
-        if (!mbar_wait(&bars[MOE_MAX_CHUNKS], 0)) {
+        if (!predecode && !mbar_wait_warp(&bars[NBARS - 1], 0)) {
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
         } else {
-            const int nbf = F / 256;
-            const uint32_t per = nrB * p.rbd;
+            trace(p, 7);
+            // lanes per expert: 32 / next_pow2(K); lane = (expert k, slot g)
+            int kp2 = 1;
+            while (kp2 < K) kp2 <<= 1;
+            const int lpe = 32 / kp2, k = lane / lpe, g = lane % lpe;
+            const int nunits = 4 * (F / 256);
+            const uint32_t per = nrB * rbd;
+            const ActQ8 ah{hq + (size_t)k * (F + 16), hd + (size_t)k * F / 32,
+                           hs32 + (size_t)k * F / 32, hs16 + (size_t)k * F / 16};
+            const double wk = k < K ? (double)s_w[k] : 0.0;
             for (uint32_t rr = warp; rr < nrB; rr += MOE_WARPS) {
-                double part[MOE_MAX_K];
-#pragma unroll
-                for (int k = 0; k < MOE_MAX_K; ++k) {
-                    if (k < K) {
-                        const uint8_t *row = sb + (size_t)k * per + (size_t)rr * p.rbd;
-                        if (p.mode == 0) {
-                            const ActQ8 ah{hq + (size_t)k * F, hd + (size_t)k * F / 32,
-                                           hs32 + (size_t)k * F / 32, hs16 + (size_t)k * F / 16};
-                            part[k] = dot_q8(p.down_type, row, nbf, ah, lane);
-                        } else {
-                            part[k] = dot_f32(p.down_type, row, nbf, hf + (size_t)k * F,
-                                              hfs + (size_t)k * F / 32, lane);
+                double part = 0.0;
+                if (k < K) {
+                    if (predecode) {
+                        const uint8_t *drow = sdec + (size_t)k * dstride + (size_t)rr * drb;
+                        for (int u = g; u < nunits; u += lpe) part += dec_q8_unit(drow, F, u, ah);
+                    } else {
+                        const uint8_t *row = sb + (size_t)k * (per + 16) + (size_t)rr * rbd;
+                        for (int u = g; u < nunits; u += lpe) {
+                            if (MODE == 0) part += unit_q8<DT>(row, u, ah);
+                            else part += unit_f32<DT>(row, u, hf + (size_t)k * F, hfs + (size_t)k * F / 32);
                         }
                     }
                 }
-#pragma unroll
-                for (int k = 0; k < MOE_MAX_K; ++k)
-                    if (k < K) part[k] = warp_sum_d(part[k]);
-                if (lane == 0) {
-                    double acc = 0.0;
-                    for (int k = 0; k < K; ++k) acc += (double)s_w[k] * (double)(float)part[k];
-                    p.y[rB0 + rr] = (float)acc;
-                }
+                if (rr == 0) trace(p, 15);
+                for (int o = 1; o < lpe; o <<= 1) part += __shfl_xor_sync(KQ_FULL, part, o);
+                double t = k < K ? wk * (double)(float)part : 0.0;
+                for (int o = lpe; o < 32; o <<= 1) t += __shfl_xor_sync(KQ_FULL, t, o);
+                if (lane == 0) p.y[rB0 + rr] = (float)t;
             }
         }
     }
+    trace(p, 8);
 
-    // ---- 6. the last CTA out re-arms the barrier counters --------------------
+    // ---- 7. the last CTA out re-arms the barrier counters --------------------
     __syncthreads();
     if (tid == 0) {
         const uint32_t prev = atomicAdd(&p.sync[1], 1u);
@@ -336,13 +598,12 @@ static inline uint32_t al128(uint32_t v) { return (v + 127u) & ~127u; }
 // Shared-memory plan for `grid` CTAs. Returns 0, or -1 when the layer does not
 // fit (the caller reports KATALI_ERR_UNSUPPORTED_SHAPE).
 int moe_plan(MoeParams &p, int grid, int max_smem) {
-    const uint32_t U = (uint32_t)p.K * p.F;
-    const uint32_t upc = (U + grid - 1) / grid;
-    uint32_t ch = (upc + 15) / 16;
-    if (ch < 4) ch = 4;
-    p.chunk_units = ch;
-    if ((upc + ch - 1) / ch + (uint32_t)p.K + 1 > (uint32_t)MOE_MAX_CHUNKS) return -1;
-    p.sa_bytes = upc * (p.rbg + p.rbu);
+    if (p.gate_type != T_Q4_K || p.up_type != T_Q4_K) return -1;
+    if (p.down_type != T_Q4_K && p.down_type != T_Q6_K) return -1;
+    const uint32_t BA = (uint32_t)p.K * p.F / HB;
+    const uint32_t maxA = (BA + grid - 1) / grid;
+    if (maxA > (uint32_t)MAX_ABLK) return -1;
+    p.sa_bytes = maxA * HB * (p.rbg + p.rbu);
     p.sb_off = al128(p.sa_bytes);
     uint32_t rg = 16;  // rows per phase-B group: 16 / gcd(rbd, 16)
     for (uint32_t v = p.rbd; v % 2 == 0 && rg > 1; v /= 2) rg /= 2;
@@ -350,25 +611,42 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     p.rg = rg;
     const uint32_t Q = (uint32_t)p.H / rg;
     const uint32_t qpc = (Q + grid - 1) / grid;
-    p.sb_bytes = (uint32_t)p.K * rg * qpc * p.rbd;
+    p.sb_bytes = (uint32_t)p.K * (rg * qpc * p.rbd + 16);
     p.act_off = al128(p.sb_off + p.sb_bytes);
-    const uint32_t act = p.mode == 0 ? p.H + p.H / 32 * 8 + p.H / 16 * 4 : p.H * 4 + p.H / 32 * 4;
+    const uint32_t act = p.mode == 0 ? 5 * p.H + p.H / 32 * 16 : 4 * p.H + p.H / 32 * 4;
     p.hact_off = al128(p.act_off + act);
     const uint32_t KF = (uint32_t)p.K * p.F;
-    const uint32_t hact = p.mode == 0 ? KF + KF / 32 * 8 + KF / 16 * 4 : KF * 4 + KF / 32 * 4;
+    const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16 : KF * 4 + KF / 32 * 4;
     p.misc_off = al128(p.hact_off + hact);
-    const uint32_t misc = 8 * (MOE_MAX_CHUNKS + 1) + (uint32_t)sizeof(Chunk) * MOE_MAX_CHUNKS +
-                          4 * MOE_MAX_K * 2 + 16 + 4 * (uint32_t)p.n_experts;
+    const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * (NBARS + 1) +
+                          8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
+                          4 * (uint32_t)p.n_experts;
     p.smem_bytes = al128(p.misc_off + misc);
+    // Decoded int8 down rows (Q6_K, q8_1 mode): reuse the phase-A staging area
+    // when it is large enough (phase A is finished by then), else append.
+    p.dec_off = 0;
+    p.dec_enabled = 0;
+    p.dec_row_bytes = (uint32_t)((p.F + p.F / 16 + 4 * (p.F / 256) + 15) & ~15);
+    if (p.mode == 0 && p.down_type == T_Q6_K) {
+        const uint32_t need = (uint32_t)p.K * (rg * qpc * p.dec_row_bytes + 16);
+        if (need <= p.sa_bytes) {
+            p.dec_off = 0;  // the phase-A staging area
+            p.dec_enabled = 1;
+        } else if (al128(p.smem_bytes) + need <= (uint32_t)max_smem) {
+            p.dec_off = al128(p.smem_bytes);
+            p.smem_bytes = al128(p.dec_off + need);
+            p.dec_enabled = 1;
+        }
+    }
     return p.smem_bytes <= (uint32_t)max_smem ? 0 : -1;
 }
 
-cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
-    // Raise the dynamic shared-memory limit once per size (never during a graph capture
-    // that follows a first eager call with the same plan).
-    static uint32_t set_bytes = 0;
+template <int MODE, uint32_t DT>
+static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
+    static uint32_t set_bytes = 0;  // raise the smem limit once per size, before any capture
     if (p.smem_bytes > set_bytes) {
-        cudaError_t e = cudaFuncSetAttribute(moe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)p.smem_bytes);
         if (e != cudaSuccess) return e;
         set_bytes = p.smem_bytes;
@@ -383,7 +661,13 @@ cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
     attr[0].val.cooperative = p.route_only ? 0 : 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_kernel, p);
+    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT>, p);
+}
+
+cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
+    if (p.mode == 0)
+        return p.down_type == T_Q6_K ? launch_t<0, T_Q6_K>(p, grid, st) : launch_t<0, T_Q4_K>(p, grid, st);
+    return p.down_type == T_Q6_K ? launch_t<1, T_Q6_K>(p, grid, st) : launch_t<1, T_Q4_K>(p, grid, st);
 }
 
 }  // namespace kq

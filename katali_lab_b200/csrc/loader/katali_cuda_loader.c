@@ -64,7 +64,8 @@
        int32_t *xs),                                                                          \
       (t, w, r, c, q, is, xs))                                                                \
     X(int, katali_cuda_debug_route, (KataliMoe * m, const float *l, int32_t *i, float *w),    \
-      (m, l, i, w))
+      (m, l, i, w))                                                                           \
+    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))
 
 #define DECLARE_PTR(ret, name, params, args) static ret(*p_##name) params;
 KATALI_FN_LIST(DECLARE_PTR)
@@ -163,7 +164,8 @@ const char *katali_cuda_strerror(int s) {
        int32_t *xs),                                                                          \
       (t, w, r, c, q, is, xs))                                                                \
     X(int, katali_cuda_debug_route, (KataliMoe * m, const float *l, int32_t *i, float *w),    \
-      (m, l, i, w))
+      (m, l, i, w))                                                                           \
+    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))
 KATALI_INT_FN_LIST(FORWARD)
 
 int katali_cuda_supports_type(uint32_t t) { return resolve() ? p_katali_cuda_supports_type(t) : 0; }

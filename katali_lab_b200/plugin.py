@@ -89,6 +89,7 @@ class Plugin:
             "katali_cuda_moe_layer_routed": ([_vp, _vp, _vp, _vp, _vp, _u32], _i32),
             "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),
+            "katali_cuda_debug_moe_trace": ([_vp, _vp, C.POINTER(_i32)], _i32),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)
@@ -166,6 +167,13 @@ class MoeLayer:
 
     def route(self, logits, ids, w) -> None:
         self.p.check(self.p.L.katali_cuda_debug_route(self.h, _ptr(logits), _ptr(ids), _ptr(w)))
+
+    def set_trace(self, buf) -> int:
+        """Record per-CTA phase timestamps into `buf` (uint64 CUDA tensor, >= grid*16
+        entries, zeroed) on later calls; None switches it off. Returns the grid size."""
+        g = _i32()
+        self.p.check(self.p.L.katali_cuda_debug_moe_trace(self.h, _ptr(buf), C.byref(g)))
+        return g.value
 
     def set_expert(self, e, gate, up, down) -> None:
         self.p.check(self.p.L.katali_cuda_moe_set_expert(self.h, e, int(gate), int(up), int(down)))
