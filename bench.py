@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2", choices=["c2", "c1"],
+                    help="c2: fused MoE layer (headline); c1: dense Q4_K GEMV 6144x2048")
+    ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -393,6 +396,117 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
         print(f"[trace]   {TRACE_NAMES[s]:20s} {v:.2f}", file=sys.stderr)
 
 
+C1_ROWS, C1_COLS = 6144, 2048
+C1_BYTES = C1_ROWS * (C1_COLS // 256 * 144)  # 7,077,888 B of Q4_K weights per call
+C1_WORKLOAD = ("C1 dense Q4_K GEMV, batch 1: W 6144x2048 from N(0,0.02) (seed 0) encoded to Q4_K, "
+               "x N(0,1) fp32 len 2048, y fp32 len 6144")
+
+
+def run_c1(args, rank, world, local_rank):
+    """C1: katali_cuda_matvec (the reference's drop-in entry) over 64 distinct weight copies
+    (453 MB, far larger than L2), one call per copy per step."""
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import Q4_K, Plugin
+    from katali_lab_b200.synth import make_dense
+    if args.dp4a:
+        os.environ["KATALI_CUDA_DP4A"] = "1"
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    plugin.set_stream(stream)
+    T = args.calls
+    ws = [make_dense(plugin, Q4_K, C1_ROWS, C1_COLS, seed=(0 if i == 0 else 1000 + i)) for i in range(T)]
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    xs = torch.randn((T, C1_COLS), generator=g, device="cuda")
+    ys = torch.empty((T, C1_ROWS), device="cuda")
+    plugin.set_async(True)
+
+    def step():
+        for i in range(T):
+            plugin.matvec(Q4_K, ws[i], C1_ROWS, C1_COLS, xs[i], ys[i])
+
+    step()
+    plugin.sync()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        plugin.set_stream(torch.cuda.current_stream())
+        step()
+    plugin.set_stream(stream)
+    for _ in range(max(args.warmup, 3)):
+        gr.replay()
+    plugin.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        s0.record(stream)
+        for _ in range(args.steps):
+            gr.replay()
+        s1.record(stream)
+        s1.synchronize()
+    plugin.sync()
+    ms = s0.elapsed_time(s1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_call = 1e3 * ms / (args.steps * T)
+    value = world * C1_BYTES / (us_call * 1e-6) / 1e9
+    # e2e: the reference's own per-projection sequence (upload x, matvec, download y)
+    xh = torch.randn(C1_COLS).pin_memory()
+    yh = torch.empty(C1_ROWS).pin_memory()
+    plugin.set_async(False)
+    L_ = plugin.L
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = min(T, 64) * args.steps
+    e0.record(stream)
+    for i in range(n_e2e):
+        plugin.check(L_.katali_cuda_upload(xs[i % T].data_ptr(), xh.data_ptr(), C1_COLS * 4))
+        plugin.matvec(Q4_K, ws[i % T], C1_ROWS, C1_COLS, xs[i % T], ys[i % T])
+        plugin.check(L_.katali_cuda_download(yh.data_ptr(), ys[i % T].data_ptr(), C1_ROWS * 4))
+    e1.record(stream)
+    e1.synchronize()
+    e2e_value = world * C1_BYTES * n_e2e / (e0.elapsed_time(e1) / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        from oracle.oracle import Ref
+        ref = Ref()
+        wh = [w.cpu().numpy() for w in ws[:8]]
+        xv = xs[0].cpu().numpy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < args.cpu_seconds or n < 8:
+            ref.matvec(Q4_K, wh[n % 8], C1_ROWS, C1_COLS, xv, n_threads=os.cpu_count() or 1)
+            n += 1
+        el = time.perf_counter() - t0
+        cpu = {"value": round(n * C1_BYTES / el / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(),
+               "kind": "reference", "sample": f"{n} katali_ggml_matvec calls ({el:.1f} s) over 8 weight "
+                                               f"copies, {os.cpu_count()} threads"}
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = C1_BYTES / (us_call * 1e-6) / 1e9
+        print(json.dumps({
+            "metric": "dense Q4_K GEMV quant-weight GB/s vs HBM peak", "value": round(value, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32", "data": "synthetic",
+            "config": {"workload": C1_WORKLOAD, "calls_per_step": T, "activations": "q8_1" if args.dp4a else "fp32",
+                       "l2": "inputs larger than L2: 64 weight copies (453 MB) rotated per call",
+                       "us_per_call": round(us_call, 3)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "algorithmic_bytes_per_launch": C1_BYTES},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": C1_COLS * 4,
+                    "d2h_bytes_per_step": C1_ROWS * 4},
+            "gpu_launches": args.steps * T, "cpu_baseline": cpu}), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -410,7 +524,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.config == "c1":
+            run_c1(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
