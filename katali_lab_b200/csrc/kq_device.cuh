@@ -216,7 +216,12 @@ struct ActQ8 {
     const float *d;
     const int *s32;
     const int *s16;
+    int pad;  // 1: q holds element e at e + 16 * (e / 64) (bank-spread layout)
 };
+// Position of q8 activation element e (a multiple of 16) in an ActQ8 array.
+__device__ __forceinline__ int qpos(const ActQ8 &a, int e) { return e + (a.pad ? ((e >> 6) << 4) : 0); }
+// fp32 activations staged with the same spreading: element e at e + 4 * (e / 64).
+__device__ __forceinline__ int fpos(int pad, int e) { return e + (pad ? ((e >> 6) << 2) : 0); }
 
 // ---------------------------------------------------------------------------
 // Block dots by "unit": 64 consecutive elements of a row whose bytes one lane
@@ -236,7 +241,7 @@ __device__ __forceinline__ double q4k_q8_unit(const uint8_t *row, int u, const A
     const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
     const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
     const int g = 8 * b + 2 * c;
-    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + 32 * g);
+    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * g));
     const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
     const uint32_t M = 0x0F0F0F0Fu;
     int lo = 0, hi = 0;
@@ -273,8 +278,8 @@ __device__ __forceinline__ double q6k_q8_unit(const uint8_t *row, int u, const A
     load16_a2(blk + 128 + 32 * h, qh);
     load16_a2(blk + 128 + 32 * h + 16, qh + 4);
     const int jA = 8 * b + 4 * h + qo, jB = jA + 2;
-    const uint4 *aA = reinterpret_cast<const uint4 *>(a.q + 32 * jA);
-    const uint4 *aB = reinterpret_cast<const uint4 *>(a.q + 32 * jB);
+    const uint4 *aA = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * jA));
+    const uint4 *aB = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * jB));
     const uint4 xA0 = aA[0], xA1 = aA[1], xB0 = aB[0], xB1 = aB[1];
     const uint32_t wa[8] = {xA0.x, xA0.y, xA0.z, xA0.w, xA1.x, xA1.y, xA1.z, xA1.w};
     const uint32_t wb[8] = {xB0.x, xB0.y, xB0.z, xB0.w, xB1.x, xB1.y, xB1.z, xB1.w};
@@ -305,14 +310,14 @@ __device__ __forceinline__ double q6k_q8_unit(const uint8_t *row, int u, const A
 
 // fp32 activations x (shared) with per-32-group sums xs.
 __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const float *x,
-                                               const float *xs) {
+                                               const float *xs, int pad = 0) {
     const int b = u >> 2, c = u & 3;
     const uint8_t *blk = row + Q4K_BYTES * b;
     const uint4 h = *reinterpret_cast<const uint4 *>(blk);
     const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
     const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
     const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    const float *xl = x + 256 * b + 64 * c;
+    const float *xl = x + fpos(pad, 256 * b + 64 * c);
     float lo = 0.0f, hi = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -336,7 +341,8 @@ __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const 
            ((double)(d * (float)sc1) * (double)hi - (double)(dmin * (float)m1) * (double)xs[g + 1]);
 }
 
-__device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const float *x) {
+__device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const float *x,
+                                               int pad = 0) {
     const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
     const uint8_t *blk = row + Q6K_BYTES * b;
     uint32_t ql[8], qh[8];
@@ -344,7 +350,8 @@ __device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const 
     load16_a2(blk + 64 * h + 32 * qo + 16, ql + 4);
     load16_a2(blk + 128 + 32 * h, qh);
     load16_a2(blk + 128 + 32 * h + 16, qh + 4);
-    const float *xA = x + 256 * b + 128 * h + 32 * qo, *xB = xA + 64;
+    const float *xA = x + fpos(pad, 256 * b + 128 * h + 32 * qo);
+    const float *xB = x + fpos(pad, 256 * b + 128 * h + 32 * qo + 64);
     const int shA = 2 * qo, shB = 2 * qo + 4;
     float fA[2] = {0.0f, 0.0f}, fB[2] = {0.0f, 0.0f};
 #pragma unroll
@@ -396,15 +403,15 @@ __device__ __forceinline__ double q6k_q8_partial(const uint8_t *row, int nb, con
     return acc;
 }
 __device__ __forceinline__ double q4k_f32_partial(const uint8_t *row, int nb, const float *x,
-                                                  const float *xs, int lane) {
+                                                  const float *xs, int lane, int pad = 0) {
     double acc = 0.0;
-    for (int u = lane; u < 4 * nb; u += 32) acc += q4k_f32_unit(row, u, x, xs);
+    for (int u = lane; u < 4 * nb; u += 32) acc += q4k_f32_unit(row, u, x, xs, pad);
     return acc;
 }
 __device__ __forceinline__ double q6k_f32_partial(const uint8_t *row, int nb, const float *x,
-                                                  int lane) {
+                                                  int lane, int pad = 0) {
     double acc = 0.0;
-    for (int u = lane; u < 4 * nb; u += 32) acc += q6k_f32_unit(row, u, x);
+    for (int u = lane; u < 4 * nb; u += 32) acc += q6k_f32_unit(row, u, x, pad);
     return acc;
 }
 

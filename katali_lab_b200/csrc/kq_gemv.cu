@@ -72,46 +72,64 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         return;
     }
 
-    // Consumers: stage the activation vector once.
+    // Consumers: stage the activation vector once, bank-spread (16 bytes of padding
+    // after every 64 elements) so the 32 lanes' units fall on distinct banks.
     uint8_t *act = smem + p.act_off;
     ActQ8 a;
     const float *xf = nullptr, *xs = nullptr;
+    const int nblk = cols / 32;
     if (MODE == 2) {
-        float *sx = reinterpret_cast<float *>(act);
-        float *sxs = sx + cols;
+        float *sx = reinterpret_cast<float *>(act);  // cols + cols/16 floats
+        float *sxs = sx + cols + cols / 16;
         for (int i = threadIdx.x; i < cols / 4; i += GEMV_CW * 32)
-            reinterpret_cast<float4 *>(sx)[i] = reinterpret_cast<const float4 *>(p.x)[i];
+            reinterpret_cast<float4 *>(sx + fpos(1, 4 * i))[0] = reinterpret_cast<const float4 *>(p.x)[i];
         asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CW * 32));
-        for (int g = warp; g < cols / 32; g += GEMV_CW) {
-            const float v = warp_sum_f(sx[32 * g + lane]);
-            if (lane == 0) sxs[g] = v;
+        for (int gb = warp; gb < nblk; gb += GEMV_CW) {
+            const float v = warp_sum_f(sx[fpos(1, 32 * gb + lane)]);
+            if (lane == 0) sxs[gb] = v;
         }
         xf = sx;
         xs = sxs;
     } else {
-        int8_t *q = reinterpret_cast<int8_t *>(act);
-        float *d = reinterpret_cast<float *>(act + cols);
-        int *s32 = reinterpret_cast<int *>(d + cols / 32);
-        int *s16 = s32 + cols / 32;
-        for (int g = warp; g < cols / 32; g += GEMV_CW) {
-            if (MODE == 0) {
-                quant_block_q8(p.x[32 * g + lane], lane, q + 32 * g, d + g, s32 + g, s16 + 2 * g,
-                               nullptr);
-            } else {
-                const uint8_t *blk = p.xq + (size_t)Q81_BYTES * g;
-                const int qi = (int)(int8_t)blk[4 + lane];
-                q[32 * g + lane] = (int8_t)qi;
-                const int sum = __reduce_add_sync(KQ_FULL, qi);
-                const int lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
-                if (lane == 0) {
-                    d[g] = h2f((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
-                    s32[g] = sum;
-                    s16[2 * g] = lo;
-                    s16[2 * g + 1] = sum - lo;
+        int8_t *q = reinterpret_cast<int8_t *>(act);  // cols + cols/4 bytes
+        float *d = reinterpret_cast<float *>(act + cols + cols / 4);
+        int *s32 = reinterpret_cast<int *>(d + nblk);
+        int *s16 = s32 + nblk;
+        // Four independent blocks per warp per round so their reductions overlap.
+        for (int g0 = warp; g0 < nblk; g0 += 4 * GEMV_CW) {
+            float v[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int gb = g0 + t * GEMV_CW;
+                v[t] = 0.0f;
+                if (gb < nblk) {
+                    if (MODE == 0) v[t] = p.x[32 * gb + lane];
+                    else v[t] = (float)(int8_t)p.xq[(size_t)Q81_BYTES * gb + 4 + lane];
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int gb = g0 + t * GEMV_CW;
+                if (gb >= nblk) break;
+                int8_t *qb = q + 32 * gb + 16 * (gb >> 1);
+                if (MODE == 0) {
+                    quant_block_q8(v[t], lane, qb, d + gb, s32 + gb, s16 + 2 * gb, nullptr);
+                } else {
+                    const uint8_t *blk = p.xq + (size_t)Q81_BYTES * gb;
+                    const int qi = (int)v[t];
+                    qb[lane] = (int8_t)qi;
+                    const int sum = __reduce_add_sync(KQ_FULL, qi);
+                    const int lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+                    if (lane == 0) {
+                        d[gb] = h2f((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+                        s32[gb] = sum;
+                        s16[2 * gb] = lo;
+                        s16[2 * gb + 1] = sum - lo;
+                    }
                 }
             }
         }
-        a = ActQ8{q, d, s32, s16};
+        a = ActQ8{q, d, s32, s16, 1};
     }
     asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CW * 32));
 
@@ -135,8 +153,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
             const uint8_t *row = base + (size_t)r * J.rb;
             double part;
             if (MODE == 2)
-                part = J.type == T_Q4_K ? q4k_f32_partial(row, nb, xf, xs, lane)
-                                        : q6k_f32_partial(row, nb, xf, lane);
+                part = J.type == T_Q4_K ? q4k_f32_partial(row, nb, xf, xs, lane, 1)
+                                        : q6k_f32_partial(row, nb, xf, lane, 1);
             else
                 part = J.type == T_Q4_K ? q4k_q8_partial(row, nb, a, lane)
                                         : q6k_q8_partial(row, nb, a, lane);
@@ -353,8 +371,9 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     p.total_tiles = tiles;
     if (tiles == 0) return cudaSuccess;
     const uint32_t cols = p.cols;
-    // activation area: fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
-    const uint32_t act_bytes = mode == 2 ? cols * 4 + cols / 32 * 4 : cols + cols / 32 * 16;
+    // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
+    const uint32_t act_bytes =
+        mode == 2 ? (cols + cols / 16) * 4 + cols / 32 * 4 : cols + cols / 4 + cols / 32 * 16;
     p.stage_bytes = stage + 16;
     p.use_tma = 1;
     int ns = (int)(98304 / p.stage_bytes);

@@ -406,7 +406,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     // ---- 3. phase A: gate/up row pairs -> h = silu(g) * u, quantised per block --
     bool ok = true;
     const int nbh = H / 256;
-    const ActQ8 ax{xq, xd, xs32, xs16};
+    const ActQ8 ax{xq, xd, xs32, xs16, 0};
     Q4Act xr;
     if (MODE == 0 && nbh == 8 && nbA > 0) xr = load_q4act(ax, lane);  // this lane's unit of x
     for (int a = 0; a < nbA; ++a) {
@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             const int nunits = 4 * (F / 256);
             const uint32_t per = nrB * rbd;
             const ActQ8 ah{hq + (size_t)k * (F + 16), hd + (size_t)k * F / 32,
-                           hs32 + (size_t)k * F / 32, hs16 + (size_t)k * F / 16};
+                           hs32 + (size_t)k * F / 32, hs16 + (size_t)k * F / 16, 0};
             const double wk = k < K ? (double)s_w[k] : 0.0;
             for (uint32_t rr = warp; rr < nrB; rr += MOE_WARPS) {
                 double part = 0.0;
