@@ -138,6 +138,26 @@ int katali_cuda_moe_layer(KataliMoe *m, const float *x, const float *router_logi
 int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *ids,
                                  const float *w, float *y, uint32_t mode);
 
+/* No-allocation variant of katali_cuda_moe_layer. No counterpart in the
+ * reference. For callers that cannot allocate device memory when a layer runs
+ * (device memory owned by another allocator, a host that forbids allocations
+ * after start-up, or a fixed memory budget): nothing is allocated; the expert
+ * table (copied from desc->experts, a HOST array of 3*n_experts device
+ * pointers), the h records and the barrier counters live in a file-scope device
+ * array of about 89 KB that every GPU loading the library keeps until exit.
+ * Limits: n_experts <= KATALI_MOE_STATIC_MAX_EXPERTS and
+ * top_k * ffn <= KATALI_MOE_STATIC_MAX_TOPK_FFN, else
+ * KATALI_ERR_UNSUPPORTED_SHAPE (katali_cuda_status() says which). Runs on
+ * `stream` (a cudaStream_t, NULL = default stream) and returns after it
+ * finished. The first call on a device looks the array up for that device:
+ * make it before any stream capture. All calls share the array, so calls that
+ * overlap on the GPU race; serialise them. */
+#define KATALI_MOE_STATIC_MAX_EXPERTS 1024
+#define KATALI_MOE_STATIC_MAX_TOPK_FFN 16384
+int katali_cuda_moe_layer_static(const KataliMoeDesc *desc, const float *x,
+                                 const float *router_logits, float *y, uint32_t mode,
+                                 void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
 /* ------------------------------------------------------------------------ */

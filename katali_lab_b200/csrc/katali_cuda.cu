@@ -129,6 +129,11 @@ int max_cols_for_smem(int mode) {
 
 }  // namespace
 
+namespace kq {
+// Lets other translation units of the plugin report a reason via katali_cuda_status().
+void set_status_message(const char *msg) { snprintf(g_status, sizeof g_status, "%s", msg); }
+}  // namespace kq
+
 struct KataliMoe {
     kq::MoeParams plan[2];  // per activation mode
     int plan_ok[2];

@@ -65,7 +65,11 @@
       (t, w, r, c, q, is, xs))                                                                \
     X(int, katali_cuda_debug_route, (KataliMoe * m, const float *l, int32_t *i, float *w),    \
       (m, l, i, w))                                                                           \
-    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))
+    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))     \
+    X(int, katali_cuda_moe_layer_static,                                                      \
+      (const KataliMoeDesc *d, const float *x, const float *l, float *y, uint32_t mo,         \
+       void *s),                                                                              \
+      (d, x, l, y, mo, s))
 
 #define DECLARE_PTR(ret, name, params, args) static ret(*p_##name) params;
 KATALI_FN_LIST(DECLARE_PTR)
@@ -165,7 +169,11 @@ const char *katali_cuda_strerror(int s) {
       (t, w, r, c, q, is, xs))                                                                \
     X(int, katali_cuda_debug_route, (KataliMoe * m, const float *l, int32_t *i, float *w),    \
       (m, l, i, w))                                                                           \
-    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))
+    X(int, katali_cuda_debug_moe_trace, (KataliMoe * m, uint64_t *t, int *g), (m, t, g))     \
+    X(int, katali_cuda_moe_layer_static,                                                      \
+      (const KataliMoeDesc *d, const float *x, const float *l, float *y, uint32_t mo,         \
+       void *s),                                                                              \
+      (d, x, l, y, mo, s))
 KATALI_INT_FN_LIST(FORWARD)
 
 int katali_cuda_supports_type(uint32_t t) { return resolve() ? p_katali_cuda_supports_type(t) : 0; }

@@ -90,6 +90,8 @@ class Plugin:
             "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_moe_trace": ([_vp, _vp, C.POINTER(_i32)], _i32),
+            "katali_cuda_moe_layer_static": ([C.POINTER(KataliMoeDesc), _vp, _vp, _vp, _u32, _vp],
+                                             _i32),
         }
         for name, (args, res) in sig.items():
             f = getattr(L, name)
