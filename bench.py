@@ -372,7 +372,8 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
     """Phase timeline of the fused MoE kernel from its %globaltimer trace (ns)."""
     import torch
     from katali_lab_b200 import MOE_Q8_1
-    buf = torch.zeros(1024 * 16, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(1024 * 20, dtype=torch.int64, device="cuda")
+    mhz = []
     rows = []
     for n in range(min(T, 32)):
         i = 0 if warm else n
@@ -381,7 +382,8 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
         lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
         plugin.sync()
         lay.set_trace(None)
-        t = buf[:grid * 16].view(grid, 16).cpu().numpy().astype(np.int64)
+        t = buf[:grid * 20].view(grid, 20).cpu().numpy().astype(np.int64)
+        mhz.append(np.median((t[:, 17] - t[:, 16]) / np.maximum(t[:, 8] - t[:, 0], 1) * 1e3))
         t0 = t[:, 0].min()
         row = [t[:, 0].max() - t0]
         for s in range(1, 16):  # CTAs without phase-A or phase-B rows leave their slot 0
@@ -394,6 +396,7 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
     print(f"[trace]   last CTA start {med[0]:.2f}", file=sys.stderr)
     for s, v in sorted(zip(range(1, 16), med[1:]), key=lambda sv: sv[1]):
         print(f"[trace]   {TRACE_NAMES[s]:20s} {v:.2f}", file=sys.stderr)
+    print(f"[trace]   SM clock inside the kernel: {np.median(mhz):.0f} MHz (cycles / ns)", file=sys.stderr)
 
 
 C1_ROWS, C1_COLS = 6144, 2048

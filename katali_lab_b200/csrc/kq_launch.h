@@ -41,7 +41,7 @@ cudaError_t launch_row_isums(uint32_t type, const void *w, uint64_t rows, uint64
 
 constexpr int MOE_MAX_K = 16;
 constexpr int MOE_MAX_CHUNKS = 64;
-constexpr int TRACE_SLOTS = 16;  // %globaltimer samples per CTA when tracing
+constexpr int TRACE_SLOTS = 20;  // 16 %globaltimer slots + clock64 at start/end  // %globaltimer samples per CTA when tracing
 
 struct MoeParams {
     const uint8_t *const *experts;  // device table: gate_e, up_e, down_e per expert
@@ -67,6 +67,7 @@ struct MoeParams {
     uint32_t sb_off, sb_bytes;
     uint32_t act_off, hact_off, misc_off, smem_bytes;
     uint32_t dec_off, dec_row_bytes;  // decoded int8 down rows (q8_1 mode, Q6_K)
+    uint32_t sdot_off;                // phase-B per-expert row dots [K][rows]
     int dec_enabled;
 };
 

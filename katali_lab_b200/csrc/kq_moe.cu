@@ -51,7 +51,11 @@ __device__ __forceinline__ uint64_t globaltimer() {
     return t;
 }
 __device__ __forceinline__ void trace(const MoeParams &p, int slot) {
-    if (p.trace && threadIdx.x == 0) p.trace[blockIdx.x * TRACE_SLOTS + slot] = globaltimer();
+    if (p.trace && threadIdx.x == 0) {
+        p.trace[blockIdx.x * TRACE_SLOTS + slot] = globaltimer();
+        if (slot == 0 || slot == 8)  // SM cycle counter beside the first and last stamps
+            p.trace[blockIdx.x * TRACE_SLOTS + 16 + (slot == 8)] = (uint64_t)clock64();
+    }
 }
 
 __device__ __forceinline__ void bulk_g2s_split(uint8_t *dst, const uint8_t *src, uint32_t bytes,
@@ -309,10 +313,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *s_logits = reinterpret_cast<float *>(s_rec + MAX_ABLK * REC_BYTES);
 
     const uint32_t BA = (uint32_t)K * F / HB;  // phase-A blocks
-    const uint32_t b0 = (uint32_t)((uint64_t)BA * c / G), b1 = (uint32_t)((uint64_t)BA * (c + 1) / G);
+    const uint32_t b0 = BA * c / G, b1 = BA * (c + 1) / G;  // 32-bit: BA * G < 2^32
     const int nbA = (int)(b1 - b0);
     const uint32_t Q = (uint32_t)H / p.rg;  // phase-B row groups (16-byte aligned copies)
-    const uint32_t q0 = (uint32_t)((uint64_t)Q * c / G), q1 = (uint32_t)((uint64_t)Q * (c + 1) / G);
+    const uint32_t q0 = Q * c / G, q1 = Q * (c + 1) / G;
     const uint32_t rB0 = p.rg * q0, nrB = p.rg * (q1 - q0);
     const uint32_t rbg = p.rbg, rbu = p.rbu, rbd = p.rbd;
     const uint32_t blk_bytes = HB * (rbg + rbu);
@@ -547,6 +551,62 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     if (nrB) {
         if (!predecode && !mbar_wait_warp(&bars[NBARS - 1], 0)) {
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
+        } else if (predecode && (F == 256 || F == 512 || F == 1024 || F == 2048)) {
+            trace(p, 7);
+            // Expert-major: warp -> (expert k, row subset); lane -> (row slot, 64-element
+            // unit u). The lane keeps unit u of expert k's h in registers and dots it
+            // with the same unit of several rows; dots meet in shared memory and the
+            // weighted sum over experts runs in expert order.
+            int kp2 = 1;
+            while (kp2 < K) kp2 <<= 1;
+            const int wpe = MOE_WARPS / kp2, k = warp / wpe, wsub = warp % wpe;
+            const int nunits = F / 64, rpl = 32 / nunits;
+            const int u = lane % nunits, rs = lane / nunits;
+            float *s_dot = reinterpret_cast<float *>(smem + p.sdot_off);  // [K][nrB]
+            if (k < K) {
+                const int8_t *hk = hq + (size_t)k * (F + 16) + 64 * u;
+                const uint4 a0 = reinterpret_cast<const uint4 *>(hk)[0];
+                const uint4 a1 = reinterpret_cast<const uint4 *>(hk)[1];
+                const uint4 a2 = reinterpret_cast<const uint4 *>(hk)[2];
+                const uint4 a3 = reinterpret_cast<const uint4 *>(hk)[3];
+                const double dx0 = (double)hd[(size_t)k * F / 32 + 2 * u];
+                const double dx1 = (double)hd[(size_t)k * F / 32 + 2 * u + 1];
+                const int4 x16 = reinterpret_cast<const int4 *>(hs16 + (size_t)k * F / 16)[u];
+                const uint4 av[4] = {a0, a1, a2, a3};
+                for (uint32_t r = wsub * rpl + rs; r < nrB + (uint32_t)rs; r += wpe * rpl) {
+                    double part = 0.0;
+                    const bool live = r < nrB;
+                    if (live) {
+                        const uint8_t *drow = sdec + (size_t)k * dstride + (size_t)r * drb;
+                        const uint4 *w = reinterpret_cast<const uint4 *>(drow + 64 * u);
+                        int sg[4];
+#pragma unroll
+                        for (int gq = 0; gq < 4; ++gq) {
+                            const uint4 wv = w[gq], xv = av[gq];
+                            int acc = __dp4a((int)wv.x, (int)xv.x, 0);
+                            acc = __dp4a((int)wv.y, (int)xv.y, acc);
+                            acc = __dp4a((int)wv.z, (int)xv.z, acc);
+                            sg[gq] = __dp4a((int)wv.w, (int)xv.w, acc);
+                        }
+                        const uint32_t scw = *reinterpret_cast<const uint32_t *>(drow + F + 4 * u);
+                        const int sc0 = (int)(int8_t)(scw & 0xFF), sc1 = (int)(int8_t)((scw >> 8) & 0xFF);
+                        const int sc2 = (int)(int8_t)((scw >> 16) & 0xFF), sc3 = (int)(int8_t)(scw >> 24);
+                        const double d = (double)reinterpret_cast<const float *>(drow + F + F / 16)[u >> 2];
+                        const int I0 = sc0 * (sg[0] - 32 * x16.x) + sc1 * (sg[1] - 32 * x16.y);
+                        const int I1 = sc2 * (sg[2] - 32 * x16.z) + sc3 * (sg[3] - 32 * x16.w);
+                        part = (d * dx0) * (double)I0 + (d * dx1) * (double)I1;
+                    }
+                    for (int o = 1; o < nunits; o <<= 1) part += __shfl_xor_sync(KQ_FULL, part, o);
+                    if (live && u == 0) s_dot[(size_t)k * nrB + r] = (float)part;
+                }
+            }
+            if (warp == 0) trace(p, 15);
+            __syncthreads();
+            for (uint32_t r = tid; r < nrB; r += MOE_THREADS) {
+                double acc = 0.0;
+                for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
+                p.y[rB0 + r] = (float)acc;
+            }
         } else {
             trace(p, 7);
             // lanes per expert: 32 / next_pow2(K); lane = (expert k, slot g)
@@ -621,7 +681,8 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * (NBARS + 1) +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
                           4 * (uint32_t)p.n_experts;
-    p.smem_bytes = al128(p.misc_off + misc);
+    p.sdot_off = al128(p.misc_off + misc);
+    p.smem_bytes = al128(p.sdot_off + 4 * (uint32_t)p.K * rg * qpc);
     // Decoded int8 down rows (Q6_K, q8_1 mode): reuse the phase-A staging area
     // when it is large enough (phase A is finished by then), else append.
     p.dec_off = 0;
