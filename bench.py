@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c1"],
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
                     help="c2: fused MoE layer (headline); c1: dense Q4_K GEMV 6144x2048")
     ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
@@ -510,6 +510,170 @@ def run_c1(args, rank, world, local_rank):
             "gpu_launches": args.steps * T, "cpu_baseline": cpu}), flush=True)
 
 
+C3_WORKLOAD = ("C3 ragged continuous batch of the C2 layer: per call T ~ U{1..64} tokens "
+               "(seeded), top-8 of softmax(N(0,1) logits) per token, pairs grouped per expert")
+
+
+def c3_plan(calls: int, seed: int = 3):
+    """Token counts per call and the host-side routing of every token (for the distinct-
+    expert byte count): T_i ~ U{1..64}, x and logits N(0,1)."""
+    rng = np.random.default_rng(seed)
+    Ts = rng.integers(1, 65, size=calls)
+    X = rng.normal(0, 1, (int(Ts.sum()), H)).astype(np.float32)
+    LG = rng.normal(0, 1, (int(Ts.sum()), E)).astype(np.float32)
+    top = np.argsort(-LG, axis=1, kind="stable")[:, :K]
+    offs = np.concatenate([[0], np.cumsum(Ts)])
+    distinct = [len(np.unique(top[offs[i]:offs[i + 1]])) for i in range(calls)]
+    return Ts, offs, X, LG, distinct
+
+
+def run_c3(args, rank, world, local_rank):
+    """C3: katali_cuda_moe_batch over ragged batches; metric = distinct selected expert
+    bytes read per second (each selected expert's rows once per call)."""
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import MoeLayer, Plugin
+    from katali_lab_b200.synth import make_expert_store
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    plugin.set_stream(stream)
+    L, n = args.layers, args.calls
+    stores = [make_expert_store(plugin, E, H, F, seed=10_000 * rank + l) for l in range(L)]
+    layers = [MoeLayer(plugin, E, H, F, K, st.pointers()) for st in stores]
+    Ts, offs, Xh, LGh, distinct = c3_plan(n, seed=3 + rank)
+    ntok = int(Ts.sum())
+    xs, lgs = torch.from_numpy(Xh).cuda(), torch.from_numpy(LGh).cuda()
+    ys = torch.empty((ntok, H), device="cuda")
+    x64 = torch.randn((64, H), device="cuda")
+    l64 = torch.randn((64, E), device="cuda")
+    y64 = torch.empty((64, H), device="cuda")
+    for l in layers:  # grow every layer's batch scratch to 64 tokens before capture
+        l.forward_batch(x64, l64, y64)
+    plugin.sync()
+    plugin.set_async(True)
+
+    def step():
+        for i in range(n):
+            a, b = int(offs[i]), int(offs[i + 1])
+            layers[i % L].forward_batch(xs[a:b], lgs[a:b], ys[a:b])
+
+    step()
+    plugin.sync()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        plugin.set_stream(torch.cuda.current_stream())
+        step()
+    plugin.set_stream(stream)
+    for _ in range(max(args.warmup, 3)):
+        gr.replay()
+    plugin.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        s0.record(stream)
+        for _ in range(args.steps):
+            gr.replay()
+        s1.record(stream)
+        s1.synchronize()
+    plugin.sync()
+    ms = s0.elapsed_time(s1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_bytes = sum(distinct) * EXPERT_BYTES
+    value = world * args.steps * step_bytes / (ms / 1e3) / 1e9
+    tok_s = world * args.steps * ntok / (ms / 1e3)
+    # e2e: pinned host inputs uploaded, the calls, outputs downloaded, every step
+    xh, lh = torch.from_numpy(Xh).pin_memory(), torch.from_numpy(LGh).pin_memory()
+    yh = torch.empty((ntok, H)).pin_memory()
+    L_ = plugin.L
+
+    def e2e_step():
+        plugin.check(L_.katali_cuda_upload(xs.data_ptr(), xh.data_ptr(), xh.numel() * 4))
+        plugin.check(L_.katali_cuda_upload(lgs.data_ptr(), lh.data_ptr(), lh.numel() * 4))
+        step()
+        plugin.check(L_.katali_cuda_download(yh.data_ptr(), ys.data_ptr(), yh.numel() * 4))
+
+    e2e_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_value = world * args.steps * step_bytes / (e_ms / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        cpu = c3_cpu_rate(stores[:2], Ts, offs, Xh, LGh, distinct, args.cpu_seconds)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        us_call = 1e3 * ms / (args.steps * n)
+        achieved = step_bytes / n / (us_call * 1e-6) / 1e9
+        print(json.dumps({
+            "metric": "MoE-layer distinct-expert quant-weight GB/s vs HBM peak",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": C3_WORKLOAD, "calls_per_step": n, "tokens_per_step": ntok,
+                       "distinct_experts_per_step": int(sum(distinct)),
+                       "tokens_per_s": round(tok_s, 1), "us_per_call": round(us_call, 3),
+                       "l2": "inputs larger than L2: 16-layer store (8.4 GB) rotated per call",
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": f"{peak_kind} hbm_gbs", "traffic": None,
+                         "scope": "whole call (six launches)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
+                    "d2h_bytes_per_step": yh.numel() * 4},
+            "gpu_launches": args.steps * n * 6, "cpu_baseline": cpu}), flush=True)
+    for l in layers:
+        l.close()
+
+
+def c3_cpu_rate(stores_or_layers, Ts, offs, Xh, LGh, distinct, seconds):
+    """The reference CPU composition, one token at a time (its engine's per-token call),
+    over the C3 calls in order until ~`seconds`; GB/s of distinct expert bytes."""
+    from oracle.oracle import MoeWeights, Ref
+    ref = Ref()
+    cores = os.cpu_count() or 1
+    hl = [s if isinstance(s, MoeWeights) else
+          MoeWeights(s.gate.cpu().numpy(), s.up.cpu().numpy(), s.down.cpu().numpy(), H, F, K)
+          for s in stores_or_layers]
+    scratch = ref.moe_scratch(hl[0])
+    calls, toks, nbytes, t0 = 0, 0, 0, time.perf_counter()
+    while True:
+        i = calls % len(Ts)
+        for t in range(int(offs[i]), int(offs[i + 1])):
+            ref.moe_layer(hl[i % len(hl)], Xh[t], LGh[t], n_threads=cores, scratch=scratch)
+        toks += int(Ts[i])
+        nbytes += distinct[i] * EXPERT_BYTES
+        calls += 1
+        el = time.perf_counter() - t0
+        if (el >= seconds and calls >= 2) or calls >= 100000:
+            break
+    ref.L.kref_moe_scratch_free(scratch)
+    return {"value": round(nbytes / el / 1e9, 3), "unit": "GB/s", "cores": cores,
+            "kind": "reference",
+            "sample": f"{calls} ragged calls ({toks} tokens, {el:.1f} s), reference CPU kernels "
+                      f"composed per token, {cores} threads"}
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -529,6 +693,8 @@ def main():
     try:
         if args.config == "c1":
             run_c1(args, rank, world, local_rank)
+        elif args.config == "c3":
+            run_c3(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

@@ -137,6 +137,18 @@ int katali_cuda_moe_layer(KataliMoe *m, const float *x, const float *router_logi
 /* Same with routing given: ids[top_k] (int32), w[top_k] (fp32). */
 int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *ids,
                                  const float *w, float *y, uint32_t mode);
+/* A ragged continuous batch (the step of a server whose live sequence count
+ * changes every step; the reference engine's per-token calls, README.md:13,17,
+ * batched): x[n_tokens][H], router_logits[n_tokens][n_experts],
+ * y[n_tokens][H], row-major device buffers. Each token is routed as in
+ * katali_cuda_moe_layer; the (token, expert) pairs are grouped by expert so
+ * every selected expert's rows are read once per call. Row t of y equals
+ * katali_cuda_moe_layer on row t up to the order of double additions.
+ * mode: KATALI_MOE_Q8_1 only (else KATALI_ERR_UNSUPPORTED_TYPE). Scratch is
+ * allocated on the layer object on first use and grown when n_tokens grows. */
+#define KATALI_MOE_BATCH_MAX_TOKENS 4096
+int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
+                          const float *router_logits, float *y, uint32_t mode);
 
 /* No-allocation variant of katali_cuda_moe_layer. No counterpart in the
  * reference. For callers that cannot allocate device memory when a layer runs

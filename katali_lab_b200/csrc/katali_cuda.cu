@@ -145,7 +145,54 @@ struct KataliMoe {
     float *dbg_w;
     uint64_t *trace;
     int grid;
+    // Ragged-batch scratch, grown on demand (katali_cuda_moe_batch).
+    unsigned char *bscratch;
+    size_t bscratch_bytes;
 };
+
+namespace {
+
+// Carves the ragged-batch scratch for T tokens out of one allocation; with base ==
+// nullptr it only returns the size. Every array starts on a 256-byte boundary.
+size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq::MoeBatchParams *b) {
+    const size_t P = (size_t)T * pl.K, H = pl.H, F = pl.F, E = pl.n_experts;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        unsigned char *ptr = base ? base + off : nullptr;
+        off += (bytes + 255) & ~(size_t)255;
+        return ptr;
+    };
+    unsigned char *ids = take(4 * P), *w = take(4 * P);
+    unsigned char *xq = take(T * H), *xd = take(4 * T * H / 32), *xs32 = take(4 * T * H / 32),
+                  *xs16 = take(4 * T * H / 16);
+    unsigned char *ge = take(4 * E), *go = take(4 * (E + 1)), *ng = take(4), *ps = take(4 * P),
+                  *po = take(4 * P);
+    unsigned char *h = take(4 * P * F), *hq = take(P * F), *hd = take(4 * P * F / 32),
+                  *hs32 = take(4 * P * F / 32), *hs16 = take(4 * P * F / 16);
+    unsigned char *part = take(4 * P * H);
+    if (b) {
+        b->ids = (int32_t *)ids;
+        b->w = (float *)w;
+        b->xq = (int8_t *)xq;
+        b->xd = (float *)xd;
+        b->xs32 = (int *)xs32;
+        b->xs16 = (int *)xs16;
+        b->grp_expert = (int *)ge;
+        b->grp_off = (int *)go;
+        b->n_groups = (int *)ng;
+        b->pair_src = (int *)ps;
+        b->pos_of = (int *)po;
+        b->h = (float *)h;
+        b->hq = (int8_t *)hq;
+        b->hd = (float *)hd;
+        b->hs32 = (int *)hs32;
+        b->hs16 = (int *)hs16;
+        b->part = (float *)part;
+    }
+    return off;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -401,6 +448,7 @@ int katali_cuda_moe_destroy(KataliMoe *m) {
     cudaFree(m->sync);
     cudaFree(m->dbg_ids);
     cudaFree(m->dbg_w);
+    cudaFree(m->bscratch);
     delete m;
     return KATALI_OK;
 }
@@ -438,6 +486,53 @@ int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *id
                                  float *y, uint32_t mode) {
     if (!aligned16(x) || !ids || !w || !y) return KATALI_ERR_BAD_ARG;
     return moe_run(m, x, nullptr, ids, w, y, mode, 0);
+}
+
+int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
+                          const float *router_logits, float *y, uint32_t mode) {
+    if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
+    if (n_tokens == 0) return KATALI_OK;
+    if (!x || !router_logits || !y || !aligned16(x) || n_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
+        return KATALI_ERR_BAD_ARG;
+    if (mode != KATALI_MOE_Q8_1) return KATALI_ERR_UNSUPPORTED_TYPE;
+    for (const uint8_t *t : m->table)
+        if (!t) return KATALI_ERR_BAD_ARG;
+    const kq::MoeParams &pl = m->plan[0];
+    const int T = (int)n_tokens;
+    const size_t need = moe_batch_layout(pl, T, nullptr, nullptr);
+    if (need > m->bscratch_bytes) {
+        // Grow: earlier calls on the stream may still read the old scratch.
+        cudaError_t e = cudaStreamSynchronize(g_stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+        cudaFree(m->bscratch);
+        m->bscratch = nullptr;
+        m->bscratch_bytes = 0;
+        e = cudaMalloc((void **)&m->bscratch, need);
+        if (e != cudaSuccess) {
+            m->bscratch = nullptr;
+            return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
+        }
+        m->bscratch_bytes = need;
+    }
+    kq::MoeBatchParams b = {};
+    moe_batch_layout(pl, T, m->bscratch, &b);
+    b.experts = m->d_table;
+    b.X = x;
+    b.logits = router_logits;
+    b.Y = y;
+    b.T = T;
+    b.n_experts = pl.n_experts;
+    b.H = pl.H;
+    b.F = pl.F;
+    b.K = pl.K;
+    b.norm = pl.norm;
+    b.gate_type = pl.gate_type;
+    b.up_type = pl.up_type;
+    b.down_type = pl.down_type;
+    b.rbg = pl.rbg;
+    b.rbu = pl.rbu;
+    b.rbd = pl.rbd;
+    return finish(kq::launch_moe_batch(b, g_stream));
 }
 
 int katali_cuda_debug_moe_trace(KataliMoe *m, uint64_t *trace, int *grid) {

@@ -72,6 +72,27 @@ struct MoeParams {
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
+
+// Ragged multi-token MoE layer (q8_1 activations); scratch owned by the layer object.
+struct MoeBatchParams {
+    const uint8_t *const *experts;
+    const float *X, *logits;
+    float *Y;
+    int T, n_experts, H, F, K, norm;
+    uint32_t gate_type, up_type, down_type, rbg, rbu, rbd;
+    int32_t *ids;
+    float *w;
+    int8_t *xq;
+    float *xd;
+    int *xs32, *xs16;
+    int *grp_expert, *grp_off, *n_groups, *pair_src, *pos_of;
+    float *h;
+    int8_t *hq;
+    float *hd;
+    int *hs32, *hs16;
+    float *part;
+};
+cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
 int moe_plan(MoeParams &p, int grid, int max_smem);
 
 }  // namespace kq

@@ -1,0 +1,257 @@
+// kq_moe_batch.cu — the MoE layer for a ragged batch of tokens (continuous batching).
+//
+// T tokens are routed independently (the same top-k and softmax weights as the
+// batch-1 kernel). The T*K (token, expert) pairs are then grouped by expert, so
+// every selected expert's gate/up/down rows are read from HBM once per call and
+// dotted with all of that expert's tokens. Every per-pair dot uses the same
+// exact block terms as the batch-1 kernel and each token's output is the same
+// fixed-order weighted sum, so a token's row of Y equals its batch-1 result.
+//
+// Pipeline (one stream, six launches):
+//   route  : one CTA per token: top-k + weights, x -> q8_1 (split layout)
+//   group  : one CTA: counting sort of the pairs by expert id
+//   gateup : CTA = (group, 32 row pairs); warp = 4 row pairs; loop over the
+//            group's tokens; h = silu(g) * u per pair
+//   hquant : h -> q8_1 per pair (split layout with 16-element sums)
+//   down   : CTA = (group, 32 output rows); warp = 4 rows; loop over tokens
+//   combine: y[t] = sum_k w[t][k] * part[pair(t,k)] in k order
+#include "kq_device.cuh"
+#include "kq_launch.h"
+
+namespace kq {
+
+constexpr int BT = 256;  // threads per CTA for the batch kernels
+
+// ---------------------------------------------------------------------------
+// route: routing decision and q8_1 activations of one token per CTA
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t bkey(float f, int idx) {
+    return ((uint64_t)order_key(f) << 32) | (uint32_t)(~idx);
+}
+
+__global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = p.H, E = p.n_experts, K = p.K;
+    const float *x = p.X + (size_t)t * H;
+    const float *lg = p.logits + (size_t)t * E;
+    if (warp == 0) {
+        // Top-k over E logits: each round takes the warp maximum of per-lane maxima
+        // of the composite key (larger logit, then lower id).
+        uint32_t mine = 0;  // taken ids of this lane (bit i = id lane + 32 i)
+        const int npl = (E + 31) / 32;
+        int ids[MOE_MAX_K];
+        for (int r = 0; r < K; ++r) {
+            uint64_t best = 0;
+            for (int i = 0; i < npl; ++i) {
+                const int e = lane + 32 * i;
+                if (e < E && !((mine >> i) & 1u)) {
+                    const uint64_t kk = bkey(lg[e], e);
+                    if (kk > best) best = kk;
+                }
+            }
+            const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
+            const uint32_t Mh = __reduce_max_sync(KQ_FULL, hi);
+            const uint32_t Ml = __reduce_max_sync(KQ_FULL, hi == Mh ? lo : 0u);
+            const int e = (int)(~Ml);
+            if ((e & 31) == lane) mine |= 1u << (e >> 5);
+            ids[r] = e;
+        }
+        const float m = lg[ids[0]];
+        double S = 0.0;
+        if (!p.norm) {  // lane-owned contiguous ranges, the batch-1 kernel's order
+            const int per = (E + 31) >> 5;
+            for (int i = 0; i < per; ++i) {
+                const int idx = lane * per + i;
+                if (idx < E) S += (double)kq_expf(__fsub_rn(lg[idx], m));
+            }
+            S = warp_sum_d(S);
+        }
+        const float ev = lane < K ? kq_expf(__fsub_rn(lg[ids[lane < K ? lane : 0]], m)) : 0.0f;
+        if (p.norm) {
+            S = 0.0;
+            for (int r = 0; r < K; ++r) S += (double)__shfl_sync(KQ_FULL, ev, r);
+        }
+        if (lane < K) {
+            p.ids[t * K + lane] = ids[lane];
+            p.w[t * K + lane] = (float)((double)ev / S);
+        }
+    } else {
+        const int nblk = H / 32;
+        int8_t *q = p.xq + (size_t)t * H;
+        float *d = p.xd + (size_t)t * nblk;
+        int *s32 = p.xs32 + (size_t)t * nblk, *s16 = p.xs16 + (size_t)t * 2 * nblk;
+        for (int g = warp - 1; g < nblk; g += BT / 32 - 1)
+            quant_block_q8(x[32 * g + lane], lane, q + 32 * g, d + g, s32 + g, s16 + 2 * g, nullptr);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// group: counting sort of the T*K pairs by expert (one CTA)
+// ---------------------------------------------------------------------------
+// Exclusive block scan over blockDim.x (<= 1024) values; also returns the total.
+__device__ __forceinline__ int block_exscan(int v, int *wsum, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(KQ_FULL, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(KQ_FULL, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < nw) wsum[lane] = w;
+    }
+    __syncthreads();
+    total = wsum[nw - 1];
+    const int excl = x - v + (warp ? wsum[warp - 1] : 0);
+    __syncthreads();
+    return excl;
+}
+
+// One CTA of n_experts (<= 1024) threads: per-expert counts, offsets, the list of
+// selected experts in ascending id, and each pair's slot (order within an expert
+// is arbitrary; every pair is computed independently).
+__global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
+    __shared__ int cnt[1024], off[1024], wsum[32];
+    const int P = p.T * p.K, E = p.n_experts, e = threadIdx.x;
+    if (e < E) cnt[e] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&cnt[p.ids[i]], 1);
+    __syncthreads();
+    const int c = e < E ? cnt[e] : 0;
+    int total, ngroups;
+    const int o = block_exscan(c, wsum, total);
+    const int gi = block_exscan(c > 0 ? 1 : 0, wsum, ngroups);
+    if (e < E) {
+        off[e] = o;
+        if (c > 0) {
+            p.grp_expert[gi] = e;
+            p.grp_off[gi] = o;
+        }
+        cnt[e] = 0;
+    }
+    if (threadIdx.x == 0) {
+        p.grp_off[ngroups] = total;
+        *p.n_groups = ngroups;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int ex = p.ids[i];
+        const int pos = off[ex] + atomicAdd(&cnt[ex], 1);
+        p.pair_src[pos] = i;  // i = t * K + k
+        p.pos_of[i] = pos;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// gateup: CTA = (group g, 32 row pairs); warp = 4 row pairs; tokens of the group
+// ---------------------------------------------------------------------------
+template <uint32_t T>
+__device__ __forceinline__ double partial_q8(const uint8_t *row, int nb, const ActQ8 &a, int lane) {
+    return T == T_Q4_K ? q4k_q8_partial(row, nb, a, lane) : q6k_q8_partial(row, nb, a, lane);
+}
+
+template <uint32_t GT, uint32_t UT>
+__global__ void __launch_bounds__(BT) moe_batch_gateup(MoeBatchParams p) {
+    const int nrb = p.F / 32;
+    const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+    if (g >= *p.n_groups) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+    const int H = p.H, F = p.F, K = p.K, nb = H / 256;
+    const uint8_t *G = p.experts[3 * e], *U = p.experts[3 * e + 1];
+    for (int jj = warp; jj < 32; jj += BT / 32) {
+        const int j = rb * 32 + jj;
+        const uint8_t *grow = G + (size_t)j * p.rbg, *urow = U + (size_t)j * p.rbu;
+        for (int q = p0; q < p1; ++q) {
+            const int src = p.pair_src[q], t = src / K;
+            const ActQ8 a{p.xq + (size_t)t * H, p.xd + (size_t)t * (H / 32), p.xs32 + (size_t)t * (H / 32),
+                          p.xs16 + (size_t)t * (H / 16), 0};
+            double dg = partial_q8<GT>(grow, nb, a, lane), du = partial_q8<UT>(urow, nb, a, lane);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                dg += __shfl_xor_sync(KQ_FULL, dg, o);
+                du += __shfl_xor_sync(KQ_FULL, du, o);
+            }
+            if (lane == 0) p.h[(size_t)q * F + j] = __fmul_rn(kq_silu((float)dg), (float)du);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// hquant: one warp per 32-element block of one pair's h
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
+    const int wg = (blockIdx.x * BT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nblk = p.F / 32;
+    const int P = p.T * p.K;
+    if (wg >= P * nblk) return;
+    const int q = wg / nblk, b = wg % nblk;
+    const float v = p.h[(size_t)q * p.F + 32 * b + lane];
+    quant_block_q8(v, lane, p.hq + (size_t)q * p.F + 32 * b, p.hd + (size_t)q * nblk + b,
+                   p.hs32 + (size_t)q * nblk + b, p.hs16 + ((size_t)q * nblk + b) * 2, nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// down: CTA = (group g, 32 output rows); warp = 4 rows x units; tokens of the group
+// ---------------------------------------------------------------------------
+template <uint32_t DT>
+__global__ void __launch_bounds__(BT) moe_batch_down(MoeBatchParams p) {
+    const int nrb = p.H / 32;
+    const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
+    if (g >= *p.n_groups) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+    const int F = p.F, nb = F / 256;
+    const uint8_t *D = p.experts[3 * e + 2];
+    for (int rr = warp; rr < 32; rr += BT / 32) {
+        const int r = rb * 32 + rr;
+        const uint8_t *row = D + (size_t)r * p.rbd;
+        for (int q = p0; q < p1; ++q) {
+            const ActQ8 a{p.hq + (size_t)q * F, p.hd + (size_t)q * (F / 32), p.hs32 + (size_t)q * (F / 32),
+                          p.hs16 + (size_t)q * (F / 16), 0};
+            double v = partial_q8<DT>(row, nb, a, lane);
+            v = warp_sum_d(v);
+            if (lane == 0) p.part[(size_t)q * p.H + r] = (float)v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// combine: y[t][r] = sum_k w[t][k] * part[pos(t,k)][r], k in rank order
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(BT) moe_batch_combine(MoeBatchParams p) {
+    const int i = blockIdx.x * BT + threadIdx.x;
+    if (i >= p.T * p.H) return;
+    const int t = i / p.H, r = i % p.H;
+    double acc = 0.0;
+    for (int k = 0; k < p.K; ++k)
+        acc += (double)p.w[t * p.K + k] * (double)p.part[(size_t)p.pos_of[t * p.K + k] * p.H + r];
+    p.Y[i] = (float)acc;
+}
+
+cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
+    const int P = p.T * p.K;
+    const int max_groups = P < p.n_experts ? P : p.n_experts;
+    moe_batch_route<<<p.T, BT, 0, st>>>(p);
+    moe_batch_group<<<1, (p.n_experts + 31) / 32 * 32, 0, st>>>(p);
+    const int ggrid = max_groups * (p.F / 32);
+    if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
+    else if (p.gate_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
+    else if (p.up_type == T_Q4_K) moe_batch_gateup<T_Q6_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
+    else moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
+    moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
+    if (p.down_type == T_Q6_K) moe_batch_down<T_Q6_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
+    else moe_batch_down<T_Q4_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
+    moe_batch_combine<<<(p.T * p.H + BT - 1) / BT, BT, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace kq

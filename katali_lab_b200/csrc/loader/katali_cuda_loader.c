@@ -59,6 +59,9 @@
       (KataliMoe * m, const float *x, const int32_t *i, const float *w, float *y,             \
        uint32_t mo),                                                                          \
       (m, x, i, w, y, mo))                                                                    \
+    X(int, katali_cuda_moe_batch,                                                             \
+      (KataliMoe * m, uint32_t n, const float *x, const float *l, float *y, uint32_t mo),     \
+      (m, n, x, l, y, mo))                                                                    \
     X(int, katali_cuda_debug_row_isums,                                                       \
       (uint32_t t, const void *w, uint64_t r, uint64_t c, const void *q, int32_t *is,         \
        int32_t *xs),                                                                          \
@@ -163,6 +166,9 @@ const char *katali_cuda_strerror(int s) {
       (KataliMoe * m, const float *x, const int32_t *i, const float *w, float *y,             \
        uint32_t mo),                                                                          \
       (m, x, i, w, y, mo))                                                                    \
+    X(int, katali_cuda_moe_batch,                                                             \
+      (KataliMoe * m, uint32_t n, const float *x, const float *l, float *y, uint32_t mo),     \
+      (m, n, x, l, y, mo))                                                                    \
     X(int, katali_cuda_debug_row_isums,                                                       \
       (uint32_t t, const void *w, uint64_t r, uint64_t c, const void *q, int32_t *is,         \
        int32_t *xs),                                                                          \

@@ -87,6 +87,7 @@ class Plugin:
             "katali_cuda_moe_destroy": ([_vp], _i32),
             "katali_cuda_moe_layer": ([_vp, _vp, _vp, _vp, _u32], _i32),
             "katali_cuda_moe_layer_routed": ([_vp, _vp, _vp, _vp, _vp, _u32], _i32),
+            "katali_cuda_moe_batch": ([_vp, _u32, _vp, _vp, _vp, _u32], _i32),
             "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_moe_trace": ([_vp, _vp, C.POINTER(_i32)], _i32),
@@ -166,6 +167,12 @@ class MoeLayer:
     def forward_routed(self, x, ids, w, y, mode=MOE_Q8_1) -> None:
         self.p.check(self.p.L.katali_cuda_moe_layer_routed(self.h, _ptr(x), _ptr(ids), _ptr(w),
                                                            _ptr(y), mode))
+
+    def forward_batch(self, x, logits, y, n_tokens=None, mode=MOE_Q8_1) -> None:
+        """Ragged batch: x [T, H], logits [T, n_experts], y [T, H] device buffers."""
+        T = int(x.shape[0]) if n_tokens is None else int(n_tokens)
+        self.p.check(self.p.L.katali_cuda_moe_batch(self.h, T, _ptr(x), _ptr(logits), _ptr(y),
+                                                    mode))
 
     def route(self, logits, ids, w) -> None:
         self.p.check(self.p.L.katali_cuda_debug_route(self.h, _ptr(logits), _ptr(ids), _ptr(w)))
