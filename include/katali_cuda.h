@@ -171,6 +171,49 @@ int katali_cuda_moe_layer_static(const KataliMoeDesc *desc, const float *x,
                                  void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* 6. Expert parallelism: experts split over n_ranks GPUs, one process each   */
+/* ------------------------------------------------------------------------ */
+/* Rank r holds experts [r*E/n_ranks, (r+1)*E/n_ranks) of a layer (the other
+ * entries of its KataliMoe table may stay NULL); every rank calls with its own
+ * tokens (at most max_tokens, the same max_tokens on every rank). The call is
+ * three stages around two all-to-all exchanges of fixed-size slots:
+ *   dispatch: route + q8_1 + one slot per (destination rank, token) -> send
+ *   exchange: recv[d] = what rank d sent to this rank (n_ranks*max_tokens slots)
+ *   experts : every received slot's pairs on this rank's experts -> ret
+ *             (per slot: sum over its owned experts, in top-k order, of
+ *             w_k * down_k(silu(gate_k x) * up_k x), as H doubles)
+ *   exchange: back[d] = what rank d returned for this rank's tokens
+ *   combine : y[t] = sum over ranks (rank order) of back[d][t], to fp32.
+ * Buffers are device memory, 16-byte aligned: send/recv n_ranks*max_tokens*
+ * slot_bytes, ret/back n_ranks*max_tokens*ret_slot_bytes. Slot (d, t) is at
+ * (d*max_tokens + t)*slot_bytes. combine must follow the dispatch of the same
+ * tokens on the same KataliMoe. Row t of y equals katali_cuda_moe_batch's up
+ * to the order of double additions. No counterpart in the reference (its
+ * engine runs on one GPU); the expert-parallel step is an extension. */
+int katali_cuda_moe_ep_slot_bytes(KataliMoe *m, uint64_t *slot_bytes,
+                                  uint64_t *ret_slot_bytes);
+int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                                uint32_t n_tokens, const float *x,
+                                const float *router_logits, void *send);
+int katali_cuda_moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank,
+                               uint32_t max_tokens, const void *recv, void *ret);
+int katali_cuda_moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                               uint32_t n_tokens, const void *back, float *y);
+
+/* The same step with both exchanges done by NCCL inside the plugin (grouped
+ * ncclSend/ncclRecv on the plugin stream; libnccl.so.2 is opened at run time).
+ * Rank 0 makes a 128-byte id with katali_cuda_ep_unique_id and hands it to every
+ * rank by its own means; every rank then calls katali_cuda_ep_create on its
+ * GPU. A failed NCCL call returns KATALI_ERR_NCCL. */
+typedef struct KataliEp KataliEp;
+int katali_cuda_ep_unique_id(void *id128);
+int katali_cuda_ep_create(uint32_t n_ranks, uint32_t rank, const void *id128, KataliEp **out);
+int katali_cuda_ep_destroy(KataliEp *ep);
+int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens,
+                             uint32_t n_tokens, const float *x, const float *router_logits,
+                             float *y);
+
+/* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
 /* ------------------------------------------------------------------------ */
 /* Integer in-block sums of every row against q8_1 xq. Q4_K: per 32-group

@@ -45,7 +45,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if force or _stale(PLUGIN, deps):
         cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared",
                "-Xcompiler", "-fPIC", "-Xptxas", "-v" if verbose else "-O3",
-               "-I", INCLUDE, "-I", CSRC, "-o", PLUGIN, *srcs]
+               "-I", INCLUDE, "-I", CSRC, "-o", PLUGIN, *srcs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

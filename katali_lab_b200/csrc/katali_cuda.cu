@@ -132,6 +132,7 @@ int max_cols_for_smem(int mode) {
 namespace kq {
 // Lets other translation units of the plugin report a reason via katali_cuda_status().
 void set_status_message(const char *msg) { snprintf(g_status, sizeof g_status, "%s", msg); }
+cudaStream_t current_stream() { return g_stream; }
 }  // namespace kq
 
 struct KataliMoe {
@@ -145,9 +146,11 @@ struct KataliMoe {
     float *dbg_w;
     uint64_t *trace;
     int grid;
-    // Ragged-batch scratch, grown on demand (katali_cuda_moe_batch).
+    // Ragged-batch scratch, grown on demand (katali_cuda_moe_batch, the EP stages).
     unsigned char *bscratch;
     size_t bscratch_bytes;
+    int32_t *ep_src_ids;  // routing of the last katali_cuda_moe_ep_dispatch
+    uint32_t ep_src_cap;  // tokens
 };
 
 namespace {
@@ -449,6 +452,7 @@ int katali_cuda_moe_destroy(KataliMoe *m) {
     cudaFree(m->dbg_ids);
     cudaFree(m->dbg_w);
     cudaFree(m->bscratch);
+    cudaFree(m->ep_src_ids);
     delete m;
     return KATALI_OK;
 }
@@ -488,38 +492,29 @@ int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *id
     return moe_run(m, x, nullptr, ids, w, y, mode, 0);
 }
 
-int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
-                          const float *router_logits, float *y, uint32_t mode) {
-    if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
-    if (n_tokens == 0) return KATALI_OK;
-    if (!x || !router_logits || !y || !aligned16(x) || n_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
-        return KATALI_ERR_BAD_ARG;
-    if (mode != KATALI_MOE_Q8_1) return KATALI_ERR_UNSUPPORTED_TYPE;
-    for (const uint8_t *t : m->table)
-        if (!t) return KATALI_ERR_BAD_ARG;
-    const kq::MoeParams &pl = m->plan[0];
-    const int T = (int)n_tokens;
-    const size_t need = moe_batch_layout(pl, T, nullptr, nullptr);
-    if (need > m->bscratch_bytes) {
-        // Grow: earlier calls on the stream may still read the old scratch.
-        cudaError_t e = cudaStreamSynchronize(g_stream);
-        if (e != cudaSuccess) return cuda_fail(e);
-        cudaFree(m->bscratch);
+static int grow_batch_scratch(KataliMoe *m, int T) {
+    const size_t need = moe_batch_layout(m->plan[0], T, nullptr, nullptr);
+    if (need <= m->bscratch_bytes) return KATALI_OK;
+    // Grow: earlier calls on the stream may still read the old scratch.
+    cudaError_t e = cudaStreamSynchronize(g_stream);
+    if (e != cudaSuccess) return cuda_fail(e);
+    cudaFree(m->bscratch);
+    m->bscratch = nullptr;
+    m->bscratch_bytes = 0;
+    e = cudaMalloc((void **)&m->bscratch, need);
+    if (e != cudaSuccess) {
         m->bscratch = nullptr;
-        m->bscratch_bytes = 0;
-        e = cudaMalloc((void **)&m->bscratch, need);
-        if (e != cudaSuccess) {
-            m->bscratch = nullptr;
-            return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
-        }
-        m->bscratch_bytes = need;
+        return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
     }
+    m->bscratch_bytes = need;
+    return KATALI_OK;
+}
+
+static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
+    const kq::MoeParams &pl = m->plan[0];
     kq::MoeBatchParams b = {};
     moe_batch_layout(pl, T, m->bscratch, &b);
     b.experts = m->d_table;
-    b.X = x;
-    b.logits = router_logits;
-    b.Y = y;
     b.T = T;
     b.n_experts = pl.n_experts;
     b.H = pl.H;
@@ -532,7 +527,118 @@ int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
     b.rbg = pl.rbg;
     b.rbu = pl.rbu;
     b.rbd = pl.rbd;
+    return b;
+}
+
+int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
+                          const float *router_logits, float *y, uint32_t mode) {
+    if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
+    if (n_tokens == 0) return KATALI_OK;
+    if (!x || !router_logits || !y || !aligned16(x) || n_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
+        return KATALI_ERR_BAD_ARG;
+    if (mode != KATALI_MOE_Q8_1) return KATALI_ERR_UNSUPPORTED_TYPE;
+    for (const uint8_t *t : m->table)
+        if (!t) return KATALI_ERR_BAD_ARG;
+    int s = grow_batch_scratch(m, (int)n_tokens);
+    if (s) return s;
+    kq::MoeBatchParams b = batch_params(m, (int)n_tokens);
+    b.X = x;
+    b.logits = router_logits;
+    b.Y = y;
     return finish(kq::launch_moe_batch(b, g_stream));
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism: the three stages around the two exchanges
+// ---------------------------------------------------------------------------
+static uint32_t ep_hdr_bytes(int K) { return (uint32_t)(16 + 8 * K + 15) & ~15u; }
+static uint32_t ep_slot_bytes(const kq::MoeParams &pl) { return ep_hdr_bytes(pl.K) + pl.H / 32 * 36; }
+
+static int ep_check(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens) {
+    if (!m || n_ranks == 0 || n_ranks > 64 || max_tokens == 0 ||
+        (uint64_t)n_ranks * max_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
+        return KATALI_ERR_BAD_ARG;
+    if (m->plan[0].n_experts % (int)n_ranks) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    return KATALI_OK;
+}
+
+static void ep_fill(kq::MoeBatchParams &b, KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens) {
+    b.ep_ranks = (int)n_ranks;
+    b.ep_tmax = (int)max_tokens;
+    b.ep_hdr_bytes = ep_hdr_bytes(m->plan[0].K);
+    b.ep_slot_bytes = ep_slot_bytes(m->plan[0]);
+    b.ep_src_ids = m->ep_src_ids;
+}
+
+int katali_cuda_moe_ep_slot_bytes(KataliMoe *m, uint64_t *slot_bytes, uint64_t *ret_slot_bytes) {
+    if (!m) return KATALI_ERR_BAD_ARG;
+    if (slot_bytes) *slot_bytes = ep_slot_bytes(m->plan[0]);
+    if (ret_slot_bytes) *ret_slot_bytes = 8ull * m->plan[0].H;
+    return KATALI_OK;
+}
+
+int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                                uint32_t n_tokens, const float *x, const float *router_logits,
+                                void *send) {
+    int s = ep_check(m, n_ranks, max_tokens);
+    if (s) return s;
+    if (n_tokens > max_tokens || !send || !aligned16(send)) return KATALI_ERR_BAD_ARG;
+    if (n_tokens && (!x || !router_logits || !aligned16(x))) return KATALI_ERR_BAD_ARG;
+    const uint32_t K = (uint32_t)m->plan[0].K;
+    if (max_tokens > m->ep_src_cap) {
+        cudaError_t e = cudaStreamSynchronize(g_stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+        cudaFree(m->ep_src_ids);
+        m->ep_src_cap = 0;
+        e = cudaMalloc((void **)&m->ep_src_ids, 4ull * K * max_tokens);
+        if (e != cudaSuccess) {
+            m->ep_src_ids = nullptr;
+            return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
+        }
+        m->ep_src_cap = max_tokens;
+    }
+    kq::MoeBatchParams b = batch_params(m, 0);
+    ep_fill(b, m, n_ranks, max_tokens);
+    b.ep_tokens = (int)n_tokens;
+    b.X = x;
+    b.logits = router_logits;
+    b.ep_send = (uint8_t *)send;
+    return finish(kq::launch_moe_ep_dispatch(b, g_stream));
+}
+
+int katali_cuda_moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank,
+                               uint32_t max_tokens, const void *recv, void *ret) {
+    int s = ep_check(m, n_ranks, max_tokens);
+    if (s) return s;
+    if (rank >= n_ranks || !recv || !ret || !aligned16(recv) || !aligned16(ret))
+        return KATALI_ERR_BAD_ARG;
+    const size_t per = m->table.size() / 3 / n_ranks;
+    for (size_t i = 3 * per * rank; i < 3 * per * (rank + 1); ++i)
+        if (!m->table[i]) return KATALI_ERR_BAD_ARG;  // this rank's experts must be resident
+    const int T = (int)(n_ranks * max_tokens);
+    s = grow_batch_scratch(m, T);
+    if (s) return s;
+    kq::MoeBatchParams b = batch_params(m, T);
+    ep_fill(b, m, n_ranks, max_tokens);
+    b.ep_recv = (const uint8_t *)recv;
+    b.ep_ret = (double *)ret;
+    return finish(kq::launch_moe_ep_experts(b, g_stream));
+}
+
+int katali_cuda_moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                               uint32_t n_tokens, const void *back, float *y) {
+    int s = ep_check(m, n_ranks, max_tokens);
+    if (s) return s;
+    if (n_tokens > max_tokens || n_tokens > m->ep_src_cap || !back || !aligned16(back))
+        return KATALI_ERR_BAD_ARG;
+    if (n_tokens == 0) return KATALI_OK;
+    if (!y) return KATALI_ERR_BAD_ARG;
+    kq::MoeBatchParams b = batch_params(m, 0);
+    ep_fill(b, m, n_ranks, max_tokens);
+    b.ep_tokens = (int)n_tokens;
+    b.ep_back = (const double *)back;
+    b.Y = y;
+    return finish(kq::launch_moe_ep_combine(b, g_stream));
 }
 
 int katali_cuda_debug_moe_trace(KataliMoe *m, uint64_t *trace, int *grid) {

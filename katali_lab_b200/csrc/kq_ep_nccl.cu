@@ -1,0 +1,205 @@
+// kq_ep_nccl.cu — expert-parallel MoE layer with the two token exchanges done by
+// NCCL inside the plugin (katali_cuda_ep_* / katali_cuda_moe_ep_layer).
+//
+// One process per GPU; rank r holds experts [r*E/G, (r+1)*E/G) of every layer.
+// Per layer call: dispatch (route + q8_1 + one slot per destination rank) ->
+// grouped ncclSend/ncclRecv of the slots -> the owned experts of every received
+// slot -> grouped ncclSend/ncclRecv of the per-slot partial sums -> combine.
+// Slots have a fixed capacity (max_tokens per rank) so no counts are exchanged
+// and the whole call can be captured in a CUDA graph.
+//
+// NCCL is opened at run time (libnccl.so.2): in a process that already loaded an
+// NCCL with that soname (a PyTorch host) the same library is shared.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "katali_cuda.h"
+
+namespace kq {
+void set_status_message(const char *msg);
+cudaStream_t current_stream();
+}  // namespace kq
+
+namespace {
+
+struct Nccl {
+    void *lib = nullptr;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+Nccl g_nccl;
+
+template <typename F>
+bool sym(F &f, const char *name) {
+    f = reinterpret_cast<F>(dlsym(g_nccl.lib, name));
+    return f != nullptr;
+}
+
+int load_nccl() {
+    if (g_nccl.lib) return KATALI_OK;
+    const char *names[] = {"libnccl.so.2", "libnccl.so"};
+    void *lib = nullptr;
+    for (const char *n : names)
+        if ((lib = dlopen(n, RTLD_NOW | RTLD_GLOBAL))) break;
+    if (!lib) {
+        kq::set_status_message("NCCL not found (dlopen libnccl.so.2 failed)");
+        return KATALI_ERR_NCCL;
+    }
+    g_nccl.lib = lib;
+    bool ok = sym(g_nccl.GetUniqueId, "ncclGetUniqueId") && sym(g_nccl.CommInitRank, "ncclCommInitRank") &&
+              sym(g_nccl.CommDestroy, "ncclCommDestroy") && sym(g_nccl.CommAbort, "ncclCommAbort") &&
+              sym(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError") &&
+              sym(g_nccl.GroupStart, "ncclGroupStart") && sym(g_nccl.GroupEnd, "ncclGroupEnd") &&
+              sym(g_nccl.Send, "ncclSend") && sym(g_nccl.Recv, "ncclRecv") &&
+              sym(g_nccl.GetErrorString, "ncclGetErrorString");
+    if (!ok) {
+        kq::set_status_message("libnccl.so.2 lacks a required symbol");
+        g_nccl.lib = nullptr;
+        return KATALI_ERR_NCCL;
+    }
+    return KATALI_OK;
+}
+
+int nccl_fail(ncclResult_t r) {
+    char msg[200];
+    snprintf(msg, sizeof msg, "NCCL: %s", g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "error");
+    kq::set_status_message(msg);
+    return KATALI_ERR_NCCL;
+}
+
+}  // namespace
+
+struct KataliEp {
+    ncclComm_t comm;
+    int n_ranks, rank;
+    // exchange buffers, grown on demand
+    unsigned char *send, *recv, *ret, *back;
+    size_t slot_cap, ret_cap;  // bytes per buffer
+};
+
+namespace {
+
+int grow(unsigned char *&p, size_t &cap, size_t need) {
+    if (need <= cap) return KATALI_OK;
+    cudaError_t e = cudaStreamSynchronize(kq::current_stream());
+    if (e == cudaSuccess) {
+        cudaFree(p);
+        p = nullptr;
+        cap = 0;
+        e = cudaMalloc((void **)&p, need);
+        if (e != cudaSuccess) p = nullptr;
+    }
+    if (e != cudaSuccess) {
+        kq::set_status_message(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
+    }
+    cap = need;
+    return KATALI_OK;
+}
+
+// Every rank sends `chunk` bytes from buf_out + d * chunk to rank d and receives
+// rank d's chunk into buf_in + d * chunk.
+int exchange(KataliEp *ep, const unsigned char *out, unsigned char *in, size_t chunk, cudaStream_t st) {
+    ncclResult_t r = g_nccl.GroupStart();
+    for (int d = 0; d < ep->n_ranks && r == ncclSuccess; ++d) {
+        r = g_nccl.Send(out + d * chunk, chunk, ncclUint8, d, ep->comm, st);
+        if (r == ncclSuccess) r = g_nccl.Recv(in + d * chunk, chunk, ncclUint8, d, ep->comm, st);
+    }
+    const ncclResult_t r2 = g_nccl.GroupEnd();
+    if (r != ncclSuccess) return nccl_fail(r);
+    if (r2 != ncclSuccess) return nccl_fail(r2);
+    return KATALI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int katali_cuda_ep_unique_id(void *id) {
+    if (!id) return KATALI_ERR_BAD_ARG;
+    int s = load_nccl();
+    if (s) return s;
+    ncclUniqueId u;
+    ncclResult_t r = g_nccl.GetUniqueId(&u);
+    if (r != ncclSuccess) return nccl_fail(r);
+    memcpy(id, u.internal, sizeof u.internal);
+    return KATALI_OK;
+}
+
+int katali_cuda_ep_create(uint32_t n_ranks, uint32_t rank, const void *id, KataliEp **out) {
+    if (!out || !id || n_ranks == 0 || n_ranks > 64 || rank >= n_ranks) return KATALI_ERR_BAD_ARG;
+    *out = nullptr;
+    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    int s = load_nccl();
+    if (s) return s;
+    ncclUniqueId u;
+    memcpy(u.internal, id, sizeof u.internal);
+    KataliEp *ep = new KataliEp();
+    ep->n_ranks = (int)n_ranks;
+    ep->rank = (int)rank;
+    ncclResult_t r = g_nccl.CommInitRank(&ep->comm, (int)n_ranks, u, (int)rank);
+    if (r != ncclSuccess) {
+        delete ep;
+        return nccl_fail(r);
+    }
+    *out = ep;
+    return KATALI_OK;
+}
+
+int katali_cuda_ep_destroy(KataliEp *ep) {
+    if (!ep) return KATALI_OK;
+    cudaStreamSynchronize(kq::current_stream());
+    ncclResult_t async = ncclSuccess;
+    g_nccl.CommGetAsyncError(ep->comm, &async);
+    // A communicator with an error pending cannot be destroyed cleanly: abort it.
+    if (async != ncclSuccess) g_nccl.CommAbort(ep->comm);
+    else g_nccl.CommDestroy(ep->comm);
+    cudaFree(ep->send);
+    cudaFree(ep->recv);
+    cudaFree(ep->ret);
+    cudaFree(ep->back);
+    delete ep;
+    return KATALI_OK;
+}
+
+int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens, uint32_t n_tokens,
+                             const float *x, const float *router_logits, float *y) {
+    if (!m || !ep) return KATALI_ERR_BAD_ARG;
+    uint64_t slot = 0, rslot = 0;
+    int s = katali_cuda_moe_ep_slot_bytes(m, &slot, &rslot);
+    if (s) return s;
+    if (max_tokens == 0 || (uint64_t)max_tokens * ep->n_ranks > KATALI_MOE_BATCH_MAX_TOKENS)
+        return KATALI_ERR_BAD_ARG;
+    const size_t chunk = slot * max_tokens, rchunk = rslot * max_tokens;
+    size_t c0 = ep->slot_cap, c1 = ep->slot_cap;
+    if ((s = grow(ep->send, c0, chunk * ep->n_ranks)) || (s = grow(ep->recv, c1, chunk * ep->n_ranks)))
+        return s;
+    ep->slot_cap = c0 < c1 ? c0 : c1;
+    size_t r0 = ep->ret_cap, r1 = ep->ret_cap;
+    if ((s = grow(ep->ret, r0, rchunk * ep->n_ranks)) || (s = grow(ep->back, r1, rchunk * ep->n_ranks)))
+        return s;
+    ep->ret_cap = r0 < r1 ? r0 : r1;
+    cudaStream_t st = kq::current_stream();
+    const uint32_t G = (uint32_t)ep->n_ranks;
+    if ((s = katali_cuda_moe_ep_dispatch(m, G, max_tokens, n_tokens, x, router_logits, ep->send)))
+        return s;
+    if ((s = exchange(ep, ep->send, ep->recv, chunk, st))) return s;
+    if ((s = katali_cuda_moe_ep_experts(m, G, (uint32_t)ep->rank, max_tokens, ep->recv, ep->ret)))
+        return s;
+    if ((s = exchange(ep, ep->ret, ep->back, rchunk, st))) return s;
+    return katali_cuda_moe_ep_combine(m, G, max_tokens, n_tokens, ep->back, y);
+}
+
+}  // extern "C"

@@ -91,8 +91,19 @@ struct MoeBatchParams {
     float *hd;
     int *hs32, *hs16;
     float *part;
+    // expert parallelism (slot exchange between ranks)
+    int ep_ranks, ep_tmax, ep_tokens;
+    uint32_t ep_slot_bytes, ep_hdr_bytes;
+    uint8_t *ep_send;
+    const uint8_t *ep_recv;
+    double *ep_ret;
+    const double *ep_back;
+    int32_t *ep_src_ids;
 };
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
+cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);
+cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st);
+cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st);
 int moe_plan(MoeParams &p, int grid, int max_smem);
 
 }  // namespace kq

@@ -29,51 +29,61 @@ __device__ __forceinline__ uint64_t bkey(float f, int idx) {
     return ((uint64_t)order_key(f) << 32) | (uint32_t)(~idx);
 }
 
+// Routing of one token by one warp: top-k of E logits (each round takes the warp
+// maximum of per-lane maxima of the composite key: larger logit, then lower id)
+// and the softmax weights with the batch-1 kernel's summation order. Lane k < K
+// returns id k in *id_out and its weight in *w_out.
+__device__ __forceinline__ void route_token(const float *lg, int E, int K, int norm, int lane,
+                                            int *id_out, float *w_out) {
+    uint32_t mine = 0;  // taken ids of this lane (bit i = id lane + 32 i)
+    const int npl = (E + 31) / 32;
+    int my_id = 0;
+    for (int r = 0; r < K; ++r) {
+        uint64_t best = 0;
+        for (int i = 0; i < npl; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((mine >> i) & 1u)) {
+                const uint64_t kk = bkey(lg[e], e);
+                if (kk > best) best = kk;
+            }
+        }
+        const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
+        const uint32_t Mh = __reduce_max_sync(KQ_FULL, hi);
+        const uint32_t Ml = __reduce_max_sync(KQ_FULL, hi == Mh ? lo : 0u);
+        const int e = (int)(~Ml);
+        if ((e & 31) == lane) mine |= 1u << (e >> 5);
+        if (lane == r) my_id = e;
+    }
+    const float m = lg[__shfl_sync(KQ_FULL, my_id, 0)];
+    double S = 0.0;
+    if (!norm) {  // lane-owned contiguous ranges, the batch-1 kernel's order
+        const int per = (E + 31) >> 5;
+        for (int i = 0; i < per; ++i) {
+            const int idx = lane * per + i;
+            if (idx < E) S += (double)kq_expf(__fsub_rn(lg[idx], m));
+        }
+        S = warp_sum_d(S);
+    }
+    const float ev = lane < K ? kq_expf(__fsub_rn(lg[my_id], m)) : 0.0f;
+    if (norm) {
+        S = 0.0;
+        for (int r = 0; r < K; ++r) S += (double)__shfl_sync(KQ_FULL, ev, r);
+    }
+    *id_out = my_id;
+    *w_out = (float)((double)ev / S);
+}
+
 __global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int H = p.H, E = p.n_experts, K = p.K;
+    const int H = p.H, K = p.K;
     const float *x = p.X + (size_t)t * H;
-    const float *lg = p.logits + (size_t)t * E;
     if (warp == 0) {
-        // Top-k over E logits: each round takes the warp maximum of per-lane maxima
-        // of the composite key (larger logit, then lower id).
-        uint32_t mine = 0;  // taken ids of this lane (bit i = id lane + 32 i)
-        const int npl = (E + 31) / 32;
-        int ids[MOE_MAX_K];
-        for (int r = 0; r < K; ++r) {
-            uint64_t best = 0;
-            for (int i = 0; i < npl; ++i) {
-                const int e = lane + 32 * i;
-                if (e < E && !((mine >> i) & 1u)) {
-                    const uint64_t kk = bkey(lg[e], e);
-                    if (kk > best) best = kk;
-                }
-            }
-            const uint32_t hi = (uint32_t)(best >> 32), lo = (uint32_t)best;
-            const uint32_t Mh = __reduce_max_sync(KQ_FULL, hi);
-            const uint32_t Ml = __reduce_max_sync(KQ_FULL, hi == Mh ? lo : 0u);
-            const int e = (int)(~Ml);
-            if ((e & 31) == lane) mine |= 1u << (e >> 5);
-            ids[r] = e;
-        }
-        const float m = lg[ids[0]];
-        double S = 0.0;
-        if (!p.norm) {  // lane-owned contiguous ranges, the batch-1 kernel's order
-            const int per = (E + 31) >> 5;
-            for (int i = 0; i < per; ++i) {
-                const int idx = lane * per + i;
-                if (idx < E) S += (double)kq_expf(__fsub_rn(lg[idx], m));
-            }
-            S = warp_sum_d(S);
-        }
-        const float ev = lane < K ? kq_expf(__fsub_rn(lg[ids[lane < K ? lane : 0]], m)) : 0.0f;
-        if (p.norm) {
-            S = 0.0;
-            for (int r = 0; r < K; ++r) S += (double)__shfl_sync(KQ_FULL, ev, r);
-        }
+        int id;
+        float w;
+        route_token(p.logits + (size_t)t * p.n_experts, p.n_experts, K, p.norm, lane, &id, &w);
         if (lane < K) {
-            p.ids[t * K + lane] = ids[lane];
-            p.w[t * K + lane] = (float)((double)ev / S);
+            p.ids[t * K + lane] = id;
+            p.w[t * K + lane] = w;
         }
     } else {
         const int nblk = H / 32;
@@ -117,13 +127,15 @@ __device__ __forceinline__ int block_exscan(int v, int *wsum, int &total) {
 
 // One CTA of n_experts (<= 1024) threads: per-expert counts, offsets, the list of
 // selected experts in ascending id, and each pair's slot (order within an expert
-// is arbitrary; every pair is computed independently).
+// is arbitrary; every pair is computed independently). Pairs with id < 0 are
+// skipped.
 __global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
     __shared__ int cnt[1024], off[1024], wsum[32];
     const int P = p.T * p.K, E = p.n_experts, e = threadIdx.x;
     if (e < E) cnt[e] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < P; i += blockDim.x) atomicAdd(&cnt[p.ids[i]], 1);
+    for (int i = threadIdx.x; i < P; i += blockDim.x)
+        if (p.ids[i] >= 0) atomicAdd(&cnt[p.ids[i]], 1);
     __syncthreads();
     const int c = e < E ? cnt[e] : 0;
     int total, ngroups;
@@ -144,6 +156,7 @@ __global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
         const int ex = p.ids[i];
+        if (ex < 0) continue;  // a pair this rank does not own (expert-parallel slots)
         const int pos = off[ex] + atomicAdd(&cnt[ex], 1);
         p.pair_src[pos] = i;  // i = t * K + k
         p.pos_of[i] = pos;
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(BT) moe_batch_gateup(MoeBatchParams p) {
 __global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
     const int wg = (blockIdx.x * BT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     const int nblk = p.F / 32;
-    const int P = p.T * p.K;
+    const int P = p.grp_off[*p.n_groups];  // grouped pairs (<= T * K)
     if (wg >= P * nblk) return;
     const int q = wg / nblk, b = wg % nblk;
     const float v = p.h[(size_t)q * p.F + 32 * b + lane];
@@ -237,20 +250,161 @@ __global__ void __launch_bounds__(BT) moe_batch_combine(MoeBatchParams p) {
     p.Y[i] = (float)acc;
 }
 
-cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
-    const int P = p.T * p.K;
-    const int max_groups = P < p.n_experts ? P : p.n_experts;
-    moe_batch_route<<<p.T, BT, 0, st>>>(p);
+// ---------------------------------------------------------------------------
+// Expert parallelism: experts split over G ranks in contiguous blocks of E/G.
+//
+// Slot (dest rank d, source token t) of a send buffer [G][Tmax][slot_bytes]:
+//   int32 n_owned, int32 t, int32 pad[2], int32 ids[K], float w[K]   (ep_hdr_bytes)
+//   the token's q8_1 row as GGUF blocks (H/32 x 36 B), present when n_owned > 0
+// ids[k] is the global expert id when rank d owns it, else -1. A return buffer
+// [G][Tmax][H] of doubles carries back, per slot, the weighted sum over the
+// slot's owned pairs in k order.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint8_t *ep_slot(const MoeBatchParams &p, uint8_t *buf, int d, int t) {
+    return buf + ((size_t)d * p.ep_tmax + t) * p.ep_slot_bytes;
+}
+
+// CTA per source token slot t < Tmax: route, quantise x to a GGUF q8_1 row in
+// shared memory, write one slot per destination rank (empty headers for t >= T).
+__global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
+    extern __shared__ __align__(16) uint8_t ep_row[];
+    __shared__ int s_ids[MOE_MAX_K];
+    __shared__ float s_w[MOE_MAX_K];
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = p.H, K = p.K, G = p.ep_ranks, per = p.n_experts / G;
+    if (t >= p.ep_tokens) {
+        for (int d = threadIdx.x; d < G; d += BT)
+            *reinterpret_cast<int4 *>(ep_slot(p, p.ep_send, d, t)) = make_int4(0, t, 0, 0);
+        return;
+    }
+    if (warp == 0) {
+        int id;
+        float w;
+        route_token(p.logits + (size_t)t * p.n_experts, p.n_experts, K, p.norm, lane, &id, &w);
+        if (lane < K) {
+            s_ids[lane] = id;
+            s_w[lane] = w;
+            p.ep_src_ids[t * K + lane] = id;
+        }
+    } else {
+        const float *x = p.X + (size_t)t * H;
+        for (int g = warp - 1; g < H / 32; g += BT / 32 - 1)
+            quant_block_q8(x[32 * g + lane], lane, nullptr, nullptr, nullptr, nullptr, ep_row + 36 * g);
+    }
+    __syncthreads();
+    const int row_bytes = H / 32 * 36;
+    for (int d = 0; d < G; ++d) {
+        uint8_t *slot = ep_slot(p, p.ep_send, d, t);
+        int n = 0;
+        for (int k = 0; k < K; ++k) n += s_ids[k] / per == d;
+        if (threadIdx.x < K) {
+            const int id = s_ids[threadIdx.x];
+            reinterpret_cast<int *>(slot + 16)[threadIdx.x] = id / per == d ? id : -1;
+            reinterpret_cast<float *>(slot + 16 + 4 * K)[threadIdx.x] = s_w[threadIdx.x];
+        }
+        if (threadIdx.x == 0) *reinterpret_cast<int4 *>(slot) = make_int4(n, t, 0, 0);
+        if (n == 0) continue;
+        uint8_t *row = slot + p.ep_hdr_bytes;
+        for (int i = threadIdx.x; i < row_bytes / 16; i += BT)
+            reinterpret_cast<int4 *>(row)[i] = reinterpret_cast<const int4 *>(ep_row)[i];
+    }
+}
+
+// CTA per received slot: header -> pair ids/weights (ids -1 for empty slots);
+// GGUF q8_1 row -> split activations with integer 32- and 16-element sums.
+__global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
+    const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = p.H, K = p.K, nblk = H / 32;
+    const uint8_t *slot = p.ep_recv + (size_t)s * p.ep_slot_bytes;
+    const int n = *reinterpret_cast<const int *>(slot);
+    if (threadIdx.x < K) {
+        p.ids[s * K + threadIdx.x] = n > 0 ? reinterpret_cast<const int *>(slot + 16)[threadIdx.x] : -1;
+        p.w[s * K + threadIdx.x] = reinterpret_cast<const float *>(slot + 16 + 4 * K)[threadIdx.x];
+    }
+    if (n == 0) return;
+    const uint8_t *row = slot + p.ep_hdr_bytes;
+    for (int g = warp; g < nblk; g += BT / 32) {
+        const uint8_t *blk = row + 36 * g;
+        const int qi = (int)(int8_t)blk[4 + lane];
+        const int sum = __reduce_add_sync(KQ_FULL, qi);
+        const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+        p.xq[(size_t)s * H + 32 * g + lane] = (int8_t)qi;
+        if (lane == 0) {
+            p.xd[(size_t)s * nblk + g] = h2f(*reinterpret_cast<const uint16_t *>(blk));
+            p.xs32[(size_t)s * nblk + g] = sum;
+            p.xs16[((size_t)s * nblk + g) * 2] = sum_lo;
+            p.xs16[((size_t)s * nblk + g) * 2 + 1] = sum - sum_lo;
+        }
+    }
+}
+
+// ret[s][r] = sum over the slot's owned pairs k (in k order) of w_k * part[pair][r].
+__global__ void __launch_bounds__(BT) moe_ep_combine_slots(MoeBatchParams p) {
+    const int s = blockIdx.y, K = p.K;
+    const int r = blockIdx.x * BT + threadIdx.x;
+    if (r >= p.H) return;
+    int any = 0;
+    double acc = 0.0;
+    for (int k = 0; k < K; ++k) {
+        if (p.ids[s * K + k] < 0) continue;
+        any = 1;
+        acc += (double)p.w[s * K + k] * (double)p.part[(size_t)p.pos_of[s * K + k] * p.H + r];
+    }
+    if (any) p.ep_ret[(size_t)s * p.H + r] = acc;
+}
+
+// y[t][r] = sum over ranks d that own one of t's experts (rank order) of back[d][t][r].
+__global__ void __launch_bounds__(BT) moe_ep_combine_tokens(MoeBatchParams p) {
+    const int i = blockIdx.x * BT + threadIdx.x;
+    if (i >= p.ep_tokens * p.H) return;
+    const int t = i / p.H, r = i % p.H, K = p.K, per = p.n_experts / p.ep_ranks;
+    double acc = 0.0;
+    for (int d = 0; d < p.ep_ranks; ++d) {
+        bool own = false;
+        for (int k = 0; k < K; ++k) own |= p.ep_src_ids[t * K + k] / per == d;
+        if (own) acc += p.ep_back[((size_t)d * p.ep_tmax + t) * p.H + r];
+    }
+    p.Y[i] = (float)acc;
+}
+
+// group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots)
+static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
     moe_batch_group<<<1, (p.n_experts + 31) / 32 * 32, 0, st>>>(p);
     const int ggrid = max_groups * (p.F / 32);
     if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
     else if (p.gate_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
     else if (p.up_type == T_Q4_K) moe_batch_gateup<T_Q6_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
     else moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
+    const int P = p.T * p.K;
     moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
     if (p.down_type == T_Q6_K) moe_batch_down<T_Q6_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
     else moe_batch_down<T_Q4_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
+}
+
+cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
+    const int P = p.T * p.K;
+    moe_batch_route<<<p.T, BT, 0, st>>>(p);
+    launch_experts(p, P < p.n_experts ? P : p.n_experts, st);
     moe_batch_combine<<<(p.T * p.H + BT - 1) / BT, BT, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st) {
+    moe_ep_dispatch<<<p.ep_tmax, BT, p.H / 32 * 36, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st) {
+    // p.T = ranks * Tmax received slots
+    const int P = p.T * p.K, local = p.n_experts / p.ep_ranks;
+    moe_ep_unpack<<<p.T, BT, 0, st>>>(p);
+    launch_experts(p, P < local ? P : local, st);
+    moe_ep_combine_slots<<<dim3((p.H + BT - 1) / BT, p.T), BT, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st) {
+    moe_ep_combine_tokens<<<(p.ep_tokens * p.H + BT - 1) / BT, BT, 0, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -62,6 +62,26 @@
     X(int, katali_cuda_moe_batch,                                                             \
       (KataliMoe * m, uint32_t n, const float *x, const float *l, float *y, uint32_t mo),     \
       (m, n, x, l, y, mo))                                                                    \
+    X(int, katali_cuda_moe_ep_slot_bytes, (KataliMoe * m, uint64_t *s, uint64_t *r),          \
+      (m, s, r))                                                                              \
+    X(int, katali_cuda_moe_ep_dispatch,                                                       \
+      (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const float *x, const float *l,    \
+       void *s),                                                                              \
+      (m, g, tm, n, x, l, s))                                                                 \
+    X(int, katali_cuda_moe_ep_experts,                                                        \
+      (KataliMoe * m, uint32_t g, uint32_t r, uint32_t tm, const void *i, void *o),           \
+      (m, g, r, tm, i, o))                                                                    \
+    X(int, katali_cuda_moe_ep_combine,                                                        \
+      (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const void *b, float *y),          \
+      (m, g, tm, n, b, y))                                                                    \
+    X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
+    X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
+      (g, r, id, o))                                                                          \
+    X(int, katali_cuda_ep_destroy, (KataliEp * e), (e))                                       \
+    X(int, katali_cuda_moe_ep_layer,                                                          \
+      (KataliMoe * m, KataliEp * e, uint32_t tm, uint32_t n, const float *x, const float *l,  \
+       float *y),                                                                             \
+      (m, e, tm, n, x, l, y))                                                                 \
     X(int, katali_cuda_debug_row_isums,                                                       \
       (uint32_t t, const void *w, uint64_t r, uint64_t c, const void *q, int32_t *is,         \
        int32_t *xs),                                                                          \
@@ -169,6 +189,26 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_moe_batch,                                                             \
       (KataliMoe * m, uint32_t n, const float *x, const float *l, float *y, uint32_t mo),     \
       (m, n, x, l, y, mo))                                                                    \
+    X(int, katali_cuda_moe_ep_slot_bytes, (KataliMoe * m, uint64_t *s, uint64_t *r),          \
+      (m, s, r))                                                                              \
+    X(int, katali_cuda_moe_ep_dispatch,                                                       \
+      (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const float *x, const float *l,    \
+       void *s),                                                                              \
+      (m, g, tm, n, x, l, s))                                                                 \
+    X(int, katali_cuda_moe_ep_experts,                                                        \
+      (KataliMoe * m, uint32_t g, uint32_t r, uint32_t tm, const void *i, void *o),           \
+      (m, g, r, tm, i, o))                                                                    \
+    X(int, katali_cuda_moe_ep_combine,                                                        \
+      (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const void *b, float *y),          \
+      (m, g, tm, n, b, y))                                                                    \
+    X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
+    X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
+      (g, r, id, o))                                                                          \
+    X(int, katali_cuda_ep_destroy, (KataliEp * e), (e))                                       \
+    X(int, katali_cuda_moe_ep_layer,                                                          \
+      (KataliMoe * m, KataliEp * e, uint32_t tm, uint32_t n, const float *x, const float *l,  \
+       float *y),                                                                             \
+      (m, e, tm, n, x, l, y))                                                                 \
     X(int, katali_cuda_debug_row_isums,                                                       \
       (uint32_t t, const void *w, uint64_t r, uint64_t c, const void *q, int32_t *is,         \
        int32_t *xs),                                                                          \

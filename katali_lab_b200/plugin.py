@@ -88,6 +88,14 @@ class Plugin:
             "katali_cuda_moe_layer": ([_vp, _vp, _vp, _vp, _u32], _i32),
             "katali_cuda_moe_layer_routed": ([_vp, _vp, _vp, _vp, _vp, _u32], _i32),
             "katali_cuda_moe_batch": ([_vp, _u32, _vp, _vp, _vp, _u32], _i32),
+            "katali_cuda_moe_ep_slot_bytes": ([_vp, C.POINTER(_u64), C.POINTER(_u64)], _i32),
+            "katali_cuda_moe_ep_dispatch": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp], _i32),
+            "katali_cuda_moe_ep_experts": ([_vp, _u32, _u32, _u32, _vp, _vp], _i32),
+            "katali_cuda_moe_ep_combine": ([_vp, _u32, _u32, _u32, _vp, _vp], _i32),
+            "katali_cuda_ep_unique_id": ([_vp], _i32),
+            "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
+            "katali_cuda_ep_destroy": ([_vp], _i32),
+            "katali_cuda_moe_ep_layer": ([_vp, _vp, _u32, _u32, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_moe_trace": ([_vp, _vp, C.POINTER(_i32)], _i32),

@@ -576,6 +576,120 @@ int kqo_moe_layer_routed(const KqoMoe *m, const float *x, const int32_t *ids,
     return 0;
 }
 
+/* ------------------------------------------------------------------------ */
+/* expert-parallel slot protocol                                             */
+/* ------------------------------------------------------------------------ */
+uint32_t kqo_ep_slot_bytes(int hidden, int top_k) {
+    return ((uint32_t)(16 + 8 * top_k + 15) & ~15u) + (uint32_t)hidden / 32 * KQO_Q8_1_BYTES;
+}
+
+static int ep_geometry_ok(const KqoMoe *m, int n_ranks, int max_tokens) {
+    return m && n_ranks > 0 && max_tokens > 0 && m->n_experts % n_ranks == 0 &&
+           m->top_k > 0 && m->top_k <= 64 && m->hidden % 256 == 0;
+}
+
+int kqo_ep_dispatch(const KqoMoe *m, int n_ranks, int max_tokens, int n_tokens,
+                    const float *x, const float *logits, uint8_t *send, int32_t *src_ids) {
+    if (!ep_geometry_ok(m, n_ranks, max_tokens) || n_tokens < 0 || n_tokens > max_tokens)
+        return -1;
+    const int H = m->hidden, K = m->top_k, per = m->n_experts / n_ranks;
+    const uint32_t sb = kqo_ep_slot_bytes(H, K), hdr = sb - (uint32_t)H / 32 * KQO_Q8_1_BYTES;
+    uint8_t *row = (uint8_t *)malloc((size_t)H / 32 * KQO_Q8_1_BYTES);
+    if (!row) return -1;
+    for (int t = 0; t < max_tokens; t++) {
+        int32_t ids[64];
+        float w[64];
+        if (t < n_tokens) {
+            if (kqo_route_topk(logits + (size_t)t * m->n_experts, m->n_experts, K, m->norm_topk,
+                               ids, w) != 0) {
+                free(row);
+                return -1;
+            }
+            memcpy(src_ids + (size_t)t * K, ids, sizeof(int32_t) * (size_t)K);
+            kqo_quantize_q8_1(x + (size_t)t * H, (uint64_t)H, row);
+        }
+        for (int d = 0; d < n_ranks; d++) {
+            uint8_t *slot = send + ((size_t)d * max_tokens + t) * sb;
+            int32_t head[4] = {0, t, 0, 0};
+            if (t < n_tokens) {
+                int32_t *sid = (int32_t *)(slot + 16);
+                float *sw = (float *)(slot + 16 + 4 * K);
+                for (int k = 0; k < K; k++) {
+                    const int own = ids[k] / per == d;
+                    head[0] += own;
+                    sid[k] = own ? ids[k] : -1;
+                    sw[k] = w[k];
+                }
+                if (head[0] > 0) memcpy(slot + hdr, row, (size_t)H / 32 * KQO_Q8_1_BYTES);
+            }
+            memcpy(slot, head, sizeof head);
+        }
+    }
+    free(row);
+    return 0;
+}
+
+int kqo_ep_experts(const KqoMoe *m, int n_ranks, int rank, int max_tokens,
+                   const uint8_t *recv, double *ret) {
+    if (!ep_geometry_ok(m, n_ranks, max_tokens) || rank < 0 || rank >= n_ranks) return -1;
+    const int H = m->hidden, F = m->ffn, K = m->top_k;
+    const uint32_t sb = kqo_ep_slot_bytes(H, K), hdr = sb - (uint32_t)H / 32 * KQO_Q8_1_BYTES;
+    const uint64_t rbg = kqo_row_bytes(m->gate_type, (uint64_t)H);
+    const uint64_t rbu = kqo_row_bytes(m->up_type, (uint64_t)H);
+    if (!rbg || !rbu || F % 256) return -1;
+    float *h = (float *)malloc((size_t)F * sizeof(float));
+    float *dv = (float *)malloc((size_t)H * sizeof(float));
+    uint8_t *hq = (uint8_t *)malloc((size_t)F / 32 * KQO_Q8_1_BYTES);
+    if (!h || !dv || !hq) { free(h); free(dv); free(hq); return -1; }
+    for (int s = 0; s < n_ranks * max_tokens; s++) {
+        const uint8_t *slot = recv + (size_t)s * sb;
+        int32_t n;
+        memcpy(&n, slot, 4);
+        if (n <= 0) continue;
+        const uint8_t *xq = slot + hdr;
+        double *acc = ret + (size_t)s * H;
+        for (int r = 0; r < H; r++) acc[r] = 0.0;
+        for (int k = 0; k < K; k++) {
+            int32_t e;
+            float w;
+            memcpy(&e, slot + 16 + 4 * k, 4);
+            memcpy(&w, slot + 16 + 4 * K + 4 * k, 4);
+            if (e < 0) continue;
+            const uint8_t *G = (const uint8_t *)m->gate[e];
+            const uint8_t *U = (const uint8_t *)m->up[e];
+            for (int j = 0; j < F; j++) {
+                const float g = kqo_dot_q8(m->gate_type, G + (uint64_t)j * rbg, xq, (uint64_t)H);
+                const float u = kqo_dot_q8(m->up_type, U + (uint64_t)j * rbu, xq, (uint64_t)H);
+                h[j] = kqo_silu(g) * u;
+            }
+            kqo_quantize_q8_1(h, (uint64_t)F, hq);
+            kqo_matvec_q8(m->down_type, (const uint8_t *)m->down[e], (uint64_t)H, (uint64_t)F, hq, dv);
+            for (int r = 0; r < H; r++) acc[r] += (double)w * (double)dv[r];
+        }
+    }
+    free(h); free(dv); free(hq);
+    return 0;
+}
+
+int kqo_ep_combine(const KqoMoe *m, int n_ranks, int max_tokens, int n_tokens,
+                   const int32_t *src_ids, const double *back, float *y) {
+    if (!ep_geometry_ok(m, n_ranks, max_tokens) || n_tokens < 0 || n_tokens > max_tokens)
+        return -1;
+    const int H = m->hidden, K = m->top_k, per = m->n_experts / n_ranks;
+    for (int t = 0; t < n_tokens; t++) {
+        for (int r = 0; r < H; r++) {
+            double acc = 0.0;
+            for (int d = 0; d < n_ranks; d++) {
+                int own = 0;
+                for (int k = 0; k < K; k++) own |= src_ids[(size_t)t * K + k] / per == d;
+                if (own) acc += back[((size_t)d * max_tokens + t) * H + r];
+            }
+            y[(size_t)t * H + r] = (float)acc;
+        }
+    }
+    return 0;
+}
+
 int kqo_moe_layer(const KqoMoe *m, const float *x, const float *logits,
                   float *y, int mode, int32_t *ids, float *w, float *h_out) {
     if (!m || m->top_k <= 0 || m->top_k > 64) return -1;

@@ -114,6 +114,26 @@ int kqo_moe_layer(const KqoMoe *m, const float *x, const float *logits,
 int kqo_moe_layer_routed(const KqoMoe *m, const float *x, const int32_t *ids,
                          const float *w, float *y, int mode, float *h_out);
 
+/* Expert-parallel slot protocol (no counterpart in the reference, whose engine
+ * runs on one GPU). Experts split over n_ranks ranks in contiguous blocks of
+ * n_experts/n_ranks. A send buffer holds n_ranks*max_tokens slots of
+ * kqo_ep_slot_bytes: slot (d, t) at (d*max_tokens + t)*slot_bytes =
+ *   int32 n_owned, int32 t, int32 0, int32 0, int32 ids[K], float w[K], padding
+ *   to 16 bytes, then the token's q8_1 row (H/32 blocks of 36 B) when n_owned > 0;
+ * ids[k] is the global expert id if rank d owns it, else -1. A return buffer
+ * holds per slot H doubles: sum over the slot's owned k (in k order) of
+ * (double)w_k * (double)down_k(q8(silu(gate_k x) * up_k x)). */
+uint32_t kqo_ep_slot_bytes(int hidden, int top_k);
+/* Routes and packs this rank's n_tokens tokens; src_ids receives top_k ids per token. */
+int kqo_ep_dispatch(const KqoMoe *m, int n_ranks, int max_tokens, int n_tokens,
+                    const float *x, const float *logits, uint8_t *send, int32_t *src_ids);
+/* Computes every received slot that owns a pair; untouched slots keep ret's contents. */
+int kqo_ep_experts(const KqoMoe *m, int n_ranks, int rank, int max_tokens,
+                   const uint8_t *recv, double *ret);
+/* y[t] = sum over ranks d owning one of t's experts (rank order) of back[d][t]. */
+int kqo_ep_combine(const KqoMoe *m, int n_ranks, int max_tokens, int n_tokens,
+                   const int32_t *src_ids, const double *back, float *y);
+
 /* Greedy argmax: first index of the strict maximum (V/src/gguf_sampler.c:62-66). */
 int kqo_argmax(const float *x, int n);
 

@@ -76,6 +76,14 @@ class Port:
         L.kqo_moe_layer_routed.argtypes = [C.c_void_p, _f32p, _i32p, _f32p, _f32p,
                                            C.c_int, C.c_void_p]
         L.kqo_argmax.argtypes = [_f32p, C.c_int]
+        L.kqo_ep_slot_bytes.argtypes = [C.c_int, C.c_int]
+        L.kqo_ep_slot_bytes.restype = C.c_uint32
+        L.kqo_ep_dispatch.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_void_p]
+        L.kqo_ep_experts.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                     C.c_void_p]
+        L.kqo_ep_combine.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                     C.c_void_p, C.c_void_p]
 
     # -- scalars ---------------------------------------------------------
     def f32_to_f16(self, v: float) -> int:
@@ -159,6 +167,50 @@ class Port:
         if rc != 0:
             raise ValueError("moe_layer failed")
         return y, ids, w, h.reshape(layer.top_k, layer.ffn)
+
+
+    # -- expert-parallel slot protocol (kqo_ep_*) ------------------------
+    def ep_slot_bytes(self, hidden: int, top_k: int) -> int:
+        return int(self.L.kqo_ep_slot_bytes(hidden, top_k))
+
+    def ep_dispatch(self, layer: "MoeWeights", n_ranks, max_tokens, x, logits, send=None):
+        """Returns (send buffer uint8 [n_ranks*max_tokens*slot], src_ids int32 [T, K])."""
+        desc, _keep = layer.oracle_desc()
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.hidden)
+        logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(x.shape[0],
+                                                                         layer.n_experts)
+        sb = self.ep_slot_bytes(layer.hidden, layer.top_k)
+        if send is None:
+            send = np.zeros(n_ranks * max_tokens * sb, dtype=np.uint8)
+        src = np.zeros((max(x.shape[0], 1), layer.top_k), dtype=np.int32)
+        rc = self.L.kqo_ep_dispatch(C.byref(desc), n_ranks, max_tokens, x.shape[0],
+                                    x.ctypes.data, logits.ctypes.data, send.ctypes.data,
+                                    src.ctypes.data)
+        if rc != 0:
+            raise ValueError("ep_dispatch failed")
+        return send, src[:x.shape[0]]
+
+    def ep_experts(self, layer: "MoeWeights", n_ranks, rank, max_tokens, recv, ret=None):
+        desc, _keep = layer.oracle_desc()
+        recv = np.ascontiguousarray(recv, dtype=np.uint8)
+        if ret is None:
+            ret = np.zeros(n_ranks * max_tokens * layer.hidden, dtype=np.float64)
+        rc = self.L.kqo_ep_experts(C.byref(desc), n_ranks, rank, max_tokens, recv.ctypes.data,
+                                   ret.ctypes.data)
+        if rc != 0:
+            raise ValueError("ep_experts failed")
+        return ret
+
+    def ep_combine(self, layer: "MoeWeights", n_ranks, max_tokens, src_ids, back):
+        desc, _keep = layer.oracle_desc()
+        src_ids = np.ascontiguousarray(src_ids, dtype=np.int32)
+        back = np.ascontiguousarray(back, dtype=np.float64)
+        y = np.zeros((src_ids.shape[0], layer.hidden), dtype=np.float32)
+        rc = self.L.kqo_ep_combine(C.byref(desc), n_ranks, max_tokens, src_ids.shape[0],
+                                   src_ids.ctypes.data, back.ctypes.data, y.ctypes.data)
+        if rc != 0:
+            raise ValueError("ep_combine failed")
+        return y
 
 
 class _KqoMoe(C.Structure):

@@ -1,0 +1,79 @@
+"""Expert parallelism across GPUs: two processes, one GPU each, NCCL.
+
+Each rank holds half of the experts and brings its own tokens; the layer runs once
+with torch.distributed's all_to_all_single as the exchange and once with the
+plugin's own NCCL communicator (katali_cuda_moe_ep_layer). Bar: every token's output
+within rel_L2 <= 1e-5 of katali_cuda_moe_batch on the full layer on the same GPU and
+>= 99.9 % of elements bit-equal. Skipped with fewer than two GPUs."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+E, H, F, K = 64, 2048, 512, 8
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port_no, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import Plugin
+    from katali_lab_b200.ep import EpComm, EpMoeLayer, local_experts, torch_exchange
+    from tests.test_gpu_moe import DevLayer, dev, empty, host
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    comm = None
+    try:
+        plugin = Plugin()
+        full = DevLayer(plugin, E, H, F, K, seed=61)
+        T, tmax = [5, 3][rank], 6
+        rng = np.random.default_rng(300 + rank)
+        X = rng.normal(0, 1, (T, H)).astype(np.float32)
+        L = rng.normal(0, 1, (T, E)).astype(np.float32)
+        ep = EpMoeLayer(plugin, E, H, F, K, [full.ptrs[e] for e in local_experts(E, world, rank)],
+                        world, rank, tmax)
+        x, lg = dev(X), dev(L)
+        y1 = empty(T * H).view(T, H)
+        ep.forward(x, lg, y1, exchange=torch_exchange())
+        comm = EpComm.from_process_group(plugin)
+        y2 = empty(T * H).view(T, H)
+        ep.forward(x, lg, y2, comm=comm)
+        want = empty(T * H).view(T, H)
+        full.layer.forward_batch(x, lg, want)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), y1=host(y1), y2=host(y2), want=host(want))
+        ep.close()
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_ep_two_gpus(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn", join=True)
+    from oracle.oracle import rel_l2
+    for r in range(2):
+        d = np.load(tmp_path / f"r{r}.npz")
+        for key in ("y1", "y2"):
+            for t in range(d["want"].shape[0]):
+                assert rel_l2(d[key][t], d["want"][t]) <= 1e-5, (r, key, t)
+                assert np.mean(d[key][t] == d["want"][t]) >= 0.999, (r, key, t)

@@ -44,6 +44,7 @@ class DevLayer:
         g, u, d = self.bufs
         ptrs = [(g.data_ptr() + e * g.shape[1], u.data_ptr() + e * u.shape[1],
                  d.data_ptr() + e * d.shape[1]) for e in range(E)]
+        self.ptrs = ptrs
         self.layer = MoeLayer(plugin, E, H, F, K, ptrs, norm_topk=norm)
         self.H, self.E, self.K = H, E, K
 
