@@ -73,7 +73,8 @@ int katali_cuda_matvec(uint32_t type, const void *w, uint64_t rows, uint64_t col
 /* 2. Streams, modes, errors                                                 */
 /* ------------------------------------------------------------------------ */
 /* Run subsequent work on `stream` (a cudaStream_t); NULL selects the plugin's
- * own non-blocking stream. */
+ * own non-blocking stream, which is not ordered with the legacy default
+ * stream: to share the legacy default stream pass cudaStreamLegacy. */
 int katali_cuda_set_stream(void *stream);
 /* 0 (default): compute calls synchronise before returning. 1: enqueue only. */
 int katali_cuda_set_async(int on);

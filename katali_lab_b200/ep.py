@@ -145,12 +145,16 @@ class EpMoeLayer:
         NCCL communicator (katali_cuda_moe_ep_layer). Exactly one of the two."""
         T = int(x.shape[0]) if n_tokens is None else int(n_tokens)
         if comm is not None:
-            self.p.check(self.p.L.katali_cuda_moe_ep_layer(
-                self.layer.h, comm.h, self.max_tokens, T, _ptr(x), _ptr(logits), _ptr(y)))
+            with self.p.torch_stream():
+                self.p.check(self.p.L.katali_cuda_moe_ep_layer(
+                    self.layer.h, comm.h, self.max_tokens, T, _ptr(x), _ptr(logits), _ptr(y)))
             return y
         if exchange is None:
             raise ValueError("give an exchange or a communicator")
-        return ep_step(self, exchange, T, x, logits, y)
+        # torch's collectives complete on torch's current stream: run the stages there
+        # so each one sees the exchange before it.
+        with self.p.torch_stream():
+            return ep_step(self, exchange, T, x, logits, y)
 
     def close(self) -> None:
         self.layer.close()

@@ -8,6 +8,7 @@ fallback in this package.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import os
 import re
@@ -64,6 +65,7 @@ class Plugin:
         self.path = path
         L = C.CDLL(path)
         self.L = L
+        self.stream = None  # what set_stream last received (None: the plugin's own stream)
         sig = {
             "katali_cuda_probe": ([], _i32),
             "katali_cuda_status": ([], C.c_char_p),
@@ -121,7 +123,22 @@ class Plugin:
     def set_stream(self, stream) -> None:
         """stream: a torch.cuda.Stream, a raw cudaStream_t int, or None (plugin stream)."""
         raw = getattr(stream, "cuda_stream", stream)
+        if stream is not None and not isinstance(stream, int) and raw == 0:
+            raw = 1  # torch's default stream is the legacy NULL stream: cudaStreamLegacy
         self.check(self.L.katali_cuda_set_stream(raw or None))
+        self.stream = stream
+
+    @contextlib.contextmanager
+    def torch_stream(self):
+        """Within the block, plugin calls run on torch's current CUDA stream, so they are
+        ordered with torch's own work on it (the plugin's own stream is non-blocking)."""
+        import torch
+        prev = self.stream
+        self.set_stream(torch.cuda.current_stream())
+        try:
+            yield self
+        finally:
+            self.set_stream(prev)
 
     def set_async(self, on: bool) -> None:
         self.check(self.L.katali_cuda_set_async(int(on)))

@@ -28,7 +28,8 @@ def quantize_matrix(plugin: Plugin, qtype: int, w32: torch.Tensor) -> torch.Tens
     """Encode a [rows, cols] fp32 CUDA tensor into a [rows, row_bytes] uint8 tensor."""
     rows, cols = w32.shape
     out = torch.empty((rows, row_bytes(qtype, cols)), dtype=torch.uint8, device=w32.device)
-    plugin.quantize_rows(qtype, w32.contiguous(), rows, cols, out)
+    with plugin.torch_stream():  # ordered after the torch work that produced w32
+        plugin.quantize_rows(qtype, w32.contiguous(), rows, cols, out)
     return out
 
 
@@ -69,7 +70,8 @@ def make_expert_store(plugin: Plugin, n_experts: int, hidden: int, ffn: int, see
             n = min(chunk, n_experts - e0)
             w = torch.randn((n * rows, cols), generator=gen, device=device, dtype=torch.float32)
             w.mul_(std)
-            plugin.quantize_rows(qt, w, n * rows, cols, dst[e0:e0 + n])
+            with plugin.torch_stream():  # ordered after randn on torch's stream
+                plugin.quantize_rows(qt, w, n * rows, cols, dst[e0:e0 + n])
             del w
     return ExpertStore(gate, up, down, hidden, ffn)
 

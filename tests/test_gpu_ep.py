@@ -41,6 +41,8 @@ def inputs(seed, T):
 
 @pytest.mark.parametrize("G,Ts", [(2, [5, 3]), (4, [1, 7, 0, 4]), (8, [1] * 8)])
 def test_ep_virtual_ranks_vs_batch(plugin, full, G, Ts):
+    # the exchange below runs on torch's current stream: order the stages on it too
+    plugin.set_stream(torch.cuda.current_stream())
     tmax = max(Ts)
     eps = ep_layers(plugin, full, G, tmax)
     ins = [inputs(60 + r, T) for r, T in enumerate(Ts)]
@@ -63,6 +65,7 @@ def test_ep_virtual_ranks_vs_batch(plugin, full, G, Ts):
             assert np.mean(y[t] == want[t]) >= 0.999, (r, t)
     for e in eps:
         e.close()
+    plugin.set_stream(None)
 
 
 def test_ep_dispatch_matches_oracle(plugin, port, full):

@@ -55,7 +55,9 @@ def _rank(rank, world, port_no, out_dir):
         want = empty(T * H).view(T, H)
         full.layer.forward_batch(x, lg, want)
         torch.cuda.synchronize()
-        np.savez(os.path.join(out_dir, f"r{rank}.npz"), y1=host(y1), y2=host(y2), want=host(want))
+        store_sum = [int(b.sum(dtype=torch.int64)) for b in full.bufs]
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), y1=host(y1), y2=host(y2), want=host(want),
+                 store_sum=np.array(store_sum))
         ep.close()
     finally:
         if comm is not None:
@@ -71,6 +73,8 @@ def test_ep_two_gpus(tmp_path):
     mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2,
                        start_method="spawn", join=True)
     from oracle.oracle import rel_l2
+    sums = [np.load(tmp_path / f"r{r}.npz")["store_sum"] for r in range(2)]
+    assert np.array_equal(sums[0], sums[1]), "the two ranks built different expert stores"
     for r in range(2):
         d = np.load(tmp_path / f"r{r}.npz")
         for key in ("y1", "y2"):
