@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent replicas instead of expert parallelism")
     ap.add_argument("--warm", action="store_true",
                     help="diagnostic: every call reuses layer 0 and input 0 (weights stay in L2)")
     ap.add_argument("--trace", action="store_true",
@@ -514,11 +516,11 @@ C3_WORKLOAD = ("C3 ragged continuous batch of the C2 layer: per call T ~ U{1..64
                "(seeded), top-8 of softmax(N(0,1) logits) per token, pairs grouped per expert")
 
 
-def c3_plan(calls: int, seed: int = 3):
+def c3_plan(calls: int, seed: int = 3, tmin: int = 1, tmax: int = 64):
     """Token counts per call and the host-side routing of every token (for the distinct-
-    expert byte count): T_i ~ U{1..64}, x and logits N(0,1)."""
+    expert byte count): T_i ~ U{tmin..tmax}, x and logits N(0,1)."""
     rng = np.random.default_rng(seed)
-    Ts = rng.integers(1, 65, size=calls)
+    Ts = rng.integers(tmin, tmax + 1, size=calls)
     X = rng.normal(0, 1, (int(Ts.sum()), H)).astype(np.float32)
     LG = rng.normal(0, 1, (int(Ts.sum()), E)).astype(np.float32)
     top = np.argsort(-LG, axis=1, kind="stable")[:, :K]
@@ -674,6 +676,138 @@ def c3_cpu_rate(stores_or_layers, Ts, offs, Xh, LGh, distinct, seconds):
                       f"composed per token, {cores} threads"}
 
 
+EP_WORKLOAD = ("{cfg} expert-parallel over {n} GPUs: 256 experts split in blocks of {per} per GPU, "
+               "every GPU brings its own tokens ({tok}); dispatch/combine by the plugin's NCCL "
+               "communicator (grouped send/recv of fixed-capacity q8_1 slots)")
+
+
+def run_ep(args, rank, world, local_rank):
+    """C2 / C3 with experts split over the GPUs (one process each): every rank holds E/N
+    experts of every layer and brings its own tokens (one per call for C2, T ~ U{1..64}
+    for C3). metric = distinct selected expert bytes of the whole job per second (every
+    selected expert is read once per call by its owner for all tokens routed to it)."""
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import Plugin
+    from katali_lab_b200.ep import EpComm, EpMoeLayer, experts_per_rank
+    from katali_lab_b200.synth import make_expert_store
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    plugin.set_stream(stream)
+    per = experts_per_rank(E, world)
+    L, n = args.layers, args.calls
+    ragged = args.config == "c3"
+    tmax = 64 if ragged else 1
+    stores = [make_expert_store(plugin, per, H, F, seed=10_000 * l + rank) for l in range(L)]
+    layers = [EpMoeLayer(plugin, E, H, F, K, st.pointers(), world, rank, tmax) for st in stores]
+    comm = EpComm.from_process_group(plugin)
+    # every rank's inputs from its seed, so every rank can count the job's distinct experts
+    plans = [c3_plan(n, seed=3 + r, tmin=1 if ragged else 1, tmax=tmax) for r in range(world)]
+    Ts, offs, Xh, LGh, _ = plans[rank]
+    distinct = []
+    for i in range(n):
+        sel = set()
+        for r in range(world):
+            _, o, _, lg, _ = plans[r]
+            top = np.argsort(-lg[o[i]:o[i + 1]], axis=1, kind="stable")[:, :K]
+            sel.update(int(e) for e in top.ravel())
+        distinct.append(len(sel))
+    ntok = int(Ts.sum())
+    xs, lgs = torch.from_numpy(Xh).cuda(), torch.from_numpy(LGh).cuda()
+    ys = torch.empty((ntok, H), device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        for i in range(n):
+            a, b = int(offs[i]), int(offs[i + 1])
+            layers[i % L].forward(xs[a:b], lgs[a:b], ys[a:b], n_tokens=b - a, comm=comm)
+
+    step()  # sizes every exchange buffer and scratch before capture
+    torch.cuda.synchronize()
+    plugin.set_async(True)
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=stream):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        gr.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        s0.record(stream)
+        for _ in range(args.steps):
+            gr.replay()
+        s1.record(stream)
+        s1.synchronize()
+    plugin.sync()
+    ms = s0.elapsed_time(s1)
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    step_bytes = sum(distinct) * EXPERT_BYTES
+    value = args.steps * step_bytes / (ms / 1e3) / 1e9
+    tok_all = sum(int(p[0].sum()) for p in plans)
+    # e2e: this rank's inputs from pinned host memory, the layer calls, outputs back
+    xh, lh = torch.from_numpy(Xh).pin_memory(), torch.from_numpy(LGh).pin_memory()
+    yh = torch.empty((ntok, H)).pin_memory()
+    L_ = plugin.L
+
+    def e2e_step():
+        plugin.check(L_.katali_cuda_upload(xs.data_ptr(), xh.data_ptr(), xh.numel() * 4))
+        plugin.check(L_.katali_cuda_upload(lgs.data_ptr(), lh.data_ptr(), lh.numel() * 4))
+        step()
+        plugin.check(L_.katali_cuda_download(yh.data_ptr(), ys.data_ptr(), yh.numel() * 4))
+
+    e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = args.steps * step_bytes / (float(t.item()) / 1e3) / 1e9
+    plugin.sync()
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        us_call = 1e3 * ms / (args.steps * n)
+        print(json.dumps({
+            "metric": METRIC if not ragged else "MoE-layer distinct-expert quant-weight GB/s vs HBM peak",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": EP_WORKLOAD.format(cfg="C3 ragged batch" if ragged else
+                                                      "C2 batch-1 decode", n=world, per=per,
+                                                      tok="T ~ U{1..64} per call" if ragged
+                                                      else "one per call"),
+                       "calls_per_step": n, "tokens_per_step_job": tok_all,
+                       "distinct_experts_per_step": int(sum(distinct)),
+                       "us_per_call": round(us_call, 3), "parallelism": f"ep{world}",
+                       "l2": "inputs larger than L2: 16-layer store rotated per call"},
+            "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(value / world / peak, 4),
+                         "peak_kind": f"{peak_kind} hbm_gbs, per GPU", "traffic": None,
+                         "scope": "whole call incl. both NCCL exchanges, per GPU"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
+                    "d2h_bytes_per_step": yh.numel() * 4},
+            "gpu_launches": args.steps * n * 8, "cpu_baseline": None}), flush=True)
+    del gr
+    comm.close()
+    for l in layers:
+        l.close()
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -693,6 +827,8 @@ def main():
     try:
         if args.config == "c1":
             run_c1(args, rank, world, local_rank)
+        elif world > 1 and not args.replicas:
+            run_ep(args, rank, world, local_rank)
         elif args.config == "c3":
             run_c3(args, rank, world, local_rank)
         else:

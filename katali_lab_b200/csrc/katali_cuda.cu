@@ -527,6 +527,7 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
     b.rbg = pl.rbg;
     b.rbu = pl.rbu;
     b.rbd = pl.rbd;
+    b.status = g_status_dev;
     return b;
 }
 

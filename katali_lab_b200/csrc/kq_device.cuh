@@ -234,78 +234,198 @@ __device__ __forceinline__ int fpos(int pad, int e) { return e + (pad ? ((e >> 6
 //                q8_1 blocks 8b+4h+qo and 8b+4h+qo+2.
 // Each unit returns the sum of its two exact per-q8-block double terms.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ double q4k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+// A unit's weight bytes, loaded once and dotted with several activations.
+struct Q4Unit {
+    uint4 h, w0, w1;  // block header (d, dmin, scales), the chunk's 32 nibble bytes
+};
+struct Q6Unit {
+    uint32_t ql[8], qh[8];
+    uint32_t sc;  // sub-scales 2qo, 2qo+1, 2qo+4, 2qo+5 of half h (one byte each)
+    float d;
+};
+
+__device__ __forceinline__ Q4Unit q4k_load_unit(const uint8_t *row, int u) {
     const int b = u >> 2, c = u & 3;
     const uint8_t *blk = row + Q4K_BYTES * b;
-    const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-    const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-    const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-    const int g = 8 * b + 2 * c;
-    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * g));
-    const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
-    const uint32_t M = 0x0F0F0F0Fu;
-    int lo = 0, hi = 0;
-    lo = __dp4a((int)(w0.x & M), (int)a0.x, lo);
-    hi = __dp4a((int)((w0.x >> 4) & M), (int)a2.x, hi);
-    lo = __dp4a((int)(w0.y & M), (int)a0.y, lo);
-    hi = __dp4a((int)((w0.y >> 4) & M), (int)a2.y, hi);
-    lo = __dp4a((int)(w0.z & M), (int)a0.z, lo);
-    hi = __dp4a((int)((w0.z >> 4) & M), (int)a2.z, hi);
-    lo = __dp4a((int)(w0.w & M), (int)a0.w, lo);
-    hi = __dp4a((int)((w0.w >> 4) & M), (int)a2.w, hi);
-    lo = __dp4a((int)(w1.x & M), (int)a1.x, lo);
-    hi = __dp4a((int)((w1.x >> 4) & M), (int)a3.x, hi);
-    lo = __dp4a((int)(w1.y & M), (int)a1.y, lo);
-    hi = __dp4a((int)((w1.y >> 4) & M), (int)a3.y, hi);
-    lo = __dp4a((int)(w1.z & M), (int)a1.z, lo);
-    hi = __dp4a((int)((w1.z >> 4) & M), (int)a3.z, hi);
-    lo = __dp4a((int)(w1.w & M), (int)a1.w, lo);
-    hi = __dp4a((int)((w1.w >> 4) & M), (int)a3.w, hi);
-    int sc0, m0, sc1, m1;
-    q4k_scales(h, c, sc0, m0, sc1, m1);
-    const double d = (double)h2f(h.x), dmin = (double)h2f(h.x >> 16);
-    const double dx0 = (double)a.d[g], dx1 = (double)a.d[g + 1];
-    return ((d * dx0) * (double)(sc0 * lo) - (dmin * dx0) * (double)(m0 * a.s32[g])) +
-           ((d * dx1) * (double)(sc1 * hi) - (dmin * dx1) * (double)(m1 * a.s32[g + 1]));
+    Q4Unit w;
+    w.h = *reinterpret_cast<const uint4 *>(blk);
+    w.w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+    w.w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+    return w;
 }
 
-__device__ __forceinline__ double q6k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+// A Q4_K unit with its nibbles split (lo: first 32 elements, hi: next 32) and its
+// scales decoded, for dotting with several activations.
+struct Q4Dec {
+    uint32_t lo[8], hi[8];
+    int sc0, m0, sc1, m1;
+    double d, dmin;
+};
+__device__ __forceinline__ Q4Dec q4k_decode(const Q4Unit &wt, int u) {
+    const uint32_t M = 0x0F0F0F0Fu;
+    const uint32_t w[8] = {wt.w0.x, wt.w0.y, wt.w0.z, wt.w0.w, wt.w1.x, wt.w1.y, wt.w1.z, wt.w1.w};
+    Q4Dec r;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r.lo[i] = w[i] & M;
+        r.hi[i] = (w[i] >> 4) & M;
+    }
+    q4k_scales(wt.h, u & 3, r.sc0, r.m0, r.sc1, r.m1);
+    r.d = (double)h2f(wt.h.x);
+    r.dmin = (double)h2f(wt.h.x >> 16);
+    return r;
+}
+__device__ __forceinline__ double q4k_q8_dec(const Q4Dec &w, int u, const ActQ8 &a) {
+    const int g = 8 * (u >> 2) + 2 * (u & 3);
+    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * g));
+    const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)w.lo[0], (int)a0.x, lo);
+    hi = __dp4a((int)w.hi[0], (int)a2.x, hi);
+    lo = __dp4a((int)w.lo[1], (int)a0.y, lo);
+    hi = __dp4a((int)w.hi[1], (int)a2.y, hi);
+    lo = __dp4a((int)w.lo[2], (int)a0.z, lo);
+    hi = __dp4a((int)w.hi[2], (int)a2.z, hi);
+    lo = __dp4a((int)w.lo[3], (int)a0.w, lo);
+    hi = __dp4a((int)w.hi[3], (int)a2.w, hi);
+    lo = __dp4a((int)w.lo[4], (int)a1.x, lo);
+    hi = __dp4a((int)w.hi[4], (int)a3.x, hi);
+    lo = __dp4a((int)w.lo[5], (int)a1.y, lo);
+    hi = __dp4a((int)w.hi[5], (int)a3.y, hi);
+    lo = __dp4a((int)w.lo[6], (int)a1.z, lo);
+    hi = __dp4a((int)w.hi[6], (int)a3.z, hi);
+    lo = __dp4a((int)w.lo[7], (int)a1.w, lo);
+    hi = __dp4a((int)w.hi[7], (int)a3.w, hi);
+    const double dx0 = (double)a.d[g], dx1 = (double)a.d[g + 1];
+    return ((w.d * dx0) * (double)(w.sc0 * lo) - (w.dmin * dx0) * (double)(w.m0 * a.s32[g])) +
+           ((w.d * dx1) * (double)(w.sc1 * hi) - (w.dmin * dx1) * (double)(w.m1 * a.s32[g + 1]));
+}
+__device__ __forceinline__ double q4k_q8_unit_w(const Q4Unit &wt, int u, const ActQ8 &a) {
+    return q4k_q8_dec(q4k_decode(wt, u), u, a);
+}
+
+__device__ __forceinline__ double q4k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+    return q4k_q8_unit_w(q4k_load_unit(row, u), u, a);
+}
+
+__device__ __forceinline__ Q6Unit q6k_load_unit(const uint8_t *row, int u) {
     const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
     const uint8_t *blk = row + Q6K_BYTES * b;
-    uint32_t ql[8], qh[8];
-    load16_a2(blk + 64 * h + 32 * qo, ql);
-    load16_a2(blk + 64 * h + 32 * qo + 16, ql + 4);
-    load16_a2(blk + 128 + 32 * h, qh);
-    load16_a2(blk + 128 + 32 * h + 16, qh + 4);
+    Q6Unit w;
+    load16_a2(blk + 64 * h + 32 * qo, w.ql);
+    load16_a2(blk + 64 * h + 32 * qo + 16, w.ql + 4);
+    load16_a2(blk + 128 + 32 * h, w.qh);
+    load16_a2(blk + 128 + 32 * h + 16, w.qh + 4);
+    const uint8_t *sc = blk + 192 + 8 * h;
+    w.sc = (uint32_t)sc[2 * qo] | ((uint32_t)sc[2 * qo + 1] << 8) | ((uint32_t)sc[2 * qo + 4] << 16) |
+           ((uint32_t)sc[2 * qo + 5] << 24);
+    w.d = h2f(ld_u16(blk + 208));
+    return w;
+}
+
+// A Q6_K unit with its 6-bit values assembled (vA: quarter qo, vB: quarter qo+2,
+// unsigned 0..63 in bytes) and its scales decoded.
+struct Q6Dec {
+    uint32_t vA[8], vB[8];
+    int s0, s1, s4, s5;
+    double d;
+};
+__device__ __forceinline__ Q6Dec q6k_decode(const Q6Unit &wt, int u) {
+    const int qo = u & 1, shA = 2 * qo, shB = 2 * qo + 4;
+    Q6Dec r;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        r.vA[i] = (wt.ql[i] & 0x0F0F0F0Fu) | (((wt.qh[i] >> shA) & 0x03030303u) << 4);
+        r.vB[i] = ((wt.ql[i] >> 4) & 0x0F0F0F0Fu) | (((wt.qh[i] >> shB) & 0x03030303u) << 4);
+    }
+    r.s0 = (int)(int8_t)(wt.sc & 0xFFu);
+    r.s1 = (int)(int8_t)((wt.sc >> 8) & 0xFFu);
+    r.s4 = (int)(int8_t)((wt.sc >> 16) & 0xFFu);
+    r.s5 = (int)(int8_t)(wt.sc >> 24);
+    r.d = (double)wt.d;
+    return r;
+}
+__device__ __forceinline__ double q6k_q8_dec(const Q6Dec &w, int u, const ActQ8 &a) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
     const int jA = 8 * b + 4 * h + qo, jB = jA + 2;
     const uint4 *aA = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * jA));
     const uint4 *aB = reinterpret_cast<const uint4 *>(a.q + qpos(a, 32 * jB));
     const uint4 xA0 = aA[0], xA1 = aA[1], xB0 = aB[0], xB1 = aB[1];
     const uint32_t wa[8] = {xA0.x, xA0.y, xA0.z, xA0.w, xA1.x, xA1.y, xA1.z, xA1.w};
     const uint32_t wb[8] = {xB0.x, xB0.y, xB0.z, xB0.w, xB1.x, xB1.y, xB1.z, xB1.w};
-    const int shA = 2 * qo, shB = 2 * qo + 4;
     int sA0 = 0, sA1 = 0, sB0 = 0, sB1 = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
-        const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
-        sA0 = __dp4a((int)vA, (int)wa[i], sA0);
-        sB0 = __dp4a((int)vB, (int)wb[i], sB0);
+        sA0 = __dp4a((int)w.vA[i], (int)wa[i], sA0);
+        sB0 = __dp4a((int)w.vB[i], (int)wb[i], sB0);
     }
 #pragma unroll
     for (int i = 4; i < 8; ++i) {
-        const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
-        const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
-        sA1 = __dp4a((int)vA, (int)wa[i], sA1);
-        sB1 = __dp4a((int)vB, (int)wb[i], sB1);
+        sA1 = __dp4a((int)w.vA[i], (int)wa[i], sA1);
+        sB1 = __dp4a((int)w.vB[i], (int)wb[i], sB1);
     }
-    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
-    const int IA = (int)sc[2 * qo] * (sA0 - 32 * a.s16[2 * jA]) +
-                   (int)sc[2 * qo + 1] * (sA1 - 32 * a.s16[2 * jA + 1]);
-    const int IB = (int)sc[2 * qo + 4] * (sB0 - 32 * a.s16[2 * jB]) +
-                   (int)sc[2 * qo + 5] * (sB1 - 32 * a.s16[2 * jB + 1]);
-    const double d = (double)h2f(ld_u16(blk + 208));
-    return (d * (double)a.d[jA]) * (double)IA + (d * (double)a.d[jB]) * (double)IB;
+    const int IA = w.s0 * (sA0 - 32 * a.s16[2 * jA]) + w.s1 * (sA1 - 32 * a.s16[2 * jA + 1]);
+    const int IB = w.s4 * (sB0 - 32 * a.s16[2 * jB]) + w.s5 * (sB1 - 32 * a.s16[2 * jB + 1]);
+    return (w.d * (double)a.d[jA]) * (double)IA + (w.d * (double)a.d[jB]) * (double)IB;
+}
+__device__ __forceinline__ double q6k_q8_unit_w(const Q6Unit &wt, int u, const ActQ8 &a) {
+    return q6k_q8_dec(q6k_decode(wt, u), u, a);
+}
+
+__device__ __forceinline__ double q6k_q8_unit(const uint8_t *row, int u, const ActQ8 &a) {
+    return q6k_q8_unit_w(q6k_load_unit(row, u), u, a);
+}
+
+// Weight unit of either type, for code templated on the row type.
+template <uint32_t T>
+struct UnitOf {
+    using type = Q4Unit;
+};
+template <>
+struct UnitOf<T_Q6_K> {
+    using type = Q6Unit;
+};
+template <uint32_t T>
+__device__ __forceinline__ typename UnitOf<T>::type load_unit(const uint8_t *row, int u) {
+    if constexpr (T == T_Q4_K) return q4k_load_unit(row, u);
+    else return q6k_load_unit(row, u);
+}
+template <uint32_t T>
+__device__ __forceinline__ double unit_dot(const typename UnitOf<T>::type &w, int u, const ActQ8 &a) {
+    if constexpr (T == T_Q4_K) return q4k_q8_unit_w(w, u, a);
+    else return q6k_q8_unit_w(w, u, a);
+}
+template <uint32_t T>
+struct DecOf {
+    using type = Q4Dec;
+};
+template <>
+struct DecOf<T_Q6_K> {
+    using type = Q6Dec;
+};
+template <uint32_t T>
+__device__ __forceinline__ typename DecOf<T>::type load_dec(const uint8_t *row, int u) {
+    if constexpr (T == T_Q4_K) return q4k_decode(q4k_load_unit(row, u), u);
+    else return q6k_decode(q6k_load_unit(row, u), u);
+}
+template <uint32_t T>
+__device__ __forceinline__ double dec_dot(const typename DecOf<T>::type &w, int u, const ActQ8 &a) {
+    if constexpr (T == T_Q4_K) return q4k_q8_dec(w, u, a);
+    else return q6k_q8_dec(w, u, a);
+}
+
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only); completes at
+// cp_async_wait_all().
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // fp32 activations x (shared) with per-32-group sums xs.

@@ -74,13 +74,16 @@ __device__ __forceinline__ void route_token(const float *lg, int E, int K, int n
 }
 
 __global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
+    __shared__ float s_lg[1024];
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K;
     const float *x = p.X + (size_t)t * H;
+    for (int i = threadIdx.x; i < p.n_experts; i += BT) s_lg[i] = p.logits[(size_t)t * p.n_experts + i];
+    __syncthreads();
     if (warp == 0) {
         int id;
         float w;
-        route_token(p.logits + (size_t)t * p.n_experts, p.n_experts, K, p.norm, lane, &id, &w);
+        route_token(s_lg, p.n_experts, K, p.norm, lane, &id, &w);
         if (lane < K) {
             p.ids[t * K + lane] = id;
             p.w[t * K + lane] = w;
@@ -164,36 +167,156 @@ __global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// gateup: CTA = (group g, 32 row pairs); warp = 4 row pairs; tokens of the group
+// Row tiles: a CTA takes `rows` consecutive rows of one selected expert matrix
+// (gate and up together for gateup), copies them into shared memory with one
+// bulk copy per matrix and computes them for every token of the expert's group.
+// LPR = 256 / rows lanes per row, each lane a strided share of the row's units;
+// tokens in chunks of BTC with one double accumulator each, so a weight unit is
+// read from shared memory once per chunk.
 // ---------------------------------------------------------------------------
-template <uint32_t T>
-__device__ __forceinline__ double partial_q8(const uint8_t *row, int nb, const ActQ8 &a, int lane) {
-    return T == T_Q4_K ? q4k_q8_partial(row, nb, a, lane) : q6k_q8_partial(row, nb, a, lane);
+constexpr int BTC = 2;  // tokens per register chunk
+
+__device__ __forceinline__ ActQ8 x_act(const MoeBatchParams &p, int t) {
+    const int nblk = p.H / 32;
+    return ActQ8{p.xq + (size_t)t * p.H, p.xd + (size_t)t * nblk, p.xs32 + (size_t)t * nblk,
+                 p.xs16 + (size_t)t * 2 * nblk, 0};
+}
+__device__ __forceinline__ ActQ8 h_act(const MoeBatchParams &p, int q) {
+    const int nblk = p.F / 32;
+    return ActQ8{p.hq + (size_t)q * p.F, p.hd + (size_t)q * nblk, p.hs32 + (size_t)q * nblk,
+                 p.hs16 + (size_t)q * 2 * nblk, 0};
+}
+// Sum over the LPR lanes of a row (LPR a power of two, lanes of a row adjacent).
+__device__ __forceinline__ double row_sum(double v, int lpr) {
+    for (int o = 1; o < lpr; o <<= 1) v += __shfl_xor_sync(KQ_FULL, v, o);
+    return v;
+}
+
+// Copies the q8_1 activations of `n` rows (row i = src_row(i)) of length L into
+// shared memory: values in the bank-spread layout (16 bytes of padding after every
+// 64), scales, 32- and 16-element sums. Returns the slot stride of the values.
+constexpr int ACT_TOKS = 4;  // activation rows staged at a time
+__host__ __device__ constexpr int act_q_stride(int L) { return L + L / 4; }
+__host__ __device__ constexpr int act_slot_bytes(int L) { return act_q_stride(L) + L / 32 * 8 + L / 16 * 4; }
+
+struct SmemAct {
+    int8_t *q;
+    float *d;
+    int *s32, *s16;
+    int L;
+    __device__ ActQ8 at(int i) const {
+        return ActQ8{q + (size_t)i * act_q_stride(L), d + (size_t)i * (L / 32),
+                     s32 + (size_t)i * (L / 32), s16 + (size_t)i * (L / 16), 1};
+    }
+};
+__device__ __forceinline__ SmemAct smem_act(uint8_t *base, int L) {
+    SmemAct a;
+    a.L = L;
+    a.q = reinterpret_cast<int8_t *>(base);
+    a.d = reinterpret_cast<float *>(base + (size_t)ACT_TOKS * act_q_stride(L));
+    a.s32 = reinterpret_cast<int *>(a.d + ACT_TOKS * (L / 32));
+    a.s16 = a.s32 + ACT_TOKS * (L / 32);
+    return a;
+}
+// Issues the copies (cp.async) of n activation rows into `sa`; the caller waits
+// with cp_async_wait_all() and a CTA barrier.
+template <typename RowOf>
+__device__ __forceinline__ void stage_act(const SmemAct &sa, int n, RowOf row_of) {
+    const int L = sa.L, nv = L / 16, nb = L / 32;
+    for (int idx = threadIdx.x; idx < n * nv; idx += BT) {
+        const int i = idx / nv, v = idx % nv;
+        cp_async16(sa.q + (size_t)i * act_q_stride(L) + 16 * v + 16 * (v >> 2), row_of(i).q + 16 * v);
+    }
+    for (int idx = threadIdx.x; idx < n * nb; idx += BT) {
+        const int i = idx / nb, b = idx % nb;
+        const ActQ8 src = row_of(i);
+        cp_async4(sa.d + i * nb + b, src.d + b);
+        cp_async4(sa.s32 + i * nb + b, src.s32 + b);
+        cp_async4(sa.s16 + (i * nb + b) * 2, src.s16 + 2 * b);
+        cp_async4(sa.s16 + (i * nb + b) * 2 + 1, src.s16 + 2 * b + 1);
+    }
+}
+
+// Thread 0 starts the weight-tile copies on `bar` (initialised here); the caller
+// makes the barrier visible with a CTA barrier before anyone waits on it.
+__device__ __forceinline__ void issue_tiles(uint64_t *bar, int n, uint8_t *const *dst,
+                                            const uint8_t *const *src, const uint32_t *bytes) {
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        uint32_t total = 0;
+        for (int i = 0; i < n; ++i) total += bytes[i];
+        mbar_arrive_expect_tx(bar, total);
+        const uint64_t pol = l2_evict_first_policy();
+        for (int i = 0; i < n; ++i) bulk_g2s_hint(dst[i], src[i], bytes[i], bar, pol);
+    }
+}
+__device__ __forceinline__ bool wait_tiles(uint64_t *bar, volatile uint32_t *status) {
+    if (mbar_wait(bar, 0)) return true;
+    if (status) atomicOr((uint32_t *)status, 4u);
+    return false;
 }
 
 template <uint32_t GT, uint32_t UT>
-__global__ void __launch_bounds__(BT) moe_batch_gateup(MoeBatchParams p) {
-    const int nrb = p.F / 32;
+__global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int rows = p.gu_rows, lpr = BT / rows;
+    const int nrb = (p.F + rows - 1) / rows;
     const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
     if (g >= *p.n_groups) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
-    const int H = p.H, F = p.F, K = p.K, nb = H / 256;
-    const uint8_t *G = p.experts[3 * e], *U = p.experts[3 * e + 1];
-    for (int jj = warp; jj < 32; jj += BT / 32) {
-        const int j = rb * 32 + jj;
-        const uint8_t *grow = G + (size_t)j * p.rbg, *urow = U + (size_t)j * p.rbu;
-        for (int q = p0; q < p1; ++q) {
-            const int src = p.pair_src[q], t = src / K;
-            const ActQ8 a{p.xq + (size_t)t * H, p.xd + (size_t)t * (H / 32), p.xs32 + (size_t)t * (H / 32),
-                          p.xs16 + (size_t)t * (H / 16), 0};
-            double dg = partial_q8<GT>(grow, nb, a, lane), du = partial_q8<UT>(urow, nb, a, lane);
+    const int F = p.F, K = p.K, U = p.H / 64;
+    const int j0 = rb * rows, nrows = min(rows, F - j0);
+    uint8_t *sg = sm, *su = sm + (size_t)rows * p.rbg;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(su + (size_t)rows * p.rbu);
+    const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.H);
+    {
+        uint8_t *dst[2] = {sg, su};
+        const uint8_t *src[2] = {p.experts[3 * e] + (size_t)j0 * p.rbg,
+                                 p.experts[3 * e + 1] + (size_t)j0 * p.rbu};
+        const uint32_t bytes[2] = {(uint32_t)nrows * p.rbg, (uint32_t)nrows * p.rbu};
+        issue_tiles(bar, 2, dst, src, bytes);
+    }
+    const int sub = threadIdx.x % lpr, jr = threadIdx.x / lpr, j = j0 + jr;
+    const bool valid = jr < nrows;
+    const uint8_t *grow = sg + (size_t)(valid ? jr : 0) * p.rbg;
+    const uint8_t *urow = su + (size_t)(valid ? jr : 0) * p.rbu;
+    bool tiles_in = false;
+    for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
+        const int nc = min(ACT_TOKS, p1 - c0);
+        __syncthreads();  // barrier init visible; the previous chunk is no longer read
+        stage_act(sa, nc, [&](int i) { return x_act(p, p.pair_src[c0 + i] / K); });
+        cp_async_wait_all();
+        __syncthreads();
+        if (!tiles_in) {
+            if (!wait_tiles(bar, p.status)) return;
+            tiles_in = true;
+        }
+        for (int i0 = 0; i0 < nc; i0 += BTC) {
+            const int nq = min(BTC, nc - i0);
+            double ag[BTC], au[BTC];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                dg += __shfl_xor_sync(KQ_FULL, dg, o);
-                du += __shfl_xor_sync(KQ_FULL, du, o);
+            for (int i = 0; i < BTC; ++i) ag[i] = au[i] = 0.0;
+            if (valid) {
+                for (int u = sub; u < U; u += lpr) {
+                    const auto wg = load_dec<GT>(grow, u);
+                    const auto wu = load_dec<UT>(urow, u);
+#pragma unroll
+                    for (int i = 0; i < BTC; ++i) {
+                        if (i < nq) {
+                            const ActQ8 a = sa.at(i0 + i);
+                            ag[i] += dec_dot<GT>(wg, u, a);
+                            au[i] += dec_dot<UT>(wu, u, a);
+                        }
+                    }
+                }
             }
-            if (lane == 0) p.h[(size_t)q * F + j] = __fmul_rn(kq_silu((float)dg), (float)du);
+#pragma unroll
+            for (int i = 0; i < BTC; ++i) {
+                const double dg = row_sum(ag[i], lpr), du = row_sum(au[i], lpr);
+                if (valid && sub == 0 && i < nq)
+                    p.h[(size_t)(c0 + i0 + i) * F + j] = __fmul_rn(kq_silu((float)dg), (float)du);
+            }
         }
     }
 }
@@ -213,26 +336,59 @@ __global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// down: CTA = (group g, 32 output rows); warp = 4 rows x units; tokens of the group
+// down: CTA = (group g, p.dn_rows output rows), same scheme as gateup
 // ---------------------------------------------------------------------------
 template <uint32_t DT>
-__global__ void __launch_bounds__(BT) moe_batch_down(MoeBatchParams p) {
-    const int nrb = p.H / 32;
+__global__ void __launch_bounds__(BT, 4) moe_batch_down(MoeBatchParams p) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int rows = p.dn_rows, lpr = BT / rows;
+    const int nrb = (p.H + rows - 1) / rows;
     const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
     if (g >= *p.n_groups) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
-    const int F = p.F, nb = F / 256;
-    const uint8_t *D = p.experts[3 * e + 2];
-    for (int rr = warp; rr < 32; rr += BT / 32) {
-        const int r = rb * 32 + rr;
-        const uint8_t *row = D + (size_t)r * p.rbd;
-        for (int q = p0; q < p1; ++q) {
-            const ActQ8 a{p.hq + (size_t)q * F, p.hd + (size_t)q * (F / 32), p.hs32 + (size_t)q * (F / 32),
-                          p.hs16 + (size_t)q * (F / 16), 0};
-            double v = partial_q8<DT>(row, nb, a, lane);
-            v = warp_sum_d(v);
-            if (lane == 0) p.part[(size_t)q * p.H + r] = (float)v;
+    const int U = p.F / 64;
+    const int r0 = rb * rows, nrows = min(rows, p.H - r0);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + (size_t)rows * p.rbd);
+    const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.F);
+    {
+        uint8_t *dst[1] = {sm};
+        const uint8_t *src[1] = {p.experts[3 * e + 2] + (size_t)r0 * p.rbd};
+        const uint32_t bytes[1] = {(uint32_t)nrows * p.rbd};
+        issue_tiles(bar, 1, dst, src, bytes);
+    }
+    const int sub = threadIdx.x % lpr, rr = threadIdx.x / lpr, r = r0 + rr;
+    const bool valid = rr < nrows;
+    const uint8_t *row = sm + (size_t)(valid ? rr : 0) * p.rbd;
+    bool tiles_in = false;
+    for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
+        const int nc = min(ACT_TOKS, p1 - c0);
+        __syncthreads();
+        stage_act(sa, nc, [&](int i) { return h_act(p, c0 + i); });
+        cp_async_wait_all();
+        __syncthreads();
+        if (!tiles_in) {
+            if (!wait_tiles(bar, p.status)) return;
+            tiles_in = true;
+        }
+        for (int i0 = 0; i0 < nc; i0 += BTC) {
+            const int nq = min(BTC, nc - i0);
+            double acc[BTC];
+#pragma unroll
+            for (int i = 0; i < BTC; ++i) acc[i] = 0.0;
+            if (valid) {
+                for (int u = sub; u < U; u += lpr) {
+                    const auto w = load_dec<DT>(row, u);
+#pragma unroll
+                    for (int i = 0; i < BTC; ++i)
+                        if (i < nq) acc[i] += dec_dot<DT>(w, u, sa.at(i0 + i));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < BTC; ++i) {
+                const double v = row_sum(acc[i], lpr);
+                if (valid && sub == 0 && i < nq)
+                    p.part[(size_t)(c0 + i0 + i) * p.H + r] = (float)v;
+            }
         }
     }
 }
@@ -277,10 +433,13 @@ __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
             *reinterpret_cast<int4 *>(ep_slot(p, p.ep_send, d, t)) = make_int4(0, t, 0, 0);
         return;
     }
+    __shared__ float s_lg[1024];
+    for (int i = threadIdx.x; i < p.n_experts; i += BT) s_lg[i] = p.logits[(size_t)t * p.n_experts + i];
+    __syncthreads();
     if (warp == 0) {
         int id;
         float w;
-        route_token(p.logits + (size_t)t * p.n_experts, p.n_experts, K, p.norm, lane, &id, &w);
+        route_token(s_lg, p.n_experts, K, p.norm, lane, &id, &w);
         if (lane < K) {
             s_ids[lane] = id;
             s_w[lane] = w;
@@ -367,18 +526,51 @@ __global__ void __launch_bounds__(BT) moe_ep_combine_tokens(MoeBatchParams p) {
     p.Y[i] = (float)acc;
 }
 
+// Largest power-of-two row count in [8, 64] whose tile fits `budget` bytes.
+static int tile_rows(uint32_t bytes_per_row, int cap, size_t budget) {
+    int r = cap;
+    while (r > 8 && (size_t)r * bytes_per_row > budget) r >>= 1;
+    return r;
+}
+
+template <typename KernelT>
+static void set_smem(KernelT k, size_t bytes) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
 // group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots)
 static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
+    // three CTAs per SM: weight tile + staged activations within ~70 KB each
+    const size_t budget = 70 * 1024 - (size_t)ACT_TOKS * act_slot_bytes(p.H > p.F ? p.H : p.F);
+    p.gu_rows = tile_rows(p.rbg + p.rbu, 16, budget);
+    p.dn_rows = tile_rows(p.rbd, 64, budget);
     moe_batch_group<<<1, (p.n_experts + 31) / 32 * 32, 0, st>>>(p);
-    const int ggrid = max_groups * (p.F / 32);
-    if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
-    else if (p.gate_type == T_Q4_K) moe_batch_gateup<T_Q4_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
-    else if (p.up_type == T_Q4_K) moe_batch_gateup<T_Q6_K, T_Q4_K><<<ggrid, BT, 0, st>>>(p);
-    else moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, 0, st>>>(p);
+    const int ggrid = max_groups * ((p.F + p.gu_rows - 1) / p.gu_rows);
+    const size_t gsm = (size_t)p.gu_rows * (p.rbg + p.rbu) + 16 + (size_t)ACT_TOKS * act_slot_bytes(p.H);
+    if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K) {
+        set_smem(moe_batch_gateup<T_Q4_K, T_Q4_K>, gsm);
+        moe_batch_gateup<T_Q4_K, T_Q4_K><<<ggrid, BT, gsm, st>>>(p);
+    } else if (p.gate_type == T_Q4_K) {
+        set_smem(moe_batch_gateup<T_Q4_K, T_Q6_K>, gsm);
+        moe_batch_gateup<T_Q4_K, T_Q6_K><<<ggrid, BT, gsm, st>>>(p);
+    } else if (p.up_type == T_Q4_K) {
+        set_smem(moe_batch_gateup<T_Q6_K, T_Q4_K>, gsm);
+        moe_batch_gateup<T_Q6_K, T_Q4_K><<<ggrid, BT, gsm, st>>>(p);
+    } else {
+        set_smem(moe_batch_gateup<T_Q6_K, T_Q6_K>, gsm);
+        moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, gsm, st>>>(p);
+    }
     const int P = p.T * p.K;
     moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
-    if (p.down_type == T_Q6_K) moe_batch_down<T_Q6_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
-    else moe_batch_down<T_Q4_K><<<max_groups * (p.H / 32), BT, 0, st>>>(p);
+    const int dgrid = max_groups * ((p.H + p.dn_rows - 1) / p.dn_rows);
+    const size_t dsm = (size_t)p.dn_rows * p.rbd + 16 + (size_t)ACT_TOKS * act_slot_bytes(p.F);
+    if (p.down_type == T_Q6_K) {
+        set_smem(moe_batch_down<T_Q6_K>, dsm);
+        moe_batch_down<T_Q6_K><<<dgrid, BT, dsm, st>>>(p);
+    } else {
+        set_smem(moe_batch_down<T_Q4_K>, dsm);
+        moe_batch_down<T_Q4_K><<<dgrid, BT, dsm, st>>>(p);
+    }
 }
 
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
