@@ -528,6 +528,7 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
     b.rbu = pl.rbu;
     b.rbd = pl.rbd;
     b.status = g_status_dev;
+    b.sms = g_num_sms;
     return b;
 }
 

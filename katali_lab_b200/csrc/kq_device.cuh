@@ -395,6 +395,66 @@ __device__ __forceinline__ double unit_dot(const typename UnitOf<T>::type &w, in
     if constexpr (T == T_Q4_K) return q4k_q8_unit_w(w, u, a);
     else return q6k_q8_unit_w(w, u, a);
 }
+// Activations with the per-block scale and 32-element sum already widened to
+// double (both exact), so a dot needs no conversion for them: (double)(m * s32)
+// equals (double)m * (double)s32 because the product is an exact integer.
+struct ActQ8D {
+    const int8_t *q;
+    const double *d, *s32;
+    const int *s16;
+    int pad;
+};
+__device__ __forceinline__ int qposd(const ActQ8D &a, int e) { return e + (a.pad ? ((e >> 6) << 4) : 0); }
+
+__device__ __forceinline__ double q4k_q8_decd(const Q4Dec &w, int u, const ActQ8D &a) {
+    const int g = 8 * (u >> 2) + 2 * (u & 3);
+    const uint4 *ap = reinterpret_cast<const uint4 *>(a.q + qposd(a, 32 * g));
+    const uint4 a0 = ap[0], a1 = ap[1], a2 = ap[2], a3 = ap[3];
+    int lo = 0, hi = 0;
+    lo = __dp4a((int)w.lo[0], (int)a0.x, lo);
+    hi = __dp4a((int)w.hi[0], (int)a2.x, hi);
+    lo = __dp4a((int)w.lo[1], (int)a0.y, lo);
+    hi = __dp4a((int)w.hi[1], (int)a2.y, hi);
+    lo = __dp4a((int)w.lo[2], (int)a0.z, lo);
+    hi = __dp4a((int)w.hi[2], (int)a2.z, hi);
+    lo = __dp4a((int)w.lo[3], (int)a0.w, lo);
+    hi = __dp4a((int)w.hi[3], (int)a2.w, hi);
+    lo = __dp4a((int)w.lo[4], (int)a1.x, lo);
+    hi = __dp4a((int)w.hi[4], (int)a3.x, hi);
+    lo = __dp4a((int)w.lo[5], (int)a1.y, lo);
+    hi = __dp4a((int)w.hi[5], (int)a3.y, hi);
+    lo = __dp4a((int)w.lo[6], (int)a1.z, lo);
+    hi = __dp4a((int)w.hi[6], (int)a3.z, hi);
+    lo = __dp4a((int)w.lo[7], (int)a1.w, lo);
+    hi = __dp4a((int)w.hi[7], (int)a3.w, hi);
+    const double dx0 = a.d[g], dx1 = a.d[g + 1];
+    return ((w.d * dx0) * (double)(w.sc0 * lo) - (w.dmin * dx0) * ((double)w.m0 * a.s32[g])) +
+           ((w.d * dx1) * (double)(w.sc1 * hi) - (w.dmin * dx1) * ((double)w.m1 * a.s32[g + 1]));
+}
+__device__ __forceinline__ double q6k_q8_decd(const Q6Dec &w, int u, const ActQ8D &a) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
+    const int jA = 8 * b + 4 * h + qo, jB = jA + 2;
+    const uint4 *aA = reinterpret_cast<const uint4 *>(a.q + qposd(a, 32 * jA));
+    const uint4 *aB = reinterpret_cast<const uint4 *>(a.q + qposd(a, 32 * jB));
+    const uint4 xA0 = aA[0], xA1 = aA[1], xB0 = aB[0], xB1 = aB[1];
+    const uint32_t wa[8] = {xA0.x, xA0.y, xA0.z, xA0.w, xA1.x, xA1.y, xA1.z, xA1.w};
+    const uint32_t wb[8] = {xB0.x, xB0.y, xB0.z, xB0.w, xB1.x, xB1.y, xB1.z, xB1.w};
+    int sA0 = 0, sA1 = 0, sB0 = 0, sB1 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sA0 = __dp4a((int)w.vA[i], (int)wa[i], sA0);
+        sB0 = __dp4a((int)w.vB[i], (int)wb[i], sB0);
+    }
+#pragma unroll
+    for (int i = 4; i < 8; ++i) {
+        sA1 = __dp4a((int)w.vA[i], (int)wa[i], sA1);
+        sB1 = __dp4a((int)w.vB[i], (int)wb[i], sB1);
+    }
+    const int IA = w.s0 * (sA0 - 32 * a.s16[2 * jA]) + w.s1 * (sA1 - 32 * a.s16[2 * jA + 1]);
+    const int IB = w.s4 * (sB0 - 32 * a.s16[2 * jB]) + w.s5 * (sB1 - 32 * a.s16[2 * jB + 1]);
+    return (w.d * a.d[jA]) * (double)IA + (w.d * a.d[jB]) * (double)IB;
+}
+
 template <uint32_t T>
 struct DecOf {
     using type = Q4Dec;
@@ -412,6 +472,11 @@ template <uint32_t T>
 __device__ __forceinline__ double dec_dot(const typename DecOf<T>::type &w, int u, const ActQ8 &a) {
     if constexpr (T == T_Q4_K) return q4k_q8_dec(w, u, a);
     else return q6k_q8_dec(w, u, a);
+}
+template <uint32_t T>
+__device__ __forceinline__ double dec_dot(const typename DecOf<T>::type &w, int u, const ActQ8D &a) {
+    if constexpr (T == T_Q4_K) return q4k_q8_decd(w, u, a);
+    else return q6k_q8_decd(w, u, a);
 }
 
 // 16-byte asynchronous global -> shared copy (cp.async, L2 only); completes at

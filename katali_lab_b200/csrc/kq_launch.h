@@ -101,6 +101,7 @@ struct MoeBatchParams {
     int32_t *ep_src_ids;
     volatile uint32_t *status;  // device-side timeout bits (mapped host word)
     int gu_rows, dn_rows;       // row-tile heights, set by the launcher
+    int sms;                    // SM count (persistent grids)
 };
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);

@@ -197,25 +197,25 @@ __device__ __forceinline__ double row_sum(double v, int lpr) {
 // 64), scales, 32- and 16-element sums. Returns the slot stride of the values.
 constexpr int ACT_TOKS = 4;  // activation rows staged at a time
 __host__ __device__ constexpr int act_q_stride(int L) { return L + L / 4; }
-__host__ __device__ constexpr int act_slot_bytes(int L) { return act_q_stride(L) + L / 32 * 8 + L / 16 * 4; }
+__host__ __device__ constexpr int act_slot_bytes(int L) { return act_q_stride(L) + L / 32 * 16 + L / 16 * 4; }
 
 struct SmemAct {
     int8_t *q;
-    float *d;
-    int *s32, *s16;
+    double *d, *s32;
+    int *s16;
     int L;
-    __device__ ActQ8 at(int i) const {
-        return ActQ8{q + (size_t)i * act_q_stride(L), d + (size_t)i * (L / 32),
-                     s32 + (size_t)i * (L / 32), s16 + (size_t)i * (L / 16), 1};
+    __device__ ActQ8D at(int i) const {
+        return ActQ8D{q + (size_t)i * act_q_stride(L), d + (size_t)i * (L / 32),
+                      s32 + (size_t)i * (L / 32), s16 + (size_t)i * (L / 16), 1};
     }
 };
 __device__ __forceinline__ SmemAct smem_act(uint8_t *base, int L) {
     SmemAct a;
     a.L = L;
     a.q = reinterpret_cast<int8_t *>(base);
-    a.d = reinterpret_cast<float *>(base + (size_t)ACT_TOKS * act_q_stride(L));
-    a.s32 = reinterpret_cast<int *>(a.d + ACT_TOKS * (L / 32));
-    a.s16 = a.s32 + ACT_TOKS * (L / 32);
+    a.d = reinterpret_cast<double *>(base + (size_t)ACT_TOKS * act_q_stride(L));
+    a.s32 = a.d + ACT_TOKS * (L / 32);
+    a.s16 = reinterpret_cast<int *>(a.s32 + ACT_TOKS * (L / 32));
     return a;
 }
 // Issues the copies (cp.async) of n activation rows into `sa`; the caller waits
@@ -230,10 +230,10 @@ __device__ __forceinline__ void stage_act(const SmemAct &sa, int n, RowOf row_of
     for (int idx = threadIdx.x; idx < n * nb; idx += BT) {
         const int i = idx / nb, b = idx % nb;
         const ActQ8 src = row_of(i);
-        cp_async4(sa.d + i * nb + b, src.d + b);
-        cp_async4(sa.s32 + i * nb + b, src.s32 + b);
         cp_async4(sa.s16 + (i * nb + b) * 2, src.s16 + 2 * b);
         cp_async4(sa.s16 + (i * nb + b) * 2 + 1, src.s16 + 2 * b + 1);
+        sa.d[i * nb + b] = (double)src.d[b];
+        sa.s32[i * nb + b] = (double)src.s32[b];
     }
 }
 
@@ -304,7 +304,7 @@ __global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
 #pragma unroll
                     for (int i = 0; i < BTC; ++i) {
                         if (i < nq) {
-                            const ActQ8 a = sa.at(i0 + i);
+                            const ActQ8D a = sa.at(i0 + i);
                             ag[i] += dec_dot<GT>(wg, u, a);
                             au[i] += dec_dot<UT>(wu, u, a);
                         }
