@@ -39,7 +39,8 @@ typedef enum KataliStatus {
     KATALI_ERR_UNSUPPORTED_SHAPE = 5,
     KATALI_ERR_TIMEOUT = 6,           /* a bounded device-side wait gave up */
     KATALI_ERR_CUDA = 7,
-    KATALI_ERR_NCCL = 8
+    KATALI_ERR_NCCL = 8,
+    KATALI_ERR_NOT_RESIDENT = 9  /* a call selected an expert with no device copy */
 } KataliStatus;
 
 /* GGUF tensor type ids used here (V/include/katali_gguf_dtype.h:20-41). */
@@ -122,7 +123,9 @@ typedef struct KataliMoeDesc {
     uint32_t gate_type, up_type, down_type;  /* Q4_K, Q4_K, Q6_K */
     uint32_t flags;       /* KATALI_MOE_NORM_TOPK */
     /* HOST array of 3*n_experts device pointers: gate_e, up_e, down_e for each
-     * expert e (16-byte aligned). NULL leaves every expert unset. */
+     * expert e (16-byte aligned). NULL leaves every expert unset. A NULL entry
+     * is an expert that is not resident: a call that selects it returns
+     * KATALI_ERR_NOT_RESIDENT (checked on the device; nothing is read). */
     const void *const *experts;
 } KataliMoeDesc;
 
@@ -213,6 +216,41 @@ int katali_cuda_ep_destroy(KataliEp *ep);
 int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens,
                              uint32_t n_tokens, const float *x, const float *router_logits,
                              float *y);
+
+/* ------------------------------------------------------------------------ */
+/* 7. Expert residency tier (the reference's expert cache, README.md:13,21,   */
+/*    329-333; its API is binary-only, these entry points are new)           */
+/* ------------------------------------------------------------------------ */
+/* n_slots device slots of slot_bytes each; one slot holds one expert's gate,
+ * up and down matrices (native GGUF bytes, each 16-byte aligned in the slot).
+ * Uploads run on the cache's own stream; the compute stream waits on events. */
+typedef struct KataliExpertCache KataliExpertCache;
+int katali_cuda_expert_cache_create(uint64_t slot_bytes, uint32_t n_slots,
+                                    KataliExpertCache **out);
+/* Layers still bound to the cache see their bound experts as not resident. */
+int katali_cuda_expert_cache_destroy(KataliExpertCache *c);
+/* Registers expert `key` (any caller id, e.g. layer * n_experts + e) with its
+ * borrowed HOST matrices (e.g. inside an mmap'd GGUF file; they must stay
+ * valid). The ranges are page-locked when possible so uploads are async. */
+int katali_cuda_expert_register(KataliExpertCache *c, uint64_t key, const void *gate,
+                                uint64_t gate_bytes, const void *up, uint64_t up_bytes,
+                                const void *down, uint64_t down_bytes);
+/* Starts the upload of `key` into a free or least-recently-used slot and
+ * returns at once (a resident key is only marked used). A refilled slot's
+ * upload waits for every compute call enqueued before it. */
+int katali_cuda_expert_prefetch_async(KataliExpertCache *c, uint64_t key);
+/* Makes expert e of layer m use the device copy of `key` (uploading it if
+ * needed): compute calls enqueued after this wait for the upload. When the
+ * slot is later refilled or evicted, the entry becomes NULL (not resident). */
+int katali_cuda_expert_bind(KataliExpertCache *c, uint64_t key, KataliMoe *m, uint32_t e);
+/* Drops `key` from the device; its bindings become NULL. */
+int katali_cuda_expert_evict(KataliExpertCache *c, uint64_t key);
+/* *resident = 1 when `key` is on the device (its slot's pointers returned in
+ * gate/up/down, each may be NULL), else 0. */
+int katali_cuda_expert_lookup(KataliExpertCache *c, uint64_t key, int *resident, void **gate,
+                              void **up, void **down);
+/* Waits for every upload started so far. */
+int katali_cuda_expert_sync(KataliExpertCache *c);
 
 /* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */

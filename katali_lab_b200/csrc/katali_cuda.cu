@@ -87,6 +87,10 @@ int take_device_status() {
     const uint32_t s = *(volatile uint32_t *)g_status_host;
     if (s) {
         *(volatile uint32_t *)g_status_host = 0;
+        if (s & kq::KQ_STATUS_NOT_RESIDENT) {
+            snprintf(g_status, sizeof g_status, "a selected expert is not resident (bits 0x%x)", s);
+            return KATALI_ERR_NOT_RESIDENT;
+        }
         snprintf(g_status, sizeof g_status, "device-side wait timed out (bits 0x%x)", s);
         return KATALI_ERR_TIMEOUT;
     }
@@ -151,7 +155,28 @@ struct KataliMoe {
     size_t bscratch_bytes;
     int32_t *ep_src_ids;  // routing of the last katali_cuda_moe_ep_dispatch
     uint32_t ep_src_cap;  // tokens
+    KataliExpertCache *cache;  // the residency cache this layer's experts are bound to
 };
+
+namespace kq {
+void cache_forget_layer(KataliExpertCache *c, KataliMoe *m);
+
+// Stream-ordered update of expert e's pointers (no host wait): calls enqueued
+// before keep the old pointers, calls enqueued after see the new ones.
+int moe_set_expert_async(KataliMoe *m, uint32_t e, const void *g, const void *u, const void *d) {
+    if (!m || e >= m->table.size() / 3) return KATALI_ERR_BAD_ARG;
+    m->table[3 * e] = (const uint8_t *)g;
+    m->table[3 * e + 1] = (const uint8_t *)u;
+    m->table[3 * e + 2] = (const uint8_t *)d;
+    // pageable source: the three pointers are captured before cudaMemcpyAsync returns
+    const cudaError_t err = cudaMemcpyAsync(m->d_table + 3 * e, &m->table[3 * e], 3 * sizeof(void *),
+                                            cudaMemcpyHostToDevice, g_stream);
+    return err == cudaSuccess ? KATALI_OK : cuda_fail(err);
+}
+uint32_t moe_n_experts(const KataliMoe *m) { return (uint32_t)(m->table.size() / 3); }
+KataliExpertCache *moe_cache(const KataliMoe *m) { return m->cache; }
+void moe_set_cache(KataliMoe *m, KataliExpertCache *c) { m->cache = c; }
+}  // namespace kq
 
 namespace {
 
@@ -218,6 +243,7 @@ const char *katali_cuda_strerror(int s) {
         case KATALI_ERR_UNSUPPORTED_TYPE: return "unsupported tensor type";
         case KATALI_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
         case KATALI_ERR_TIMEOUT: return "device-side wait timed out";
+        case KATALI_ERR_NOT_RESIDENT: return "selected expert not resident";
         case KATALI_ERR_CUDA: return "CUDA error";
         case KATALI_ERR_NCCL: return "NCCL error";
         default: return "unknown status";
@@ -445,6 +471,7 @@ int katali_cuda_moe_set_expert(KataliMoe *m, uint32_t e, const void *gate, const
 
 int katali_cuda_moe_destroy(KataliMoe *m) {
     if (!m) return KATALI_OK;
+    if (m->cache) kq::cache_forget_layer(m->cache, m);
     if (g_stream) cudaStreamSynchronize(g_stream);
     cudaFree(m->d_table);
     cudaFree(m->hbuf);
@@ -461,8 +488,6 @@ static int moe_run(KataliMoe *m, const float *x, const float *logits, const int3
                    const float *w, float *y, uint32_t mode, int route_only) {
     if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
     if (!m->plan_ok[mode]) return KATALI_ERR_UNSUPPORTED_SHAPE;
-    for (const uint8_t *t : m->table)
-        if (!t) return KATALI_ERR_BAD_ARG;  // every expert must be resident
     kq::MoeParams p = m->plan[mode];
     p.experts = m->d_table;
     p.x = x;
@@ -539,8 +564,6 @@ int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
     if (!x || !router_logits || !y || !aligned16(x) || n_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
         return KATALI_ERR_BAD_ARG;
     if (mode != KATALI_MOE_Q8_1) return KATALI_ERR_UNSUPPORTED_TYPE;
-    for (const uint8_t *t : m->table)
-        if (!t) return KATALI_ERR_BAD_ARG;
     int s = grow_batch_scratch(m, (int)n_tokens);
     if (s) return s;
     kq::MoeBatchParams b = batch_params(m, (int)n_tokens);
@@ -614,9 +637,6 @@ int katali_cuda_moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank,
     if (s) return s;
     if (rank >= n_ranks || !recv || !ret || !aligned16(recv) || !aligned16(ret))
         return KATALI_ERR_BAD_ARG;
-    const size_t per = m->table.size() / 3 / n_ranks;
-    for (size_t i = 3 * per * rank; i < 3 * per * (rank + 1); ++i)
-        if (!m->table[i]) return KATALI_ERR_BAD_ARG;  // this rank's experts must be resident
     const int T = (int)(n_ranks * max_tokens);
     s = grow_batch_scratch(m, T);
     if (s) return s;

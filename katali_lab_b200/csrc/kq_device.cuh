@@ -153,6 +153,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Completes `bytes` of a barrier's expected transaction count without a copy (an
+// expert that is not resident: its copy is skipped and the call reports it).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
 // L2 policy for streamed weights: read once per call, so they are marked
 // evict-first and do not push code, pointer tables and activations out of L2.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

@@ -6,6 +6,11 @@
 
 namespace kq {
 
+// Status bits the kernels set in the mapped status word (1, 2, 4: a bounded
+// wait gave up).
+constexpr uint32_t KQ_STATUS_NOT_RESIDENT = 8u;  // a selected expert has no device copy
+
+
 struct GemvJob {
     const uint8_t *w;  // device matrix, native GGUF rows, 16-byte aligned
     float *y;

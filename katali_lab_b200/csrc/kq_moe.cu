@@ -59,7 +59,13 @@ __device__ __forceinline__ void trace(const MoeParams &p, int slot) {
 }
 
 __device__ __forceinline__ void bulk_g2s_split(uint8_t *dst, const uint8_t *src, uint32_t bytes,
-                                               uint64_t *bar, uint64_t pol) {
+                                               uint64_t *bar, uint64_t pol,
+                                               volatile uint32_t *status = nullptr) {
+    if (!src) {  // expert not resident: account for the bytes, report, copy nothing
+        if (status) atomicOr((uint32_t *)status, KQ_STATUS_NOT_RESIDENT);
+        mbar_complete_tx(bar, bytes);
+        return;
+    }
     while (bytes) {
         const uint32_t n = bytes > 32768u ? 32768u : bytes;
         bulk_g2s_hint(dst, src, n, bar, pol);
@@ -383,13 +389,15 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 const int k = (int)(blk / (F / HB));
                 const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
                 const uint32_t rb = up ? rbu : rbg;
-                const uint8_t *src = s_tab[3 * s_ids[k] + up] + (size_t)j0 * rb;
+                const uint8_t *base = s_tab[3 * s_ids[k] + up];
+                const uint8_t *src = base ? base + (size_t)j0 * rb : nullptr;
                 uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
-                bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol);
+                bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol, p.status);
             } else {  // down rows [rB0, rB0 + nrB) of selected expert k
                 const int k = q - 2 * nchunk;
-                bulk_g2s_split(sb + (size_t)k * (per + 16), s_tab[3 * s_ids[k] + 2] + (size_t)rB0 * rbd,
-                               per, &bars[NBARS - 1], pol);
+                const uint8_t *base = s_tab[3 * s_ids[k] + 2];
+                bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
+                               per, &bars[NBARS - 1], pol, p.status);
             }
         }
         trace(p, 3);

@@ -267,6 +267,10 @@ __global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
     const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
     const int F = p.F, K = p.K, U = p.H / 64;
     const int j0 = rb * rows, nrows = min(rows, F - j0);
+    if (!p.experts[3 * e] || !p.experts[3 * e + 1]) {  // not resident: report, skip
+        if (threadIdx.x == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+        return;
+    }
     uint8_t *sg = sm, *su = sm + (size_t)rows * p.rbg;
     uint64_t *bar = reinterpret_cast<uint64_t *>(su + (size_t)rows * p.rbu);
     const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.H);
@@ -348,6 +352,10 @@ __global__ void __launch_bounds__(BT, 4) moe_batch_down(MoeBatchParams p) {
     const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
     const int U = p.F / 64;
     const int r0 = rb * rows, nrows = min(rows, p.H - r0);
+    if (!p.experts[3 * e + 2]) {  // not resident: report, skip
+        if (threadIdx.x == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+        return;
+    }
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm + (size_t)rows * p.rbd);
     const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.F);
     {

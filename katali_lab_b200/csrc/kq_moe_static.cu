@@ -92,8 +92,8 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     const uint64_t rbg = rbytes(d->gate_type, d->hidden), rbu = rbytes(d->up_type, d->hidden);
     const uint64_t rbd = rbytes(d->down_type, d->ffn);
     if (!rbg || !rbu || !rbd || rbg % 16 || rbu % 16) return KATALI_ERR_UNSUPPORTED_SHAPE;
-    for (uint32_t i = 0; i < 3 * d->n_experts; ++i)
-        if (!d->experts[i] || ((uintptr_t)d->experts[i] & 15u)) return KATALI_ERR_BAD_ARG;
+    for (uint32_t i = 0; i < 3 * d->n_experts; ++i)  // NULL: not resident (checked on device)
+        if ((uintptr_t)d->experts[i] & 15u) return KATALI_ERR_BAD_ARG;
 
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
@@ -138,5 +138,6 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     e = cudaMemcpyAsync(&status, sync + 2, sizeof status, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return KATALI_ERR_CUDA;
+    if (status & kq::KQ_STATUS_NOT_RESIDENT) return KATALI_ERR_NOT_RESIDENT;
     return status ? KATALI_ERR_TIMEOUT : KATALI_OK;
 }

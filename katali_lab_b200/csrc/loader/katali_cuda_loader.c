@@ -74,6 +74,22 @@
     X(int, katali_cuda_moe_ep_combine,                                                        \
       (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const void *b, float *y),          \
       (m, g, tm, n, b, y))                                                                    \
+    X(int, katali_cuda_expert_cache_create, (uint64_t b, uint32_t n, KataliExpertCache **o),  \
+      (b, n, o))                                                                              \
+    X(int, katali_cuda_expert_cache_destroy, (KataliExpertCache * c), (c))                    \
+    X(int, katali_cuda_expert_register,                                                       \
+      (KataliExpertCache * c, uint64_t k, const void *g, uint64_t gb, const void *u,          \
+       uint64_t ub, const void *d, uint64_t db),                                              \
+      (c, k, g, gb, u, ub, d, db))                                                            \
+    X(int, katali_cuda_expert_prefetch_async, (KataliExpertCache * c, uint64_t k), (c, k))    \
+    X(int, katali_cuda_expert_bind, (KataliExpertCache * c, uint64_t k, KataliMoe * m,        \
+                                     uint32_t e),                                             \
+      (c, k, m, e))                                                                           \
+    X(int, katali_cuda_expert_evict, (KataliExpertCache * c, uint64_t k), (c, k))             \
+    X(int, katali_cuda_expert_lookup,                                                         \
+      (KataliExpertCache * c, uint64_t k, int *r, void **g, void **u, void **d),              \
+      (c, k, r, g, u, d))                                                                     \
+    X(int, katali_cuda_expert_sync, (KataliExpertCache * c), (c))                             \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -201,6 +217,22 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_moe_ep_combine,                                                        \
       (KataliMoe * m, uint32_t g, uint32_t tm, uint32_t n, const void *b, float *y),          \
       (m, g, tm, n, b, y))                                                                    \
+    X(int, katali_cuda_expert_cache_create, (uint64_t b, uint32_t n, KataliExpertCache **o),  \
+      (b, n, o))                                                                              \
+    X(int, katali_cuda_expert_cache_destroy, (KataliExpertCache * c), (c))                    \
+    X(int, katali_cuda_expert_register,                                                       \
+      (KataliExpertCache * c, uint64_t k, const void *g, uint64_t gb, const void *u,          \
+       uint64_t ub, const void *d, uint64_t db),                                              \
+      (c, k, g, gb, u, ub, d, db))                                                            \
+    X(int, katali_cuda_expert_prefetch_async, (KataliExpertCache * c, uint64_t k), (c, k))    \
+    X(int, katali_cuda_expert_bind, (KataliExpertCache * c, uint64_t k, KataliMoe * m,        \
+                                     uint32_t e),                                             \
+      (c, k, m, e))                                                                           \
+    X(int, katali_cuda_expert_evict, (KataliExpertCache * c, uint64_t k), (c, k))             \
+    X(int, katali_cuda_expert_lookup,                                                         \
+      (KataliExpertCache * c, uint64_t k, int *r, void **g, void **u, void **d),              \
+      (c, k, r, g, u, d))                                                                     \
+    X(int, katali_cuda_expert_sync, (KataliExpertCache * c), (c))                             \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

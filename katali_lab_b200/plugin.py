@@ -94,6 +94,15 @@ class Plugin:
             "katali_cuda_moe_ep_dispatch": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp], _i32),
             "katali_cuda_moe_ep_experts": ([_vp, _u32, _u32, _u32, _vp, _vp], _i32),
             "katali_cuda_moe_ep_combine": ([_vp, _u32, _u32, _u32, _vp, _vp], _i32),
+            "katali_cuda_expert_cache_create": ([_u64, _u32, C.POINTER(_vp)], _i32),
+            "katali_cuda_expert_cache_destroy": ([_vp], _i32),
+            "katali_cuda_expert_register": ([_vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64], _i32),
+            "katali_cuda_expert_prefetch_async": ([_vp, _u64], _i32),
+            "katali_cuda_expert_bind": ([_vp, _u64, _vp, _u32], _i32),
+            "katali_cuda_expert_evict": ([_vp, _u64], _i32),
+            "katali_cuda_expert_lookup": ([_vp, _u64, C.POINTER(_i32), C.POINTER(_vp), C.POINTER(_vp),
+                                           C.POINTER(_vp)], _i32),
+            "katali_cuda_expert_sync": ([_vp], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -222,3 +231,47 @@ class MoeLayer:
             self.close()
         except Exception:
             pass
+
+
+class ExpertCache:
+    """The plugin's expert residency tier (katali_cuda_expert_*): device slots fed from
+    host memory by asynchronous uploads on a side stream."""
+
+    def __init__(self, plugin: Plugin, slot_bytes: int, n_slots: int):
+        self.p = plugin
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_expert_cache_create(slot_bytes, n_slots, C.byref(h)))
+        self.h = h
+        self._keep = {}  # host arrays must outlive their registration
+
+    def register(self, key: int, gate, up, down) -> None:
+        """gate/up/down: contiguous host numpy uint8 arrays (borrowed, kept alive here)."""
+        self._keep[key] = (gate, up, down)
+        self.p.check(self.p.L.katali_cuda_expert_register(
+            self.h, key, gate.ctypes.data, gate.nbytes, up.ctypes.data, up.nbytes,
+            down.ctypes.data, down.nbytes))
+
+    def prefetch(self, key: int) -> None:
+        self.p.check(self.p.L.katali_cuda_expert_prefetch_async(self.h, key))
+
+    def bind(self, key: int, layer: "MoeLayer", e: int) -> None:
+        self.p.check(self.p.L.katali_cuda_expert_bind(self.h, key, layer.h, e))
+
+    def evict(self, key: int) -> None:
+        self.p.check(self.p.L.katali_cuda_expert_evict(self.h, key))
+
+    def lookup(self, key: int):
+        """None when not resident, else the (gate, up, down) device addresses."""
+        r = _i32()
+        g, u, d = _vp(), _vp(), _vp()
+        self.p.check(self.p.L.katali_cuda_expert_lookup(self.h, key, C.byref(r), C.byref(g),
+                                                        C.byref(u), C.byref(d)))
+        return (g.value, u.value, d.value) if r.value else None
+
+    def sync(self) -> None:
+        self.p.check(self.p.L.katali_cuda_expert_sync(self.h))
+
+    def close(self) -> None:
+        if self.h:
+            self.p.L.katali_cuda_expert_cache_destroy(self.h)
+            self.h = None
