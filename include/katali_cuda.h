@@ -253,6 +253,48 @@ int katali_cuda_expert_lookup(KataliExpertCache *c, uint64_t key, int *resident,
 int katali_cuda_expert_sync(KataliExpertCache *c);
 
 /* ------------------------------------------------------------------------ */
+/* 8. Dense decoder decode on the device (the reference's dense CPU forward,  */
+/*    V/src/gguf_model.c:570-703, with its per-projection GPU crossings       */
+/*    removed; README.md:164-171). Qwen3 layout: RMSNorm, q/k/v, per-head q/k  */
+/*    RMSNorm, RoPE, GQA with an fp32 KV cache, o + residual, RMSNorm,         */
+/*    gate/up, SiLU * up, down + residual, final RMSNorm, LM head, greedy.     */
+/* ------------------------------------------------------------------------ */
+typedef struct KataliDenseLayerW {
+    const float *attn_norm, *ffn_norm;  /* device fp32, hidden entries */
+    const float *q_norm, *k_norm;       /* device fp32, head_dim entries, or NULL */
+    const void *wq, *wk, *wv, *wo, *gate, *up, *down;  /* device GGUF matrices */
+    uint32_t wq_type, wk_type, wv_type, wo_type, gate_type, up_type, down_type;
+} KataliDenseLayerW;
+
+typedef struct KataliDenseDesc {
+    uint32_t n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim, vocab;
+    uint32_t kv_cap;    /* positions in the KV cache (<= 51200) */
+    uint32_t rope_dim;  /* 0 = head_dim */
+    float rms_eps, rope_theta;
+    const void *embed;  /* device, vocab rows of `hidden` (embed_type) */
+    uint32_t embed_type;
+    const float *out_norm;  /* device fp32, hidden entries */
+    const void *lm_head;    /* device, vocab rows of `hidden` (lm_head_type) */
+    uint32_t lm_head_type;
+    const KataliDenseLayerW *layers;  /* HOST array of n_layers (copied) */
+} KataliDenseDesc;
+
+typedef struct KataliDense KataliDense;
+int katali_cuda_dense_create(const KataliDenseDesc *desc, KataliDense **out);
+int katali_cuda_dense_destroy(KataliDense *m);
+/* Empties the KV cache (next position 0). */
+int katali_cuda_dense_reset(KataliDense *m);
+/* Greedy decode continuing at the current position: feeds prompt[0..n_prompt)
+ * (HOST ints), then feeds back each argmax; out_tokens (HOST) receives the
+ * n_gen generated tokens (the argmax after the last prompt token first). The
+ * whole loop stays on the device (one graph replay per step). */
+int katali_cuda_dense_generate(KataliDense *m, const int32_t *prompt, uint32_t n_prompt,
+                               uint32_t n_gen, int32_t *out_tokens);
+/* Device pointer to the logits of the last step (vocab floats) and the next
+ * position. */
+int katali_cuda_dense_logits(KataliDense *m, const float **logits_dev, int32_t *position);
+
+/* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
 /* ------------------------------------------------------------------------ */
 /* Integer in-block sums of every row against q8_1 xq. Q4_K: per 32-group

@@ -137,6 +137,9 @@ namespace kq {
 // Lets other translation units of the plugin report a reason via katali_cuda_status().
 void set_status_message(const char *msg) { snprintf(g_status, sizeof g_status, "%s", msg); }
 cudaStream_t current_stream() { return g_stream; }
+volatile uint32_t *device_status_word() { return g_status_dev; }
+// After the stream was synchronised: KATALI_OK or the device-side status.
+int take_status_after_sync() { return take_device_status(); }
 }  // namespace kq
 
 struct KataliMoe {

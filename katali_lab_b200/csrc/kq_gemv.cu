@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
                 part = J.type == T_Q4_K ? q4k_q8_partial(row, nb, a, lane)
                                         : q6k_q8_partial(row, nb, a, lane);
             part = warp_sum_d(part);
-            if (lane == 0) J.y[r0 + r] = (float)part;
+            if (lane == 0) J.y[r0 + r] = J.accum ? __fadd_rn(J.y[r0 + r], (float)part) : (float)part;
         }
         g += nrows;
         __syncwarp();

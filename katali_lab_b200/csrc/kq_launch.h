@@ -19,6 +19,7 @@ struct GemvJob {
     uint32_t rb;     // bytes per row
     uint32_t tr;     // rows per tile (set by the launcher)
     uint32_t tile0;  // first global tile of this job (set by the launcher)
+    uint32_t accum;  // 1: y[r] += W x (the residual add of a decoder layer), else y[r] = W x
 };
 
 struct GemvParams {
@@ -113,5 +114,31 @@ cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st);
 int moe_plan(MoeParams &p, int grid, int max_smem);
+
+// Dense decoder decode step (kq_dense.cu).
+struct DenseLayer {  // host-side view for the launcher
+    const float *attn_norm, *ffn_norm;
+};
+struct DenseParams {
+    int H, F, NH, NKV, HD, NL, vocab, kv_cap, rope_half;
+    float eps, attn_scale;
+    const uint8_t *embed;
+    uint32_t embed_type, embed_rb;
+    const float *out_norm;
+    const DenseLayer *L;              // host array, n_layers
+    const float *const *q_norm_dev;   // device arrays of n_layers pointers (entries may be NULL)
+    const float *const *k_norm_dev;
+    float *x, *xb, *q, *k, *v, *attn, *gate, *up, *logits;
+    float *kv_k, *kv_v;               // [NL][NKV][kv_cap][HD]
+    const float *rope_cos, *rope_sin; // [kv_cap][rope_half]
+    int *tok, *pos, *step, *n_forced; // device control words
+    const int *forced;                // prompt tokens (forced inputs)
+    int *out_tokens;                  // argmax of every step of a call
+    int out_cap;
+    float *arg_v;
+    int *arg_i;
+};
+cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st);
+cudaError_t dense_set_attention_smem(int kv_cap);
 
 }  // namespace kq

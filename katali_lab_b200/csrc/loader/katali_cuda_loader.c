@@ -90,6 +90,14 @@
       (KataliExpertCache * c, uint64_t k, int *r, void **g, void **u, void **d),              \
       (c, k, r, g, u, d))                                                                     \
     X(int, katali_cuda_expert_sync, (KataliExpertCache * c), (c))                             \
+    X(int, katali_cuda_dense_create, (const KataliDenseDesc *d, KataliDense **o), (d, o))     \
+    X(int, katali_cuda_dense_destroy, (KataliDense * m), (m))                                 \
+    X(int, katali_cuda_dense_reset, (KataliDense * m), (m))                                   \
+    X(int, katali_cuda_dense_generate,                                                        \
+      (KataliDense * m, const int32_t *p, uint32_t np, uint32_t ng, int32_t *o),              \
+      (m, p, np, ng, o))                                                                      \
+    X(int, katali_cuda_dense_logits, (KataliDense * m, const float **l, int32_t *p),          \
+      (m, l, p))                                                                              \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -233,6 +241,14 @@ const char *katali_cuda_strerror(int s) {
       (KataliExpertCache * c, uint64_t k, int *r, void **g, void **u, void **d),              \
       (c, k, r, g, u, d))                                                                     \
     X(int, katali_cuda_expert_sync, (KataliExpertCache * c), (c))                             \
+    X(int, katali_cuda_dense_create, (const KataliDenseDesc *d, KataliDense **o), (d, o))     \
+    X(int, katali_cuda_dense_destroy, (KataliDense * m), (m))                                 \
+    X(int, katali_cuda_dense_reset, (KataliDense * m), (m))                                   \
+    X(int, katali_cuda_dense_generate,                                                        \
+      (KataliDense * m, const int32_t *p, uint32_t np, uint32_t ng, int32_t *o),              \
+      (m, p, np, ng, o))                                                                      \
+    X(int, katali_cuda_dense_logits, (KataliDense * m, const float **l, int32_t *p),          \
+      (m, l, p))                                                                              \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

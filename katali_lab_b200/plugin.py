@@ -30,6 +30,21 @@ class KataliError(RuntimeError):
         self.code = code
 
 
+class KataliDenseLayerW(C.Structure):
+    _fields_ = [("attn_norm", _vp), ("ffn_norm", _vp), ("q_norm", _vp), ("k_norm", _vp),
+                ("wq", _vp), ("wk", _vp), ("wv", _vp), ("wo", _vp), ("gate", _vp), ("up", _vp),
+                ("down", _vp), ("wq_type", _u32), ("wk_type", _u32), ("wv_type", _u32),
+                ("wo_type", _u32), ("gate_type", _u32), ("up_type", _u32), ("down_type", _u32)]
+
+
+class KataliDenseDesc(C.Structure):
+    _fields_ = [("n_layers", _u32), ("hidden", _u32), ("ffn", _u32), ("n_heads", _u32),
+                ("n_kv_heads", _u32), ("head_dim", _u32), ("vocab", _u32), ("kv_cap", _u32),
+                ("rope_dim", _u32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
+                ("embed", _vp), ("embed_type", _u32), ("out_norm", _vp), ("lm_head", _vp),
+                ("lm_head_type", _u32), ("layers", C.POINTER(KataliDenseLayerW))]
+
+
 class KataliMoeDesc(C.Structure):
     _fields_ = [("n_experts", _u32), ("hidden", _u32), ("ffn", _u32), ("top_k", _u32),
                 ("gate_type", _u32), ("up_type", _u32), ("down_type", _u32), ("flags", _u32),
@@ -103,6 +118,11 @@ class Plugin:
             "katali_cuda_expert_lookup": ([_vp, _u64, C.POINTER(_i32), C.POINTER(_vp), C.POINTER(_vp),
                                            C.POINTER(_vp)], _i32),
             "katali_cuda_expert_sync": ([_vp], _i32),
+            "katali_cuda_dense_create": ([C.POINTER(KataliDenseDesc), C.POINTER(_vp)], _i32),
+            "katali_cuda_dense_destroy": ([_vp], _i32),
+            "katali_cuda_dense_reset": ([_vp], _i32),
+            "katali_cuda_dense_generate": ([_vp, _vp, _u32, _u32, _vp], _i32),
+            "katali_cuda_dense_logits": ([_vp, C.POINTER(_vp), C.POINTER(_i32)], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -274,4 +294,53 @@ class ExpertCache:
     def close(self) -> None:
         if self.h:
             self.p.L.katali_cuda_expert_cache_destroy(self.h)
+            self.h = None
+
+
+class DenseModel:
+    """A dense Qwen3-style decoder resident on the device (katali_cuda_dense_*)."""
+
+    def __init__(self, plugin: Plugin, model):
+        """model: katali_lab_b200.synth.DenseWeights (device tensors) or any object with the
+        same attributes."""
+        self.p = plugin
+        cfg = model.cfg
+        ly = (KataliDenseLayerW * cfg.n_layers)()
+        for l, w in enumerate(model.layers):
+            ly[l] = KataliDenseLayerW(
+                _ptr(w["attn_norm"]), _ptr(w["ffn_norm"]), _ptr(w.get("q_norm")),
+                _ptr(w.get("k_norm")), _ptr(w["wq"]), _ptr(w["wk"]), _ptr(w["wv"]), _ptr(w["wo"]),
+                _ptr(w["gate"]), _ptr(w["up"]), _ptr(w["down"]), *[model.types[k] for k in
+                ("wq", "wk", "wv", "wo", "gate", "up", "down")])
+        self._layers = ly
+        desc = KataliDenseDesc(cfg.n_layers, cfg.hidden, cfg.ffn, cfg.n_heads, cfg.n_kv_heads,
+                               cfg.head_dim, cfg.vocab, cfg.kv_cap, cfg.rope_dim, cfg.rms_eps,
+                               cfg.rope_theta, _ptr(model.embed), model.types["embed"],
+                               _ptr(model.out_norm), _ptr(model.lm_head), model.types["lm_head"],
+                               C.cast(ly, C.POINTER(KataliDenseLayerW)))
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_dense_create(C.byref(desc), C.byref(h)))
+        self.h = h
+        self.vocab = cfg.vocab
+
+    def reset(self) -> None:
+        self.p.check(self.p.L.katali_cuda_dense_reset(self.h))
+
+    def generate(self, prompt, n_gen: int):
+        import numpy as np
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, dtype=np.int32)
+        self.p.check(self.p.L.katali_cuda_dense_generate(self.h, pr.ctypes.data, pr.size, n_gen,
+                                                         out.ctypes.data))
+        return out
+
+    def logits(self):
+        """(device address of the last step's logits, next position)."""
+        ptr, pos = _vp(), _i32()
+        self.p.check(self.p.L.katali_cuda_dense_logits(self.h, C.byref(ptr), C.byref(pos)))
+        return ptr.value, pos.value
+
+    def close(self) -> None:
+        if self.h:
+            self.p.L.katali_cuda_dense_destroy(self.h)
             self.h = None

@@ -82,3 +82,75 @@ def make_dense(plugin: Plugin, qtype: int, rows: int, cols: int, seed: int, std:
     gen.manual_seed(seed)
     w = torch.randn((rows, cols), generator=gen, device=device, dtype=torch.float32).mul_(std)
     return quantize_matrix(plugin, qtype, w)
+
+
+# ---------------------------------------------------------------------------
+# Dense decoder (Qwen3 layout) with synthetic weights
+# ---------------------------------------------------------------------------
+@dataclass
+class DenseConfig:
+    n_layers: int
+    hidden: int
+    ffn: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    kv_cap: int
+    rope_dim: int = 0
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+
+
+# Qwen3-8B shape (36 layers, hidden 4096, FFN 12288, 32 q / 8 kv heads of 128, vocab 151936).
+QWEN3_8B = DenseConfig(36, 4096, 12288, 32, 8, 128, 151936, 4096)
+
+# "Q4_K_M"-style types: Q4_K everywhere except Q6_K for attn_v, ffn_down and the output.
+DENSE_TYPES = {"wq": Q4_K, "wk": Q4_K, "wv": Q6_K, "wo": Q4_K, "gate": Q4_K, "up": Q4_K,
+               "down": Q6_K, "embed": Q4_K, "lm_head": Q6_K}
+
+
+@dataclass
+class DenseWeights:
+    cfg: DenseConfig
+    embed: torch.Tensor
+    lm_head: torch.Tensor
+    out_norm: torch.Tensor
+    layers: list
+    types: dict
+
+    @property
+    def weight_bytes_per_token(self) -> int:
+        """Quantised bytes one decode step reads (every matrix once, one embedding row)."""
+        n = self.lm_head.numel() + self.embed.shape[1]
+        for w in self.layers:
+            n += sum(w[k].numel() for k in ("wq", "wk", "wv", "wo", "gate", "up", "down"))
+        return n
+
+
+def make_dense_model(plugin: Plugin, cfg: DenseConfig, seed: int, std: float = 0.02) -> DenseWeights:
+    """Weights ~ N(0, std) encoded on the device; norm weights 1 + 0.1 N(0, 1) (fp32)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    H, F, NH, NKV, HD = cfg.hidden, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+    T = DENSE_TYPES
+
+    def mat(kind, rows, cols):
+        w = torch.randn((rows, cols), generator=gen, device="cuda", dtype=torch.float32).mul_(std)
+        return quantize_matrix(plugin, T[kind], w)
+
+    def norm(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=gen, device="cuda", dtype=torch.float32)).contiguous()
+
+    layers = []
+    for _ in range(cfg.n_layers):
+        layers.append({
+            "attn_norm": norm(H), "ffn_norm": norm(H), "q_norm": norm(HD), "k_norm": norm(HD),
+            "wq": mat("wq", NH * HD, H), "wk": mat("wk", NKV * HD, H), "wv": mat("wv", NKV * HD, H),
+            "wo": mat("wo", H, NH * HD), "gate": mat("gate", F, H), "up": mat("up", F, H),
+            "down": mat("down", H, F)})
+    embed = mat("embed", cfg.vocab, H)
+    lm_head = mat("lm_head", cfg.vocab, H)
+    out_norm = norm(H)
+    torch.cuda.synchronize()
+    return DenseWeights(cfg, embed, lm_head, out_norm, layers, dict(T))

@@ -345,3 +345,52 @@ def rel_l2(a, b) -> float:
     b = np.asarray(b, dtype=np.float64)
     den = np.linalg.norm(b)
     return float(np.linalg.norm(a - b) / (den if den > 0 else 1.0))
+
+
+class RefDense:
+    """The dense decode step composed from the reference's kernels (kref_dense_*), on HOST
+    copies of a katali_lab_b200.synth.DenseWeights model."""
+
+    def __init__(self, ref: "Ref", model, n_threads: int = 0):
+        import torch  # noqa: F401  (host copies come from torch tensors)
+        cfg = model.cfg
+        self.ref, self.cfg = ref, cfg
+        h = lambda t: np.ascontiguousarray(t.cpu().numpy())  # noqa: E731
+        self._keep = []
+        keep = self._keep.append
+        NL = cfg.n_layers
+        an = (C.c_void_p * NL)(); fn = (C.c_void_p * NL)(); qn = (C.c_void_p * NL)(); kn = (C.c_void_p * NL)()
+        ws = (C.c_void_p * (7 * NL))(); ts = (C.c_uint32 * (7 * NL))()
+        names = ("wq", "wk", "wv", "wo", "gate", "up", "down")
+        for l, w in enumerate(model.layers):
+            for arr, key in ((an, "attn_norm"), (fn, "ffn_norm"), (qn, "q_norm"), (kn, "k_norm")):
+                a = h(w[key]); keep(a); arr[l] = a.ctypes.data
+            for i, k in enumerate(names):
+                a = h(w[k]); keep(a); ws[7 * l + i] = a.ctypes.data; ts[7 * l + i] = model.types[k]
+        emb, lm, on = h(model.embed), h(model.lm_head), h(model.out_norm)
+        for a in (emb, lm, on, an, fn, qn, kn, ws, ts):
+            keep(a)
+        L = ref.L
+        L.kref_dense_new.restype = C.c_void_p
+        L.kref_dense_new.argtypes = [C.c_int] * 9 + [C.c_float, C.c_float, C.c_void_p, C.c_uint32,
+                                                     C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p,
+                                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                     C.c_void_p, C.c_int]
+        L.kref_dense_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.kref_dense_free.argtypes = [C.c_void_p]
+        self.h = L.kref_dense_new(NL, cfg.hidden, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                                  cfg.vocab, cfg.kv_cap, cfg.rope_dim, cfg.rms_eps, cfg.rope_theta,
+                                  emb.ctypes.data, model.types["embed"], lm.ctypes.data,
+                                  model.types["lm_head"], on.ctypes.data, an, fn, qn, kn, ws, ts,
+                                  n_threads or os.cpu_count() or 1)
+        self.logits = np.zeros(cfg.vocab, dtype=np.float32)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        if self.ref.L.kref_dense_step(self.h, int(token), int(pos), self.logits.ctypes.data) != 0:
+            raise ValueError("kref_dense_step failed")
+        return self.logits
+
+    def close(self):
+        if self.h:
+            self.ref.L.kref_dense_free(self.h)
+            self.h = None

@@ -140,3 +140,128 @@ int kref_moe_layer(int n_experts, int hidden, int ffn, int top_k, int norm_topk,
     if (w_out) memcpy(w_out, w, sizeof(float) * (size_t)top_k);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Dense decoder decode step composed from the reference's kernels, following */
+/* gguf_forward_token (V/src/gguf_model.c:570-703) call by call: embedding     */
+/* row (katali_ggml_dequant_ref), katali_gguf_rmsnorm, q/k/v through           */
+/* katali_ggml_matvec, per-head katali_gguf_rmsnorm_inplace, RoPE with the      */
+/* rope_prepare table (:466-475, rope_inv from :344) through                    */
+/* katali_gguf_rope_apply, KV append, katali_gguf_gqa_decode_scratch, o + add,  */
+/* gate/up, katali_ggml_silu_mul_avx2 (scalar silu without AVX2), down + add,   */
+/* final norm and the LM head. Weights and norms are HOST arrays.               */
+/* ------------------------------------------------------------------------ */
+typedef struct KrefDenseLayer {
+    const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+    const void *w[7]; /* wq wk wv wo gate up down */
+    uint32_t t[7];
+} KrefDenseLayer;
+
+typedef struct KrefDense {
+    int NL, H, F, NH, NKV, HD, vocab, cap, rd, n_threads;
+    float eps, theta;
+    const void *embed, *lm;
+    uint32_t embed_t, lm_t;
+    const float *out_norm;
+    KrefDenseLayer *L;
+    float *x, *xb, *q, *k, *v, *attn, *gate, *up, *down, *logits, *kv_k, *kv_v;
+    float *scores, *rope_inv, *rope_cos, *rope_sin;
+} KrefDense;
+
+void *kref_dense_new(int NL, int H, int F, int NH, int NKV, int HD, int vocab, int cap,
+                     int rope_dim, float eps, float theta, const void *embed, uint32_t embed_t,
+                     const void *lm, uint32_t lm_t, const float *out_norm,
+                     const float *const *attn_norm, const float *const *ffn_norm,
+                     const float *const *q_norm, const float *const *k_norm,
+                     const void *const *w /* 7 per layer */, const uint32_t *t, int n_threads) {
+    KrefDense *m = (KrefDense *)calloc(1, sizeof(*m));
+    if (!m) return NULL;
+    m->NL = NL; m->H = H; m->F = F; m->NH = NH; m->NKV = NKV; m->HD = HD; m->vocab = vocab;
+    m->cap = cap; m->eps = eps; m->theta = theta; m->n_threads = n_threads;
+    m->rd = (rope_dim == 0 || rope_dim > HD) ? HD : rope_dim;
+    m->embed = embed; m->embed_t = embed_t; m->lm = lm; m->lm_t = lm_t; m->out_norm = out_norm;
+    m->L = (KrefDenseLayer *)calloc((size_t)NL, sizeof(KrefDenseLayer));
+    for (int l = 0; l < NL; l++) {
+        m->L[l].attn_norm = attn_norm[l];
+        m->L[l].ffn_norm = ffn_norm[l];
+        m->L[l].q_norm = q_norm ? q_norm[l] : NULL;
+        m->L[l].k_norm = k_norm ? k_norm[l] : NULL;
+        for (int i = 0; i < 7; i++) { m->L[l].w[i] = w[7 * l + i]; m->L[l].t[i] = t[7 * l + i]; }
+    }
+    m->x = (float *)calloc((size_t)H, 4); m->xb = (float *)calloc((size_t)H, 4);
+    m->q = (float *)calloc((size_t)NH * HD, 4); m->k = (float *)calloc((size_t)NKV * HD, 4);
+    m->v = (float *)calloc((size_t)NKV * HD, 4); m->attn = (float *)calloc((size_t)NH * HD, 4);
+    m->gate = (float *)calloc((size_t)F, 4); m->up = (float *)calloc((size_t)F, 4);
+    m->down = (float *)calloc((size_t)H, 4); m->logits = (float *)calloc((size_t)vocab, 4);
+    m->kv_k = (float *)calloc((size_t)NL * NKV * cap * HD, 4);
+    m->kv_v = (float *)calloc((size_t)NL * NKV * cap * HD, 4);
+    m->scores = (float *)calloc((size_t)cap, 4);
+    m->rope_inv = (float *)calloc((size_t)m->rd / 2, 4);
+    m->rope_cos = (float *)calloc((size_t)m->rd / 2, 4);
+    m->rope_sin = (float *)calloc((size_t)m->rd / 2, 4);
+    for (int i = 0; i < m->rd / 2; i++)
+        m->rope_inv[i] = 1.0f / powf(theta, (2.0f * (float)i) / (float)m->rd);
+    return m;
+}
+
+void kref_dense_free(void *p) {
+    KrefDense *m = (KrefDense *)p;
+    if (!m) return;
+    free(m->L); free(m->x); free(m->xb); free(m->q); free(m->k); free(m->v); free(m->attn);
+    free(m->gate); free(m->up); free(m->down); free(m->logits); free(m->kv_k); free(m->kv_v);
+    free(m->scores); free(m->rope_inv); free(m->rope_cos); free(m->rope_sin);
+    free(m);
+}
+
+/* One step at position pos with input token; logits_out may be NULL. */
+int kref_dense_step(void *p, int token, int pos, float *logits_out) {
+    KrefDense *m = (KrefDense *)p;
+    if (!m || token < 0 || token >= m->vocab || pos < 0 || pos >= m->cap) return -1;
+    const int H = m->H, F = m->F, NH = m->NH, NKV = m->NKV, HD = m->HD, nt = m->n_threads;
+    const uint64_t erb = katali_ggml_row_bytes(m->embed_t, (uint64_t)H);
+    if (katali_ggml_dequant_ref(m->embed_t, (const uint8_t *)m->embed + (size_t)token * erb,
+                                (uint64_t)H, m->x) != 0)
+        return -1;
+    const int half = m->rd / 2;
+    for (int i = 0; i < half; i++) {
+        float freq = (float)pos * m->rope_inv[i];
+        m->rope_cos[i] = cosf(freq);
+        m->rope_sin[i] = sinf(freq);
+    }
+    const size_t per_layer = (size_t)NKV * m->cap * HD;
+    for (int l = 0; l < m->NL; l++) {
+        const KrefDenseLayer *L = &m->L[l];
+        katali_gguf_rmsnorm(m->x, L->attn_norm, (size_t)H, m->eps, m->xb);
+        kref_matvec(L->t[0], L->w[0], (uint64_t)NH * HD, (uint64_t)H, m->xb, m->q, nt);
+        kref_matvec(L->t[1], L->w[1], (uint64_t)NKV * HD, (uint64_t)H, m->xb, m->k, nt);
+        kref_matvec(L->t[2], L->w[2], (uint64_t)NKV * HD, (uint64_t)H, m->xb, m->v, nt);
+        if (L->q_norm)
+            for (int h = 0; h < NH; h++)
+                katali_gguf_rmsnorm_inplace(m->q + (size_t)h * HD, L->q_norm, (size_t)HD, m->eps);
+        katali_gguf_rope_apply(m->q, (size_t)NH, (size_t)HD, (size_t)m->rd, m->rope_cos, m->rope_sin);
+        if (L->k_norm)
+            for (int h = 0; h < NKV; h++)
+                katali_gguf_rmsnorm_inplace(m->k + (size_t)h * HD, L->k_norm, (size_t)HD, m->eps);
+        katali_gguf_rope_apply(m->k, (size_t)NKV, (size_t)HD, (size_t)m->rd, m->rope_cos, m->rope_sin);
+        float *lk = m->kv_k + (size_t)l * per_layer, *lv = m->kv_v + (size_t)l * per_layer;
+        for (int h = 0; h < NKV; h++) {
+            memcpy(lk + ((size_t)h * m->cap + pos) * HD, m->k + (size_t)h * HD, (size_t)HD * 4);
+            memcpy(lv + ((size_t)h * m->cap + pos) * HD, m->v + (size_t)h * HD, (size_t)HD * 4);
+        }
+        katali_gguf_gqa_decode_scratch(m->q, lk, lv, (size_t)pos + 1, (size_t)m->cap, (size_t)NH,
+                                       (size_t)NKV, (size_t)HD, m->attn, m->scores);
+        kref_matvec(L->t[3], L->w[3], (uint64_t)H, (uint64_t)NH * HD, m->attn, m->down, nt);
+        katali_gguf_add_inplace(m->x, m->down, (size_t)H);
+        katali_gguf_rmsnorm(m->x, L->ffn_norm, (size_t)H, m->eps, m->xb);
+        kref_matvec(L->t[4], L->w[4], (uint64_t)F, (uint64_t)H, m->xb, m->gate, nt);
+        kref_matvec(L->t[5], L->w[5], (uint64_t)F, (uint64_t)H, m->xb, m->up, nt);
+        if (katali_ggml_silu_mul_avx2(m->gate, m->up, (size_t)F) != 0)
+            for (int i = 0; i < F; i++) m->gate[i] = katali_gguf_silu(m->gate[i]) * m->up[i];
+        kref_matvec(L->t[6], L->w[6], (uint64_t)H, (uint64_t)F, m->gate, m->down, nt);
+        katali_gguf_add_inplace(m->x, m->down, (size_t)H);
+    }
+    katali_gguf_rmsnorm(m->x, m->out_norm, (size_t)H, m->eps, m->xb);
+    kref_matvec(m->lm_t, m->lm, (uint64_t)m->vocab, (uint64_t)H, m->xb, m->logits, nt);
+    if (logits_out) memcpy(logits_out, m->logits, (size_t)m->vocab * 4);
+    return 0;
+}
