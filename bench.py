@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3"],
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4"],
                     help="c2: fused MoE layer (headline); c1: dense Q4_K GEMV 6144x2048")
     ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
@@ -808,6 +808,92 @@ def run_ep(args, rank, world, local_rank):
         l.close()
 
 
+C4_WORKLOAD = ("C4 dense Qwen3-8B-shape greedy decode on one GPU: 36 layers, hidden 4096, FFN 12288, "
+               "32 q / 8 kv heads of 128, vocab 151936, fp32 KV cache; Q4_K with Q6_K attn_v, "
+               "ffn_down and output (N(0,0.02) weights); {n} tokens per step after a 1-token prompt")
+
+
+def run_c4(args, rank, world, local_rank):
+    """C4: katali_cuda_dense_generate; a step = one greedy generation of `calls` tokens from
+    an empty cache. metric = quantised weight bytes read per second (every matrix once per
+    token); tokens/s in config."""
+    import torch
+
+    from katali_lab_b200 import DenseModel, Plugin
+    from katali_lab_b200.synth import QWEN3_8B, make_dense_model
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    model = make_dense_model(plugin, QWEN3_8B, seed=8 + rank)
+    plugin.set_stream(stream)
+    dm = DenseModel(plugin, model, q8=args.dp4a)
+    n = args.calls * 2  # 128 tokens by default
+    prompt = [1]
+    for _ in range(max(args.warmup, 3)):
+        dm.reset()
+        dm.generate(prompt, n)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        s0.record(stream)
+        for _ in range(args.steps):
+            dm.reset()
+            toks = dm.generate(prompt, n)
+        s1.record(stream)
+        s1.synchronize()
+    ms = s0.elapsed_time(s1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    bpt = model.weight_bytes_per_token
+    tok_s = world * args.steps * n / (ms / 1e3)
+    value = tok_s * bpt / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        from oracle.oracle import Ref, RefDense
+        ref = RefDense(Ref(), model)
+        cores = os.cpu_count() or 1
+        t0, k, tok = time.perf_counter(), 0, 1
+        while time.perf_counter() - t0 < args.cpu_seconds or k < 2:
+            lg = ref.step(tok, k)
+            tok = int(np.argmax(lg))
+            k += 1
+        el = time.perf_counter() - t0
+        ref.close()
+        cpu = {"value": round(k * bpt / el / 1e9, 3), "unit": "GB/s", "cores": cores,
+               "kind": "reference", "tokens_per_s": round(k / el, 3),
+               "sample": f"{k} greedy decode steps ({el:.1f} s) of the same model through the "
+                         f"reference's CPU kernels (gguf_forward_token composition), {cores} threads"}
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = value / world
+        print(json.dumps({
+            "metric": "dense decode quant-weight GB/s vs HBM peak", "value": round(value, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32",
+            "data": "synthetic",
+            "config": {"workload": C4_WORKLOAD.format(n=n), "tokens_per_step": n,
+                       "activations": "q8_1 (DP4A)" if args.dp4a else "fp32",
+                       "tokens_per_s": round(tok_s, 1), "weight_bytes_per_token": bpt,
+                       "us_per_token": round(1e3 * ms / (args.steps * n), 2),
+                       "l2": "inputs larger than L2: 4.9 GB of weights read per token",
+                       "parallelism": f"replicas x{world}", "last_tokens": [int(t) for t in toks[:8]]},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "scope": "whole decode step (all kernels)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * len(prompt),
+                    "d2h_bytes_per_step": 4 * n},
+            "gpu_launches": args.steps * n * (2 + 9 * 36 + 3), "cpu_baseline": cpu}), flush=True)
+    dm.close()
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -827,6 +913,8 @@ def main():
     try:
         if args.config == "c1":
             run_c1(args, rank, world, local_rank)
+        elif args.config == "c4":
+            run_c4(args, rank, world, local_rank)
         elif world > 1 and not args.replicas:
             run_ep(args, rank, world, local_rank)
         elif args.config == "c3":

@@ -277,7 +277,12 @@ typedef struct KataliDenseDesc {
     const void *lm_head;    /* device, vocab rows of `hidden` (lm_head_type) */
     uint32_t lm_head_type;
     const KataliDenseLayerW *layers;  /* HOST array of n_layers (copied) */
+    uint32_t flags;  /* KATALI_DENSE_Q8_1: projections with q8_1 activations (DP4A) */
 } KataliDenseDesc;
+/* Projections quantise their fp32 input to q8_1 on the device and use integer
+ * block dots (the reference's KATALI_CUDA_DP4A mode, README.md:17); default:
+ * fp32 activations, the parity mode against the CPU path. */
+#define KATALI_DENSE_Q8_1 1u
 
 typedef struct KataliDense KataliDense;
 int katali_cuda_dense_create(const KataliDenseDesc *desc, KataliDense **out);

@@ -216,11 +216,16 @@ __global__ void k_argmax_part(DenseParams p) {
     }
 }
 __global__ void k_argmax_final(DenseParams p, int nparts) {
-    if (threadIdx.x != 0) return;
     float bv = -INFINITY;
     int bi = -1;
-    for (int b = 0; b < nparts; ++b)
+    for (int b = threadIdx.x; b < nparts; b += 32)
         if (p.arg_i[b] >= 0) better(bv, bi, p.arg_v[b], p.arg_i[b]);
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(KQ_FULL, bv, o);
+        const int oi = __shfl_xor_sync(KQ_FULL, bi, o);
+        if (oi >= 0) better(bv, bi, ov, oi);
+    }
+    if (threadIdx.x != 0) return;
     const int step = *p.step;
     if (step < p.out_cap) p.out_tokens[step] = bi < 0 ? 0 : bi;
     // the next step's input: the forced prompt token while prefilling, else this argmax
@@ -238,18 +243,18 @@ cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st) {
     for (int l = 0; l < p.NL; ++l) {
         const DenseLayer &L = p.L[l];
         k_rmsnorm<<<1, 1024, 0, st>>>(p.x, L.attn_norm, p.H, p.eps, p.xb);
-        cudaError_t e = launch_gemv(g[4 * l + 0], 2, st);
+        cudaError_t e = launch_gemv(g[4 * l + 0], p.gemv_mode, st);
         if (e != cudaSuccess) return e;
         k_qk_rope<<<p.NH + p.NKV, p.HD, 0, st>>>(p, l);
         k_attention<<<p.NH, DT, (size_t)p.kv_cap * sizeof(float), st>>>(p, l);
-        if ((e = launch_gemv(g[4 * l + 1], 2, st)) != cudaSuccess) return e;
+        if ((e = launch_gemv(g[4 * l + 1], p.gemv_mode, st)) != cudaSuccess) return e;
         k_rmsnorm<<<1, 1024, 0, st>>>(p.x, L.ffn_norm, p.H, p.eps, p.xb);
-        if ((e = launch_gemv(g[4 * l + 2], 2, st)) != cudaSuccess) return e;
+        if ((e = launch_gemv(g[4 * l + 2], p.gemv_mode, st)) != cudaSuccess) return e;
         k_silu_mul<<<(p.F + DT - 1) / DT, DT, 0, st>>>(p.gate, p.up, p.F);
-        if ((e = launch_gemv(g[4 * l + 3], 2, st)) != cudaSuccess) return e;
+        if ((e = launch_gemv(g[4 * l + 3], p.gemv_mode, st)) != cudaSuccess) return e;
     }
     k_rmsnorm<<<1, 1024, 0, st>>>(p.x, p.out_norm, p.H, p.eps, p.xb);
-    cudaError_t e = launch_gemv(g[4 * p.NL], 2, st);
+    cudaError_t e = launch_gemv(g[4 * p.NL], p.gemv_mode, st);
     if (e != cudaSuccess) return e;
     k_argmax_part<<<nparts, DT, 0, st>>>(p);
     k_argmax_final<<<1, 32, 0, st>>>(p, nparts);

@@ -82,6 +82,10 @@ int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
         return bad("katali_cuda_dense_create: zero dimension");
     if (NH % NKV || HD > 512 || HD % 32 || H % 256 || F % 256 || (NH * HD) % 256)
         return KATALI_ERR_UNSUPPORTED_SHAPE;
+    if (d->flags & ~KATALI_DENSE_Q8_1) return bad("katali_cuda_dense_create: unknown flags");
+    // widest projection input (fp32 staging in the GEMV): fp32 24576 columns, q8_1 65536
+    if ((d->flags & KATALI_DENSE_Q8_1) ? (F > 65536 || NH * HD > 65536) : (F > 24576 || NH * HD > 24576))
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
     const uint32_t rd = (d->rope_dim == 0 || d->rope_dim > HD) ? HD : d->rope_dim;
     if ((uint64_t)d->kv_cap * 4 > 200 * 1024) return KATALI_ERR_UNSUPPORTED_SHAPE;  // scores in smem
     if (!rbytes(d->embed_type, H) || !rbytes(d->lm_head_type, H) || !a16(d->embed) ||
@@ -139,6 +143,7 @@ int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
     p.kv_cap = (int)cap;
     p.rope_half = (int)rh;
     p.eps = d->rms_eps;
+    p.gemv_mode = (d->flags & KATALI_DENSE_Q8_1) ? 0 : 2;
     p.attn_scale = 1.0f / sqrtf((float)HD);  // as the reference's attention (gguf_kernels.c)
     p.embed = (const uint8_t *)d->embed;
     p.embed_type = d->embed_type;

@@ -500,6 +500,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // fp32 activations x (shared) with per-32-group sums xs.
+// Byte k (0..3) of w, an integer below 2^23, as float minus `bias`: the byte is
+// placed under the exponent of 2^23 (0x4B000000) by one byte permute and one
+// float add removes 2^23 + bias. Exact, and cheaper than an int -> float conversion.
+__device__ __forceinline__ float byte_as_float(uint32_t w, int k, float bias2p23) {
+    return __fsub_rn(__int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)k)), bias2p23);
+}
+constexpr float TWO23 = 8388608.0f;         // 2^23
+constexpr float TWO23_P32 = 8388640.0f;     // 2^23 + 32 (Q6_K values are stored + 32)
+
 __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const float *x,
                                                const float *xs, int pad = 0) {
     const int b = u >> 2, c = u & 3;
@@ -514,15 +523,15 @@ __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const 
     for (int i = 0; i < 8; ++i) {
         const float4 xa = *reinterpret_cast<const float4 *>(xl + 4 * i);
         const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 + 4 * i);
-        const uint32_t w = ww[i];
-        lo = fmaf((float)(w & 15u), xa.x, lo);
-        hi = fmaf((float)((w >> 4) & 15u), xb.x, hi);
-        lo = fmaf((float)((w >> 8) & 15u), xa.y, lo);
-        hi = fmaf((float)((w >> 12) & 15u), xb.y, hi);
-        lo = fmaf((float)((w >> 16) & 15u), xa.z, lo);
-        hi = fmaf((float)((w >> 20) & 15u), xb.z, hi);
-        lo = fmaf((float)((w >> 24) & 15u), xa.w, lo);
-        hi = fmaf((float)(w >> 28), xb.w, hi);
+        const uint32_t wl = ww[i] & 0x0F0F0F0Fu, wh = (ww[i] >> 4) & 0x0F0F0F0Fu;
+        lo = fmaf(byte_as_float(wl, 0, TWO23), xa.x, lo);
+        hi = fmaf(byte_as_float(wh, 0, TWO23), xb.x, hi);
+        lo = fmaf(byte_as_float(wl, 1, TWO23), xa.y, lo);
+        hi = fmaf(byte_as_float(wh, 1, TWO23), xb.y, hi);
+        lo = fmaf(byte_as_float(wl, 2, TWO23), xa.z, lo);
+        hi = fmaf(byte_as_float(wh, 2, TWO23), xb.z, hi);
+        lo = fmaf(byte_as_float(wl, 3, TWO23), xa.w, lo);
+        hi = fmaf(byte_as_float(wh, 3, TWO23), xb.w, hi);
     }
     int sc0, m0, sc1, m1;
     q4k_scales(h, c, sc0, m0, sc1, m1);
@@ -552,14 +561,14 @@ __device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const 
         const float4 a4 = *reinterpret_cast<const float4 *>(xA + 4 * i);
         const float4 b4 = *reinterpret_cast<const float4 *>(xB + 4 * i);
         float &fa = fA[i >> 2], &fb = fB[i >> 2];
-        fa = fmaf((float)((int)(vA & 63u) - 32), a4.x, fa);
-        fa = fmaf((float)((int)((vA >> 8) & 63u) - 32), a4.y, fa);
-        fa = fmaf((float)((int)((vA >> 16) & 63u) - 32), a4.z, fa);
-        fa = fmaf((float)((int)((vA >> 24) & 63u) - 32), a4.w, fa);
-        fb = fmaf((float)((int)(vB & 63u) - 32), b4.x, fb);
-        fb = fmaf((float)((int)((vB >> 8) & 63u) - 32), b4.y, fb);
-        fb = fmaf((float)((int)((vB >> 16) & 63u) - 32), b4.z, fb);
-        fb = fmaf((float)((int)((vB >> 24) & 63u) - 32), b4.w, fb);
+        fa = fmaf(byte_as_float(vA, 0, TWO23_P32), a4.x, fa);
+        fa = fmaf(byte_as_float(vA, 1, TWO23_P32), a4.y, fa);
+        fa = fmaf(byte_as_float(vA, 2, TWO23_P32), a4.z, fa);
+        fa = fmaf(byte_as_float(vA, 3, TWO23_P32), a4.w, fa);
+        fb = fmaf(byte_as_float(vB, 0, TWO23_P32), b4.x, fb);
+        fb = fmaf(byte_as_float(vB, 1, TWO23_P32), b4.y, fb);
+        fb = fmaf(byte_as_float(vB, 2, TWO23_P32), b4.z, fb);
+        fb = fmaf(byte_as_float(vB, 3, TWO23_P32), b4.w, fb);
     }
     const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
     const float d = h2f(ld_u16(blk + 208));

@@ -137,6 +137,7 @@ struct DenseParams {
     int out_cap;
     float *arg_v;
     int *arg_i;
+    int gemv_mode;                    // 2: fp32 activations, 0: q8_1 (quantised in the GEMV)
 };
 cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st);
 cudaError_t dense_set_attention_smem(int kv_cap);

@@ -42,7 +42,8 @@ class KataliDenseDesc(C.Structure):
                 ("n_kv_heads", _u32), ("head_dim", _u32), ("vocab", _u32), ("kv_cap", _u32),
                 ("rope_dim", _u32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
                 ("embed", _vp), ("embed_type", _u32), ("out_norm", _vp), ("lm_head", _vp),
-                ("lm_head_type", _u32), ("layers", C.POINTER(KataliDenseLayerW))]
+                ("lm_head_type", _u32), ("layers", C.POINTER(KataliDenseLayerW)),
+                ("flags", _u32)]
 
 
 class KataliMoeDesc(C.Structure):
@@ -300,9 +301,9 @@ class ExpertCache:
 class DenseModel:
     """A dense Qwen3-style decoder resident on the device (katali_cuda_dense_*)."""
 
-    def __init__(self, plugin: Plugin, model):
+    def __init__(self, plugin: Plugin, model, q8: bool = False):
         """model: katali_lab_b200.synth.DenseWeights (device tensors) or any object with the
-        same attributes."""
+        same attributes. q8: q8_1 activations (DP4A) instead of fp32."""
         self.p = plugin
         cfg = model.cfg
         ly = (KataliDenseLayerW * cfg.n_layers)()
@@ -317,7 +318,7 @@ class DenseModel:
                                cfg.head_dim, cfg.vocab, cfg.kv_cap, cfg.rope_dim, cfg.rms_eps,
                                cfg.rope_theta, _ptr(model.embed), model.types["embed"],
                                _ptr(model.out_norm), _ptr(model.lm_head), model.types["lm_head"],
-                               C.cast(ly, C.POINTER(KataliDenseLayerW)))
+                               C.cast(ly, C.POINTER(KataliDenseLayerW)), 1 if q8 else 0)
         h = _vp()
         plugin.check(plugin.L.katali_cuda_dense_create(C.byref(desc), C.byref(h)))
         self.h = h

@@ -87,3 +87,16 @@ def test_qwen3_8b_shape_greedy(plugin, ref, port):
     assert model.weight_bytes_per_token == 4923568128 + 2304
     g, c = greedy_both(plugin, ref, port, model, [100, 2000, 30000], 4)
     assert g == c
+
+
+def test_q8_mode_close_to_reference(plugin, ref, port, small):
+    """q8_1 activations (DP4A): logits within 2e-2 rel_L2 of the fp32 CPU reference (the
+    quantisation error of q8_1 activations) and the first greedy token unchanged."""
+    dm = DenseModel(plugin, small, q8=True)
+    rd = RefDense(ref, small)
+    tok = int(dm.generate([5], 1)[0])
+    lc = rd.step(5, 0)
+    lg = logits_of(dm, SMALL.vocab)
+    assert rel_l2(lg, lc) <= 2e-2
+    rd.close()
+    dm.close()
