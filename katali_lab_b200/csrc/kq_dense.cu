@@ -11,6 +11,8 @@
 // and the position from device memory, so one captured CUDA graph serves every
 // step and generation never returns to the host between tokens.
 //
+// RMSNorm runs inside the GEMVs' activation staging (kq_gemv.cu), the per-head q/k
+// RMSNorm and RoPE inside attention, so a layer is six launches.
 // Arithmetic follows the reference's kernels (V/src/gguf_kernels.c):
 //   rmsnorm      :13-25   double sum of squares, inv = 1/sqrtf(mean + eps) in
 //                         float, out = x * inv * w (two float products)
@@ -82,70 +84,64 @@ __global__ void k_embed(DenseParams p) {
         p.x[i] = dequant_elem(p.embed_type, row, i);
 }
 
-// out = rmsnorm(x) * w over n elements (one CTA).
-__global__ void __launch_bounds__(1024) k_rmsnorm(const float *x, const float *w, int n, float eps,
-                                                  float *out) {
-    __shared__ double sh[32];
-    double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i] * (double)x[i];
-    s = block_sum_d(s, sh);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / (double)n), eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], inv), w[i]);
-}
-
-// Per head: RMSNorm over head_dim (q heads with q_norm, k heads with k_norm),
-// RoPE with the table row of the current position, then k and v appended to
-// the layer's KV cache. CTA h < NH: q head h; NH <= h < NH + NKV: k/v head.
-__global__ void k_qk_rope(DenseParams p, int layer) {
-    __shared__ double sh[32];
-    __shared__ float sv[512];
-    const int HD = p.HD, rh = p.rope_half, pos = *p.pos;
-    const bool isq = (int)blockIdx.x < p.NH;
-    const int h = isq ? blockIdx.x : blockIdx.x - p.NH;
-    float *v = (isq ? p.q : p.k) + (size_t)h * HD;
-    const float *nw = isq ? p.q_norm_dev[layer] : p.k_norm_dev[layer];
-    const int i = threadIdx.x;  // blockDim.x == HD
-    float val = v[i];
+// One head of q or k: RMSNorm over head_dim (when nw), then RoPE with the table
+// row of position pos, written to dst (shared memory). All threads of the CTA call it.
+__device__ __forceinline__ void norm_rope_head(const DenseParams &p, const float *src, const float *nw,
+                                               int pos, float *tmp, float *dst, double *sh) {
+    const int HD = p.HD, rh = p.rope_half, i = threadIdx.x;
+    float val = i < HD ? src[i] : 0.0f;
     if (nw) {
-        const double s = block_sum_d((double)val * (double)val, sh);
+        const double s = block_sum_d(i < HD ? (double)val * (double)val : 0.0, sh);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(s / (double)HD), p.eps)));
-        val = __fmul_rn(__fmul_rn(val, inv), nw[i]);
+        if (i < HD) val = __fmul_rn(__fmul_rn(val, inv), nw[i]);
     }
-    sv[i] = val;
+    if (i < HD) tmp[i] = val;
     __syncthreads();
-    float out = val;  // pairs (i, i + rh) for i < rh, rh = rope_dim / 2
-    if (i < rh) {
-        const float c = p.rope_cos[(size_t)pos * rh + i], s = p.rope_sin[(size_t)pos * rh + i];
-        out = __fsub_rn(__fmul_rn(val, c), __fmul_rn(sv[i + rh], s));
-    } else if (i < 2 * rh) {
-        const int j = i - rh;
-        const float c = p.rope_cos[(size_t)pos * rh + j], s = p.rope_sin[(size_t)pos * rh + j];
-        out = __fadd_rn(__fmul_rn(val, c), __fmul_rn(sv[j], s));
+    if (i < HD) {
+        float out = val;  // pairs (i, i + rh) for i < rh, rh = rope_dim / 2
+        if (i < rh) {
+            const float c = p.rope_cos[(size_t)pos * rh + i], s = p.rope_sin[(size_t)pos * rh + i];
+            out = __fsub_rn(__fmul_rn(val, c), __fmul_rn(tmp[i + rh], s));
+        } else if (i < 2 * rh) {
+            const int j = i - rh;
+            const float c = p.rope_cos[(size_t)pos * rh + j], s = p.rope_sin[(size_t)pos * rh + j];
+            out = __fadd_rn(__fmul_rn(val, c), __fmul_rn(tmp[j], s));
+        }
+        dst[i] = out;
     }
-    if (isq) {
-        v[i] = out;
-    } else {
-        const size_t kv_off = ((size_t)layer * p.NKV + h) * p.kv_cap * HD + (size_t)pos * HD + i;
-        p.kv_k[kv_off] = out;
-        p.kv_v[kv_off] = p.v[(size_t)h * HD + i];
-    }
+    __syncthreads();
 }
 
-// Grouped-query decode attention: one CTA per query head over kv_len = pos + 1.
+// Grouped-query decode attention, one CTA per query head over kv_len = pos + 1. The
+// CTA first applies the per-head q/k RMSNorm and RoPE (gguf_forward_token's order:
+// q norm, q rope, k norm, k rope); the first CTA of each kv group appends k and v to
+// the layer's cache, and every CTA uses its own copy of the new k and v for t = pos.
 __global__ void __launch_bounds__(DT) k_attention(DenseParams p, int layer) {
     extern __shared__ float scores[];  // kv_cap floats
     __shared__ double sh[32];
     __shared__ float red[32];
+    __shared__ float sq[512], sk[512], sv[512], tmp[512];
     const int HD = p.HD, hq = blockIdx.x, reps = p.NH / p.NKV;
-    const int hk = hq / reps, kv_len = *p.pos + 1;
-    const float *q = p.q + (size_t)hq * HD;
+    const int hk = hq / reps, pos = *p.pos, kv_len = pos + 1;
+    norm_rope_head(p, p.q + (size_t)hq * HD, p.q_norm_dev[layer], pos, tmp, sq, sh);
+    norm_rope_head(p, p.k + (size_t)hk * HD, p.k_norm_dev[layer], pos, tmp, sk, sh);
     const float *K = p.kv_k + ((size_t)layer * p.NKV + hk) * p.kv_cap * HD;
     const float *V = p.kv_v + ((size_t)layer * p.NKV + hk) * p.kv_cap * HD;
+    if (threadIdx.x < HD) {
+        sv[threadIdx.x] = p.v[(size_t)hk * HD + threadIdx.x];
+        if (hq % reps == 0) {
+            const size_t o = (size_t)pos * HD + threadIdx.x;
+            const_cast<float *>(K)[o] = sk[threadIdx.x];
+            const_cast<float *>(V)[o] = sv[threadIdx.x];
+        }
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // scores: one warp per key row, lanes over head dims, double accumulation
     for (int t = warp; t < kv_len; t += DT / 32) {
+        const float *kt = t == pos ? sk : K + (size_t)t * HD;
         double acc = 0.0;
-        for (int d = lane; d < HD; d += 32) acc += (double)q[d] * (double)K[(size_t)t * HD + d];
+        for (int d = lane; d < HD; d += 32) acc += (double)sq[d] * (double)kt[d];
         acc = warp_sum_d(acc);
         if (lane == 0) scores[t] = __fmul_rn((float)acc, p.attn_scale);
     }
@@ -169,7 +165,8 @@ __global__ void __launch_bounds__(DT) k_attention(DenseParams p, int layer) {
     __syncthreads();
     for (int d = threadIdx.x; d < HD; d += DT) {
         float o = 0.0f;
-        for (int t = 0; t < kv_len; ++t) o = __fadd_rn(o, __fmul_rn(scores[t], V[(size_t)t * HD + d]));
+        for (int t = 0; t < pos; ++t) o = __fadd_rn(o, __fmul_rn(scores[t], V[(size_t)t * HD + d]));
+        o = __fadd_rn(o, __fmul_rn(scores[pos], sv[d]));
         p.attn[(size_t)hq * HD + d] = o;
     }
 }
@@ -237,23 +234,20 @@ __global__ void k_argmax_final(DenseParams p, int nparts) {
 }  // namespace
 
 cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st) {
-    // g[0..4] per layer: qkv, o (+residual), gate/up, down (+residual); g[4*NL] the LM head
+    // g[4 l + 0..3]: qkv (attn RMSNorm in the staging), o (+ residual), gate/up (ffn
+    // RMSNorm in the staging), down (+ residual) after SiLU * up; g[4 NL]: the LM head
+    // (final RMSNorm in the staging).
     const int nparts = 148;
     k_embed<<<(p.H + DT - 1) / DT, DT, 0, st>>>(p);
     for (int l = 0; l < p.NL; ++l) {
-        const DenseLayer &L = p.L[l];
-        k_rmsnorm<<<1, 1024, 0, st>>>(p.x, L.attn_norm, p.H, p.eps, p.xb);
         cudaError_t e = launch_gemv(g[4 * l + 0], p.gemv_mode, st);
         if (e != cudaSuccess) return e;
-        k_qk_rope<<<p.NH + p.NKV, p.HD, 0, st>>>(p, l);
         k_attention<<<p.NH, DT, (size_t)p.kv_cap * sizeof(float), st>>>(p, l);
         if ((e = launch_gemv(g[4 * l + 1], p.gemv_mode, st)) != cudaSuccess) return e;
-        k_rmsnorm<<<1, 1024, 0, st>>>(p.x, L.ffn_norm, p.H, p.eps, p.xb);
         if ((e = launch_gemv(g[4 * l + 2], p.gemv_mode, st)) != cudaSuccess) return e;
         k_silu_mul<<<(p.F + DT - 1) / DT, DT, 0, st>>>(p.gate, p.up, p.F);
         if ((e = launch_gemv(g[4 * l + 3], p.gemv_mode, st)) != cudaSuccess) return e;
     }
-    k_rmsnorm<<<1, 1024, 0, st>>>(p.x, p.out_norm, p.H, p.eps, p.xb);
     cudaError_t e = launch_gemv(g[4 * p.NL], p.gemv_mode, st);
     if (e != cudaSuccess) return e;
     k_argmax_part<<<nparts, DT, 0, st>>>(p);

@@ -52,11 +52,16 @@ struct KataliDense {
 namespace {
 
 kq::GemvParams gemv_job(const float *x, uint64_t cols, int n, const void *const *w,
-                        const uint32_t *types, const uint64_t *rows, float *const *y, int accum) {
+                        const uint32_t *types, const uint64_t *rows, float *const *y, int accum,
+                        const float *norm_w = nullptr, float eps = 0.0f,
+                        const float *x_mul = nullptr) {
     kq::GemvParams g = {};
     g.njobs = n;
     g.cols = (uint32_t)cols;
     g.x = x;
+    g.norm_w = norm_w;
+    g.norm_eps = eps;
+    g.x_mul = x_mul;
     g.status = kq::device_status_word();
     for (int j = 0; j < n; ++j) {
         g.job[j].w = (const uint8_t *)w[j];
@@ -220,7 +225,7 @@ int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
             const uint32_t ts[3] = {w.wq_type, w.wk_type, w.wv_type};
             const uint64_t rows[3] = {(uint64_t)NH * HD, (uint64_t)NKV * HD, (uint64_t)NKV * HD};
             float *ys[3] = {p.q, p.k, p.v};
-            m->g[4 * l] = gemv_job(p.xb, H, 3, ws, ts, rows, ys, 0);
+            m->g[4 * l] = gemv_job(p.x, H, 3, ws, ts, rows, ys, 0, w.attn_norm, d->rms_eps);
         }
         {
             const void *ws[1] = {w.wo};
@@ -234,7 +239,7 @@ int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
             const uint32_t ts[2] = {w.gate_type, w.up_type};
             const uint64_t rows[2] = {F, F};
             float *ys[2] = {p.gate, p.up};
-            m->g[4 * l + 2] = gemv_job(p.xb, H, 2, ws, ts, rows, ys, 0);
+            m->g[4 * l + 2] = gemv_job(p.x, H, 2, ws, ts, rows, ys, 0, w.ffn_norm, d->rms_eps);
         }
         {
             const void *ws[1] = {w.down};
@@ -249,7 +254,7 @@ int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
         const uint32_t ts[1] = {d->lm_head_type};
         const uint64_t rows[1] = {d->vocab};
         float *ys[1] = {p.logits};
-        m->g[4 * NL] = gemv_job(p.xb, H, 1, ws, ts, rows, ys, 0);
+        m->g[4 * NL] = gemv_job(p.x, H, 1, ws, ts, rows, ys, 0, d->out_norm, d->rms_eps);
     }
     *out = m;
     return KATALI_OK;

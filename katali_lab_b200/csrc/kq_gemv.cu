@@ -78,11 +78,38 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     ActQ8 a;
     const float *xf = nullptr, *xs = nullptr;
     const int nblk = cols / 32;
+    float inv = 1.0f;
+    if (MODE != 1 && p.norm_w) {  // RMSNorm prologue: every CTA computes the same sum
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < cols; i += GEMV_CW * 32) ss += (double)p.x[i] * (double)p.x[i];
+        ss = warp_sum_d(ss);
+        double *red = reinterpret_cast<double *>(act);
+        if (lane == 0) red[warp] = ss;
+        asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CW * 32));
+        ss = 0.0;
+        for (int w = 0; w < GEMV_CW; ++w) ss += red[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / (double)cols), p.norm_eps)));
+        asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CW * 32));
+    }
+    auto xval = [&](int i, float v) {
+        if (p.x_mul) v = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, kq_expf(-v))), p.x_mul[i]);
+        if (p.norm_w) v = __fmul_rn(__fmul_rn(v, inv), p.norm_w[i]);
+        return v;
+    };
+    const bool pro = p.x_mul || p.norm_w;
     if (MODE == 2) {
         float *sx = reinterpret_cast<float *>(act);  // cols + cols/16 floats
         float *sxs = sx + cols + cols / 16;
-        for (int i = threadIdx.x; i < cols / 4; i += GEMV_CW * 32)
-            reinterpret_cast<float4 *>(sx + fpos(1, 4 * i))[0] = reinterpret_cast<const float4 *>(p.x)[i];
+        for (int i = threadIdx.x; i < cols / 4; i += GEMV_CW * 32) {
+            float4 v = reinterpret_cast<const float4 *>(p.x)[i];
+            if (pro) {
+                v.x = xval(4 * i, v.x);
+                v.y = xval(4 * i + 1, v.y);
+                v.z = xval(4 * i + 2, v.z);
+                v.w = xval(4 * i + 3, v.w);
+            }
+            reinterpret_cast<float4 *>(sx + fpos(1, 4 * i))[0] = v;
+        }
         asm volatile("bar.sync 1, %0;" ::"r"(GEMV_CW * 32));
         for (int gb = warp; gb < nblk; gb += GEMV_CW) {
             const float v = warp_sum_f(sx[fpos(1, 32 * gb + lane)]);
@@ -103,7 +130,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
                 const int gb = g0 + t * GEMV_CW;
                 v[t] = 0.0f;
                 if (gb < nblk) {
-                    if (MODE == 0) v[t] = p.x[32 * gb + lane];
+                    if (MODE == 0) v[t] = pro ? xval(32 * gb + lane, p.x[32 * gb + lane]) : p.x[32 * gb + lane];
                     else v[t] = (float)(int8_t)p.xq[(size_t)Q81_BYTES * gb + 4 + lane];
                 }
             }

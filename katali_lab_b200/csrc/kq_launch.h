@@ -34,6 +34,12 @@ struct GemvParams {
     const float *x;     // fp32 activations (modes 0 and 2)
     const uint8_t *xq;  // q8_1 blocks (mode 1)
     volatile uint32_t *status;
+    // Optional prologue applied to x while it is staged (modes 0 and 2):
+    //   x_mul  : x_i <- silu(x_i) * x_mul_i            (the SwiGLU product)
+    //   norm_w : x_i <- (x_i * inv) * norm_w_i, inv = 1 / sqrt(mean(x^2) + norm_eps)
+    const float *x_mul;
+    const float *norm_w;
+    float norm_eps;
 };
 
 // mode 0: q8_1 activations quantised in-kernel from fp32 x; 1: from q8_1 blocks;
