@@ -19,6 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIBDIR = os.path.join(PKG, "lib")
 PLUGIN = os.path.join(LIBDIR, "libkatali_cuda.so")
 LOADER = os.path.join(LIBDIR, "libkatali_cuda_loader.so")
+CHECK = os.path.join(LIBDIR, "katali_cuda_check")  # command-line checks (cuda-info / cuda-check ...)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -53,10 +54,15 @@ def build(force: bool = False, verbose: bool = False) -> str:
         if verbose:
             sys.stderr.write(r.stderr)
     loader_src = os.path.join(CSRC, "loader", "katali_cuda_loader.c")
+    cc = os.environ.get("CC", "gcc")
     if os.path.exists(loader_src) and (force or _stale(LOADER, [loader_src] + deps)):
-        cc = os.environ.get("CC", "gcc")
         subprocess.run([cc, "-std=c11", "-O2", "-fPIC", "-shared", "-Wall", "-I", INCLUDE,
                         "-o", LOADER, loader_src, "-ldl"], check=True)
+    check_src = os.path.join(CSRC, "loader", "katali_cuda_check.c")
+    if os.path.exists(check_src) and (force or _stale(CHECK, [check_src, LOADER] + deps)):
+        subprocess.run([cc, "-std=c11", "-O2", "-Wall", "-I", INCLUDE, "-o", CHECK, check_src,
+                        "-L", LIBDIR, "-lkatali_cuda_loader", "-Wl,-rpath,$ORIGIN", "-lm"],
+                       check=True)
     return PLUGIN
 
 

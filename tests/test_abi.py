@@ -103,3 +103,19 @@ def test_argument_checks_before_device(built):
     h = C.c_void_p()
     assert p.L.katali_cuda_moe_create(C.byref(bad), C.byref(h)) == 3
     assert p.L.katali_cuda_strerror(6) == b"device-side wait timed out"
+
+
+def test_check_cli_reports_no_device():
+    """The command-line check (cuda-info equivalent) exits 2 with the probe's reason when no
+    usable GPU is present (this CPU-only test runs where CUDA is unavailable)."""
+    import subprocess
+
+    import torch
+    from katali_lab_b200.build import CHECK
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    r = subprocess.run([CHECK, "info"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2
+    assert "katali_cuda:" in r.stdout
+    r = subprocess.run([CHECK, "check"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2
