@@ -297,12 +297,15 @@ __device__ __forceinline__ double dec_q8_unit(const uint8_t *drow, int F, int u,
            ((double)d * (double)a.d[2 * u + 1]) * (double)I1;
 }
 
-template <int MODE, uint32_t DT>
+// SHAPE 1: the layer shape is compile-time (hidden 2048, FFN 512, top-8, Q4_K gate/up, Q6_K
+// down: C2 and its family), so shape-dependent branches and loop bounds fold away; SHAPE 0
+// reads every size from the parameters.
+template <int MODE, uint32_t DT, int SHAPE>
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_constant__ MoeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
-    const int H = p.H, F = p.F, K = p.K;
+    const int H = SHAPE ? 2048 : p.H, F = SHAPE ? 512 : p.F, K = SHAPE ? 8 : p.K;
     trace(p, 0);
 
     uint8_t *sa = smem;
@@ -324,7 +327,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     const uint32_t Q = (uint32_t)H / p.rg;  // phase-B row groups (16-byte aligned copies)
     const uint32_t q0 = Q * c / G, q1 = Q * (c + 1) / G;
     const uint32_t rB0 = p.rg * q0, nrB = p.rg * (q1 - q0);
-    const uint32_t rbg = p.rbg, rbu = p.rbu, rbd = p.rbd;
+    const uint32_t rbg = SHAPE ? 1152u : p.rbg, rbu = SHAPE ? 1152u : p.rbu,
+                   rbd = SHAPE ? 420u : p.rbd;
     const uint32_t blk_bytes = HB * (rbg + rbu);
 
     if (p.route_only) {  // check entry point: the routing decision only
@@ -710,11 +714,11 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     return p.smem_bytes <= (uint32_t)max_smem ? 0 : -1;
 }
 
-template <int MODE, uint32_t DT>
+template <int MODE, uint32_t DT, int SHAPE>
 static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     static uint32_t set_bytes = 0;  // raise the smem limit once per size, before any capture
     if (p.smem_bytes > set_bytes) {
-        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT>,
+        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)p.smem_bytes);
         if (e != cudaSuccess) return e;
@@ -730,13 +734,19 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     attr[0].val.cooperative = p.route_only ? 0 : 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT>, p);
+    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE>, p);
 }
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
-    if (p.mode == 0)
-        return p.down_type == T_Q6_K ? launch_t<0, T_Q6_K>(p, grid, st) : launch_t<0, T_Q4_K>(p, grid, st);
-    return p.down_type == T_Q6_K ? launch_t<1, T_Q6_K>(p, grid, st) : launch_t<1, T_Q4_K>(p, grid, st);
+    const bool c2 = p.H == 2048 && p.F == 512 && p.K == 8 && p.gate_type == T_Q4_K &&
+                    p.up_type == T_Q4_K && p.down_type == T_Q6_K;
+    if (p.mode == 0) {
+        if (c2) return launch_t<0, T_Q6_K, 1>(p, grid, st);
+        return p.down_type == T_Q6_K ? launch_t<0, T_Q6_K, 0>(p, grid, st)
+                                     : launch_t<0, T_Q4_K, 0>(p, grid, st);
+    }
+    return p.down_type == T_Q6_K ? launch_t<1, T_Q6_K, 0>(p, grid, st)
+                                 : launch_t<1, T_Q4_K, 0>(p, grid, st);
 }
 
 }  // namespace kq
