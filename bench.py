@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--p2p", action="store_true",
+                    help="N > 1: exchange over NVLink peer memory inside the kernels instead of NCCL")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent replicas instead of expert parallelism")
     ap.add_argument("--warm", action="store_true",
@@ -677,8 +679,7 @@ def c3_cpu_rate(stores_or_layers, Ts, offs, Xh, LGh, distinct, seconds):
 
 
 EP_WORKLOAD = ("{cfg} expert-parallel over {n} GPUs: 256 experts split in blocks of {per} per GPU, "
-               "every GPU brings its own tokens ({tok}); dispatch/combine by the plugin's NCCL "
-               "communicator (grouped send/recv of fixed-capacity q8_1 slots)")
+               "every GPU brings its own tokens ({tok}); dispatch/combine {how}")
 
 
 def run_ep(args, rank, world, local_rank):
@@ -706,6 +707,8 @@ def run_ep(args, rank, world, local_rank):
     stores = [make_expert_store(plugin, per, H, F, seed=10_000 * l + rank) for l in range(L)]
     layers = [EpMoeLayer(plugin, E, H, F, K, st.pointers(), world, rank, tmax) for st in stores]
     comm = EpComm.from_process_group(plugin)
+    if args.p2p:
+        comm.use_peer_memory(True)
     # every rank's inputs from its seed, so every rank can count the job's distinct experts
     plans = [c3_plan(n, seed=3 + r, tmin=1 if ragged else 1, tmax=tmax) for r in range(world)]
     Ts, offs, Xh, LGh, _ = plans[rank]
@@ -788,7 +791,10 @@ def run_ep(args, rank, world, local_rank):
             "config": {"workload": EP_WORKLOAD.format(cfg="C3 ragged batch" if ragged else
                                                       "C2 batch-1 decode", n=world, per=per,
                                                       tok="T ~ U{1..64} per call" if ragged
-                                                      else "one per call"),
+                                                      else "one per call",
+                                                      how="over NVLink peer memory inside the kernels"
+                                                      if args.p2p else "by the plugin's NCCL communicator "
+                                                      "(grouped send/recv of fixed-capacity q8_1 slots)"),
                        "calls_per_step": n, "tokens_per_step_job": tok_all,
                        "distinct_experts_per_step": int(sum(distinct)),
                        "us_per_call": round(us_call, 3), "parallelism": f"ep{world}",

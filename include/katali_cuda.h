@@ -216,6 +216,14 @@ int katali_cuda_ep_destroy(KataliEp *ep);
 int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens,
                              uint32_t n_tokens, const float *x, const float *router_logits,
                              float *y);
+/* on != 0: later katali_cuda_moe_ep_layer calls exchange over NVLink peer memory
+ * instead of NCCL: the dispatch kernel stores each slot straight into the owner
+ * rank's receive window and the experts kernel stores each partial sum straight
+ * into the source rank's window, each signalled by a flag the reader polls with
+ * a bounded wait (a wait that runs out returns KATALI_ERR_TIMEOUT). The windows
+ * are allocated and mapped between the ranks (CUDA IPC) by the first such call,
+ * collectively, for that call's layer shape and max_tokens. */
+int katali_cuda_ep_use_peer_memory(KataliEp *ep, int on);
 
 /* ------------------------------------------------------------------------ */
 /* 7. Expert residency tier (the reference's expert cache, README.md:13,21,   */

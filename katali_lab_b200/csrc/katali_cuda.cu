@@ -605,12 +605,27 @@ int katali_cuda_moe_ep_slot_bytes(KataliMoe *m, uint64_t *slot_bytes, uint64_t *
     return KATALI_OK;
 }
 
-int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
-                                uint32_t n_tokens, const float *x, const float *router_logits,
-                                void *send) {
+}  // extern "C"
+
+static void ep_peer_fill(kq::MoeBatchParams &b, const kq::EpPeer *pp) {
+    if (!pp) return;
+    b.ep_p2p = 1;
+    b.ep_rank = pp->rank;
+    b.ep_peer_recv = pp->recv;
+    b.ep_peer_back = pp->back;
+    b.ep_peer_flags = pp->flags;
+    b.ep_epoch = pp->epoch;
+    b.ep_done = pp->done;
+}
+
+namespace kq {
+// The three stages; pp != nullptr selects the exchange over peer memory (the
+// buffers are the communicator's windows then, and send / recv / ret / back unused).
+int moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                    const float *x, const float *router_logits, void *send, const EpPeer *pp) {
     int s = ep_check(m, n_ranks, max_tokens);
     if (s) return s;
-    if (n_tokens > max_tokens || !send || !aligned16(send)) return KATALI_ERR_BAD_ARG;
+    if (n_tokens > max_tokens || (!pp && (!send || !aligned16(send)))) return KATALI_ERR_BAD_ARG;
     if (n_tokens && (!x || !router_logits || !aligned16(x))) return KATALI_ERR_BAD_ARG;
     const uint32_t K = (uint32_t)m->plan[0].K;
     if (max_tokens > m->ep_src_cap) {
@@ -627,6 +642,7 @@ int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tok
     }
     kq::MoeBatchParams b = batch_params(m, 0);
     ep_fill(b, m, n_ranks, max_tokens);
+    ep_peer_fill(b, pp);
     b.ep_tokens = (int)n_tokens;
     b.X = x;
     b.logits = router_logits;
@@ -634,36 +650,57 @@ int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tok
     return finish(kq::launch_moe_ep_dispatch(b, g_stream));
 }
 
-int katali_cuda_moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank,
-                               uint32_t max_tokens, const void *recv, void *ret) {
+int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_tokens,
+                   const void *recv, void *ret, const EpPeer *pp) {
     int s = ep_check(m, n_ranks, max_tokens);
     if (s) return s;
-    if (rank >= n_ranks || !recv || !ret || !aligned16(recv) || !aligned16(ret))
+    if (rank >= n_ranks || (!pp && (!recv || !ret || !aligned16(recv) || !aligned16(ret))))
         return KATALI_ERR_BAD_ARG;
     const int T = (int)(n_ranks * max_tokens);
     s = grow_batch_scratch(m, T);
     if (s) return s;
     kq::MoeBatchParams b = batch_params(m, T);
     ep_fill(b, m, n_ranks, max_tokens);
+    ep_peer_fill(b, pp);
     b.ep_recv = (const uint8_t *)recv;
     b.ep_ret = (double *)ret;
     return finish(kq::launch_moe_ep_experts(b, g_stream));
 }
 
-int katali_cuda_moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
-                               uint32_t n_tokens, const void *back, float *y) {
+int moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                   const void *back, float *y, const EpPeer *pp) {
     int s = ep_check(m, n_ranks, max_tokens);
     if (s) return s;
-    if (n_tokens > max_tokens || n_tokens > m->ep_src_cap || !back || !aligned16(back))
+    if (n_tokens > max_tokens || n_tokens > m->ep_src_cap || (!pp && (!back || !aligned16(back))))
         return KATALI_ERR_BAD_ARG;
-    if (n_tokens == 0) return KATALI_OK;
-    if (!y) return KATALI_ERR_BAD_ARG;
+    if (n_tokens == 0 && !pp) return KATALI_OK;  // over peer memory the call must still close
+    if (n_tokens && !y) return KATALI_ERR_BAD_ARG;
     kq::MoeBatchParams b = batch_params(m, 0);
     ep_fill(b, m, n_ranks, max_tokens);
+    ep_peer_fill(b, pp);
     b.ep_tokens = (int)n_tokens;
     b.ep_back = (const double *)back;
     b.Y = y;
     return finish(kq::launch_moe_ep_combine(b, g_stream));
+}
+}  // namespace kq
+
+extern "C" {
+
+int katali_cuda_moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                                uint32_t n_tokens, const float *x, const float *router_logits,
+                                void *send) {
+    return kq::moe_ep_dispatch(m, n_ranks, max_tokens, n_tokens, x, router_logits, send, nullptr);
+}
+
+int katali_cuda_moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank,
+                               uint32_t max_tokens, const void *recv, void *ret) {
+    return kq::moe_ep_experts(m, n_ranks, rank, max_tokens, recv, ret, nullptr);
+}
+
+int katali_cuda_moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens,
+                               uint32_t n_tokens, const void *back, float *y) {
+    return kq::moe_ep_combine(m, n_ranks, max_tokens, n_tokens, back, y, nullptr);
 }
 
 int katali_cuda_debug_moe_trace(KataliMoe *m, uint64_t *trace, int *grid) {

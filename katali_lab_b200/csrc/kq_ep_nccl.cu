@@ -16,11 +16,20 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <vector>
+
 #include "katali_cuda.h"
+#include "kq_launch.h"
 
 namespace kq {
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
+int moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                    const float *x, const float *router_logits, void *send, const EpPeer *pp);
+int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_tokens,
+                   const void *recv, void *ret, const EpPeer *pp);
+int moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                   const void *back, float *y, const EpPeer *pp);
 }  // namespace kq
 
 namespace {
@@ -36,6 +45,7 @@ struct Nccl {
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char *(*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -63,6 +73,7 @@ int load_nccl() {
               sym(g_nccl.CommGetAsyncError, "ncclCommGetAsyncError") &&
               sym(g_nccl.GroupStart, "ncclGroupStart") && sym(g_nccl.GroupEnd, "ncclGroupEnd") &&
               sym(g_nccl.Send, "ncclSend") && sym(g_nccl.Recv, "ncclRecv") &&
+              sym(g_nccl.AllGather, "ncclAllGather") &&
               sym(g_nccl.GetErrorString, "ncclGetErrorString");
     if (!ok) {
         kq::set_status_message("libnccl.so.2 lacks a required symbol");
@@ -70,6 +81,13 @@ int load_nccl() {
         return KATALI_ERR_NCCL;
     }
     return KATALI_OK;
+}
+
+int cuda_err(cudaError_t e, const char *what) {
+    char msg[200];
+    snprintf(msg, sizeof msg, "%s: %s", what, cudaGetErrorString(e));
+    kq::set_status_message(msg);
+    return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
 }
 
 int nccl_fail(ncclResult_t r) {
@@ -87,6 +105,14 @@ struct KataliEp {
     // exchange buffers, grown on demand
     unsigned char *send, *recv, *ret, *back;
     size_t slot_cap, ret_cap;  // bytes per buffer
+    // exchange over peer memory (katali_cuda_ep_use_peer_memory)
+    int peer_mode;
+    unsigned char *win;        // this rank's window: recv, back, flags
+    uint64_t win_slot;
+    uint32_t win_h, win_tmax;
+    std::vector<void *> opened;  // other ranks' windows mapped here
+    void *dev_arrays;          // recv[G], back[G], flags[G] pointers, then epoch + 3 counters
+    kq::EpPeer peer;
 };
 
 namespace {
@@ -123,9 +149,83 @@ int exchange(KataliEp *ep, const unsigned char *out, unsigned char *in, size_t c
     return KATALI_OK;
 }
 
+// Collective: every rank allocates its window, the IPC handles are all-gathered over
+// the communicator and every other rank's window is mapped into this process.
+int peer_setup(KataliEp *ep, uint64_t slot, uint32_t H, uint32_t tmax, cudaStream_t st) {
+    if (ep->win) {
+        if (ep->win_slot == slot && ep->win_h == H && ep->win_tmax == tmax) return KATALI_OK;
+        kq::set_status_message("peer-memory exchange: layer shape or max_tokens differs from the window");
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    }
+    const size_t G = (size_t)ep->n_ranks;
+    auto r256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t recv = r256(2 * G * tmax * slot), back = r256(2 * G * tmax * (size_t)H * 8),
+                 flags = r256(4 * G * sizeof(uint32_t));
+    cudaError_t e = cudaMalloc((void **)&ep->win, recv + back + flags);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ep->win, 0, recv + back + flags, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_err(e, "peer window");
+    cudaIpcMemHandle_t mine;
+    e = cudaIpcGetMemHandle(&mine, ep->win);
+    if (e != cudaSuccess) return cuda_err(e, "cudaIpcGetMemHandle");
+    unsigned char *hbuf = nullptr;  // [own handle][G handles]
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    e = cudaMalloc((void **)&hbuf, hb * (G + 1));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(hbuf, &mine, hb, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_err(e, "peer handles");
+    ncclResult_t r = g_nccl.AllGather(hbuf, hbuf + hb, hb, ncclUint8, ep->comm, st);
+    if (r != ncclSuccess) {
+        cudaFree(hbuf);
+        return nccl_fail(r);
+    }
+    std::vector<cudaIpcMemHandle_t> all(G);
+    e = cudaMemcpyAsync(all.data(), hbuf + hb, hb * G, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(hbuf);
+    if (e != cudaSuccess) return cuda_err(e, "peer handles");
+    std::vector<unsigned char *> base(G);
+    for (size_t d = 0; d < G; ++d) {
+        if ((int)d == ep->rank) {
+            base[d] = ep->win;
+            continue;
+        }
+        void *p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, all[d], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return cuda_err(e, "cudaIpcOpenMemHandle");
+        ep->opened.push_back(p);
+        base[d] = (unsigned char *)p;
+    }
+    std::vector<void *> arrays(3 * G);
+    for (size_t d = 0; d < G; ++d) {
+        arrays[d] = base[d];
+        arrays[G + d] = base[d] + recv;
+        arrays[2 * G + d] = base[d] + recv + back;
+    }
+    e = cudaMalloc(&ep->dev_arrays, 3 * G * sizeof(void *) + 64);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(ep->dev_arrays, arrays.data(), 3 * G * sizeof(void *), cudaMemcpyHostToDevice, st);
+    uint32_t *words = (uint32_t *)((unsigned char *)ep->dev_arrays + 3 * G * sizeof(void *));
+    if (e == cudaSuccess) e = cudaMemsetAsync(words, 0, 64, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_err(e, "peer arrays");
+    void **arr = (void **)ep->dev_arrays;
+    ep->peer = kq::EpPeer{ep->rank, (uint8_t *const *)arr, (double *const *)(arr + G),
+                          (uint32_t *const *)(arr + 2 * G), words, words + 1};
+    ep->win_slot = slot;
+    ep->win_h = H;
+    ep->win_tmax = tmax;
+    return KATALI_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int katali_cuda_ep_use_peer_memory(KataliEp *ep, int on) {
+    if (!ep) return KATALI_ERR_BAD_ARG;
+    ep->peer_mode = on ? 1 : 0;
+    return KATALI_OK;
+}
 
 int katali_cuda_ep_unique_id(void *id) {
     if (!id) return KATALI_ERR_BAD_ARG;
@@ -160,9 +260,24 @@ int katali_cuda_ep_create(uint32_t n_ranks, uint32_t rank, const void *id, Katal
 
 int katali_cuda_ep_destroy(KataliEp *ep) {
     if (!ep) return KATALI_OK;
-    cudaStreamSynchronize(kq::current_stream());
+    cudaStream_t st = kq::current_stream();
+    cudaStreamSynchronize(st);
     ncclResult_t async = ncclSuccess;
     g_nccl.CommGetAsyncError(ep->comm, &async);
+    if (ep->win) {
+        // no rank may still write into a window that is released: meet first
+        if (async == ncclSuccess) {
+            void *tmp = nullptr;
+            if (cudaMalloc(&tmp, 4 * ep->n_ranks) == cudaSuccess) {
+                g_nccl.AllGather(tmp, tmp, 4, ncclUint8, ep->comm, st);  // in place: slot `rank`
+                cudaStreamSynchronize(st);
+                cudaFree(tmp);
+            }
+        }
+        for (void *p : ep->opened) cudaIpcCloseMemHandle(p);
+        cudaFree(ep->dev_arrays);
+        cudaFree(ep->win);
+    }
     // A communicator with an error pending cannot be destroyed cleanly: abort it.
     if (async != ncclSuccess) g_nccl.CommAbort(ep->comm);
     else g_nccl.CommDestroy(ep->comm);
@@ -182,6 +297,16 @@ int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens, ui
     if (s) return s;
     if (max_tokens == 0 || (uint64_t)max_tokens * ep->n_ranks > KATALI_MOE_BATCH_MAX_TOKENS)
         return KATALI_ERR_BAD_ARG;
+    cudaStream_t st = kq::current_stream();
+    const uint32_t G = (uint32_t)ep->n_ranks;
+    if (ep->peer_mode) {  // both exchanges inside the kernels, over NVLink peer memory
+        if ((s = peer_setup(ep, slot, (uint32_t)(rslot / 8), max_tokens, st))) return s;
+        if ((s = kq::moe_ep_dispatch(m, G, max_tokens, n_tokens, x, router_logits, nullptr, &ep->peer)))
+            return s;
+        if ((s = kq::moe_ep_experts(m, G, (uint32_t)ep->rank, max_tokens, nullptr, nullptr, &ep->peer)))
+            return s;
+        return kq::moe_ep_combine(m, G, max_tokens, n_tokens, nullptr, y, &ep->peer);
+    }
     const size_t chunk = slot * max_tokens, rchunk = rslot * max_tokens;
     size_t c0 = ep->slot_cap, c1 = ep->slot_cap;
     if ((s = grow(ep->send, c0, chunk * ep->n_ranks)) || (s = grow(ep->recv, c1, chunk * ep->n_ranks)))
@@ -191,8 +316,6 @@ int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens, ui
     if ((s = grow(ep->ret, r0, rchunk * ep->n_ranks)) || (s = grow(ep->back, r1, rchunk * ep->n_ranks)))
         return s;
     ep->ret_cap = r0 < r1 ? r0 : r1;
-    cudaStream_t st = kq::current_stream();
-    const uint32_t G = (uint32_t)ep->n_ranks;
     if ((s = katali_cuda_moe_ep_dispatch(m, G, max_tokens, n_tokens, x, router_logits, ep->send)))
         return s;
     if ((s = exchange(ep, ep->send, ep->recv, chunk, st))) return s;

@@ -114,6 +114,25 @@ struct MoeBatchParams {
     volatile uint32_t *status;  // device-side timeout bits (mapped host word)
     int gu_rows, dn_rows;       // row-tile heights, set by the launcher
     int sms;                    // SM count (persistent grids)
+    // expert parallelism over peer memory (ep_p2p = 1): every rank's window holds
+    // recv [2][G][Tmax][slot], back [2][G][Tmax][H] doubles and flags [2][2][G]
+    // (recv flags, then back flags, per parity); entry d of each array is rank d's
+    // window as mapped in this process (this rank's own entry is local memory).
+    int ep_p2p, ep_rank;
+    uint8_t *const *ep_peer_recv;
+    double *const *ep_peer_back;
+    uint32_t *const *ep_peer_flags;
+    uint32_t *ep_epoch;  // calls completed by this rank (the next call is *ep_epoch + 1)
+    uint32_t *ep_done;   // last-CTA counters of the three peer kernels
+};
+// The peer-memory exchange of an expert-parallel communicator (device arrays of
+// n_ranks window pointers; see MoeBatchParams).
+struct EpPeer {
+    int rank;
+    uint8_t *const *recv;
+    double *const *back;
+    uint32_t *const *flags;
+    uint32_t *epoch, *done;
 };
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);

@@ -428,6 +428,45 @@ __device__ __forceinline__ uint8_t *ep_slot(const MoeBatchParams &p, uint8_t *bu
     return buf + ((size_t)d * p.ep_tmax + t) * p.ep_slot_bytes;
 }
 
+// --- peer-memory exchange -----------------------------------------------------
+// Call e (= *ep_epoch + 1, the same on every rank) uses parity e & 1 of every
+// window. A slot written for call e is reused at call e + 2 only: the writer gets
+// there after its combine of call e + 1, which waited for the reader's return of
+// e + 1, which the reader sent after consuming call e.
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait until *flag == e; false (status bit 2) when the limit runs out.
+__device__ __forceinline__ bool wait_flag(const MoeBatchParams &p, const uint32_t *flag, uint32_t e) {
+    for (uint32_t it = 0; it < SPIN_LIMIT; ++it) {
+        if (ld_acquire_sys(flag) == e) return true;
+        if (it > 16) __nanosleep(128);
+    }
+    if (p.status) atomicOr((uint32_t *)p.status, 2u);
+    return false;
+}
+__device__ __forceinline__ uint32_t *flag_at(uint32_t *flags, int kind, uint32_t par, int G, int d) {
+    return flags + ((size_t)kind * 2 + par) * G + d;  // kind 0: recv, 1: back
+}
+// After every CTA's stores to peer memory: the last CTA to finish raises this
+// rank's flag of `kind` in every peer's window.
+__device__ __forceinline__ void signal_peers(const MoeBatchParams &p, int counter, int kind, uint32_t e) {
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const uint32_t prev = atomicAdd(&p.ep_done[counter], 1u);
+    if (prev != gridDim.x * gridDim.y * gridDim.z - 1) return;
+    p.ep_done[counter] = 0u;
+    __threadfence_system();
+    for (int d = 0; d < p.ep_ranks; ++d)
+        st_release_sys(flag_at(p.ep_peer_flags[d], kind, e & 1u, p.ep_ranks, p.ep_rank), e);
+}
+
 // CTA per source token slot t < Tmax: route, quantise x to a GGUF q8_1 row in
 // shared memory, write one slot per destination rank (empty headers for t >= T).
 __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
@@ -436,9 +475,15 @@ __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
     __shared__ float s_w[MOE_MAX_K];
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K, G = p.ep_ranks, per = p.n_experts / G;
+    const uint32_t e = p.ep_p2p ? *p.ep_epoch + 1 : 0u;
+    // slot (d, t): the send buffer, or rank d's receive window (this rank's row) over peer memory
+    auto dst = [&](int d) {
+        if (!p.ep_p2p) return ep_slot(p, p.ep_send, d, t);
+        return p.ep_peer_recv[d] + (((size_t)(e & 1u) * G + p.ep_rank) * p.ep_tmax + t) * p.ep_slot_bytes;
+    };
     if (t >= p.ep_tokens) {
-        for (int d = threadIdx.x; d < G; d += BT)
-            *reinterpret_cast<int4 *>(ep_slot(p, p.ep_send, d, t)) = make_int4(0, t, 0, 0);
+        for (int d = threadIdx.x; d < G; d += BT) *reinterpret_cast<int4 *>(dst(d)) = make_int4(0, t, 0, 0);
+        if (p.ep_p2p) signal_peers(p, 0, 0, e);
         return;
     }
     __shared__ float s_lg[1024];
@@ -461,7 +506,7 @@ __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
     __syncthreads();
     const int row_bytes = H / 32 * 36;
     for (int d = 0; d < G; ++d) {
-        uint8_t *slot = ep_slot(p, p.ep_send, d, t);
+        uint8_t *slot = dst(d);
         int n = 0;
         for (int k = 0; k < K; ++k) n += s_ids[k] / per == d;
         if (threadIdx.x < K) {
@@ -475,6 +520,7 @@ __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
         for (int i = threadIdx.x; i < row_bytes / 16; i += BT)
             reinterpret_cast<int4 *>(row)[i] = reinterpret_cast<const int4 *>(ep_row)[i];
     }
+    if (p.ep_p2p) signal_peers(p, 0, 0, e);
 }
 
 // CTA per received slot: header -> pair ids/weights (ids -1 for empty slots);
@@ -483,21 +529,35 @@ __global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
     const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K, nblk = H / 32;
     const uint8_t *slot = p.ep_recv + (size_t)s * p.ep_slot_bytes;
-    const int n = *reinterpret_cast<const int *>(slot);
+    if (p.ep_p2p) {  // this rank's window, current parity; wait for the source's flag
+        const uint32_t e = *p.ep_epoch + 1;
+        const int G = p.ep_ranks, src = s / p.ep_tmax;
+        slot = p.ep_peer_recv[p.ep_rank] + ((size_t)(e & 1u) * G * p.ep_tmax + s) * p.ep_slot_bytes;
+        __shared__ int ok;
+        if (threadIdx.x == 0)
+            ok = wait_flag(p, flag_at(p.ep_peer_flags[p.ep_rank], 0, e & 1u, G, src), e);
+        __syncthreads();
+        if (!ok) {  // treated as an empty slot; the call reports the timeout
+            if (threadIdx.x < K) p.ids[s * K + threadIdx.x] = -1;
+            return;
+        }
+    }
+    // slots written by other GPUs (or by NCCL): L2 loads, no stale L1 lines
+    const int n = __ldcg(reinterpret_cast<const int *>(slot));
     if (threadIdx.x < K) {
-        p.ids[s * K + threadIdx.x] = n > 0 ? reinterpret_cast<const int *>(slot + 16)[threadIdx.x] : -1;
-        p.w[s * K + threadIdx.x] = reinterpret_cast<const float *>(slot + 16 + 4 * K)[threadIdx.x];
+        p.ids[s * K + threadIdx.x] = n > 0 ? __ldcg(reinterpret_cast<const int *>(slot + 16) + threadIdx.x) : -1;
+        p.w[s * K + threadIdx.x] = __ldcg(reinterpret_cast<const float *>(slot + 16 + 4 * K) + threadIdx.x);
     }
     if (n == 0) return;
     const uint8_t *row = slot + p.ep_hdr_bytes;
     for (int g = warp; g < nblk; g += BT / 32) {
         const uint8_t *blk = row + 36 * g;
-        const int qi = (int)(int8_t)blk[4 + lane];
+        const int qi = (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
         const int sum = __reduce_add_sync(KQ_FULL, qi);
         const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
         p.xq[(size_t)s * H + 32 * g + lane] = (int8_t)qi;
         if (lane == 0) {
-            p.xd[(size_t)s * nblk + g] = h2f(*reinterpret_cast<const uint16_t *>(blk));
+            p.xd[(size_t)s * nblk + g] = h2f(__ldcg(reinterpret_cast<const unsigned short *>(blk)));
             p.xs32[(size_t)s * nblk + g] = sum;
             p.xs16[((size_t)s * nblk + g) * 2] = sum_lo;
             p.xs16[((size_t)s * nblk + g) * 2 + 1] = sum - sum_lo;
@@ -509,29 +569,60 @@ __global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
 __global__ void __launch_bounds__(BT) moe_ep_combine_slots(MoeBatchParams p) {
     const int s = blockIdx.y, K = p.K;
     const int r = blockIdx.x * BT + threadIdx.x;
-    if (r >= p.H) return;
-    int any = 0;
-    double acc = 0.0;
-    for (int k = 0; k < K; ++k) {
-        if (p.ids[s * K + k] < 0) continue;
-        any = 1;
-        acc += (double)p.w[s * K + k] * (double)p.part[(size_t)p.pos_of[s * K + k] * p.H + r];
+    if (r < p.H) {
+        int any = 0;
+        double acc = 0.0;
+        for (int k = 0; k < K; ++k) {
+            if (p.ids[s * K + k] < 0) continue;
+            any = 1;
+            acc += (double)p.w[s * K + k] * (double)p.part[(size_t)p.pos_of[s * K + k] * p.H + r];
+        }
+        if (any) {
+            if (!p.ep_p2p) {
+                p.ep_ret[(size_t)s * p.H + r] = acc;
+            } else {  // straight into the source rank's back window, this rank's row
+                const uint32_t e = *p.ep_epoch + 1;
+                const int G = p.ep_ranks, src = s / p.ep_tmax, t = s % p.ep_tmax;
+                p.ep_peer_back[src][(((size_t)(e & 1u) * G + p.ep_rank) * p.ep_tmax + t) * p.H + r] = acc;
+            }
+        }
     }
-    if (any) p.ep_ret[(size_t)s * p.H + r] = acc;
+    if (p.ep_p2p) signal_peers(p, 1, 1, *p.ep_epoch + 1);
 }
 
 // y[t][r] = sum over ranks d that own one of t's experts (rank order) of back[d][t][r].
 __global__ void __launch_bounds__(BT) moe_ep_combine_tokens(MoeBatchParams p) {
     const int i = blockIdx.x * BT + threadIdx.x;
-    if (i >= p.ep_tokens * p.H) return;
-    const int t = i / p.H, r = i % p.H, K = p.K, per = p.n_experts / p.ep_ranks;
-    double acc = 0.0;
-    for (int d = 0; d < p.ep_ranks; ++d) {
-        bool own = false;
-        for (int k = 0; k < K; ++k) own |= p.ep_src_ids[t * K + k] / per == d;
-        if (own) acc += p.ep_back[((size_t)d * p.ep_tmax + t) * p.H + r];
+    const double *back = p.ep_back;
+    uint32_t e = 0;
+    if (p.ep_p2p) {  // every rank's return for this call has landed in this rank's window
+        e = *p.ep_epoch + 1;
+        const int G = p.ep_ranks;
+        back = p.ep_peer_back[p.ep_rank] + (size_t)(e & 1u) * G * p.ep_tmax * p.H;
+        if (threadIdx.x < G) wait_flag(p, flag_at(p.ep_peer_flags[p.ep_rank], 1, e & 1u, G, threadIdx.x), e);
+        __syncthreads();
     }
-    p.Y[i] = (float)acc;
+    if (i < p.ep_tokens * p.H) {
+        const int t = i / p.H, r = i % p.H, K = p.K, per = p.n_experts / p.ep_ranks;
+        double acc = 0.0;
+        for (int d = 0; d < p.ep_ranks; ++d) {
+            bool own = false;
+            for (int k = 0; k < K; ++k) own |= p.ep_src_ids[t * K + k] / per == d;
+            if (own) acc += __ldcg(back + ((size_t)d * p.ep_tmax + t) * p.H + r);
+        }
+        p.Y[i] = (float)acc;
+    }
+    if (p.ep_p2p) {  // the last CTA out advances the epoch: the next call uses the other parity
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t prev = atomicAdd(&p.ep_done[2], 1u);
+            if (prev == gridDim.x - 1) {
+                p.ep_done[2] = 0u;
+                __threadfence();
+                *p.ep_epoch = e;
+            }
+        }
+    }
 }
 
 // Largest power-of-two row count in [8, 64] whose tile fits `budget` bytes.
@@ -604,7 +695,10 @@ cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st) {
 }
 
 cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st) {
-    moe_ep_combine_tokens<<<(p.ep_tokens * p.H + BT - 1) / BT, BT, 0, st>>>(p);
+    // over peer memory it always runs (also with no tokens): it closes the call's epoch
+    const int grid = (p.ep_tokens * p.H + BT - 1) / BT;
+    if (grid == 0 && !p.ep_p2p) return cudaSuccess;
+    moe_ep_combine_tokens<<<grid > 0 ? grid : 1, BT, 0, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -102,6 +102,7 @@
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
     X(int, katali_cuda_ep_destroy, (KataliEp * e), (e))                                       \
+    X(int, katali_cuda_ep_use_peer_memory, (KataliEp * e, int on), (e, on))                   \
     X(int, katali_cuda_moe_ep_layer,                                                          \
       (KataliMoe * m, KataliEp * e, uint32_t tm, uint32_t n, const float *x, const float *l,  \
        float *y),                                                                             \
@@ -253,6 +254,7 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
     X(int, katali_cuda_ep_destroy, (KataliEp * e), (e))                                       \
+    X(int, katali_cuda_ep_use_peer_memory, (KataliEp * e, int on), (e, on))                   \
     X(int, katali_cuda_moe_ep_layer,                                                          \
       (KataliMoe * m, KataliEp * e, uint32_t tm, uint32_t n, const float *x, const float *l,  \
        float *y),                                                                             \

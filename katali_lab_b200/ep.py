@@ -93,6 +93,11 @@ class EpComm:
         dist.broadcast_object_list(obj, src=0, group=group)
         return cls(plugin, n, rank, obj[0])
 
+    def use_peer_memory(self, on: bool = True) -> None:
+        """Exchange over NVLink peer memory inside the kernels instead of NCCL (the windows
+        are mapped by the next layer call, collectively)."""
+        self.p.check(self.p.L.katali_cuda_ep_use_peer_memory(self.h, int(on)))
+
     def close(self) -> None:
         if self.h:
             self.p.L.katali_cuda_ep_destroy(self.h)

@@ -127,6 +127,7 @@ class Plugin:
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
+            "katali_cuda_ep_use_peer_memory": ([_vp, _i32], _i32),
             "katali_cuda_moe_ep_layer": ([_vp, _vp, _u32, _u32, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_row_isums": ([_u32, _vp, _u64, _u64, _vp, _vp, _vp], _i32),
             "katali_cuda_debug_route": ([_vp, _vp, _vp, _vp], _i32),

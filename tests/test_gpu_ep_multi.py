@@ -1,8 +1,9 @@
 """Expert parallelism across GPUs: two processes, one GPU each, NCCL.
 
-Each rank holds half of the experts and brings its own tokens; the layer runs once
-with torch.distributed's all_to_all_single as the exchange and once with the
-plugin's own NCCL communicator (katali_cuda_moe_ep_layer). Bar: every token's output
+Each rank holds half of the experts and brings its own tokens; the layer runs with
+torch.distributed's all_to_all_single as the exchange, with the plugin's own NCCL
+communicator (katali_cuda_moe_ep_layer), and twice with the exchange over NVLink peer
+memory inside the kernels (katali_cuda_ep_use_peer_memory; both window parities). Bar: every token's output
 within rel_L2 <= 1e-5 of katali_cuda_moe_batch on the full layer on the same GPU and
 >= 99.9 % of elements bit-equal. Skipped with fewer than two GPUs."""
 import datetime
@@ -52,12 +53,17 @@ def _rank(rank, world, port_no, out_dir):
         comm = EpComm.from_process_group(plugin)
         y2 = empty(T * H).view(T, H)
         ep.forward(x, lg, y2, comm=comm)
+        comm.use_peer_memory(True)  # the same layer over NVLink peer memory, both parities
+        y3 = empty(T * H).view(T, H)
+        ep.forward(x, lg, y3, comm=comm)
+        y4 = empty(T * H).view(T, H)
+        ep.forward(x, lg, y4, comm=comm)
         want = empty(T * H).view(T, H)
         full.layer.forward_batch(x, lg, want)
         torch.cuda.synchronize()
         store_sum = [int(b.sum(dtype=torch.int64)) for b in full.bufs]
-        np.savez(os.path.join(out_dir, f"r{rank}.npz"), y1=host(y1), y2=host(y2), want=host(want),
-                 store_sum=np.array(store_sum))
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), y1=host(y1), y2=host(y2), y3=host(y3),
+                 y4=host(y4), want=host(want), store_sum=np.array(store_sum))
         ep.close()
     finally:
         if comm is not None:
@@ -77,7 +83,7 @@ def test_ep_two_gpus(tmp_path):
     assert np.array_equal(sums[0], sums[1]), "the two ranks built different expert stores"
     for r in range(2):
         d = np.load(tmp_path / f"r{r}.npz")
-        for key in ("y1", "y2"):
+        for key in ("y1", "y2", "y3", "y4"):
             for t in range(d["want"].shape[0]):
                 assert rel_l2(d[key][t], d["want"][t]) <= 1e-5, (r, key, t)
                 assert np.mean(d[key][t] == d["want"][t]) >= 0.999, (r, key, t)
