@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--hot", type=int, default=0,
+                    help="c3: every token routed among experts 0..hot-1 (groups of many tokens)")
+    ap.add_argument("--tmin", type=int, default=1, help="c3: smallest batch per call")
     ap.add_argument("--p2p", action="store_true",
                     help="N > 1: exchange over NVLink peer memory inside the kernels instead of NCCL")
     ap.add_argument("--replicas", action="store_true",
@@ -518,13 +521,16 @@ C3_WORKLOAD = ("C3 ragged continuous batch of the C2 layer: per call T ~ U{1..64
                "(seeded), top-8 of softmax(N(0,1) logits) per token, pairs grouped per expert")
 
 
-def c3_plan(calls: int, seed: int = 3, tmin: int = 1, tmax: int = 64):
+def c3_plan(calls: int, seed: int = 3, tmin: int = 1, tmax: int = 64, hot: int = 0):
     """Token counts per call and the host-side routing of every token (for the distinct-
-    expert byte count): T_i ~ U{tmin..tmax}, x and logits N(0,1)."""
+    expert byte count): T_i ~ U{tmin..tmax}, x and logits N(0,1); hot > 0 adds 8 to the
+    logits of experts 0..hot-1 (every token then picks among them: large groups)."""
     rng = np.random.default_rng(seed)
     Ts = rng.integers(tmin, tmax + 1, size=calls)
     X = rng.normal(0, 1, (int(Ts.sum()), H)).astype(np.float32)
     LG = rng.normal(0, 1, (int(Ts.sum()), E)).astype(np.float32)
+    if hot:
+        LG[:, :hot] += 8.0
     top = np.argsort(-LG, axis=1, kind="stable")[:, :K]
     offs = np.concatenate([[0], np.cumsum(Ts)])
     distinct = [len(np.unique(top[offs[i]:offs[i + 1]])) for i in range(calls)]
@@ -549,7 +555,7 @@ def run_c3(args, rank, world, local_rank):
     L, n = args.layers, args.calls
     stores = [make_expert_store(plugin, E, H, F, seed=10_000 * rank + l) for l in range(L)]
     layers = [MoeLayer(plugin, E, H, F, K, st.pointers()) for st in stores]
-    Ts, offs, Xh, LGh, distinct = c3_plan(n, seed=3 + rank)
+    Ts, offs, Xh, LGh, distinct = c3_plan(n, seed=3 + rank, tmin=args.tmin, hot=args.hot)
     ntok = int(Ts.sum())
     xs, lgs = torch.from_numpy(Xh).cuda(), torch.from_numpy(LGh).cuda()
     ys = torch.empty((ntok, H), device="cuda")
@@ -632,7 +638,10 @@ def run_c3(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": C3_WORKLOAD, "calls_per_step": n, "tokens_per_step": ntok,
+            "config": {"workload": C3_WORKLOAD + (f"; hot experts 0..{args.hot - 1} (+8 logits)"
+                                                   if args.hot else ""),
+                       "tensor_cores": os.environ.get("KATALI_CUDA_NO_TC") != "1",
+                       "calls_per_step": n, "tokens_per_step": ntok,
                        "distinct_experts_per_step": int(sum(distinct)),
                        "tokens_per_s": round(tok_s, 1), "us_per_call": round(us_call, 3),
                        "l2": "inputs larger than L2: 16-layer store (8.4 GB) rotated per call",

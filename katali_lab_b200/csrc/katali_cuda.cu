@@ -557,6 +557,13 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
     b.rbd = pl.rbd;
     b.status = g_status_dev;
     b.sms = g_num_sms;
+    // Groups of >= 16 tokens run gate/up on the tensor cores (Q4_K gate and up only);
+    // KATALI_CUDA_NO_TC=1 keeps every group on the DP4A kernels.
+    const char *no_tc = getenv("KATALI_CUDA_NO_TC");
+    b.tc_min = (pl.gate_type == KATALI_TYPE_Q4_K && pl.up_type == KATALI_TYPE_Q4_K && pl.F % 128 == 0 &&
+                !(no_tc && no_tc[0] == '1'))
+                   ? 16
+                   : 0;
     return b;
 }
 

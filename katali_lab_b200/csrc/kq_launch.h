@@ -124,6 +124,7 @@ struct MoeBatchParams {
     uint32_t *const *ep_peer_flags;
     uint32_t *ep_epoch;  // calls completed by this rank (the next call is *ep_epoch + 1)
     uint32_t *ep_done;   // last-CTA counters of the three peer kernels
+    int tc_min;          // groups with >= tc_min tokens: gate/up on the tensor cores (0: never)
 };
 // The peer-memory exchange of an expert-parallel communicator (device arrays of
 // n_ranks window pointers; see MoeBatchParams).
@@ -135,6 +136,7 @@ struct EpPeer {
     uint32_t *epoch, *done;
 };
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
+void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st);
 cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st);

@@ -265,6 +265,7 @@ __global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
     const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
     if (g >= *p.n_groups) return;
     const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+    if (p.tc_min > 0 && p1 - p0 >= p.tc_min) return;  // the tensor-core kernel takes it
     const int F = p.F, K = p.K, U = p.H / 64;
     const int j0 = rb * rows, nrows = min(rows, F - j0);
     if (!p.experts[3 * e] || !p.experts[3 * e + 1]) {  // not resident: report, skip
@@ -659,6 +660,7 @@ static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
         set_smem(moe_batch_gateup<T_Q6_K, T_Q6_K>, gsm);
         moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, gsm, st>>>(p);
     }
+    if (p.tc_min > 0) launch_gateup_tc(p, max_groups, st);
     const int P = p.T * p.K;
     moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
     const int dgrid = max_groups * ((p.H + p.dn_rows - 1) / p.dn_rows);

@@ -3,9 +3,11 @@
 Bars, per token of a batch: routing identical to the batch-1 kernel, output within
 rel_L2 <= 1e-5 of the q8_1 restatement (port.moe_layer, mode 0) and at least 99.9 %
 of elements bit-equal to it; the same bars against the batch-1 kernel's output for
-the same token. Edge cases: one token, every token on the same experts (>= 16
-tokens per expert), batch sizes that grow and shrink between calls, no-norm
-routing, 1024 experts with top-16, and the argument checks."""
+the same token. Groups of >= 16 tokens run gate/up on the tensor cores (tcgen05
+int8 MMA) with fp32 block terms; their bar is TC_TOL below. Edge cases: one token,
+every token on the same experts, groups of 16 / 33 / 100 tokens, batch sizes that
+grow and shrink between calls, no-norm routing, 1024 experts with top-16, and the
+argument checks."""
 import numpy as np
 import pytest
 
@@ -64,13 +66,40 @@ def test_batch_single_token_equals_batch1(c3_layer):
         assert np.mean(Y[0] == y1) >= 0.999
 
 
-def test_batch_skewed_routing(c3_layer, port):
-    """Every token on the same 8 experts: 48 tokens per expert."""
+TC_TOL = 5e-4  # tensor-core gate/up: fp32 block terms, then q8_1 of h can flip a rounding
+
+
+def check_tokens_tc(layer, port, X, L, Y):
+    """Tokens whose experts ran on the tensor-core path: each block term is rounded to
+    fp32 (the DP4A path keeps exact double terms), and the q8_1 quantisation of h can
+    then flip the odd rounding, so the bar against the q8_1 restatement is TC_TOL, two
+    orders of magnitude below the q8_1 vs fp32 activation difference (~1e-2)."""
+    for t in range(X.shape[0]):
+        want, _, _, _ = port.moe_layer(layer.host, X[t], L[t], mode=0)
+        assert rel_l2(Y[t], want) <= TC_TOL, t
+
+
+def test_batch_skewed_routing(c3_layer, port, monkeypatch):
+    """Every token on the same 8 experts: 48 tokens per expert, the tensor-core path
+    (tcgen05 int8 MMA) for gate/up; and the same batch with it switched off."""
     X, L = batch_inputs(500, 48, 2048, 64, bias=[3, 9, 10, 17, 33, 40, 41, 63])
     Y = run_batch(c3_layer, X, L)
-    check_tokens(c3_layer, port, X[:12], L[:12], Y[:12], against_batch1=False)
-    # the rest: same bar against the restatement on a sample
-    check_tokens(c3_layer, port, X[40:], L[40:], Y[40:], against_batch1=False)
+    check_tokens_tc(c3_layer, port, X, L, Y)
+    monkeypatch.setenv("KATALI_CUDA_NO_TC", "1")
+    Y2 = run_batch(c3_layer, X, L)
+    check_tokens(c3_layer, port, X[:12], L[:12], Y2[:12], against_batch1=False)
+    check_tokens(c3_layer, port, X[40:], L[40:], Y2[40:], against_batch1=False)
+    assert rel_l2(Y.ravel(), Y2.ravel()) <= TC_TOL
+
+
+@pytest.mark.parametrize("T,hot", [(16, 8), (33, 8), (100, 8), (64, 3)])
+def test_batch_tensor_core_groups(c3_layer, port, T, hot):
+    """Groups of exactly 16, of 33 (a partial second token tile), of 100 tokens, and a
+    mix where some experts have >= 16 tokens and others fewer."""
+    X, L = batch_inputs(600 + T + hot, T, 2048, 64, bias=list(range(hot)))
+    Y = run_batch(c3_layer, X, L)
+    idx = sorted({0, T // 3, T // 2, T - 1})
+    check_tokens_tc(c3_layer, port, X[idx], L[idx], Y[idx])
 
 
 def test_batch_ragged_sequence(c3_layer, port):
