@@ -135,7 +135,10 @@ int katali_cuda_moe_set_expert(KataliMoe *m, uint32_t e, const void *gate,
                                const void *up, const void *down);
 int katali_cuda_moe_destroy(KataliMoe *m);
 /* One token: y[H] = sum_k w_k * down_ek(silu(gate_ek x) * up_ek x), with
- * (e_k, w_k) the top-k of softmax(router_logits[n_experts]). One launch. */
+ * (e_k, w_k) the top-k of softmax(router_logits[n_experts]). One launch. A layer
+ * shape whose single-launch plan does not fit shared memory (e.g. FFN 768) runs
+ * the ragged-batch pipeline with one token instead (q8_1 mode; in fp32 mode such
+ * shapes return KATALI_ERR_UNSUPPORTED_SHAPE). */
 int katali_cuda_moe_layer(KataliMoe *m, const float *x, const float *router_logits,
                           float *y, uint32_t mode);
 /* Same with routing given: ids[top_k] (int32), w[top_k] (fp32). */

@@ -487,10 +487,26 @@ int katali_cuda_moe_destroy(KataliMoe *m) {
     return KATALI_OK;
 }
 
+static int grow_batch_scratch(KataliMoe *m, int T);
+static kq::MoeBatchParams batch_params(KataliMoe *m, int T);
+
 static int moe_run(KataliMoe *m, const float *x, const float *logits, const int32_t *ids,
                    const float *w, float *y, uint32_t mode, int route_only) {
     if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
-    if (!m->plan_ok[mode]) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    if (!m->plan_ok[mode]) {
+        // Shapes whose fused single-launch plan does not fit shared memory (e.g. FFN 768):
+        // the ragged-batch pipeline with one token, q8_1 activations.
+        if (mode != KATALI_MOE_Q8_1 || route_only) return KATALI_ERR_UNSUPPORTED_SHAPE;
+        int s = grow_batch_scratch(m, 1);
+        if (s) return s;
+        kq::MoeBatchParams b = batch_params(m, 1);
+        b.X = x;
+        b.logits = logits;
+        b.ids_in = ids;
+        b.w_in = w;
+        b.Y = y;
+        return finish(kq::launch_moe_batch(b, g_stream));
+    }
     kq::MoeParams p = m->plan[mode];
     p.experts = m->d_table;
     p.x = x;

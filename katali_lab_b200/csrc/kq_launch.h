@@ -125,6 +125,8 @@ struct MoeBatchParams {
     uint32_t *ep_epoch;  // calls completed by this rank (the next call is *ep_epoch + 1)
     uint32_t *ep_done;   // last-CTA counters of the three peer kernels
     int tc_min;          // groups with >= tc_min tokens: gate/up on the tensor cores (0: never)
+    const int32_t *ids_in;  // routing given (ids / weights [T][K]) instead of logits
+    const float *w_in;
 };
 // The peer-memory exchange of an expert-parallel communicator (device arrays of
 // n_ranks window pointers; see MoeBatchParams).

@@ -78,12 +78,20 @@ __global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K;
     const float *x = p.X + (size_t)t * H;
-    for (int i = threadIdx.x; i < p.n_experts; i += BT) s_lg[i] = p.logits[(size_t)t * p.n_experts + i];
+    if (!p.ids_in)
+        for (int i = threadIdx.x; i < p.n_experts; i += BT) s_lg[i] = p.logits[(size_t)t * p.n_experts + i];
     __syncthreads();
     if (warp == 0) {
-        int id;
-        float w;
-        route_token(s_lg, p.n_experts, K, p.norm, lane, &id, &w);
+        int id = 0;
+        float w = 0.0f;
+        if (p.ids_in) {  // routing given by the caller
+            if (lane < K) {
+                id = p.ids_in[t * K + lane];
+                w = p.w_in[t * K + lane];
+            }
+        } else {
+            route_token(s_lg, p.n_experts, K, p.norm, lane, &id, &w);
+        }
         if (lane < K) {
             p.ids[t * K + lane] = id;
             p.w[t * K + lane] = w;
