@@ -34,8 +34,15 @@ constexpr int HB = 32;        // row pairs per phase-A block = one q8_1 block of
 constexpr int HCH = 16;       // row pairs per TMA chunk
 constexpr int NCH = HB / HCH; // chunks per block
 constexpr int MAX_ABLK = 8;   // phase-A blocks per CTA
-constexpr int NBARS = MAX_ABLK * NCH + 1;
+constexpr int DBAR = MAX_ABLK * NCH;       // first down-row barrier (one per selected expert)
+constexpr int NBARS = DBAR + MOE_MAX_K;
+constexpr int BAR_SLOTS = (NBARS + 2) & ~1;  // barriers + a spare, an even count of 8-byte slots
 constexpr int REC_BYTES = 48; // q8_1 record of h: 32 x int8, d, sum32, sum16[2]
+// The misc region holds, from a 128-byte boundary: the expert table (48-byte pairs), the
+// barriers, ids, weights, h values and the q8_1 records of h, which are read as 16-byte
+// vectors and so must start on a 16-byte boundary.
+static_assert((8 * BAR_SLOTS + 8 * MOE_MAX_K + 4 * MAX_ABLK * HB) % 16 == 0,
+              "q8_1 records of h must start 16-byte aligned");
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
     uint32_t v;
@@ -242,10 +249,13 @@ __device__ __forceinline__ double q4k_q8_unit_r(const uint8_t *row, int u, const
 }
 
 // Decode Q6_K unit u of a raw row (quarter pair {qo, qo+2} of half h of block b)
-// into its unsigned 6-bit values q at vals (element order), and, once per block,
-// its 16 int8 sub-scales and fp16 scale (as float).
+// into its unsigned 6-bit values q at vals, and, once per block, its 16 int8
+// sub-scales and fp16 scale (as float). nun = 0: element order. nun = F / 64:
+// chunk-major order, the 16-element chunk c of unit v at 16 * (c * nun + v), so
+// that eight lanes reading chunk c of eight consecutive units touch 128
+// contiguous bytes (no bank conflicts).
 __device__ __forceinline__ void q6k_decode_unit(const uint8_t *row, int u, int8_t *vals,
-                                                int8_t *scales, float *dd) {
+                                                int8_t *scales, float *dd, int nun = 0) {
     const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
     const uint8_t *blk = row + Q6K_BYTES * b;
     uint32_t ql[8], qh[8];
@@ -260,12 +270,14 @@ __device__ __forceinline__ void q6k_decode_unit(const uint8_t *row, int u, int8_
         va[i] = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
         vb[i] = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
     }
-    uint4 *da = reinterpret_cast<uint4 *>(vals + 256 * b + 128 * h + 32 * qo);
-    uint4 *db = reinterpret_cast<uint4 *>(vals + 256 * b + 128 * h + 32 * qo + 64);
-    da[0] = make_uint4(va[0], va[1], va[2], va[3]);
-    da[1] = make_uint4(va[4], va[5], va[6], va[7]);
-    db[0] = make_uint4(vb[0], vb[1], vb[2], vb[3]);
-    db[1] = make_uint4(vb[4], vb[5], vb[6], vb[7]);
+    // va: elements [32 qo, 32 qo + 32) of unit 4b + 2h; vb: the same of unit 4b + 2h + 1
+    const int va0 = nun ? 16 * (2 * qo * nun + 4 * b + 2 * h) : 256 * b + 128 * h + 32 * qo;
+    const int vb0 = nun ? va0 + 16 : va0 + 64;
+    const int c1 = nun ? 16 * nun : 16;  // from chunk 2qo to chunk 2qo + 1
+    *reinterpret_cast<uint4 *>(vals + va0) = make_uint4(va[0], va[1], va[2], va[3]);
+    *reinterpret_cast<uint4 *>(vals + va0 + c1) = make_uint4(va[4], va[5], va[6], va[7]);
+    *reinterpret_cast<uint4 *>(vals + vb0) = make_uint4(vb[0], vb[1], vb[2], vb[3]);
+    *reinterpret_cast<uint4 *>(vals + vb0 + c1) = make_uint4(vb[4], vb[5], vb[6], vb[7]);
     if ((u & 3) == 0) {
         uint32_t sc[4];
         load16_a2(blk + 192, sc);
@@ -315,7 +327,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     uint8_t *misc = smem + p.misc_off;
     const uint8_t **s_tab = reinterpret_cast<const uint8_t **>(misc);  // 3 * n_experts pointers
     uint64_t *bars = reinterpret_cast<uint64_t *>(misc + 24 * ((p.n_experts + 1) & ~1));
-    int32_t *s_ids = reinterpret_cast<int32_t *>(bars + NBARS + 1);
+    int32_t *s_ids = reinterpret_cast<int32_t *>(bars + BAR_SLOTS);
     float *s_w = reinterpret_cast<float *>(s_ids + MOE_MAX_K);
     float *s_h = s_w + MOE_MAX_K;                                   // MAX_ABLK * HB floats
     uint8_t *s_rec = reinterpret_cast<uint8_t *>(s_h + MAX_ABLK * HB);  // MAX_ABLK * REC_BYTES
@@ -380,13 +392,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         const int nchunk = nbA * NCH;
         const uint32_t per = nrB * rbd;
         if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
-        if (lane == 31 && nrB) mbar_arrive_expect_tx(&bars[NBARS - 1], per * (uint32_t)K);
+        if (nrB && lane < K) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
         __syncwarp();
         const int nB = nrB ? K : 0;
         const int ncopy = 2 * nchunk + nB;
-        // Down rows first: they are decoded while the gate/up rows are still arriving.
-        for (int q0 = lane; q0 < ncopy; q0 += 32) {
-            const int q = q0 < nB ? 2 * nchunk + q0 : q0 - nB;
+        // Gate/up rows first (phase A waits for them), then each selected expert's
+        // down rows on its own barrier, decoded as they arrive.
+        for (int q = lane; q < ncopy; q += 32) {
             if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
                 const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
                 const uint32_t blk = b0 + a;
@@ -401,7 +413,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 const int k = q - 2 * nchunk;
                 const uint8_t *base = s_tab[3 * s_ids[k] + 2];
                 bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
-                               per, &bars[NBARS - 1], pol, p.status);
+                               per, &bars[DBAR + k], pol, p.status);
             }
         }
         trace(p, 3);
@@ -486,30 +498,38 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     }
 
     // ---- 4. grid barrier: arrive, decode the down rows while waiting, then wait ----
+    // The CTA barrier orders every thread's h stores before thread 0's release.
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        red_release_gpu_add(&p.sync[0], 1u);
-    }
+    if (tid == 0) red_release_gpu_add(&p.sync[0], 1u);
     const bool predecode = MODE == 0 && DT == T_Q6_K && p.dec_enabled && nrB != 0;
+    // Phase B's expert-major path (F a power of two from 256 to 2048) reads h and the
+    // decoded down rows in chunk-major order; the row-major path in element order.
+    const bool xmaj = predecode && (F == 256 || F == 512 || F == 1024 || F == 2048);
     uint8_t *sdec = smem + p.dec_off;
     const uint32_t drb = p.dec_row_bytes;
     const uint32_t dstride = nrB * drb + 16;  // padded decoded expert stride
     if (predecode) {
-        if (!mbar_wait_warp(&bars[NBARS - 1], 0)) {
-            if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
-        } else {
-            trace(p, 13);
-            const int upr = F / 64;  // units per row
-            const int total = K * (int)nrB * upr;
-            for (int t = tid; t < total; t += MOE_THREADS) {
-                const int u = t % upr, r = t / upr, kk = r / (int)nrB, rr = r - kk * (int)nrB;
-                uint8_t *drow = sdec + (size_t)kk * dstride + (size_t)rr * drb;
-                q6k_decode_unit(sb + (size_t)kk * (nrB * rbd + 16) + (size_t)rr * rbd, u,
-                                reinterpret_cast<int8_t *>(drow),
-                                reinterpret_cast<int8_t *>(drow + F),
-                                reinterpret_cast<float *>(drow + F + F / 16));
+        // Units in expert order; a thread waits for an expert's rows only when it
+        // reaches that expert's units, so decoding overlaps the later arrivals.
+        trace(p, 13);
+        const int upr = F / 64;  // units per row
+        const int per_k = (int)nrB * upr;
+        const int total = K * per_k;
+        int kw = -1;  // the expert whose rows this thread has seen arrive
+        for (int t = tid; t < total; t += MOE_THREADS) {
+            const int kk = t / per_k, rem = t - kk * per_k, rr = rem / upr, u = rem - rr * upr;
+            if (kk != kw) {
+                if (!mbar_wait(&bars[DBAR + kk], 0)) {
+                    *p.status |= ERR_TIMEOUT_TMA;
+                    break;
+                }
+                kw = kk;
             }
+            uint8_t *drow = sdec + (size_t)kk * dstride + (size_t)rr * drb;
+            q6k_decode_unit(sb + (size_t)kk * (nrB * rbd + 16) + (size_t)rr * rbd, u,
+                            reinterpret_cast<int8_t *>(drow),
+                            reinterpret_cast<int8_t *>(drow + F),
+                            reinterpret_cast<float *>(drow + F + F / 16), xmaj ? upr : 0);
         }
     }
     trace(p, 14);
@@ -535,12 +555,15 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *hfs = hf + (size_t)K * F;
     if (MODE == 0) {
         const int nrec = (int)BA;
+        const int nun = F / 64;
         for (int t = tid; t < 3 * nrec; t += MOE_THREADS) {
             const int r = t / 3, part = t - 3 * r;
             const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.hbuf) + t);
-            if (part < 2) {
+            if (part < 2) {  // elements [32 jb + 16 part, +16) of expert kk's h
                 const int kk = r / (F / HB), jb = r - kk * (F / HB);
-                reinterpret_cast<uint4 *>(hq + (size_t)kk * (F + 16) + HB * jb)[part] = v;
+                const int off = xmaj ? 16 * ((2 * (jb & 1) + part) * nun + (jb >> 1))
+                                     : HB * jb + 16 * part;
+                *reinterpret_cast<uint4 *>(hq + (size_t)kk * (F + 16) + off) = v;
             } else {
                 hd[r] = __uint_as_float(v.x);
                 hs32[r] = (int)v.y;
@@ -561,9 +584,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
 
     // ---- 6. phase B: K down rows per output row, fixed-order weighted sum ------
     if (nrB) {
-        if (!predecode && !mbar_wait_warp(&bars[NBARS - 1], 0)) {
+        bool down_in = true;  // the decode loop has already waited in predecode mode
+        if (!predecode)
+            for (int kk = 0; kk < K; ++kk) down_in &= mbar_wait_warp(&bars[DBAR + kk], 0);
+        if (!down_in) {
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
-        } else if (predecode && (F == 256 || F == 512 || F == 1024 || F == 2048)) {
+        } else if (xmaj) {
             trace(p, 7);
             // Expert-major: warp -> (expert k, row subset); lane -> (row slot, 64-element
             // unit u). The lane keeps unit u of expert k's h in registers and dots it
@@ -576,11 +602,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             const int u = lane % nunits, rs = lane / nunits;
             float *s_dot = reinterpret_cast<float *>(smem + p.sdot_off);  // [K][nrB]
             if (k < K) {
-                const int8_t *hk = hq + (size_t)k * (F + 16) + 64 * u;
-                const uint4 a0 = reinterpret_cast<const uint4 *>(hk)[0];
-                const uint4 a1 = reinterpret_cast<const uint4 *>(hk)[1];
-                const uint4 a2 = reinterpret_cast<const uint4 *>(hk)[2];
-                const uint4 a3 = reinterpret_cast<const uint4 *>(hk)[3];
+                const int8_t *hk = hq + (size_t)k * (F + 16) + 16 * u;  // chunk-major
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(hk);
+                const uint4 a1 = *reinterpret_cast<const uint4 *>(hk + 16 * nunits);
+                const uint4 a2 = *reinterpret_cast<const uint4 *>(hk + 32 * nunits);
+                const uint4 a3 = *reinterpret_cast<const uint4 *>(hk + 48 * nunits);
                 const double dx0 = (double)hd[(size_t)k * F / 32 + 2 * u];
                 const double dx1 = (double)hd[(size_t)k * F / 32 + 2 * u + 1];
                 const int4 x16 = reinterpret_cast<const int4 *>(hs16 + (size_t)k * F / 16)[u];
@@ -590,11 +616,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                     const bool live = r < nrB;
                     if (live) {
                         const uint8_t *drow = sdec + (size_t)k * dstride + (size_t)r * drb;
-                        const uint4 *w = reinterpret_cast<const uint4 *>(drow + 64 * u);
+                        const uint8_t *w = drow + 16 * u;  // chunk-major
                         int sg[4];
 #pragma unroll
                         for (int gq = 0; gq < 4; ++gq) {
-                            const uint4 wv = w[gq], xv = av[gq];
+                            const uint4 wv = *reinterpret_cast<const uint4 *>(w + 16 * gq * nunits);
+                            const uint4 xv = av[gq];
                             int acc = __dp4a((int)wv.x, (int)xv.x, 0);
                             acc = __dp4a((int)wv.y, (int)xv.y, acc);
                             acc = __dp4a((int)wv.z, (int)xv.z, acc);
@@ -690,7 +717,7 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     const uint32_t KF = (uint32_t)p.K * p.F;
     const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16 : KF * 4 + KF / 32 * 4;
     p.misc_off = al128(p.hact_off + hact);
-    const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * (NBARS + 1) +
+    const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * BAR_SLOTS +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
                           4 * (uint32_t)p.n_experts;
     p.sdot_off = al128(p.misc_off + misc);
