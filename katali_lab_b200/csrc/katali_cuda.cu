@@ -193,10 +193,14 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
         off += (bytes + 255) & ~(size_t)255;
         return ptr;
     };
+    // First, at an offset that does not depend on T: the group count and the counters
+    // that must keep their values from one call to the next (the fused pipeline's grid
+    // barrier is left zero by each launch, whatever the batch size of the next).
+    unsigned char *ng = take(32);
     unsigned char *ids = take(4 * P), *w = take(4 * P);
     unsigned char *xq = take(T * H), *xd = take(4 * T * H / 32), *xs32 = take(4 * T * H / 32),
                   *xs16 = take(4 * T * H / 16);
-    unsigned char *ge = take(4 * E), *go = take(4 * (E + 1)), *ng = take(4), *ps = take(4 * P),
+    unsigned char *ge = take(4 * E), *go = take(4 * (E + 1)), *ps = take(4 * P),
                   *po = take(4 * P);
     unsigned char *h = take(4 * P * F), *hq = take(P * F), *hd = take(4 * P * F / 32),
                   *hs32 = take(4 * P * F / 32), *hs16 = take(4 * P * F / 16);
@@ -211,6 +215,7 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
         b->grp_expert = (int *)ge;
         b->grp_off = (int *)go;
         b->n_groups = (int *)ng;
+        b->work = (uint32_t *)(ng + 4);
         b->pair_src = (int *)ps;
         b->pos_of = (int *)po;
         b->h = (float *)h;
@@ -551,7 +556,10 @@ static int grow_batch_scratch(KataliMoe *m, int T) {
         return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
     }
     m->bscratch_bytes = need;
-    return KATALI_OK;
+    // zero once: the fused pipeline's grid-barrier counters start from zero (each
+    // launch leaves them zero again)
+    e = cudaMemsetAsync(m->bscratch, 0, need, g_stream);
+    return e == cudaSuccess ? KATALI_OK : cuda_fail(e);
 }
 
 static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {

@@ -7,20 +7,22 @@
 //  1. Every CTA routes redundantly (warp 0: top-k over the router logits held
 //     in registers, deterministic ties) while the other warps stage x in
 //     shared memory with one vector load per thread.
-//  2. Thread 0 then requests ALL of the CTA's expert bytes at once with
-//     cp.async.bulk (TMA, no multicast) into shared memory: its phase-A blocks
-//     (32 gate/up row pairs each, four 8-pair chunks with one mbarrier each)
-//     and its slice of the H down rows for all K selected experts (phase B, one
-//     mbarrier). At the C2 shape (H 2048, F 512, top-8) that is ~120 KB per
-//     SM, so the whole 16.3 MB layer is in flight from the start.
+//  2. The CTA then requests ALL of its expert bytes at once with cp.async.bulk
+//     (TMA, no multicast) into shared memory, one copy per warp in turn: its
+//     phase-A blocks (32 gate/up row pairs each, two 16-pair chunks with one
+//     mbarrier each) first, then its slice of the H down rows for each of the K
+//     selected experts (one mbarrier per expert). At the C2 shape (H 2048, F 512,
+//     top-8) that is ~120 KB per SM, so the whole 16.3 MB layer is in flight.
 //  3. Phase A: each warp computes two gate/up row pairs against q8_1(x) with
 //     DP4A; silu(g)*u lands in shared memory and the CTA quantises its
 //     32-value block of h to q8_1 itself, writing one 48-byte record.
-//  4. Grid barrier (one counter, bounded spin, error bit on timeout).
+//  4. Grid barrier (one counter, bounded spin, error bit on timeout); while it
+//     waits, the CTA decodes each expert's Q6_K down rows to 6-bit values as
+//     they arrive.
 //  5. Phase B: every CTA loads the K*F/32 h records (6 KB at C2) with one vector
-//     load per thread, then a warp per output row dots the K down rows
-//     (already in shared memory) and forms sum_k w_k * down_k in a fixed order:
-//     deterministic, no atomics.
+//     load per thread, dots each expert's decoded rows with its h (both in a
+//     chunk-major order that keeps the lanes' 16-byte reads conflict-free) and
+//     forms sum_k w_k * down_k in a fixed order: deterministic, no atomics.
 // Optional tracing: when p.trace is set, thread 0 of every CTA records
 // %globaltimer at the phase boundaries (TRACE_SLOTS per CTA).
 #include "kq_device.cuh"
@@ -343,6 +345,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                    rbd = SHAPE ? 420u : p.rbd;
     const uint32_t blk_bytes = HB * (rbg + rbu);
 
+    if (tid == 32 && !p.route_only) {  // warp 1: keep warp 0 free for routing
+        for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+
     if (p.route_only) {  // check entry point: the routing decision only
         if (warp == 0) {
             route(p, s_logits, s_ids, s_w, lane);
@@ -352,10 +359,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             }
         }
         return;
-    }
-    if (tid == 32) {  // warp 1: keep warp 0 free for routing
-        for (int i = 0; i < NBARS; ++i) mbar_init(&bars[i], 1);
-        fence_mbar_init();
     }
 
     // ---- 1. routing (warp 0) and x staging (all other threads) --------------
@@ -386,39 +389,45 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     __syncthreads();
     trace(p, 2);
 
-    // ---- 2. request every expert byte this CTA needs (warp 0, one copy per lane) ----
-    if (warp == 0) {
+    // ---- 2. request every expert byte this CTA needs (lane 0 of every warp) ----
+    // Copy q: gate/up rows first (phase A waits for them), then each selected expert's
+    // down rows on its own barrier, decoded as they arrive. Copy q is issued by warp
+    // q % 16, so the copies leave the SM without queueing behind one issuing thread;
+    // a copy may complete before warp 0 has armed its barrier (the transaction count
+    // goes negative until the expect-tx arrival), which the barrier allows.
+    const int nchunk = nbA * NCH;
+    const uint32_t per = nrB * rbd;
+    const int ncopy = 2 * nchunk + (nrB ? K : 0);
+    auto issue = [&](int q) {
         const uint64_t pol = l2_evict_first_policy();
-        const int nchunk = nbA * NCH;
-        const uint32_t per = nrB * rbd;
+        if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
+            const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
+            const uint32_t blk = b0 + a;
+            const int k = (int)(blk / (F / HB));
+            const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
+            const uint32_t rb = up ? rbu : rbg;
+            const uint8_t *base = s_tab[3 * s_ids[k] + up];
+            const uint8_t *src = base ? base + (size_t)j0 * rb : nullptr;
+            uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
+            bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol, p.status);
+        } else {  // down rows [rB0, rB0 + nrB) of selected expert k
+            const int k = q - 2 * nchunk;
+            const uint8_t *base = s_tab[3 * s_ids[k] + 2];
+            bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
+                           per, &bars[DBAR + k], pol, p.status);
+        }
+    };
+    if (warp == 0) {
         if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
         if (nrB && lane < K) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
         __syncwarp();
-        const int nB = nrB ? K : 0;
-        const int ncopy = 2 * nchunk + nB;
-        // Gate/up rows first (phase A waits for them), then each selected expert's
-        // down rows on its own barrier, decoded as they arrive.
-        for (int q = lane; q < ncopy; q += 32) {
-            if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
-                const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
-                const uint32_t blk = b0 + a;
-                const int k = (int)(blk / (F / HB));
-                const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
-                const uint32_t rb = up ? rbu : rbg;
-                const uint8_t *base = s_tab[3 * s_ids[k] + up];
-                const uint8_t *src = base ? base + (size_t)j0 * rb : nullptr;
-                uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
-                bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol, p.status);
-            } else {  // down rows [rB0, rB0 + nrB) of selected expert k
-                const int k = q - 2 * nchunk;
-                const uint8_t *base = s_tab[3 * s_ids[k] + 2];
-                bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
-                               per, &bars[DBAR + k], pol, p.status);
-            }
-        }
+        for (int q = 0; q < ncopy; q += MOE_WARPS)
+            if (lane == 0) issue(q);
         trace(p, 3);
         if (!p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
     } else if (warp > 0) {
+        for (int q = warp; q < ncopy; q += MOE_WARPS)
+            if (lane == 0) issue(q);
         for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
             const float v = xf[32 * g + lane];
             if (MODE == 0) {

@@ -10,11 +10,13 @@
 // Pipeline (one stream, six launches):
 //   route  : one CTA per token: top-k + weights, x -> q8_1 (split layout)
 //   group  : one CTA: counting sort of the pairs by expert id
-//   gateup : CTA = (group, 32 row pairs); warp = 4 row pairs; loop over the
-//            group's tokens; h = silu(g) * u per pair
+//   gateup : item = (group, a tile of up to 16 rows of F); the grid is the resident CTAs, which
+//            take items from a counter; loop over the group's tokens; h = silu(g) * u
 //   hquant : h -> q8_1 per pair (split layout with 16-element sums)
-//   down   : CTA = (group, 32 output rows); warp = 4 rows; loop over tokens
+//   down   : item = (group, up to 64 output rows), scheduled the same way
 //   combine: y[t] = sum_k w[t][k] * part[pair(t,k)] in k order
+#include <cstdlib>
+
 #include "kq_device.cuh"
 #include "kq_launch.h"
 
@@ -73,9 +75,9 @@ __device__ __forceinline__ void route_token(const float *lg, int E, int K, int n
     *w_out = (float)((double)ev / S);
 }
 
-__global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
-    __shared__ float s_lg[1024];
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Token t by the whole CTA (s_lg: 1024 floats of shared memory).
+__device__ __forceinline__ void route_one(const MoeBatchParams &p, int t, float *s_lg) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K;
     const float *x = p.X + (size_t)t * H;
     if (!p.ids_in)
@@ -104,6 +106,11 @@ __global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
         for (int g = warp - 1; g < nblk; g += BT / 32 - 1)
             quant_block_q8(x[32 * g + lane], lane, q + 32 * g, d + g, s32 + g, s16 + 2 * g, nullptr);
     }
+}
+
+__global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
+    __shared__ float s_lg[1024];
+    route_one(p, blockIdx.x, s_lg);
 }
 
 // ---------------------------------------------------------------------------
@@ -136,33 +143,44 @@ __device__ __forceinline__ int block_exscan(int v, int *wsum, int &total) {
     return excl;
 }
 
-// One CTA of n_experts (<= 1024) threads: per-expert counts, offsets, the list of
-// selected experts in ascending id, and each pair's slot (order within an expert
-// is arbitrary; every pair is computed independently). Pairs with id < 0 are
-// skipped.
-__global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
-    __shared__ int cnt[1024], off[1024], wsum[32];
-    const int P = p.T * p.K, E = p.n_experts, e = threadIdx.x;
-    if (e < E) cnt[e] = 0;
+// One CTA (any size up to 1024 threads; n_experts <= 1024): per-expert counts,
+// offsets, the list of selected experts in ascending id, and each pair's slot
+// (order within an expert is arbitrary; every pair is computed independently).
+// Pairs with id < 0 are skipped. Thread i owns the contiguous experts
+// [i * epT, (i + 1) * epT), epT = ceil(E / blockDim.x), so the scans keep id order.
+__device__ void group_body(const MoeBatchParams &p, int *cnt, int *off, int *wsum) {
+    const int P = p.T * p.K, E = p.n_experts;
+    const int epT = (E + (int)blockDim.x - 1) / (int)blockDim.x, e0 = threadIdx.x * epT;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x)
         if (p.ids[i] >= 0) atomicAdd(&cnt[p.ids[i]], 1);
     __syncthreads();
-    const int c = e < E ? cnt[e] : 0;
+    int c = 0, nz = 0;
+    for (int e = e0; e < e0 + epT && e < E; ++e) {
+        c += cnt[e];
+        nz += cnt[e] > 0;
+    }
     int total, ngroups;
-    const int o = block_exscan(c, wsum, total);
-    const int gi = block_exscan(c > 0 ? 1 : 0, wsum, ngroups);
-    if (e < E) {
+    int o = block_exscan(c, wsum, total);
+    int gi = block_exscan(nz, wsum, ngroups);
+    for (int e = e0; e < e0 + epT && e < E; ++e) {
+        const int ce = cnt[e];
         off[e] = o;
-        if (c > 0) {
+        if (ce > 0) {
             p.grp_expert[gi] = e;
             p.grp_off[gi] = o;
+            ++gi;
         }
-        cnt[e] = 0;
+        o += ce;
     }
+    __syncthreads();  // every count read before the second pass reuses cnt
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     if (threadIdx.x == 0) {
         p.grp_off[ngroups] = total;
         *p.n_groups = ngroups;
+        p.work[0] = 0u;  // the item counters of this call's gate/up and down kernels
+        p.work[1] = 0u;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
@@ -172,6 +190,11 @@ __global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
         p.pair_src[pos] = i;  // i = t * K + k
         p.pos_of[i] = pos;
     }
+}
+
+__global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
+    __shared__ int cnt[1024], off[1024], wsum[32];
+    group_body(p, cnt, off, wsum);
 }
 
 // ---------------------------------------------------------------------------
@@ -245,13 +268,18 @@ __device__ __forceinline__ void stage_act(const SmemAct &sa, int n, RowOf row_of
     }
 }
 
-// Thread 0 starts the weight-tile copies on `bar` (initialised here); the caller
-// makes the barrier visible with a CTA barrier before anyone waits on it.
-__device__ __forceinline__ void issue_tiles(uint64_t *bar, int n, uint8_t *const *dst,
-                                            const uint8_t *const *src, const uint32_t *bytes) {
+// Thread 0 arms `bar` for the next phase and starts the weight-tile copies on it.
+// The barrier is initialised once per CTA (init_tiles_bar) and reused: every item
+// toggles the phase the CTA waits on.
+__device__ __forceinline__ void init_tiles_bar(uint64_t *bar) {
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
+    }
+}
+__device__ __forceinline__ void issue_tiles(uint64_t *bar, int n, uint8_t *const *dst,
+                                            const uint8_t *const *src, const uint32_t *bytes) {
+    if (threadIdx.x == 0) {
         uint32_t total = 0;
         for (int i = 0; i < n; ++i) total += bytes[i];
         mbar_arrive_expect_tx(bar, total);
@@ -259,168 +287,260 @@ __device__ __forceinline__ void issue_tiles(uint64_t *bar, int n, uint8_t *const
         for (int i = 0; i < n; ++i) bulk_g2s_hint(dst[i], src[i], bytes[i], bar, pol);
     }
 }
-__device__ __forceinline__ bool wait_tiles(uint64_t *bar, volatile uint32_t *status) {
-    if (mbar_wait(bar, 0)) return true;
-    if (status) atomicOr((uint32_t *)status, 4u);
+// All threads wait for phase `parity`; the outcome is made uniform across the CTA
+// so that a timeout ends every thread (and is recorded once).
+__device__ __forceinline__ bool wait_tiles(uint64_t *bar, uint32_t parity,
+                                           volatile uint32_t *status) {
+    const bool ok = mbar_wait(bar, parity);
+    if (!__syncthreads_or(!ok)) return true;
+    if (threadIdx.x == 0 && status) atomicOr((uint32_t *)status, 4u);
     return false;
+}
+
+// Item scheduling of the gate/up and down kernels: the grid is sized to the resident
+// CTAs (not to the worst-case group count). A CTA starts on item blockIdx.x and then
+// takes items gridDim.x, gridDim.x + 1, ... from a counter in arrival order, so CTAs
+// that drew small groups take more items and no CTA exists for a group the batch
+// does not have. Thread 0 asks for the next item when it starts the current one
+// and hands it over after the item, so the atomic's latency is hidden.
+__device__ __forceinline__ uint32_t next_item_async(uint32_t *counter) {
+    return threadIdx.x == 0 ? gridDim.x + atomicAdd(counter, 1u) : 0u;
+}
+// Two slots, used in turn: a thread still reading the previous hand-over's slot
+// cannot be overtaken, since thread 0 passes the next hand-over's CTA barrier only
+// after every thread has read it.
+__device__ __forceinline__ int hand_over_item(uint32_t next, int *s_next, int &slot) {
+    if (threadIdx.x == 0) s_next[slot] = (int)next;
+    __syncthreads();
+    const int v = s_next[slot];
+    slot ^= 1;
+    return v;
+}
+
+// Shared memory of an item kernel: the tile barrier, the weight tile (128-byte
+// aligned), then the staged activations of ACT_TOKS rows of length L.
+struct ItemSmem {
+    uint64_t *bar;
+    uint8_t *tile;
+    uint8_t *act;
+};
+__host__ __device__ constexpr size_t align128(size_t v) { return (v + 127) & ~(size_t)127; }
+__host__ __device__ constexpr size_t item_smem_bytes(size_t tile_bytes, int L) {
+    return 128 + align128(tile_bytes) + (size_t)ACT_TOKS * act_slot_bytes(L);
+}
+__device__ __forceinline__ ItemSmem item_smem(uint8_t *sm, size_t tile_bytes) {
+    return ItemSmem{reinterpret_cast<uint64_t *>(sm), sm + 128, sm + 128 + align128(tile_bytes)};
+}
+// Per-CTA state that carries across item loops: the tile barrier's next parity and
+// the hand-over slot.
+struct ItemState {
+    uint32_t phase;
+    int slot;
+};
+
+// ---------------------------------------------------------------------------
+// gate/up: work item = (group g, p.gu_rows rows of F). Returns false when a tile
+// wait timed out (the whole CTA then stops).
+// ---------------------------------------------------------------------------
+template <uint32_t GT, uint32_t UT>
+__device__ bool gateup_items(const MoeBatchParams &p, const ItemSmem &S, int *s_next, ItemState &st) {
+    const int rows = p.gu_rows, lpr = BT / rows;
+    const int nrb = (p.F + rows - 1) / rows;
+    const int items = *p.n_groups * nrb;
+    const int F = p.F, K = p.K, U = p.H / 64;
+    uint8_t *sg = S.tile, *su = S.tile + (size_t)rows * p.rbg;
+    const SmemAct sa = smem_act(S.act, p.H);
+    const int sub = threadIdx.x % lpr, jr = threadIdx.x / lpr;
+    for (int it = blockIdx.x; it < items;) {
+        const uint32_t next = next_item_async(&p.work[0]);
+        const int g = it / nrb, rb = it % nrb;
+        const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+        const bool tc = p.tc_min > 0 && p1 - p0 >= p.tc_min;  // the tensor-core kernel takes it
+        const bool resident = p.experts[3 * e] && p.experts[3 * e + 1];
+        if (!resident && threadIdx.x == 0 && p.status)  // not resident: report, skip
+            atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+        if (p1 <= p0 || tc || !resident) {
+            it = hand_over_item(next, s_next, st.slot);
+            continue;
+        }
+        const int j0 = rb * rows, nrows = min(rows, F - j0), j = j0 + jr;
+        const bool valid = jr < nrows;
+        __syncthreads();  // barrier init visible; the previous item's tiles are no longer read
+        {
+            uint8_t *dst[2] = {sg, su};
+            const uint8_t *src[2] = {p.experts[3 * e] + (size_t)j0 * p.rbg,
+                                     p.experts[3 * e + 1] + (size_t)j0 * p.rbu};
+            const uint32_t bytes[2] = {(uint32_t)nrows * p.rbg, (uint32_t)nrows * p.rbu};
+            issue_tiles(S.bar, 2, dst, src, bytes);
+        }
+        const uint8_t *grow = sg + (size_t)(valid ? jr : 0) * p.rbg;
+        const uint8_t *urow = su + (size_t)(valid ? jr : 0) * p.rbu;
+        bool tiles_in = false;
+        for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
+            const int nc = min(ACT_TOKS, p1 - c0);
+            if (c0 != p0) __syncthreads();  // the previous chunk is no longer read
+            stage_act(sa, nc, [&](int i) { return x_act(p, p.pair_src[c0 + i] / K); });
+            cp_async_wait_all();
+            __syncthreads();
+            if (!tiles_in) {
+                if (!wait_tiles(S.bar, st.phase, p.status)) return false;
+                st.phase ^= 1u;
+                tiles_in = true;
+            }
+            for (int i0 = 0; i0 < nc; i0 += BTC) {
+                const int nq = min(BTC, nc - i0);
+                double ag[BTC], au[BTC];
+#pragma unroll
+                for (int i = 0; i < BTC; ++i) ag[i] = au[i] = 0.0;
+                if (valid) {
+                    for (int u = sub; u < U; u += lpr) {
+                        const auto wg = load_dec<GT>(grow, u);
+                        const auto wu = load_dec<UT>(urow, u);
+#pragma unroll
+                        for (int i = 0; i < BTC; ++i) {
+                            if (i < nq) {
+                                const ActQ8D a = sa.at(i0 + i);
+                                ag[i] += dec_dot<GT>(wg, u, a);
+                                au[i] += dec_dot<UT>(wu, u, a);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < BTC; ++i) {
+                    const double dg = row_sum(ag[i], lpr), du = row_sum(au[i], lpr);
+                    if (valid && sub == 0 && i < nq)
+                        p.h[(size_t)(c0 + i0 + i) * F + j] = __fmul_rn(kq_silu((float)dg), (float)du);
+                }
+            }
+        }
+        it = hand_over_item(next, s_next, st.slot);
+    }
+    return true;
 }
 
 template <uint32_t GT, uint32_t UT>
 __global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int rows = p.gu_rows, lpr = BT / rows;
-    const int nrb = (p.F + rows - 1) / rows;
-    const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
-    if (g >= *p.n_groups) return;
-    const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
-    if (p.tc_min > 0 && p1 - p0 >= p.tc_min) return;  // the tensor-core kernel takes it
-    const int F = p.F, K = p.K, U = p.H / 64;
-    const int j0 = rb * rows, nrows = min(rows, F - j0);
-    if (!p.experts[3 * e] || !p.experts[3 * e + 1]) {  // not resident: report, skip
-        if (threadIdx.x == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
-        return;
-    }
-    uint8_t *sg = sm, *su = sm + (size_t)rows * p.rbg;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(su + (size_t)rows * p.rbu);
-    const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.H);
-    {
-        uint8_t *dst[2] = {sg, su};
-        const uint8_t *src[2] = {p.experts[3 * e] + (size_t)j0 * p.rbg,
-                                 p.experts[3 * e + 1] + (size_t)j0 * p.rbu};
-        const uint32_t bytes[2] = {(uint32_t)nrows * p.rbg, (uint32_t)nrows * p.rbu};
-        issue_tiles(bar, 2, dst, src, bytes);
-    }
-    const int sub = threadIdx.x % lpr, jr = threadIdx.x / lpr, j = j0 + jr;
-    const bool valid = jr < nrows;
-    const uint8_t *grow = sg + (size_t)(valid ? jr : 0) * p.rbg;
-    const uint8_t *urow = su + (size_t)(valid ? jr : 0) * p.rbu;
-    bool tiles_in = false;
-    for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
-        const int nc = min(ACT_TOKS, p1 - c0);
-        __syncthreads();  // barrier init visible; the previous chunk is no longer read
-        stage_act(sa, nc, [&](int i) { return x_act(p, p.pair_src[c0 + i] / K); });
-        cp_async_wait_all();
-        __syncthreads();
-        if (!tiles_in) {
-            if (!wait_tiles(bar, p.status)) return;
-            tiles_in = true;
-        }
-        for (int i0 = 0; i0 < nc; i0 += BTC) {
-            const int nq = min(BTC, nc - i0);
-            double ag[BTC], au[BTC];
-#pragma unroll
-            for (int i = 0; i < BTC; ++i) ag[i] = au[i] = 0.0;
-            if (valid) {
-                for (int u = sub; u < U; u += lpr) {
-                    const auto wg = load_dec<GT>(grow, u);
-                    const auto wu = load_dec<UT>(urow, u);
-#pragma unroll
-                    for (int i = 0; i < BTC; ++i) {
-                        if (i < nq) {
-                            const ActQ8D a = sa.at(i0 + i);
-                            ag[i] += dec_dot<GT>(wg, u, a);
-                            au[i] += dec_dot<UT>(wu, u, a);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < BTC; ++i) {
-                const double dg = row_sum(ag[i], lpr), du = row_sum(au[i], lpr);
-                if (valid && sub == 0 && i < nq)
-                    p.h[(size_t)(c0 + i0 + i) * F + j] = __fmul_rn(kq_silu((float)dg), (float)du);
-            }
-        }
-    }
+    __shared__ int s_next[2];
+    const ItemSmem S = item_smem(sm, (size_t)p.gu_rows * (p.rbg + p.rbu));
+    init_tiles_bar(S.bar);
+    ItemState st{0u, 0};
+    gateup_items<GT, UT>(p, S, s_next, st);
 }
 
 // ---------------------------------------------------------------------------
-// hquant: one warp per 32-element block of one pair's h
+// hquant: one warp per 32-element block of one pair's h (warps w0, w0 + ws, ...)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
-    const int wg = (blockIdx.x * BT + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void hquant_range(const MoeBatchParams &p, int w0, int ws) {
+    const int lane = threadIdx.x & 31;
     const int nblk = p.F / 32;
     const int P = p.grp_off[*p.n_groups];  // grouped pairs (<= T * K)
-    if (wg >= P * nblk) return;
-    const int q = wg / nblk, b = wg % nblk;
-    const float v = p.h[(size_t)q * p.F + 32 * b + lane];
-    quant_block_q8(v, lane, p.hq + (size_t)q * p.F + 32 * b, p.hd + (size_t)q * nblk + b,
-                   p.hs32 + (size_t)q * nblk + b, p.hs16 + ((size_t)q * nblk + b) * 2, nullptr);
+    for (int wg = w0; wg < P * nblk; wg += ws) {
+        const int q = wg / nblk, b = wg % nblk;
+        const float v = p.h[(size_t)q * p.F + 32 * b + lane];
+        quant_block_q8(v, lane, p.hq + (size_t)q * p.F + 32 * b, p.hd + (size_t)q * nblk + b,
+                       p.hs32 + (size_t)q * nblk + b, p.hs16 + ((size_t)q * nblk + b) * 2, nullptr);
+    }
+}
+__global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
+    hquant_range(p, (blockIdx.x * BT + threadIdx.x) >> 5, gridDim.x * (BT / 32));
 }
 
 // ---------------------------------------------------------------------------
-// down: CTA = (group g, p.dn_rows output rows), same scheme as gateup
+// down: work item = (group g, p.dn_rows output rows), same scheme as gateup
 // ---------------------------------------------------------------------------
+template <uint32_t DT>
+__device__ bool down_items(const MoeBatchParams &p, const ItemSmem &S, int *s_next, ItemState &st) {
+    const int rows = p.dn_rows, lpr = BT / rows;
+    const int nrb = (p.H + rows - 1) / rows;
+    const int items = *p.n_groups * nrb;
+    const int U = p.F / 64;
+    const SmemAct sa = smem_act(S.act, p.F);
+    const int sub = threadIdx.x % lpr, rr = threadIdx.x / lpr;
+    for (int it = blockIdx.x; it < items;) {
+        const uint32_t next = next_item_async(&p.work[1]);
+        const int g = it / nrb, rb = it % nrb;
+        const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+        const bool resident = p.experts[3 * e + 2] != nullptr;
+        if (!resident && threadIdx.x == 0 && p.status)  // not resident: report, skip
+            atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+        if (p1 <= p0 || !resident) {
+            it = hand_over_item(next, s_next, st.slot);
+            continue;
+        }
+        const int r0 = rb * rows, nrows = min(rows, p.H - r0), r = r0 + rr;
+        const bool valid = rr < nrows;
+        __syncthreads();  // barrier init visible; the previous item's tile is no longer read
+        {
+            uint8_t *dst[1] = {S.tile};
+            const uint8_t *src[1] = {p.experts[3 * e + 2] + (size_t)r0 * p.rbd};
+            const uint32_t bytes[1] = {(uint32_t)nrows * p.rbd};
+            issue_tiles(S.bar, 1, dst, src, bytes);
+        }
+        const uint8_t *row = S.tile + (size_t)(valid ? rr : 0) * p.rbd;
+        bool tiles_in = false;
+        for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
+            const int nc = min(ACT_TOKS, p1 - c0);
+            if (c0 != p0) __syncthreads();
+            stage_act(sa, nc, [&](int i) { return h_act(p, c0 + i); });
+            cp_async_wait_all();
+            __syncthreads();
+            if (!tiles_in) {
+                if (!wait_tiles(S.bar, st.phase, p.status)) return false;
+                st.phase ^= 1u;
+                tiles_in = true;
+            }
+            for (int i0 = 0; i0 < nc; i0 += BTC) {
+                const int nq = min(BTC, nc - i0);
+                double acc[BTC];
+#pragma unroll
+                for (int i = 0; i < BTC; ++i) acc[i] = 0.0;
+                if (valid) {
+                    for (int u = sub; u < U; u += lpr) {
+                        const auto w = load_dec<DT>(row, u);
+#pragma unroll
+                        for (int i = 0; i < BTC; ++i)
+                            if (i < nq) acc[i] += dec_dot<DT>(w, u, sa.at(i0 + i));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < BTC; ++i) {
+                    const double v = row_sum(acc[i], lpr);
+                    if (valid && sub == 0 && i < nq)
+                        p.part[(size_t)(c0 + i0 + i) * p.H + r] = (float)v;
+                }
+            }
+        }
+        it = hand_over_item(next, s_next, st.slot);
+    }
+    return true;
+}
+
 template <uint32_t DT>
 __global__ void __launch_bounds__(BT, 4) moe_batch_down(MoeBatchParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
-    const int rows = p.dn_rows, lpr = BT / rows;
-    const int nrb = (p.H + rows - 1) / rows;
-    const int g = blockIdx.x / nrb, rb = blockIdx.x % nrb;
-    if (g >= *p.n_groups) return;
-    const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
-    const int U = p.F / 64;
-    const int r0 = rb * rows, nrows = min(rows, p.H - r0);
-    if (!p.experts[3 * e + 2]) {  // not resident: report, skip
-        if (threadIdx.x == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
-        return;
-    }
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + (size_t)rows * p.rbd);
-    const SmemAct sa = smem_act(reinterpret_cast<uint8_t *>(bar) + 16, p.F);
-    {
-        uint8_t *dst[1] = {sm};
-        const uint8_t *src[1] = {p.experts[3 * e + 2] + (size_t)r0 * p.rbd};
-        const uint32_t bytes[1] = {(uint32_t)nrows * p.rbd};
-        issue_tiles(bar, 1, dst, src, bytes);
-    }
-    const int sub = threadIdx.x % lpr, rr = threadIdx.x / lpr, r = r0 + rr;
-    const bool valid = rr < nrows;
-    const uint8_t *row = sm + (size_t)(valid ? rr : 0) * p.rbd;
-    bool tiles_in = false;
-    for (int c0 = p0; c0 < p1; c0 += ACT_TOKS) {
-        const int nc = min(ACT_TOKS, p1 - c0);
-        __syncthreads();
-        stage_act(sa, nc, [&](int i) { return h_act(p, c0 + i); });
-        cp_async_wait_all();
-        __syncthreads();
-        if (!tiles_in) {
-            if (!wait_tiles(bar, p.status)) return;
-            tiles_in = true;
-        }
-        for (int i0 = 0; i0 < nc; i0 += BTC) {
-            const int nq = min(BTC, nc - i0);
-            double acc[BTC];
-#pragma unroll
-            for (int i = 0; i < BTC; ++i) acc[i] = 0.0;
-            if (valid) {
-                for (int u = sub; u < U; u += lpr) {
-                    const auto w = load_dec<DT>(row, u);
-#pragma unroll
-                    for (int i = 0; i < BTC; ++i)
-                        if (i < nq) acc[i] += dec_dot<DT>(w, u, sa.at(i0 + i));
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < BTC; ++i) {
-                const double v = row_sum(acc[i], lpr);
-                if (valid && sub == 0 && i < nq)
-                    p.part[(size_t)(c0 + i0 + i) * p.H + r] = (float)v;
-            }
-        }
-    }
+    __shared__ int s_next[2];
+    const ItemSmem S = item_smem(sm, (size_t)p.dn_rows * p.rbd);
+    init_tiles_bar(S.bar);
+    ItemState st{0u, 0};
+    down_items<DT>(p, S, s_next, st);
 }
 
 // ---------------------------------------------------------------------------
 // combine: y[t][r] = sum_k w[t][k] * part[pos(t,k)][r], k in rank order
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void combine_range(const MoeBatchParams &p, int i0, int is) {
+    for (int i = i0; i < p.T * p.H; i += is) {
+        const int t = i / p.H, r = i % p.H;
+        double acc = 0.0;
+        for (int k = 0; k < p.K; ++k)
+            acc += (double)p.w[t * p.K + k] * (double)p.part[(size_t)p.pos_of[t * p.K + k] * p.H + r];
+        p.Y[i] = (float)acc;
+    }
+}
 __global__ void __launch_bounds__(BT) moe_batch_combine(MoeBatchParams p) {
-    const int i = blockIdx.x * BT + threadIdx.x;
-    if (i >= p.T * p.H) return;
-    const int t = i / p.H, r = i % p.H;
-    double acc = 0.0;
-    for (int k = 0; k < p.K; ++k)
-        acc += (double)p.w[t * p.K + k] * (double)p.part[(size_t)p.pos_of[t * p.K + k] * p.H + r];
-    p.Y[i] = (float)acc;
+    combine_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
 }
 
 // ---------------------------------------------------------------------------
@@ -532,20 +652,22 @@ __global__ void __launch_bounds__(BT) moe_ep_dispatch(MoeBatchParams p) {
     if (p.ep_p2p) signal_peers(p, 0, 0, e);
 }
 
-// CTA per received slot: header -> pair ids/weights (ids -1 for empty slots);
-// GGUF q8_1 row -> split activations with integer 32- and 16-element sums.
-__global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
-    const int s = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Received slot s by the whole CTA: header -> pair ids/weights (ids -1 for empty
+// slots); GGUF q8_1 row -> split activations with integer 32- and 16-element sums.
+// s_ok: one int of shared memory.
+__device__ void unpack_slot(const MoeBatchParams &p, int s, int *s_ok) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int H = p.H, K = p.K, nblk = H / 32;
     const uint8_t *slot = p.ep_recv + (size_t)s * p.ep_slot_bytes;
     if (p.ep_p2p) {  // this rank's window, current parity; wait for the source's flag
         const uint32_t e = *p.ep_epoch + 1;
         const int G = p.ep_ranks, src = s / p.ep_tmax;
         slot = p.ep_peer_recv[p.ep_rank] + ((size_t)(e & 1u) * G * p.ep_tmax + s) * p.ep_slot_bytes;
-        __shared__ int ok;
         if (threadIdx.x == 0)
-            ok = wait_flag(p, flag_at(p.ep_peer_flags[p.ep_rank], 0, e & 1u, G, src), e);
+            *s_ok = wait_flag(p, flag_at(p.ep_peer_flags[p.ep_rank], 0, e & 1u, G, src), e);
         __syncthreads();
+        const bool ok = *s_ok;
+        __syncthreads();  // s_ok may be rewritten for the next slot
         if (!ok) {  // treated as an empty slot; the call reports the timeout
             if (threadIdx.x < K) p.ids[s * K + threadIdx.x] = -1;
             return;
@@ -573,12 +695,17 @@ __global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
         }
     }
 }
+__global__ void __launch_bounds__(BT) moe_ep_unpack(MoeBatchParams p) {
+    __shared__ int s_ok;
+    unpack_slot(p, blockIdx.x, &s_ok);
+}
 
-// ret[s][r] = sum over the slot's owned pairs k (in k order) of w_k * part[pair][r].
-__global__ void __launch_bounds__(BT) moe_ep_combine_slots(MoeBatchParams p) {
-    const int s = blockIdx.y, K = p.K;
-    const int r = blockIdx.x * BT + threadIdx.x;
-    if (r < p.H) {
+// ret[s][r] = sum over the slot's owned pairs k (in k order) of w_k * part[pair][r],
+// for the (slot, row) indices i = s * H + r in i0, i0 + is, ...
+__device__ __forceinline__ void combine_slots_range(const MoeBatchParams &p, int i0, int is) {
+    const int K = p.K;
+    for (int i = i0; i < p.T * p.H; i += is) {
+        const int s = i / p.H, r = i % p.H;
         int any = 0;
         double acc = 0.0;
         for (int k = 0; k < K; ++k) {
@@ -596,6 +723,10 @@ __global__ void __launch_bounds__(BT) moe_ep_combine_slots(MoeBatchParams p) {
             }
         }
     }
+}
+__global__ void __launch_bounds__(BT) moe_ep_combine_slots(MoeBatchParams p) {
+    const int r = blockIdx.x * BT + threadIdx.x;  // grid (H / BT, slots): one (slot, row) each
+    if (r < p.H) combine_slots_range(p, blockIdx.y * p.H + r, p.T * p.H);
     if (p.ep_p2p) signal_peers(p, 1, 1, *p.ep_epoch + 1);
 }
 
@@ -634,6 +765,100 @@ __global__ void __launch_bounds__(BT) moe_ep_combine_tokens(MoeBatchParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Fused small-batch pipeline: one cooperative launch runs route (or, expert-
+// parallel, the unpack of the received slots), group, gate/up, h quantisation,
+// down and the combine (or the per-slot sums returned to the sources), separated
+// by grid barriers. It runs the same per-item code as the separate kernels, so
+// the results are the same; it saves the launch gaps, which cost more than the
+// work when the batch is a few tokens (or the few slots an expert-parallel rank
+// receives at batch-1 decode).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Grid barrier on a counter that only grows within a launch: the n-th barrier waits
+// for n * gridDim.x arrivals. Bounded spin: on timeout the status gets
+// ERR_TIMEOUT_GRID and the CTA carries on (the call then reports the timeout).
+__device__ void grid_sync(uint32_t *ctr, uint32_t &target, volatile uint32_t *status) {
+    __syncthreads();
+    target += gridDim.x;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(ctr, 1u);
+        for (uint32_t it = 0; ld_acquire_gpu_u32(ctr) < target; ++it) {
+            if (it > SPIN_LIMIT) {
+                if (status) atomicOr((uint32_t *)status, ERR_TIMEOUT_GRID);
+                break;
+            }
+            if (it > 32) __nanosleep(32);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+}
+
+// Tile region of the fused kernel: the larger weight tile, and at least the group
+// phase's scratch (counts, offsets, warp sums: 2 * 1024 + 32 ints) and the route
+// phase's logits (1024 floats), which use the same bytes in earlier phases.
+__host__ __device__ inline size_t fused_tile_bytes(const MoeBatchParams &p) {
+    const size_t gu = (size_t)p.gu_rows * (p.rbg + p.rbu), dn = (size_t)p.dn_rows * p.rbd;
+    const size_t t = gu > dn ? gu : dn;
+    return t > 4 * (2 * 1024 + 32) ? t : 4 * (2 * 1024 + 32);
+}
+
+template <uint32_t GT, uint32_t UT, uint32_t DT>
+__global__ void __launch_bounds__(BT, 3) moe_batch_fused(MoeBatchParams p, int ep) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    __shared__ int s_next[2], s_ok;
+    const ItemSmem S = item_smem(sm, fused_tile_bytes(p));
+    init_tiles_bar(S.bar);  // visible after the first grid barrier's CTA barrier
+    uint32_t *ctr = p.work + 2;  // [0] barrier arrivals, [1] CTAs finished
+    uint32_t target = 0;
+    ItemState st{0u, 0};
+    // 1. route the tokens, or unpack the received slots
+    for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
+        if (ep) unpack_slot(p, t, &s_ok);
+        else route_one(p, t, reinterpret_cast<float *>(S.tile));
+        __syncthreads();  // shared scratch reused by the next token
+    }
+    grid_sync(ctr, target, p.status);
+    // 2. group (one CTA; it also zeroes the item counters)
+    if (blockIdx.x == 0) {
+        int *g = reinterpret_cast<int *>(S.tile);
+        group_body(p, g, g + 1024, g + 2048);
+    }
+    // the tile bytes held logits / group scratch (generic stores); the bulk copies
+    // that come next write them through the async proxy
+    fence_proxy_async_smem();
+    grid_sync(ctr, target, p.status);
+    // 3. gate/up; a CTA whose tile wait timed out does no more item work but still
+    //    takes part in every barrier
+    bool ok = gateup_items<GT, UT>(p, S, s_next, st);
+    grid_sync(ctr, target, p.status);
+    // 4. h -> q8_1
+    hquant_range(p, (blockIdx.x * BT + threadIdx.x) >> 5, gridDim.x * (BT / 32));
+    grid_sync(ctr, target, p.status);
+    // 5. down
+    if (ok) ok = down_items<DT>(p, S, s_next, st);
+    grid_sync(ctr, target, p.status);
+    // 6. combine, or the per-slot sums for the source ranks
+    if (ep) combine_slots_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
+    else combine_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
+    if (ep && p.ep_p2p) signal_peers(p, 1, 1, *p.ep_epoch + 1);
+    // 7. the last CTA out re-arms the barrier counters (every CTA has left its waits)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(&ctr[1], 1u);
+        if (prev == gridDim.x - 1) {
+            ctr[0] = 0u;
+            ctr[1] = 0u;
+        }
+    }
+}
+
 // Largest power-of-two row count in [8, 64] whose tile fits `budget` bytes.
 static int tile_rows(uint32_t bytes_per_row, int cap, size_t budget) {
     int r = cap;
@@ -646,43 +871,98 @@ static void set_smem(KernelT k, size_t bytes) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-// group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots)
-static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
-    // three CTAs per SM: weight tile + staged activations within ~70 KB each
+// Launches a grid-stride item kernel on min(worst-case items, resident CTAs) CTAs.
+template <typename KernelT>
+static void launch_items(KernelT k, int max_items, size_t smem, int sms, const MoeBatchParams &p,
+                         cudaStream_t st) {
+    // The limit is set on every launch: another layer shape may have lowered it.
+    set_smem(k, smem);
+    // resident CTAs per SM, asked once per (kernel, shared-memory size) and thread
+    struct Occ { const void *fn; size_t smem; int per_sm; };
+    thread_local Occ cache[16];
+    thread_local int ncache = 0;
+    int per_sm = 0;
+    for (int i = 0; i < ncache && i < 16 && !per_sm; ++i)
+        if (cache[i].fn == (const void *)k && cache[i].smem == smem) per_sm = cache[i].per_sm;
+    if (!per_sm) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, BT, smem) != cudaSuccess ||
+            per_sm < 1)
+            per_sm = 1;
+        cache[ncache % 16] = Occ{(const void *)k, smem, per_sm};
+        ++ncache;
+    }
+    const int resident = per_sm * (sms > 0 ? sms : 1);
+    const int grid = max_items < resident ? max_items : resident;
+    if (grid > 0) k<<<grid, BT, smem, st>>>(p);
+}
+
+// Tile heights: three CTAs per SM, each weight tile + staged activations within ~70 KB.
+static void plan_tiles(MoeBatchParams &p) {
     const size_t budget = 70 * 1024 - (size_t)ACT_TOKS * act_slot_bytes(p.H > p.F ? p.H : p.F);
     p.gu_rows = tile_rows(p.rbg + p.rbu, 16, budget);
     p.dn_rows = tile_rows(p.rbd, 64, budget);
+}
+
+// group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots)
+static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
+    plan_tiles(p);
     moe_batch_group<<<1, (p.n_experts + 31) / 32 * 32, 0, st>>>(p);
-    const int ggrid = max_groups * ((p.F + p.gu_rows - 1) / p.gu_rows);
-    const size_t gsm = (size_t)p.gu_rows * (p.rbg + p.rbu) + 16 + (size_t)ACT_TOKS * act_slot_bytes(p.H);
-    if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K) {
-        set_smem(moe_batch_gateup<T_Q4_K, T_Q4_K>, gsm);
-        moe_batch_gateup<T_Q4_K, T_Q4_K><<<ggrid, BT, gsm, st>>>(p);
-    } else if (p.gate_type == T_Q4_K) {
-        set_smem(moe_batch_gateup<T_Q4_K, T_Q6_K>, gsm);
-        moe_batch_gateup<T_Q4_K, T_Q6_K><<<ggrid, BT, gsm, st>>>(p);
-    } else if (p.up_type == T_Q4_K) {
-        set_smem(moe_batch_gateup<T_Q6_K, T_Q4_K>, gsm);
-        moe_batch_gateup<T_Q6_K, T_Q4_K><<<ggrid, BT, gsm, st>>>(p);
-    } else {
-        set_smem(moe_batch_gateup<T_Q6_K, T_Q6_K>, gsm);
-        moe_batch_gateup<T_Q6_K, T_Q6_K><<<ggrid, BT, gsm, st>>>(p);
-    }
+    const int gitems = max_groups * ((p.F + p.gu_rows - 1) / p.gu_rows);
+    const size_t gsm = item_smem_bytes((size_t)p.gu_rows * (p.rbg + p.rbu), p.H);
+    if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K)
+        launch_items(moe_batch_gateup<T_Q4_K, T_Q4_K>, gitems, gsm, p.sms, p, st);
+    else if (p.gate_type == T_Q4_K)
+        launch_items(moe_batch_gateup<T_Q4_K, T_Q6_K>, gitems, gsm, p.sms, p, st);
+    else if (p.up_type == T_Q4_K)
+        launch_items(moe_batch_gateup<T_Q6_K, T_Q4_K>, gitems, gsm, p.sms, p, st);
+    else
+        launch_items(moe_batch_gateup<T_Q6_K, T_Q6_K>, gitems, gsm, p.sms, p, st);
     if (p.tc_min > 0) launch_gateup_tc(p, max_groups, st);
     const int P = p.T * p.K;
     moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
-    const int dgrid = max_groups * ((p.H + p.dn_rows - 1) / p.dn_rows);
-    const size_t dsm = (size_t)p.dn_rows * p.rbd + 16 + (size_t)ACT_TOKS * act_slot_bytes(p.F);
-    if (p.down_type == T_Q6_K) {
-        set_smem(moe_batch_down<T_Q6_K>, dsm);
-        moe_batch_down<T_Q6_K><<<dgrid, BT, dsm, st>>>(p);
-    } else {
-        set_smem(moe_batch_down<T_Q4_K>, dsm);
-        moe_batch_down<T_Q4_K><<<dgrid, BT, dsm, st>>>(p);
+    const int ditems = max_groups * ((p.H + p.dn_rows - 1) / p.dn_rows);
+    const size_t dsm = item_smem_bytes((size_t)p.dn_rows * p.rbd, p.F);
+    if (p.down_type == T_Q6_K)
+        launch_items(moe_batch_down<T_Q6_K>, ditems, dsm, p.sms, p, st);
+    else
+        launch_items(moe_batch_down<T_Q4_K>, ditems, dsm, p.sms, p, st);
+}
+
+// The fused pipeline serves batches of at most FUSED_MAX_ROWS tokens (or received
+// slots) whose groups all stay below the tensor-core threshold, for Q4_K gate/up.
+// KATALI_CUDA_NO_FUSED=1 switches it off.
+constexpr int FUSED_MAX_ROWS = 16;
+static bool fused_wanted(const MoeBatchParams &p) {
+    const char *env = getenv("KATALI_CUDA_NO_FUSED");
+    const bool off = env && env[0] == '1';
+    return !off && p.T > 0 && p.T <= FUSED_MAX_ROWS && (p.tc_min == 0 || p.T < p.tc_min) &&
+           p.gate_type == T_Q4_K && p.up_type == T_Q4_K &&
+           (p.down_type == T_Q6_K || p.down_type == T_Q4_K) && p.n_experts <= 1024;
+}
+template <uint32_t DT>
+static cudaError_t launch_fused_t(MoeBatchParams &p, int ep, cudaStream_t st) {
+    auto k = moe_batch_fused<T_Q4_K, T_Q4_K, DT>;
+    const size_t smem = item_smem_bytes(fused_tile_bytes(p), p.H > p.F ? p.H : p.F);
+    set_smem(k, smem);
+    static thread_local size_t occ_smem = 0;
+    static thread_local int occ = 0;
+    if (occ_smem != smem) {  // co-resident CTAs per SM for this size (a cooperative grid)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, BT, smem) != cudaSuccess)
+            occ = 0;
+        occ_smem = smem;
     }
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    const int grid = occ * (p.sms > 0 ? p.sms : 1);
+    void *args[] = {(void *)&p, (void *)&ep};
+    return cudaLaunchCooperativeKernel((const void *)k, dim3(grid), dim3(BT), args, smem, st);
+}
+static cudaError_t launch_fused(MoeBatchParams &p, int ep, cudaStream_t st) {
+    plan_tiles(p);
+    return p.down_type == T_Q6_K ? launch_fused_t<T_Q6_K>(p, ep, st) : launch_fused_t<T_Q4_K>(p, ep, st);
 }
 
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
+    if (fused_wanted(p)) return launch_fused(p, 0, st);
     const int P = p.T * p.K;
     moe_batch_route<<<p.T, BT, 0, st>>>(p);
     launch_experts(p, P < p.n_experts ? P : p.n_experts, st);
@@ -697,6 +977,7 @@ cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st) {
 
 cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st) {
     // p.T = ranks * Tmax received slots
+    if (fused_wanted(p)) return launch_fused(p, 1, st);
     const int P = p.T * p.K, local = p.n_experts / p.ep_ranks;
     moe_ep_unpack<<<p.T, BT, 0, st>>>(p);
     launch_experts(p, P < local ? P : local, st);
