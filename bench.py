@@ -97,12 +97,32 @@ REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_pow
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed region: NVML
+    read every ~2 ms from a thread (read-only queries), or nvidia-smi when NVML is not
+    importable. The GPU is looked up by its NVML index (CUDA_VISIBLE_DEVICES aware)."""
 
     def __init__(self, index: int):
-        self.index, self.rows, self.proc = index, [], None
+        self.index, self.rows, self.proc, self.nvml = index, [], None, None
+        self.stop = threading.Event()
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            try:
+                nv = torch.cuda._get_nvml_device_index(index)
+            except Exception:
+                nv = index
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(nv)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
 
     def __enter__(self):
+        if self.nvml is not None:
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,"
@@ -114,6 +134,17 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.rows.append([str(sm), str(self.max_mhz), hex(rs)])
+            except Exception:
+                return
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
@@ -121,6 +152,9 @@ class ClockSampler:
                 self.rows.append(parts)
 
     def __exit__(self, *a):
+        self.stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -144,7 +178,7 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(self.rows)}
+                "samples": len(self.rows), "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------

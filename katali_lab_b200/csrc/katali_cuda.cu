@@ -193,9 +193,8 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
         off += (bytes + 255) & ~(size_t)255;
         return ptr;
     };
-    // First, at an offset that does not depend on T: the group count and the counters
-    // that must keep their values from one call to the next (the fused pipeline's grid
-    // barrier is left zero by each launch, whatever the batch size of the next).
+    // First, at an offset that does not depend on T: the group count and the item
+    // counters (a call never reads what a call of another batch size left there).
     unsigned char *ng = take(32);
     unsigned char *ids = take(4 * P), *w = take(4 * P);
     unsigned char *xq = take(T * H), *xd = take(4 * T * H / 32), *xs32 = take(4 * T * H / 32),
@@ -556,10 +555,7 @@ static int grow_batch_scratch(KataliMoe *m, int T) {
         return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
     }
     m->bscratch_bytes = need;
-    // zero once: the fused pipeline's grid-barrier counters start from zero (each
-    // launch leaves them zero again)
-    e = cudaMemsetAsync(m->bscratch, 0, need, g_stream);
-    return e == cudaSuccess ? KATALI_OK : cuda_fail(e);
+    return KATALI_OK;
 }
 
 static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {

@@ -98,8 +98,7 @@ struct MoeBatchParams {
     float *xd;
     int *xs32, *xs16;
     int *grp_expert, *grp_off, *n_groups, *pair_src, *pos_of;
-    uint32_t *work;  // [0..1] item counters of the gate/up and down kernels (zeroed by the
-                     // group step); [2..3] the fused pipeline's grid barrier (left zero)
+    uint32_t *work;  // item counters of the gate/up and down kernels, zeroed by the group kernel
     float *h;
     int8_t *hq;
     float *hd;

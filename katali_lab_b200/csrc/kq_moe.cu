@@ -7,8 +7,8 @@
 //  1. Every CTA routes redundantly (warp 0: top-k over the router logits held
 //     in registers, deterministic ties) while the other warps stage x in
 //     shared memory with one vector load per thread.
-//  2. The CTA then requests ALL of its expert bytes at once with cp.async.bulk
-//     (TMA, no multicast) into shared memory, one copy per warp in turn: its
+//  2. Warp 0 then requests ALL of the CTA's expert bytes at once with cp.async.bulk
+//     (TMA, no multicast) into shared memory, one copy per lane: its
 //     phase-A blocks (32 gate/up row pairs each, two 16-pair chunks with one
 //     mbarrier each) first, then its slice of the H down rows for each of the K
 //     selected experts (one mbarrier per expert). At the C2 shape (H 2048, F 512,
@@ -389,12 +389,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     __syncthreads();
     trace(p, 2);
 
-    // ---- 2. request every expert byte this CTA needs (lane 0 of every warp) ----
+    // ---- 2. request every expert byte this CTA needs (warp 0, one copy per lane) ----
     // Copy q: gate/up rows first (phase A waits for them), then each selected expert's
-    // down rows on its own barrier, decoded as they arrive. Copy q is issued by warp
-    // q % 16, so the copies leave the SM without queueing behind one issuing thread;
-    // a copy may complete before warp 0 has armed its barrier (the transaction count
-    // goes negative until the expect-tx arrival), which the barrier allows.
+    // down rows on its own barrier, decoded as they arrive. One warp keeps that order
+    // (copies issued from every warp interleave and delay the first gate/up chunk).
     const int nchunk = nbA * NCH;
     const uint32_t per = nrB * rbd;
     const int ncopy = 2 * nchunk + (nrB ? K : 0);
@@ -421,13 +419,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
         if (nrB && lane < K) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
         __syncwarp();
-        for (int q = 0; q < ncopy; q += MOE_WARPS)
-            if (lane == 0) issue(q);
+        for (int q = lane; q < ncopy; q += 32) issue(q);
         trace(p, 3);
         if (!p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
     } else if (warp > 0) {
-        for (int q = warp; q < ncopy; q += MOE_WARPS)
-            if (lane == 0) issue(q);
         for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
             const float v = xf[32 * g + lane];
             if (MODE == 0) {
@@ -448,28 +443,33 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     if (MODE == 0 && nbh == 8 && nbA > 0) xr = load_q4act(ax, lane);  // this lane's unit of x
     for (int a = 0; a < nbA; ++a) {
         const uint8_t *base = sa + (size_t)a * blk_bytes;
-        const int p0 = warp, p1 = warp + MOE_WARPS;  // two row pairs per warp
-        ok &= mbar_wait_warp(&bars[a * NCH + p0 / HCH], 0);
-        if (a == 0) trace(p, 4);
-        ok &= mbar_wait_warp(&bars[a * NCH + p1 / HCH], 0);
-        if (a == 0) trace(p, 12);
+        const int p0 = warp, p1 = warp + MOE_WARPS;  // two row pairs per warp, one per chunk
         const uint8_t *g0 = base + (size_t)p0 * rbg, *g1 = base + (size_t)p1 * rbg;
         const uint8_t *u0 = base + (size_t)HB * rbg + (size_t)p0 * rbu;
         const uint8_t *u1 = base + (size_t)HB * rbg + (size_t)p1 * rbu;
         double pg0, pu0, pg1, pu1;
+        // pair p0 (first chunk) is computed while the second chunk is still arriving
+        ok &= mbar_wait_warp(&bars[a * NCH + p0 / HCH], 0);
+        if (a == 0) trace(p, 4);
         if (MODE == 0 && nbh == 8) {
             pg0 = q4k_q8_unit_r(g0, lane, xr);
             pu0 = q4k_q8_unit_r(u0, lane, xr);
-            pg1 = q4k_q8_unit_r(g1, lane, xr);
-            pu1 = q4k_q8_unit_r(u1, lane, xr);
         } else if (MODE == 0) {
             pg0 = q4k_q8_partial(g0, nbh, ax, lane);
             pu0 = q4k_q8_partial(u0, nbh, ax, lane);
-            pg1 = q4k_q8_partial(g1, nbh, ax, lane);
-            pu1 = q4k_q8_partial(u1, nbh, ax, lane);
         } else {
             pg0 = q4k_f32_partial(g0, nbh, xf, xfs, lane);
             pu0 = q4k_f32_partial(u0, nbh, xf, xfs, lane);
+        }
+        ok &= mbar_wait_warp(&bars[a * NCH + p1 / HCH], 0);
+        if (a == 0) trace(p, 12);
+        if (MODE == 0 && nbh == 8) {
+            pg1 = q4k_q8_unit_r(g1, lane, xr);
+            pu1 = q4k_q8_unit_r(u1, lane, xr);
+        } else if (MODE == 0) {
+            pg1 = q4k_q8_partial(g1, nbh, ax, lane);
+            pu1 = q4k_q8_partial(u1, nbh, ax, lane);
+        } else {
             pg1 = q4k_f32_partial(g1, nbh, xf, xfs, lane);
             pu1 = q4k_f32_partial(u1, nbh, xf, xfs, lane);
         }

@@ -15,8 +15,6 @@
 //   hquant : h -> q8_1 per pair (split layout with 16-element sums)
 //   down   : item = (group, up to 64 output rows), scheduled the same way
 //   combine: y[t] = sum_k w[t][k] * part[pair(t,k)] in k order
-#include <cstdlib>
-
 #include "kq_device.cuh"
 #include "kq_launch.h"
 
@@ -765,100 +763,6 @@ __global__ void __launch_bounds__(BT) moe_ep_combine_tokens(MoeBatchParams p) {
     }
 }
 
-// ---------------------------------------------------------------------------
-// Fused small-batch pipeline: one cooperative launch runs route (or, expert-
-// parallel, the unpack of the received slots), group, gate/up, h quantisation,
-// down and the combine (or the per-slot sums returned to the sources), separated
-// by grid barriers. It runs the same per-item code as the separate kernels, so
-// the results are the same; it saves the launch gaps, which cost more than the
-// work when the batch is a few tokens (or the few slots an expert-parallel rank
-// receives at batch-1 decode).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-// Grid barrier on a counter that only grows within a launch: the n-th barrier waits
-// for n * gridDim.x arrivals. Bounded spin: on timeout the status gets
-// ERR_TIMEOUT_GRID and the CTA carries on (the call then reports the timeout).
-__device__ void grid_sync(uint32_t *ctr, uint32_t &target, volatile uint32_t *status) {
-    __syncthreads();
-    target += gridDim.x;
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
-        for (uint32_t it = 0; ld_acquire_gpu_u32(ctr) < target; ++it) {
-            if (it > SPIN_LIMIT) {
-                if (status) atomicOr((uint32_t *)status, ERR_TIMEOUT_GRID);
-                break;
-            }
-            if (it > 32) __nanosleep(32);
-        }
-        __threadfence();
-    }
-    __syncthreads();
-}
-
-// Tile region of the fused kernel: the larger weight tile, and at least the group
-// phase's scratch (counts, offsets, warp sums: 2 * 1024 + 32 ints) and the route
-// phase's logits (1024 floats), which use the same bytes in earlier phases.
-__host__ __device__ inline size_t fused_tile_bytes(const MoeBatchParams &p) {
-    const size_t gu = (size_t)p.gu_rows * (p.rbg + p.rbu), dn = (size_t)p.dn_rows * p.rbd;
-    const size_t t = gu > dn ? gu : dn;
-    return t > 4 * (2 * 1024 + 32) ? t : 4 * (2 * 1024 + 32);
-}
-
-template <uint32_t GT, uint32_t UT, uint32_t DT>
-__global__ void __launch_bounds__(BT, 3) moe_batch_fused(MoeBatchParams p, int ep) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    __shared__ int s_next[2], s_ok;
-    const ItemSmem S = item_smem(sm, fused_tile_bytes(p));
-    init_tiles_bar(S.bar);  // visible after the first grid barrier's CTA barrier
-    uint32_t *ctr = p.work + 2;  // [0] barrier arrivals, [1] CTAs finished
-    uint32_t target = 0;
-    ItemState st{0u, 0};
-    // 1. route the tokens, or unpack the received slots
-    for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
-        if (ep) unpack_slot(p, t, &s_ok);
-        else route_one(p, t, reinterpret_cast<float *>(S.tile));
-        __syncthreads();  // shared scratch reused by the next token
-    }
-    grid_sync(ctr, target, p.status);
-    // 2. group (one CTA; it also zeroes the item counters)
-    if (blockIdx.x == 0) {
-        int *g = reinterpret_cast<int *>(S.tile);
-        group_body(p, g, g + 1024, g + 2048);
-    }
-    // the tile bytes held logits / group scratch (generic stores); the bulk copies
-    // that come next write them through the async proxy
-    fence_proxy_async_smem();
-    grid_sync(ctr, target, p.status);
-    // 3. gate/up; a CTA whose tile wait timed out does no more item work but still
-    //    takes part in every barrier
-    bool ok = gateup_items<GT, UT>(p, S, s_next, st);
-    grid_sync(ctr, target, p.status);
-    // 4. h -> q8_1
-    hquant_range(p, (blockIdx.x * BT + threadIdx.x) >> 5, gridDim.x * (BT / 32));
-    grid_sync(ctr, target, p.status);
-    // 5. down
-    if (ok) ok = down_items<DT>(p, S, s_next, st);
-    grid_sync(ctr, target, p.status);
-    // 6. combine, or the per-slot sums for the source ranks
-    if (ep) combine_slots_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
-    else combine_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
-    if (ep && p.ep_p2p) signal_peers(p, 1, 1, *p.ep_epoch + 1);
-    // 7. the last CTA out re-arms the barrier counters (every CTA has left its waits)
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t prev = atomicAdd(&ctr[1], 1u);
-        if (prev == gridDim.x - 1) {
-            ctr[0] = 0u;
-            ctr[1] = 0u;
-        }
-    }
-}
-
 // Largest power-of-two row count in [8, 64] whose tile fits `budget` bytes.
 static int tile_rows(uint32_t bytes_per_row, int cap, size_t budget) {
     int r = cap;
@@ -928,41 +832,7 @@ static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
         launch_items(moe_batch_down<T_Q4_K>, ditems, dsm, p.sms, p, st);
 }
 
-// The fused pipeline serves batches of at most FUSED_MAX_ROWS tokens (or received
-// slots) whose groups all stay below the tensor-core threshold, for Q4_K gate/up.
-// KATALI_CUDA_NO_FUSED=1 switches it off.
-constexpr int FUSED_MAX_ROWS = 16;
-static bool fused_wanted(const MoeBatchParams &p) {
-    const char *env = getenv("KATALI_CUDA_NO_FUSED");
-    const bool off = env && env[0] == '1';
-    return !off && p.T > 0 && p.T <= FUSED_MAX_ROWS && (p.tc_min == 0 || p.T < p.tc_min) &&
-           p.gate_type == T_Q4_K && p.up_type == T_Q4_K &&
-           (p.down_type == T_Q6_K || p.down_type == T_Q4_K) && p.n_experts <= 1024;
-}
-template <uint32_t DT>
-static cudaError_t launch_fused_t(MoeBatchParams &p, int ep, cudaStream_t st) {
-    auto k = moe_batch_fused<T_Q4_K, T_Q4_K, DT>;
-    const size_t smem = item_smem_bytes(fused_tile_bytes(p), p.H > p.F ? p.H : p.F);
-    set_smem(k, smem);
-    static thread_local size_t occ_smem = 0;
-    static thread_local int occ = 0;
-    if (occ_smem != smem) {  // co-resident CTAs per SM for this size (a cooperative grid)
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, BT, smem) != cudaSuccess)
-            occ = 0;
-        occ_smem = smem;
-    }
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    const int grid = occ * (p.sms > 0 ? p.sms : 1);
-    void *args[] = {(void *)&p, (void *)&ep};
-    return cudaLaunchCooperativeKernel((const void *)k, dim3(grid), dim3(BT), args, smem, st);
-}
-static cudaError_t launch_fused(MoeBatchParams &p, int ep, cudaStream_t st) {
-    plan_tiles(p);
-    return p.down_type == T_Q6_K ? launch_fused_t<T_Q6_K>(p, ep, st) : launch_fused_t<T_Q4_K>(p, ep, st);
-}
-
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
-    if (fused_wanted(p)) return launch_fused(p, 0, st);
     const int P = p.T * p.K;
     moe_batch_route<<<p.T, BT, 0, st>>>(p);
     launch_experts(p, P < p.n_experts ? P : p.n_experts, st);
@@ -977,7 +847,6 @@ cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st) {
 
 cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st) {
     // p.T = ranks * Tmax received slots
-    if (fused_wanted(p)) return launch_fused(p, 1, st);
     const int P = p.T * p.K, local = p.n_experts / p.ep_ranks;
     moe_ep_unpack<<<p.T, BT, 0, st>>>(p);
     launch_experts(p, P < local ? P : local, st);

@@ -3,8 +3,7 @@
 Bars, per token of a batch: routing identical to the batch-1 kernel, output within
 rel_L2 <= 1e-5 of the q8_1 restatement (port.moe_layer, mode 0) and at least 99.9 %
 of elements bit-equal to it; the same bars against the batch-1 kernel's output for
-the same token. Batches of up to 15 tokens run as one fused cooperative launch,
-bit-identical to the six-launch pipeline. Groups of >= 16 tokens run gate/up on the tensor cores (tcgen05
+the same token. Groups of >= 16 tokens run gate/up on the tensor cores (tcgen05
 int8 MMA) with fp32 block terms; their bar is TC_TOL below. Edge cases: one token,
 every token on the same experts, groups of 16 / 33 / 100 tokens, batch sizes that
 grow and shrink between calls, no-norm routing, 1024 experts with top-16, and the
@@ -110,27 +109,6 @@ def test_batch_ragged_sequence(c3_layer, port):
         Y = run_batch(c3_layer, X, L)
         idx = sorted({0, T // 2, T - 1})
         check_tokens(c3_layer, port, X[idx], L[idx], Y[idx], against_batch1=False)
-
-
-@pytest.mark.parametrize("T", [1, 6, 15])
-def test_batch_fused_matches_pipeline(c3_layer, monkeypatch, T):
-    """Batches of up to 15 tokens run as one cooperative launch (route, group, gate/up,
-    h quantisation, down, combine between grid barriers); the same per-item code as
-    the six-launch pipeline, so the outputs are bit-identical."""
-    X, L = batch_inputs(650 + T, T, 2048, 64)
-    fused = run_batch(c3_layer, X, L)
-    monkeypatch.setenv("KATALI_CUDA_NO_FUSED", "1")
-    staged = run_batch(c3_layer, X, L)
-    assert np.array_equal(fused, staged)
-
-
-def test_batch_fused_1024_experts(plugin, monkeypatch):
-    """The fused launch groups 1024 experts with 256 threads (four experts each)."""
-    lay = DevLayer(plugin, 1024, 256, 256, 16, seed=34)
-    X, L = batch_inputs(660, 7, 256, 1024)
-    fused = run_batch(lay, X, L)
-    monkeypatch.setenv("KATALI_CUDA_NO_FUSED", "1")
-    assert np.array_equal(fused, run_batch(lay, X, L))
 
 
 def test_batch_deterministic(c3_layer):
