@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "katali_cuda.h"
@@ -445,7 +446,11 @@ int katali_cuda_moe_create(const KataliMoeDesc *d, KataliMoe **out) {
     }
     // +1 pointer: the kernel copies the table in 16-byte pairs
     cudaError_t e = cudaMalloc((void **)&m->d_table, (m->table.size() + 1) * sizeof(void *));
-    if (e == cudaSuccess) e = cudaMalloc((void **)&m->hbuf, sizeof(float) * d->top_k * d->ffn);
+    // h scratch: top_k * ffn floats (fp32 mode), or the q8_1 records (48 B per 32 values) of up
+    // to MOE_EP_MAX_SLOTS * top_k expert-parallel pairs
+    const size_t hbuf_bytes = std::max(sizeof(float) * d->top_k * d->ffn,
+                                       (size_t)kq::MOE_EP_MAX_SLOTS * d->top_k * d->ffn / 32 * 48);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&m->hbuf, hbuf_bytes);
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->sync, 16);
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->dbg_ids, 4 * kq::MOE_MAX_K);
     if (e == cudaSuccess) e = cudaMalloc((void **)&m->dbg_w, 4 * kq::MOE_MAX_K);
@@ -609,6 +614,19 @@ int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
 static uint32_t ep_hdr_bytes(int K) { return (uint32_t)(16 + 8 * K + 15) & ~15u; }
 static uint32_t ep_slot_bytes(const kq::MoeParams &pl) { return ep_hdr_bytes(pl.K) + pl.H / 32 * 36; }
 
+// The experts stage runs in the fused kernel (pairs mode) for up to MOE_EP_MAX_SLOTS
+// received slots when the layer has a q8_1 fused plan with decoded Q6_K down rows and
+// one phase-A block per CTA per round (K * F / 32 <= grid); KATALI_CUDA_NO_EP_FUSED=1
+// keeps the ragged-batch pipeline.
+static bool ep_fused_ok(const KataliMoe *m, int slots) {
+    const char *off = getenv("KATALI_CUDA_NO_EP_FUSED");
+    if (off && off[0] == '1') return false;
+    const kq::MoeParams &pl = m->plan[KATALI_MOE_Q8_1];
+    const bool pow2_f = pl.F == 256 || pl.F == 512 || pl.F == 1024 || pl.F == 2048;
+    return m->plan_ok[KATALI_MOE_Q8_1] && slots <= kq::MOE_EP_MAX_SLOTS && pl.dec_enabled &&
+           pl.down_type == KATALI_TYPE_Q6_K && pow2_f && pl.K * pl.F / 32 <= m->grid;
+}
+
 static int ep_check(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens) {
     if (!m || n_ranks == 0 || n_ranks > 64 || max_tokens == 0 ||
         (uint64_t)n_ranks * max_tokens > KATALI_MOE_BATCH_MAX_TOKENS)
@@ -684,6 +702,28 @@ int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_t
     if (rank >= n_ranks || (!pp && (!recv || !ret || !aligned16(recv) || !aligned16(ret))))
         return KATALI_ERR_BAD_ARG;
     const int T = (int)(n_ranks * max_tokens);
+    if (!pp && ep_fused_ok(m, T)) {  // the fused kernel over the received pairs
+        kq::MoeParams p = m->plan[KATALI_MOE_Q8_1];
+        p.experts = m->d_table;
+        p.x = nullptr;
+        p.logits = nullptr;
+        p.ids = nullptr;
+        p.w = nullptr;
+        p.y = nullptr;
+        p.hbuf = m->hbuf;
+        p.sync = m->sync;
+        p.status = g_status_dev;
+        p.dbg_ids = m->dbg_ids;
+        p.dbg_w = m->dbg_w;
+        p.route_only = 0;
+        p.trace = nullptr;
+        p.ep_recv = (const uint8_t *)recv;
+        p.ep_ret = (double *)ret;
+        p.ep_slots = (uint32_t)T;
+        p.ep_slot_bytes = ep_slot_bytes(m->plan[0]);
+        p.ep_hdr_bytes = ep_hdr_bytes(m->plan[0].K);
+        return finish(kq::launch_moe_ep(p, m->grid, g_stream));
+    }
     s = grow_batch_scratch(m, T);
     if (s) return s;
     kq::MoeBatchParams b = batch_params(m, T);

@@ -52,6 +52,10 @@ cudaError_t launch_row_isums(uint32_t type, const void *w, uint64_t rows, uint64
                              cudaStream_t st);
 
 constexpr int MOE_MAX_K = 16;
+// Expert-parallel experts stage in the fused kernel: at most this many received slots
+// (pairs processed in rounds of K), else the ragged-batch pipeline.
+constexpr int MOE_EP_MAX_SLOTS = 16;
+constexpr int MOE_EP_MAX_PAIRS = MOE_EP_MAX_SLOTS * MOE_MAX_K;
 constexpr int MOE_MAX_CHUNKS = 64;
 constexpr int TRACE_SLOTS = 20;  // 16 %globaltimer slots + clock64 at start/end  // %globaltimer samples per CTA when tracing
 
@@ -81,9 +85,18 @@ struct MoeParams {
     uint32_t dec_off, dec_row_bytes;  // decoded int8 down rows (q8_1 mode, Q6_K)
     uint32_t sdot_off;                // phase-B per-expert row dots [K][rows]
     int dec_enabled;
+    // Expert-parallel experts stage (launch_moe_ep): the received slots in (the slot
+    // layout of katali_cuda_moe_ep_dispatch), per-slot weighted sums out (doubles).
+    // hbuf then holds ep_slots * K * F / 32 q8_1 records of h.
+    const uint8_t *ep_recv;
+    double *ep_ret;
+    uint32_t ep_slots, ep_slot_bytes, ep_hdr_bytes;
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
+// The experts stage of an expert-parallel layer for at most MOE_EP_MAX_SLOTS received
+// slots (q8_1, Q6_K down, F a power of two in [256, 2048], K * F / 32 <= grid).
+cudaError_t launch_moe_ep(MoeParams &p, int grid, cudaStream_t st);
 
 // Ragged multi-token MoE layer (q8_1 activations); scratch owned by the layer object.
 struct MoeBatchParams {

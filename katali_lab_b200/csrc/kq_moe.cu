@@ -311,10 +311,53 @@ __device__ __forceinline__ double dec_q8_unit(const uint8_t *drow, int F, int u,
            ((double)d * (double)a.d[2 * u + 1]) * (double)I1;
 }
 
+// Expert-parallel pairs of the received slots, in slot then k order (warp 0): a slot
+// header holds n_owned, t, pad[2], ids[K] (global expert id, or -1 when another rank
+// owns it), w[K]; slots with n_owned == 0 carry no pairs.
+__device__ void ep_pairs(const MoeParams &p, int K, int lane, int *pslot, int *pid, float *pw, int *np) {
+    int base = 0;
+    for (int s0 = 0; s0 < (int)p.ep_slots; s0 += 32) {
+        const int s = s0 + lane;
+        const uint8_t *slot = p.ep_recv + (size_t)s * p.ep_slot_bytes;
+        const int *ids = reinterpret_cast<const int *>(slot + 16);
+        const float *ws = reinterpret_cast<const float *>(slot + 16 + 4 * K);
+        const bool live = s < (int)p.ep_slots && __ldcg(reinterpret_cast<const int *>(slot)) > 0;
+        int cnt = 0;
+        if (live)
+            for (int k = 0; k < K; ++k) cnt += __ldcg(ids + k) >= 0;
+        int incl = cnt;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(KQ_FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int off = base + incl - cnt;
+        if (live)
+            for (int k = 0; k < K; ++k) {
+                const int id = __ldcg(ids + k);
+                if (id >= 0) {
+                    pslot[off] = s;
+                    pid[off] = id;
+                    pw[off] = __ldcg(ws + k);
+                    ++off;
+                }
+            }
+        base += __shfl_sync(KQ_FULL, incl, 31);
+    }
+    if (lane == 0) *np = base;
+    __syncwarp();
+}
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // SHAPE 1: the layer shape is compile-time (hidden 2048, FFN 512, top-8, Q4_K gate/up, Q6_K
 // down: C2 and its family), so shape-dependent branches and loop bounds fold away; SHAPE 0
 // reads every size from the parameters.
-template <int MODE, uint32_t DT, int SHAPE>
+// EP 1: the experts stage of an expert-parallel layer. The (slot, k) pairs this rank owns
+// come from the received slots instead of routing, each pair with its own token's q8_1 x;
+// they run in rounds of K pairs (phase A, grid barrier, phase B per round) and each slot's
+// weighted sum over its pairs, in k order, accumulates in double into p.ep_ret.
+template <int MODE, uint32_t DT, int SHAPE, int EP>
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_constant__ MoeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -334,10 +377,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *s_h = s_w + MOE_MAX_K;                                   // MAX_ABLK * HB floats
     uint8_t *s_rec = reinterpret_cast<uint8_t *>(s_h + MAX_ABLK * HB);  // MAX_ABLK * REC_BYTES
     float *s_logits = reinterpret_cast<float *>(s_rec + MAX_ABLK * REC_BYTES);
+    // expert-parallel pairs: slot, expert, weight of each owned pair; the round's slots
+    int *s_pslot = reinterpret_cast<int *>(s_logits + p.n_experts);
+    int *s_pid = s_pslot + MOE_EP_MAX_PAIRS;
+    float *s_pw = reinterpret_cast<float *>(s_pid + MOE_EP_MAX_PAIRS);
+    int *s_slotr = reinterpret_cast<int *>(s_pw + MOE_EP_MAX_PAIRS);
+    int *s_np = s_slotr + MOE_MAX_K;
 
-    const uint32_t BA = (uint32_t)K * F / HB;  // phase-A blocks
-    const uint32_t b0 = BA * c / G, b1 = BA * (c + 1) / G;  // 32-bit: BA * G < 2^32
-    const int nbA = (int)(b1 - b0);
     const uint32_t Q = (uint32_t)H / p.rg;  // phase-B row groups (16-byte aligned copies)
     const uint32_t q0 = Q * c / G, q1 = Q * (c + 1) / G;
     const uint32_t rB0 = p.rg * q0, nrB = p.rg * (q1 - q0);
@@ -368,7 +414,19 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     int *xs32 = reinterpret_cast<int *>(xd + H / 32);
     int *xs16 = xs32 + H / 32;
     float *xfs = reinterpret_cast<float *>(act + 4 * H);  // fp32 mode: per-32 sums
-    if (warp == 0) {
+    int npairs = K, nrounds = 1;
+    if constexpr (EP) {
+        if (warp == 0) {
+            ep_pairs(p, K, lane, s_pslot, s_pid, s_pw, s_np);
+        } else {
+            const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
+            for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
+                reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
+        }
+        __syncthreads();
+        npairs = *s_np;
+        nrounds = (npairs + K - 1) / K;
+    } else if (warp == 0) {
         if (p.ids) {
             if (lane < K) {
                 s_ids[lane] = p.ids[lane];
@@ -386,8 +444,34 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
             reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
     }
-    __syncthreads();
+    if constexpr (!EP) __syncthreads();
     trace(p, 2);
+
+    for (int rd = 0; rd < nrounds; ++rd) {
+    // pairs of this round: K (one token's experts), or expert-parallel pairs [rd K, rd K + KR)
+    const int KR = EP ? min(K, npairs - rd * K) : K;
+    if constexpr (EP) {
+        if (rd > 0) {  // every wait of the previous round has returned: re-arm the barriers
+            __syncthreads();
+            if (tid == 32) {
+                for (int i = 0; i < NBARS; ++i) {
+                    mbar_inval(&bars[i]);
+                    mbar_init(&bars[i], 1);
+                }
+                fence_mbar_init();
+            }
+        }
+        if (tid < KR) {
+            s_ids[tid] = s_pid[rd * K + tid];
+            s_w[tid] = s_pw[rd * K + tid];
+            s_slotr[tid] = s_pslot[rd * K + tid];
+        }
+        __syncthreads();
+    }
+    const uint32_t BA = (uint32_t)KR * F / HB;  // phase-A blocks of this round
+    const uint32_t b0 = BA * c / G, b1 = BA * (c + 1) / G;  // 32-bit: BA * G < 2^32
+    const int nbA = (int)(b1 - b0);
+    const uint32_t hb0 = EP ? (uint32_t)(rd * K) * (F / HB) : 0u;  // first h record of the round
 
     // ---- 2. request every expert byte this CTA needs (warp 0, one copy per lane) ----
     // Copy q: gate/up rows first (phase A waits for them), then each selected expert's
@@ -395,7 +479,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     // (copies issued from every warp interleave and delay the first gate/up chunk).
     const int nchunk = nbA * NCH;
     const uint32_t per = nrB * rbd;
-    const int ncopy = 2 * nchunk + (nrB ? K : 0);
+    const int ncopy = 2 * nchunk + (nrB ? KR : 0);
     auto issue = [&](int q) {
         const uint64_t pol = l2_evict_first_policy();
         if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
@@ -417,11 +501,30 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     };
     if (warp == 0) {
         if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
-        if (nrB && lane < K) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
+        if (nrB && lane < KR) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
         __syncwarp();
         for (int q = lane; q < ncopy; q += 32) issue(q);
         trace(p, 3);
-        if (!p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+        if (!EP && !p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+    } else if (EP) {
+        // x of this CTA's phase-A block: its pair's token, from the slot's q8_1 row
+        if (nbA > 0) {
+            const int kb = (int)(b0 / (F / HB));
+            const uint8_t *row = p.ep_recv + (size_t)s_slotr[kb] * p.ep_slot_bytes + p.ep_hdr_bytes;
+            for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
+                const uint8_t *blk = row + 36 * g;
+                const int qi = (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
+                const int sum = __reduce_add_sync(KQ_FULL, qi);
+                const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+                xq[32 * g + lane] = (int8_t)qi;
+                if (lane == 0) {
+                    xd[g] = h2f(__ldcg(reinterpret_cast<const unsigned short *>(blk)));
+                    xs32[g] = sum;
+                    xs16[2 * g] = sum_lo;
+                    xs16[2 * g + 1] = sum - sum_lo;
+                }
+            }
+        }
     } else if (warp > 0) {
         for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
             const float v = xf[32 * g + lane];
@@ -499,7 +602,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             quant_block_q8(v, lane, reinterpret_cast<int8_t *>(r), md, ms, ms + 1, nullptr);
             __syncwarp();
             if (lane < 3)
-                reinterpret_cast<uint4 *>(p.hbuf)[3 * blk + lane] =
+                reinterpret_cast<uint4 *>(p.hbuf)[3 * (hb0 + blk) + lane] =
                     reinterpret_cast<const uint4 *>(r)[lane];
         } else {
             p.hbuf[HB * blk + lane] = v;
@@ -523,7 +626,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         trace(p, 13);
         const int upr = F / 64;  // units per row
         const int per_k = (int)nrB * upr;
-        const int total = K * per_k;
+        const int total = KR * per_k;
         int kw = -1;  // the expert whose rows this thread has seen arrive
         for (int t = tid; t < total; t += MOE_THREADS) {
             const int kk = t / per_k, rem = t - kk * per_k, rr = rem / upr, u = rem - rr * upr;
@@ -544,7 +647,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     trace(p, 14);
     if (tid == 0) {
         uint32_t it = 0;
-        while (ld_acquire_gpu(&p.sync[0]) < G) {
+        while (ld_acquire_gpu(&p.sync[0]) < (uint32_t)(rd + 1) * G) {
             if (++it > SPIN_LIMIT) {
                 *p.status |= ERR_TIMEOUT_GRID;
                 break;
@@ -567,7 +670,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         const int nun = F / 64;
         for (int t = tid; t < 3 * nrec; t += MOE_THREADS) {
             const int r = t / 3, part = t - 3 * r;
-            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.hbuf) + t);
+            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(p.hbuf) + 3 * hb0 + t);
             if (part < 2) {  // elements [32 jb + 16 part, +16) of expert kk's h
                 const int kk = r / (F / HB), jb = r - kk * (F / HB);
                 const int off = xmaj ? 16 * ((2 * (jb & 1) + part) * nun + (jb >> 1))
@@ -595,7 +698,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     if (nrB) {
         bool down_in = true;  // the decode loop has already waited in predecode mode
         if (!predecode)
-            for (int kk = 0; kk < K; ++kk) down_in &= mbar_wait_warp(&bars[DBAR + kk], 0);
+            for (int kk = 0; kk < KR; ++kk) down_in &= mbar_wait_warp(&bars[DBAR + kk], 0);
         if (!down_in) {
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
         } else if (xmaj) {
@@ -606,11 +709,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             // weighted sum over experts runs in expert order.
             int kp2 = 1;
             while (kp2 < K) kp2 <<= 1;
-            const int wpe = MOE_WARPS / kp2, k = warp / wpe, wsub = warp % wpe;
+            const int wpe = MOE_WARPS / kp2, k = warp / wpe, wsub = warp % wpe;  // k >= KR: idle
             const int nunits = F / 64, rpl = 32 / nunits;
             const int u = lane % nunits, rs = lane / nunits;
             float *s_dot = reinterpret_cast<float *>(smem + p.sdot_off);  // [K][nrB]
-            if (k < K) {
+            if (k < KR) {
                 const int8_t *hk = hq + (size_t)k * (F + 16) + 16 * u;  // chunk-major
                 const uint4 a0 = *reinterpret_cast<const uint4 *>(hk);
                 const uint4 a1 = *reinterpret_cast<const uint4 *>(hk + 16 * nunits);
@@ -651,9 +754,27 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             if (warp == 0) trace(p, 15);
             __syncthreads();
             for (uint32_t r = tid; r < nrB; r += MOE_THREADS) {
-                double acc = 0.0;
-                for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
-                p.y[rB0 + r] = (float)acc;
+                if constexpr (EP) {
+                    // runs of one slot's pairs, in k order; a run that began in the previous
+                    // round continues from that round's sum (same thread, same row)
+                    int cur = -1;
+                    double acc = 0.0;
+                    for (int kk = 0; kk < KR; ++kk) {
+                        const int sl = s_slotr[kk];
+                        if (sl != cur) {
+                            if (cur >= 0) p.ep_ret[(size_t)cur * H + rB0 + r] = acc;
+                            const bool cont = kk == 0 && rd > 0 && s_pslot[rd * K - 1] == sl;
+                            acc = cont ? p.ep_ret[(size_t)sl * H + rB0 + r] : 0.0;
+                            cur = sl;
+                        }
+                        acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
+                    }
+                    if (cur >= 0) p.ep_ret[(size_t)cur * H + rB0 + r] = acc;
+                } else {
+                    double acc = 0.0;
+                    for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
+                    p.y[rB0 + r] = (float)acc;
+                }
             }
         } else {
             trace(p, 7);
@@ -684,10 +805,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 for (int o = 1; o < lpe; o <<= 1) part += __shfl_xor_sync(KQ_FULL, part, o);
                 double t = k < K ? wk * (double)(float)part : 0.0;
                 for (int o = lpe; o < 32; o <<= 1) t += __shfl_xor_sync(KQ_FULL, t, o);
-                if (lane == 0) p.y[rB0 + rr] = (float)t;
+                if (!EP && lane == 0) p.y[rB0 + rr] = (float)t;
             }
         }
     }
+    }  // rounds
     trace(p, 8);
 
     // ---- 7. the last CTA out re-arms the barrier counters --------------------
@@ -728,7 +850,7 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     p.misc_off = al128(p.hact_off + hact);
     const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * BAR_SLOTS +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
-                          4 * (uint32_t)p.n_experts;
+                          4 * (uint32_t)p.n_experts + 12 * MOE_EP_MAX_PAIRS + 4 * MOE_MAX_K + 16;
     p.sdot_off = al128(p.misc_off + misc);
     p.smem_bytes = al128(p.sdot_off + 4 * (uint32_t)p.K * rg * qpc);
     // Decoded int8 down rows (Q6_K, q8_1 mode): reuse the phase-A staging area
@@ -750,11 +872,11 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     return p.smem_bytes <= (uint32_t)max_smem ? 0 : -1;
 }
 
-template <int MODE, uint32_t DT, int SHAPE>
+template <int MODE, uint32_t DT, int SHAPE, int EP = 0>
 static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     static uint32_t set_bytes = 0;  // raise the smem limit once per size, before any capture
     if (p.smem_bytes > set_bytes) {
-        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE>,
+        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE, EP>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)p.smem_bytes);
         if (e != cudaSuccess) return e;
@@ -770,7 +892,7 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     attr[0].val.cooperative = p.route_only ? 0 : 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE>, p);
+    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
 }
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
@@ -783,6 +905,14 @@ cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
     }
     return p.down_type == T_Q6_K ? launch_t<1, T_Q6_K, 0>(p, grid, st)
                                  : launch_t<1, T_Q4_K, 0>(p, grid, st);
+}
+
+cudaError_t launch_moe_ep(MoeParams &p, int grid, cudaStream_t st) {
+    if (p.mode != 0 || p.down_type != T_Q6_K || !p.dec_enabled || p.ep_slots > MOE_EP_MAX_SLOTS)
+        return cudaErrorInvalidValue;
+    const bool c2 = p.H == 2048 && p.F == 512 && p.K == 8 && p.gate_type == T_Q4_K &&
+                    p.up_type == T_Q4_K;
+    return c2 ? launch_t<0, T_Q6_K, 1, 1>(p, grid, st) : launch_t<0, T_Q6_K, 0, 1>(p, grid, st);
 }
 
 }  // namespace kq

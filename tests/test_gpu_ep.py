@@ -114,6 +114,41 @@ def test_ep_experts_match_oracle(plugin, port, full):
         e.close()
 
 
+@pytest.mark.parametrize("G,Ts", [(8, [1] * 8), (2, [5, 3])])
+def test_ep_experts_fused_matches_pipeline(plugin, full, monkeypatch, G, Ts):
+    """Up to 16 received slots run the experts stage in the fused MoE kernel (pairs of
+    the slots in rounds of K, one token's x per pair); the same sums as the ragged-batch
+    pipeline within rel_L2 <= 1e-5 per slot and >= 99.9 % bit-equal. (2, [5, 3]) gives
+    each rank ~30 pairs: four rounds, with slots whose pairs span two rounds."""
+    plugin.set_stream(torch.cuda.current_stream())  # the exchange runs on torch's stream
+    tmax = max(Ts)
+    eps = ep_layers(plugin, full, G, tmax)
+    sends = []
+    for r, T in enumerate(Ts):
+        X, L = inputs(95 + r, T)
+        sends.append(eps[r].dispatch(T, dev(X), dev(L)).clone())
+    recvs = exchange(sends, G)
+    sb = eps[0].slot_bytes
+    for r in sorted({0, G // 2, G - 1}):
+        monkeypatch.delenv("KATALI_CUDA_NO_EP_FUSED", raising=False)
+        fused = host(eps[r].experts(recvs[r])).copy()
+        monkeypatch.setenv("KATALI_CUDA_NO_EP_FUSED", "1")
+        staged = host(eps[r].experts(recvs[r])).copy()
+        slots = host(recvs[r]).reshape(G * tmax, sb)
+        n_checked = 0
+        for s_ in range(G * tmax):
+            ids = slots[s_, 16:16 + 4 * K].view(np.int32)
+            if slots[s_, :4].view(np.int32)[0] > 0 and (ids >= 0).any():
+                a, b = fused[s_ * H:(s_ + 1) * H], staged[s_ * H:(s_ + 1) * H]
+                assert rel_l2(a, b) <= 1e-5, (r, s_)
+                assert np.mean(a == b) >= 0.999, (r, s_)
+                n_checked += 1
+        assert n_checked > 0
+    for e in eps:
+        e.close()
+    plugin.set_stream(None)
+
+
 def test_ep_arg_checks(plugin, full):
     from katali_lab_b200 import KataliError
     ep = ep_layers(plugin, full, 2, 4)[0]
