@@ -61,8 +61,10 @@ def parse():
     ap.add_argument("--hot", type=int, default=0,
                     help="c3: every token routed among experts 0..hot-1 (groups of many tokens)")
     ap.add_argument("--tmin", type=int, default=1, help="c3: smallest batch per call")
-    ap.add_argument("--p2p", action="store_true",
-                    help="N > 1: exchange over NVLink peer memory inside the kernels instead of NCCL")
+    ap.add_argument("--nccl", action="store_true",
+                    help="N > 1: exchange with the plugin's NCCL communicator instead of over NVLink "
+                         "peer memory inside the kernels (the default)")
+    ap.add_argument("--p2p", action="store_true", help=argparse.SUPPRESS)  # the default; kept for old command lines
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent replicas instead of expert parallelism")
     ap.add_argument("--warm", action="store_true",
@@ -750,7 +752,7 @@ def run_ep(args, rank, world, local_rank):
     stores = [make_expert_store(plugin, per, H, F, seed=10_000 * l + rank) for l in range(L)]
     layers = [EpMoeLayer(plugin, E, H, F, K, st.pointers(), world, rank, tmax) for st in stores]
     comm = EpComm.from_process_group(plugin)
-    if args.p2p:
+    if not args.nccl:
         comm.use_peer_memory(True)
     # every rank's inputs from its seed, so every rank can count the job's distinct experts
     plans = [c3_plan(n, seed=3 + r, tmin=1 if ragged else 1, tmax=tmax) for r in range(world)]
@@ -835,8 +837,11 @@ def run_ep(args, rank, world, local_rank):
                                                       "C2 batch-1 decode", n=world, per=per,
                                                       tok="T ~ U{1..64} per call" if ragged
                                                       else "one per call",
-                                                      how="over NVLink peer memory inside the kernels"
-                                                      if args.p2p else "by the plugin's NCCL communicator "
+                                                      how=("over NVLink peer memory inside the kernels"
+                                                           + ("" if ragged else "; the whole layer "
+                                                              "(dispatch, experts, return, combine) in one "
+                                                              "launch per GPU"))
+                                                      if not args.nccl else "by the plugin's NCCL communicator "
                                                       "(grouped send/recv of fixed-capacity q8_1 slots)"),
                        "calls_per_step": n, "tokens_per_step_job": tok_all,
                        "distinct_experts_per_step": int(sum(distinct)),

@@ -734,6 +734,64 @@ int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_t
     return finish(kq::launch_moe_ep_experts(b, g_stream));
 }
 
+// The whole layer over peer memory in one launch (dispatch, experts in the fused kernel,
+// return, combine), when the exchange is small enough for it; KATALI_OK when it ran,
+// KATALI_ERR_UNSUPPORTED_SHAPE when the caller should run the three stages instead.
+int moe_ep_layer_fused(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                       const float *x, const float *router_logits, float *y, const EpPeer *pp,
+                       double *ret_scratch) {
+    int s = ep_check(m, n_ranks, max_tokens);
+    if (s) return s;
+    if (!pp || !ret_scratch || !ep_fused_ok(m, (int)(n_ranks * max_tokens)))
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    if (n_tokens > max_tokens) return KATALI_ERR_BAD_ARG;
+    if (n_tokens && (!x || !router_logits || !y || !aligned16(x))) return KATALI_ERR_BAD_ARG;
+    const uint32_t K = (uint32_t)m->plan[0].K;
+    if (max_tokens > m->ep_src_cap) {
+        cudaError_t e = cudaStreamSynchronize(g_stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+        cudaFree(m->ep_src_ids);
+        m->ep_src_cap = 0;
+        e = cudaMalloc((void **)&m->ep_src_ids, 4ull * K * max_tokens);
+        if (e != cudaSuccess) {
+            m->ep_src_ids = nullptr;
+            return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
+        }
+        m->ep_src_cap = max_tokens;
+    }
+    kq::MoeParams p = m->plan[KATALI_MOE_Q8_1];
+    p.experts = m->d_table;
+    p.x = x;
+    p.logits = router_logits;
+    p.ids = nullptr;
+    p.w = nullptr;
+    p.y = y;
+    p.hbuf = m->hbuf;
+    p.sync = m->sync;
+    p.status = g_status_dev;
+    p.dbg_ids = m->dbg_ids;
+    p.dbg_w = m->dbg_w;
+    p.route_only = 0;
+    p.trace = nullptr;
+    p.trace = m->trace;  // optional per-stage timestamps (katali_cuda_debug_moe_trace)
+    p.ep_recv = nullptr;  // this rank's window, chosen on the device
+    p.ep_ret = ret_scratch;
+    p.ep_slots = n_ranks * max_tokens;
+    p.ep_slot_bytes = ep_slot_bytes(m->plan[0]);
+    p.ep_hdr_bytes = ep_hdr_bytes(K);
+    p.ep_rank = pp->rank;
+    p.ep_ranks = (int)n_ranks;
+    p.ep_tmax = (int)max_tokens;
+    p.ep_tokens = (int)n_tokens;
+    p.ep_src_ids = m->ep_src_ids;
+    p.ep_peer_recv = pp->recv;
+    p.ep_peer_back = pp->back;
+    p.ep_peer_flags = pp->flags;
+    p.ep_epoch = pp->epoch;
+    p.ep_done = pp->done;
+    return finish(kq::launch_moe_ep_layer(p, m->grid, g_stream));
+}
+
 int moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
                    const void *back, float *y, const EpPeer *pp) {
     int s = ep_check(m, n_ranks, max_tokens);

@@ -30,6 +30,9 @@ int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_t
                    const void *recv, void *ret, const EpPeer *pp);
 int moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
                    const void *back, float *y, const EpPeer *pp);
+int moe_ep_layer_fused(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                       const float *x, const float *router_logits, float *y, const EpPeer *pp,
+                       double *ret_scratch);
 }  // namespace kq
 
 namespace {
@@ -301,6 +304,15 @@ int katali_cuda_moe_ep_layer(KataliMoe *m, KataliEp *ep, uint32_t max_tokens, ui
     const uint32_t G = (uint32_t)ep->n_ranks;
     if (ep->peer_mode) {  // both exchanges inside the kernels, over NVLink peer memory
         if ((s = peer_setup(ep, slot, (uint32_t)(rslot / 8), max_tokens, st))) return s;
+        // small exchanges: the whole layer in one launch (local scratch for the per-slot sums)
+        size_t r0 = ep->ret_cap, r1 = ep->ret_cap;
+        if ((s = grow(ep->ret, r0, rslot * max_tokens * ep->n_ranks)) ||
+            (s = grow(ep->back, r1, rslot * max_tokens * ep->n_ranks)))
+            return s;
+        ep->ret_cap = r0 < r1 ? r0 : r1;
+        s = kq::moe_ep_layer_fused(m, G, max_tokens, n_tokens, x, router_logits, y, &ep->peer,
+                                   (double *)ep->ret);
+        if (s != KATALI_ERR_UNSUPPORTED_SHAPE) return s;
         if ((s = kq::moe_ep_dispatch(m, G, max_tokens, n_tokens, x, router_logits, nullptr, &ep->peer)))
             return s;
         if ((s = kq::moe_ep_experts(m, G, (uint32_t)ep->rank, max_tokens, nullptr, nullptr, &ep->peer)))

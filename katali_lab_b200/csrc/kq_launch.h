@@ -91,12 +91,26 @@ struct MoeParams {
     const uint8_t *ep_recv;
     double *ep_ret;
     uint32_t ep_slots, ep_slot_bytes, ep_hdr_bytes;
+    // The whole expert-parallel layer over peer memory in one launch (launch_moe_ep_layer):
+    // this rank's ep_tokens (<= ep_tmax) tokens in x / logits, out in y; ep_recv and
+    // ep_slots are then derived on the device (this rank's window of the call's parity)
+    // and ep_ret is local scratch for the per-slot sums. Windows as in EpPeer.
+    int ep_rank, ep_ranks, ep_tmax, ep_tokens;
+    int32_t *ep_src_ids;
+    uint8_t *const *ep_peer_recv;
+    double *const *ep_peer_back;
+    uint32_t *const *ep_peer_flags;
+    uint32_t *ep_epoch, *ep_done;
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
 // The experts stage of an expert-parallel layer for at most MOE_EP_MAX_SLOTS received
 // slots (q8_1, Q6_K down, F a power of two in [256, 2048], K * F / 32 <= grid).
 cudaError_t launch_moe_ep(MoeParams &p, int grid, cudaStream_t st);
+// The whole expert-parallel layer (dispatch, experts, return, combine) over NVLink peer
+// memory in one cooperative launch per rank; same conditions as launch_moe_ep, with
+// ep_ranks * ep_tmax <= MOE_EP_MAX_SLOTS.
+cudaError_t launch_moe_ep_layer(MoeParams &p, int grid, cudaStream_t st);
 
 // Ragged multi-token MoE layer (q8_1 activations); scratch owned by the layer object.
 struct MoeBatchParams {

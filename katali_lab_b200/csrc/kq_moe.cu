@@ -85,22 +85,22 @@ __device__ __forceinline__ void bulk_g2s_split(uint8_t *dst, const uint8_t *src,
 }
 
 // Softmax weights of the chosen ids (lane 0 writes s_w); shared by both top-k paths.
-__device__ __forceinline__ void route_weights(const MoeParams &p, const float *lg, int npl,
+__device__ __forceinline__ void route_weights(const MoeParams &p, const float *L, const float *lg, int npl,
                                               int lane, int32_t *s_ids, float *s_w) {
     const int n = p.n_experts, K = p.K;
-    const float m = __ldg(&p.logits[s_ids[0]]);
+    const float m = __ldg(&L[s_ids[0]]);
     double S = 0.0;
     if (!p.norm) {  // sum over all n logits (lane-owned contiguous ranges)
         const int per = (n + 31) >> 5;
         for (int i = 0; i < per; ++i) {
             const int idx = lane * per + i;
-            if (idx < n) S += (double)kq_expf(__fsub_rn(lg ? lg[i] : __ldg(&p.logits[idx]), m));
+            if (idx < n) S += (double)kq_expf(__fsub_rn(lg ? lg[i] : __ldg(&L[idx]), m));
         }
         S = warp_sum_d(S);
     }
     // lane t < K: e_t; every lane then sums e_0..e_{K-1} in order (the
     // restatement's order) and lane t divides its own weight.
-    const float e = lane < K ? kq_expf(__fsub_rn(__ldg(&p.logits[s_ids[lane]]), m)) : 0.0f;
+    const float e = lane < K ? kq_expf(__fsub_rn(__ldg(&L[s_ids[lane]]), m)) : 0.0f;
     if (p.norm) {
         S = 0.0;
         for (int t = 0; t < K; ++t) S += (double)__shfl_sync(KQ_FULL, e, t);
@@ -123,14 +123,14 @@ __device__ __forceinline__ void ce_desc(uint64_t &a, uint64_t &b) {
 // Top-k by one warp for n <= 256: lane l owns ids [8l, 8l+8), sorts its 8 keys
 // (Batcher odd-even merge network), then each round takes the warp maximum of
 // the lane heads with two redux steps and the winning lane pops its head.
-__device__ __forceinline__ void route_regs(const MoeParams &p, int lane, int32_t *s_ids,
+__device__ __forceinline__ void route_regs(const MoeParams &p, const float *L, int lane, int32_t *s_ids,
                                            float *s_w, bool weights) {
     const int n = p.n_experts, K = p.K;
     const int npl = (n + 31) >> 5;
     uint64_t v[8];
     if (n == 256) {  // two 16-byte loads per lane, contiguous across the warp
-        const float4 l0 = __ldg(reinterpret_cast<const float4 *>(p.logits) + 2 * lane);
-        const float4 l1 = __ldg(reinterpret_cast<const float4 *>(p.logits) + 2 * lane + 1);
+        const float4 l0 = __ldg(reinterpret_cast<const float4 *>(L) + 2 * lane);
+        const float4 l1 = __ldg(reinterpret_cast<const float4 *>(L) + 2 * lane + 1);
         const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = route_key(lv[i], 8 * lane + i);
@@ -138,7 +138,7 @@ __device__ __forceinline__ void route_regs(const MoeParams &p, int lane, int32_t
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int idx = lane * npl + i;
-            v[i] = (i < npl && idx < n) ? route_key(__ldg(&p.logits[idx]), idx) : 0ull;
+            v[i] = (i < npl && idx < n) ? route_key(__ldg(&L[idx]), idx) : 0ull;
         }
     }
     trace(p, 9);
@@ -161,14 +161,14 @@ __device__ __forceinline__ void route_regs(const MoeParams &p, int lane, int32_t
     }
     __syncwarp();
     trace(p, 11);
-    if (weights) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+    if (weights) route_weights(p, L, nullptr, 0, lane, s_ids, s_w);
 }
 
 // Generic top-k for n_experts > 256: logits staged in shared memory.
-__device__ void route_smem(const MoeParams &p, float *s_logits, int32_t *s_ids, float *s_w,
+__device__ void route_smem(const MoeParams &p, const float *L, float *s_logits, int32_t *s_ids, float *s_w,
                            int lane, bool weights) {
     const int n = p.n_experts, K = p.K;
-    for (int i = lane; i < n; i += 32) s_logits[i] = p.logits[i];
+    for (int i = lane; i < n; i += 32) s_logits[i] = L[i];
     __syncwarp();
     const int npl = (n + 31) >> 5;
     uint32_t taken = 0;
@@ -198,13 +198,13 @@ __device__ void route_smem(const MoeParams &p, float *s_logits, int32_t *s_ids, 
         const int idx = lane * npl + i;
         lg[i] = idx < n ? s_logits[idx] : 0.0f;
     }
-    if (weights) route_weights(p, lg, npl, lane, s_ids, s_w);
+    if (weights) route_weights(p, L, lg, npl, lane, s_ids, s_w);
 }
 
-__device__ __forceinline__ void route(const MoeParams &p, float *s_logits, int32_t *s_ids,
+__device__ __forceinline__ void route(const MoeParams &p, const float *L, float *s_logits, int32_t *s_ids,
                                       float *s_w, int lane, bool weights = true) {
-    if (p.n_experts <= 256) route_regs(p, lane, s_ids, s_w, weights);
-    else route_smem(p, s_logits, s_ids, s_w, lane, weights);
+    if (p.n_experts <= 256) route_regs(p, L, lane, s_ids, s_w, weights);
+    else route_smem(p, L, s_logits, s_ids, s_w, lane, weights);
 }
 
 // This lane's Q4_K unit of x held in registers (phase A reuses it for every row).
@@ -311,20 +311,185 @@ __device__ __forceinline__ double dec_q8_unit(const uint8_t *drow, int F, int u,
            ((double)d * (double)a.d[2 * u + 1]) * (double)I1;
 }
 
+__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Grid barrier on p.sync[0], shared with the per-round barriers: the n-th barrier of a
+// launch waits for n * gridDim.x arrivals (the last CTA out resets the counter).
+__device__ void grid_barrier(const MoeParams &p, int &nbar) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        red_release_gpu_add(&p.sync[0], 1u);
+        const uint32_t target = (uint32_t)(nbar + 1) * gridDim.x;
+        uint32_t it = 0;
+        while (ld_acquire_gpu(&p.sync[0]) < target) {
+            if (++it > SPIN_LIMIT) {
+                *p.status |= ERR_TIMEOUT_GRID;
+                break;
+            }
+            if (it > 32) __nanosleep(20);
+        }
+    }
+    ++nbar;
+    __syncthreads();
+}
+
+// --- the whole expert-parallel layer over peer memory (EP 2) --------------------
+// Call e (= *ep_epoch + 1, the same on every rank) uses parity e & 1 of every window:
+// recv [2][G sources][tmax][slot bytes], back [2][G sources][tmax][H] doubles, flags
+// [2 kinds][2 parities][G sources]. A rank stores its slots and sums straight into the
+// owners' windows (NVLink stores; peer loads are long dependent chains here) and raises
+// its flag in every window. A window part of call e is rewritten at call e + 2 only: every
+// rank's call e + 1 waited for every rank's sums of e + 1, which each rank raises after
+// it has read everything of call e.
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *a, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *a, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ uint32_t *ep_flag(uint32_t *flags, int kind, uint32_t par, int G, int d) {
+    return flags + ((size_t)kind * 2 + par) * G + d;  // kind 0: slots landed, 1: sums landed
+}
+// After this CTA's stores into peer windows (every thread's, ordered by a CTA barrier):
+// the last of `writers` CTAs to count itself raises this rank's flag of `kind` for call
+// e in every rank's window. (A cross-GPU signal costs ~6 us here whichever way it is
+// fenced: per-CTA system fences, acquire-release ones, or one by the last CTA only.)
+__device__ __forceinline__ void ep_signal(const MoeParams &p, int kind, uint32_t e, uint32_t writers) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();  // this CTA's NVLink stores, before it is counted
+        const uint32_t prev = atom_add_acq_rel_gpu(&p.ep_done[kind], 1u);
+        if (prev == writers - 1) {
+            p.ep_done[kind] = 0u;
+            for (int d = 0; d < p.ep_ranks; ++d)
+                st_release_sys_u32(ep_flag(p.ep_peer_flags[d], kind, e & 1u, p.ep_ranks, p.ep_rank), e);
+        }
+    }
+}
+// Every rank's flag of `kind` for call e in this rank's window (thread d polls rank d's
+// entry; bounded).
+__device__ void ep_wait_all(const MoeParams &p, int kind, uint32_t e) {
+    const int d = threadIdx.x;
+    if (d < p.ep_ranks) {
+        const uint32_t *f = ep_flag(p.ep_peer_flags[p.ep_rank], kind, e & 1u, p.ep_ranks, d);
+        uint32_t it = 0;
+        while (ld_acquire_sys_u32(f) != e) {
+            if (++it > SPIN_LIMIT) {
+                *p.status |= ERR_TIMEOUT_GRID;
+                break;
+            }
+            if (it > 16) __nanosleep(64);
+        }
+    }
+    __syncthreads();
+}
+// This rank's window's slot from source src's token t for call e.
+__device__ __forceinline__ const uint8_t *ep2_slot(const MoeParams &p, uint32_t e, int src, int t) {
+    return p.ep_peer_recv[p.ep_rank] + (((size_t)(e & 1u) * p.ep_ranks + src) * p.ep_tmax + t) * p.ep_slot_bytes;
+}
+// Dispatch: CTA t < tmax routes this rank's token t, quantises its x to a GGUF q8_1 row
+// (`row`, shared) and writes slot (this rank, t) into every rank's window (empty headers
+// for t >= ep_tokens). Slot: n_owned, t, pad[2], ids[K] (-1 where another rank owns the
+// expert), w[K], then the row when n_owned > 0.
+__device__ void ep2_dispatch(const MoeParams &p, uint32_t e, int K, int H, float *s_logits,
+                             int32_t *s_ids, float *s_w, uint8_t *row) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
+    const int row_bytes = H / 32 * 36;
+    for (int t = blockIdx.x; t < tmax; t += gridDim.x) {
+        auto dst = [&](int d) {
+            return p.ep_peer_recv[d] + (((size_t)(e & 1u) * G + me) * tmax + t) * p.ep_slot_bytes;
+        };
+        if (t >= p.ep_tokens) {
+            if (tid < G) *reinterpret_cast<int4 *>(dst(tid)) = make_int4(0, t, 0, 0);
+            continue;
+        }
+        if (warp == 0) {
+            route(p, p.logits + (size_t)t * p.n_experts, s_logits, s_ids, s_w, lane, true);
+            if (lane < K) p.ep_src_ids[t * K + lane] = s_ids[lane];
+        } else {
+            const float *x = p.x + (size_t)t * H;
+            for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1)
+                quant_block_q8(__ldg(x + 32 * g + lane), lane, nullptr, nullptr, nullptr, nullptr,
+                               row + 36 * g);
+        }
+        __syncthreads();
+        for (int d = 0; d < G; ++d) {
+            uint8_t *slot = dst(d);
+            int n = 0;
+            for (int k = 0; k < K; ++k) n += s_ids[k] / per == d;
+            if (tid < K) {
+                const int id = s_ids[tid];
+                reinterpret_cast<int *>(slot + 16)[tid] = id / per == d ? id : -1;
+                reinterpret_cast<float *>(slot + 16 + 4 * K)[tid] = s_w[tid];
+            }
+            if (tid == 0) *reinterpret_cast<int4 *>(slot) = make_int4(n, t, 0, 0);
+            if (n > 0)
+                for (int i = tid; i < row_bytes / 16; i += MOE_THREADS)
+                    reinterpret_cast<int4 *>(slot + p.ep_hdr_bytes)[i] = reinterpret_cast<const int4 *>(row)[i];
+        }
+        trace(p, 16);
+        __syncthreads();  // row and routing reused by the next token
+    }
+}
+// Combine: y[t][r] = sum over ranks d owning one of t's experts (rank order) of back
+// [d][t][r] from this rank's back window.
+__device__ void ep2_combine(const MoeParams &p, uint32_t e, int K, int H) {
+    const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
+    const double *back = p.ep_peer_back[me] + (size_t)(e & 1u) * G * tmax * H;
+    const size_t n = (size_t)p.ep_tokens * H;
+    for (size_t i = (size_t)blockIdx.x * MOE_THREADS + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * MOE_THREADS) {
+        const int t = (int)(i / H), r = (int)(i % H);
+        double acc = 0.0;
+        for (int d = 0; d < G; ++d) {
+            bool own = false;
+            for (int k = 0; k < K; ++k) own |= __ldcg(p.ep_src_ids + t * K + k) / per == d;
+            if (own) acc += __ldcg(back + ((size_t)d * tmax + t) * H + r);
+        }
+        p.y[i] = (float)acc;
+    }
+}
 // Expert-parallel pairs of the received slots, in slot then k order (warp 0): a slot
 // header holds n_owned, t, pad[2], ids[K] (global expert id, or -1 when another rank
 // owns it), w[K]; slots with n_owned == 0 carry no pairs.
-__device__ void ep_pairs(const MoeParams &p, int K, int lane, int *pslot, int *pid, float *pw, int *np) {
+template <int EP>
+__device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, uint32_t e, int nslots, int K,
+                         int lane, int *pslot, int *pid, float *pw, int *np) {
     int base = 0;
-    for (int s0 = 0; s0 < (int)p.ep_slots; s0 += 32) {
+    for (int s0 = 0; s0 < nslots; s0 += 32) {
         const int s = s0 + lane;
-        const uint8_t *slot = p.ep_recv + (size_t)s * p.ep_slot_bytes;
+        const uint8_t *slot = EP == 2 ? ep2_slot(p, e, s / p.ep_tmax, s % p.ep_tmax)
+                                      : recv + (size_t)s * p.ep_slot_bytes;  // EP 2: this rank's window
         const int *ids = reinterpret_cast<const int *>(slot + 16);
         const float *ws = reinterpret_cast<const float *>(slot + 16 + 4 * K);
-        const bool live = s < (int)p.ep_slots && __ldcg(reinterpret_cast<const int *>(slot)) > 0;
+        int idv[MOE_MAX_K];
+        float wv[MOE_MAX_K];
+        bool live = false;
+        if (s < nslots) {  // every header word loaded before any is used
+            const int n = __ldcg(reinterpret_cast<const int *>(slot));
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; ++k)
+                if (k < K) {
+                    idv[k] = __ldcg(ids + k);
+                    wv[k] = __ldcg(ws + k);
+                }
+            live = n > 0;
+        }
         int cnt = 0;
         if (live)
-            for (int k = 0; k < K; ++k) cnt += __ldcg(ids + k) >= 0;
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; ++k)
+                if (k < K) cnt += idv[k] >= 0;
         int incl = cnt;
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(KQ_FULL, incl, o);
@@ -332,22 +497,29 @@ __device__ void ep_pairs(const MoeParams &p, int K, int lane, int *pslot, int *p
         }
         int off = base + incl - cnt;
         if (live)
-            for (int k = 0; k < K; ++k) {
-                const int id = __ldcg(ids + k);
-                if (id >= 0) {
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; ++k)
+                if (k < K && idv[k] >= 0) {
                     pslot[off] = s;
-                    pid[off] = id;
-                    pw[off] = __ldcg(ws + k);
+                    pid[off] = idv[k];
+                    pw[off] = wv[k];
                     ++off;
                 }
-            }
         base += __shfl_sync(KQ_FULL, incl, 31);
     }
     if (lane == 0) *np = base;
     __syncwarp();
 }
-__device__ __forceinline__ void mbar_inval(uint64_t *bar) {
-    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+// A slot's sum for one row: in ep_ret (a run of the slot's pairs continues from it in the
+// next round) and, EP 2, in the source rank's back window (a partial value is overwritten
+// by the final one before the flag is raised).
+template <int EP>
+__device__ __forceinline__ void ep_store_t(const MoeParams &p, uint32_t e, int slot, int H, uint32_t row, double v) {
+    p.ep_ret[(size_t)slot * H + row] = v;
+    if (EP == 2) {  // the source rank's window: back[e & 1][this rank][t], slot = src * tmax + t
+        const int src = slot / p.ep_tmax, t = slot % p.ep_tmax;
+        p.ep_peer_back[src][(((size_t)(e & 1u) * p.ep_ranks + p.ep_rank) * p.ep_tmax + t) * H + row] = v;
+    }
 }
 
 // SHAPE 1: the layer shape is compile-time (hidden 2048, FFN 512, top-8, Q4_K gate/up, Q6_K
@@ -398,7 +570,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
 
     if (p.route_only) {  // check entry point: the routing decision only
         if (warp == 0) {
-            route(p, s_logits, s_ids, s_w, lane);
+            route(p, p.logits, s_logits, s_ids, s_w, lane);
             if (c == 0 && lane < K) {
                 p.dbg_ids[lane] = s_ids[lane];
                 p.dbg_w[lane] = s_w[lane];
@@ -415,9 +587,24 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     int *xs16 = xs32 + H / 32;
     float *xfs = reinterpret_cast<float *>(act + 4 * H);  // fp32 mode: per-32 sums
     int npairs = K, nrounds = 1;
-    if constexpr (EP) {
+    int nbar = 0;  // grid barriers passed
+    const uint8_t *ep_recv = p.ep_recv;
+    int ep_nslots = (int)p.ep_slots;
+    uint32_t ep_e = 0;
+    if constexpr (EP == 2) {
+        ep_e = *p.ep_epoch + 1;
+        ep_nslots = p.ep_ranks * p.ep_tmax;  // slot s = source rank * tmax + token
+        ep2_dispatch(p, ep_e, K, H, s_logits, s_ids, s_w, act);
+        const uint32_t writers = (uint32_t)min((int)G, p.ep_tmax);  // CTAs that wrote slots
+        if (c < writers) ep_signal(p, 0, ep_e, writers);
+        trace(p, 9);
+        if (c < writers) trace(p, 1);
+        ep_wait_all(p, 0, ep_e);
+        trace(p, 10);
+    }
+    if constexpr (EP != 0) {
         if (warp == 0) {
-            ep_pairs(p, K, lane, s_pslot, s_pid, s_pw, s_np);
+            ep_pairs<EP>(p, ep_recv, ep_e, ep_nslots, K, lane, s_pslot, s_pid, s_pw, s_np);
         } else {
             const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
             for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
@@ -426,6 +613,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         __syncthreads();
         npairs = *s_np;
         nrounds = (npairs + K - 1) / K;
+        trace(p, 11);
     } else if (warp == 0) {
         if (p.ids) {
             if (lane < K) {
@@ -434,7 +622,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             }
             __syncwarp();
         } else {
-            route(p, s_logits, s_ids, s_w, lane, false);  // weights after the copies are issued
+            route(p, p.logits, s_logits, s_ids, s_w, lane, false);  // weights after the copies are issued
         }
         trace(p, 1);
     } else {
@@ -505,12 +693,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         __syncwarp();
         for (int q = lane; q < ncopy; q += 32) issue(q);
         trace(p, 3);
-        if (!EP && !p.ids) route_weights(p, nullptr, 0, lane, s_ids, s_w);
+        if (!EP && !p.ids) route_weights(p, p.logits, nullptr, 0, lane, s_ids, s_w);
     } else if (EP) {
         // x of this CTA's phase-A block: its pair's token, from the slot's q8_1 row
         if (nbA > 0) {
             const int kb = (int)(b0 / (F / HB));
-            const uint8_t *row = p.ep_recv + (size_t)s_slotr[kb] * p.ep_slot_bytes + p.ep_hdr_bytes;
+            const int sl = s_slotr[kb];
+            const uint8_t *row = (EP == 2 ? ep2_slot(p, ep_e, sl / p.ep_tmax, sl % p.ep_tmax)
+                                          : ep_recv + (size_t)sl * p.ep_slot_bytes) + p.ep_hdr_bytes;
             for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
                 const uint8_t *blk = row + 36 * g;
                 const int qi = (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
@@ -647,7 +837,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     trace(p, 14);
     if (tid == 0) {
         uint32_t it = 0;
-        while (ld_acquire_gpu(&p.sync[0]) < (uint32_t)(rd + 1) * G) {
+        while (ld_acquire_gpu(&p.sync[0]) < (uint32_t)(nbar + 1) * G) {
             if (++it > SPIN_LIMIT) {
                 *p.status |= ERR_TIMEOUT_GRID;
                 break;
@@ -655,6 +845,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             if (it > 32) __nanosleep(20);
         }
     }
+    ++nbar;
     __syncthreads();
     trace(p, 6);
 
@@ -762,14 +953,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                     for (int kk = 0; kk < KR; ++kk) {
                         const int sl = s_slotr[kk];
                         if (sl != cur) {
-                            if (cur >= 0) p.ep_ret[(size_t)cur * H + rB0 + r] = acc;
+                            if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc);
                             const bool cont = kk == 0 && rd > 0 && s_pslot[rd * K - 1] == sl;
                             acc = cont ? p.ep_ret[(size_t)sl * H + rB0 + r] : 0.0;
                             cur = sl;
                         }
                         acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
                     }
-                    if (cur >= 0) p.ep_ret[(size_t)cur * H + rB0 + r] = acc;
+                    if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc);
                 } else {
                     double acc = 0.0;
                     for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
@@ -810,6 +1001,15 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     }
     }  // rounds
+    if constexpr (EP == 2) {
+        // every CTA stored its rows' sums into the sources' back windows in phase B
+        ep_signal(p, 1, ep_e, G);
+        trace(p, 2);
+        ep_wait_all(p, 1, ep_e);
+        trace(p, 18);
+        ep2_combine(p, ep_e, K, H);
+        trace(p, 19);
+    }
     trace(p, 8);
 
     // ---- 7. the last CTA out re-arms the barrier counters --------------------
@@ -819,6 +1019,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         if (prev == G - 1) {
             atomicExch(&p.sync[0], 0u);
             atomicExch(&p.sync[1], 0u);
+            if (EP == 2) {  // the next call uses the other parity of every window
+                __threadfence();
+                *p.ep_epoch = ep_e;
+            }
         }
     }
 }
@@ -913,6 +1117,15 @@ cudaError_t launch_moe_ep(MoeParams &p, int grid, cudaStream_t st) {
     const bool c2 = p.H == 2048 && p.F == 512 && p.K == 8 && p.gate_type == T_Q4_K &&
                     p.up_type == T_Q4_K;
     return c2 ? launch_t<0, T_Q6_K, 1, 1>(p, grid, st) : launch_t<0, T_Q6_K, 0, 1>(p, grid, st);
+}
+
+cudaError_t launch_moe_ep_layer(MoeParams &p, int grid, cudaStream_t st) {
+    if (p.mode != 0 || p.down_type != T_Q6_K || !p.dec_enabled ||
+        p.ep_ranks * p.ep_tmax > MOE_EP_MAX_SLOTS || p.ep_tokens > p.ep_tmax)
+        return cudaErrorInvalidValue;
+    const bool c2 = p.H == 2048 && p.F == 512 && p.K == 8 && p.gate_type == T_Q4_K &&
+                    p.up_type == T_Q4_K;
+    return c2 ? launch_t<0, T_Q6_K, 1, 2>(p, grid, st) : launch_t<0, T_Q6_K, 0, 2>(p, grid, st);
 }
 
 }  // namespace kq
