@@ -1,11 +1,11 @@
-"""Expert parallelism across GPUs: two processes, one GPU each, NCCL.
+"""Expert parallelism across GPUs: two (or four) processes, one GPU each.
 
 Each rank holds half of the experts and brings its own tokens; the layer runs with
 torch.distributed's all_to_all_single as the exchange, with the plugin's own NCCL
 communicator (katali_cuda_moe_ep_layer), and twice with the exchange over NVLink peer
 memory inside the kernels (katali_cuda_ep_use_peer_memory; both window parities). Bar: every token's output
 within rel_L2 <= 1e-5 of katali_cuda_moe_batch on the full layer on the same GPU and
->= 99.9 % of elements bit-equal. Skipped with fewer than two GPUs."""
+>= 99.9 % of elements bit-equal. Skipped with fewer than two GPUs; four ranks on a box with four GPUs or more."""
 import datetime
 import os
 import socket
@@ -41,7 +41,8 @@ def _rank(rank, world, port_no, out_dir):
     try:
         plugin = Plugin()
         full = DevLayer(plugin, E, H, F, K, seed=61)
-        T, tmax = [5, 3][rank], 6
+        # world 2: 12 slots; world 4: 16 slots (both within the single-launch peer-memory layer)
+        T, tmax = ([5, 3][rank], 6) if world == 2 else ([4, 3, 2, 4][rank], 4)
         rng = np.random.default_rng(300 + rank)
         X = rng.normal(0, 1, (T, H)).astype(np.float32)
         L = rng.normal(0, 1, (T, E)).astype(np.float32)
@@ -71,17 +72,21 @@ def _rank(rank, world, port_no, out_dir):
         dist.destroy_process_group()
 
 
-def test_ep_two_gpus(tmp_path):
+def test_ep_multi_gpu(tmp_path):
+    """Two ranks, or four when the box has four GPUs or more."""
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
+    n = torch.cuda.device_count()
+    if n < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+    world = 4 if n >= 4 else 2
+    mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                        start_method="spawn", join=True)
     from oracle.oracle import rel_l2
-    sums = [np.load(tmp_path / f"r{r}.npz")["store_sum"] for r in range(2)]
-    assert np.array_equal(sums[0], sums[1]), "the two ranks built different expert stores"
-    for r in range(2):
+    sums = [np.load(tmp_path / f"r{r}.npz")["store_sum"] for r in range(world)]
+    for r in range(1, world):
+        assert np.array_equal(sums[0], sums[r]), "the ranks built different expert stores"
+    for r in range(world):
         d = np.load(tmp_path / f"r{r}.npz")
         for key in ("y1", "y2", "y3", "y4"):
             for t in range(d["want"].shape[0]):
