@@ -51,8 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4"],
-                    help="c2: fused MoE layer (headline); c1: dense Q4_K GEMV 6144x2048")
+    ap.add_argument("--config", default="c2", choices=["c2", "c1", "c3", "c4", "c5"],
+                    help="c2: fused MoE layer (headline); c1: dense Q4_K GEMV 6144x2048; c3: ragged "
+                         "batch; c4: dense Qwen3-8B decode; c5: hybrid GDN/attention MoE decode")
     ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--calls", type=int, default=64)
@@ -948,6 +949,110 @@ def run_c4(args, rank, world, local_rank):
     dm.close()
 
 
+C5_WORKLOAD = ("C5 35B-A3B-class hybrid greedy decode on one GPU: 40 layers (30 Gated DeltaNet: 16 q/k "
+               "and 32 v heads of 128, conv 4; 10 gated attention: 16 q / 2 kv heads of 256, RoPE on 64 "
+               "dims, fp32 KV), MoE every layer as C2 (256 experts, FFN 512, top-8, fp32 router), "
+               "hidden 2048, vocab 248320; Q4_K with Q6_K attn_v, expert down and output (N(0,0.02) "
+               "weights); {n} tokens per step after a 1-token prompt")
+
+
+def run_c5(args, rank, world, local_rank):
+    """C5: katali_cuda_hybrid_generate; a step = one greedy generation of 32 tokens from an
+    empty state. metric = decode tokens/s (whole job); roofline = weight + state bytes per
+    token x tokens/s against the HBM peak."""
+    import torch
+
+    from katali_lab_b200 import HybridModel, Plugin
+    from katali_lab_b200.synth import HYBRID_35B, make_hybrid_model
+    torch.cuda.set_device(local_rank)
+    plugin = Plugin()
+    if not plugin.probe():
+        raise SystemExit(f"no usable B200: {plugin.status()}")
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    model = make_hybrid_model(plugin, HYBRID_35B, seed=35 + rank)
+    plugin.set_stream(stream)
+    hm = HybridModel(plugin, model, q8=args.dp4a)
+    n = 32
+    prompt = [1]
+    for _ in range(max(args.warmup, 3)):
+        hm.reset()
+        hm.generate(prompt, n)
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = args.steps  # each a 32-token generation
+    with ClockSampler(local_rank) as clk:
+        s0.record(stream)
+        for _ in range(steps):
+            hm.reset()
+            toks = hm.generate(prompt, n)
+        s1.record(stream)
+        s1.synchronize()
+    ms = s0.elapsed_time(s1)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    bpt = model.weight_bytes_per_token + model.state_bytes_per_token
+    tok_s = world * steps * n / (ms / 1e3)
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        cpu = c5_cpu_leg(model, toks, bpt, args.cpu_seconds, fp32=not args.dp4a)
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = tok_s / world * bpt / 1e9
+        print(json.dumps({
+            "metric": "hybrid MoE decode tok/s", "value": round(tok_s, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32",
+            "data": "synthetic",
+            "config": {"workload": C5_WORKLOAD.format(n=n), "tokens_per_step": n,
+                       "activations": "q8_1 (DP4A)" if args.dp4a else "fp32",
+                       "bytes_per_token": bpt, "us_per_token": round(1e3 * ms / (steps * n), 2),
+                       "l2": "inputs larger than L2: ~1.9 GB of weights and states read per token",
+                       "parallelism": f"replicas x{world}", "last_tokens": [int(t) for t in toks[:8]]},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "scope": "whole decode step (all kernels)"},
+            "clocks": clk.summary(),
+            "e2e": {"value": round(tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * len(prompt),
+                    "d2h_bytes_per_step": 4 * n},
+            "gpu_launches": steps * n * (1 + 5 * 40 + 3), "cpu_baseline": cpu}), flush=True)
+    hm.close()
+
+
+def c5_cpu_leg(model, gpu_tokens, bpt, seconds, fp32=True):
+    """The same decode through the CPU composition (reference kernels + the Gated DeltaNet
+    restatement) on host copies of the model, for ~`seconds`; its greedy tokens are compared
+    with the GPU's (fp32 activations)."""
+    try:
+        import psutil
+        need = sum(w["experts"].gate.numel() * 3 for w in model.layers)
+        if psutil.virtual_memory().available < 2 * need:
+            return {"value": None, "unit": "tokens/s", "kind": "reference", "cores": 0,
+                    "sample": "skipped: not enough host memory for a host copy of the model"}
+    except Exception:
+        pass
+    from oracle.oracle import Ref, RefHybrid
+    cores = os.cpu_count() or 1
+    rh = RefHybrid(Ref(), model)
+    t0, k, tok, toks = time.perf_counter(), 0, 1, []
+    while k < len(gpu_tokens) and (time.perf_counter() - t0 < seconds or k < 2):
+        lg = rh.step(tok, k)
+        tok = int(np.argmax(lg))
+        toks.append(tok)
+        k += 1
+    el = time.perf_counter() - t0
+    rh.close()
+    match = [int(a) for a in gpu_tokens[:len(toks)]] == toks if fp32 else None
+    return {"value": round(k / el, 3), "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "gbs": round(k * bpt / el / 1e9, 3), "greedy_tokens_match_gpu": match,
+            "sample": f"{k} greedy decode steps ({el:.1f} s) of the same model through the "
+                      f"reference's CPU kernels + the Gated DeltaNet restatement, {cores} threads"}
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -969,6 +1074,8 @@ def main():
             run_c1(args, rank, world, local_rank)
         elif args.config == "c4":
             run_c4(args, rank, world, local_rank)
+        elif args.config == "c5":
+            run_c5(args, rank, world, local_rank)
         elif world > 1 and not args.replicas:
             run_ep(args, rank, world, local_rank)
         elif args.config == "c3":

@@ -311,6 +311,69 @@ int katali_cuda_dense_generate(KataliDense *m, const int32_t *prompt, uint32_t n
 int katali_cuda_dense_logits(KataliDense *m, const float **logits_dev, int32_t *position);
 
 /* ------------------------------------------------------------------------ */
+/* 9. Hybrid MoE decoder decode on the device: Gated DeltaNet (linear        */
+/*    attention) and gated full-attention layers, each followed by the fused  */
+/*    MoE block — the Qwen3.5/3.6-35B-A3B layer family the reference runs     */
+/*    with KATALI_CUDA_MOE=1 / KATALI_CUDA_GDN=1 (README.md:15,19,322-336;    */
+/*    binary-only there, so these entry points are new). Per layer: RMSNorm,  */
+/*    the mixer (GDN or gated attention) + residual, RMSNorm, fp32 router,    */
+/*    top-k MoE + residual; then final RMSNorm, LM head, greedy argmax.       */
+/* ------------------------------------------------------------------------ */
+#define KATALI_HYBRID_GDN 0u   /* Gated DeltaNet layer */
+#define KATALI_HYBRID_ATTN 1u  /* gated full-attention layer */
+
+typedef struct KataliHybridLayerW {
+    uint32_t kind;                 /* KATALI_HYBRID_GDN or KATALI_HYBRID_ATTN */
+    const float *attn_norm;        /* device fp32 [hidden]: RMSNorm before the mixer */
+    const float *ffn_norm;         /* device fp32 [hidden]: RMSNorm before the MoE block */
+    const float *router;           /* device fp32 [n_experts][hidden] router rows */
+    KataliMoe *moe;                /* the layer's experts (katali_cuda_moe_create) */
+    /* GDN: in-projections (cols hidden) q|k|v (rows 2 nk dk + nv dv), z (nv dv),
+     * b (nv), a (nv); out projection (rows hidden, cols nv dv) */
+    const void *ssm_qkv, *ssm_z, *ssm_b, *ssm_a, *ssm_out;
+    uint32_t ssm_qkv_type, ssm_z_type, ssm_b_type, ssm_a_type, ssm_out_type;
+    const float *ssm_conv;         /* device fp32 [2 nk dk + nv dv][ssm_conv] */
+    const float *ssm_a_log;        /* device fp32 [nv] */
+    const float *ssm_dt_bias;      /* device fp32 [nv] */
+    const float *ssm_norm;         /* device fp32 [dv]: gated RMSNorm weight */
+    /* attention: wq rows n_heads * 2 head_dim (per head: q rows, then gate rows),
+     * wk / wv rows n_kv_heads * head_dim, wo rows hidden (cols n_heads * head_dim) */
+    const void *wq, *wk, *wv, *wo;
+    uint32_t wq_type, wk_type, wv_type, wo_type;
+    const float *q_norm, *k_norm;  /* device fp32 [head_dim], or NULL */
+} KataliHybridLayerW;
+
+typedef struct KataliHybridDesc {
+    uint32_t n_layers, hidden, vocab;
+    uint32_t kv_cap;               /* positions of the attention layers' KV cache */
+    uint32_t n_heads, n_kv_heads, head_dim, rope_dim;  /* rope_dim 0 = head_dim */
+    float rms_eps, rope_theta;
+    uint32_t ssm_k_heads, ssm_v_heads, ssm_head_dim, ssm_conv;  /* dk = dv = ssm_head_dim */
+    const void *embed;             /* device, vocab rows of `hidden` (embed_type) */
+    uint32_t embed_type;
+    const float *out_norm;         /* device fp32 [hidden] */
+    const void *lm_head;           /* device, vocab rows of `hidden` (lm_head_type) */
+    uint32_t lm_head_type;
+    const KataliHybridLayerW *layers;  /* HOST array of n_layers (copied) */
+    uint32_t flags;                /* KATALI_DENSE_Q8_1: q8_1 activations in the projections
+                                      and the MoE block (DP4A); default fp32 (parity mode) */
+} KataliHybridDesc;
+/* Supported: ssm_head_dim 128, ssm_v_heads a multiple of ssm_k_heads, ssm_conv
+ * 2..8, head_dim <= 256 and a multiple of 32, hidden <= 8192 (multiple of 256),
+ * every layer's MoE with the decoder's hidden size and a fused single-launch
+ * plan; else KATALI_ERR_UNSUPPORTED_SHAPE. The MoE objects stay owned by the
+ * caller and must outlive the decoder. */
+typedef struct KataliHybrid KataliHybrid;
+int katali_cuda_hybrid_create(const KataliHybridDesc *desc, KataliHybrid **out);
+int katali_cuda_hybrid_destroy(KataliHybrid *m);
+/* Empties the KV cache and zeroes the recurrent (GDN) and conv states. */
+int katali_cuda_hybrid_reset(KataliHybrid *m);
+/* Greedy decode as katali_cuda_dense_generate (one graph replay per step). */
+int katali_cuda_hybrid_generate(KataliHybrid *m, const int32_t *prompt, uint32_t n_prompt,
+                                uint32_t n_gen, int32_t *out_tokens);
+int katali_cuda_hybrid_logits(KataliHybrid *m, const float **logits_dev, int32_t *position);
+
+/* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
 /* ------------------------------------------------------------------------ */
 /* Integer in-block sums of every row against q8_1 xq. Q4_K: per 32-group

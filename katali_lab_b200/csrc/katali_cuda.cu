@@ -230,6 +230,24 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
 
 }  // namespace
 
+namespace kq {
+// The fused single-launch call of MoE layer m in activation mode `mode`, for a decoder that
+// launches it from its own step (kq_hybrid.cu): every field but x, logits, y and accum.
+int moe_fused_params(KataliMoe *m, uint32_t mode, MoeParams *p, int *grid) {
+    if (!m || mode > 1) return KATALI_ERR_BAD_ARG;
+    if (!m->plan_ok[mode]) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    *p = m->plan[mode];
+    p->experts = m->d_table;
+    p->hbuf = m->hbuf;
+    p->sync = m->sync;
+    p->status = g_status_dev;
+    p->trace = nullptr;
+    p->route_only = 0;
+    *grid = m->grid;
+    return KATALI_OK;
+}
+}  // namespace kq
+
 extern "C" {
 
 int katali_cuda_probe(void) {

@@ -255,6 +255,18 @@ cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_dense_embed(DenseParams &p, cudaStream_t st) {
+    k_embed<<<(p.H + DT - 1) / DT, DT, 0, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st) {
+    const int nparts = 148;
+    k_argmax_part<<<nparts, DT, 0, st>>>(p);
+    k_argmax_final<<<1, 32, 0, st>>>(p, nparts);
+    return cudaGetLastError();
+}
+
 cudaError_t dense_set_attention_smem(int kv_cap) {
     return cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kv_cap * (int)sizeof(float));

@@ -77,6 +77,7 @@ struct MoeParams {
     uint32_t rbg, rbu, rbd;
     uint32_t rg;           // phase-B rows per aligned group (set by moe_plan)
     int route_only;        // 1: routing decision only (check entry point)
+    int accum;             // 1: y[r] += layer output (a decoder's residual add), 0: y[r] = output
     // shared-memory plan (bytes), identical for every CTA
     uint32_t chunk_units;  // max row pairs per phase-A chunk
     uint32_t sa_bytes;     // phase-A staging capacity
@@ -198,5 +199,39 @@ struct DenseParams {
 };
 cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st);
 cudaError_t dense_set_attention_smem(int kv_cap);
+// Pieces of the dense step shared with the hybrid decoder: the embedding row of *p.tok
+// into p.x, and the greedy argmax of p.logits (advances tok / pos / step).
+cudaError_t launch_dense_embed(DenseParams &p, cudaStream_t st);
+cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st);
+
+// Hybrid decoder (kq_hybrid.cu): Gated DeltaNet and gated-attention layers, each followed
+// by a fused MoE block. Per-layer device pointers, passed by value to that layer's launches.
+struct HybridLayer {
+    int kind;                        // 0: Gated DeltaNet, 1: gated full attention
+    const float *conv_w;             // GDN: [C][conv_k] depthwise causal conv, C = 2 nk dk + nv dv
+    const float *a_log, *dt_bias;    // GDN: [nv]
+    const float *ssm_norm;           // GDN: [dv] weight of the gated RMSNorm
+    float *ring;                     // GDN: [conv_k][C] last conv_k inputs (slot pos % conv_k)
+    float *state;                    // GDN: [nv][dv][dk] recurrent state, column j of head h contiguous
+    const float *q_norm, *k_norm;    // attention: [HD]
+    float *kv_k, *kv_v;              // attention: [NKV][kv_cap][HD] of this layer
+    const float *ffn_norm;           // [H]
+    const float *router;             // fp32 [n_experts][H]
+};
+struct HybridParams {
+    DenseParams d;                   // x, xb, q (q and gate per head), k, v, attn, logits, KV, RoPE,
+                                     // control words, argmax scratch
+    int nk, nv, dk, dv, conv_k, n_experts;
+    float *qkv;                      // GDN in-projection: [q nk*dk][k nk*dk][v nv*dv]
+    float *z;                        // [nv*dv] output gate
+    float *ba;                       // [nv] beta logits, then [nv] decay inputs
+    float *go;                       // [nv*dv] gated-norm output of the recurrence
+    float *rlogits;                  // [n_experts] router logits
+};
+// One decode step: g[2 l], g[2 l + 1] are layer l's input and output projections, g[2 NL]
+// the LM head; moe[l] / moe_grid[l] the layer's fused MoE launch (x = xb, y = x, accum).
+cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams *g,
+                               MoeParams *moe, const int *moe_grid, cudaStream_t st);
+cudaError_t hybrid_set_attention_smem(int kv_cap);
 
 }  // namespace kq

@@ -456,7 +456,7 @@ __device__ void ep2_combine(const MoeParams &p, uint32_t e, int K, int H) {
             for (int k = 0; k < K; ++k) own |= __ldcg(p.ep_src_ids + t * K + k) / per == d;
             if (own) acc += __ldcg(back + ((size_t)d * tmax + t) * H + r);
         }
-        p.y[i] = (float)acc;
+        p.y[i] = p.accum ? __fadd_rn(p.y[i], (float)acc) : (float)acc;
     }
 }
 // Expert-parallel pairs of the received slots, in slot then k order (warp 0): a slot
@@ -964,7 +964,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 } else {
                     double acc = 0.0;
                     for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
-                    p.y[rB0 + r] = (float)acc;
+                    p.y[rB0 + r] = p.accum ? __fadd_rn(p.y[rB0 + r], (float)acc) : (float)acc;
                 }
             }
         } else {
@@ -996,7 +996,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 for (int o = 1; o < lpe; o <<= 1) part += __shfl_xor_sync(KQ_FULL, part, o);
                 double t = k < K ? wk * (double)(float)part : 0.0;
                 for (int o = lpe; o < 32; o <<= 1) t += __shfl_xor_sync(KQ_FULL, t, o);
-                if (!EP && lane == 0) p.y[rB0 + rr] = (float)t;
+                if (!EP && lane == 0)
+                    p.y[rB0 + rr] = p.accum ? __fadd_rn(p.y[rB0 + rr], (float)t) : (float)t;
             }
         }
     }

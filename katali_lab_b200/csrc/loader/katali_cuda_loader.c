@@ -98,6 +98,14 @@
       (m, p, np, ng, o))                                                                      \
     X(int, katali_cuda_dense_logits, (KataliDense * m, const float **l, int32_t *p),          \
       (m, l, p))                                                                              \
+    X(int, katali_cuda_hybrid_create, (const KataliHybridDesc *d, KataliHybrid **o), (d, o))  \
+    X(int, katali_cuda_hybrid_destroy, (KataliHybrid * m), (m))                               \
+    X(int, katali_cuda_hybrid_reset, (KataliHybrid * m), (m))                                 \
+    X(int, katali_cuda_hybrid_generate,                                                       \
+      (KataliHybrid * m, const int32_t *p, uint32_t np, uint32_t ng, int32_t *o),             \
+      (m, p, np, ng, o))                                                                      \
+    X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
+      (m, l, p))                                                                              \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -249,6 +257,14 @@ const char *katali_cuda_strerror(int s) {
       (KataliDense * m, const int32_t *p, uint32_t np, uint32_t ng, int32_t *o),              \
       (m, p, np, ng, o))                                                                      \
     X(int, katali_cuda_dense_logits, (KataliDense * m, const float **l, int32_t *p),          \
+      (m, l, p))                                                                              \
+    X(int, katali_cuda_hybrid_create, (const KataliHybridDesc *d, KataliHybrid **o), (d, o))  \
+    X(int, katali_cuda_hybrid_destroy, (KataliHybrid * m), (m))                               \
+    X(int, katali_cuda_hybrid_reset, (KataliHybrid * m), (m))                                 \
+    X(int, katali_cuda_hybrid_generate,                                                       \
+      (KataliHybrid * m, const int32_t *p, uint32_t np, uint32_t ng, int32_t *o),             \
+      (m, p, np, ng, o))                                                                      \
+    X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
       (m, l, p))                                                                              \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \

@@ -46,6 +46,25 @@ class KataliDenseDesc(C.Structure):
                 ("flags", _u32)]
 
 
+class KataliHybridLayerW(C.Structure):
+    _fields_ = [("kind", _u32), ("attn_norm", _vp), ("ffn_norm", _vp), ("router", _vp), ("moe", _vp),
+                ("ssm_qkv", _vp), ("ssm_z", _vp), ("ssm_b", _vp), ("ssm_a", _vp), ("ssm_out", _vp),
+                ("ssm_qkv_type", _u32), ("ssm_z_type", _u32), ("ssm_b_type", _u32),
+                ("ssm_a_type", _u32), ("ssm_out_type", _u32), ("ssm_conv", _vp), ("ssm_a_log", _vp),
+                ("ssm_dt_bias", _vp), ("ssm_norm", _vp), ("wq", _vp), ("wk", _vp), ("wv", _vp),
+                ("wo", _vp), ("wq_type", _u32), ("wk_type", _u32), ("wv_type", _u32),
+                ("wo_type", _u32), ("q_norm", _vp), ("k_norm", _vp)]
+
+
+class KataliHybridDesc(C.Structure):
+    _fields_ = [("n_layers", _u32), ("hidden", _u32), ("vocab", _u32), ("kv_cap", _u32),
+                ("n_heads", _u32), ("n_kv_heads", _u32), ("head_dim", _u32), ("rope_dim", _u32),
+                ("rms_eps", C.c_float), ("rope_theta", C.c_float), ("ssm_k_heads", _u32),
+                ("ssm_v_heads", _u32), ("ssm_head_dim", _u32), ("ssm_conv", _u32), ("embed", _vp),
+                ("embed_type", _u32), ("out_norm", _vp), ("lm_head", _vp), ("lm_head_type", _u32),
+                ("layers", C.POINTER(KataliHybridLayerW)), ("flags", _u32)]
+
+
 class KataliMoeDesc(C.Structure):
     _fields_ = [("n_experts", _u32), ("hidden", _u32), ("ffn", _u32), ("top_k", _u32),
                 ("gate_type", _u32), ("up_type", _u32), ("down_type", _u32), ("flags", _u32),
@@ -124,6 +143,11 @@ class Plugin:
             "katali_cuda_dense_reset": ([_vp], _i32),
             "katali_cuda_dense_generate": ([_vp, _vp, _u32, _u32, _vp], _i32),
             "katali_cuda_dense_logits": ([_vp, C.POINTER(_vp), C.POINTER(_i32)], _i32),
+            "katali_cuda_hybrid_create": ([C.POINTER(KataliHybridDesc), C.POINTER(_vp)], _i32),
+            "katali_cuda_hybrid_destroy": ([_vp], _i32),
+            "katali_cuda_hybrid_reset": ([_vp], _i32),
+            "katali_cuda_hybrid_generate": ([_vp, _vp, _u32, _u32, _vp], _i32),
+            "katali_cuda_hybrid_logits": ([_vp, C.POINTER(_vp), C.POINTER(_i32)], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -346,3 +370,78 @@ class DenseModel:
         if self.h:
             self.p.L.katali_cuda_dense_destroy(self.h)
             self.h = None
+
+
+class HybridModel:
+    """A hybrid MoE decoder (Gated DeltaNet + gated attention, MoE every layer) resident on
+    the device (katali_cuda_hybrid_*)."""
+
+    def __init__(self, plugin: Plugin, model, q8: bool = False):
+        """model: katali_lab_b200.synth.HybridWeights (device tensors). q8: q8_1 activations
+        (DP4A) in the projections and the MoE block instead of fp32."""
+        self.p = plugin
+        cfg = model.cfg
+        T = model.types
+        self.moes = []
+        ly = (KataliHybridLayerW * cfg.n_layers)()
+        for l, w in enumerate(model.layers):
+            st = w["experts"]
+            moe = MoeLayer(plugin, cfg.n_experts, cfg.hidden, cfg.ffn, cfg.top_k, st.pointers(),
+                           norm_topk=True, gate_type=T["gate"], up_type=T["up"], down_type=T["down"])
+            self.moes.append(moe)
+            e = KataliHybridLayerW()
+            e.kind = w["kind"]
+            e.attn_norm, e.ffn_norm, e.router = _ptr(w["attn_norm"]), _ptr(w["ffn_norm"]), _ptr(w["router"])
+            e.moe = moe.h.value
+            if w["kind"] == 0:
+                for k in ("ssm_qkv", "ssm_z", "ssm_b", "ssm_a", "ssm_out"):
+                    setattr(e, k, _ptr(w[k]))
+                    setattr(e, k + "_type", T[k])
+                for k in ("ssm_conv", "ssm_a_log", "ssm_dt_bias", "ssm_norm"):
+                    setattr(e, k, _ptr(w[k]))
+            else:
+                for k in ("wq", "wk", "wv", "wo"):
+                    setattr(e, k, _ptr(w[k]))
+                    setattr(e, k + "_type", T[k])
+                e.q_norm, e.k_norm = _ptr(w.get("q_norm")), _ptr(w.get("k_norm"))
+            ly[l] = e
+        self._layers = ly
+        desc = KataliHybridDesc(cfg.n_layers, cfg.hidden, cfg.vocab, cfg.kv_cap, cfg.n_heads,
+                                cfg.n_kv_heads, cfg.head_dim, cfg.rope_dim, cfg.rms_eps,
+                                cfg.rope_theta, cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim,
+                                cfg.ssm_conv, _ptr(model.embed), T["embed"], _ptr(model.out_norm),
+                                _ptr(model.lm_head), T["lm_head"],
+                                C.cast(ly, C.POINTER(KataliHybridLayerW)), 1 if q8 else 0)
+        h = _vp()
+        rc = plugin.L.katali_cuda_hybrid_create(C.byref(desc), C.byref(h))
+        if rc != 0:
+            for m in self.moes:
+                m.close()
+            plugin.check(rc)
+        self.h = h
+        self.vocab = cfg.vocab
+
+    def reset(self) -> None:
+        self.p.check(self.p.L.katali_cuda_hybrid_reset(self.h))
+
+    def generate(self, prompt, n_gen: int):
+        import numpy as np
+        pr = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, dtype=np.int32)
+        self.p.check(self.p.L.katali_cuda_hybrid_generate(self.h, pr.ctypes.data, pr.size, n_gen,
+                                                          out.ctypes.data))
+        return out
+
+    def logits(self):
+        """(device address of the last step's logits, next position)."""
+        ptr, pos = _vp(), _i32()
+        self.p.check(self.p.L.katali_cuda_hybrid_logits(self.h, C.byref(ptr), C.byref(pos)))
+        return ptr.value, pos.value
+
+    def close(self) -> None:
+        if self.h:
+            self.p.L.katali_cuda_hybrid_destroy(self.h)
+            self.h = None
+        for m in self.moes:
+            m.close()
+        self.moes = []

@@ -154,3 +154,123 @@ def make_dense_model(plugin: Plugin, cfg: DenseConfig, seed: int, std: float = 0
     out_norm = norm(H)
     torch.cuda.synchronize()
     return DenseWeights(cfg, embed, lm_head, out_norm, layers, dict(T))
+
+
+# ---------------------------------------------------------------------------
+# Hybrid MoE decoder (Gated DeltaNet + gated attention, MoE every layer)
+# ---------------------------------------------------------------------------
+@dataclass
+class HybridConfig:
+    n_layers: int
+    hidden: int
+    vocab: int
+    kv_cap: int
+    n_heads: int          # gated attention: query heads
+    n_kv_heads: int
+    head_dim: int
+    rope_dim: int         # RoPE on the first rope_dim dimensions of a head
+    ssm_k_heads: int      # GDN: q/k heads
+    ssm_v_heads: int      # GDN: value heads (a multiple of ssm_k_heads)
+    ssm_head_dim: int     # dk = dv
+    ssm_conv: int         # causal conv kernel
+    n_experts: int
+    ffn: int              # expert FFN
+    top_k: int
+    attn_every: int = 4   # layer l is full attention when (l + 1) % attn_every == 0
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e7
+
+    def kind(self, l: int) -> int:
+        return 1 if (l + 1) % self.attn_every == 0 else 0
+
+
+# 35B-A3B class (config 5): 40 layers = 30 GDN + 10 gated attention, hidden 2048, MoE every
+# layer as config 2 (256 experts, FFN 512, top-8, renormalised top-k weights). Mixer
+# dimensions follow the Qwen3.5 / Qwen3-Next family: GDN 16 q/k heads and 32 value heads of
+# 128, conv kernel 4; attention 16 q / 2 kv heads of 256 with RoPE on 64 dims (theta 1e7);
+# vocab 248320.
+HYBRID_35B = HybridConfig(n_layers=40, hidden=2048, vocab=248320, kv_cap=4096, n_heads=16,
+                          n_kv_heads=2, head_dim=256, rope_dim=64, ssm_k_heads=16,
+                          ssm_v_heads=32, ssm_head_dim=128, ssm_conv=4, n_experts=256, ffn=512,
+                          top_k=8)
+
+HYBRID_TYPES = {"ssm_qkv": Q4_K, "ssm_z": Q4_K, "ssm_b": Q4_K, "ssm_a": Q4_K, "ssm_out": Q4_K,
+                "wq": Q4_K, "wk": Q4_K, "wv": Q6_K, "wo": Q4_K, "embed": Q4_K, "lm_head": Q6_K,
+                "gate": Q4_K, "up": Q4_K, "down": Q6_K}
+
+
+@dataclass
+class HybridWeights:
+    cfg: HybridConfig
+    embed: torch.Tensor
+    lm_head: torch.Tensor
+    out_norm: torch.Tensor
+    layers: list          # dicts of device tensors; "experts" holds the layer's ExpertStore
+    types: dict
+
+    @property
+    def weight_bytes_per_token(self) -> int:
+        """Weight bytes one decode step reads: every mixer matrix and router once, the
+        top_k selected experts of every layer, the LM head and one embedding row."""
+        c = self.cfg
+        n = self.lm_head.numel() + self.embed.shape[1]
+        for w in self.layers:
+            keys = ("ssm_qkv", "ssm_z", "ssm_b", "ssm_a", "ssm_out", "ssm_conv") if w["kind"] == 0 \
+                else ("wq", "wk", "wv", "wo")
+            n += sum(w[k].numel() * w[k].element_size() for k in keys)
+            n += w["router"].numel() * 4 + c.top_k * w["experts"].expert_bytes
+        return n
+
+    @property
+    def state_bytes_per_token(self) -> int:
+        """Recurrent-state bytes one decode step reads and writes (GDN states)."""
+        c = self.cfg
+        n_gdn = sum(1 for w in self.layers if w["kind"] == 0)
+        return 2 * n_gdn * c.ssm_v_heads * c.ssm_head_dim * c.ssm_head_dim * 4
+
+
+def make_hybrid_model(plugin: Plugin, cfg: HybridConfig, seed: int, std: float = 0.02) -> HybridWeights:
+    """GGUF matrices ~ N(0, std) encoded on the device; fp32 router rows ~ N(0, std); norm
+    weights 1 + 0.1 N(0, 1); conv taps N(0, 0.3); A_log = log U(1, 16); dt_bias U(-4, -2)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    H, T = cfg.hidden, HYBRID_TYPES
+    C = (2 * cfg.ssm_k_heads + cfg.ssm_v_heads) * cfg.ssm_head_dim
+    VD = cfg.ssm_v_heads * cfg.ssm_head_dim
+    QD, KD = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+
+    def randn(*shape, s=1.0):
+        return torch.randn(shape, generator=gen, device="cuda", dtype=torch.float32).mul_(s)
+
+    def mat(kind, rows, cols):
+        return quantize_matrix(plugin, T[kind], randn(rows, cols, s=std))
+
+    def norm(n):
+        return (1.0 + 0.1 * randn(n)).contiguous()
+
+    def uniform(n, lo, hi):
+        return (lo + (hi - lo) * torch.rand(n, generator=gen, device="cuda")).contiguous()
+
+    layers = []
+    for l in range(cfg.n_layers):
+        w = {"kind": cfg.kind(l), "attn_norm": norm(H), "ffn_norm": norm(H),
+             "router": randn(cfg.n_experts, H, s=std).contiguous()}
+        if w["kind"] == 0:
+            w.update({"ssm_qkv": mat("ssm_qkv", C, H), "ssm_z": mat("ssm_z", VD, H),
+                      "ssm_b": mat("ssm_b", cfg.ssm_v_heads, H), "ssm_a": mat("ssm_a", cfg.ssm_v_heads, H),
+                      "ssm_out": mat("ssm_out", H, VD),
+                      "ssm_conv": randn(C, cfg.ssm_conv, s=0.3).contiguous(),
+                      "ssm_a_log": torch.log(uniform(cfg.ssm_v_heads, 1.0, 16.0)).contiguous(),
+                      "ssm_dt_bias": uniform(cfg.ssm_v_heads, -4.0, -2.0),
+                      "ssm_norm": norm(cfg.ssm_head_dim)})
+        else:
+            w.update({"wq": mat("wq", 2 * QD, H), "wk": mat("wk", KD, H), "wv": mat("wv", KD, H),
+                      "wo": mat("wo", H, QD), "q_norm": norm(cfg.head_dim),
+                      "k_norm": norm(cfg.head_dim)})
+        w["experts"] = make_expert_store(plugin, cfg.n_experts, H, cfg.ffn, seed=seed * 1000 + l, std=std)
+        layers.append(w)
+    embed = mat("embed", cfg.vocab, H)
+    lm_head = mat("lm_head", cfg.vocab, H)
+    out_norm = norm(H)
+    torch.cuda.synchronize()
+    return HybridWeights(cfg, embed, lm_head, out_norm, layers, dict(T))

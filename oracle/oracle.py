@@ -394,3 +394,95 @@ class RefDense:
         if self.h:
             self.ref.L.kref_dense_free(self.h)
             self.h = None
+
+
+class _KrefHybridLayer(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p),
+                ("router", C.c_void_p), ("w_qkv", C.c_void_p), ("w_z", C.c_void_p),
+                ("w_b", C.c_void_p), ("w_a", C.c_void_p), ("w_out", C.c_void_p),
+                ("t_qkv", C.c_uint32), ("t_z", C.c_uint32), ("t_b", C.c_uint32), ("t_a", C.c_uint32),
+                ("t_out", C.c_uint32), ("conv", C.c_void_p), ("a_log", C.c_void_p),
+                ("dt_bias", C.c_void_p), ("ssm_norm", C.c_void_p), ("wq", C.c_void_p),
+                ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p), ("tq", C.c_uint32),
+                ("tk", C.c_uint32), ("tv", C.c_uint32), ("to", C.c_uint32), ("q_norm", C.c_void_p),
+                ("k_norm", C.c_void_p), ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p)]
+
+
+class RefHybrid:
+    """The hybrid MoE decode step (kref_hybrid_*: the reference's kernels plus the Gated
+    DeltaNet restatement) on HOST copies of a katali_lab_b200.synth.HybridWeights model."""
+
+    def __init__(self, ref: "Ref", model, n_threads: int = 0):
+        cfg = model.cfg
+        self.ref, self.cfg = ref, cfg
+        h = lambda t: np.ascontiguousarray(t.cpu().numpy())  # noqa: E731
+        self._keep = []
+        keep = self._keep.append
+        T = model.types
+        NL = cfg.n_layers
+        ly = (_KrefHybridLayer * NL)()
+        for l, w in enumerate(model.layers):
+            e = _KrefHybridLayer()
+            e.kind = w["kind"]
+
+            def hp(key):
+                a = h(w[key])
+                keep(a)
+                return a.ctypes.data
+            e.attn_norm, e.ffn_norm, e.router = hp("attn_norm"), hp("ffn_norm"), hp("router")
+            if w["kind"] == 0:
+                e.w_qkv, e.w_z, e.w_b, e.w_a, e.w_out = (hp(k) for k in ("ssm_qkv", "ssm_z", "ssm_b",
+                                                                         "ssm_a", "ssm_out"))
+                e.t_qkv, e.t_z, e.t_b, e.t_a, e.t_out = (T[k] for k in ("ssm_qkv", "ssm_z", "ssm_b",
+                                                                        "ssm_a", "ssm_out"))
+                e.conv, e.a_log, e.dt_bias, e.ssm_norm = (hp(k) for k in ("ssm_conv", "ssm_a_log",
+                                                                          "ssm_dt_bias", "ssm_norm"))
+            else:
+                e.wq, e.wk, e.wv, e.wo = (hp(k) for k in ("wq", "wk", "wv", "wo"))
+                e.tq, e.tk, e.tv, e.to = (T[k] for k in ("wq", "wk", "wv", "wo"))
+                e.q_norm, e.k_norm = hp("q_norm"), hp("k_norm")
+            st = w["experts"]
+            for name, dev in (("gate", st.gate), ("up", st.up), ("down", st.down)):
+                a = h(dev)
+                keep(a)
+                ptrs = (C.c_void_p * cfg.n_experts)(*[a.ctypes.data + i * a.shape[1]
+                                                      for i in range(cfg.n_experts)])
+                keep(ptrs)
+                setattr(e, name, C.cast(ptrs, C.c_void_p).value)
+            ly[l] = e
+        keep(ly)
+        emb, lm, on = h(model.embed), h(model.lm_head), h(model.out_norm)
+        for a in (emb, lm, on):
+            keep(a)
+        dims = (C.c_int32 * 16)(NL, cfg.hidden, cfg.vocab, cfg.kv_cap, cfg.n_heads, cfg.n_kv_heads,
+                                cfg.head_dim, cfg.rope_dim, cfg.ssm_k_heads, cfg.ssm_v_heads,
+                                cfg.ssm_head_dim, cfg.ssm_conv, cfg.n_experts, cfg.ffn, cfg.top_k, 1)
+        keep(dims)
+        L = ref.L
+        L.kref_hybrid_new.restype = C.c_void_p
+        L.kref_hybrid_new.argtypes = [C.c_void_p, C.c_float, C.c_float, C.c_void_p, C.c_uint32,
+                                      C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_uint32,
+                                      C.c_uint32, C.c_void_p, C.c_int]
+        L.kref_hybrid_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+        L.kref_hybrid_step.restype = C.c_int
+        L.kref_hybrid_free.argtypes = [C.c_void_p]
+        L.kref_hybrid_reset.argtypes = [C.c_void_p]
+        self.h = L.kref_hybrid_new(dims, cfg.rms_eps, cfg.rope_theta, emb.ctypes.data, T["embed"],
+                                   lm.ctypes.data, T["lm_head"], on.ctypes.data, T["gate"], T["up"],
+                                   T["down"], C.cast(ly, C.c_void_p), n_threads or os.cpu_count() or 1)
+        if not self.h:
+            raise MemoryError("kref_hybrid_new failed")
+        self.logits = np.zeros(cfg.vocab, dtype=np.float32)
+
+    def reset(self):
+        self.ref.L.kref_hybrid_reset(self.h)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        if self.ref.L.kref_hybrid_step(self.h, int(token), int(pos), self.logits.ctypes.data) != 0:
+            raise ValueError("kref_hybrid_step failed")
+        return self.logits
+
+    def close(self):
+        if self.h:
+            self.ref.L.kref_hybrid_free(self.h)
+            self.h = None

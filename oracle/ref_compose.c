@@ -265,3 +265,275 @@ int kref_dense_step(void *p, int token, int pos, float *logits_out) {
     if (logits_out) memcpy(logits_out, m->logits, (size_t)m->vocab * 4);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Hybrid MoE decoder step (Qwen3.5/3.6-35B-A3B layer family; the reference   */
+/* runs it only in its binaries, README.md:15,19,322-336). Composed from the  */
+/* reference's kernels where the checkout has them — katali_gguf_rmsnorm[_    */
+/* inplace], katali_ggml_matvec (Q4_K/Q6_K and the F32 router), katali_gguf_ */
+/* rope_apply on the first rope_dim dimensions, katali_gguf_gqa_decode_       */
+/* scratch, katali_gguf_sigmoid, katali_gguf_add_inplace and the composed MoE */
+/* layer above — plus a RESTATEMENT of the Gated DeltaNet decode step, which  */
+/* has no reference source: the published gated delta rule (Yang, Kautz,     */
+/* Hatamizadeh, ICLR 2025) in the Qwen3-Next/Qwen3.5 layer layout:            */
+/*   depthwise causal conv (kernel K) over q|k|v + SiLU; q, k L2-normalised   */
+/*   per head (eps 1e-6), q scaled by 1/sqrt(dk); beta = sigmoid(b),          */
+/*   g = -exp(A_log) softplus(a + dt_bias); S <- exp(g) S; kv = S^T k;        */
+/*   S <- S + k (beta (v - kv))^T; o = S^T q; out = RMSNorm(o) w silu(z).     */
+/* Parity of the GDN step and the gated attention is therefore unpinned by    */
+/* the reference; the arithmetic order matches the plugin's kq_hybrid.cu.     */
+/* ------------------------------------------------------------------------ */
+typedef struct KrefHybridLayer {
+    int32_t kind; /* 0 GDN, 1 gated attention */
+    const float *attn_norm, *ffn_norm, *router;
+    const void *w_qkv, *w_z, *w_b, *w_a, *w_out;
+    uint32_t t_qkv, t_z, t_b, t_a, t_out;
+    const float *conv, *a_log, *dt_bias, *ssm_norm;
+    const void *wq, *wk, *wv, *wo;
+    uint32_t tq, tk, tv, to;
+    const float *q_norm, *k_norm;
+    const void *const *gate;  /* n_experts host pointers each */
+    const void *const *up;
+    const void *const *down;
+} KrefHybridLayer;
+
+typedef struct KrefHybrid {
+    int NL, H, vocab, cap, NH, NKV, HD, rd, nk, nv, dh, K, E, F, top_k, norm_topk, n_threads;
+    uint32_t gate_t, up_t, down_t, embed_t, lm_t;
+    float eps, theta;
+    const void *embed, *lm;
+    const float *out_norm;
+    KrefHybridLayer *L;
+    float *x, *xb, *tmp, *qkv, *cv, *z, *b, *a, *go, *qg, *q, *gt, *k, *v, *attn, *rl, *logits;
+    float *kv_k, *kv_v, *ring, *state, *scores, *rope_inv, *rope_cos, *rope_sin;
+    void *moe_scratch;
+} KrefHybrid;
+
+void kref_hybrid_free(void *p) {
+    KrefHybrid *m = (KrefHybrid *)p;
+    if (!m) return;
+    free(m->L); free(m->x); free(m->xb); free(m->tmp); free(m->qkv); free(m->cv); free(m->z);
+    free(m->b); free(m->a); free(m->go); free(m->qg); free(m->q); free(m->gt); free(m->k);
+    free(m->v); free(m->attn); free(m->rl); free(m->logits); free(m->kv_k); free(m->kv_v);
+    free(m->ring); free(m->state); free(m->scores); free(m->rope_inv); free(m->rope_cos);
+    free(m->rope_sin);
+    kref_moe_scratch_free(m->moe_scratch);
+    free(m);
+}
+
+static int kh_count(const KrefHybrid *m, int kind) {
+    int n = 0;
+    for (int l = 0; l < m->NL; l++) n += m->L[l].kind == kind;
+    return n;
+}
+
+void *kref_hybrid_new(const int32_t *dims /* NL H vocab cap NH NKV HD rope_dim nk nv dh K E F top_k norm_topk */,
+                      float eps, float theta, const void *embed, uint32_t embed_t, const void *lm,
+                      uint32_t lm_t, const float *out_norm, uint32_t gate_t, uint32_t up_t,
+                      uint32_t down_t, const KrefHybridLayer *layers, int n_threads) {
+    KrefHybrid *m = (KrefHybrid *)calloc(1, sizeof(*m));
+    if (!m) return NULL;
+    m->NL = dims[0]; m->H = dims[1]; m->vocab = dims[2]; m->cap = dims[3]; m->NH = dims[4];
+    m->NKV = dims[5]; m->HD = dims[6]; m->nk = dims[8]; m->nv = dims[9]; m->dh = dims[10];
+    m->K = dims[11]; m->E = dims[12]; m->F = dims[13]; m->top_k = dims[14]; m->norm_topk = dims[15];
+    m->rd = (dims[7] == 0 || dims[7] > m->HD) ? m->HD : dims[7];
+    m->eps = eps; m->theta = theta; m->embed = embed; m->embed_t = embed_t; m->lm = lm;
+    m->lm_t = lm_t; m->out_norm = out_norm; m->gate_t = gate_t; m->up_t = up_t; m->down_t = down_t;
+    m->n_threads = n_threads;
+    m->L = (KrefHybridLayer *)malloc(sizeof(KrefHybridLayer) * (size_t)m->NL);
+    memcpy(m->L, layers, sizeof(KrefHybridLayer) * (size_t)m->NL);
+    const size_t H = (size_t)m->H, C = (size_t)(2 * m->nk + m->nv) * m->dh, VD = (size_t)m->nv * m->dh;
+    const size_t QD = (size_t)m->NH * m->HD, KD = (size_t)m->NKV * m->HD;
+    const int n_gdn = kh_count(m, 0), n_attn = kh_count(m, 1);
+    m->x = calloc(H, 4); m->xb = calloc(H, 4); m->tmp = calloc(H, 4);
+    m->qkv = calloc(C + 1, 4); m->cv = calloc(C + 1, 4); m->z = calloc(VD + 1, 4);
+    m->b = calloc((size_t)m->nv + 1, 4); m->a = calloc((size_t)m->nv + 1, 4); m->go = calloc(VD + 1, 4);
+    m->qg = calloc(2 * QD + 1, 4); m->q = calloc(QD + 1, 4); m->gt = calloc(QD + 1, 4);
+    m->k = calloc(KD + 1, 4); m->v = calloc(KD + 1, 4); m->attn = calloc(QD + 1, 4);
+    m->rl = calloc((size_t)m->E, 4); m->logits = calloc((size_t)m->vocab, 4);
+    m->kv_k = calloc((size_t)n_attn * KD * m->cap + 1, 4);
+    m->kv_v = calloc((size_t)n_attn * KD * m->cap + 1, 4);
+    m->ring = calloc((size_t)n_gdn * m->K * C + 1, 4);
+    m->state = calloc((size_t)n_gdn * VD * m->dh + 1, 4);
+    m->scores = calloc((size_t)m->cap, 4);
+    m->rope_inv = calloc((size_t)m->rd / 2 + 1, 4); m->rope_cos = calloc((size_t)m->rd / 2 + 1, 4);
+    m->rope_sin = calloc((size_t)m->rd / 2 + 1, 4);
+    for (int i = 0; i < m->rd / 2; i++)
+        m->rope_inv[i] = 1.0f / powf(theta, (2.0f * (float)i) / (float)m->rd);
+    m->moe_scratch = kref_moe_scratch_new(m->E, m->H, m->F, m->top_k);
+    if (!m->x || !m->state || !m->ring || !m->kv_k || !m->kv_v || !m->moe_scratch) {
+        kref_hybrid_free(m);
+        return NULL;
+    }
+    return m;
+}
+
+void kref_hybrid_reset(void *p) {
+    KrefHybrid *m = (KrefHybrid *)p;
+    const size_t C = (size_t)(2 * m->nk + m->nv) * m->dh, VD = (size_t)m->nv * m->dh;
+    const int n_gdn = kh_count(m, 0);
+    memset(m->ring, 0, (size_t)n_gdn * m->K * C * 4);
+    memset(m->state, 0, (size_t)n_gdn * VD * m->dh * 4);
+}
+
+static float kh_silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* The Gated DeltaNet decode step (restatement, see above) of one layer at position pos:
+ * qkv (C), z (nv dh), b / a (nv) in; out (nv dh) = the gated RMSNorm of the recurrence. */
+static void kref_gdn_step(const KrefHybrid *m, const KrefHybridLayer *L, int pos, float *ring,
+                          float *state, float *out) {
+    const int nk = m->nk, nv = m->nv, dh = m->dh, K = m->K, ratio = nv / nk;
+    const int C = (2 * nk + nv) * dh;
+    for (int c = 0; c < C; c++) {
+        float acc = 0.0f;
+        for (int j = 0; j < K - 1; j++) {
+            const int t = pos - (K - 1) + j;
+            const int slot = ((t % K) + K) % K;
+            acc = acc + L->conv[(size_t)c * K + j] * ring[(size_t)slot * C + c];
+        }
+        acc = acc + L->conv[(size_t)c * K + K - 1] * m->qkv[c];
+        m->cv[c] = kh_silu(acc);
+    }
+    for (int c = 0; c < C; c++) ring[(size_t)(pos % K) * C + c] = m->qkv[c];
+    const float scale = 1.0f / sqrtf((float)dh);
+    for (int h = 0; h < 2 * nk; h++) {
+        float *v = m->cv + (size_t)h * dh;
+        double ss = 0.0;
+        for (int i = 0; i < dh; i++) ss += (double)v[i] * (double)v[i];
+        const float inv = 1.0f / sqrtf((float)ss + 1e-6f);
+        for (int i = 0; i < dh; i++) v[i] = h < nk ? v[i] * inv * scale : v[i] * inv;
+    }
+    float *o = m->tmp; /* dh floats (H >= dh) */
+    for (int vh = 0; vh < nv; vh++) {
+        const int kh = vh / ratio;
+        const float *q = m->cv + (size_t)kh * dh, *k = m->cv + (size_t)(nk + kh) * dh;
+        const float *v = m->cv + (size_t)(2 * nk) * dh + (size_t)vh * dh;
+        const float beta = 1.0f / (1.0f + expf(-m->b[vh]));
+        const float xa = m->a[vh] + L->dt_bias[vh];
+        const float sp = xa > 20.0f ? xa : log1pf(expf(xa));
+        const float g = -(expf(L->a_log[vh]) * sp);
+        const float decay = expf(g);
+        float *S = state + (size_t)vh * dh * dh;
+        for (int j = 0; j < dh; j++) {
+            float *col = S + (size_t)j * dh;
+            double kv = 0.0;
+            for (int i = 0; i < dh; i++) {
+                col[i] = col[i] * decay;
+                kv += (double)col[i] * (double)k[i];
+            }
+            const float delta = (v[j] - (float)kv) * beta;
+            double acc = 0.0;
+            for (int i = 0; i < dh; i++) {
+                col[i] = col[i] + k[i] * delta;
+                acc += (double)col[i] * (double)q[i];
+            }
+            o[j] = (float)acc;
+        }
+        double ss = 0.0;
+        for (int j = 0; j < dh; j++) ss += (double)o[j] * (double)o[j];
+        const float inv = 1.0f / sqrtf((float)(ss / (double)dh) + m->eps);
+        for (int j = 0; j < dh; j++)
+            out[(size_t)vh * dh + j] = o[j] * inv * L->ssm_norm[j] * kh_silu(m->z[(size_t)vh * dh + j]);
+    }
+}
+
+/* One step at position pos with input token; logits_out may be NULL. */
+int kref_hybrid_step(void *p, int token, int pos, float *logits_out) {
+    KrefHybrid *m = (KrefHybrid *)p;
+    if (!m || token < 0 || token >= m->vocab || pos < 0 || pos >= m->cap) return -1;
+    const int H = m->H, NH = m->NH, NKV = m->NKV, HD = m->HD, nt = m->n_threads;
+    const int nv = m->nv, dh = m->dh, C = (2 * m->nk + nv) * dh;
+    const uint64_t erb = katali_ggml_row_bytes(m->embed_t, (uint64_t)H);
+    if (katali_ggml_dequant_ref(m->embed_t, (const uint8_t *)m->embed + (size_t)token * erb,
+                                (uint64_t)H, m->x) != 0)
+        return -1;
+    const int half = m->rd / 2;
+    for (int i = 0; i < half; i++) {
+        const float freq = (float)pos * m->rope_inv[i];
+        m->rope_cos[i] = cosf(freq);
+        m->rope_sin[i] = sinf(freq);
+    }
+    const size_t KD = (size_t)NKV * HD, QD = (size_t)NH * HD;
+    int gi = 0, ai = 0;
+    for (int l = 0; l < m->NL; l++) {
+        const KrefHybridLayer *L = &m->L[l];
+        katali_gguf_rmsnorm(m->x, L->attn_norm, (size_t)H, m->eps, m->xb);
+        if (L->kind == 0) {
+            kref_matvec(L->t_qkv, L->w_qkv, (uint64_t)C, (uint64_t)H, m->xb, m->qkv, nt);
+            kref_matvec(L->t_z, L->w_z, (uint64_t)nv * dh, (uint64_t)H, m->xb, m->z, nt);
+            kref_matvec(L->t_b, L->w_b, (uint64_t)nv, (uint64_t)H, m->xb, m->b, nt);
+            kref_matvec(L->t_a, L->w_a, (uint64_t)nv, (uint64_t)H, m->xb, m->a, nt);
+            float *ring = m->ring + (size_t)gi * m->K * C;
+            float *state = m->state + (size_t)gi * nv * dh * dh;
+            gi++;
+            kref_gdn_step(m, L, pos, ring, state, m->go);
+            kref_matvec(L->t_out, L->w_out, (uint64_t)H, (uint64_t)nv * dh, m->go, m->tmp, nt);
+        } else {
+            kref_matvec(L->tq, L->wq, (uint64_t)2 * QD, (uint64_t)H, m->xb, m->qg, nt);
+            for (int h = 0; h < NH; h++) {
+                memcpy(m->q + (size_t)h * HD, m->qg + (size_t)h * 2 * HD, (size_t)HD * 4);
+                memcpy(m->gt + (size_t)h * HD, m->qg + (size_t)h * 2 * HD + HD, (size_t)HD * 4);
+            }
+            kref_matvec(L->tk, L->wk, (uint64_t)KD, (uint64_t)H, m->xb, m->k, nt);
+            kref_matvec(L->tv, L->wv, (uint64_t)KD, (uint64_t)H, m->xb, m->v, nt);
+            if (L->q_norm)
+                for (int h = 0; h < NH; h++)
+                    katali_gguf_rmsnorm_inplace(m->q + (size_t)h * HD, L->q_norm, (size_t)HD, m->eps);
+            katali_gguf_rope_apply(m->q, (size_t)NH, (size_t)HD, (size_t)m->rd, m->rope_cos, m->rope_sin);
+            if (L->k_norm)
+                for (int h = 0; h < NKV; h++)
+                    katali_gguf_rmsnorm_inplace(m->k + (size_t)h * HD, L->k_norm, (size_t)HD, m->eps);
+            katali_gguf_rope_apply(m->k, (size_t)NKV, (size_t)HD, (size_t)m->rd, m->rope_cos, m->rope_sin);
+            float *lk = m->kv_k + (size_t)ai * KD * m->cap, *lv = m->kv_v + (size_t)ai * KD * m->cap;
+            ai++;
+            for (int h = 0; h < NKV; h++) {
+                memcpy(lk + ((size_t)h * m->cap + pos) * HD, m->k + (size_t)h * HD, (size_t)HD * 4);
+                memcpy(lv + ((size_t)h * m->cap + pos) * HD, m->v + (size_t)h * HD, (size_t)HD * 4);
+            }
+            katali_gguf_gqa_decode_scratch(m->q, lk, lv, (size_t)pos + 1, (size_t)m->cap, (size_t)NH,
+                                           (size_t)NKV, (size_t)HD, m->attn, m->scores);
+            for (size_t i = 0; i < QD; i++) m->attn[i] = m->attn[i] * katali_gguf_sigmoid(m->gt[i]);
+            kref_matvec(L->to, L->wo, (uint64_t)H, (uint64_t)QD, m->attn, m->tmp, nt);
+        }
+        katali_gguf_add_inplace(m->x, m->tmp, (size_t)H);
+        katali_gguf_rmsnorm(m->x, L->ffn_norm, (size_t)H, m->eps, m->xb);
+        kref_matvec(KGGML_F32, L->router, (uint64_t)m->E, (uint64_t)H, m->xb, m->rl, nt);
+        if (kref_moe_layer(m->E, H, m->F, m->top_k, m->norm_topk, m->gate_t, m->up_t, m->down_t,
+                           L->gate, L->up, L->down, m->xb, m->rl, m->tmp, nt, m->moe_scratch,
+                           NULL, NULL) != 0)
+            return -1;
+        katali_gguf_add_inplace(m->x, m->tmp, (size_t)H);
+    }
+    katali_gguf_rmsnorm(m->x, m->out_norm, (size_t)H, m->eps, m->xb);
+    kref_matvec(m->lm_t, m->lm, (uint64_t)m->vocab, (uint64_t)H, m->xb, m->logits, nt);
+    if (logits_out) memcpy(logits_out, m->logits, (size_t)m->vocab * 4);
+    return 0;
+}
+
+/* T decode steps of one Gated DeltaNet mixer from zero conv and recurrent state (the
+ * restatement above, for the CPU test that checks it against a matrix-form formulation):
+ * qkv [T][(2 nk + nv) dh], z [T][nv dh], b / a [T][nv] in, out [T][nv dh]. */
+int kref_gdn_apply(int nk, int nv, int dh, int K, int T, float eps, const float *conv,
+                   const float *a_log, const float *dt_bias, const float *norm_w,
+                   const float *qkv, const float *z, const float *b, const float *a, float *out) {
+    KrefHybrid m;
+    memset(&m, 0, sizeof m);
+    m.nk = nk; m.nv = nv; m.dh = dh; m.K = K; m.eps = eps;
+    const size_t C = (size_t)(2 * nk + nv) * dh, VD = (size_t)nv * dh;
+    KrefHybridLayer L;
+    memset(&L, 0, sizeof L);
+    L.conv = conv; L.a_log = a_log; L.dt_bias = dt_bias; L.ssm_norm = norm_w;
+    m.qkv = calloc(C, 4); m.cv = calloc(C, 4); m.z = calloc(VD, 4); m.b = calloc((size_t)nv, 4);
+    m.a = calloc((size_t)nv, 4); m.tmp = calloc((size_t)dh, 4);
+    float *ring = calloc((size_t)K * C, 4), *state = calloc(VD * (size_t)dh, 4);
+    int rc = (m.qkv && m.cv && m.z && m.b && m.a && m.tmp && ring && state) ? 0 : -1;
+    for (int t = 0; rc == 0 && t < T; t++) {
+        memcpy(m.qkv, qkv + (size_t)t * C, C * 4);
+        memcpy(m.z, z + (size_t)t * VD, VD * 4);
+        memcpy(m.b, b + (size_t)t * nv, (size_t)nv * 4);
+        memcpy(m.a, a + (size_t)t * nv, (size_t)nv * 4);
+        kref_gdn_step(&m, &L, t, ring, state, out + (size_t)t * VD);
+    }
+    free(m.qkv); free(m.cv); free(m.z); free(m.b); free(m.a); free(m.tmp); free(ring); free(state);
+    return rc;
+}
