@@ -20,6 +20,7 @@ calls, download of the outputs, each step. N > 1 GPUs run independent replicas
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -56,6 +57,8 @@ def parse():
                          "batch; c4: dense Qwen3-8B decode; c5: hybrid GDN/attention MoE decode")
     ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--hybrid-layers", type=int, default=40,
+                    help="c5: decoder layers (every 4th is gated attention); 40 is the configuration")
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
@@ -970,7 +973,9 @@ def run_c5(args, rank, world, local_rank):
         raise SystemExit(f"no usable B200: {plugin.status()}")
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    model = make_hybrid_model(plugin, HYBRID_35B, seed=35 + rank)
+    cfg = HYBRID_35B if args.hybrid_layers == HYBRID_35B.n_layers else \
+        dataclasses.replace(HYBRID_35B, n_layers=args.hybrid_layers)
+    model = make_hybrid_model(plugin, cfg, seed=35 + rank)
     plugin.set_stream(stream)
     hm = HybridModel(plugin, model, q8=args.dp4a)
     n = 32
@@ -1009,6 +1014,7 @@ def run_c5(args, rank, world, local_rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32",
             "data": "synthetic",
             "config": {"workload": C5_WORKLOAD.format(n=n), "tokens_per_step": n,
+                       "n_layers": cfg.n_layers,
                        "activations": "q8_1 (DP4A)" if args.dp4a else "fp32",
                        "bytes_per_token": bpt, "us_per_token": round(1e3 * ms / (steps * n), 2),
                        "l2": "inputs larger than L2: ~1.9 GB of weights and states read per token",
@@ -1019,7 +1025,7 @@ def run_c5(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": steps * n * (1 + 5 * 40 + 3), "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": steps * n * (1 + 5 * cfg.n_layers + 3), "cpu_baseline": cpu}), flush=True)
     hm.close()
 
 

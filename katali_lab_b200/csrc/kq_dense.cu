@@ -78,6 +78,8 @@ __device__ __forceinline__ float dequant_elem(uint32_t type, const uint8_t *row,
 }
 
 __global__ void k_embed(DenseParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int tok = *p.tok;
     const uint8_t *row = p.embed + (size_t)tok * p.embed_rb;
     for (int i = blockIdx.x * DT + threadIdx.x; i < p.H; i += gridDim.x * DT)
@@ -190,6 +192,8 @@ __device__ __forceinline__ void better(float &bv, int &bi, float v, int i) {
 __global__ void k_argmax_part(DenseParams p) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    pdl_trigger();
+    pdl_wait();
     float bv = -INFINITY;
     int bi = -1;
     for (int i = blockIdx.x * DT + threadIdx.x; i < p.vocab; i += gridDim.x * DT)
@@ -213,6 +217,8 @@ __global__ void k_argmax_part(DenseParams p) {
     }
 }
 __global__ void k_argmax_final(DenseParams p, int nparts) {
+    pdl_trigger();
+    pdl_wait();
     float bv = -INFINITY;
     int bi = -1;
     for (int b = threadIdx.x; b < nparts; b += 32)
@@ -260,11 +266,11 @@ cudaError_t launch_dense_embed(DenseParams &p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st) {
+cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st, int pdl) {
     const int nparts = 148;
-    k_argmax_part<<<nparts, DT, 0, st>>>(p);
-    k_argmax_final<<<1, 32, 0, st>>>(p, nparts);
-    return cudaGetLastError();
+    cudaError_t e = launch_k(k_argmax_part, dim3(nparts), dim3(DT), 0, st, pdl, p);
+    if (e == cudaSuccess) e = launch_k(k_argmax_final, dim3(1), dim3(32), 0, st, pdl, p, nparts);
+    return e;
 }
 
 cudaError_t dense_set_attention_smem(int kv_cap) {

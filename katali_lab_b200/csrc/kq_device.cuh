@@ -89,6 +89,19 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the programmatic stream
+// serialization attribute may start before the previous kernel on its stream has
+// finished; pdl_wait() blocks the calling thread until that kernel has completed
+// and its memory is visible (a no-op for an ordinary launch). pdl_trigger() lets
+// the next such kernel be scheduled once every CTA of this grid has issued it.
+// Rule for every kernel that is launched this way: read only constant data
+// (weights) before pdl_wait(); every read of a predecessor's output and every
+// global write comes after it, in at least one thread of every CTA.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // mbarrier + bulk (TMA, non-tensor) copies, no multicast.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.act_off - 16 * p.nstages);
     uint64_t *empty = full + p.nstages;
     const int cols = (int)p.cols;
+    pdl_trigger();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.nstages; ++s) {
@@ -73,7 +74,10 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
 
     // Consumers: stage the activation vector once, bank-spread (16 bytes of padding
-    // after every 64 elements) so the 32 lanes' units fall on distinct banks.
+    // after every 64 elements) so the 32 lanes' units fall on distinct banks. Under a
+    // programmatic launch the producer above streams weights (constant) while the
+    // previous kernel finishes; x (and y, when accumulating) only after pdl_wait().
+    pdl_wait();
     uint8_t *act = smem + p.act_off;
     ActQ8 a;
     const float *xf = nullptr, *xs = nullptr;
@@ -424,8 +428,21 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         set_bytes[mode] = smem;
     }
-    fn<<<grid, GEMV_THREADS, smem, st>>>(p);
-    return cudaGetLastError();
+    if (!p.pdl) {
+        fn<<<grid, GEMV_THREADS, smem, st>>>(p);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, p);
 }
 
 cudaError_t launch_quantize_q8_1(const float *x, uint64_t n, void *out, cudaStream_t st) {

@@ -31,7 +31,7 @@ namespace {
 constexpr int DT = 256;           // threads of the attention kernel (head_dim <= 256)
 constexpr int GD = 128;           // GDN head dimension (dk = dv)
 constexpr int GDN_THREADS = 512;  // 16 warps x 8 state columns
-constexpr int RT = 64;            // router: two warps, one expert row each
+constexpr int RW = 4;             // router: warps per CTA, one expert row each
 
 __device__ __forceinline__ double block_sum_d(double v, double *sh) {
     v = warp_sum_d(v);
@@ -68,6 +68,16 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
     const int vh = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ratio = p.nv / p.nk, kh = vh / ratio;
     const int C = 2 * p.nk * GD + p.nv * GD, K = p.conv_k;
+    // The head's state columns are loaded before pdl_wait(): this layer's state was last
+    // written by this kernel one token earlier, and every MoE launch in between (an
+    // ordinary, non-programmatic launch) started only after all earlier kernels completed.
+    float *S = L.state + (size_t)vh * GD * GD;
+    float4 s[GD / 16];
+#pragma unroll
+    for (int c = 0; c < GD / 16; ++c)
+        s[c] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(warp + 16 * c) * GD) + lane);
+    pdl_trigger();
+    pdl_wait();
     const int pos = *p.d.pos;
     if (tid < 3 * GD) {
         const int which = tid / GD, c = tid % GD;
@@ -84,10 +94,10 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
         }
         acc = __fadd_rn(acc, __fmul_rn(w[K - 1], cur));
         if (which == 2 || vh % ratio == 0) L.ring[(size_t)(pos % K) * C + ch] = cur;
-        const float s = silu_f(acc);
-        if (which == 0) sq[c] = s;
-        else if (which == 1) sk[c] = s;
-        else sv[c] = s;
+        const float act = silu_f(acc);
+        if (which == 0) sq[c] = act;
+        else if (which == 1) sk[c] = act;
+        else sv[c] = act;
     }
     if (tid == 0) {
         const float b = p.ba[vh], a = p.ba[p.nv + vh];
@@ -109,14 +119,9 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
     }
     __syncthreads();
 
-    float *S = L.state + (size_t)vh * GD * GD;
     const float beta = s_par[0], decay = s_par[1];
     const float4 kk = reinterpret_cast<const float4 *>(sk)[lane];
     const float4 qq = reinterpret_cast<const float4 *>(sq)[lane];
-    float4 s[GD / 16];
-#pragma unroll
-    for (int c = 0; c < GD / 16; ++c)
-        s[c] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(warp + 16 * c) * GD) + lane);
 #pragma unroll
     for (int c = 0; c < GD / 16; ++c) {
         const int j = warp + 16 * c;
@@ -189,6 +194,8 @@ __global__ void __launch_bounds__(DT) k_attn_gated(HybridParams hp, HybridLayer 
     __shared__ double sh[32];
     __shared__ float red[32];
     __shared__ float sq[DT], sk[DT], sv[DT], tmp[DT];
+    pdl_trigger();
+    pdl_wait();
     const int HD = p.HD, hq = blockIdx.x, reps = p.NH / p.NKV;
     const int hk = hq / reps, pos = *p.pos, kv_len = pos + 1;
     const float *qh = p.q + (size_t)hq * 2 * HD;
@@ -240,60 +247,83 @@ __global__ void __launch_bounds__(DT) k_attn_gated(HybridParams hp, HybridLayer 
 }
 
 // MoE block input: xb = RMSNorm(x) * ffn_norm (written by CTA 0; every CTA recomputes it in
-// shared memory), router logits = R xb with fp32 rows and double accumulation.
-__global__ void __launch_bounds__(RT) k_router(HybridParams hp, HybridLayer L) {
+// shared memory), router logits = R xb with fp32 rows and double accumulation. One warp per
+// expert row; the row (NV float4 per lane, H = 128 NV) is loaded into registers before
+// pdl_wait(), so under a programmatic launch the 2 MB of router weights stream while the
+// previous kernel finishes. NV = 0: any H, loads in the dot loop.
+template <int NV>
+__global__ void __launch_bounds__(RW * 32) k_router(HybridParams hp, HybridLayer L) {
     extern __shared__ __align__(16) float xn[];  // H floats
     __shared__ double sh[32];
     const DenseParams &p = hp.d;
-    const int H = p.H, tid = threadIdx.x;
+    const int H = p.H, tid = threadIdx.x, lane = tid & 31;
+    const int r = blockIdx.x * RW + (tid >> 5);
+    const bool live = r < hp.n_experts;
+    const float4 *w = reinterpret_cast<const float4 *>(L.router + (size_t)(live ? r : 0) * H);
+    float4 wr[NV > 0 ? NV : 1];
+    if constexpr (NV > 0) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) wr[i] = __ldcs(w + lane + 32 * i);
+    }
+    pdl_trigger();
+    pdl_wait();
     double ss = 0.0;
-    for (int i = tid; i < H; i += RT) ss += (double)p.x[i] * (double)p.x[i];
+    for (int i = tid; i < H; i += RW * 32) ss += (double)p.x[i] * (double)p.x[i];
     ss = block_sum_d(ss, sh);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / (double)H), p.eps)));
-    for (int i = tid; i < H; i += RT) {
+    for (int i = tid; i < H; i += RW * 32) {
         const float v = __fmul_rn(__fmul_rn(p.x[i], inv), L.ffn_norm[i]);
         xn[i] = v;
         if (blockIdx.x == 0) p.xb[i] = v;
     }
     __syncthreads();
-    const int r = blockIdx.x * (RT / 32) + (tid >> 5), lane = tid & 31;
-    if (r < hp.n_experts) {
-        const float4 *w = reinterpret_cast<const float4 *>(L.router + (size_t)r * H);
-        const float4 *xv = reinterpret_cast<const float4 *>(xn);
-        double acc = 0.0;
-#pragma unroll 4
-        for (int i = lane; i < H / 4; i += 32) {
-            const float4 a = __ldcs(w + i), b = xv[i];
-            acc += (double)a.x * (double)b.x;
-            acc += (double)a.y * (double)b.y;
-            acc += (double)a.z * (double)b.z;
-            acc += (double)a.w * (double)b.w;
-        }
-        acc = warp_sum_d(acc);
-        if (lane == 0) hp.rlogits[r] = (float)acc;
+    if (!live) return;
+    const float4 *xv = reinterpret_cast<const float4 *>(xn);
+    double acc = 0.0;
+    auto dot4 = [&](const float4 a, const float4 b) {
+        acc += (double)a.x * (double)b.x;
+        acc += (double)a.y * (double)b.y;
+        acc += (double)a.z * (double)b.z;
+        acc += (double)a.w * (double)b.w;
+    };
+    if constexpr (NV > 0) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) dot4(wr[i], xv[lane + 32 * i]);
+    } else {
+        for (int i = lane; i < H / 4; i += 32) dot4(__ldcs(w + i), xv[i]);
     }
+    acc = warp_sum_d(acc);
+    if (lane == 0) hp.rlogits[r] = (float)acc;
 }
 
 }  // namespace
 
 cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams *g,
                                MoeParams *moe, const int *moe_grid, cudaStream_t st) {
+    // Every launch but the first (the embedding) and the cooperative MoE kernels is a
+    // programmatic dependent of the one before it (the GEMVs carry it in GemvParams.pdl).
     cudaError_t e = launch_dense_embed(p.d, st);
     if (e != cudaSuccess) return e;
     const int mode = p.d.gemv_mode;
     const size_t att_smem = (size_t)p.d.kv_cap * sizeof(float);
     const size_t rt_smem = (size_t)p.d.H * sizeof(float);
+    void (*router)(HybridParams, HybridLayer) = p.d.H == 2048   ? k_router<16>
+                                                : p.d.H == 1024 ? k_router<8>
+                                                : p.d.H == 4096 ? k_router<32>
+                                                                : k_router<0>;
+    const dim3 rgrid((p.n_experts + RW - 1) / RW);
     for (int l = 0; l < p.d.NL; ++l) {
         if ((e = launch_gemv(g[2 * l], mode, st)) != cudaSuccess) return e;
-        if (L[l].kind == 0) k_gdn<<<p.nv, GDN_THREADS, 0, st>>>(p, L[l]);
-        else k_attn_gated<<<p.d.NH, DT, att_smem, st>>>(p, L[l]);
+        if (L[l].kind == 0) e = launch_k(k_gdn, dim3(p.nv), dim3(GDN_THREADS), 0, st, 1, p, L[l]);
+        else e = launch_k(k_attn_gated, dim3(p.d.NH), dim3(DT), att_smem, st, 1, p, L[l]);
+        if (e != cudaSuccess) return e;
         if ((e = launch_gemv(g[2 * l + 1], mode, st)) != cudaSuccess) return e;
-        k_router<<<(p.n_experts + RT / 32 - 1) / (RT / 32), RT, rt_smem, st>>>(p, L[l]);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = launch_k(router, rgrid, dim3(RW * 32), rt_smem, st, 1, p, L[l])) != cudaSuccess)
+            return e;
         if ((e = launch_moe(moe[l], moe_grid[l], st)) != cudaSuccess) return e;
     }
     if ((e = launch_gemv(g[2 * p.d.NL], mode, st)) != cudaSuccess) return e;
-    return launch_dense_argmax(p.d, st);
+    return launch_dense_argmax(p.d, st, 1);
 }
 
 cudaError_t hybrid_set_attention_smem(int kv_cap) {

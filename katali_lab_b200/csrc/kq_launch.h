@@ -40,7 +40,26 @@ struct GemvParams {
     const float *x_mul;
     const float *norm_w;
     float norm_eps;
+    int pdl;  // 1: launched as a programmatic dependent of the previous kernel on the stream
 };
+
+// Launch of kernel k, as a programmatic dependent of the previous kernel on st when pdl
+// (the kernel then follows the pdl_wait() rule of kq_device.cuh).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            int pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k, args...);
+}
 
 // mode 0: q8_1 activations quantised in-kernel from fp32 x; 1: from q8_1 blocks;
 // 2: fp32 activations.
@@ -202,7 +221,7 @@ cudaError_t dense_set_attention_smem(int kv_cap);
 // Pieces of the dense step shared with the hybrid decoder: the embedding row of *p.tok
 // into p.x, and the greedy argmax of p.logits (advances tok / pos / step).
 cudaError_t launch_dense_embed(DenseParams &p, cudaStream_t st);
-cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st);
+cudaError_t launch_dense_argmax(DenseParams &p, cudaStream_t st, int pdl = 0);
 
 // Hybrid decoder (kq_hybrid.cu): Gated DeltaNet and gated-attention layers, each followed
 // by a fused MoE block. Per-layer device pointers, passed by value to that layer's launches.

@@ -536,6 +536,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const int H = SHAPE ? 2048 : p.H, F = SHAPE ? 512 : p.F, K = SHAPE ? 8 : p.K;
     trace(p, 0);
+    pdl_trigger();  // a following programmatic launch (a decoder's next GEMV) may be scheduled
 
     uint8_t *sa = smem;
     uint8_t *sb = smem + p.sb_off;
