@@ -123,6 +123,8 @@ __global__ void __launch_bounds__(DT) k_attention(DenseParams p, int layer) {
     __shared__ double sh[32];
     __shared__ float red[32];
     __shared__ float sq[512], sk[512], sv[512], tmp[512];
+    pdl_trigger();
+    pdl_wait();
     const int HD = p.HD, hq = blockIdx.x, reps = p.NH / p.NKV;
     const int hk = hq / reps, pos = *p.pos, kv_len = pos + 1;
     norm_rope_head(p, p.q + (size_t)hq * HD, p.q_norm_dev[layer], pos, tmp, sq, sh);
@@ -174,6 +176,8 @@ __global__ void __launch_bounds__(DT) k_attention(DenseParams p, int layer) {
 }
 
 __global__ void k_silu_mul(float *g, const float *u, int n) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * DT + threadIdx.x;
     if (i < n) {
         const float x = g[i];
@@ -242,23 +246,24 @@ __global__ void k_argmax_final(DenseParams p, int nparts) {
 cudaError_t launch_dense_step(DenseParams &p, GemvParams *g, cudaStream_t st) {
     // g[4 l + 0..3]: qkv (attn RMSNorm in the staging), o (+ residual), gate/up (ffn
     // RMSNorm in the staging), down (+ residual) after SiLU * up; g[4 NL]: the LM head
-    // (final RMSNorm in the staging).
-    const int nparts = 148;
+    // (final RMSNorm in the staging). Every launch after the embedding is a programmatic
+    // dependent of the one before it (GEMV weights stream while the previous kernel ends).
     k_embed<<<(p.H + DT - 1) / DT, DT, 0, st>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     for (int l = 0; l < p.NL; ++l) {
-        cudaError_t e = launch_gemv(g[4 * l + 0], p.gemv_mode, st);
+        if ((e = launch_gemv(g[4 * l + 0], p.gemv_mode, st)) != cudaSuccess) return e;
+        e = launch_k(k_attention, dim3(p.NH), dim3(DT), (size_t)p.kv_cap * sizeof(float), st, 1, p, l);
         if (e != cudaSuccess) return e;
-        k_attention<<<p.NH, DT, (size_t)p.kv_cap * sizeof(float), st>>>(p, l);
         if ((e = launch_gemv(g[4 * l + 1], p.gemv_mode, st)) != cudaSuccess) return e;
         if ((e = launch_gemv(g[4 * l + 2], p.gemv_mode, st)) != cudaSuccess) return e;
-        k_silu_mul<<<(p.F + DT - 1) / DT, DT, 0, st>>>(p.gate, p.up, p.F);
+        e = launch_k(k_silu_mul, dim3((p.F + DT - 1) / DT), dim3(DT), 0, st, 1, p.gate,
+                     (const float *)p.up, p.F);
+        if (e != cudaSuccess) return e;
         if ((e = launch_gemv(g[4 * l + 3], p.gemv_mode, st)) != cudaSuccess) return e;
     }
-    cudaError_t e = launch_gemv(g[4 * p.NL], p.gemv_mode, st);
-    if (e != cudaSuccess) return e;
-    k_argmax_part<<<nparts, DT, 0, st>>>(p);
-    k_argmax_final<<<1, 32, 0, st>>>(p, nparts);
-    return cudaGetLastError();
+    if ((e = launch_gemv(g[4 * p.NL], p.gemv_mode, st)) != cudaSuccess) return e;
+    return launch_dense_argmax(p, st, 1);
 }
 
 cudaError_t launch_dense_embed(DenseParams &p, cudaStream_t st) {

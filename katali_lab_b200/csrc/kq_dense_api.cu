@@ -63,6 +63,7 @@ kq::GemvParams gemv_job(const float *x, uint64_t cols, int n, const void *const 
     g.norm_eps = eps;
     g.x_mul = x_mul;
     g.status = kq::device_status_word();
+    g.pdl = 1;  // programmatic dependent of the previous launch of the decode step
     for (int j = 0; j < n; ++j) {
         g.job[j].w = (const uint8_t *)w[j];
         g.job[j].y = y[j];
