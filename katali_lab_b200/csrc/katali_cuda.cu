@@ -548,6 +548,7 @@ static int moe_run(KataliMoe *m, const float *x, const float *logits, const int3
     p.dbg_w = m->dbg_w;
     p.route_only = route_only;
     p.trace = route_only ? nullptr : m->trace;
+    p.pdl = 1;  // overlaps this launch's prologue with the end of the previous kernel
     return finish(kq::launch_moe(p, route_only ? 1 : m->grid, g_stream));
 }
 

@@ -312,6 +312,7 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
         mp.logits = hp.rlogits;
         mp.y = p.x;
         mp.accum = 1;
+        mp.pdl = 1;
     }
     {
         const void *ws[1] = {d->lm_head};

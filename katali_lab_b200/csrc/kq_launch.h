@@ -97,6 +97,7 @@ struct MoeParams {
     uint32_t rg;           // phase-B rows per aligned group (set by moe_plan)
     int route_only;        // 1: routing decision only (check entry point)
     int accum;             // 1: y[r] += layer output (a decoder's residual add), 0: y[r] = output
+    int pdl;               // 1: programmatic dependent of the previous kernel (not EP, not route_only)
     // shared-memory plan (bytes), identical for every CTA
     uint32_t chunk_units;  // max row pairs per phase-A chunk
     uint32_t sa_bytes;     // phase-A staging capacity

@@ -570,6 +570,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     }
 
     if (p.route_only) {  // check entry point: the routing decision only
+        pdl_wait();
         if (warp == 0) {
             route(p, p.logits, s_logits, s_ids, s_w, lane);
             if (c == 0 && lane < K) {
@@ -593,6 +594,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     int ep_nslots = (int)p.ep_slots;
     uint32_t ep_e = 0;
     if constexpr (EP == 2) {
+        pdl_wait();
         ep_e = *p.ep_epoch + 1;
         ep_nslots = p.ep_ranks * p.ep_tmax;  // slot s = source rank * tmax + token
         ep2_dispatch(p, ep_e, K, H, s_logits, s_ids, s_w, act);
@@ -604,6 +606,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         trace(p, 10);
     }
     if constexpr (EP != 0) {
+        pdl_wait();
         if (warp == 0) {
             ep_pairs<EP>(p, ep_recv, ep_e, ep_nslots, K, lane, s_pslot, s_pid, s_pw, s_np);
         } else {
@@ -616,6 +619,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         nrounds = (npairs + K - 1) / K;
         trace(p, 11);
     } else if (warp == 0) {
+        pdl_wait();  // under a programmatic launch: x, logits / ids, scratch only after this
         if (p.ids) {
             if (lane < K) {
                 s_ids[lane] = p.ids[lane];
@@ -627,11 +631,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
         trace(p, 1);
     } else {
-        for (int i = tid - 32; i < H / 4; i += MOE_THREADS - 32)
-            reinterpret_cast<float4 *>(xf)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
+        // The expert pointer table changes only through stream-ordered copies (a copy ends
+        // any programmatic overlap), so it is read before pdl_wait(); x after it.
         const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
         for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
             reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
+        pdl_wait();
+        for (int i = tid - 32; i < H / 4; i += MOE_THREADS - 32)
+            reinterpret_cast<float4 *>(xf)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
     }
     if constexpr (!EP) __syncthreads();
     trace(p, 2);
@@ -1093,12 +1100,25 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     cfg.blockDim = dim3(MOE_THREADS);
     cfg.dynamicSmemBytes = p.smem_bytes;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = p.route_only ? 0 : 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
+    // A programmatic launch when asked for and accepted: the first such launch (always an
+    // eager one, before any graph capture) that the runtime refuses switches it off.
+    static int pdl_ok = 1;
+    const bool pdl = p.pdl && pdl_ok && !EP && !p.route_only;
+    cfg.numAttrs = pdl ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
+    if (pdl && (e == cudaErrorInvalidValue || e == cudaErrorNotSupported)) {
+        cudaGetLastError();
+        pdl_ok = 0;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
+    }
+    return e;
 }
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
