@@ -941,10 +941,13 @@ def run_c4(args, rank, world, local_rank):
                        "tokens_per_s": round(tok_s, 1), "weight_bytes_per_token": bpt,
                        "us_per_token": round(1e3 * ms / (args.steps * n), 2),
                        "l2": "inputs larger than L2: 4.9 GB of weights read per token",
-                       "parallelism": f"replicas x{world}", "last_tokens": [int(t) for t in toks[:8]]},
+                       "parallelism": (f"ep{world}: experts of every layer split over the GPUs, "
+                                       "one sequence per GPU, MoE blocks over NVLink peer memory")
+                       if ep else f"replicas x{world}",
+                       "last_tokens": [int(t) for t in toks[:8]]},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                         "traffic": None, "scope": "whole decode step (all kernels)"},
+                         "traffic": None, "scope": "whole decode step (all kernels), per GPU"},
             "clocks": clk.summary(),
             "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
@@ -975,11 +978,20 @@ def run_c5(args, rank, world, local_rank):
     torch.cuda.set_stream(stream)
     cfg = HYBRID_35B if args.hybrid_layers == HYBRID_35B.n_layers else \
         dataclasses.replace(HYBRID_35B, n_layers=args.hybrid_layers)
-    model = make_hybrid_model(plugin, cfg, seed=35 + rank)
+    ep = world > 1 and not args.replicas  # experts sharded over the GPUs, one sequence per rank
+    q8 = args.dp4a or ep                  # the expert-parallel layer runs q8_1 activations
+    model = make_hybrid_model(plugin, cfg, seed=35 if ep else 35 + rank,
+                              ep=(world, rank) if ep else None)
     plugin.set_stream(stream)
-    hm = HybridModel(plugin, model, q8=args.dp4a)
+    hm = HybridModel(plugin, model, q8=q8)
+    comm = None
+    if ep:
+        from katali_lab_b200.ep import EpComm
+        comm = EpComm.from_process_group(plugin)
+        comm.use_peer_memory(True)
+        hm.set_ep(comm)
     n = 32
-    prompt = [1]
+    prompt = [1 + rank]
     for _ in range(max(args.warmup, 3)):
         hm.reset()
         hm.generate(prompt, n)
@@ -1003,7 +1015,7 @@ def run_c5(args, rank, world, local_rank):
     tok_s = world * steps * n / (ms / 1e3)
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
-        cpu = c5_cpu_leg(model, toks, bpt, args.cpu_seconds, fp32=not args.dp4a)
+        cpu = c5_cpu_leg(model, toks, bpt, args.cpu_seconds, fp32=not q8)
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = tok_s / world * bpt / 1e9
@@ -1011,22 +1023,27 @@ def run_c5(args, rank, world, local_rank):
             "metric": "hybrid MoE decode tok/s", "value": round(tok_s, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32",
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8" if q8 else "f32",
             "data": "synthetic",
             "config": {"workload": C5_WORKLOAD.format(n=n), "tokens_per_step": n,
                        "n_layers": cfg.n_layers,
-                       "activations": "q8_1 (DP4A)" if args.dp4a else "fp32",
+                       "activations": "q8_1 (DP4A)" if q8 else "fp32",
                        "bytes_per_token": bpt, "us_per_token": round(1e3 * ms / (steps * n), 2),
                        "l2": "inputs larger than L2: ~1.9 GB of weights and states read per token",
-                       "parallelism": f"replicas x{world}", "last_tokens": [int(t) for t in toks[:8]]},
+                       "parallelism": (f"ep{world}: experts of every layer split over the GPUs, "
+                                       "one sequence per GPU, MoE blocks over NVLink peer memory")
+                       if ep else f"replicas x{world}",
+                       "last_tokens": [int(t) for t in toks[:8]]},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                         "traffic": None, "scope": "whole decode step (all kernels)"},
+                         "traffic": None, "scope": "whole decode step (all kernels), per GPU"},
             "clocks": clk.summary(),
             "e2e": {"value": round(tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
             "gpu_launches": steps * n * (1 + 5 * cfg.n_layers + 3), "cpu_baseline": cpu}), flush=True)
     hm.close()
+    if comm is not None:
+        comm.close()
 
 
 def c5_cpu_leg(model, gpu_tokens, bpt, seconds, fp32=True):

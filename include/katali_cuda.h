@@ -372,6 +372,14 @@ int katali_cuda_hybrid_reset(KataliHybrid *m);
 int katali_cuda_hybrid_generate(KataliHybrid *m, const int32_t *prompt, uint32_t n_prompt,
                                 uint32_t n_gen, int32_t *out_tokens);
 int katali_cuda_hybrid_logits(KataliHybrid *m, const float **logits_dev, int32_t *position);
+/* Expert parallelism for the MoE blocks (collective: every rank of ep calls it, then
+ * every rank runs the same sequence of generate calls, each with its own sequence).
+ * Rank r's KataliMoe tables hold experts [r E/G, (r+1) E/G) of every layer (others
+ * NULL); each layer's MoE block then runs as the single-launch expert-parallel layer
+ * over NVLink peer memory (ep in peer-memory mode, katali_cuda_ep_use_peer_memory):
+ * the token's slot goes to the owners of its top-k experts, which return per-slot
+ * partial sums. Needs KATALI_DENSE_Q8_1. ep NULL: back to the local MoE launches. */
+int katali_cuda_hybrid_set_ep(KataliHybrid *m, KataliEp *ep);
 
 /* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */

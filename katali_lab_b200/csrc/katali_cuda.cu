@@ -756,9 +756,11 @@ int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_t
 // The whole layer over peer memory in one launch (dispatch, experts in the fused kernel,
 // return, combine), when the exchange is small enough for it; KATALI_OK when it ran,
 // KATALI_ERR_UNSUPPORTED_SHAPE when the caller should run the three stages instead.
-int moe_ep_layer_fused(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
-                       const float *x, const float *router_logits, float *y, const EpPeer *pp,
-                       double *ret_scratch) {
+// The single-launch expert-parallel layer's parameters (moe_ep_layer_fused without the
+// launch); allocates the layer's routing record on first use, so it runs before any capture.
+int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                        const float *x, const float *router_logits, float *y, const EpPeer *pp,
+                        double *ret_scratch, MoeParams *out, int *grid) {
     int s = ep_check(m, n_ranks, max_tokens);
     if (s) return s;
     if (!pp || !ret_scratch || !ep_fused_ok(m, (int)(n_ranks * max_tokens)))
@@ -808,7 +810,20 @@ int moe_ep_layer_fused(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint
     p.ep_peer_flags = pp->flags;
     p.ep_epoch = pp->epoch;
     p.ep_done = pp->done;
-    return finish(kq::launch_moe_ep_layer(p, m->grid, g_stream));
+    *out = p;
+    *grid = m->grid;
+    return KATALI_OK;
+}
+
+int moe_ep_layer_fused(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                       const float *x, const float *router_logits, float *y, const EpPeer *pp,
+                       double *ret_scratch) {
+    kq::MoeParams p;
+    int grid = 0;
+    const int s = moe_ep_fused_params(m, n_ranks, max_tokens, n_tokens, x, router_logits, y, pp,
+                                      ret_scratch, &p, &grid);
+    if (s) return s;
+    return finish(kq::launch_moe_ep_layer(p, grid, g_stream));
 }
 
 int moe_ep_combine(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,

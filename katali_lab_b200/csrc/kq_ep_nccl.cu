@@ -222,6 +222,36 @@ int peer_setup(KataliEp *ep, uint64_t slot, uint32_t H, uint32_t tmax, cudaStrea
 
 }  // namespace
 
+namespace kq {
+// For a decoder that launches the single-launch expert-parallel layer from its own step
+// (kq_hybrid_api.cu): maps the peer windows (collective on the first call, as the first
+// katali_cuda_moe_ep_layer call) and sizes the per-slot scratch for layer m with max_tokens
+// tokens per rank; returns the communicator's rank count, peer arrays and scratch.
+int ep_peer_prepare(KataliEp *ep, KataliMoe *m, uint32_t max_tokens, uint32_t *n_ranks,
+                    const EpPeer **pp, double **ret) {
+    if (!ep || !m || max_tokens == 0) return KATALI_ERR_BAD_ARG;
+    if (!ep->peer_mode) {
+        set_status_message("expert-parallel decode needs the peer-memory exchange "
+                           "(katali_cuda_ep_use_peer_memory)");
+        return KATALI_ERR_BAD_ARG;
+    }
+    uint64_t slot = 0, rslot = 0;
+    int s = katali_cuda_moe_ep_slot_bytes(m, &slot, &rslot);
+    if (s) return s;
+    cudaStream_t st = current_stream();
+    if ((s = peer_setup(ep, slot, (uint32_t)(rslot / 8), max_tokens, st))) return s;
+    size_t r0 = ep->ret_cap, r1 = ep->ret_cap;
+    if ((s = grow(ep->ret, r0, rslot * max_tokens * ep->n_ranks)) ||
+        (s = grow(ep->back, r1, rslot * max_tokens * ep->n_ranks)))
+        return s;
+    ep->ret_cap = r0 < r1 ? r0 : r1;
+    *n_ranks = (uint32_t)ep->n_ranks;
+    *pp = &ep->peer;
+    *ret = (double *)ep->ret;
+    return KATALI_OK;
+}
+}  // namespace kq
+
 extern "C" {
 
 int katali_cuda_ep_use_peer_memory(KataliEp *ep, int on) {

@@ -320,7 +320,8 @@ cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams
         if ((e = launch_gemv(g[2 * l + 1], mode, st)) != cudaSuccess) return e;
         if ((e = launch_k(router, rgrid, dim3(RW * 32), rt_smem, st, 1, p, L[l])) != cudaSuccess)
             return e;
-        if ((e = launch_moe(moe[l], moe_grid[l], st)) != cudaSuccess) return e;
+        e = p.moe_ep ? launch_moe_ep_layer(moe[l], moe_grid[l], st) : launch_moe(moe[l], moe_grid[l], st);
+        if (e != cudaSuccess) return e;
     }
     if ((e = launch_gemv(g[2 * p.d.NL], mode, st)) != cudaSuccess) return e;
     return launch_dense_argmax(p.d, st, 1);

@@ -17,6 +17,11 @@ cudaStream_t current_stream();
 volatile uint32_t *device_status_word();
 int take_status_after_sync();
 int moe_fused_params(KataliMoe *m, uint32_t mode, MoeParams *p, int *grid);
+int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
+                        const float *x, const float *router_logits, float *y, const EpPeer *pp,
+                        double *ret_scratch, MoeParams *out, int *grid);
+int ep_peer_prepare(KataliEp *ep, KataliMoe *m, uint32_t max_tokens, uint32_t *n_ranks,
+                    const EpPeer **pp, double **ret);
 }  // namespace kq
 
 namespace {
@@ -67,8 +72,10 @@ struct KataliHybrid {
     std::vector<KataliHybridLayerW> lw;
     std::vector<kq::HybridLayer> L;
     std::vector<kq::GemvParams> g;  // 2 per layer + LM head
-    std::vector<kq::MoeParams> moe;
+    std::vector<kq::MoeParams> moe;       // the launches the step uses
     std::vector<int> moe_grid;
+    std::vector<kq::MoeParams> moe_local;  // single-GPU launches (kept while expert-parallel)
+    std::vector<int> grid_local;
     kq::HybridParams p;
     void *mem = nullptr;
     size_t state_off = 0, state_bytes = 0;  // GDN states + conv rings (zeroed by reset)
@@ -321,7 +328,50 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
         float *ys[1] = {p.logits};
         m->g[2 * NL] = gemv_jobs(p.x, H, 1, ws, ts, rows, ys, 0, d->out_norm, d->rms_eps);
     }
+    m->moe_local = m->moe;
+    m->grid_local = m->moe_grid;
     *out = m;
+    return KATALI_OK;
+}
+
+int katali_cuda_hybrid_set_ep(KataliHybrid *m, KataliEp *ep) {
+    if (!m) return KATALI_ERR_BAD_ARG;
+    cudaStream_t st = kq::current_stream();
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return KATALI_ERR_CUDA;
+    if (m->exec) {  // the step's launches change: capture again at the next generate
+        cudaGraphExecDestroy(m->exec);
+        cudaGraphDestroy(m->graph);
+        m->exec = nullptr;
+        m->graph = nullptr;
+    }
+    if (!ep) {
+        m->moe = m->moe_local;
+        m->moe_grid = m->grid_local;
+        m->p.moe_ep = 0;
+        return KATALI_OK;
+    }
+    if (m->p.d.gemv_mode != 0) {
+        kq::set_status_message("katali_cuda_hybrid_set_ep: expert parallelism needs q8_1 activations "
+                               "(KATALI_DENSE_Q8_1)");
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    }
+    std::vector<kq::MoeParams> mp(m->lw.size());
+    std::vector<int> grid(m->lw.size());
+    for (size_t l = 0; l < m->lw.size(); ++l) {
+        uint32_t G = 0;
+        const kq::EpPeer *pp = nullptr;
+        double *ret = nullptr;
+        int s = kq::ep_peer_prepare(ep, m->lw[l].moe, 1, &G, &pp, &ret);
+        if (s) return s;
+        s = kq::moe_ep_fused_params(m->lw[l].moe, G, 1, 1, m->p.d.xb, m->p.rlogits, m->p.d.x, pp,
+                                    ret, &mp[l], &grid[l]);
+        if (s) return s;
+        mp[l].accum = 1;
+    }
+    m->moe = mp;
+    m->moe_grid = grid;
+    m->p.moe_ep = 1;
     return KATALI_OK;
 }
 

@@ -247,6 +247,7 @@ struct HybridParams {
     float *ba;                       // [nv] beta logits, then [nv] decay inputs
     float *go;                       // [nv*dv] gated-norm output of the recurrence
     float *rlogits;                  // [n_experts] router logits
+    int moe_ep;                      // 1: the MoE blocks run expert-parallel over peer memory
 };
 // One decode step: g[2 l], g[2 l + 1] are layer l's input and output projections, g[2 NL]
 // the LM head; moe[l] / moe_grid[l] the layer's fused MoE launch (x = xb, y = x, accum).

@@ -106,6 +106,7 @@
       (m, p, np, ng, o))                                                                      \
     X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
       (m, l, p))                                                                              \
+    X(int, katali_cuda_hybrid_set_ep, (KataliHybrid * m, KataliEp * e), (m, e))               \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -266,6 +267,7 @@ const char *katali_cuda_strerror(int s) {
       (m, p, np, ng, o))                                                                      \
     X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
       (m, l, p))                                                                              \
+    X(int, katali_cuda_hybrid_set_ep, (KataliHybrid * m, KataliEp * e), (m, e))               \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

@@ -148,6 +148,7 @@ class Plugin:
             "katali_cuda_hybrid_reset": ([_vp], _i32),
             "katali_cuda_hybrid_generate": ([_vp, _vp, _u32, _u32, _vp], _i32),
             "katali_cuda_hybrid_logits": ([_vp, C.POINTER(_vp), C.POINTER(_i32)], _i32),
+            "katali_cuda_hybrid_set_ep": ([_vp, _vp], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -386,7 +387,13 @@ class HybridModel:
         ly = (KataliHybridLayerW * cfg.n_layers)()
         for l, w in enumerate(model.layers):
             st = w["experts"]
-            moe = MoeLayer(plugin, cfg.n_experts, cfg.hidden, cfg.ffn, cfg.top_k, st.pointers(),
+            # experts [base, base + n) of the layer are resident here (all of them on one GPU;
+            # this rank's block under expert parallelism); the other table entries stay NULL
+            base = w.get("expert_base", 0)
+            table = [(0, 0, 0)] * cfg.n_experts
+            for i, ptrs in enumerate(st.pointers()):
+                table[base + i] = ptrs
+            moe = MoeLayer(plugin, cfg.n_experts, cfg.hidden, cfg.ffn, cfg.top_k, table,
                            norm_topk=True, gate_type=T["gate"], up_type=T["up"], down_type=T["down"])
             self.moes.append(moe)
             e = KataliHybridLayerW()
@@ -423,6 +430,11 @@ class HybridModel:
 
     def reset(self) -> None:
         self.p.check(self.p.L.katali_cuda_hybrid_reset(self.h))
+
+    def set_ep(self, comm) -> None:
+        """Expert-parallel MoE blocks over `comm` (katali_lab_b200.ep.EpComm in peer-memory
+        mode; collective). None: back to the local MoE launches."""
+        self.p.check(self.p.L.katali_cuda_hybrid_set_ep(self.h, comm.h if comm is not None else None))
 
     def generate(self, prompt, n_gen: int):
         import numpy as np

@@ -218,7 +218,7 @@ class HybridWeights:
             keys = ("ssm_qkv", "ssm_z", "ssm_b", "ssm_a", "ssm_out", "ssm_conv") if w["kind"] == 0 \
                 else ("wq", "wk", "wv", "wo")
             n += sum(w[k].numel() * w[k].element_size() for k in keys)
-            n += w["router"].numel() * 4 + c.top_k * w["experts"].expert_bytes
+            n += w["router"].numel() * 4 + c.top_k * w["experts"].expert_bytes  # top_k experts read
         return n
 
     @property
@@ -229,9 +229,13 @@ class HybridWeights:
         return 2 * n_gdn * c.ssm_v_heads * c.ssm_head_dim * c.ssm_head_dim * 4
 
 
-def make_hybrid_model(plugin: Plugin, cfg: HybridConfig, seed: int, std: float = 0.02) -> HybridWeights:
+def make_hybrid_model(plugin: Plugin, cfg: HybridConfig, seed: int, std: float = 0.02,
+                      ep: tuple | None = None) -> HybridWeights:
     """GGUF matrices ~ N(0, std) encoded on the device; fp32 router rows ~ N(0, std); norm
-    weights 1 + 0.1 N(0, 1); conv taps N(0, 0.3); A_log = log U(1, 16); dt_bias U(-4, -2)."""
+    weights 1 + 0.1 N(0, 1); conv taps N(0, 0.3); A_log = log U(1, 16); dt_bias U(-4, -2).
+    ep = (n_ranks, rank): only this rank's block of n_experts / n_ranks experts per layer is
+    generated (seeded by layer and block, so the ranks together hold one consistent model;
+    the mixer, router and LM-head weights depend on `seed` only)."""
     gen = torch.Generator(device="cuda")
     gen.manual_seed(seed)
     H, T = cfg.hidden, HYBRID_TYPES
@@ -267,10 +271,32 @@ def make_hybrid_model(plugin: Plugin, cfg: HybridConfig, seed: int, std: float =
             w.update({"wq": mat("wq", 2 * QD, H), "wk": mat("wk", KD, H), "wv": mat("wv", KD, H),
                       "wo": mat("wo", H, QD), "q_norm": norm(cfg.head_dim),
                       "k_norm": norm(cfg.head_dim)})
-        w["experts"] = make_expert_store(plugin, cfg.n_experts, H, cfg.ffn, seed=seed * 1000 + l, std=std)
+        if ep is None:
+            w["experts"] = make_expert_store(plugin, cfg.n_experts, H, cfg.ffn, seed=seed * 1000 + l, std=std)
+            w["expert_base"] = 0
+        else:
+            G, r = ep
+            per = cfg.n_experts // G
+            w["experts"] = make_expert_store(plugin, per, H, cfg.ffn, seed=(seed * 1000 + l) * 64 + r, std=std)
+            w["expert_base"] = r * per
         layers.append(w)
     embed = mat("embed", cfg.vocab, H)
     lm_head = mat("lm_head", cfg.vocab, H)
     out_norm = norm(H)
     torch.cuda.synchronize()
     return HybridWeights(cfg, embed, lm_head, out_norm, layers, dict(T))
+
+
+def hybrid_ep_view(model: HybridWeights, n_ranks: int, rank: int) -> HybridWeights:
+    """The same model with only rank's block of every layer's experts (views of the full
+    stores): what one rank of an expert-parallel decoder holds."""
+    per = model.cfg.n_experts // n_ranks
+    layers = []
+    for w in model.layers:
+        st = w["experts"]
+        sl = slice(rank * per, (rank + 1) * per)
+        v = dict(w)
+        v["experts"] = ExpertStore(st.gate[sl], st.up[sl], st.down[sl], st.hidden, st.ffn)
+        v["expert_base"] = rank * per
+        layers.append(v)
+    return HybridWeights(model.cfg, model.embed, model.lm_head, model.out_norm, layers, model.types)
