@@ -382,6 +382,48 @@ int katali_cuda_hybrid_logits(KataliHybrid *m, const float **logits_dev, int32_t
 int katali_cuda_hybrid_set_ep(KataliHybrid *m, KataliEp *ep);
 
 /* ------------------------------------------------------------------------ */
+/* 10. GGUF container: parse a model file and upload tensors to the device in */
+/*     their native block layout (the reference's reader, katali_gguf_open /  */
+/*     katali_gguf_find_tensor / katali_gguf_get_*, V/include/katali_gguf.h:  */
+/*     117-152, V/src/gguf_reader.c:351-545, feeding its backends as           */
+/*     V/src/gguf_model.c:187-227 does). GGUF v2 and v3.                        */
+/* ------------------------------------------------------------------------ */
+typedef struct KataliGguf KataliGguf;
+typedef struct KataliGgufTensorInfo {
+    const char *name;   /* NUL-terminated, owned by the reader until close */
+    uint32_t type;      /* ggml type id */
+    uint32_t n_dims;    /* 1..4 */
+    uint64_t dims[4];   /* dims[0] contiguous; unused dims are 1 */
+    uint64_t offset;    /* absolute file offset of the tensor's bytes */
+    uint64_t nbytes;    /* 0 for a type the reader does not size (not uploadable) */
+} KataliGgufTensorInfo;
+/* Maps the file read-only and parses its directory. A malformed file (bad magic
+ * or version, truncation, nested arrays, misaligned or out-of-range tensor data)
+ * returns KATALI_ERR_BAD_ARG and katali_cuda_status() says why. No GPU needed. */
+int katali_cuda_gguf_open(const char *path, KataliGguf **out);
+int katali_cuda_gguf_close(KataliGguf *g);
+int katali_cuda_gguf_counts(const KataliGguf *g, uint64_t *n_tensors, uint64_t *n_kv,
+                            uint32_t *version);
+int katali_cuda_gguf_tensor(const KataliGguf *g, uint64_t index, KataliGgufTensorInfo *info);
+/* KATALI_ERR_BAD_ARG when no tensor has that name. */
+int katali_cuda_gguf_find(const KataliGguf *g, const char *name, uint64_t *index);
+/* Metadata. get_int: integer and bool scalars; get_float: any numeric scalar;
+ * get_str: string value, not NUL-terminated (len bytes, points into the mapping);
+ * array: element type and count; array_int: element i of an integer array.
+ * A missing key or a type mismatch returns KATALI_ERR_BAD_ARG. */
+int katali_cuda_gguf_get_int(const KataliGguf *g, const char *key, int64_t *value);
+int katali_cuda_gguf_get_float(const KataliGguf *g, const char *key, double *value);
+int katali_cuda_gguf_get_str(const KataliGguf *g, const char *key, const char **value,
+                             uint64_t *len);
+int katali_cuda_gguf_array(const KataliGguf *g, const char *key, uint32_t *elem_type,
+                           uint64_t *count);
+int katali_cuda_gguf_array_int(const KataliGguf *g, const char *key, uint64_t i, int64_t *value);
+/* Copies tensor `index`'s nbytes, unchanged, to device memory dev (e.g. from
+ * katali_cuda_malloc) on the plugin stream through pinned staging buffers;
+ * returns after the copy has finished. */
+int katali_cuda_gguf_upload(KataliGguf *g, uint64_t index, void *dev);
+
+/* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */
 /* ------------------------------------------------------------------------ */
 /* Integer in-block sums of every row against q8_1 xq. Q4_K: per 32-group

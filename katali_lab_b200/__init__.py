@@ -6,7 +6,7 @@ host code, built by ``build.py``) plus the dlopen shim
 (``plugin.py``) for tests, the smoke test and the benchmark.
 """
 from .plugin import (MOE_F32, MOE_NORM_TOPK, MOE_Q8_1, Q4_K, Q6_K, Q8_1, DenseModel,
-                     ExpertCache, HybridModel, KataliError, MoeLayer, Plugin, header_symbols)
+                     ExpertCache, Gguf, HybridModel, KataliError, MoeLayer, Plugin, header_symbols)
 
-__all__ = ["Plugin", "MoeLayer", "ExpertCache", "DenseModel", "HybridModel", "KataliError", "header_symbols", "Q4_K", "Q6_K", "Q8_1",
+__all__ = ["Plugin", "MoeLayer", "ExpertCache", "DenseModel", "HybridModel", "Gguf", "KataliError", "header_symbols", "Q4_K", "Q6_K", "Q8_1",
            "MOE_Q8_1", "MOE_F32", "MOE_NORM_TOPK"]

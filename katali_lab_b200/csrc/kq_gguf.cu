@@ -1,0 +1,400 @@
+// kq_gguf.cu — GGUF container reader and native-layout device upload (katali_cuda_gguf_*).
+//
+// The reference's engine reads GGUF files with its own parser (V/src/gguf_reader.c:351-545,
+// V/include/katali_gguf.h:64-152) and hands tensor bytes to its backends in their native
+// block layout (V/src/gguf_model.c:187-227). Here the same container is parsed on the host
+// from a read-only memory mapping, every read bounds-checked, and a tensor's bytes go to
+// device memory unchanged (GGUF super-blocks are the kernels' layout) through two pinned
+// staging buffers: the CPU copy of chunk i + 1 out of the mapping overlaps the DMA of
+// chunk i on the plugin stream.
+//
+// Container (GGUF v2/v3, little-endian): magic "GGUF", u32 version, u64 tensor count,
+// u64 metadata count; metadata entries (string key, u32 value type, value; arrays carry
+// an element type and u64 count and may not nest); tensor entries (string name, u32 n_dims,
+// u64 dims[n_dims] with dims[0] contiguous, u32 ggml type, u64 offset); the data section
+// starts at the next multiple of general.alignment (default 32) and every tensor offset is
+// relative to it and aligned to it.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <stdio.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <string>
+#include <vector>
+
+#include "katali_cuda.h"
+
+namespace kq {
+void set_status_message(const char *msg);
+cudaStream_t current_stream();
+}  // namespace kq
+
+namespace {
+
+constexpr uint32_t GGUF_MAGIC = 0x46554747u;  // "GGUF"
+enum : uint32_t {
+    V_U8 = 0, V_I8 = 1, V_U16 = 2, V_I16 = 3, V_U32 = 4, V_I32 = 5, V_F32 = 6, V_BOOL = 7,
+    V_STR = 8, V_ARR = 9, V_U64 = 10, V_I64 = 11, V_F64 = 12
+};
+constexpr uint64_t MAX_STR = 1ull << 30;
+constexpr uint32_t MAX_DIMS = 4;
+constexpr size_t STAGE = 32u << 20;  // bytes per pinned staging buffer
+
+// Elements per block and bytes per block of the ggml types this reader sizes; 0: unknown.
+void type_block(uint32_t t, uint64_t &per, uint64_t &bytes) {
+    per = 1;
+    switch (t) {
+        case 0: bytes = 4; return;    // F32
+        case 1: bytes = 2; return;    // F16
+        case 2: per = 32; bytes = 18; return;    // Q4_0
+        case 3: per = 32; bytes = 20; return;    // Q4_1
+        case 6: per = 32; bytes = 22; return;    // Q5_0
+        case 7: per = 32; bytes = 24; return;    // Q5_1
+        case 8: per = 32; bytes = 34; return;    // Q8_0
+        case 9: per = 32; bytes = 36; return;    // Q8_1
+        case 10: per = 256; bytes = 84; return;  // Q2_K
+        case 11: per = 256; bytes = 110; return; // Q3_K
+        case 12: per = 256; bytes = 144; return; // Q4_K
+        case 13: per = 256; bytes = 176; return; // Q5_K
+        case 14: per = 256; bytes = 210; return; // Q6_K
+        case 15: per = 256; bytes = 292; return; // Q8_K
+        case 24: bytes = 1; return;   // I8
+        case 25: bytes = 2; return;   // I16
+        case 26: bytes = 4; return;   // I32
+        case 27: bytes = 8; return;   // I64
+        case 28: bytes = 8; return;   // F64
+        case 30: bytes = 2; return;   // BF16
+        default: bytes = 0; return;
+    }
+}
+
+struct Kv {
+    std::string key;
+    uint32_t type = 0, elem = 0;  // elem: array element type
+    uint64_t count = 0;           // array length
+    uint64_t pos = 0;             // file offset of the value (array: of its first element)
+};
+
+struct Tensor {
+    std::string name;
+    uint32_t n_dims = 0, type = 0;
+    uint64_t dims[MAX_DIMS] = {1, 1, 1, 1};
+    uint64_t rel = 0, abs = 0, nbytes = 0;
+};
+
+struct Cursor {
+    const uint8_t *p;
+    uint64_t size, at;
+    bool ok = true;
+    bool need(uint64_t n) {
+        if (!ok || n > size - at) ok = false;
+        return ok;
+    }
+    template <typename T>
+    T get() {
+        T v{};
+        if (need(sizeof(T))) {
+            memcpy(&v, p + at, sizeof(T));
+            at += sizeof(T);
+        }
+        return v;
+    }
+    bool str(std::string *out) {
+        const uint64_t n = get<uint64_t>();
+        if (!ok || n > MAX_STR || !need(n)) return ok = false;
+        if (out) out->assign(reinterpret_cast<const char *>(p + at), (size_t)n);
+        at += n;
+        return true;
+    }
+};
+
+uint64_t scalar_size(uint32_t t) {
+    switch (t) {
+        case V_U8: case V_I8: case V_BOOL: return 1;
+        case V_U16: case V_I16: return 2;
+        case V_U32: case V_I32: case V_F32: return 4;
+        case V_U64: case V_I64: case V_F64: return 8;
+        default: return 0;
+    }
+}
+
+}  // namespace
+
+struct KataliGguf {
+    int fd = -1;
+    const uint8_t *map = nullptr;
+    uint64_t size = 0;
+    uint32_t version = 0;
+    uint64_t alignment = 32, data_off = 0;
+    std::vector<Kv> kv;
+    std::vector<Tensor> t;
+    void *stage[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+};
+
+namespace {
+
+int fail(KataliGguf *g, const char *why) {
+    kq::set_status_message(why);
+    if (g) katali_cuda_gguf_close(g);
+    return KATALI_ERR_BAD_ARG;
+}
+
+const Kv *find_kv(const KataliGguf *g, const char *key) {
+    for (const Kv &k : g->kv)
+        if (k.key == key) return &k;
+    return nullptr;
+}
+
+bool read_scalar(const KataliGguf *g, const Kv &k, uint32_t type, uint64_t pos, int64_t *iv, double *fv) {
+    const uint8_t *q = g->map + pos;
+    switch (type) {
+        case V_U8: *iv = q[0]; break;
+        case V_I8: *iv = (int8_t)q[0]; break;
+        case V_BOOL: *iv = q[0] != 0; break;
+        case V_U16: { uint16_t v; memcpy(&v, q, 2); *iv = v; break; }
+        case V_I16: { int16_t v; memcpy(&v, q, 2); *iv = v; break; }
+        case V_U32: { uint32_t v; memcpy(&v, q, 4); *iv = v; break; }
+        case V_I32: { int32_t v; memcpy(&v, q, 4); *iv = v; break; }
+        case V_U64: { uint64_t v; memcpy(&v, q, 8); *iv = (int64_t)v; break; }
+        case V_I64: { int64_t v; memcpy(&v, q, 8); *iv = v; break; }
+        case V_F32: { float v; memcpy(&v, q, 4); *fv = v; return true; }
+        case V_F64: { double v; memcpy(&v, q, 8); *fv = v; return true; }
+        default: return false;
+    }
+    *fv = (double)*iv;
+    (void)k;
+    return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int katali_cuda_gguf_open(const char *path, KataliGguf **out) {
+    if (!path || !out) return KATALI_ERR_BAD_ARG;
+    *out = nullptr;
+    KataliGguf *g = new KataliGguf();
+    g->fd = open(path, O_RDONLY | O_CLOEXEC);
+    if (g->fd < 0) return fail(g, "katali_cuda_gguf_open: cannot open the file");
+    struct stat st;
+    if (fstat(g->fd, &st) != 0 || st.st_size < 24) return fail(g, "katali_cuda_gguf_open: not a GGUF file (too short)");
+    g->size = (uint64_t)st.st_size;
+    void *m = mmap(nullptr, (size_t)g->size, PROT_READ, MAP_PRIVATE, g->fd, 0);
+    if (m == MAP_FAILED) return fail(g, "katali_cuda_gguf_open: mmap failed");
+    g->map = (const uint8_t *)m;
+    Cursor c{g->map, g->size, 0};
+    if (c.get<uint32_t>() != GGUF_MAGIC) return fail(g, "katali_cuda_gguf_open: bad magic");
+    g->version = c.get<uint32_t>();
+    if (g->version != 2 && g->version != 3) return fail(g, "katali_cuda_gguf_open: unsupported GGUF version");
+    const uint64_t nt = c.get<uint64_t>(), nkv = c.get<uint64_t>();
+    // every entry needs at least 8 (string length) + 4 bytes: bounds the counts
+    if (!c.ok || nt > g->size / 12 || nkv > g->size / 12) return fail(g, "katali_cuda_gguf_open: bad counts");
+    g->kv.resize((size_t)nkv);
+    for (Kv &k : g->kv) {
+        if (!c.str(&k.key)) return fail(g, "katali_cuda_gguf_open: truncated metadata key");
+        k.type = c.get<uint32_t>();
+        if (!c.ok) return fail(g, "katali_cuda_gguf_open: truncated metadata");
+        if (k.type == V_STR) {
+            k.pos = c.at;
+            if (!c.str(nullptr)) return fail(g, "katali_cuda_gguf_open: truncated string value");
+        } else if (k.type == V_ARR) {
+            k.elem = c.get<uint32_t>();
+            k.count = c.get<uint64_t>();
+            if (!c.ok) return fail(g, "katali_cuda_gguf_open: truncated array");
+            if (k.elem == V_ARR) return fail(g, "katali_cuda_gguf_open: nested metadata array");
+            k.pos = c.at;
+            if (k.elem == V_STR) {
+                if (k.count > (g->size - c.at) / 8) return fail(g, "katali_cuda_gguf_open: bad array length");
+                for (uint64_t i = 0; i < k.count; ++i)
+                    if (!c.str(nullptr)) return fail(g, "katali_cuda_gguf_open: truncated string array");
+            } else {
+                const uint64_t es = scalar_size(k.elem);
+                if (!es) return fail(g, "katali_cuda_gguf_open: bad array element type");
+                if (k.count > (g->size - c.at) / es || !c.need(k.count * es))
+                    return fail(g, "katali_cuda_gguf_open: truncated array");
+                c.at += k.count * es;
+            }
+        } else {
+            const uint64_t es = scalar_size(k.type);
+            if (!es) return fail(g, "katali_cuda_gguf_open: bad metadata value type");
+            k.pos = c.at;
+            if (!c.need(es)) return fail(g, "katali_cuda_gguf_open: truncated metadata value");
+            c.at += es;
+        }
+    }
+    if (const Kv *a = find_kv(g, "general.alignment")) {
+        int64_t iv = 0;
+        double fv = 0;
+        if (a->type == V_ARR || a->type == V_STR || !read_scalar(g, *a, a->type, a->pos, &iv, &fv) ||
+            iv <= 0 || (iv & (iv - 1)) != 0)
+            return fail(g, "katali_cuda_gguf_open: bad general.alignment");
+        g->alignment = (uint64_t)iv;
+    }
+    g->t.resize((size_t)nt);
+    for (Tensor &t : g->t) {
+        if (!c.str(&t.name)) return fail(g, "katali_cuda_gguf_open: truncated tensor name");
+        t.n_dims = c.get<uint32_t>();
+        if (!c.ok || t.n_dims == 0 || t.n_dims > MAX_DIMS) return fail(g, "katali_cuda_gguf_open: bad tensor rank");
+        for (uint32_t d = 0; d < t.n_dims; ++d) t.dims[d] = c.get<uint64_t>();
+        t.type = c.get<uint32_t>();
+        t.rel = c.get<uint64_t>();
+        if (!c.ok) return fail(g, "katali_cuda_gguf_open: truncated tensor entry");
+    }
+    g->data_off = (c.at + g->alignment - 1) / g->alignment * g->alignment;
+    if (g->data_off > g->size) return fail(g, "katali_cuda_gguf_open: truncated before the data section");
+    for (Tensor &t : g->t) {
+        uint64_t n = 1;
+        for (uint32_t d = 0; d < t.n_dims; ++d) {
+            if (t.dims[d] == 0 || n > UINT64_MAX / t.dims[d]) return fail(g, "katali_cuda_gguf_open: bad tensor dims");
+            n *= t.dims[d];
+        }
+        if (t.rel % g->alignment) return fail(g, "katali_cuda_gguf_open: misaligned tensor offset");
+        uint64_t per, bytes;
+        type_block(t.type, per, bytes);
+        if (bytes && t.dims[0] % per == 0) {
+            const uint64_t rb = t.dims[0] / per * bytes;
+            if (n / t.dims[0] > UINT64_MAX / rb) return fail(g, "katali_cuda_gguf_open: tensor too large");
+            t.nbytes = rb * (n / t.dims[0]);
+        }
+        if (t.rel > g->size - g->data_off || t.nbytes > g->size - g->data_off - t.rel)
+            return fail(g, "katali_cuda_gguf_open: tensor data out of range");
+        t.abs = g->data_off + t.rel;
+    }
+    *out = g;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_close(KataliGguf *g) {
+    if (!g) return KATALI_OK;
+    for (int i = 0; i < 2; ++i) {
+        if (g->done[i]) {
+            cudaEventSynchronize(g->done[i]);
+            cudaEventDestroy(g->done[i]);
+        }
+        if (g->stage[i]) cudaFreeHost(g->stage[i]);
+    }
+    if (g->map) munmap((void *)g->map, (size_t)g->size);
+    if (g->fd >= 0) close(g->fd);
+    delete g;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_counts(const KataliGguf *g, uint64_t *n_tensors, uint64_t *n_kv, uint32_t *version) {
+    if (!g) return KATALI_ERR_BAD_ARG;
+    if (n_tensors) *n_tensors = g->t.size();
+    if (n_kv) *n_kv = g->kv.size();
+    if (version) *version = g->version;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_tensor(const KataliGguf *g, uint64_t i, KataliGgufTensorInfo *info) {
+    if (!g || !info || i >= g->t.size()) return KATALI_ERR_BAD_ARG;
+    const Tensor &t = g->t[(size_t)i];
+    info->name = t.name.c_str();
+    info->type = t.type;
+    info->n_dims = t.n_dims;
+    for (uint32_t d = 0; d < 4; ++d) info->dims[d] = t.dims[d];
+    info->offset = t.abs;
+    info->nbytes = t.nbytes;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_find(const KataliGguf *g, const char *name, uint64_t *index) {
+    if (!g || !name || !index) return KATALI_ERR_BAD_ARG;
+    for (size_t i = 0; i < g->t.size(); ++i)
+        if (g->t[i].name == name) {
+            *index = i;
+            return KATALI_OK;
+        }
+    kq::set_status_message("katali_cuda_gguf_find: no tensor of that name");
+    return KATALI_ERR_BAD_ARG;
+}
+
+int katali_cuda_gguf_get_int(const KataliGguf *g, const char *key, int64_t *v) {
+    if (!g || !key || !v) return KATALI_ERR_BAD_ARG;
+    const Kv *k = find_kv(g, key);
+    double fv = 0;
+    if (!k || k->type == V_ARR || k->type == V_STR || k->type == V_F32 || k->type == V_F64 ||
+        !read_scalar(g, *k, k->type, k->pos, v, &fv))
+        return KATALI_ERR_BAD_ARG;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_get_float(const KataliGguf *g, const char *key, double *v) {
+    if (!g || !key || !v) return KATALI_ERR_BAD_ARG;
+    const Kv *k = find_kv(g, key);
+    int64_t iv = 0;
+    if (!k || k->type == V_ARR || k->type == V_STR || !read_scalar(g, *k, k->type, k->pos, &iv, v))
+        return KATALI_ERR_BAD_ARG;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_get_str(const KataliGguf *g, const char *key, const char **s, uint64_t *len) {
+    if (!g || !key || !s) return KATALI_ERR_BAD_ARG;
+    const Kv *k = find_kv(g, key);
+    if (!k || k->type != V_STR) return KATALI_ERR_BAD_ARG;
+    uint64_t n;
+    memcpy(&n, g->map + k->pos, 8);
+    *s = reinterpret_cast<const char *>(g->map + k->pos + 8);
+    if (len) *len = n;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_array(const KataliGguf *g, const char *key, uint32_t *elem_type, uint64_t *count) {
+    if (!g || !key) return KATALI_ERR_BAD_ARG;
+    const Kv *k = find_kv(g, key);
+    if (!k || k->type != V_ARR) return KATALI_ERR_BAD_ARG;
+    if (elem_type) *elem_type = k->elem;
+    if (count) *count = k->count;
+    return KATALI_OK;
+}
+
+int katali_cuda_gguf_array_int(const KataliGguf *g, const char *key, uint64_t i, int64_t *v) {
+    if (!g || !key || !v) return KATALI_ERR_BAD_ARG;
+    const Kv *k = find_kv(g, key);
+    double fv = 0;
+    if (!k || k->type != V_ARR || i >= k->count || k->elem == V_STR || k->elem == V_F32 ||
+        k->elem == V_F64)
+        return KATALI_ERR_BAD_ARG;
+    return read_scalar(g, *k, k->elem, k->pos + i * scalar_size(k->elem), v, &fv) ? KATALI_OK
+                                                                                  : KATALI_ERR_BAD_ARG;
+}
+
+int katali_cuda_gguf_upload(KataliGguf *g, uint64_t i, void *dev) {
+    if (!g || !dev || i >= g->t.size()) return KATALI_ERR_BAD_ARG;
+    const Tensor &t = g->t[(size_t)i];
+    if (!t.nbytes) {
+        kq::set_status_message("katali_cuda_gguf_upload: tensor type not sized by this reader");
+        return KATALI_ERR_UNSUPPORTED_TYPE;
+    }
+    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    cudaError_t e = cudaSuccess;
+    for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+        if (!g->stage[b]) e = cudaHostAlloc(&g->stage[b], STAGE, cudaHostAllocDefault);
+        if (e == cudaSuccess && !g->done[b]) e = cudaEventCreateWithFlags(&g->done[b], cudaEventDisableTiming);
+    }
+    cudaStream_t st = kq::current_stream();
+    const uint8_t *src = g->map + t.abs;
+    uint8_t *dst = static_cast<uint8_t *>(dev);
+    for (uint64_t off = 0, c = 0; e == cudaSuccess && off < t.nbytes; off += STAGE, ++c) {
+        const int b = (int)(c & 1);
+        const size_t n = (size_t)(t.nbytes - off < STAGE ? t.nbytes - off : STAGE);
+        e = cudaEventSynchronize(g->done[b]);  // the DMA out of this buffer two chunks ago
+        if (e != cudaSuccess) break;
+        memcpy(g->stage[b], src + off, n);     // page faults pull the file in here
+        e = cudaMemcpyAsync(dst + off, g->stage[b], n, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(g->done[b], st);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        kq::set_status_message(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
+    }
+    return KATALI_OK;
+}
+
+}  // extern "C"

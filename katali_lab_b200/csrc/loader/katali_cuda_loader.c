@@ -107,6 +107,25 @@
     X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
       (m, l, p))                                                                              \
     X(int, katali_cuda_hybrid_set_ep, (KataliHybrid * m, KataliEp * e), (m, e))               \
+    X(int, katali_cuda_gguf_open, (const char *p, KataliGguf **o), (p, o))                    \
+    X(int, katali_cuda_gguf_close, (KataliGguf * g), (g))                                     \
+    X(int, katali_cuda_gguf_counts, (const KataliGguf *g, uint64_t *t, uint64_t *k,          \
+                                     uint32_t *v),                                            \
+      (g, t, k, v))                                                                           \
+    X(int, katali_cuda_gguf_tensor, (const KataliGguf *g, uint64_t i, KataliGgufTensorInfo *o), \
+      (g, i, o))                                                                              \
+    X(int, katali_cuda_gguf_find, (const KataliGguf *g, const char *n, uint64_t *i), (g, n, i)) \
+    X(int, katali_cuda_gguf_get_int, (const KataliGguf *g, const char *k, int64_t *v), (g, k, v)) \
+    X(int, katali_cuda_gguf_get_float, (const KataliGguf *g, const char *k, double *v),      \
+      (g, k, v))                                                                              \
+    X(int, katali_cuda_gguf_get_str,                                                          \
+      (const KataliGguf *g, const char *k, const char **v, uint64_t *n), (g, k, v, n))        \
+    X(int, katali_cuda_gguf_array, (const KataliGguf *g, const char *k, uint32_t *t,         \
+                                    uint64_t *n),                                             \
+      (g, k, t, n))                                                                           \
+    X(int, katali_cuda_gguf_array_int,                                                        \
+      (const KataliGguf *g, const char *k, uint64_t i, int64_t *v), (g, k, i, v))             \
+    X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -268,6 +287,25 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_hybrid_logits, (KataliHybrid * m, const float **l, int32_t *p),        \
       (m, l, p))                                                                              \
     X(int, katali_cuda_hybrid_set_ep, (KataliHybrid * m, KataliEp * e), (m, e))               \
+    X(int, katali_cuda_gguf_open, (const char *p, KataliGguf **o), (p, o))                    \
+    X(int, katali_cuda_gguf_close, (KataliGguf * g), (g))                                     \
+    X(int, katali_cuda_gguf_counts, (const KataliGguf *g, uint64_t *t, uint64_t *k,          \
+                                     uint32_t *v),                                            \
+      (g, t, k, v))                                                                           \
+    X(int, katali_cuda_gguf_tensor, (const KataliGguf *g, uint64_t i, KataliGgufTensorInfo *o), \
+      (g, i, o))                                                                              \
+    X(int, katali_cuda_gguf_find, (const KataliGguf *g, const char *n, uint64_t *i), (g, n, i)) \
+    X(int, katali_cuda_gguf_get_int, (const KataliGguf *g, const char *k, int64_t *v), (g, k, v)) \
+    X(int, katali_cuda_gguf_get_float, (const KataliGguf *g, const char *k, double *v),      \
+      (g, k, v))                                                                              \
+    X(int, katali_cuda_gguf_get_str,                                                          \
+      (const KataliGguf *g, const char *k, const char **v, uint64_t *n), (g, k, v, n))        \
+    X(int, katali_cuda_gguf_array, (const KataliGguf *g, const char *k, uint32_t *t,         \
+                                    uint64_t *n),                                             \
+      (g, k, t, n))                                                                           \
+    X(int, katali_cuda_gguf_array_int,                                                        \
+      (const KataliGguf *g, const char *k, uint64_t i, int64_t *v), (g, k, i, v))             \
+    X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

@@ -65,6 +65,11 @@ class KataliHybridDesc(C.Structure):
                 ("layers", C.POINTER(KataliHybridLayerW)), ("flags", _u32)]
 
 
+class KataliGgufTensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("type", _u32), ("n_dims", _u32), ("dims", _u64 * 4),
+                ("offset", _u64), ("nbytes", _u64)]
+
+
 class KataliMoeDesc(C.Structure):
     _fields_ = [("n_experts", _u32), ("hidden", _u32), ("ffn", _u32), ("top_k", _u32),
                 ("gate_type", _u32), ("up_type", _u32), ("down_type", _u32), ("flags", _u32),
@@ -149,6 +154,17 @@ class Plugin:
             "katali_cuda_hybrid_generate": ([_vp, _vp, _u32, _u32, _vp], _i32),
             "katali_cuda_hybrid_logits": ([_vp, C.POINTER(_vp), C.POINTER(_i32)], _i32),
             "katali_cuda_hybrid_set_ep": ([_vp, _vp], _i32),
+            "katali_cuda_gguf_open": ([C.c_char_p, C.POINTER(_vp)], _i32),
+            "katali_cuda_gguf_close": ([_vp], _i32),
+            "katali_cuda_gguf_counts": ([_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u32)], _i32),
+            "katali_cuda_gguf_tensor": ([_vp, _u64, C.POINTER(KataliGgufTensorInfo)], _i32),
+            "katali_cuda_gguf_find": ([_vp, C.c_char_p, C.POINTER(_u64)], _i32),
+            "katali_cuda_gguf_get_int": ([_vp, C.c_char_p, C.POINTER(C.c_int64)], _i32),
+            "katali_cuda_gguf_get_float": ([_vp, C.c_char_p, C.POINTER(C.c_double)], _i32),
+            "katali_cuda_gguf_get_str": ([_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_u64)], _i32),
+            "katali_cuda_gguf_array": ([_vp, C.c_char_p, C.POINTER(_u32), C.POINTER(_u64)], _i32),
+            "katali_cuda_gguf_array_int": ([_vp, C.c_char_p, _u64, C.POINTER(C.c_int64)], _i32),
+            "katali_cuda_gguf_upload": ([_vp, _u64, _vp], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -457,3 +473,63 @@ class HybridModel:
         for m in self.moes:
             m.close()
         self.moes = []
+
+
+class Gguf:
+    """A GGUF model file parsed by the plugin (katali_cuda_gguf_*); tensors upload to the
+    device in their native block layout."""
+
+    def __init__(self, plugin: Plugin, path: str):
+        self.p = plugin
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_gguf_open(os.fsencode(path), C.byref(h)))
+        self.h = h
+        nt, nkv, ver = _u64(), _u64(), _u32()
+        plugin.check(plugin.L.katali_cuda_gguf_counts(h, C.byref(nt), C.byref(nkv), C.byref(ver)))
+        self.n_tensors, self.n_kv, self.version = nt.value, nkv.value, ver.value
+
+    def tensor(self, i: int) -> dict:
+        info = KataliGgufTensorInfo()
+        self.p.check(self.p.L.katali_cuda_gguf_tensor(self.h, i, C.byref(info)))
+        return {"name": info.name.decode(), "type": info.type, "n_dims": info.n_dims,
+                "dims": tuple(info.dims[:info.n_dims]), "offset": info.offset, "nbytes": info.nbytes}
+
+    def tensors(self) -> list:
+        return [self.tensor(i) for i in range(self.n_tensors)]
+
+    def find(self, name: str) -> int | None:
+        i = _u64()
+        rc = self.p.L.katali_cuda_gguf_find(self.h, name.encode(), C.byref(i))
+        return i.value if rc == 0 else None
+
+    def get_int(self, key: str):
+        v = C.c_int64()
+        return v.value if self.p.L.katali_cuda_gguf_get_int(self.h, key.encode(), C.byref(v)) == 0 else None
+
+    def get_float(self, key: str):
+        v = C.c_double()
+        return v.value if self.p.L.katali_cuda_gguf_get_float(self.h, key.encode(), C.byref(v)) == 0 else None
+
+    def get_str(self, key: str):
+        ptr, n = _vp(), _u64()
+        if self.p.L.katali_cuda_gguf_get_str(self.h, key.encode(), C.byref(ptr), C.byref(n)) != 0:
+            return None
+        return C.string_at(ptr.value, n.value).decode()
+
+    def array(self, key: str):
+        et, n = _u32(), _u64()
+        if self.p.L.katali_cuda_gguf_array(self.h, key.encode(), C.byref(et), C.byref(n)) != 0:
+            return None
+        return et.value, n.value
+
+    def array_int(self, key: str, i: int):
+        v = C.c_int64()
+        return v.value if self.p.L.katali_cuda_gguf_array_int(self.h, key.encode(), i, C.byref(v)) == 0 else None
+
+    def upload(self, i: int, dev) -> None:
+        self.p.check(self.p.L.katali_cuda_gguf_upload(self.h, i, _ptr(dev)))
+
+    def close(self) -> None:
+        if self.h:
+            self.p.L.katali_cuda_gguf_close(self.h)
+            self.h = None

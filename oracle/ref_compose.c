@@ -537,3 +537,65 @@ int kref_gdn_apply(int nk, int nv, int dh, int K, int T, float eps, const float 
     free(m.qkv); free(m.cv); free(m.z); free(m.b); free(m.a); free(m.tmp); free(ring); free(state);
     return rc;
 }
+
+/* ------------------------------------------------------------------------ */
+/* The reference's GGUF reader (V/src/gguf_reader.c, katali_gguf_open and the */
+/* getters of V/include/katali_gguf.h:117-152) behind a handle, so the tests  */
+/* can compare the plugin's reader with it on the same files.                 */
+/* ------------------------------------------------------------------------ */
+#include "katali_gguf.h"
+
+void *kref_gguf_open(const char *path, char *err, int err_cap) {
+    KataliGgufFile *f = (KataliGgufFile *)calloc(1, sizeof(*f));
+    if (!f) return NULL;
+    if (katali_gguf_open(f, path, 1, err, (size_t)err_cap) != 0) {
+        free(f);
+        return NULL;
+    }
+    return f;
+}
+
+void kref_gguf_close(void *p) {
+    if (!p) return;
+    katali_gguf_close((KataliGgufFile *)p);
+    free(p);
+}
+
+void kref_gguf_counts(void *p, uint64_t *nt, uint64_t *nkv, uint32_t *version) {
+    const KataliGgufFile *f = (const KataliGgufFile *)p;
+    *nt = f->tensor_count;
+    *nkv = f->kv_count;
+    *version = f->version;
+}
+
+/* Tensor i: name, type, n_dims, dims[4], absolute file offset of its data (or 0 when
+ * the reader exposes no data pointer), nbytes. */
+int kref_gguf_tensor(void *p, uint64_t i, const char **name, uint32_t *type, uint32_t *n_dims,
+                     uint64_t *dims, uint64_t *abs_off, uint64_t *nbytes) {
+    const KataliGgufFile *f = (const KataliGgufFile *)p;
+    if (i >= f->tensor_count) return -1;
+    const KataliGgufTensor *t = &f->tensors[i];
+    *name = t->name;
+    *type = t->type;
+    *n_dims = t->n_dims;
+    for (uint32_t d = 0; d < 4; d++) dims[d] = d < t->n_dims ? t->dims[d] : 1;
+    *abs_off = t->data ? (uint64_t)(t->data - f->map) : 0;
+    *nbytes = t->nbytes;
+    return 0;
+}
+
+int64_t kref_gguf_get_int(void *p, const char *key, int64_t def) {
+    return katali_gguf_get_int((const KataliGgufFile *)p, key, def);
+}
+double kref_gguf_get_float(void *p, const char *key, double def) {
+    return katali_gguf_get_float((const KataliGgufFile *)p, key, def);
+}
+const char *kref_gguf_get_str(void *p, const char *key, size_t *len) {
+    return katali_gguf_get_str((const KataliGgufFile *)p, key, NULL, len);
+}
+int64_t kref_gguf_array_len(void *p, const char *key, uint32_t *et) {
+    return katali_gguf_array_len((const KataliGgufFile *)p, key, et);
+}
+int64_t kref_gguf_array_int(void *p, const char *key, uint64_t i) {
+    return katali_gguf_array_int((const KataliGgufFile *)p, key, i);
+}

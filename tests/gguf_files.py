@@ -1,0 +1,119 @@
+"""A GGUF v2/v3 writer for tests (test infrastructure): metadata of every value type,
+tensors of any ggml type id with caller-given bytes, optional general.alignment, and the
+malformed variants the readers must reject."""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+
+U8, I8, U16, I16, U32, I32, F32, BOOL, STR, ARR, U64, I64, F64 = range(13)
+_FMT = {U8: "<B", I8: "<b", U16: "<H", I16: "<h", U32: "<I", I32: "<i", F32: "<f", BOOL: "<B",
+        U64: "<Q", I64: "<q", F64: "<d"}
+
+
+def _s(b: bytes | str) -> bytes:
+    b = b.encode() if isinstance(b, str) else b
+    return struct.pack("<Q", len(b)) + b
+
+
+def _value(vtype, v) -> bytes:
+    if vtype == STR:
+        return _s(v)
+    if vtype == ARR:
+        et, items = v
+        out = struct.pack("<IQ", et, len(items))
+        return out + b"".join(_value(et, x) for x in items)
+    return struct.pack(_FMT[vtype], v)
+
+
+def build(kvs, tensors, version=3, alignment=None):
+    """kvs: [(key, vtype, value)] (ARR value = (elem_type, items)); tensors:
+    [(name, ggml_type, dims, data_bytes)] with dims[0] contiguous. Returns (file bytes,
+    {name: absolute data offset})."""
+    kvs = list(kvs)
+    align = 32
+    if alignment is not None:
+        kvs.append(("general.alignment", U32, alignment))
+        align = alignment
+    head = struct.pack("<IIQQ", 0x46554747, version, len(tensors), len(kvs))
+    head += b"".join(_s(k) + struct.pack("<I", t) + _value(t, v) for k, t, v in kvs)
+    rel, off = [], 0
+    for _, _, _, data in tensors:
+        rel.append(off)
+        off += (len(data) + align - 1) // align * align
+    for (name, gt, dims, _), r in zip(tensors, rel):
+        head += _s(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}Q", *dims)
+        head += struct.pack("<IQ", gt, r)
+    data_off = (len(head) + align - 1) // align * align
+    body = bytearray(head + b"\0" * (data_off - len(head)))
+    for (_, _, _, data), r in zip(tensors, rel):
+        body += b"\0" * (data_off + r - len(body)) + bytes(data)
+    offsets = {t[0]: data_off + r for t, r in zip(tensors, rel)}
+    return bytes(body), offsets
+
+
+def sample_file(alignment=None, version=3, extra_tensors=()):
+    """Metadata of every type and F32 / Q4_K / Q6_K / Q8_0 / unknown-type tensors."""
+    rng = np.random.default_rng(5)
+    kvs = [("general.architecture", STR, "qwen3"), ("qwen3.block_count", U32, 2),
+           ("qwen3.rope.freq_base", F32, 1e6), ("general.flag", BOOL, 1), ("t.u8", U8, 200),
+           ("t.i8", I8, -5), ("t.u16", U16, 60000), ("t.i16", I16, -30000), ("t.i32", I32, -7),
+           ("t.u64", U64, 1 << 40), ("t.i64", I64, -(1 << 40)), ("t.f64", F64, 0.125),
+           ("tokenizer.ggml.tokens", ARR, (STR, ["a", "bb", "ccc"])),
+           ("test.nums", ARR, (I32, [10, 20, 30])), ("test.u8s", ARR, (U8, [1, 2, 250]))]
+    tensors = [("odd.weight", 200, (16,), b"\1" * 16),
+               ("f32.weight", 0, (8, 3), rng.normal(0, 1, 24).astype(np.float32).tobytes()),
+               ("q4k.weight", 12, (512, 3), rng.integers(0, 256, 2 * 144 * 3, dtype=np.uint8).tobytes()),
+               ("q6k.weight", 14, (256, 5), rng.integers(0, 256, 210 * 5, dtype=np.uint8).tobytes()),
+               ("q80.weight", 8, (64, 2), rng.integers(0, 256, 2 * 34 * 2, dtype=np.uint8).tobytes())
+               ] + list(extra_tensors)
+    return build(kvs, tensors, version=version, alignment=alignment)
+
+
+def malformed():
+    """(reason, file bytes) pairs every reader must reject."""
+    good, _ = sample_file()
+    out = [("bad magic", b"X" + good[1:]),
+           ("bad version", good[:4] + struct.pack("<I", 99) + good[8:]),
+           ("truncated", good[:-8])]
+    far, _ = build([], [("t0", 0, (4, 2), np.zeros(8, np.float32).tobytes())])
+    # patch the single tensor's offset (last 8 bytes of its entry) far past the end
+    i = far.index(b"t0") + 2 + 4 + 16 + 4
+    out.append(("out-of-range offset", far[:i] + struct.pack("<Q", 1 << 40) + far[i + 8:]))
+    nested = struct.pack("<IIQQ", 0x46554747, 3, 0, 1) + _s("bad") + struct.pack("<IIQ", ARR, ARR, 1)
+    out.append(("nested array", nested))
+    return out
+
+
+def dense_model_file(port, cfg, seed=0, std=0.02):
+    """A Qwen3-layout dense model (llama.cpp tensor names) with weights ~ N(0, std) encoded
+    by the oracle's encoder: Q4_K, with Q6_K attn_v / ffn_down / output; fp32 norms."""
+    from oracle.oracle import Q4_K, Q6_K
+    rng = np.random.default_rng(seed)
+    H, F, NH, NKV, HD = cfg.hidden, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+
+    def mat(qt, rows, cols):
+        return (qt, (cols, rows), port.quantize(qt, rng.normal(0, std, (rows, cols)).astype(np.float32)).tobytes())
+
+    def norm(n):
+        return (0, (n,), (1.0 + 0.1 * rng.normal(0, 1, n)).astype(np.float32).tobytes())
+
+    ts = [("token_embd.weight",) + mat(Q4_K, cfg.vocab, H)]
+    for l in range(cfg.n_layers):
+        p = f"blk.{l}."
+        ts += [(p + "attn_norm.weight",) + norm(H), (p + "attn_q.weight",) + mat(Q4_K, NH * HD, H),
+               (p + "attn_k.weight",) + mat(Q4_K, NKV * HD, H), (p + "attn_v.weight",) + mat(Q6_K, NKV * HD, H),
+               (p + "attn_output.weight",) + mat(Q4_K, H, NH * HD), (p + "attn_q_norm.weight",) + norm(HD),
+               (p + "attn_k_norm.weight",) + norm(HD), (p + "ffn_norm.weight",) + norm(H),
+               (p + "ffn_gate.weight",) + mat(Q4_K, F, H), (p + "ffn_up.weight",) + mat(Q4_K, F, H),
+               (p + "ffn_down.weight",) + mat(Q6_K, H, F)]
+    ts += [("output_norm.weight",) + norm(H), ("output.weight",) + mat(Q6_K, cfg.vocab, H)]
+    kvs = [("general.architecture", STR, "qwen3"), ("qwen3.block_count", U32, cfg.n_layers),
+           ("qwen3.embedding_length", U32, H), ("qwen3.feed_forward_length", U32, F),
+           ("qwen3.attention.head_count", U32, NH), ("qwen3.attention.head_count_kv", U32, NKV),
+           ("qwen3.attention.key_length", U32, HD), ("qwen3.context_length", U32, cfg.kv_cap),
+           ("qwen3.rope.freq_base", F32, cfg.rope_theta),
+           ("qwen3.attention.layer_norm_rms_epsilon", F32, cfg.rms_eps),
+           ("tokenizer.ggml.tokens", ARR, (STR, [f"t{i}" for i in range(cfg.vocab)]))]
+    return build(kvs, [(n, t, d, b) for n, t, d, b in ts])
