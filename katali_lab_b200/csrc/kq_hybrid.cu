@@ -19,10 +19,13 @@
 // MoE block: RMSNorm (ffn_norm), fp32 router GEMV (double accumulation, as the reference's
 // F32 dot, V/src/gguf_dtype.c:640-644), then the fused MoE kernel (kq_moe.cu) adding its
 // output into the residual stream.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "kq_device.cuh"
 #include "kq_launch.h"
+
+namespace cg = cooperative_groups;
 
 namespace kq {
 
@@ -30,7 +33,8 @@ namespace {
 
 constexpr int DT = 256;           // threads of the attention kernel (head_dim <= 256)
 constexpr int GD = 128;           // GDN head dimension (dk = dv)
-constexpr int GDN_THREADS = 512;  // 16 warps x 8 state columns
+constexpr int GDN_CPH = 4;        // CTAs (one cluster) per GDN value head
+constexpr int GDN_THREADS = 256;  // 8 warps x 4 state columns per CTA
 constexpr int RW = 4;             // router: warps per CTA, one expert row each
 
 __device__ __forceinline__ double block_sum_d(double v, double *sh) {
@@ -54,46 +58,55 @@ __device__ __forceinline__ float sigmoid_f(float x) {
     return __fdiv_rn(1.0f, __fadd_rn(1.0f, kq_expf(-x)));
 }
 
-// One Gated DeltaNet decode step for value head blockIdx.x: conv + SiLU of the head's q, k
-// and v channels (ring slot pos % conv_k takes the new input; the q/k channels shared by
-// `ratio` value heads are written by the first of them), L2 norms, gates, the delta-rule
-// update of the head's dv x dk state (column j contiguous, one warp per column, four dk
-// values per lane), and the gated RMSNorm of the output.
+// One Gated DeltaNet decode step for value head h = blockIdx.x / GDN_CPH, split over a cluster
+// of GDN_CPH CTAs: CTA rank r owns state columns [r 32, r 32 + 32) of the head (8 warps x 4
+// columns, four dk values per lane). Every CTA computes the head's conv + SiLU for q and k (the
+// q/k channels shared by `ratio` value heads are written back to the ring by rank 0 of the first
+// of them) and for its own 32 v channels, the L2 norms and gates; after the delta-rule update the
+// gated RMSNorm needs the sum of squares over all 128 outputs: each CTA publishes its partial in
+// shared memory and, after a cluster barrier, reads the others' through distributed shared
+// memory in rank order (the same double sum on every CTA).
 __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer L) {
+    cg::cluster_group cluster = cg::this_cluster();
     __shared__ __align__(16) float sq[GD];
     __shared__ __align__(16) float sk[GD];
-    __shared__ float sv[GD], so[GD];
+    __shared__ float sv[GD / GDN_CPH], so[GD / GDN_CPH];
     __shared__ double sh[32];
+    __shared__ double s_part;
     __shared__ float s_par[2];
-    const int vh = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rank = (int)cluster.block_rank();
+    const int vh = blockIdx.x / GDN_CPH, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ratio = p.nv / p.nk, kh = vh / ratio;
     const int C = 2 * p.nk * GD + p.nv * GD, K = p.conv_k;
-    // The head's state columns are loaded before pdl_wait(): this layer's state was last
-    // written by this kernel one token earlier, and every MoE launch in between (an
-    // ordinary, non-programmatic launch) started only after all earlier kernels completed.
+    constexpr int CW = GD / GDN_CPH;          // columns of this CTA
+    constexpr int CPW = CW / (GDN_THREADS / 32);  // columns per warp
+    const int j0 = rank * CW;
+    // The state columns are loaded before pdl_wait(): this layer's state was last written by
+    // this kernel in the previous decode step, a separate graph launch (or eager launch
+    // sequence) whose every kernel completed before this step's first launch started.
     float *S = L.state + (size_t)vh * GD * GD;
-    float4 s[GD / 16];
+    float4 s[CPW];
 #pragma unroll
-    for (int c = 0; c < GD / 16; ++c)
-        s[c] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(warp + 16 * c) * GD) + lane);
+    for (int c = 0; c < CPW; ++c)
+        s[c] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(j0 + warp + 8 * c) * GD) + lane);
     pdl_trigger();
     pdl_wait();
     const int pos = *p.d.pos;
-    if (tid < 3 * GD) {
-        const int which = tid / GD, c = tid % GD;
+    for (int t = tid; t < 2 * GD + CW; t += GDN_THREADS) {
+        const int which = t < GD ? 0 : t < 2 * GD ? 1 : 2, c = which < 2 ? t % GD : t - 2 * GD;
         const int ch = which == 0   ? kh * GD + c
                        : which == 1 ? p.nk * GD + kh * GD + c
-                                    : 2 * p.nk * GD + vh * GD + c;
+                                    : 2 * p.nk * GD + vh * GD + j0 + c;
         const float cur = p.qkv[ch];
         const float *w = L.conv_w + (size_t)ch * K;
         float acc = 0.0f;
         for (int j = 0; j < K - 1; ++j) {
-            const int t = pos - (K - 1) + j;  // input position; slots of t < 0 hold zeros
-            const int slot = ((t % K) + K) % K;
+            const int tp = pos - (K - 1) + j;  // input position; slots of tp < 0 hold zeros
+            const int slot = ((tp % K) + K) % K;
             acc = __fadd_rn(acc, __fmul_rn(w[j], L.ring[(size_t)slot * C + ch]));
         }
         acc = __fadd_rn(acc, __fmul_rn(w[K - 1], cur));
-        if (which == 2 || vh % ratio == 0) L.ring[(size_t)(pos % K) * C + ch] = cur;
+        if (which == 2 || (vh % ratio == 0 && rank == 0)) L.ring[(size_t)(pos % K) * C + ch] = cur;
         const float act = silu_f(acc);
         if (which == 0) sq[c] = act;
         else if (which == 1) sk[c] = act;
@@ -123,8 +136,8 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
     const float4 kk = reinterpret_cast<const float4 *>(sk)[lane];
     const float4 qq = reinterpret_cast<const float4 *>(sq)[lane];
 #pragma unroll
-    for (int c = 0; c < GD / 16; ++c) {
-        const int j = warp + 16 * c;
+    for (int c = 0; c < CPW; ++c) {
+        const int jl = warp + 8 * c, j = j0 + jl;
         float4 v = s[c];
         v.x = __fmul_rn(v.x, decay);
         v.y = __fmul_rn(v.y, decay);
@@ -135,7 +148,7 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
         kv += (double)v.z * kk.z;
         kv += (double)v.w * kk.w;
         kv = warp_sum_d(kv);
-        const float delta = __fmul_rn(__fsub_rn(sv[j], (float)kv), beta);
+        const float delta = __fmul_rn(__fsub_rn(sv[jl], (float)kv), beta);
         v.x = __fadd_rn(v.x, __fmul_rn(kk.x, delta));
         v.y = __fadd_rn(v.y, __fmul_rn(kk.y, delta));
         v.z = __fadd_rn(v.z, __fmul_rn(kk.z, delta));
@@ -146,16 +159,21 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
         o += (double)v.w * qq.w;
         o = warp_sum_d(o);
         __stcs(reinterpret_cast<float4 *>(S + (size_t)j * GD) + lane, v);
-        if (lane == 0) so[j] = (float)o;
+        if (lane == 0) so[jl] = (float)o;
     }
     __syncthreads();
-    const double no = block_sum_d(tid < GD ? (double)so[tid] * (double)so[tid] : 0.0, sh);
-    if (tid < GD) {
+    const double part = block_sum_d(tid < CW ? (double)so[tid] * (double)so[tid] : 0.0, sh);
+    if (tid == 0) s_part = part;
+    cluster.sync();  // every CTA's partial is published
+    double no = 0.0;
+    for (int r = 0; r < GDN_CPH; ++r) no += *cluster.map_shared_rank(&s_part, r);
+    if (tid < CW) {
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(no / (double)GD), p.d.eps)));
-        const float zz = p.z[(size_t)vh * GD + tid];
-        p.go[(size_t)vh * GD + tid] =
-            __fmul_rn(__fmul_rn(__fmul_rn(so[tid], inv), L.ssm_norm[tid]), silu_f(zz));
+        const float zz = p.z[(size_t)vh * GD + j0 + tid];
+        p.go[(size_t)vh * GD + j0 + tid] =
+            __fmul_rn(__fmul_rn(__fmul_rn(so[tid], inv), L.ssm_norm[j0 + tid]), silu_f(zz));
     }
+    cluster.sync();  // no CTA leaves while another still reads its partial
 }
 
 // One head of q or k: RMSNorm over head_dim (when nw), then RoPE on the first 2 * rope_half
@@ -296,6 +314,24 @@ __global__ void __launch_bounds__(RW * 32) k_router(HybridParams hp, HybridLayer
     if (lane == 0) hp.rlogits[r] = (float)acc;
 }
 
+// k_gdn: clusters of GDN_CPH CTAs, programmatic dependent of the in-projection GEMV.
+cudaError_t launch_gdn(HybridParams &p, const HybridLayer &L, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.nv * GDN_CPH));
+    cfg.blockDim = dim3(GDN_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = GDN_CPH;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, k_gdn, p, L);
+}
+
 }  // namespace
 
 cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams *g,
@@ -314,7 +350,7 @@ cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams
     const dim3 rgrid((p.n_experts + RW - 1) / RW);
     for (int l = 0; l < p.d.NL; ++l) {
         if ((e = launch_gemv(g[2 * l], mode, st)) != cudaSuccess) return e;
-        if (L[l].kind == 0) e = launch_k(k_gdn, dim3(p.nv), dim3(GDN_THREADS), 0, st, 1, p, L[l]);
+        if (L[l].kind == 0) e = launch_gdn(p, L[l], st);
         else e = launch_k(k_attn_gated, dim3(p.d.NH), dim3(DT), att_smem, st, 1, p, L[l]);
         if (e != cudaSuccess) return e;
         if ((e = launch_gemv(g[2 * l + 1], mode, st)) != cudaSuccess) return e;
