@@ -57,6 +57,8 @@ def parse():
                          "batch; c4: dense Qwen3-8B decode; c5: hybrid GDN/attention MoE decode")
     ap.add_argument("--dp4a", action="store_true", help="c1: q8_1 activations (KATALI_CUDA_DP4A=1)")
     ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--dense-layers", type=int, default=36,
+                    help="c4: decoder layers; 36 is the configuration (fewer for small profiles)")
     ap.add_argument("--hybrid-layers", type=int, default=40,
                     help="c5: decoder layers (every 4th is gated attention); 40 is the configuration")
     ap.add_argument("--calls", type=int, default=64)
@@ -885,7 +887,9 @@ def run_c4(args, rank, world, local_rank):
         raise SystemExit(f"no usable B200: {plugin.status()}")
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    model = make_dense_model(plugin, QWEN3_8B, seed=8 + rank)
+    cfg = QWEN3_8B if args.dense_layers == QWEN3_8B.n_layers else \
+        dataclasses.replace(QWEN3_8B, n_layers=args.dense_layers)
+    model = make_dense_model(plugin, cfg, seed=8 + rank)
     plugin.set_stream(stream)
     dm = DenseModel(plugin, model, q8=args.dp4a)
     n = args.calls * 2  # 128 tokens by default
@@ -937,6 +941,7 @@ def run_c4(args, rank, world, local_rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8" if args.dp4a else "f32",
             "data": "synthetic",
             "config": {"workload": C4_WORKLOAD.format(n=n), "tokens_per_step": n,
+                       "n_layers": cfg.n_layers,
                        "activations": "q8_1 (DP4A)" if args.dp4a else "fp32",
                        "tokens_per_s": round(tok_s, 1), "weight_bytes_per_token": bpt,
                        "us_per_token": round(1e3 * ms / (args.steps * n), 2),
@@ -951,7 +956,7 @@ def run_c4(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": args.steps * n * (2 + 9 * 36 + 3), "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": args.steps * n * (1 + 6 * cfg.n_layers + 3), "cpu_baseline": cpu}), flush=True)
     dm.close()
 
 
