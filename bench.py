@@ -946,13 +946,10 @@ def run_c4(args, rank, world, local_rank):
                        "tokens_per_s": round(tok_s, 1), "weight_bytes_per_token": bpt,
                        "us_per_token": round(1e3 * ms / (args.steps * n), 2),
                        "l2": "inputs larger than L2: 4.9 GB of weights read per token",
-                       "parallelism": (f"ep{world}: experts of every layer split over the GPUs, "
-                                       "one sequence per GPU, MoE blocks over NVLink peer memory")
-                       if ep else f"replicas x{world}",
-                       "last_tokens": [int(t) for t in toks[:8]]},
+                       "parallelism": f"replicas x{world}", "last_tokens": [int(t) for t in toks[:8]]},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                         "traffic": None, "scope": "whole decode step (all kernels), per GPU"},
+                         "traffic": None, "scope": "whole decode step (all kernels)"},
             "clocks": clk.summary(),
             "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
