@@ -11,8 +11,12 @@
 
 namespace kq {
 
-constexpr int GEMV_CW = 8;                       // consumer warps
-constexpr int GEMV_THREADS = (GEMV_CW + 1) * 32; // + one producer warp
+// Consumer warps per CTA (+ one producer warp): 8 for launches that stream less than
+// GEMV_BIG_BYTES of weights, 12 above (more rows in flight per SM for the long streams;
+// the short ones run as programmatic dependents inside decode steps, where fewer, lighter
+// CTAs overlap the previous kernel better).
+constexpr int GEMV_CW_SMALL = 8, GEMV_CW_BIG = 12;
+constexpr uint64_t GEMV_BIG_BYTES = 16ull << 20;
 
 __device__ __forceinline__ void gemv_tile(const GemvParams &p, uint32_t t, int &job,
                                           uint64_t &r0, uint32_t &nrows) {
@@ -24,8 +28,8 @@ __device__ __forceinline__ void gemv_tile(const GemvParams &p, uint32_t t, int &
     nrows = (uint32_t)(rem < J.tr ? rem : J.tr);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(GEMV_THREADS)
+template <int MODE, int GEMV_CW>
+__global__ void __launch_bounds__((GEMV_CW + 1) * 32)
     gemv_kernel(const __grid_constant__ GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -198,9 +202,6 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
 }
 
-template __global__ void gemv_kernel<0>(const __grid_constant__ GemvParams p);
-template __global__ void gemv_kernel<1>(const __grid_constant__ GemvParams p);
-template __global__ void gemv_kernel<2>(const __grid_constant__ GemvParams p);
 
 // ---------------------------------------------------------------------------
 // q8_1 quantiser: one warp per 32-element block.
@@ -421,20 +422,27 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     const size_t smem = p.act_off + act_bytes;
     int grid = 2 * num_sms();
     if ((uint32_t)grid > tiles) grid = (int)tiles;
-    void (*fn)(GemvParams) = mode == 0 ? gemv_kernel<0> : (mode == 1 ? gemv_kernel<1> : gemv_kernel<2>);
-    static size_t set_bytes[3] = {0, 0, 0};
-    if (smem > set_bytes[mode]) {
+    uint64_t bytes = 0;
+    for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
+    const bool big = bytes >= GEMV_BIG_BYTES;
+    const int threads = ((big ? GEMV_CW_BIG : GEMV_CW_SMALL) + 1) * 32;
+    void (*const fns[2][3])(GemvParams) = {
+        {gemv_kernel<0, GEMV_CW_SMALL>, gemv_kernel<1, GEMV_CW_SMALL>, gemv_kernel<2, GEMV_CW_SMALL>},
+        {gemv_kernel<0, GEMV_CW_BIG>, gemv_kernel<1, GEMV_CW_BIG>, gemv_kernel<2, GEMV_CW_BIG>}};
+    void (*fn)(GemvParams) = fns[big][mode];
+    static size_t set_bytes[2][3] = {{0, 0, 0}, {0, 0, 0}};
+    if (smem > set_bytes[big][mode]) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        set_bytes[mode] = smem;
+        set_bytes[big][mode] = smem;
     }
     if (!p.pdl) {
-        fn<<<grid, GEMV_THREADS, smem, st>>>(p);
+        fn<<<grid, threads, smem, st>>>(p);
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
