@@ -406,9 +406,15 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
     const uint32_t act_bytes =
         mode == 2 ? (cols + cols / 16) * 4 + cols / 32 * 4 : cols + cols / 4 + cols / 32 * 16;
+    uint64_t bytes = 0;
+    for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
+    const bool big = bytes >= GEMV_BIG_BYTES;
+    // A standalone small launch (not a programmatic dependent inside a decode step) runs up
+    // to 3 CTAs per SM with 64 KB rings; the others 2 CTAs per SM with 96 KB rings.
+    const bool three = !p.pdl && !big;
     p.stage_bytes = stage + 16;
     p.use_tma = 1;
-    int ns = (int)(98304 / p.stage_bytes);
+    int ns = (int)((three ? 65536 : 98304) / p.stage_bytes);
     if (ns > 8) ns = 8;
     if (ns < 2) {
         ns = 2;
@@ -420,11 +426,6 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     p.nstages = ns;
     p.act_off = ((uint32_t)ns * p.stage_bytes + 16 * ns + 127u) & ~127u;
     const size_t smem = p.act_off + act_bytes;
-    int grid = 2 * num_sms();
-    if ((uint32_t)grid > tiles) grid = (int)tiles;
-    uint64_t bytes = 0;
-    for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
-    const bool big = bytes >= GEMV_BIG_BYTES;
     const int threads = ((big ? GEMV_CW_BIG : GEMV_CW_SMALL) + 1) * 32;
     void (*const fns[2][3])(GemvParams) = {
         {gemv_kernel<0, GEMV_CW_SMALL>, gemv_kernel<1, GEMV_CW_SMALL>, gemv_kernel<2, GEMV_CW_SMALL>},
@@ -436,6 +437,13 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         set_bytes[big][mode] = smem;
     }
+    int per = 2;
+    if (three && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, threads, smem) != cudaSuccess)
+        per = 2;
+    if (per < 1) per = 1;
+    if (per > 3) per = 3;
+    int grid = per * num_sms();
+    if ((uint32_t)grid > tiles) grid = (int)tiles;
     if (!p.pdl) {
         fn<<<grid, threads, smem, st>>>(p);
         return cudaGetLastError();
