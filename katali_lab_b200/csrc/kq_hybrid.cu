@@ -354,7 +354,8 @@ cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams
         else e = launch_k(k_attn_gated, dim3(p.d.NH), dim3(DT), att_smem, st, 1, p, L[l]);
         if (e != cudaSuccess) return e;
         if ((e = launch_gemv(g[2 * l + 1], mode, st)) != cudaSuccess) return e;
-        if ((e = launch_k(router, rgrid, dim3(RW * 32), rt_smem, st, 1, p, L[l])) != cudaSuccess)
+        if ((p.moe_ep || !moe[l].rt_w) &&  // else the router runs inside the MoE launch
+            (e = launch_k(router, rgrid, dim3(RW * 32), rt_smem, st, 1, p, L[l])) != cudaSuccess)
             return e;
         e = p.moe_ep ? launch_moe_ep_layer(moe[l], moe_grid[l], st) : launch_moe(moe[l], moe_grid[l], st);
         if (e != cudaSuccess) return e;

@@ -315,11 +315,21 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
         }
         kq::MoeParams &mp = m->moe[l];
         kq::moe_fused_params(w.moe, q8 ? KATALI_MOE_Q8_1 : KATALI_MOE_F32, &mp, &m->moe_grid[l]);
-        mp.x = p.xb;
         mp.logits = hp.rlogits;
         mp.y = p.x;
         mp.accum = 1;
         mp.pdl = 1;
+        const int grid = m->moe_grid[l];
+        if (H <= 4u * 512u && (n_experts + grid - 1) / grid <= (uint32_t)kq::MOE_RT_ROWS) {
+            // the router runs inside the MoE launch: x is the residual stream itself (read by
+            // every CTA before the launch's first grid barrier, added to after the last)
+            mp.x = p.x;
+            mp.rt_w = w.router;
+            mp.rt_norm = w.ffn_norm;
+            mp.rt_eps = d->rms_eps;
+        } else {
+            mp.x = p.xb;  // RMSNorm and router logits from the router kernel
+        }
     }
     {
         const void *ws[1] = {d->lm_head};

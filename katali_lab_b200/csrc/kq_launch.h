@@ -76,6 +76,7 @@ constexpr int MOE_MAX_K = 16;
 constexpr int MOE_EP_MAX_SLOTS = 16;
 constexpr int MOE_EP_MAX_PAIRS = MOE_EP_MAX_SLOTS * MOE_MAX_K;
 constexpr int MOE_MAX_CHUNKS = 64;
+constexpr int MOE_RT_ROWS = 4;   // router rows per CTA when the router is folded into the launch
 constexpr int TRACE_SLOTS = 20;  // 16 %globaltimer slots + clock64 at start/end  // %globaltimer samples per CTA when tracing
 
 struct MoeParams {
@@ -98,6 +99,13 @@ struct MoeParams {
     int route_only;        // 1: routing decision only (check entry point)
     int accum;             // 1: y[r] += layer output (a decoder's residual add), 0: y[r] = output
     int pdl;               // 1: programmatic dependent of the previous kernel (not EP, not route_only)
+    // Router folded into the launch (a decoder's MoE block, not EP): x is the residual stream,
+    // the kernel forms RMSNorm(x) * rt_norm itself and the logits R xb (fp32 rows rt_w, double
+    // sums) into the scratch p.logits before routing. Needs H <= 4 * MOE_THREADS and at most
+    // MOE_RT_ROWS router rows per CTA.
+    const float *rt_w;
+    const float *rt_norm;
+    float rt_eps;
     // shared-memory plan (bytes), identical for every CTA
     uint32_t chunk_units;  // max row pairs per phase-A chunk
     uint32_t sa_bytes;     // phase-A staging capacity

@@ -84,23 +84,37 @@ __device__ __forceinline__ void bulk_g2s_split(uint8_t *dst, const uint8_t *src,
     }
 }
 
+// Router logits are read through the read-only path, except when this launch wrote them
+// itself (router folded into the launch: other CTAs' stores, seen after a grid barrier).
+template <int RT>
+__device__ __forceinline__ float ld_logit(const float *a) {
+    if constexpr (RT != 0) return __ldcg(a);
+    else return __ldg(a);
+}
+template <int RT>
+__device__ __forceinline__ float4 ld_logit4(const float *a) {
+    if constexpr (RT != 0) return __ldcg(reinterpret_cast<const float4 *>(a));
+    else return __ldg(reinterpret_cast<const float4 *>(a));
+}
+
 // Softmax weights of the chosen ids (lane 0 writes s_w); shared by both top-k paths.
+template <int RT = 0>
 __device__ __forceinline__ void route_weights(const MoeParams &p, const float *L, const float *lg, int npl,
                                               int lane, int32_t *s_ids, float *s_w) {
     const int n = p.n_experts, K = p.K;
-    const float m = __ldg(&L[s_ids[0]]);
+    const float m = ld_logit<RT>(&L[s_ids[0]]);
     double S = 0.0;
     if (!p.norm) {  // sum over all n logits (lane-owned contiguous ranges)
         const int per = (n + 31) >> 5;
         for (int i = 0; i < per; ++i) {
             const int idx = lane * per + i;
-            if (idx < n) S += (double)kq_expf(__fsub_rn(lg ? lg[i] : __ldg(&L[idx]), m));
+            if (idx < n) S += (double)kq_expf(__fsub_rn(lg ? lg[i] : ld_logit<RT>(&L[idx]), m));
         }
         S = warp_sum_d(S);
     }
     // lane t < K: e_t; every lane then sums e_0..e_{K-1} in order (the
     // restatement's order) and lane t divides its own weight.
-    const float e = lane < K ? kq_expf(__fsub_rn(__ldg(&L[s_ids[lane]]), m)) : 0.0f;
+    const float e = lane < K ? kq_expf(__fsub_rn(ld_logit<RT>(&L[s_ids[lane]]), m)) : 0.0f;
     if (p.norm) {
         S = 0.0;
         for (int t = 0; t < K; ++t) S += (double)__shfl_sync(KQ_FULL, e, t);
@@ -123,14 +137,15 @@ __device__ __forceinline__ void ce_desc(uint64_t &a, uint64_t &b) {
 // Top-k by one warp for n <= 256: lane l owns ids [8l, 8l+8), sorts its 8 keys
 // (Batcher odd-even merge network), then each round takes the warp maximum of
 // the lane heads with two redux steps and the winning lane pops its head.
+template <int RT = 0>
 __device__ __forceinline__ void route_regs(const MoeParams &p, const float *L, int lane, int32_t *s_ids,
                                            float *s_w, bool weights) {
     const int n = p.n_experts, K = p.K;
     const int npl = (n + 31) >> 5;
     uint64_t v[8];
     if (n == 256) {  // two 16-byte loads per lane, contiguous across the warp
-        const float4 l0 = __ldg(reinterpret_cast<const float4 *>(L) + 2 * lane);
-        const float4 l1 = __ldg(reinterpret_cast<const float4 *>(L) + 2 * lane + 1);
+        const float4 l0 = ld_logit4<RT>(L + 8 * lane);
+        const float4 l1 = ld_logit4<RT>(L + 8 * lane + 4);
         const float lv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = route_key(lv[i], 8 * lane + i);
@@ -138,7 +153,7 @@ __device__ __forceinline__ void route_regs(const MoeParams &p, const float *L, i
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int idx = lane * npl + i;
-            v[i] = (i < npl && idx < n) ? route_key(__ldg(&L[idx]), idx) : 0ull;
+            v[i] = (i < npl && idx < n) ? route_key(ld_logit<RT>(&L[idx]), idx) : 0ull;
         }
     }
     trace(p, 9);
@@ -161,14 +176,15 @@ __device__ __forceinline__ void route_regs(const MoeParams &p, const float *L, i
     }
     __syncwarp();
     trace(p, 11);
-    if (weights) route_weights(p, L, nullptr, 0, lane, s_ids, s_w);
+    if (weights) route_weights<RT>(p, L, nullptr, 0, lane, s_ids, s_w);
 }
 
 // Generic top-k for n_experts > 256: logits staged in shared memory.
+template <int RT = 0>
 __device__ void route_smem(const MoeParams &p, const float *L, float *s_logits, int32_t *s_ids, float *s_w,
                            int lane, bool weights) {
     const int n = p.n_experts, K = p.K;
-    for (int i = lane; i < n; i += 32) s_logits[i] = L[i];
+    for (int i = lane; i < n; i += 32) s_logits[i] = ld_logit<RT>(&L[i]);
     __syncwarp();
     const int npl = (n + 31) >> 5;
     uint32_t taken = 0;
@@ -198,13 +214,14 @@ __device__ void route_smem(const MoeParams &p, const float *L, float *s_logits, 
         const int idx = lane * npl + i;
         lg[i] = idx < n ? s_logits[idx] : 0.0f;
     }
-    if (weights) route_weights(p, L, lg, npl, lane, s_ids, s_w);
+    if (weights) route_weights<RT>(p, L, lg, npl, lane, s_ids, s_w);
 }
 
+template <int RT = 0>
 __device__ __forceinline__ void route(const MoeParams &p, const float *L, float *s_logits, int32_t *s_ids,
                                       float *s_w, int lane, bool weights = true) {
-    if (p.n_experts <= 256) route_regs(p, L, lane, s_ids, s_w, weights);
-    else route_smem(p, L, s_logits, s_ids, s_w, lane, weights);
+    if (p.n_experts <= 256) route_regs<RT>(p, L, lane, s_ids, s_w, weights);
+    else route_smem<RT>(p, L, s_logits, s_ids, s_w, lane, weights);
 }
 
 // This lane's Q4_K unit of x held in registers (phase A reuses it for every row).
@@ -529,7 +546,7 @@ __device__ __forceinline__ void ep_store_t(const MoeParams &p, uint32_t e, int s
 // come from the received slots instead of routing, each pair with its own token's q8_1 x;
 // they run in rounds of K pairs (phase A, grid barrier, phase B per round) and each slot's
 // weighted sum over its pairs, in k order, accumulates in double into p.ep_ret.
-template <int MODE, uint32_t DT, int SHAPE, int EP>
+template <int MODE, uint32_t DT, int SHAPE, int EP, int RT = 0>
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_constant__ MoeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -618,6 +635,64 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         npairs = *s_np;
         nrounds = (npairs + K - 1) / K;
         trace(p, 11);
+    } else if (RT) {
+        // Router folded into the launch: this CTA's router rows [r0, r0 + nr) are loaded into
+        // registers before pdl_wait() (constant weights), then every CTA forms xb = RMSNorm(x) *
+        // rt_norm in xf (the order of the reference's rmsnorm: (x * inv) * w), dots its rows
+        // with it (double sums), publishes the logits, and after a grid barrier warp 0 routes
+        // on the whole vector.
+        const int E = p.n_experts, r0 = E * (int)c / (int)G, nr = E * ((int)c + 1) / (int)G - r0;
+        const bool xl = tid < H / 4;
+        float4 rw[MOE_RT_ROWS];
+#pragma unroll
+        for (int i = 0; i < MOE_RT_ROWS; ++i)
+            rw[i] = (i < nr && xl) ? __ldcs(reinterpret_cast<const float4 *>(p.rt_w + (size_t)(r0 + i) * H) + tid)
+                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
+        for (int i = tid; i < npair; i += MOE_THREADS)
+            reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
+        pdl_wait();
+        double *red = reinterpret_cast<double *>(s_h);  // MOE_WARPS doubles, free until phase A
+        auto block_sum = [&](double v) {
+            v = warp_sum_d(v);
+            if (lane == 0) red[warp] = v;
+            __syncthreads();
+            double t = 0.0;
+            for (int w = 0; w < MOE_WARPS; ++w) t += red[w];
+            __syncthreads();
+            return t;
+        };
+        float4 xv = xl ? __ldcg(reinterpret_cast<const float4 *>(p.x) + tid) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        double ss = (double)xv.x * (double)xv.x;
+        ss += (double)xv.y * (double)xv.y;
+        ss += (double)xv.z * (double)xv.z;
+        ss += (double)xv.w * (double)xv.w;
+        ss = block_sum(ss);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / (double)H), p.rt_eps)));
+        if (xl) {
+            const float4 nw = __ldg(reinterpret_cast<const float4 *>(p.rt_norm) + tid);
+            xv.x = __fmul_rn(__fmul_rn(xv.x, inv), nw.x);
+            xv.y = __fmul_rn(__fmul_rn(xv.y, inv), nw.y);
+            xv.z = __fmul_rn(__fmul_rn(xv.z, inv), nw.z);
+            xv.w = __fmul_rn(__fmul_rn(xv.w, inv), nw.w);
+            reinterpret_cast<float4 *>(xf)[tid] = xv;
+        }
+#pragma unroll
+        for (int i = 0; i < MOE_RT_ROWS; ++i) {
+            if (i < nr) {  // uniform across the CTA
+                double d = (double)rw[i].x * (double)xv.x;
+                d += (double)rw[i].y * (double)xv.y;
+                d += (double)rw[i].z * (double)xv.z;
+                d += (double)rw[i].w * (double)xv.w;
+                d = block_sum(xl ? d : 0.0);
+                if (tid == 0) const_cast<float *>(p.logits)[r0 + i] = (float)d;
+            }
+        }
+        grid_barrier(p, nbar);  // every CTA's logits published
+        if (warp == 0) {
+            route<RT>(p, p.logits, s_logits, s_ids, s_w, lane, false);  // weights after the copies are issued
+            trace(p, 1);
+        }
     } else if (warp == 0) {
         pdl_wait();  // under a programmatic launch: x, logits / ids, scratch only after this
         if (p.ids) {
@@ -701,7 +776,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         __syncwarp();
         for (int q = lane; q < ncopy; q += 32) issue(q);
         trace(p, 3);
-        if (!EP && !p.ids) route_weights(p, p.logits, nullptr, 0, lane, s_ids, s_w);
+        if (!EP && !p.ids) route_weights<RT>(p, p.logits, nullptr, 0, lane, s_ids, s_w);
     } else if (EP) {
         // x of this CTA's phase-A block: its pair's token, from the slot's q8_1 row
         if (nbA > 0) {
@@ -1085,11 +1160,11 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     return p.smem_bytes <= (uint32_t)max_smem ? 0 : -1;
 }
 
-template <int MODE, uint32_t DT, int SHAPE, int EP = 0>
+template <int MODE, uint32_t DT, int SHAPE, int EP = 0, int RT = 0>
 static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     static uint32_t set_bytes = 0;  // raise the smem limit once per size, before any capture
     if (p.smem_bytes > set_bytes) {
-        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE, EP>,
+        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE, EP, RT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)p.smem_bytes);
         if (e != cudaSuccess) return e;
@@ -1111,12 +1186,12 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     static int pdl_ok = 1;
     const bool pdl = p.pdl && pdl_ok && !EP && !p.route_only;
     cfg.numAttrs = pdl ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP, RT>, p);
     if (pdl && (e == cudaErrorInvalidValue || e == cudaErrorNotSupported)) {
         cudaGetLastError();
         pdl_ok = 0;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP>, p);
+        e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP, RT>, p);
     }
     return e;
 }
@@ -1124,6 +1199,15 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st) {
     const bool c2 = p.H == 2048 && p.F == 512 && p.K == 8 && p.gate_type == T_Q4_K &&
                     p.up_type == T_Q4_K && p.down_type == T_Q6_K;
+    if (p.rt_w) {  // the router folded into the launch (a decoder's MoE block)
+        if (p.mode == 0) {
+            if (c2) return launch_t<0, T_Q6_K, 1, 0, 1>(p, grid, st);
+            return p.down_type == T_Q6_K ? launch_t<0, T_Q6_K, 0, 0, 1>(p, grid, st)
+                                         : launch_t<0, T_Q4_K, 0, 0, 1>(p, grid, st);
+        }
+        return p.down_type == T_Q6_K ? launch_t<1, T_Q6_K, 0, 0, 1>(p, grid, st)
+                                     : launch_t<1, T_Q4_K, 0, 0, 1>(p, grid, st);
+    }
     if (p.mode == 0) {
         if (c2) return launch_t<0, T_Q6_K, 1>(p, grid, st);
         return p.down_type == T_Q6_K ? launch_t<0, T_Q6_K, 0>(p, grid, st)
