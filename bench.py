@@ -1042,7 +1042,8 @@ def run_c5(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": steps * n * (1 + 5 * cfg.n_layers + 3), "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": steps * n * (1 + (5 if ep else 4) * cfg.n_layers + 3), "cpu_baseline": cpu}),
+          flush=True)
     hm.close()
     if comm is not None:
         comm.close()
