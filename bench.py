@@ -1090,6 +1090,8 @@ def main():
     if world > 1:
         import datetime
 
+        # stdout carries exactly one JSON line: NCCL's banner lines stay off unless asked for
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
