@@ -89,15 +89,23 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
 #pragma unroll
     for (int c = 0; c < CPW; ++c)
         s[c] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(j0 + warp + 8 * c) * GD) + lane);
-    pdl_trigger();
-    pdl_wait();
+    // Also before pdl_wait(): the position (advanced by the previous step), each channel's
+    // conv over its older inputs (ring slots written by earlier steps; this step writes slot
+    // pos % K, which is not among them) and the gate constants. The new input, b and a come
+    // from the in-projection GEMV: after the wait.
+    constexpr int NCH = (2 * GD + CW + GDN_THREADS - 1) / GDN_THREADS;  // channels per thread
     const int pos = *p.d.pos;
-    for (int t = tid; t < 2 * GD + CW; t += GDN_THREADS) {
+    int chs[NCH];
+    float pre[NCH], wl[NCH];
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        const int t = tid + q * GDN_THREADS;
+        chs[q] = -1;
+        if (t >= 2 * GD + CW) continue;
         const int which = t < GD ? 0 : t < 2 * GD ? 1 : 2, c = which < 2 ? t % GD : t - 2 * GD;
         const int ch = which == 0   ? kh * GD + c
                        : which == 1 ? p.nk * GD + kh * GD + c
                                     : 2 * p.nk * GD + vh * GD + j0 + c;
-        const float cur = p.qkv[ch];
         const float *w = L.conv_w + (size_t)ch * K;
         float acc = 0.0f;
         for (int j = 0; j < K - 1; ++j) {
@@ -105,7 +113,21 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
             const int slot = ((tp % K) + K) % K;
             acc = __fadd_rn(acc, __fmul_rn(w[j], L.ring[(size_t)slot * C + ch]));
         }
-        acc = __fadd_rn(acc, __fmul_rn(w[K - 1], cur));
+        chs[q] = ch;
+        pre[q] = acc;
+        wl[q] = w[K - 1];
+    }
+    const float ea = kq_expf(L.a_log[vh]), dtb = L.dt_bias[vh];
+    pdl_trigger();
+    pdl_wait();
+#pragma unroll
+    for (int q = 0; q < NCH; ++q) {
+        if (chs[q] < 0) continue;
+        const int t = tid + q * GDN_THREADS;
+        const int which = t < GD ? 0 : t < 2 * GD ? 1 : 2, c = which < 2 ? t % GD : t - 2 * GD;
+        const int ch = chs[q];
+        const float cur = p.qkv[ch];
+        const float acc = __fadd_rn(pre[q], __fmul_rn(wl[q], cur));
         if (which == 2 || (vh % ratio == 0 && rank == 0)) L.ring[(size_t)(pos % K) * C + ch] = cur;
         const float act = silu_f(acc);
         if (which == 0) sq[c] = act;
@@ -114,9 +136,9 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
     }
     if (tid == 0) {
         const float b = p.ba[vh], a = p.ba[p.nv + vh];
-        const float xa = __fadd_rn(a, L.dt_bias[vh]);
+        const float xa = __fadd_rn(a, dtb);
         const float sp = xa > 20.0f ? xa : log1pf(kq_expf(xa));  // softplus
-        const float g = -__fmul_rn(kq_expf(L.a_log[vh]), sp);
+        const float g = -__fmul_rn(ea, sp);
         s_par[0] = sigmoid_f(b);
         s_par[1] = kq_expf(g);
     }
