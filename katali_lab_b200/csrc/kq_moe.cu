@@ -651,6 +651,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
         for (int i = tid; i < npair; i += MOE_THREADS)
             reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
+        const float4 nw = xl ? __ldg(reinterpret_cast<const float4 *>(p.rt_norm) + tid)
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         pdl_wait();
         double *red = reinterpret_cast<double *>(s_h);  // MOE_WARPS doubles, free until phase A
         auto block_sum = [&](double v) {
@@ -670,7 +672,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         ss = block_sum(ss);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)(ss / (double)H), p.rt_eps)));
         if (xl) {
-            const float4 nw = __ldg(reinterpret_cast<const float4 *>(p.rt_norm) + tid);
             xv.x = __fmul_rn(__fmul_rn(xv.x, inv), nw.x);
             xv.y = __fmul_rn(__fmul_rn(xv.y, inv), nw.y);
             xv.z = __fmul_rn(__fmul_rn(xv.z, inv), nw.z);
