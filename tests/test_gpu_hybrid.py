@@ -104,3 +104,25 @@ def test_35b_class_dims_greedy(plugin, ref, port):
     assert [w["kind"] for w in model.layers] == [0, 0, 0, 1]
     g, c = greedy_both(plugin, ref, port, model, [100, 2000], 3)
     assert g == c
+
+
+@pytest.mark.parametrize("change,code", [
+    ({"ssm_head_dim": 64}, 5),   # GDN kernels are written for 128-wide heads
+    ({"head_dim": 512}, 5),      # attention head_dim <= 256
+    ({"ssm_conv": 1}, 5),        # conv kernel 2..8
+])
+def test_create_rejects_unsupported_shapes(plugin, small, change, code):
+    """Shapes the kernels do not cover come back as status codes (nothing is launched)."""
+    bad = dataclasses.replace(small, cfg=dataclasses.replace(SMALL, **change))
+    with pytest.raises(KataliError) as e:
+        HybridModel(plugin, bad)
+    assert e.value.code == code
+
+
+def test_create_rejects_missing_router(plugin, small):
+    layers = [dict(w) for w in small.layers]
+    layers[1]["router"] = None
+    bad = dataclasses.replace(small, layers=layers)
+    with pytest.raises(KataliError) as e:
+        HybridModel(plugin, bad)
+    assert e.value.code == 3
