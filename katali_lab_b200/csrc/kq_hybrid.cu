@@ -17,8 +17,9 @@
 // as V/src/gguf_kernels.c:45-61), GQA decode attention as the dense decoder (kq_dense.cu), the
 // head output multiplied by sigmoid(gate).
 // MoE block: RMSNorm (ffn_norm), fp32 router GEMV (double accumulation, as the reference's
-// F32 dot, V/src/gguf_dtype.c:640-644), then the fused MoE kernel (kq_moe.cu) adding its
-// output into the residual stream.
+// F32 dot, V/src/gguf_dtype.c:640-644) and the fused MoE kernel (kq_moe.cu) adding its output
+// into the residual stream. On one GPU the RMSNorm and the router run inside the MoE launch
+// (MoeParams.rt_w); under expert parallelism k_router below runs before the MoE launch.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
