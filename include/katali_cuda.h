@@ -422,6 +422,19 @@ int katali_cuda_gguf_array_int(const KataliGguf *g, const char *key, uint64_t i,
  * katali_cuda_malloc) on the plugin stream through pinned staging buffers;
  * returns after the copy has finished. */
 int katali_cuda_gguf_upload(KataliGguf *g, uint64_t index, void *dev);
+/* The on-device dense decoder (section 8) of a qwen3-architecture file: dimensions from
+ * the metadata (qwen3.block_count, embedding_length, feed_forward_length,
+ * attention.head_count[_kv], attention.key_length, rope.freq_base,
+ * attention.layer_norm_rms_epsilon, rope.dimension_count), tensors by their llama.cpp
+ * names (token_embd, output_norm, output — the embedding when absent —, blk.N.attn_norm,
+ * attn_q, attn_k, attn_v, attn_output, attn_q_norm, attn_k_norm, ffn_norm, ffn_gate,
+ * ffn_up, ffn_down), uploaded unchanged into one device allocation that the decoder owns
+ * (freed by katali_cuda_dense_destroy). The file may be closed afterwards. A missing
+ * tensor or metadata key, or an fp32 norm of the wrong size, returns KATALI_ERR_BAD_ARG;
+ * another architecture KATALI_ERR_UNSUPPORTED_SHAPE; matrices of other types
+ * KATALI_ERR_UNSUPPORTED_TYPE. flags as KataliDenseDesc.flags. */
+int katali_cuda_dense_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t flags,
+                                       KataliDense **out);
 
 /* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */

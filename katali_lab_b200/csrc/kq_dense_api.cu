@@ -47,7 +47,13 @@ struct KataliDense {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     cudaStream_t graph_stream = nullptr;
+    void *weights = nullptr;        // weight memory owned for the caller (a decoder made from a file)
 };
+
+namespace kq {
+// A decoder created from a model file owns the device memory its weights were uploaded to.
+void dense_adopt_weights(KataliDense *m, void *mem) { m->weights = mem; }
+}  // namespace kq
 
 namespace {
 
@@ -268,6 +274,7 @@ int katali_cuda_dense_destroy(KataliDense *m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     cudaFree(m->mem);
+    cudaFree(m->weights);
     delete m;
     return KATALI_OK;
 }

@@ -30,6 +30,7 @@
 namespace kq {
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
+void dense_adopt_weights(KataliDense *m, void *mem);
 }  // namespace kq
 
 namespace {
@@ -394,6 +395,170 @@ int katali_cuda_gguf_upload(KataliGguf *g, uint64_t i, void *dev) {
         kq::set_status_message(cudaGetErrorString(e));
         return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
     }
+    return KATALI_OK;
+}
+
+
+// A Qwen3-layout dense decoder straight from a model file: metadata (llama.cpp key names under
+// the file's general.architecture), tensors by their llama.cpp names (token_embd, output_norm,
+// output — the embedding when absent —, blk.N.attn_norm / attn_q / attn_k / attn_v /
+// attn_output / attn_q_norm / attn_k_norm / ffn_norm / ffn_gate / ffn_up / ffn_down), every
+// tensor uploaded unchanged into one device allocation the decoder then owns.
+int katali_cuda_dense_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t flags,
+                                       KataliDense **out) {
+    if (!g || !out || !kv_cap) return KATALI_ERR_BAD_ARG;
+    *out = nullptr;
+    const char *arch = nullptr;
+    uint64_t alen = 0;
+    if (katali_cuda_gguf_get_str(g, "general.architecture", &arch, &alen) != KATALI_OK)
+        return fail(nullptr, "katali_cuda_dense_create_from_gguf: no general.architecture");
+    const std::string A(arch, (size_t)alen);
+    if (A != "qwen3") {
+        kq::set_status_message("katali_cuda_dense_create_from_gguf: architecture is not qwen3");
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    }
+    auto meta = [&](const char *key, int64_t def) {
+        int64_t v = def;
+        if (katali_cuda_gguf_get_int(g, (A + "." + key).c_str(), &v) != KATALI_OK) v = def;
+        return v;
+    };
+    auto metaf = [&](const char *key, double def) {
+        double v = def;
+        if (katali_cuda_gguf_get_float(g, (A + "." + key).c_str(), &v) != KATALI_OK) v = def;
+        return v;
+    };
+    const int64_t NL = meta("block_count", 0), H = meta("embedding_length", 0),
+                  F = meta("feed_forward_length", 0), NH = meta("attention.head_count", 0);
+    const int64_t NKV = meta("attention.head_count_kv", NH);
+    const int64_t HD = meta("attention.key_length", NH > 0 ? H / NH : 0);
+    const int64_t RD = meta("rope.dimension_count", 0);
+    if (NL <= 0 || H <= 0 || F <= 0 || NH <= 0 || NKV <= 0 || HD <= 0 || NL > 4096)
+        return fail(nullptr, "katali_cuda_dense_create_from_gguf: missing or bad qwen3 dimensions");
+
+    // every tensor: index, with its expected type class (0: fp32 norm, 1: GGUF matrix), dims
+    struct Want {
+        uint64_t idx;
+        uint64_t off;
+    };
+    std::vector<Want> wants;
+    uint64_t total = 0;
+    auto take = [&](const std::string &name, bool matrix, uint64_t d0, uint64_t d1, uint64_t *slot,
+                    uint32_t *type, bool optional = false) -> int {
+        uint64_t i = 0;
+        if (katali_cuda_gguf_find(g, name.c_str(), &i) != KATALI_OK) {
+            if (optional) {
+                *slot = UINT64_MAX;
+                return KATALI_OK;
+            }
+            kq::set_status_message(("katali_cuda_dense_create_from_gguf: missing tensor " + name).c_str());
+            return KATALI_ERR_BAD_ARG;
+        }
+        const Tensor &t = g->t[(size_t)i];
+        const bool shape_ok = matrix ? (t.n_dims == 2 && t.dims[0] == d0 && t.dims[1] == d1)
+                                     : (t.n_dims == 1 && t.dims[0] == d0 && t.type == 0);
+        if (!shape_ok || !t.nbytes) {
+            kq::set_status_message(("katali_cuda_dense_create_from_gguf: unexpected shape or type of " + name).c_str());
+            return matrix ? KATALI_ERR_UNSUPPORTED_TYPE : KATALI_ERR_BAD_ARG;
+        }
+        if (type) *type = t.type;
+        *slot = wants.size();
+        wants.push_back(Want{i, total});
+        total += (t.nbytes + 255) & ~(uint64_t)255;
+        return KATALI_OK;
+    };
+    uint64_t emb_i, on_i, lm_i;
+    uint32_t emb_t = 0, lm_t = 0;
+    uint64_t vocab = 0;
+    {
+        uint64_t i = 0;
+        if (katali_cuda_gguf_find(g, "token_embd.weight", &i) != KATALI_OK || g->t[(size_t)i].n_dims != 2)
+            return fail(nullptr, "katali_cuda_dense_create_from_gguf: missing tensor token_embd.weight");
+        vocab = g->t[(size_t)i].dims[1];
+    }
+    int s;
+    if ((s = take("token_embd.weight", true, (uint64_t)H, vocab, &emb_i, &emb_t))) return s;
+    if ((s = take("output_norm.weight", false, (uint64_t)H, 0, &on_i, nullptr))) return s;
+    if ((s = take("output.weight", true, (uint64_t)H, vocab, &lm_i, &lm_t, true))) return s;
+    if (lm_i == UINT64_MAX) {  // tied embeddings: the LM head is the embedding matrix
+        lm_i = emb_i;
+        lm_t = emb_t;
+    }
+    struct LayerSlots {
+        uint64_t an, fn, qn, kn, w[7];
+        uint32_t t[7];
+    };
+    std::vector<LayerSlots> ls((size_t)NL);
+    const char *mats[7] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+    const uint64_t cols[7] = {(uint64_t)H, (uint64_t)H, (uint64_t)H, (uint64_t)(NH * HD),
+                              (uint64_t)H, (uint64_t)H, (uint64_t)F};
+    const uint64_t rows[7] = {(uint64_t)(NH * HD), (uint64_t)(NKV * HD), (uint64_t)(NKV * HD),
+                              (uint64_t)H, (uint64_t)F, (uint64_t)F, (uint64_t)H};
+    for (int64_t l = 0; l < NL; ++l) {
+        const std::string pfx = "blk." + std::to_string(l) + ".";
+        LayerSlots &L = ls[(size_t)l];
+        if ((s = take(pfx + "attn_norm.weight", false, (uint64_t)H, 0, &L.an, nullptr))) return s;
+        if ((s = take(pfx + "ffn_norm.weight", false, (uint64_t)H, 0, &L.fn, nullptr))) return s;
+        if ((s = take(pfx + "attn_q_norm.weight", false, (uint64_t)HD, 0, &L.qn, nullptr, true))) return s;
+        if ((s = take(pfx + "attn_k_norm.weight", false, (uint64_t)HD, 0, &L.kn, nullptr, true))) return s;
+        for (int j = 0; j < 7; ++j)
+            if ((s = take(pfx + mats[j] + ".weight", true, cols[j], rows[j], &L.w[j], &L.t[j]))) return s;
+    }
+    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    unsigned char *mem = nullptr;
+    cudaError_t e = cudaMalloc((void **)&mem, total);
+    if (e != cudaSuccess) {
+        kq::set_status_message(cudaGetErrorString(e));
+        return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
+    }
+    for (const Want &w : wants)
+        if ((s = katali_cuda_gguf_upload(g, w.idx, mem + w.off)) != KATALI_OK) {
+            cudaFree(mem);
+            return s;
+        }
+    auto ptr = [&](uint64_t slot) -> const void * {
+        return slot == UINT64_MAX ? nullptr : mem + wants[(size_t)slot].off;
+    };
+    std::vector<KataliDenseLayerW> lw((size_t)NL);
+    for (int64_t l = 0; l < NL; ++l) {
+        const LayerSlots &L = ls[(size_t)l];
+        KataliDenseLayerW &w = lw[(size_t)l];
+        w.attn_norm = (const float *)ptr(L.an);
+        w.ffn_norm = (const float *)ptr(L.fn);
+        w.q_norm = (const float *)ptr(L.qn);
+        w.k_norm = (const float *)ptr(L.kn);
+        const void **m[7] = {&w.wq, &w.wk, &w.wv, &w.wo, &w.gate, &w.up, &w.down};
+        uint32_t *t[7] = {&w.wq_type, &w.wk_type, &w.wv_type, &w.wo_type, &w.gate_type, &w.up_type,
+                          &w.down_type};
+        for (int j = 0; j < 7; ++j) {
+            *m[j] = ptr(L.w[j]);
+            *t[j] = L.t[j];
+        }
+    }
+    KataliDenseDesc d = {};
+    d.n_layers = (uint32_t)NL;
+    d.hidden = (uint32_t)H;
+    d.ffn = (uint32_t)F;
+    d.n_heads = (uint32_t)NH;
+    d.n_kv_heads = (uint32_t)NKV;
+    d.head_dim = (uint32_t)HD;
+    d.vocab = (uint32_t)vocab;
+    d.kv_cap = kv_cap;
+    d.rope_dim = (uint32_t)(RD > 0 ? RD : 0);
+    d.rms_eps = (float)metaf("attention.layer_norm_rms_epsilon", 1e-6);
+    d.rope_theta = (float)metaf("rope.freq_base", 1e6);
+    d.embed = ptr(emb_i);
+    d.embed_type = emb_t;
+    d.out_norm = (const float *)ptr(on_i);
+    d.lm_head = ptr(lm_i);
+    d.lm_head_type = lm_t;
+    d.layers = lw.data();
+    d.flags = flags;
+    s = katali_cuda_dense_create(&d, out);
+    if (s != KATALI_OK) {
+        cudaFree(mem);
+        return s;
+    }
+    kq::dense_adopt_weights(*out, mem);
     return KATALI_OK;
 }
 

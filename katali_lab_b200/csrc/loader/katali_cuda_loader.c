@@ -126,6 +126,8 @@
     X(int, katali_cuda_gguf_array_int,                                                        \
       (const KataliGguf *g, const char *k, uint64_t i, int64_t *v), (g, k, i, v))             \
     X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
+    X(int, katali_cuda_dense_create_from_gguf,                                                \
+      (KataliGguf * g, uint32_t c, uint32_t f, KataliDense **o), (g, c, f, o))                \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -306,6 +308,8 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_gguf_array_int,                                                        \
       (const KataliGguf *g, const char *k, uint64_t i, int64_t *v), (g, k, i, v))             \
     X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
+    X(int, katali_cuda_dense_create_from_gguf,                                                \
+      (KataliGguf * g, uint32_t c, uint32_t f, KataliDense **o), (g, c, f, o))                \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

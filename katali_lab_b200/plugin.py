@@ -165,6 +165,7 @@ class Plugin:
             "katali_cuda_gguf_array": ([_vp, C.c_char_p, C.POINTER(_u32), C.POINTER(_u64)], _i32),
             "katali_cuda_gguf_array_int": ([_vp, C.c_char_p, _u64, C.POINTER(C.c_int64)], _i32),
             "katali_cuda_gguf_upload": ([_vp, _u64, _vp], _i32),
+            "katali_cuda_dense_create_from_gguf": ([_vp, _u32, _u32, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -365,6 +366,20 @@ class DenseModel:
         plugin.check(plugin.L.katali_cuda_dense_create(C.byref(desc), C.byref(h)))
         self.h = h
         self.vocab = cfg.vocab
+
+    @classmethod
+    def from_gguf(cls, plugin: Plugin, gguf, kv_cap: int, q8: bool = False) -> "DenseModel":
+        """The decoder of a qwen3-architecture GGUF file (katali_cuda_dense_create_from_gguf);
+        gguf: an open katali_lab_b200.Gguf."""
+        self = cls.__new__(cls)
+        self.p = plugin
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_dense_create_from_gguf(gguf.h, kv_cap, 1 if q8 else 0,
+                                                                 C.byref(h)))
+        self.h = h
+        nt = gguf.find("token_embd.weight")
+        self.vocab = gguf.tensor(nt)["dims"][1]
+        return self
 
     def reset(self) -> None:
         self.p.check(self.p.L.katali_cuda_dense_reset(self.h))

@@ -134,3 +134,48 @@ def test_malformed_rejected_by_both(lib, ref, tmp_path, case):
 def test_missing_file(lib, tmp_path):
     with pytest.raises(KataliError):
         Gguf(lib, str(tmp_path / "absent.gguf"))
+
+
+def _dense_file(tmp_path, drop=None, arch="qwen3"):
+    from oracle.oracle import Port
+    from katali_lab_b200.synth import DenseConfig
+    from tests.gguf_files import STR, build, dense_model_file
+    import struct
+    cfg = DenseConfig(n_layers=2, hidden=256, ffn=512, n_heads=2, n_kv_heads=1, head_dim=128,
+                      vocab=256, kv_cap=32)
+    data, _ = dense_model_file(Port(), cfg, seed=1)
+    g_path = tmp_path / "d.gguf"
+    g_path.write_bytes(data)
+    if drop is None and arch == "qwen3":
+        return g_path
+    # rebuild with one tensor renamed away or another architecture string
+    L = Plugin()
+    g = Gguf(L, str(g_path))
+    tensors = []
+    for t in g.tensors():
+        name = t["name"] if t["name"] != drop else "unused.weight"
+        tensors.append((name, t["type"], t["dims"], data[t["offset"]:t["offset"] + t["nbytes"]]))
+    kvs = [("general.architecture", STR, arch)]
+    for key in ("block_count", "embedding_length", "feed_forward_length", "attention.head_count",
+                "attention.head_count_kv", "attention.key_length", "context_length"):
+        kvs.append((f"{arch}.{key}", 4, g.get_int(f"qwen3.{key}")))
+    g.close()
+    out, _ = build(kvs, tensors)
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(out)
+    return p
+
+
+@pytest.mark.parametrize("drop,arch,code", [("blk.1.ffn_up.weight", "qwen3", 3),
+                                            (None, "llama", 5)])
+def test_dense_from_gguf_rejects_before_any_gpu_work(lib, tmp_path, drop, arch, code):
+    """A missing tensor or another architecture is reported from the file alone."""
+    import ctypes as C2
+    path = _dense_file(tmp_path, drop=drop, arch=arch)
+    g = Gguf(lib, str(path))
+    h = C2.c_void_p()
+    rc = lib.L.katali_cuda_dense_create_from_gguf(g.h, 16, 0, C2.byref(h))
+    assert rc == code
+    if drop:
+        assert drop in lib.status()
+    g.close()

@@ -71,3 +71,45 @@ def test_gguf_upload_and_decode(plugin, ref, port, tmp_path):
         assert tok_g == tok_c, s
     rd.close()
     dm.close()
+
+
+def test_dense_decoder_straight_from_gguf(plugin, ref, port, tmp_path):
+    """katali_cuda_dense_create_from_gguf builds the decoder from the file alone (metadata,
+    tensor names, uploads); its greedy tokens and logits equal the reference CPU decode of the
+    same file's tensors."""
+    import torch
+    data, _ = dense_model_file(port, CFG, seed=13)
+    path = tmp_path / "dense.gguf"
+    path.write_bytes(data)
+    g = Gguf(plugin, str(path))
+    dm = DenseModel.from_gguf(plugin, g, kv_cap=CFG.kv_cap)
+    # the reference decode on host copies of the same tensors
+    host = {t["name"]: torch.from_numpy(np.frombuffer(data, np.uint8, t["nbytes"], t["offset"]).copy())
+            for t in g.tensors()}
+    types_ = {t["name"]: t["type"] for t in g.tensors()}
+    g.close()
+    f32 = lambda n: host[n].view(torch.float32)  # noqa: E731
+    names = {"wq": "attn_q", "wk": "attn_k", "wv": "attn_v", "wo": "attn_output", "gate": "ffn_gate",
+             "up": "ffn_up", "down": "ffn_down"}
+    layers = [{**{k: host[f"blk.{l}.{v}.weight"] for k, v in names.items()},
+               "attn_norm": f32(f"blk.{l}.attn_norm.weight"), "ffn_norm": f32(f"blk.{l}.ffn_norm.weight"),
+               "q_norm": f32(f"blk.{l}.attn_q_norm.weight"), "k_norm": f32(f"blk.{l}.attn_k_norm.weight")}
+              for l in range(CFG.n_layers)]
+    model = types.SimpleNamespace(
+        cfg=CFG, embed=host["token_embd.weight"], lm_head=host["output.weight"],
+        out_norm=f32("output_norm.weight"), layers=layers,
+        types={**{k: types_[f"blk.0.{v}.weight"] for k, v in names.items()},
+               "embed": types_["token_embd.weight"], "lm_head": types_["output.weight"]})
+    rd = RefDense(ref, model)
+    tok_g = tok_c = 11
+    for s in range(10):
+        tok_g = int(dm.generate([tok_g], 1)[0])
+        lc = rd.step(tok_c, s)
+        tok_c = port.argmax(lc)
+        ptr, _ = dm.logits()
+        lg = np.empty(CFG.vocab, np.float32)
+        plugin.check(plugin.L.katali_cuda_download(lg.ctypes.data, ptr, lg.nbytes))
+        assert rel_l2(lg, lc) <= 1e-5, s
+        assert tok_g == tok_c, s
+    rd.close()
+    dm.close()
