@@ -108,6 +108,8 @@ __device__ __forceinline__ void route_one(const MoeBatchParams &p, int t, float 
 
 __global__ void __launch_bounds__(BT) moe_batch_route(MoeBatchParams p) {
     __shared__ float s_lg[1024];
+    pdl_trigger();
+    pdl_wait();
     route_one(p, blockIdx.x, s_lg);
 }
 
@@ -192,6 +194,8 @@ __device__ void group_body(const MoeBatchParams &p, int *cnt, int *off, int *wsu
 
 __global__ void __launch_bounds__(1024) moe_batch_group(MoeBatchParams p) {
     __shared__ int cnt[1024], off[1024], wsum[32];
+    pdl_trigger();
+    pdl_wait();
     group_body(p, cnt, off, wsum);
 }
 
@@ -421,6 +425,8 @@ template <uint32_t GT, uint32_t UT>
 __global__ void __launch_bounds__(BT, 3) moe_batch_gateup(MoeBatchParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ int s_next[2];
+    pdl_trigger();
+    pdl_wait();
     const ItemSmem S = item_smem(sm, (size_t)p.gu_rows * (p.rbg + p.rbu));
     init_tiles_bar(S.bar);
     ItemState st{0u, 0};
@@ -442,6 +448,8 @@ __device__ __forceinline__ void hquant_range(const MoeBatchParams &p, int w0, in
     }
 }
 __global__ void __launch_bounds__(BT) moe_batch_hquant(MoeBatchParams p) {
+    pdl_trigger();
+    pdl_wait();
     hquant_range(p, (blockIdx.x * BT + threadIdx.x) >> 5, gridDim.x * (BT / 32));
 }
 
@@ -519,6 +527,8 @@ template <uint32_t DT>
 __global__ void __launch_bounds__(BT, 4) moe_batch_down(MoeBatchParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     __shared__ int s_next[2];
+    pdl_trigger();
+    pdl_wait();
     const ItemSmem S = item_smem(sm, (size_t)p.dn_rows * p.rbd);
     init_tiles_bar(S.bar);
     ItemState st{0u, 0};
@@ -538,6 +548,8 @@ __device__ __forceinline__ void combine_range(const MoeBatchParams &p, int i0, i
     }
 }
 __global__ void __launch_bounds__(BT) moe_batch_combine(MoeBatchParams p) {
+    pdl_trigger();
+    pdl_wait();
     combine_range(p, blockIdx.x * BT + threadIdx.x, gridDim.x * BT);
 }
 
@@ -778,7 +790,7 @@ static void set_smem(KernelT k, size_t bytes) {
 // Launches a grid-stride item kernel on min(worst-case items, resident CTAs) CTAs.
 template <typename KernelT>
 static void launch_items(KernelT k, int max_items, size_t smem, int sms, const MoeBatchParams &p,
-                         cudaStream_t st) {
+                         cudaStream_t st, int pdl) {
     // The limit is set on every launch: another layer shape may have lowered it.
     set_smem(k, smem);
     // resident CTAs per SM, asked once per (kernel, shared-memory size) and thread
@@ -797,7 +809,7 @@ static void launch_items(KernelT k, int max_items, size_t smem, int sms, const M
     }
     const int resident = per_sm * (sms > 0 ? sms : 1);
     const int grid = max_items < resident ? max_items : resident;
-    if (grid > 0) k<<<grid, BT, smem, st>>>(p);
+    if (grid > 0) launch_k(k, dim3(grid), dim3(BT), smem, st, pdl, p);
 }
 
 // Tile heights: three CTAs per SM, each weight tile + staged activations within ~70 KB.
@@ -807,36 +819,38 @@ static void plan_tiles(MoeBatchParams &p) {
     p.dn_rows = tile_rows(p.rbd, 64, budget);
 }
 
-// group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots)
-static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st) {
+// group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots).
+// pdl: every launch a programmatic dependent of the one before (each kernel waits for its
+// predecessor before its first statement); the tensor-core gate/up launch stays ordinary.
+static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st, int pdl = 0) {
     plan_tiles(p);
-    moe_batch_group<<<1, (p.n_experts + 31) / 32 * 32, 0, st>>>(p);
+    launch_k(moe_batch_group, dim3(1), dim3((p.n_experts + 31) / 32 * 32), 0, st, pdl, p);
     const int gitems = max_groups * ((p.F + p.gu_rows - 1) / p.gu_rows);
     const size_t gsm = item_smem_bytes((size_t)p.gu_rows * (p.rbg + p.rbu), p.H);
     if (p.gate_type == T_Q4_K && p.up_type == T_Q4_K)
-        launch_items(moe_batch_gateup<T_Q4_K, T_Q4_K>, gitems, gsm, p.sms, p, st);
+        launch_items(moe_batch_gateup<T_Q4_K, T_Q4_K>, gitems, gsm, p.sms, p, st, pdl);
     else if (p.gate_type == T_Q4_K)
-        launch_items(moe_batch_gateup<T_Q4_K, T_Q6_K>, gitems, gsm, p.sms, p, st);
+        launch_items(moe_batch_gateup<T_Q4_K, T_Q6_K>, gitems, gsm, p.sms, p, st, pdl);
     else if (p.up_type == T_Q4_K)
-        launch_items(moe_batch_gateup<T_Q6_K, T_Q4_K>, gitems, gsm, p.sms, p, st);
+        launch_items(moe_batch_gateup<T_Q6_K, T_Q4_K>, gitems, gsm, p.sms, p, st, pdl);
     else
-        launch_items(moe_batch_gateup<T_Q6_K, T_Q6_K>, gitems, gsm, p.sms, p, st);
+        launch_items(moe_batch_gateup<T_Q6_K, T_Q6_K>, gitems, gsm, p.sms, p, st, pdl);
     if (p.tc_min > 0) launch_gateup_tc(p, max_groups, st);
     const int P = p.T * p.K;
-    moe_batch_hquant<<<(P * (p.F / 32) * 32 + BT - 1) / BT, BT, 0, st>>>(p);
+    launch_k(moe_batch_hquant, dim3((P * (p.F / 32) * 32 + BT - 1) / BT), dim3(BT), 0, st, pdl, p);
     const int ditems = max_groups * ((p.H + p.dn_rows - 1) / p.dn_rows);
     const size_t dsm = item_smem_bytes((size_t)p.dn_rows * p.rbd, p.F);
     if (p.down_type == T_Q6_K)
-        launch_items(moe_batch_down<T_Q6_K>, ditems, dsm, p.sms, p, st);
+        launch_items(moe_batch_down<T_Q6_K>, ditems, dsm, p.sms, p, st, pdl);
     else
-        launch_items(moe_batch_down<T_Q4_K>, ditems, dsm, p.sms, p, st);
+        launch_items(moe_batch_down<T_Q4_K>, ditems, dsm, p.sms, p, st, pdl);
 }
 
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {
     const int P = p.T * p.K;
     moe_batch_route<<<p.T, BT, 0, st>>>(p);
-    launch_experts(p, P < p.n_experts ? P : p.n_experts, st);
-    moe_batch_combine<<<(p.T * p.H + BT - 1) / BT, BT, 0, st>>>(p);
+    launch_experts(p, P < p.n_experts ? P : p.n_experts, st, 1);
+    launch_k(moe_batch_combine, dim3((p.T * p.H + BT - 1) / BT), dim3(BT), 0, st, 1, p);
     return cudaGetLastError();
 }
 
