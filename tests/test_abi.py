@@ -9,7 +9,8 @@ import sys
 import pytest
 
 from katali_lab_b200 import build as B
-from katali_lab_b200.plugin import KataliMoeDesc, Plugin, header_symbols
+from katali_lab_b200.plugin import (KataliHybridDesc, KataliHybridLayerW, KataliMoeDesc, Plugin,
+                                    header_symbols)
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -91,6 +92,13 @@ def test_no_device_is_an_error_code_not_a_crash(built):
     desc = KataliMoeDesc(8, 512, 256, 2, 12, 12, 14, 1, None)
     h = C.c_void_p()
     assert p.L.katali_cuda_moe_create(C.byref(desc), C.byref(h)) == 1
+    # the decoders check their arguments first, then the device
+    layer = (KataliHybridLayerW * 1)()
+    hd = KataliHybridDesc(n_layers=1, hidden=2048, vocab=256, kv_cap=16, layers=layer)
+    assert p.L.katali_cuda_hybrid_create(None, C.byref(h)) == 3
+    assert p.L.katali_cuda_hybrid_create(C.byref(hd), None) == 3
+    assert p.L.katali_cuda_hybrid_create(C.byref(hd), C.byref(h)) == 1
+    assert not h.value
 
 
 def test_argument_checks_before_device(built):
