@@ -41,3 +41,31 @@ def test_c5_layer_mix_and_expert_bytes():
     assert kinds.count(0) == 30 and kinds.count(1) == 10
     assert c.ssm_v_heads % c.ssm_k_heads == 0
     assert c.n_layers * c.top_k * bench.EXPERT_BYTES == 652_738_560
+
+
+def test_hybrid_ep_view_partitions_every_layers_experts():
+    """Each rank's view holds the contiguous block [r E/G, (r+1) E/G) of every layer's
+    experts, as views of the full store, and the blocks of all ranks tile the store."""
+    import torch
+    from dataclasses import replace
+    from katali_lab_b200.synth import ExpertStore, HybridWeights, hybrid_ep_view
+    cfg = replace(HYBRID_35B, n_layers=2, n_experts=16)
+    layers = []
+    for l in range(cfg.n_layers):
+        st = ExpertStore(torch.arange(16 * 4, dtype=torch.uint8).view(16, 4) + l,
+                         torch.zeros(16, 4, dtype=torch.uint8), torch.zeros(16, 2, dtype=torch.uint8),
+                         cfg.hidden, cfg.ffn)
+        layers.append({"kind": cfg.kind(l), "experts": st})
+    full = HybridWeights(cfg, None, None, None, layers, {})
+    for G in (1, 2, 4, 8):
+        seen = [[] for _ in range(cfg.n_layers)]
+        for r in range(G):
+            v = hybrid_ep_view(full, G, r)
+            for l, w in enumerate(v.layers):
+                st = w["experts"]
+                assert st.n_experts == 16 // G and w["expert_base"] == r * (16 // G)
+                assert st.gate.data_ptr() == layers[l]["experts"].gate[r * (16 // G)].data_ptr()
+                assert st.expert_bytes == layers[l]["experts"].expert_bytes
+                seen[l].extend(st.gate[:, 0].tolist())
+        for l in range(cfg.n_layers):
+            assert seen[l] == layers[l]["experts"].gate[:, 0].tolist()
