@@ -167,8 +167,8 @@ int katali_cuda_moe_batch(KataliMoe *m, uint32_t n_tokens, const float *x,
  * Limits: n_experts <= KATALI_MOE_STATIC_MAX_EXPERTS and
  * top_k * ffn <= KATALI_MOE_STATIC_MAX_TOPK_FFN, else
  * KATALI_ERR_UNSUPPORTED_SHAPE (katali_cuda_status() says which). Runs on
- * `stream` (a cudaStream_t, NULL = default stream) and returns after it
- * finished. The first call on a device looks the array up for that device:
+ * `stream` (a cudaStream_t, NULL = default stream) and is synchronous: it
+ * returns after the layer finished, with the kernel's status read back. The first call on a device looks the array up for that device:
  * make it before any stream capture. All calls share the array, so calls that
  * overlap on the GPU race; serialise them. */
 #define KATALI_MOE_STATIC_MAX_EXPERTS 1024

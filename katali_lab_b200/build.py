@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -20,6 +21,7 @@ LIBDIR = os.path.join(PKG, "lib")
 PLUGIN = os.path.join(LIBDIR, "libkatali_cuda.so")
 LOADER = os.path.join(LIBDIR, "libkatali_cuda_loader.so")
 CHECK = os.path.join(LIBDIR, "katali_cuda_check")  # command-line checks (cuda-info / cuda-check ...)
+OBJDIR = os.path.join(LIBDIR, "obj")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -38,21 +40,36 @@ def _stale(target: str, deps: list[str]) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def _compile(src: str, obj: str, verbose: bool) -> str:
+    cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-c", "-Xcompiler", "-fPIC",
+           "-Xptxas", "-v" if verbose else "-O3", "-I", INCLUDE, "-I", CSRC, "-o", obj, src]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stdout}{r.stderr}")
+    return r.stderr if verbose else ""
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
-    os.makedirs(LIBDIR, exist_ok=True)
+    """Compile every csrc/*.cu to an object (in parallel, only the stale ones), link the
+    plugin, then the loader and the check CLI."""
+    os.makedirs(OBJDIR, exist_ok=True)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    deps = srcs + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) \
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) \
         + glob.glob(os.path.join(INCLUDE, "*.h"))
-    if force or _stale(PLUGIN, deps):
-        cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--shared",
-               "-Xcompiler", "-fPIC", "-Xptxas", "-v" if verbose else "-O3",
-               "-I", INCLUDE, "-I", CSRC, "-o", PLUGIN, *srcs, "-ldl"]
+    deps = srcs + headers
+    objs = [os.path.join(OBJDIR, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    todo = [(s, o) for s, o in zip(srcs, objs) if force or _stale(o, [s] + headers)]
+    if todo:
+        with ThreadPoolExecutor(max_workers=min(len(todo), os.cpu_count() or 4)) as ex:
+            for log in ex.map(lambda so: _compile(so[0], so[1], verbose), todo):
+                if log:
+                    sys.stderr.write(log)
+    if force or todo or _stale(PLUGIN, objs):
+        cmd = [_nvcc(), *ARCH, "--shared", "-Xcompiler", "-fPIC", "-o", PLUGIN, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
-            raise RuntimeError("nvcc failed")
-        if verbose:
-            sys.stderr.write(r.stderr)
+            raise RuntimeError("nvcc link failed")
     loader_src = os.path.join(CSRC, "loader", "katali_cuda_loader.c")
     cc = os.environ.get("CC", "gcc")
     if os.path.exists(loader_src) and (force or _stale(LOADER, [loader_src] + deps)):

@@ -372,16 +372,7 @@ __global__ void row_isums_kernel(uint32_t type, const uint8_t *w, uint64_t rows,
 // ---------------------------------------------------------------------------
 namespace kq {
 
-static int g_num_sms = 0;
-static int num_sms() {
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
-    return g_num_sms;
-}
+static int num_sms() { return device_sms(); }
 
 cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     // Rows per tile: ~16 KB stages; Q6_K tiles in row multiples that keep every
@@ -431,11 +422,10 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
         {gemv_kernel<0, GEMV_CW_SMALL>, gemv_kernel<1, GEMV_CW_SMALL>, gemv_kernel<2, GEMV_CW_SMALL>},
         {gemv_kernel<0, GEMV_CW_BIG>, gemv_kernel<1, GEMV_CW_BIG>, gemv_kernel<2, GEMV_CW_BIG>}};
     void (*fn)(GemvParams) = fns[big][mode];
-    static size_t set_bytes[2][3] = {{0, 0, 0}, {0, 0, 0}};
-    if (smem > set_bytes[big][mode]) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static size_t set_bytes[2][3][KQ_MAX_DEVICES];
+    {
+        cudaError_t e = ensure_smem_limit(fn, smem, set_bytes[big][mode]);
         if (e != cudaSuccess) return e;
-        set_bytes[big][mode] = smem;
     }
     int per = 2;
     if (three && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, fn, threads, smem) != cudaSuccess)

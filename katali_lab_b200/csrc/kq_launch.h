@@ -43,6 +43,38 @@ struct GemvParams {
     int pdl;  // 1: launched as a programmatic dependent of the previous kernel on the stream
 };
 
+// Kernel attributes such as the dynamic shared-memory limit belong to a device, so what a
+// launcher remembers about them is kept per device. Devices with an id of KQ_MAX_DEVICES or
+// more are not cached: their attribute is set on every launch.
+constexpr int KQ_MAX_DEVICES = 64;
+inline int current_device() {
+    int d = -1;
+    if (cudaGetDevice(&d) != cudaSuccess) d = -1;
+    return d;
+}
+// Raises k's dynamic shared-memory limit on the current device to at least `bytes`;
+// per_device[d] holds the limit already set on device d.
+template <typename KernelT>
+inline cudaError_t ensure_smem_limit(KernelT k, size_t bytes, size_t *per_device) {
+    const int d = current_device();
+    const bool cached = d >= 0 && d < KQ_MAX_DEVICES;
+    if (cached && per_device[d] >= bytes) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess && cached) per_device[d] = bytes;
+    return e;
+}
+// SM count of the current device (cached per device).
+inline int device_sms() {
+    static int sms[KQ_MAX_DEVICES];
+    const int d = current_device();
+    if (d >= 0 && d < KQ_MAX_DEVICES && sms[d] > 0) return sms[d];
+    int n = 0;
+    if (d < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0)
+        n = 148;
+    if (d >= 0 && d < KQ_MAX_DEVICES) sms[d] = n;
+    return n;
+}
+
 // Launch of kernel k, as a programmatic dependent of the previous kernel on st when pdl
 // (the kernel then follows the pdl_wait() rule of kq_device.cuh).
 template <typename... KArgs, typename... Args>

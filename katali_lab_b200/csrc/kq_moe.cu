@@ -1163,13 +1163,12 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
 
 template <int MODE, uint32_t DT, int SHAPE, int EP = 0, int RT = 0>
 static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
-    static uint32_t set_bytes = 0;  // raise the smem limit once per size, before any capture
-    if (p.smem_bytes > set_bytes) {
-        cudaError_t e = cudaFuncSetAttribute(moe_kernel<MODE, DT, SHAPE, EP, RT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)p.smem_bytes);
+    // The shared-memory limit is raised once per device and size (an eager call precedes
+    // any capture on that device).
+    static size_t set_bytes[KQ_MAX_DEVICES];
+    {
+        cudaError_t e = ensure_smem_limit(moe_kernel<MODE, DT, SHAPE, EP, RT>, p.smem_bytes, set_bytes);
         if (e != cudaSuccess) return e;
-        set_bytes = p.smem_bytes;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
@@ -1182,15 +1181,18 @@ static cudaError_t launch_t(MoeParams &p, int grid, cudaStream_t st) {
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    // A programmatic launch when asked for and accepted: the first such launch (always an
-    // eager one, before any graph capture) that the runtime refuses switches it off.
-    static int pdl_ok = 1;
-    const bool pdl = p.pdl && pdl_ok && !EP && !p.route_only;
+    // A programmatic launch when asked for and accepted: the first such launch on a device
+    // (always an eager one, before any graph capture) that the runtime refuses switches it
+    // off for that device.
+    static int pdl_refused[KQ_MAX_DEVICES];
+    const int dev = current_device();
+    const bool dev_ok = dev < 0 || dev >= KQ_MAX_DEVICES || !pdl_refused[dev];
+    const bool pdl = p.pdl && dev_ok && !EP && !p.route_only;
     cfg.numAttrs = pdl ? 2 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP, RT>, p);
     if (pdl && (e == cudaErrorInvalidValue || e == cudaErrorNotSupported)) {
         cudaGetLastError();
-        pdl_ok = 0;
+        if (dev >= 0 && dev < KQ_MAX_DEVICES) pdl_refused[dev] = 1;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, moe_kernel<MODE, DT, SHAPE, EP, RT>, p);
     }

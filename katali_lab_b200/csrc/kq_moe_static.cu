@@ -15,7 +15,9 @@
 // (cudaGetSymbolAddress), so make that first call before any stream capture.
 // Every call shares the one array and overwrites what the previous call left
 // there; calls that overlap on the GPU (different streams, or two host threads)
-// race on it and must be serialised by the caller.
+// race on it and must be serialised by the caller. A call is synchronous: it
+// copies the expert table from host memory, launches the layer, reads the
+// kernel's status word back and waits for its stream before it returns.
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <string.h>
@@ -28,6 +30,18 @@ void set_status_message(const char *msg);
 }
 
 namespace {
+
+// Every error return names its reason for katali_cuda_status().
+int fail(int code, const char *msg) {
+    kq::set_status_message(msg);
+    return code;
+}
+int fail_cuda(const char *what, cudaError_t e) {
+    char msg[200];
+    snprintf(msg, sizeof msg, "katali_cuda_moe_layer_static: %s: %s", what, cudaGetErrorString(e));
+    kq::set_status_message(msg);
+    return KATALI_ERR_CUDA;
+}
 
 constexpr size_t TABLE_BYTES = 3u * KATALI_MOE_STATIC_MAX_EXPERTS * sizeof(void *) + 256;
 constexpr size_t H_BYTES = (size_t)KATALI_MOE_STATIC_MAX_TOPK_FFN * sizeof(float);
@@ -61,9 +75,9 @@ int setup_device(int dev) {
         return KATALI_ERR_CUDA;
     }
     int sms = 0, smem = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-        return KATALI_ERR_CUDA;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return fail_cuda("device attribute query", e);
     g_sms[dev] = sms;
     g_smem[dev] = smem;
     g_scratch[dev] = static_cast<unsigned char *>(ptr);
@@ -75,9 +89,12 @@ int setup_device(int dev) {
 extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float *x,
                                             const float *router_logits, float *y, uint32_t mode,
                                             void *stream) {
-    if (!d || !d->experts || !x || !router_logits || !y || mode > 1) return KATALI_ERR_BAD_ARG;
-    if (((uintptr_t)x & 15u) != 0) return KATALI_ERR_BAD_ARG;
-    if (d->top_k == 0 || d->top_k > 16 || d->top_k > d->n_experts) return KATALI_ERR_BAD_ARG;
+    if (!d || !d->experts || !x || !router_logits || !y || mode > 1)
+        return fail(KATALI_ERR_BAD_ARG, "katali_cuda_moe_layer_static: NULL argument or mode > 1");
+    if (((uintptr_t)x & 15u) != 0)
+        return fail(KATALI_ERR_BAD_ARG, "katali_cuda_moe_layer_static: x is not 16-byte aligned");
+    if (d->top_k == 0 || d->top_k > (uint32_t)kq::MOE_MAX_K || d->top_k > d->n_experts)
+        return fail(KATALI_ERR_BAD_ARG, "katali_cuda_moe_layer_static: top_k out of range");
     if (d->n_experts > KATALI_MOE_STATIC_MAX_EXPERTS ||
         (uint64_t)d->top_k * d->ffn > KATALI_MOE_STATIC_MAX_TOPK_FFN) {
         char msg[200];
@@ -91,13 +108,17 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     }
     const uint64_t rbg = rbytes(d->gate_type, d->hidden), rbu = rbytes(d->up_type, d->hidden);
     const uint64_t rbd = rbytes(d->down_type, d->ffn);
-    if (!rbg || !rbu || !rbd || rbg % 16 || rbu % 16) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    if (!rbg || !rbu || !rbd || rbg % 16 || rbu % 16)
+        return fail(KATALI_ERR_UNSUPPORTED_SHAPE,
+                    "katali_cuda_moe_layer_static: gate/up must be Q4_K and down Q4_K or Q6_K, "
+                    "with hidden and ffn multiples of 256");
     for (uint32_t i = 0; i < 3 * d->n_experts; ++i)  // NULL: not resident (checked on device)
-        if ((uintptr_t)d->experts[i] & 15u) return KATALI_ERR_BAD_ARG;
+        if ((uintptr_t)d->experts[i] & 15u)
+            return fail(KATALI_ERR_BAD_ARG, "katali_cuda_moe_layer_static: expert tensor not 16-byte aligned");
 
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
-        return KATALI_ERR_NO_DEVICE;
+        return fail(KATALI_ERR_NO_DEVICE, "katali_cuda_moe_layer_static: no current CUDA device");
     int s = setup_device(dev);
     if (s) return s;
 
@@ -115,7 +136,9 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     p.rbu = (uint32_t)rbu;
     p.rbd = (uint32_t)rbd;
     const int grid = g_sms[dev];
-    if (kq::moe_plan(p, grid, g_smem[dev]) != 0) return KATALI_ERR_UNSUPPORTED_SHAPE;
+    if (kq::moe_plan(p, grid, g_smem[dev]) != 0)
+        return fail(KATALI_ERR_UNSUPPORTED_SHAPE,
+                    "katali_cuda_moe_layer_static: the layer does not fit the fused kernel's shared memory");
 
     unsigned char *base = g_scratch[dev];
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -124,7 +147,7 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     cudaError_t e = cudaMemcpyAsync(base, d->experts, 3u * d->n_experts * sizeof(void *),
                                     cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(sync, 0, 16, st);
-    if (e != cudaSuccess) return KATALI_ERR_CUDA;
+    if (e != cudaSuccess) return fail_cuda("table copy / counter reset", e);
     p.experts = reinterpret_cast<const uint8_t *const *>(base);
     p.x = x;
     p.logits = router_logits;
@@ -133,11 +156,18 @@ extern "C" int katali_cuda_moe_layer_static(const KataliMoeDesc *d, const float 
     p.sync = sync;
     p.status = sync + 2;
     e = kq::launch_moe(p, grid, st);
-    if (e != cudaSuccess) return KATALI_ERR_CUDA;
+    if (e != cudaSuccess) return fail_cuda("launch", e);
     uint32_t status = 0;  // a device-side wait that gave up leaves a bit here
     e = cudaMemcpyAsync(&status, sync + 2, sizeof status, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    if (e != cudaSuccess) return KATALI_ERR_CUDA;
-    if (status & kq::KQ_STATUS_NOT_RESIDENT) return KATALI_ERR_NOT_RESIDENT;
-    return status ? KATALI_ERR_TIMEOUT : KATALI_OK;
+    if (e != cudaSuccess) return fail_cuda("status read-back", e);
+    if (status) {
+        char msg[160];
+        const bool nr = (status & kq::KQ_STATUS_NOT_RESIDENT) != 0;
+        snprintf(msg, sizeof msg, "katali_cuda_moe_layer_static: %s (bits 0x%x)",
+                 nr ? "a selected expert is not resident" : "device-side wait timed out", status);
+        kq::set_status_message(msg);
+        return nr ? KATALI_ERR_NOT_RESIDENT : KATALI_ERR_TIMEOUT;
+    }
+    return KATALI_OK;
 }

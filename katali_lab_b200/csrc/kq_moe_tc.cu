@@ -244,11 +244,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
 }
 
 void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
-    static bool set = false;
-    if (!set) {
-        cudaFuncSetAttribute(moe_batch_gateup_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
-        set = true;
-    }
+    static size_t set_bytes[KQ_MAX_DEVICES];
+    ensure_smem_limit(moe_batch_gateup_tc, TC_SMEM, set_bytes);
     moe_batch_gateup_tc<<<max_groups * (p.F / TC_ROWS), TC_THREADS, TC_SMEM, st>>>(p);
 }
 

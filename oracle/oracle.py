@@ -32,12 +32,23 @@ _i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 
 
+def reference_root() -> str | None:
+    """The reference checkout (the katali-lab tree): $KATALI_REF_ROOT, else a directory
+    named ``reference`` beside this repository; None where neither exists (a GPU box,
+    which uses the prebuilt libraries)."""
+    cand = os.environ.get("KATALI_REF_ROOT") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
+
+
 def build(force: bool = False) -> None:
     """Build the checkers with make (the reference part only where its checkout exists)."""
-    if force or not os.path.exists(PORT_LIB) or (
-        os.path.isdir("/root/reference") and not os.path.exists(REF_LIB)
-    ):
-        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    root = reference_root()
+    if force or not os.path.exists(PORT_LIB) or (root and not os.path.exists(REF_LIB)):
+        env = dict(os.environ)
+        if root:
+            env["KATALI_REF_ROOT"] = root
+        subprocess.run(["make", "-s", "-C", HERE], check=True, env=env)
 
 
 def row_bytes(qtype: int, cols: int) -> int:

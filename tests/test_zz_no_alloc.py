@@ -3,9 +3,10 @@
 Hosts whose device memory is owned by another allocator, or that may not allocate
 once a layer runs, call this entry point instead of katali_cuda_moe_layer; it keeps
 its scratch in a fixed device array inside the library. This checks, through the C
-ABI, that two calls in a row give the same output as the allocating entry point,
-and that a layer larger than the fixed array is refused. Collected last (zz) so a
-failure here cannot stop the rest of the GPU suite.
+ABI, that calls in a row give bit-for-bit the output of the allocating entry point
+(the same kernel, deterministic), that the q8_1 output matches the C restatement of
+the layer, and that a layer larger than the fixed array is refused. Collected last
+(zz) so a failure here cannot stop the rest of the GPU suite.
 """
 import ctypes as C
 
@@ -15,7 +16,7 @@ import pytest
 from katali_lab_b200 import MOE_NORM_TOPK, MOE_Q8_1, MOE_F32, Q4_K, Q6_K, MoeLayer
 from katali_lab_b200.plugin import KataliMoeDesc
 from katali_lab_b200.synth import make_expert_store
-from oracle.oracle import rel_l2
+from oracle.oracle import MoeWeights, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -25,7 +26,7 @@ def _desc(store, top_k, flat):
                          MOE_NORM_TOPK, C.cast(flat, C.POINTER(C.c_void_p)))
 
 
-def test_static_entry_matches_allocating_entry(plugin):
+def test_static_entry_matches_allocating_entry(plugin, port):
     import torch
     E, H, F, K = 64, 2048, 512, 8
     store = make_expert_store(plugin, E, H, F, seed=61)
@@ -46,17 +47,20 @@ def test_static_entry_matches_allocating_entry(plugin):
         assert rc == 0, plugin.status()
         a, b = y.cpu().numpy(), y_ref.cpu().numpy()
         assert np.all(np.isfinite(a)), f"call {call}"
-        assert rel_l2(a, b) <= 1e-5, f"call {call}"
+        assert np.array_equal(a, b), f"call {call}: rel_L2 {rel_l2(a, b)}"
+        if call == 1:  # the second q8_1 call against the restatement (bar of test_gpu_moe)
+            host = MoeWeights(store.gate.cpu().numpy(), store.up.cpu().numpy(),
+                              store.down.cpu().numpy(), H, F, K)
+            want, _, _, _ = port.moe_layer(host, x.cpu().numpy(), logits.cpu().numpy(), mode=0)
+            assert rel_l2(a, want) <= 1e-5, f"restatement rel_L2 {rel_l2(a, want)}"
     layer.close()
 
 
 def test_static_entry_rejects_layers_beyond_its_array(plugin):
     import torch
-    store = make_expert_store(plugin, 8, 256, 4096, seed=63)  # top_k * ffn = 16 * 4096 > 16384
+    store = make_expert_store(plugin, 8, 256, 4096, seed=63)  # top_k * ffn = 8 * 4096 = 32768 > 16384
     flat = (C.c_void_p * 24)(*[a for tri in store.pointers() for a in tri])
     desc = _desc(store, 8, flat)
-    desc.top_k = 8
-    desc.ffn = 4096
     x = torch.zeros(256, device="cuda")
     lg = torch.zeros(8, device="cuda")
     y = torch.zeros(256, device="cuda")
