@@ -3,8 +3,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-A step is one pass of the hot path over one batch of synthetic input: CALLS
-fused-MoE-layer calls, call i on layer i % LAYERS of a LAYERS-deep expert store
+A step is one pass of the hot path over one batch of synthetic input: REPS replays
+of a CUDA graph of CALLS fused-MoE-layer calls (1024 layer calls by default), call i
+on layer i % LAYERS of a LAYERS-deep expert store
 (256 experts x {gate, up Q4_K 512x2048; down Q6_K 2048x512} per layer, 522 MB),
 each with its own seeded x (N(0,1), 2048) and router logits (N(0,1), 256).
 The store (16 x 522 MB = 8.4 GB) is far larger than the 126 MB L2 and each call
@@ -14,8 +15,17 @@ metric = quantised expert bytes read per second (16,318,464 B per call), whole
 job; `value` is timed on the device with inputs already in HBM (CUDA graph of
 the step's launches, CUDA events); `e2e` is the same metric through the C ABI
 with host buffers: upload of the step's inputs from pinned memory, the layer
-calls, download of the outputs, each step. N > 1 GPUs run independent replicas
-(one process per GPU, weak scaling) and report the max time over ranks.
+calls, download of the outputs, each step. N > 1 GPUs run the layer expert-parallel
+(experts split over the GPUs, one process per GPU, weak scaling: every GPU brings its
+own tokens) and report the max time over ranks; the line then carries a parity check
+of every rank's tokens against the single-GPU layer.
+
+The default run also measures the other configurations in the same process and puts
+their lines, slimmed, under "secondary": at N = 1 C2 with fp32 activations (the mode
+pinned to the reference's CPU kernels), C1 (fp32 and q8_1 activations), C3, C4 (fp32
+and q8_1) and C5 (fp32 and q8_1, with the greedy tokens compared against the CPU
+composition); at N > 1 C2 as independent replicas, C3 and C5 expert-parallel.
+`--no-secondary` skips them; `--config X` measures one configuration alone.
 """
 from __future__ import annotations
 
@@ -62,6 +72,13 @@ def parse():
     ap.add_argument("--hybrid-layers", type=int, default=40,
                     help="c5: decoder layers (every 4th is gated attention); 40 is the configuration")
     ap.add_argument("--calls", type=int, default=64)
+    ap.add_argument("--reps", type=int, default=16,
+                    help="c2: replays of the CALLS-call graph per step (a step is CALLS x REPS layer "
+                         "calls, so the timed region spans enough clock samples)")
+    ap.add_argument("--f32", action="store_true",
+                    help="c2: fp32 activations (the mode pinned to the reference's CPU kernels)")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="default run: skip the other configurations (C1, C3, C4, C5, C2 fp32)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--hot", type=int, default=0,
@@ -256,7 +273,7 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
-    from katali_lab_b200 import MOE_Q8_1, MoeLayer, Plugin
+    from katali_lab_b200 import MOE_F32, MOE_Q8_1, MoeLayer, Plugin
     from katali_lab_b200.synth import make_expert_store
 
     torch.cuda.set_device(local_rank)
@@ -277,11 +294,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     plugin.set_async(True)
+    mode = MOE_F32 if args.f32 else MOE_Q8_1
+    reps = max(args.reps, 1)
 
     def step():
         for i in range(T):
             j = 0 if args.warm else i
-            layers[j % L].forward(xs[j], lgs[j], ys[i], MOE_Q8_1)
+            layers[j % L].forward(xs[j], lgs[j], ys[i], mode)
 
     # correctness guard: first call equals a synchronous run
     step()
@@ -302,7 +321,12 @@ def run_ours(args, rank, world, local_rank):
             torch.cuda.synchronize()
             graph = None
 
-    run = graph.replay if graph is not None else step
+    one = graph.replay if graph is not None else step
+
+    def run():
+        for _ in range(reps):
+            one()
+
     for _ in range(max(args.warmup, 3)):
         run()
     plugin.sync()
@@ -327,8 +351,8 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * args.steps * T * CALL_BYTES / (ms / 1e3) / 1e9
-    us_per_call = 1e3 * ms / (args.steps * T)
+    value = world * args.steps * reps * T * CALL_BYTES / (ms / 1e3) / 1e9
+    us_per_call = 1e3 * ms / (args.steps * reps * T)
 
     if args.trace and rank == 0:
         print_trace(plugin, layers, xs, lgs, ys, T, L, args.warm)
@@ -345,7 +369,7 @@ def run_ours(args, rank, world, local_rank):
         plugin.check(L_.katali_cuda_upload(xs.data_ptr(), xh.data_ptr(), xh.numel() * 4))
         plugin.check(L_.katali_cuda_upload(lgs.data_ptr(), lh.data_ptr(), lh.numel() * 4))
         for i in range(T):
-            layers[i % L].forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+            layers[i % L].forward(xs[i], lgs[i], ys[i], mode)
         plugin.check(L_.katali_cuda_download(yh.data_ptr(), ys.data_ptr(), yh.numel() * 4))
 
     for _ in range(2):
@@ -379,6 +403,7 @@ def run_ours(args, rank, world, local_rank):
             cpu = {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"unavailable: {e}"}
 
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = CALL_BYTES / (us_per_call * 1e-6) / 1e9
@@ -386,9 +411,11 @@ def run_ours(args, rank, world, local_rank):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic",
-            "config": {"workload": WORKLOAD, "calls_per_step": T, "layers_in_store": L,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if args.f32 else "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD if not args.f32 else WORKLOAD.replace(
+                           "x N(0,1) quantised to q8_1 on device", "fp32 activations (x N(0,1))"),
+                       "calls_per_step": T * reps, "graph_calls": T, "layers_in_store": L,
                        "store_bytes_per_gpu": L * E * EXPERT_BYTES,
                        "l2": "inputs larger than L2: 16-layer store (8.4 GB) rotated per call",
                        "graph": graph is not None, "parallelism": f"replicas x{world}",
@@ -402,12 +429,14 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
                     "d2h_bytes_per_step": yh.numel() * 4},
-            "gpu_launches": args.steps * T,
+            "e2e_scope": f"{T} layer calls per e2e step through the C ABI (eager), inputs "
+                         f"uploaded and outputs downloaded every step",
+            "gpu_launches": args.steps * reps * T,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
     for l in layers:
         l.close()
+    return line
 
 
 TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first chunk in",
@@ -457,13 +486,22 @@ C1_WORKLOAD = ("C1 dense Q4_K GEMV, batch 1: W 6144x2048 from N(0,0.02) (seed 0)
 def run_c1(args, rank, world, local_rank):
     """C1: katali_cuda_matvec (the reference's drop-in entry) over 64 distinct weight copies
     (453 MB, far larger than L2), one call per copy per step."""
-    import torch
-    import torch.distributed as dist
-
     from katali_lab_b200 import Q4_K, Plugin
     from katali_lab_b200.synth import make_dense
-    if args.dp4a:
-        os.environ["KATALI_CUDA_DP4A"] = "1"
+    old = os.environ.get("KATALI_CUDA_DP4A")
+    os.environ["KATALI_CUDA_DP4A"] = "1" if args.dp4a else "0"
+    try:
+        return _run_c1(args, rank, world, local_rank, Q4_K, Plugin, make_dense)
+    finally:
+        if old is None:
+            os.environ.pop("KATALI_CUDA_DP4A", None)
+        else:
+            os.environ["KATALI_CUDA_DP4A"] = old
+
+
+def _run_c1(args, rank, world, local_rank, Q4_K, Plugin, make_dense):
+    import torch
+    import torch.distributed as dist
     torch.cuda.set_device(local_rank)
     plugin = Plugin()
     if not plugin.probe():
@@ -539,10 +577,11 @@ def run_c1(args, rank, world, local_rank):
         cpu = {"value": round(n * C1_BYTES / el / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(),
                "kind": "reference", "sample": f"{n} katali_ggml_matvec calls ({el:.1f} s) over 8 weight "
                                                f"copies, {os.cpu_count()} threads"}
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = C1_BYTES / (us_call * 1e-6) / 1e9
-        print(json.dumps({
+        line = {
             "metric": "dense Q4_K GEMV quant-weight GB/s vs HBM peak", "value": round(value, 2),
             "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "weak",
@@ -556,7 +595,8 @@ def run_c1(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": C1_COLS * 4,
                     "d2h_bytes_per_step": C1_ROWS * 4},
-            "gpu_launches": args.steps * T, "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": args.steps * T, "cpu_baseline": cpu}
+    return line
 
 
 C3_WORKLOAD = ("C3 ragged continuous batch of the C2 layer: per call T ~ U{1..64} tokens "
@@ -670,11 +710,12 @@ def run_c3(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         cpu = c3_cpu_rate(stores[:2], Ts, offs, Xh, LGh, distinct, args.cpu_seconds)
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         us_call = 1e3 * ms / (args.steps * n)
         achieved = step_bytes / n / (us_call * 1e-6) / 1e9
-        print(json.dumps({
+        line = {
             "metric": "MoE-layer distinct-expert quant-weight GB/s vs HBM peak",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -696,9 +737,10 @@ def run_c3(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
                     "d2h_bytes_per_step": yh.numel() * 4},
-            "gpu_launches": args.steps * n * 6, "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": args.steps * n * 6, "cpu_baseline": cpu}
     for l in layers:
         l.close()
+    return line
 
 
 def c3_cpu_rate(stores_or_layers, Ts, offs, Xh, LGh, distinct, seconds):
@@ -731,6 +773,47 @@ def c3_cpu_rate(stores_or_layers, Ts, offs, Xh, LGh, distinct, seconds):
 
 EP_WORKLOAD = ("{cfg} expert-parallel over {n} GPUs: 256 experts split in blocks of {per} per GPU, "
                "every GPU brings its own tokens ({tok}); dispatch/combine {how}")
+
+
+def ep_parity(plugin, store, world, xs, lgs, ys, offs):
+    """Each rank's call-0 tokens (layer 0) of the expert-parallel run against the single-GPU
+    fused layer over all experts of layer 0, gathered from every rank's slice (NCCL
+    all-gather), at the bar of the expert-parallel GPU tests (rel_L2 <= 1e-5). The single-GPU
+    kernel is pinned to the C restatement by the GPU test suite; this check runs no oracle
+    code. Returns the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from katali_lab_b200 import MOE_Q8_1, MoeLayer
+    full = []
+    for t in (store.gate, store.up, store.down):
+        out = torch.empty((world * t.shape[0], t.shape[1]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous())
+        full.append(out)
+    torch.cuda.synchronize()
+    g, u, d = full
+    ptrs = [(g.data_ptr() + e * g.shape[1], u.data_ptr() + e * u.shape[1],
+             d.data_ptr() + e * d.shape[1]) for e in range(g.shape[0])]
+    layer = MoeLayer(plugin, g.shape[0], H, F, K, ptrs)
+    y1 = torch.empty(H, device="cuda")
+    worst, equal, n = 0.0, 0, 0
+    for t in range(int(offs[0]), int(offs[1])):
+        layer.forward(xs[t], lgs[t], y1, MOE_Q8_1)
+        torch.cuda.synchronize()
+        den = float(y1.norm())
+        worst = max(worst, float((ys[t] - y1).norm()) / (den if den > 0 else 1.0))
+        equal += int((ys[t] == y1).sum())
+        n += H
+    layer.close()
+    v = torch.tensor([worst, float(equal), float(n)], device="cuda", dtype=torch.float64)
+    w = v.clone()
+    dist.all_reduce(w[:1], op=dist.ReduceOp.MAX)
+    dist.all_reduce(w[1:], op=dist.ReduceOp.SUM)
+    del full
+    return {"ok": bool(w[0].item() <= 1e-5), "max_rel_l2": float(w[0].item()),
+            "bit_equal_frac": round(float(w[1].item() / max(w[2].item(), 1.0)), 6),
+            "against": "single-GPU fused layer over all experts (gathered), every rank's call-0 tokens",
+            "bar": "rel_L2 <= 1e-5"}
 
 
 def run_ep(args, rank, world, local_rank):
@@ -783,6 +866,7 @@ def run_ep(args, rank, world, local_rank):
 
     step()  # sizes every exchange buffer and scratch before capture
     torch.cuda.synchronize()
+    parity = None if ragged else ep_parity(plugin, stores[0], world, xs, lgs, ys, offs)
     plugin.set_async(True)
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gr, stream=stream):
@@ -830,10 +914,11 @@ def run_ep(args, rank, world, local_rank):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_value = args.steps * step_bytes / (float(t.item()) / 1e3) / 1e9
     plugin.sync()
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         us_call = 1e3 * ms / (args.steps * n)
-        print(json.dumps({
+        line = {
             "metric": METRIC if not ragged else "MoE-layer distinct-expert quant-weight GB/s vs HBM peak",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -861,11 +946,14 @@ def run_ep(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
                     "d2h_bytes_per_step": yh.numel() * 4},
-            "gpu_launches": args.steps * n * 8, "cpu_baseline": None}), flush=True)
+            "parity": parity,
+            "gpu_launches": args.steps * n * (1 if not ragged and not args.nccl else 8),
+            "cpu_baseline": None}
     del gr
     comm.close()
     for l in layers:
         l.close()
+    return line
 
 
 C4_WORKLOAD = ("C4 dense Qwen3-8B-shape greedy decode on one GPU: 36 layers, hidden 4096, FFN 12288, "
@@ -931,10 +1019,11 @@ def run_c4(args, rank, world, local_rank):
                "kind": "reference", "tokens_per_s": round(k / el, 3),
                "sample": f"{k} greedy decode steps ({el:.1f} s) of the same model through the "
                          f"reference's CPU kernels (gguf_forward_token composition), {cores} threads"}
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = value / world
-        print(json.dumps({
+        line = {
             "metric": "dense decode quant-weight GB/s vs HBM peak", "value": round(value, 2),
             "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
@@ -953,8 +1042,9 @@ def run_c4(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": args.steps * n * (1 + 6 * cfg.n_layers + 3), "cpu_baseline": cpu}), flush=True)
+            "gpu_launches": args.steps * n * (1 + 6 * cfg.n_layers + 3), "cpu_baseline": cpu}
     dm.close()
+    return line
 
 
 C5_WORKLOAD = ("C5 35B-A3B-class hybrid greedy decode on one GPU: 40 layers (30 Gated DeltaNet: 16 q/k "
@@ -1018,10 +1108,11 @@ def run_c5(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and args.cpu_seconds > 0:
         cpu = c5_cpu_leg(model, toks, bpt, args.cpu_seconds, fp32=not q8)
+    line = None
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = tok_s / world * bpt / 1e9
-        print(json.dumps({
+        line = {
             "metric": "hybrid MoE decode tok/s", "value": round(tok_s, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": steps, "warmup": args.warmup,
             "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
@@ -1042,11 +1133,13 @@ def run_c5(args, rank, world, local_rank):
             "clocks": clk.summary(),
             "e2e": {"value": round(tok_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * len(prompt),
                     "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": steps * n * (1 + (5 if ep else 4) * cfg.n_layers + 3), "cpu_baseline": cpu}),
-          flush=True)
+            "greedy_match": cpu.get("greedy_tokens_match_gpu") if cpu else None,
+            "tokens": n,
+            "gpu_launches": steps * n * (1 + (5 if ep else 4) * cfg.n_layers + 3), "cpu_baseline": cpu}
     hm.close()
     if comm is not None:
         comm.close()
+    return line
 
 
 def c5_cpu_leg(model, gpu_tokens, bpt, seconds, fp32=True):
@@ -1075,8 +1168,74 @@ def c5_cpu_leg(model, gpu_tokens, bpt, seconds, fp32=True):
     match = [int(a) for a in gpu_tokens[:len(toks)]] == toks if fp32 else None
     return {"value": round(k / el, 3), "unit": "tokens/s", "cores": cores, "kind": "reference",
             "gbs": round(k * bpt / el / 1e9, 3), "greedy_tokens_match_gpu": match,
+            "tokens_compared": len(toks) if fp32 else 0,
             "sample": f"{k} greedy decode steps ({el:.1f} s) of the same model through the "
                       f"reference's CPU kernels + the Gated DeltaNet restatement, {cores} threads"}
+
+
+# Keys of a secondary configuration's line kept in the headline's `secondary` object.
+SECONDARY_KEYS = ("metric", "value", "unit", "steps", "warmup", "ms_per_step", "dtype", "config",
+                  "roofline", "clocks", "e2e", "gpu_launches", "cpu_baseline", "parity",
+                  "greedy_match", "tokens")
+
+
+def run_secondary(args, rank, world, local_rank, headline):
+    """The other configurations of the workload, measured in the same process after the
+    headline, each under the same rules (>= 3 warm-up steps, CUDA events on the launching
+    stream, inputs larger than L2, clocks sampled, e2e through the C ABI, CPU baseline on
+    the reference's kernels at N = 1 with a shorter sample). Returns {name: line}."""
+    import gc
+
+    import torch
+
+    def sub(**kw):
+        a = argparse.Namespace(**vars(args))
+        a.__dict__.update(kw)
+        return a
+
+    cs = min(args.cpu_seconds, 5.0)
+    w = max(args.warmup, 3)
+    if world == 1:
+        plans = [
+            ("c2_f32", run_ours, sub(f32=True, cpu_seconds=0, reps=4)),
+            ("c1_f32", run_c1, sub(config="c1", dp4a=False, calls=64, steps=max(args.steps, 200),
+                                   cpu_seconds=cs)),
+            ("c1_q8_1", run_c1, sub(config="c1", dp4a=True, calls=64, steps=max(args.steps, 200),
+                                    cpu_seconds=0)),
+            ("c3", run_c3, sub(config="c3", calls=64, cpu_seconds=cs)),
+            ("c4_f32", run_c4, sub(config="c4", dp4a=False, calls=64, steps=min(args.steps, 3),
+                                   warmup=3, cpu_seconds=2 * cs)),
+            ("c4_q8_1", run_c4, sub(config="c4", dp4a=True, calls=64, steps=min(args.steps, 3),
+                                    warmup=3, cpu_seconds=0)),
+            ("c5_f32", run_c5, sub(config="c5", dp4a=False, steps=min(args.steps, 10), warmup=w,
+                                   cpu_seconds=max(cs, 1.0))),
+            ("c5_q8_1", run_c5, sub(config="c5", dp4a=True, steps=min(args.steps, 10), warmup=w,
+                                    cpu_seconds=0)),
+        ]
+    else:
+        plans = [
+            ("c2_replicas", run_ours, sub(replicas=True, cpu_seconds=0)),
+            ("c3_ep", run_ep, sub(config="c3", calls=64)),
+            ("c5_ep", run_c5, sub(config="c5", steps=min(args.steps, 10), warmup=w, cpu_seconds=0)),
+        ]
+    out = {}
+    for name, fn, a in plans:
+        t0 = time.time()
+        try:
+            line = fn(a, rank, world, local_rank)
+        except Exception as e:  # reported, not fatal: the headline stands
+            line = {"error": f"{type(e).__name__}: {e}"[:300]}
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if rank == 0 and line is not None:
+            kept = {k: line[k] for k in SECONDARY_KEYS if k in line} if "error" not in line else line
+            kept["wall_s"] = round(time.time() - t0, 1)
+            out[name] = kept
+    if rank == 0 and world == 1 and "c2_f32" in out and headline and "cpu_baseline" in out["c2_f32"]:
+        # the reference CPU layer runs fp32 activations: the headline's CPU leg is this twin's too
+        out["c2_f32"]["cpu_baseline"] = headline.get("cpu_baseline")
+    return out
 
 
 def main():
@@ -1099,17 +1258,24 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         if args.config == "c1":
-            run_c1(args, rank, world, local_rank)
+            line = run_c1(args, rank, world, local_rank)
         elif args.config == "c4":
-            run_c4(args, rank, world, local_rank)
+            line = run_c4(args, rank, world, local_rank)
         elif args.config == "c5":
-            run_c5(args, rank, world, local_rank)
+            line = run_c5(args, rank, world, local_rank)
         elif world > 1 and not args.replicas:
-            run_ep(args, rank, world, local_rank)
+            line = run_ep(args, rank, world, local_rank)
         elif args.config == "c3":
-            run_c3(args, rank, world, local_rank)
+            line = run_c3(args, rank, world, local_rank)
         else:
-            run_ours(args, rank, world, local_rank)
+            line = run_ours(args, rank, world, local_rank)
+        if args.config == "c2" and not args.no_secondary and not args.f32 and not args.warm \
+                and not args.trace:
+            sec = run_secondary(args, rank, world, local_rank, line)
+            if rank == 0 and line is not None:
+                line["secondary"] = sec
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -22,15 +22,17 @@ def _bound(fn):
     if fn.args.kwarg:
         names.add(fn.args.kwarg.arg)
     for n in ast.walk(fn):
-        if isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef, ast.ClassDef)) and n is not fn:
+        if isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef)) and n is not fn:
+            names.add(n.name)  # a nested function: its name and its parameters
+            names.update(a.arg for a in n.args.args + n.args.kwonlyargs)
+            names.update(a.arg for a in (n.args.vararg, n.args.kwarg) if a)
+        elif isinstance(n, ast.ClassDef):
             names.add(n.name)
         elif isinstance(n, (ast.Import, ast.ImportFrom)):
             names.update((a.asname or a.name).split(".")[0] for a in n.names)
         elif isinstance(n, ast.ExceptHandler) and n.name:
             names.add(n.name)
         elif isinstance(n, ast.Lambda):
-            names.update(a.arg for a in n.args.args)
-        elif isinstance(n, (ast.FunctionDef, ast.AsyncFunctionDef)):
             names.update(a.arg for a in n.args.args)
     names.update(_targets(fn))
     return names

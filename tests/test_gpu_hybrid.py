@@ -6,7 +6,8 @@ Bars (fp32 activations): every step's logits within rel_L2 <= 1e-5; greedy token
 byte-identical, each side feeding back its own argmax. One multi-token call (graph replays)
 equals token-by-token calls; reset clears the recurrent, conv and KV state. The 35B-A3B-class
 dimensions (256 experts, vocab 248320, GDN 16/32 heads of 128, attention 16/2 heads of 256)
-run a short greedy decode with 4 of the 40 layers."""
+run a short greedy decode with 4 of the 40 layers, and configuration 5 at length: all 40
+layers, 32 greedy tokens, logits checked at every step."""
 import dataclasses
 
 import numpy as np
@@ -103,6 +104,17 @@ def test_35b_class_dims_greedy(plugin, ref, port):
     model = make_hybrid_model(plugin, cfg, seed=35)
     assert [w["kind"] for w in model.layers] == [0, 0, 0, 1]
     g, c = greedy_both(plugin, ref, port, model, [100, 2000], 3)
+    assert g == c
+
+
+def test_35b_class_full_40_layers_32_tokens(plugin, ref, port):
+    """Configuration 5 at length: the 40-layer model (30 Gated DeltaNet + 10 gated attention,
+    MoE every layer), 32 greedy tokens after a 1-token prompt, logits within rel_L2 <= 1e-5
+    of the CPU composition at every step and the tokens byte-identical."""
+    model = make_hybrid_model(plugin, HYBRID_35B, seed=35)
+    assert len(model.layers) == 40 and sum(w["kind"] for w in model.layers) == 10
+    g, c = greedy_both(plugin, ref, port, model, [1], 32)
+    assert len(g) == 32
     assert g == c
 
 
