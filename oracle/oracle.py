@@ -478,6 +478,7 @@ class RefHybrid:
         L.kref_hybrid_step.restype = C.c_int
         L.kref_hybrid_free.argtypes = [C.c_void_p]
         L.kref_hybrid_reset.argtypes = [C.c_void_p]
+        L.kref_hybrid_route_gaps.argtypes = [C.c_void_p, C.c_void_p]
         self.h = L.kref_hybrid_new(dims, cfg.rms_eps, cfg.rope_theta, emb.ctypes.data, T["embed"],
                                    lm.ctypes.data, T["lm_head"], on.ctypes.data, T["gate"], T["up"],
                                    T["down"], C.cast(ly, C.c_void_p), n_threads or os.cpu_count() or 1)
@@ -492,6 +493,14 @@ class RefHybrid:
         if self.ref.L.kref_hybrid_step(self.h, int(token), int(pos), self.logits.ctypes.data) != 0:
             raise ValueError("kref_hybrid_step failed")
         return self.logits
+
+    def route_gaps(self) -> np.ndarray:
+        """Per layer, for the last step: the relative margin between the top_k-th and the
+        (top_k + 1)-th router logit (where a ~1e-7 difference in the logits can change
+        which experts are selected)."""
+        out = np.empty(self.cfg.n_layers, np.float32)
+        self.ref.L.kref_hybrid_route_gaps(C.c_void_p(self.h), out.ctypes.data)
+        return out
 
     def close(self):
         if self.h:

@@ -306,6 +306,7 @@ typedef struct KrefHybrid {
     KrefHybridLayer *L;
     float *x, *xb, *tmp, *qkv, *cv, *z, *b, *a, *go, *qg, *q, *gt, *k, *v, *attn, *rl, *logits;
     float *kv_k, *kv_v, *ring, *state, *scores, *rope_inv, *rope_cos, *rope_sin;
+    float *route_gap; /* per layer, last step: (top_k-th - (top_k+1)-th router logit) / |top_k-th| */
     void *moe_scratch;
 } KrefHybrid;
 
@@ -316,7 +317,7 @@ void kref_hybrid_free(void *p) {
     free(m->b); free(m->a); free(m->go); free(m->qg); free(m->q); free(m->gt); free(m->k);
     free(m->v); free(m->attn); free(m->rl); free(m->logits); free(m->kv_k); free(m->kv_v);
     free(m->ring); free(m->state); free(m->scores); free(m->rope_inv); free(m->rope_cos);
-    free(m->rope_sin);
+    free(m->rope_sin); free(m->route_gap);
     kref_moe_scratch_free(m->moe_scratch);
     free(m);
 }
@@ -361,7 +362,8 @@ void *kref_hybrid_new(const int32_t *dims /* NL H vocab cap NH NKV HD rope_dim n
     for (int i = 0; i < m->rd / 2; i++)
         m->rope_inv[i] = 1.0f / powf(theta, (2.0f * (float)i) / (float)m->rd);
     m->moe_scratch = kref_moe_scratch_new(m->E, m->H, m->F, m->top_k);
-    if (!m->x || !m->state || !m->ring || !m->kv_k || !m->kv_v || !m->moe_scratch) {
+    m->route_gap = calloc((size_t)m->NL + 1, 4);
+    if (!m->x || !m->route_gap || !m->state || !m->ring || !m->kv_k || !m->kv_v || !m->moe_scratch) {
         kref_hybrid_free(m);
         return NULL;
     }
@@ -437,6 +439,30 @@ static void kref_gdn_step(const KrefHybrid *m, const KrefHybridLayer *L, int pos
     }
 }
 
+/* Margin of a routing decision: (k-th largest - (k+1)-th largest logit) / |k-th largest|.
+ * Two implementations whose router logits differ by a relative ~1e-7 can select different
+ * experts only where this margin is of that order. */
+static float kref_route_gap(const float *lg, int n, int k) {
+    if (k <= 0 || k >= n || k > 16) return 1.0f;
+    float top[17];  /* the k + 1 largest logits so far, descending */
+    int cnt = 0;
+    for (int i = 0; i < n; i++) {
+        const float v = lg[i];
+        if (cnt == k + 1 && !(v > top[k])) continue;
+        int j = cnt < k + 1 ? cnt++ : k;
+        while (j > 0 && top[j - 1] < v) { top[j] = top[j - 1]; j--; }
+        top[j] = v;
+    }
+    const float a = fabsf(top[k - 1]);
+    return (top[k - 1] - top[k]) / (a > 0.0f ? a : 1.0f);
+}
+
+/* The routing margins of every layer at the last step (NL floats). */
+void kref_hybrid_route_gaps(const void *p, float *out) {
+    const KrefHybrid *m = (const KrefHybrid *)p;
+    memcpy(out, m->route_gap, (size_t)m->NL * 4);
+}
+
 /* One step at position pos with input token; logits_out may be NULL. */
 int kref_hybrid_step(void *p, int token, int pos, float *logits_out) {
     KrefHybrid *m = (KrefHybrid *)p;
@@ -498,6 +524,7 @@ int kref_hybrid_step(void *p, int token, int pos, float *logits_out) {
         katali_gguf_add_inplace(m->x, m->tmp, (size_t)H);
         katali_gguf_rmsnorm(m->x, L->ffn_norm, (size_t)H, m->eps, m->xb);
         kref_matvec(KGGML_F32, L->router, (uint64_t)m->E, (uint64_t)H, m->xb, m->rl, nt);
+        m->route_gap[l] = kref_route_gap(m->rl, m->E, m->top_k);
         if (kref_moe_layer(m->E, H, m->F, m->top_k, m->norm_topk, m->gate_t, m->up_t, m->down_t,
                            L->gate, L->up, L->down, m->xb, m->rl, m->tmp, nt, m->moe_scratch,
                            NULL, NULL) != 0)

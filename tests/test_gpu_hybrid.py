@@ -109,13 +109,40 @@ def test_35b_class_dims_greedy(plugin, ref, port):
 
 def test_35b_class_full_40_layers_32_tokens(plugin, ref, port):
     """Configuration 5 at length: the 40-layer model (30 Gated DeltaNet + 10 gated attention,
-    MoE every layer), 32 greedy tokens after a 1-token prompt, logits within rel_L2 <= 1e-5
-    of the CPU composition at every step and the tokens byte-identical."""
+    MoE every layer), 32 greedy tokens after a 1-token prompt, the tokens byte-identical to
+    the CPU composition at every step.
+
+    Logits: rel_L2 <= 1e-5 for the first step (one pass through all 40 layers). The Gated
+    DeltaNet states and the KV cache carry each step's rounding differences forward (the
+    reference's AVX2 GEMV rounds fp32 partial sums inside each block, the device forms exact
+    block terms: ~1e-7 relative per output), so the following steps are held to 1e-4. The
+    router logits of the two sides therefore differ by ~1e-7 too, and a layer whose 8th and
+    9th router logits are closer than that selects a different 8th expert on each side; from
+    such a step on, the hidden states differ by a few percent (seed 35: layer 17 at step 6,
+    margin 3.5e-6) and only the tokens are compared. A step beyond 1e-4 must be one where
+    the CPU side saw such a near-tie (margin < 1e-5): nothing else may explain it."""
     model = make_hybrid_model(plugin, HYBRID_35B, seed=35)
     assert len(model.layers) == 40 and sum(w["kind"] for w in model.layers) == 10
-    g, c = greedy_both(plugin, ref, port, model, [1], 32)
-    assert len(g) == 32
-    assert g == c
+    hm = HybridModel(plugin, model)
+    rh = RefHybrid(ref, model)
+    tok_g = tok_c = 1
+    flipped = False
+    for s in range(32):
+        g = int(hm.generate([tok_g], 1)[0])
+        lc = rh.step(tok_c, s)
+        c = port.argmax(lc)
+        lg = logits_of(hm, HYBRID_35B.vocab)
+        err = rel_l2(lg, lc)
+        margin = float(rh.route_gaps().min())
+        assert g == c, (s, g, c)
+        if s == 0:
+            assert err <= 1e-5, err
+        elif not flipped and err > 1e-4:
+            assert margin < 1e-5, (s, err, margin)
+            flipped = True
+        tok_g, tok_c = g, c
+    rh.close()
+    hm.close()
 
 
 @pytest.mark.parametrize("change,code", [
