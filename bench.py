@@ -461,6 +461,8 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
         plugin.sync()
         lay.set_trace(None)
         t = buf[:grid * 20].view(grid, 20).cpu().numpy().astype(np.int64)
+        t = t[t[:, 0] > 0]  # the CTAs that ran (a launch may use fewer than the grid size)
+        buf.zero_()
         mhz.append(np.median((t[:, 17] - t[:, 16]) / np.maximum(t[:, 8] - t[:, 0], 1) * 1e3))
         t0 = t[:, 0].min()
         row = [t[:, 0].max() - t0]
