@@ -14,7 +14,9 @@
  * Search order: $KATALI_CUDA_DLL, then libkatali_cuda.so beside this loader,
  * then the dynamic linker's default path.
  */
+#ifndef _GNU_SOURCE
 #define _GNU_SOURCE
+#endif
 #include <dlfcn.h>
 #include <stdio.h>
 #include <stdlib.h>

@@ -23,6 +23,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_LIB = os.path.join(HERE, "_port", "libkq_oracle.so")
 REF_LIB = os.path.join(HERE, "_ref", "libkatali_ref.so")
+DROPIN = os.path.join(HERE, "_ref", "katali_dropin")  # the reference's dense backend + our loader
 
 Q8_1, Q4_K, Q6_K = 9, 12, 14
 BLOCK = {Q8_1: (32, 36), Q4_K: (256, 144), Q6_K: (256, 210)}
@@ -44,7 +45,8 @@ def reference_root() -> str | None:
 def build(force: bool = False) -> None:
     """Build the checkers with make (the reference part only where its checkout exists)."""
     root = reference_root()
-    if force or not os.path.exists(PORT_LIB) or (root and not os.path.exists(REF_LIB)):
+    if force or not os.path.exists(PORT_LIB) or (
+            root and not (os.path.exists(REF_LIB) and os.path.exists(DROPIN))):
         env = dict(os.environ)
         if root:
             env["KATALI_REF_ROOT"] = root

@@ -86,9 +86,25 @@ def malformed():
     return out
 
 
-def dense_model_file(port, cfg, seed=0, std=0.02):
+def gpt2_byte_tokens():
+    """The 256 single-byte tokens of a GPT-2 style byte-level vocabulary (the public
+    byte -> unicode convention: printable bytes map to themselves, the others to 256 + n)."""
+    direct = set(range(33, 127)) | set(range(161, 173)) | set(range(174, 256))
+    out, n = [], 0
+    for b in range(256):
+        if b in direct:
+            out.append(chr(b))
+        else:
+            out.append(chr(256 + n))
+            n += 1
+    return out
+
+
+def dense_model_file(port, cfg, seed=0, std=0.02, byte_vocab=False):
     """A Qwen3-layout dense model (llama.cpp tensor names) with weights ~ N(0, std) encoded
-    by the oracle's encoder: Q4_K, with Q6_K attn_v / ffn_down / output; fp32 norms."""
+    by the oracle's encoder: Q4_K, with Q6_K attn_v / ffn_down / output; fp32 norms.
+    byte_vocab: the first 256 tokens are the GPT-2 byte tokens, so a byte-level tokenizer
+    (the reference's) encodes any prompt without merges."""
     from oracle.oracle import Q4_K, Q6_K
     rng = np.random.default_rng(seed)
     H, F, NH, NKV, HD = cfg.hidden, cfg.ffn, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
@@ -115,5 +131,8 @@ def dense_model_file(port, cfg, seed=0, std=0.02):
            ("qwen3.attention.key_length", U32, HD), ("qwen3.context_length", U32, cfg.kv_cap),
            ("qwen3.rope.freq_base", F32, cfg.rope_theta),
            ("qwen3.attention.layer_norm_rms_epsilon", F32, cfg.rms_eps),
-           ("tokenizer.ggml.tokens", ARR, (STR, [f"t{i}" for i in range(cfg.vocab)]))]
+           ("tokenizer.ggml.tokens", ARR, (STR, (gpt2_byte_tokens() if byte_vocab else []) +
+                                             [f"t{i}" for i in range(256 if byte_vocab else 0, cfg.vocab)]))]
+    if byte_vocab:
+        kvs.append(("tokenizer.ggml.model", STR, "gpt2"))
     return build(kvs, [(n, t, d, b) for n, t, d, b in ts])
