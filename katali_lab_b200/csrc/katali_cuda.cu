@@ -85,6 +85,7 @@ int cuda_fail(cudaError_t e) {
 }
 
 int take_device_status() {
+    if (!g_status_host) return KATALI_OK;  // no call has launched work yet
     const uint32_t s = *(volatile uint32_t *)g_status_host;
     if (s) {
         *(volatile uint32_t *)g_status_host = 0;
@@ -135,6 +136,9 @@ int max_cols_for_smem(int mode) {
 }  // namespace
 
 namespace kq {
+// The plugin's runtime state (device probe, own stream, mapped status word), created on the
+// first call that needs it; the entry points of the other translation units call this first.
+int ensure_runtime() { return ensure(); }
 // Lets other translation units of the plugin report a reason via katali_cuda_status().
 void set_status_message(const char *msg) { snprintf(g_status, sizeof g_status, "%s", msg); }
 cudaStream_t current_stream() { return g_stream; }

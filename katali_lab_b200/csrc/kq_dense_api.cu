@@ -12,6 +12,7 @@
 #include "kq_launch.h"
 
 namespace kq {
+int ensure_runtime();
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
 volatile uint32_t *device_status_word();
@@ -88,7 +89,8 @@ extern "C" {
 int katali_cuda_dense_create(const KataliDenseDesc *d, KataliDense **out) {
     if (!d || !out || !d->layers) return KATALI_ERR_BAD_ARG;
     *out = nullptr;
-    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    // device, own stream and mapped status word (KATALI_ERR_NO_DEVICE without a usable GPU)
+    if (const int rs = kq::ensure_runtime()) return rs;
     const uint32_t H = d->hidden, F = d->ffn, NH = d->n_heads, NKV = d->n_kv_heads, HD = d->head_dim;
     if (!d->n_layers || !H || !F || !NH || !NKV || !HD || !d->vocab || !d->kv_cap)
         return bad("katali_cuda_dense_create: zero dimension");

@@ -22,6 +22,7 @@
 #include "kq_launch.h"
 
 namespace kq {
+int ensure_runtime();
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
 int moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_t n_tokens,
@@ -274,7 +275,8 @@ int katali_cuda_ep_unique_id(void *id) {
 int katali_cuda_ep_create(uint32_t n_ranks, uint32_t rank, const void *id, KataliEp **out) {
     if (!out || !id || n_ranks == 0 || n_ranks > 64 || rank >= n_ranks) return KATALI_ERR_BAD_ARG;
     *out = nullptr;
-    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    // device, own stream and mapped status word (KATALI_ERR_NO_DEVICE without a usable GPU)
+    if (const int rs = kq::ensure_runtime()) return rs;
     int s = load_nccl();
     if (s) return s;
     ncclUniqueId u;

@@ -26,6 +26,7 @@
 #include "katali_cuda.h"
 
 namespace kq {
+int ensure_runtime();
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
 int moe_set_expert_async(KataliMoe *m, uint32_t e, const void *g, const void *u, const void *d);
@@ -145,7 +146,8 @@ extern "C" {
 int katali_cuda_expert_cache_create(uint64_t slot_bytes, uint32_t n_slots, KataliExpertCache **out) {
     if (!out || slot_bytes == 0 || n_slots == 0) return KATALI_ERR_BAD_ARG;
     *out = nullptr;
-    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    // device, own stream and mapped status word (KATALI_ERR_NO_DEVICE without a usable GPU)
+    if (const int rs = kq::ensure_runtime()) return rs;
     KataliExpertCache *c = new KataliExpertCache();
     c->slot_bytes = align16(slot_bytes);
     c->slots.resize(n_slots);

@@ -28,6 +28,7 @@
 #include "katali_cuda.h"
 
 namespace kq {
+int ensure_runtime();
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
 void dense_adopt_weights(KataliDense *m, void *mem);
@@ -372,7 +373,8 @@ int katali_cuda_gguf_upload(KataliGguf *g, uint64_t i, void *dev) {
         kq::set_status_message("katali_cuda_gguf_upload: tensor type not sized by this reader");
         return KATALI_ERR_UNSUPPORTED_TYPE;
     }
-    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    // device, own stream and mapped status word (KATALI_ERR_NO_DEVICE without a usable GPU)
+    if (const int rs = kq::ensure_runtime()) return rs;
     cudaError_t e = cudaSuccess;
     for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
         if (!g->stage[b]) e = cudaHostAlloc(&g->stage[b], STAGE, cudaHostAllocDefault);
@@ -503,7 +505,8 @@ int katali_cuda_dense_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t 
         for (int j = 0; j < 7; ++j)
             if ((s = take(pfx + mats[j] + ".weight", true, cols[j], rows[j], &L.w[j], &L.t[j]))) return s;
     }
-    if (katali_cuda_probe() != 1) return KATALI_ERR_NO_DEVICE;
+    // device, own stream and mapped status word (KATALI_ERR_NO_DEVICE without a usable GPU)
+    if (const int rs = kq::ensure_runtime()) return rs;
     unsigned char *mem = nullptr;
     cudaError_t e = cudaMalloc((void **)&mem, total);
     if (e != cudaSuccess) {
