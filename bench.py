@@ -1253,6 +1253,7 @@ def main():
 
         # stdout carries exactly one JSON line: NCCL's banner lines stay off unless asked for
         os.environ.setdefault("NCCL_DEBUG", "WARN")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # NCCL's version banner off stdout
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
