@@ -814,6 +814,11 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
     p.ep_peer_flags = pp->flags;
     p.ep_epoch = pp->epoch;
     p.ep_done = pp->done;
+    p.ep_peer_trecv = pp->trecv;
+    p.ep_peer_tback = pp->tback;
+    p.ep_peer_tdone = pp->tdone;
+    p.ep_tslot_words = pp->tslot_words;
+    if (!pp->trecv) return KATALI_ERR_UNSUPPORTED_SHAPE;  // window without the tagged regions
     *out = p;
     *grid = m->grid;
     return KATALI_OK;

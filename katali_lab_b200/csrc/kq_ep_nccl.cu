@@ -165,8 +165,15 @@ int peer_setup(KataliEp *ep, uint64_t slot, uint32_t H, uint32_t tmax, cudaStrea
     auto r256 = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t recv = r256(2 * G * tmax * slot), back = r256(2 * G * tmax * (size_t)H * 8),
                  flags = r256(4 * G * sizeof(uint32_t));
-    cudaError_t e = cudaMalloc((void **)&ep->win, recv + back + flags);
-    if (e == cudaSuccess) e = cudaMemsetAsync(ep->win, 0, recv + back + flags, st);
+    // tagged regions for the single-launch layer, when the exchange is small enough for it
+    const bool tagged = G * tmax <= (size_t)kq::MOE_EP_MAX_SLOTS;
+    const uint32_t tsw = kq::ep_tslot_words(H);
+    const size_t trecv = tagged ? r256(2 * G * tmax * tsw * 8) : 0,
+                 tback = tagged ? r256(2 * G * tmax * (size_t)H * 16) : 0,
+                 tdone = tagged ? r256(2 * G * 8) : 0;
+    const size_t total = recv + back + flags + trecv + tback + tdone;
+    cudaError_t e = cudaMalloc((void **)&ep->win, total);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ep->win, 0, total, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_err(e, "peer window");
     cudaIpcMemHandle_t mine;
@@ -199,22 +206,29 @@ int peer_setup(KataliEp *ep, uint64_t slot, uint32_t H, uint32_t tmax, cudaStrea
         ep->opened.push_back(p);
         base[d] = (unsigned char *)p;
     }
-    std::vector<void *> arrays(3 * G);
+    std::vector<void *> arrays(6 * G);
     for (size_t d = 0; d < G; ++d) {
-        arrays[d] = base[d];
-        arrays[G + d] = base[d] + recv;
-        arrays[2 * G + d] = base[d] + recv + back;
+        unsigned char *b = base[d];
+        arrays[d] = b;
+        arrays[G + d] = b + recv;
+        arrays[2 * G + d] = b + recv + back;
+        arrays[3 * G + d] = tagged ? b + recv + back + flags : nullptr;
+        arrays[4 * G + d] = tagged ? b + recv + back + flags + trecv : nullptr;
+        arrays[5 * G + d] = tagged ? b + recv + back + flags + trecv + tback : nullptr;
     }
-    e = cudaMalloc(&ep->dev_arrays, 3 * G * sizeof(void *) + 64);
+    e = cudaMalloc(&ep->dev_arrays, 6 * G * sizeof(void *) + 64);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(ep->dev_arrays, arrays.data(), 3 * G * sizeof(void *), cudaMemcpyHostToDevice, st);
-    uint32_t *words = (uint32_t *)((unsigned char *)ep->dev_arrays + 3 * G * sizeof(void *));
+        e = cudaMemcpyAsync(ep->dev_arrays, arrays.data(), 6 * G * sizeof(void *), cudaMemcpyHostToDevice, st);
+    uint32_t *words = (uint32_t *)((unsigned char *)ep->dev_arrays + 6 * G * sizeof(void *));
     if (e == cudaSuccess) e = cudaMemsetAsync(words, 0, 64, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_err(e, "peer arrays");
     void **arr = (void **)ep->dev_arrays;
     ep->peer = kq::EpPeer{ep->rank, (uint8_t *const *)arr, (double *const *)(arr + G),
-                          (uint32_t *const *)(arr + 2 * G), words, words + 1};
+                          (uint32_t *const *)(arr + 2 * G), words, words + 1,
+                          tagged ? (uint64_t *const *)(arr + 3 * G) : nullptr,
+                          tagged ? (uint64_t *const *)(arr + 4 * G) : nullptr,
+                          tagged ? (uint64_t *const *)(arr + 5 * G) : nullptr, tsw};
     ep->win_slot = slot;
     ep->win_h = H;
     ep->win_tmax = tmax;

@@ -162,6 +162,11 @@ struct MoeParams {
     double *const *ep_peer_back;
     uint32_t *const *ep_peer_flags;
     uint32_t *ep_epoch, *ep_done;
+    // tagged regions of the peer windows (EpPeer)
+    uint64_t *const *ep_peer_trecv;
+    uint64_t *const *ep_peer_tback;
+    uint64_t *const *ep_peer_tdone;
+    uint32_t ep_tslot_words;
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
@@ -225,7 +230,22 @@ struct EpPeer {
     double *const *back;
     uint32_t *const *flags;
     uint32_t *epoch, *done;
+    // Tagged regions of the windows for the single-launch layer (NULL when the exchange is too
+    // large for it): 8-byte words {32-bit payload, 32-bit call number}, so a receiver polls the
+    // data itself and no flag or system-scope fence is needed. trecv [2][G src][tmax][tslot_words]
+    // slots, tback [2][G owner][tmax][H][2] per-row sums (hi, lo words of the double), tdone
+    // [2][G] "finished reading this call's window" words.
+    uint64_t *const *trecv;
+    uint64_t *const *tback;
+    uint64_t *const *tdone;
+    uint32_t tslot_words;
 };
+// Word offsets in a tagged slot: n_owned, ids[MOE_MAX_K], weights[MOE_MAX_K], then the q8_1
+// row (9 words per 32-element block).
+constexpr int EPT_IDS = 1;
+constexpr int EPT_W = 1 + MOE_MAX_K;
+constexpr int EPT_ROW = 1 + 2 * MOE_MAX_K;
+inline uint32_t ep_tslot_words(uint32_t H) { return EPT_ROW + H / 32 * 9; }
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
 void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st);
 cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);

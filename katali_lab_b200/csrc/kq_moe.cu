@@ -128,81 +128,53 @@ __device__ void grid_barrier(const MoeParams &p, int &nbar) {
 }
 
 // --- the whole expert-parallel layer over peer memory (EP 2) --------------------
-// Call e (= *ep_epoch + 1, the same on every rank) uses parity e & 1 of every window:
-// recv [2][G sources][tmax][slot bytes], back [2][G sources][tmax][H] doubles, flags
-// [2 kinds][2 parities][G sources]. A rank stores its slots and sums straight into the
-// owners' windows (NVLink stores; peer loads are long dependent chains here) and raises
-// its flag in every window. A window part of call e is rewritten at call e + 2 only: every
-// rank's call e + 1 waited for every rank's sums of e + 1, which each rank raises after
-// it has read everything of call e.
-__device__ __forceinline__ void st_release_sys_u32(uint32_t *a, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+// Call e (= *ep_epoch + 1, the same on every rank) uses parity e & 1 of the windows' tagged
+// regions (EpPeer): every word a rank stores into another rank's window is 8 bytes, 32 bits
+// of payload and the call number e, so a receiver polls the data itself until it carries e
+// (no flag, no system-scope fence; a release flag cost ~6 us per exchange here). A rank
+// stores its slots (header, and the q8_1 row where the owner has pairs) straight into the
+// owners' windows (NVLink stores; peer loads are long dependent chains here), the owners
+// store each slot's final per-row sums (two words per double) into the source's window,
+// and each rank writes a "done" word into every window once none of its CTAs reads its own
+// window of call e any more. A window part of call e is rewritten at call e + 2 only: a
+// rank's call e + 1 ends after it has seen every rank's done word of e + 1, which each
+// rank writes after it has finished call e.
+// Tagged words: a plain (relaxed, system-scope) 8-byte store and load are single-copy atomic,
+// so payload and call number arrive together.
+__device__ __forceinline__ void st_tagged(uint64_t *a, uint32_t payload, uint32_t e) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(((uint64_t)e << 32) | payload) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *a) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-    return v;
-}
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t *a, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
-    return old;
-}
-__device__ __forceinline__ uint32_t *ep_flag(uint32_t *flags, int kind, uint32_t par, int G, int d) {
-    return flags + ((size_t)kind * 2 + par) * G + d;  // kind 0: slots landed, 1: sums landed
-}
-// After this CTA's stores into peer windows (every thread's, ordered by a CTA barrier):
-// the last of `writers` CTAs to count itself raises this rank's flag of `kind` for call
-// e in every rank's window. (A cross-GPU signal costs ~6 us here whichever way it is
-// fenced: per-CTA system fences, acquire-release ones, or one by the last CTA only.)
-__device__ __forceinline__ void ep_signal(const MoeParams &p, int kind, uint32_t e, uint32_t writers) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();  // this CTA's NVLink stores, before it is counted
-        const uint32_t prev = atom_add_acq_rel_gpu(&p.ep_done[kind], 1u);
-        if (prev == writers - 1) {
-            p.ep_done[kind] = 0u;
-            for (int d = 0; d < p.ep_ranks; ++d)
-                st_release_sys_u32(ep_flag(p.ep_peer_flags[d], kind, e & 1u, p.ep_ranks, p.ep_rank), e);
+// The payload of a tagged word once it carries call e (bounded; once any wait of the call
+// has given up the others give up at their next check).
+__device__ __forceinline__ uint32_t poll_tagged(const uint64_t *a, uint32_t e, volatile uint32_t *status) {
+    uint64_t v = 0;
+    for (uint32_t it = 0;; ++it) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+        if ((uint32_t)(v >> 32) == e) break;
+        if (it > SPIN_LIMIT || ((it & 1023u) == 1023u && (*status & ERR_TIMEOUT_GRID))) {
+            atomicOr((uint32_t *)status, ERR_TIMEOUT_GRID);
+            break;
         }
+        if (it > 16) __nanosleep(32);
     }
+    return (uint32_t)v;
 }
-// Every rank's flag of `kind` for call e in this rank's window (thread d polls rank d's
-// entry; bounded).
-__device__ void ep_wait_all(const MoeParams &p, int kind, uint32_t e) {
-    const int d = threadIdx.x;
-    if (d < p.ep_ranks) {
-        const uint32_t *f = ep_flag(p.ep_peer_flags[p.ep_rank], kind, e & 1u, p.ep_ranks, d);
-        uint32_t it = 0;
-        while (ld_acquire_sys_u32(f) != e) {
-            if (++it > SPIN_LIMIT) {
-                *p.status |= ERR_TIMEOUT_GRID;
-                break;
-            }
-            if (it > 16) __nanosleep(64);
-        }
-    }
-    __syncthreads();
-}
-// This rank's window's slot from source src's token t for call e.
-__device__ __forceinline__ const uint8_t *ep2_slot(const MoeParams &p, uint32_t e, int src, int t) {
-    return p.ep_peer_recv[p.ep_rank] + (((size_t)(e & 1u) * p.ep_ranks + src) * p.ep_tmax + t) * p.ep_slot_bytes;
+// Tagged slot (source src, token t) of call e in rank d's window.
+__device__ __forceinline__ uint64_t *ep2_tslot(const MoeParams &p, int d, uint32_t e, int src, int t) {
+    return p.ep_peer_trecv[d] + (((size_t)(e & 1u) * p.ep_ranks + src) * p.ep_tmax + t) * p.ep_tslot_words;
 }
 // Dispatch: CTA t < tmax routes this rank's token t, quantises its x to a GGUF q8_1 row
-// (`row`, shared) and writes slot (this rank, t) into every rank's window (empty headers
-// for t >= ep_tokens). Slot: n_owned, t, pad[2], ids[K] (-1 where another rank owns the
-// expert), w[K], then the row when n_owned > 0.
+// (`row`, shared) and stores slot (this rank, t) into every rank's window as tagged words:
+// n_owned, ids[K] (-1 where another rank owns the expert), w[K], then the row's words when
+// n_owned > 0 (a slot of a token t >= ep_tokens is n_owned 0 only).
 __device__ void ep2_dispatch(const MoeParams &p, uint32_t e, int K, int H, float *s_logits,
                              int32_t *s_ids, float *s_w, uint8_t *row) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
-    const int row_bytes = H / 32 * 36;
+    const int row_words = H / 32 * 9;
     for (int t = blockIdx.x; t < tmax; t += gridDim.x) {
-        auto dst = [&](int d) {
-            return p.ep_peer_recv[d] + (((size_t)(e & 1u) * G + me) * tmax + t) * p.ep_slot_bytes;
-        };
         if (t >= p.ep_tokens) {
-            if (tid < G) *reinterpret_cast<int4 *>(dst(tid)) = make_int4(0, t, 0, 0);
+            if (tid < G) st_tagged(ep2_tslot(p, tid, e, me, t), 0u, e);
             continue;
         }
         if (warp == 0) {
@@ -215,38 +187,41 @@ __device__ void ep2_dispatch(const MoeParams &p, uint32_t e, int K, int H, float
                                row + 36 * g);
         }
         __syncthreads();
+        const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
         for (int d = 0; d < G; ++d) {
-            uint8_t *slot = dst(d);
+            uint64_t *slot = ep2_tslot(p, d, e, me, t);
             int n = 0;
             for (int k = 0; k < K; ++k) n += s_ids[k] / per == d;
             if (tid < K) {
                 const int id = s_ids[tid];
-                reinterpret_cast<int *>(slot + 16)[tid] = id / per == d ? id : -1;
-                reinterpret_cast<float *>(slot + 16 + 4 * K)[tid] = s_w[tid];
+                st_tagged(slot + EPT_IDS + tid, (uint32_t)(id / per == d ? id : -1), e);
+                st_tagged(slot + EPT_W + tid, __float_as_uint(s_w[tid]), e);
             }
-            if (tid == 0) *reinterpret_cast<int4 *>(slot) = make_int4(n, t, 0, 0);
+            if (tid == 0) st_tagged(slot, (uint32_t)n, e);
             if (n > 0)
-                for (int i = tid; i < row_bytes / 16; i += MOE_THREADS)
-                    reinterpret_cast<int4 *>(slot + p.ep_hdr_bytes)[i] = reinterpret_cast<const int4 *>(row)[i];
+                for (int i = tid; i < row_words; i += MOE_THREADS) st_tagged(slot + EPT_ROW + i, rw[i], e);
         }
         trace(p, 16);
         __syncthreads();  // row and routing reused by the next token
     }
 }
-// Combine: y[t][r] = sum over ranks d owning one of t's experts (rank order) of back
-// [d][t][r] from this rank's back window.
+// Combine: y[t][r] = sum over ranks d owning one of t's experts (rank order) of the sum
+// rank d stored for slot (this rank, t), two tagged words per double in this rank's window.
 __device__ void ep2_combine(const MoeParams &p, uint32_t e, int K, int H) {
     const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
-    const double *back = p.ep_peer_back[me] + (size_t)(e & 1u) * G * tmax * H;
+    const uint64_t *back = p.ep_peer_tback[me] + (size_t)(e & 1u) * G * tmax * H * 2;
     const size_t n = (size_t)p.ep_tokens * H;
     for (size_t i = (size_t)blockIdx.x * MOE_THREADS + threadIdx.x; i < n;
          i += (size_t)gridDim.x * MOE_THREADS) {
         const int t = (int)(i / H), r = (int)(i % H);
+        uint32_t owners = 0;  // ranks owning one of t's experts
+        for (int k = 0; k < K; ++k) owners |= 1u << (__ldcg(p.ep_src_ids + t * K + k) / per);
         double acc = 0.0;
         for (int d = 0; d < G; ++d) {
-            bool own = false;
-            for (int k = 0; k < K; ++k) own |= __ldcg(p.ep_src_ids + t * K + k) / per == d;
-            if (own) acc += __ldcg(back + ((size_t)d * tmax + t) * H + r);
+            if (!((owners >> d) & 1u)) continue;
+            const uint64_t *w = back + (((size_t)d * tmax + t) * H + r) * 2;
+            const uint32_t hi = poll_tagged(w, e, p.status), lo = poll_tagged(w + 1, e, p.status);
+            acc += __hiloint2double((int)hi, (int)lo);
         }
         p.y[i] = p.accum ? __fadd_rn(p.y[i], (float)acc) : (float)acc;
     }
@@ -260,14 +235,24 @@ __device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, uint32_t e, in
     int base = 0;
     for (int s0 = 0; s0 < nslots; s0 += 32) {
         const int s = s0 + lane;
-        const uint8_t *slot = EP == 2 ? ep2_slot(p, e, s / p.ep_tmax, s % p.ep_tmax)
-                                      : recv + (size_t)s * p.ep_slot_bytes;  // EP 2: this rank's window
-        const int *ids = reinterpret_cast<const int *>(slot + 16);
-        const float *ws = reinterpret_cast<const float *>(slot + 16 + 4 * K);
         int idv[MOE_MAX_K];
         float wv[MOE_MAX_K];
         bool live = false;
-        if (s < nslots) {  // every header word loaded before any is used
+        if (EP == 2 && s < nslots) {  // this rank's window: tagged words of call e
+            const uint64_t *slot = ep2_tslot(p, p.ep_rank, e, s / p.ep_tmax, s % p.ep_tmax);
+            const int n = (int)poll_tagged(slot, e, p.status);
+            live = n > 0;
+            if (live)
+#pragma unroll
+                for (int k = 0; k < MOE_MAX_K; ++k)
+                    if (k < K) {
+                        idv[k] = (int)poll_tagged(slot + EPT_IDS + k, e, p.status);
+                        wv[k] = __uint_as_float(poll_tagged(slot + EPT_W + k, e, p.status));
+                    }
+        } else if (EP != 2 && s < nslots) {  // every header word loaded before any is used
+            const uint8_t *slot = recv + (size_t)s * p.ep_slot_bytes;
+            const int *ids = reinterpret_cast<const int *>(slot + 16);
+            const float *ws = reinterpret_cast<const float *>(slot + 16 + 4 * K);
             const int n = __ldcg(reinterpret_cast<const int *>(slot));
 #pragma unroll
             for (int k = 0; k < MOE_MAX_K; ++k)
@@ -303,14 +288,18 @@ __device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, uint32_t e, in
     __syncwarp();
 }
 // A slot's sum for one row: in ep_ret (a run of the slot's pairs continues from it in the
-// next round) and, EP 2, in the source rank's back window (a partial value is overwritten
-// by the final one before the flag is raised).
+// next round) and, EP 2, once the sum is final, into the source rank's window as two tagged
+// words (the source takes the first value that carries the call number).
 template <int EP>
-__device__ __forceinline__ void ep_store_t(const MoeParams &p, uint32_t e, int slot, int H, uint32_t row, double v) {
+__device__ __forceinline__ void ep_store_t(const MoeParams &p, uint32_t e, int slot, int H, uint32_t row,
+                                           double v, bool final_sum) {
     p.ep_ret[(size_t)slot * H + row] = v;
-    if (EP == 2) {  // the source rank's window: back[e & 1][this rank][t], slot = src * tmax + t
+    if (EP == 2 && final_sum) {  // tback[e & 1][this rank][t][row], slot = src * tmax + t
         const int src = slot / p.ep_tmax, t = slot % p.ep_tmax;
-        p.ep_peer_back[src][(((size_t)(e & 1u) * p.ep_ranks + p.ep_rank) * p.ep_tmax + t) * H + row] = v;
+        uint64_t *w = p.ep_peer_tback[src] +
+                      ((((size_t)(e & 1u) * p.ep_ranks + p.ep_rank) * p.ep_tmax + t) * H + row) * 2;
+        st_tagged(w, (uint32_t)__double2hiint(v), e);
+        st_tagged(w + 1, (uint32_t)__double2loint(v), e);
     }
 }
 
@@ -394,12 +383,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         ep_e = *p.ep_epoch + 1;
         ep_nslots = p.ep_ranks * p.ep_tmax;  // slot s = source rank * tmax + token
         ep2_dispatch(p, ep_e, K, H, s_logits, s_ids, s_w, act);
-        const uint32_t writers = (uint32_t)min((int)G, p.ep_tmax);  // CTAs that wrote slots
-        if (c < writers) ep_signal(p, 0, ep_e, writers);
-        trace(p, 9);
-        if (c < writers) trace(p, 1);
-        ep_wait_all(p, 0, ep_e);
-        trace(p, 10);
+        if (c < (uint32_t)p.ep_tmax) trace(p, 1);
+        __syncthreads();  // s_ids / s_w / act reused below
     }
     if constexpr (EP != 0) {
         pdl_wait();
@@ -568,16 +553,22 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         if (nbA > 0) {
             const int kb = (int)(b0 / (F / HB));
             const int sl = s_slotr[kb];
-            const uint8_t *row = (EP == 2 ? ep2_slot(p, ep_e, sl / p.ep_tmax, sl % p.ep_tmax)
-                                          : ep_recv + (size_t)sl * p.ep_slot_bytes) + p.ep_hdr_bytes;
+            // EP 2: the row's tagged words in this rank's window (9 per block: d | sum, then
+            // 32 int8 four to a word); EP 1: the received bytes
+            const uint64_t *trow = EP == 2 ? ep2_tslot(p, p.ep_rank, ep_e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_ROW
+                                           : nullptr;
+            const uint8_t *row = EP == 2 ? nullptr : ep_recv + (size_t)sl * p.ep_slot_bytes + p.ep_hdr_bytes;
             for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
-                const uint8_t *blk = row + 36 * g;
-                const int qi = (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
+                const uint8_t *blk = EP == 2 ? nullptr : row + 36 * g;
+                const int qi = EP == 2
+                    ? (int)(signed char)(poll_tagged(trow + 9 * g + 1 + (lane >> 2), ep_e, p.status) >> (8 * (lane & 3)))
+                    : (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
                 const int sum = __reduce_add_sync(KQ_FULL, qi);
                 const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
                 xq[32 * g + lane] = (int8_t)qi;
                 if (lane == 0) {
-                    xd[g] = h2f(__ldcg(reinterpret_cast<const unsigned short *>(blk)));
+                    xd[g] = h2f(EP == 2 ? poll_tagged(trow + 9 * g, ep_e, p.status) & 0xFFFFu
+                                        : __ldcg(reinterpret_cast<const unsigned short *>(blk)));
                     xs32[g] = sum;
                     xs16[2 * g] = sum_lo;
                     xs16[2 * g + 1] = sum - sum_lo;
@@ -821,15 +812,17 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                     double acc = 0.0;
                     for (int kk = 0; kk < KR; ++kk) {
                         const int sl = s_slotr[kk];
-                        if (sl != cur) {
-                            if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc);
+                        if (sl != cur) {  // the previous slot's run ends here: its sum is final
+                            if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, true);
                             const bool cont = kk == 0 && rd > 0 && s_pslot[rd * K - 1] == sl;
                             acc = cont ? p.ep_ret[(size_t)sl * H + rB0 + r] : 0.0;
                             cur = sl;
                         }
                         acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
                     }
-                    if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc);
+                    // final unless the slot's run continues in the next round
+                    const int nx = rd * K + KR;
+                    if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, nx >= npairs || s_pslot[nx] != cur);
                 } else {
                     double acc = 0.0;
                     for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
@@ -872,11 +865,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     }
     }  // rounds
     if constexpr (EP == 2) {
-        // every CTA stored its rows' sums into the sources' back windows in phase B
-        ep_signal(p, 1, ep_e, G);
+        // no CTA reads this rank's window of call e any more: the last one to count itself
+        // writes this rank's done word into every rank's window
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t prev = atomicAdd(&p.ep_done[1], 1u);
+            if (prev == G - 1) {
+                p.ep_done[1] = 0u;
+                for (int d = 0; d < p.ep_ranks; ++d)
+                    st_tagged(p.ep_peer_tdone[d] + (size_t)(ep_e & 1u) * p.ep_ranks + p.ep_rank, 1u, ep_e);
+            }
+        }
         trace(p, 2);
-        ep_wait_all(p, 1, ep_e);
-        trace(p, 18);
         ep2_combine(p, ep_e, K, H);
         trace(p, 19);
     }
@@ -889,7 +889,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         if (prev == G - 1) {
             atomicExch(&p.sync[0], 0u);
             atomicExch(&p.sync[1], 0u);
-            if (EP == 2) {  // the next call uses the other parity of every window
+            if (EP == 2) {
+                // every rank has finished reading its window of call e, so call e + 2 may
+                // rewrite this parity; the next call uses the other one
+                for (int d = 0; d < p.ep_ranks; ++d)
+                    poll_tagged(p.ep_peer_tdone[p.ep_rank] + (size_t)(ep_e & 1u) * p.ep_ranks + d, ep_e, p.status);
                 __threadfence();
                 *p.ep_epoch = ep_e;
             }
