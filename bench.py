@@ -439,6 +439,7 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+TRACE_SLOTS = 24  # per CTA, as the plugin writes them
 TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first chunk in",
                5: "gate/up done", 6: "barrier passed", 7: "phase B start", 8: "end",
                9: "route: logits in", 10: "route: sorted", 11: "route: top-k done",
@@ -446,37 +447,49 @@ TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first ch
                15: "phase B row0 dots"}
 
 
-def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False):
-    """Phase timeline of the fused MoE kernel from its %globaltimer trace (ns)."""
+EP_TRACE_NAMES = {**TRACE_NAMES, 1: "slots stored", 11: "pairs received", 18: "rounds done",
+                  19: "combine done", 20: "dispatch: routed", 21: "x rows staged",
+                  22: "round 0 done", 23: "next round requested"}
+
+
+def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False, call=None, names=TRACE_NAMES,
+                tag="[trace]"):
+    """Phase timeline of the fused MoE kernel from its %globaltimer trace (ns). `call(i)`
+    runs layer call i (default: the single-GPU layer on token i)."""
     import torch
     from katali_lab_b200 import MOE_Q8_1
-    buf = torch.zeros(1024 * 20, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(1024 * TRACE_SLOTS, dtype=torch.int64, device="cuda")
     mhz = []
     rows = []
+    slots = sorted(names)
     for n in range(min(T, 32)):
         i = 0 if warm else n
         lay = layers[i % L]
         grid = lay.set_trace(buf)
-        lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+        if call is None:
+            lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+        else:
+            call(i)
         plugin.sync()
         lay.set_trace(None)
-        t = buf[:grid * 20].view(grid, 20).cpu().numpy().astype(np.int64)
+        t = buf[:grid * TRACE_SLOTS].view(grid, TRACE_SLOTS).cpu().numpy().astype(np.int64)
         t = t[t[:, 0] > 0]  # the CTAs that ran (a launch may use fewer than the grid size)
         buf.zero_()
         mhz.append(np.median((t[:, 17] - t[:, 16]) / np.maximum(t[:, 8] - t[:, 0], 1) * 1e3))
         t0 = t[:, 0].min()
         row = [t[:, 0].max() - t0]
-        for s in range(1, 16):  # CTAs without phase-A or phase-B rows leave their slot 0
+        for s in slots:  # CTAs without phase-A or phase-B rows leave their slot 0
             v = t[:, s][t[:, s] > 0]
             row.append((v.max() - t0) if v.size else 0)
         rows.append(row)
     med = np.median(np.array(rows, dtype=np.float64), axis=0) / 1e3
-    print("[trace] median over calls, us after the first CTA started (max over CTAs):",
+    print(f"{tag} median over calls, us after the first CTA started (max over CTAs):",
           file=sys.stderr)
-    print(f"[trace]   last CTA start {med[0]:.2f}", file=sys.stderr)
-    for s, v in sorted(zip(range(1, 16), med[1:]), key=lambda sv: sv[1]):
-        print(f"[trace]   {TRACE_NAMES[s]:20s} {v:.2f}", file=sys.stderr)
-    print(f"[trace]   SM clock inside the kernel: {np.median(mhz):.0f} MHz (cycles / ns)", file=sys.stderr)
+    print(f"{tag}   last CTA start {med[0]:.2f}", file=sys.stderr)
+    for s, v in sorted(zip(slots, med[1:]), key=lambda sv: sv[1]):
+        if v > 0:
+            print(f"{tag}   {names[s]:20s} {v:.2f}", file=sys.stderr)
+    print(f"{tag}   SM clock inside the kernel: {np.median(mhz):.0f} MHz (cycles / ns)", file=sys.stderr)
 
 
 C1_ROWS, C1_COLS = 6144, 2048
@@ -818,6 +831,66 @@ def ep_parity(plugin, store, world, xs, lgs, ys, offs):
             "bar": "rel_L2 <= 1e-5"}
 
 
+def ep_trace(plugin, layers, step, stream, rank, world, L, n):
+    """Phase timeline of the single-launch expert-parallel layer as the timed graph runs it
+    (calls back to back, ranks in lock step): one trace buffer per layer keeps that layer's
+    last call of a replay; rank 0 prints, per rank, the median over layers of each phase's
+    end (max over CTAs) after the first CTA of the call started on any rank (%globaltimer;
+    the GPUs' timers agree only to within their offset) and the gap from a call's end to the
+    next call's first CTA on the same rank."""
+    import torch
+    import torch.distributed as dist
+    bufs = torch.zeros((L, 1024 * TRACE_SLOTS), dtype=torch.int64, device="cuda")
+    grids = [layers[l].layer.set_trace(bufs[l]) for l in range(L)]
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        step()
+    for _ in range(3):
+        g2.replay()
+    torch.cuda.synchronize()
+    for l in layers:
+        l.layer.set_trace(None)
+    del g2
+    gath = [torch.empty_like(bufs) for _ in range(world)]
+    dist.all_gather(gath, bufs)
+    torch.cuda.synchronize()
+    if rank != 0:
+        return
+    tr = [g.cpu().numpy() for g in gath]
+    last = sorted(range(L), key=lambda l: (n - 1 - l) // L * L + l)  # layers in call order
+    names = {0: "CTAs started", **EP_TRACE_NAMES}
+    slots = sorted(names)
+    rows = {r: [] for r in range(world)}
+    gaps = {r: [] for r in range(world)}
+    for l in range(L):
+        ts = []
+        for r in range(world):
+            t = tr[r][l][:grids[l] * TRACE_SLOTS].reshape(grids[l], TRACE_SLOTS)
+            ts.append(t[t[:, 0] > 0])
+        t0 = min(int(t[:, 0].min()) for t in ts)
+        for r, t in enumerate(ts):
+            row = []
+            for s in slots:
+                v = t[:, s][t[:, s] > 0]
+                row.append((int(v.max()) - t0) if v.size else np.nan)
+            rows[r].append(row)
+    for i in range(L - 1):  # consecutive calls i, i + 1 of the last stretch of the step
+        a, b = last[i], last[i + 1]
+        for r in range(world):
+            ta = tr[r][a][:grids[a] * TRACE_SLOTS].reshape(grids[a], TRACE_SLOTS)
+            tb = tr[r][b][:grids[b] * TRACE_SLOTS].reshape(grids[b], TRACE_SLOTS)
+            ta, tb = ta[ta[:, 0] > 0], tb[tb[:, 0] > 0]
+            gaps[r].append(int(tb[:, 0].min()) - int(ta[:, 8].max()))
+    print("[trace] median over layers, us after the call's first CTA on any rank "
+          "(max over a rank's CTAs):", file=sys.stderr)
+    for r in range(world):
+        med = np.nanmedian(np.array(rows[r], dtype=np.float64), axis=0) / 1e3
+        parts = sorted(((v, names[s]) for s, v in zip(slots, med) if v == v and v > 0))
+        print(f"[trace r{r}] " + ", ".join(f"{nm} {v:.2f}" for v, nm in parts), file=sys.stderr)
+        print(f"[trace r{r}] call end -> next call start: median {np.median(gaps[r]) / 1e3:.2f} us",
+              file=sys.stderr)
+
+
 def run_ep(args, rank, world, local_rank):
     """C2 / C3 with experts split over the GPUs (one process each): every rank holds E/N
     experts of every layer and brings its own tokens (one per call for C2, T ~ U{1..64}
@@ -943,7 +1016,15 @@ def run_ep(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": round(value / world, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(value / world / peak, 4),
                          "peak_kind": f"{peak_kind} hbm_gbs, per GPU", "traffic": None,
-                         "scope": "whole call incl. both NCCL exchanges, per GPU"},
+                         "scope": ("whole call per GPU: one launch doing dispatch, expert "
+                                   "decode, return and combine over NVLink peer memory"
+                                   if not args.nccl and not ragged else
+                                   "whole call per GPU: the layer's launches and the exchanges "
+                                   + ("over NVLink peer memory" if not args.nccl
+                                      else "by NCCL send/recv"))},
+            "collective": ("none on the data path: peer-memory loads and stores inside the "
+                           "kernels (NCCL only all-gathers the IPC handles once, at setup)"
+                           if not args.nccl else "NCCL grouped send/recv, twice per call"),
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": xh.numel() * 4 + lh.numel() * 4,
@@ -952,6 +1033,8 @@ def run_ep(args, rank, world, local_rank):
             "gpu_launches": args.steps * n * (1 if not ragged and not args.nccl else 8),
             "cpu_baseline": None}
     del gr
+    if args.trace:
+        ep_trace(plugin, layers, step, stream, rank, world, L, n)
     comm.close()
     for l in layers:
         l.close()
@@ -1248,12 +1331,15 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
+    out_fd = 1
     if world > 1:
+        # Libraries print to file descriptor 1 (NCCL's version banner): for the whole run it
+        # points at stderr, and the one JSON line goes to the saved stdout.
+        out_fd = os.dup(1)
+        os.dup2(2, 1)
         import datetime
 
-        # stdout carries exactly one JSON line: NCCL's banner lines stay off unless asked for
         os.environ.setdefault("NCCL_DEBUG", "WARN")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")  # NCCL's version banner off stdout
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
@@ -1278,7 +1364,8 @@ def main():
             if rank == 0 and line is not None:
                 line["secondary"] = sec
         if rank == 0 and line is not None:
-            print(json.dumps(line), flush=True)
+            sys.stdout.flush()
+            os.write(out_fd, (json.dumps(line) + "\n").encode())
     finally:
         if world > 1:
             import torch.distributed as dist

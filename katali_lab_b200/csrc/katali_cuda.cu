@@ -161,7 +161,7 @@ struct KataliMoe {
     // Ragged-batch scratch, grown on demand (katali_cuda_moe_batch, the EP stages).
     unsigned char *bscratch;
     size_t bscratch_bytes;
-    int32_t *ep_src_ids;  // routing of the last katali_cuda_moe_ep_dispatch
+    int32_t *ep_src_ids;  // routing of the last dispatch (8 bytes per id: tagged in the fused layer)
     uint32_t ep_src_cap;  // tokens
     KataliExpertCache *cache;  // the residency cache this layer's experts are bound to
 };
@@ -701,7 +701,7 @@ int moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_
         if (e != cudaSuccess) return cuda_fail(e);
         cudaFree(m->ep_src_ids);
         m->ep_src_cap = 0;
-        e = cudaMalloc((void **)&m->ep_src_ids, 4ull * K * max_tokens);
+        e = cudaMalloc((void **)&m->ep_src_ids, 8ull * K * max_tokens);  // tagged in the fused layer
         if (e != cudaSuccess) {
             m->ep_src_ids = nullptr;
             return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
@@ -727,6 +727,7 @@ int moe_ep_experts(KataliMoe *m, uint32_t n_ranks, uint32_t rank, uint32_t max_t
     const int T = (int)(n_ranks * max_tokens);
     if (!pp && ep_fused_ok(m, T)) {  // the fused kernel over the received pairs
         kq::MoeParams p = m->plan[KATALI_MOE_Q8_1];
+        kq::moe_plan_dec_apart(p, g_max_smem);  // rounds overlap when shared memory allows
         p.experts = m->d_table;
         p.x = nullptr;
         p.logits = nullptr;
@@ -777,7 +778,7 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
         if (e != cudaSuccess) return cuda_fail(e);
         cudaFree(m->ep_src_ids);
         m->ep_src_cap = 0;
-        e = cudaMalloc((void **)&m->ep_src_ids, 4ull * K * max_tokens);
+        e = cudaMalloc((void **)&m->ep_src_ids, 8ull * K * max_tokens);  // tagged in the fused layer
         if (e != cudaSuccess) {
             m->ep_src_ids = nullptr;
             return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
@@ -785,6 +786,7 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
         m->ep_src_cap = max_tokens;
     }
     kq::MoeParams p = m->plan[KATALI_MOE_Q8_1];
+    kq::moe_plan_dec_apart(p, g_max_smem);  // rounds overlap when shared memory allows
     p.experts = m->d_table;
     p.x = x;
     p.logits = router_logits;
@@ -797,7 +799,6 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
     p.dbg_ids = m->dbg_ids;
     p.dbg_w = m->dbg_w;
     p.route_only = 0;
-    p.trace = nullptr;
     p.trace = m->trace;  // optional per-stage timestamps (katali_cuda_debug_moe_trace)
     p.ep_recv = nullptr;  // this rank's window, chosen on the device
     p.ep_ret = ret_scratch;

@@ -109,7 +109,8 @@ constexpr int MOE_EP_MAX_SLOTS = 16;
 constexpr int MOE_EP_MAX_PAIRS = MOE_EP_MAX_SLOTS * MOE_MAX_K;
 constexpr int MOE_MAX_CHUNKS = 64;
 constexpr int MOE_RT_ROWS = 4;   // router rows per CTA when the router is folded into the launch
-constexpr int TRACE_SLOTS = 20;  // 16 %globaltimer slots + clock64 at start/end  // %globaltimer samples per CTA when tracing
+// Per CTA when tracing: %globaltimer slots 0-15 and 18-23, clock64 at start and end in 16, 17.
+constexpr int TRACE_SLOTS = 24;
 
 struct MoeParams {
     const uint8_t *const *experts;  // device table: gate_e, up_e, down_e per expert
@@ -144,6 +145,7 @@ struct MoeParams {
     uint32_t sb_off, sb_bytes;
     uint32_t act_off, hact_off, misc_off, smem_bytes;
     uint32_t dec_off, dec_row_bytes;  // decoded int8 down rows (q8_1 mode, Q6_K)
+    uint32_t dec_bytes;               // their area (dec_off == 0: inside the phase-A staging)
     uint32_t sdot_off;                // phase-B per-expert row dots [K][rows]
     int dec_enabled;
     // Expert-parallel experts stage (launch_moe_ep): the received slots in (the slot
@@ -170,6 +172,10 @@ struct MoeParams {
 };
 
 cudaError_t launch_moe(MoeParams &p, int grid, cudaStream_t st);
+// Move the decoded down rows out of the phase-A staging area when shared memory allows, so
+// that the expert-parallel kernel can request a round's gate/up rows while the previous
+// round still decodes and sums (its rounds then overlap). Returns 1 when moved.
+int moe_plan_dec_apart(MoeParams &p, int max_smem);
 // The experts stage of an expert-parallel layer for at most MOE_EP_MAX_SLOTS received
 // slots (q8_1, Q6_K down, F a power of two in [256, 2048], K * F / 32 <= grid).
 cudaError_t launch_moe_ep(MoeParams &p, int grid, cudaStream_t st);

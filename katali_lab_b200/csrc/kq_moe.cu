@@ -107,21 +107,30 @@ __device__ __forceinline__ void mbar_inval(uint64_t *bar) {
     asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Grid barrier on p.sync[0], shared with the per-round barriers: the n-th barrier of a
-// launch waits for n * gridDim.x arrivals (the last CTA out resets the counter).
-__device__ void grid_barrier(const MoeParams &p, int &nbar) {
+// Grid barriers count arrivals on p.sync[0], which only grows (32-bit, compared modulo
+// 2^32): the n-th barrier of a launch waits until it reaches base + n * gridDim.x, where base
+// (p.sync[3]) is where the previous launch left it; CTA 0 records the new value at the end of
+// a launch. Thread 0 of every CTA reads base after the programmatic wait.
+__device__ __forceinline__ uint32_t sync_base(const MoeParams &p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.sync + 3) : "memory");
+    return v;
+}
+__device__ __forceinline__ void grid_wait(const MoeParams &p, uint32_t target) {
+    uint32_t it = 0;
+    while ((int32_t)(ld_acquire_gpu(&p.sync[0]) - target) < 0) {
+        if (++it > SPIN_LIMIT) {
+            *p.status |= ERR_TIMEOUT_GRID;
+            break;
+        }
+        if (it > 32) __nanosleep(20);
+    }
+}
+__device__ void grid_barrier(const MoeParams &p, int &nbar, uint32_t sbase) {
     __syncthreads();
     if (threadIdx.x == 0) {
         red_release_gpu_add(&p.sync[0], 1u);
-        const uint32_t target = (uint32_t)(nbar + 1) * gridDim.x;
-        uint32_t it = 0;
-        while (ld_acquire_gpu(&p.sync[0]) < target) {
-            if (++it > SPIN_LIMIT) {
-                *p.status |= ERR_TIMEOUT_GRID;
-                break;
-            }
-            if (it > 32) __nanosleep(20);
-        }
+        grid_wait(p, sbase + (uint32_t)(nbar + 1) * gridDim.x);
     }
     ++nbar;
     __syncthreads();
@@ -141,115 +150,228 @@ __device__ void grid_barrier(const MoeParams &p, int &nbar) {
 // rank writes after it has finished call e.
 // Tagged words: a plain (relaxed, system-scope) 8-byte store and load are single-copy atomic,
 // so payload and call number arrive together.
-__device__ __forceinline__ void st_tagged(uint64_t *a, uint32_t payload, uint32_t e) {
-    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(((uint64_t)e << 32) | payload) : "memory");
+__device__ __forceinline__ uint64_t tag_word(uint32_t payload, uint32_t e) {
+    return ((uint64_t)e << 32) | payload;
 }
-// The payload of a tagged word once it carries call e (bounded; once any wait of the call
-// has given up the others give up at their next check).
-__device__ __forceinline__ uint32_t poll_tagged(const uint64_t *a, uint32_t e, volatile uint32_t *status) {
-    uint64_t v = 0;
-    for (uint32_t it = 0;; ++it) {
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
-        if ((uint32_t)(v >> 32) == e) break;
+__device__ __forceinline__ void st_tagged(uint64_t *a, uint32_t payload, uint32_t e) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(tag_word(payload, e)) : "memory");
+}
+// Two tagged words (16-byte aligned) in one vector store; each word is single-copy atomic on
+// its own and the reader checks both tags.
+__device__ __forceinline__ void st_tagged2(uint64_t *a, uint32_t p0, uint32_t p1, uint32_t e) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(a), "l"(tag_word(p0, e)),
+                 "l"(tag_word(p1, e)) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_tagged(const uint64_t *a) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ld_tagged2(const uint64_t *a, uint64_t &v0, uint64_t &v1) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(a) : "memory");
+}
+// The payload of a tagged word once it carries call e, starting from a value v already
+// loaded from it (bounded; once any wait of the call has given up the others give up at
+// their next check).
+__device__ __forceinline__ uint32_t tagged_value(const uint64_t *a, uint64_t v, uint32_t e,
+                                                 volatile uint32_t *status) {
+    for (uint32_t it = 0; (uint32_t)(v >> 32) != e; ++it) {
         if (it > SPIN_LIMIT || ((it & 1023u) == 1023u && (*status & ERR_TIMEOUT_GRID))) {
             atomicOr((uint32_t *)status, ERR_TIMEOUT_GRID);
             break;
         }
         if (it > 16) __nanosleep(32);
+        v = ld_tagged(a);
     }
     return (uint32_t)v;
+}
+__device__ __forceinline__ uint32_t poll_tagged(const uint64_t *a, uint32_t e, volatile uint32_t *status) {
+    return tagged_value(a, ld_tagged(a), e, status);
 }
 // Tagged slot (source src, token t) of call e in rank d's window.
 __device__ __forceinline__ uint64_t *ep2_tslot(const MoeParams &p, int d, uint32_t e, int src, int t) {
     return p.ep_peer_trecv[d] + (((size_t)(e & 1u) * p.ep_ranks + src) * p.ep_tmax + t) * p.ep_tslot_words;
 }
-// Dispatch: CTA t < tmax routes this rank's token t, quantises its x to a GGUF q8_1 row
-// (`row`, shared) and stores slot (this rank, t) into every rank's window as tagged words:
-// n_owned, ids[K] (-1 where another rank owns the expert), w[K], then the row's words when
-// n_owned > 0 (a slot of a token t >= ep_tokens is n_owned 0 only).
+// Dispatch of call e. Warp 0 of CTA t (< tmax) routes this rank's token t, records the
+// routing (tagged, for the combine) and stores slot (this rank, t)'s header into every rank's
+// window: n_owned, ids[K] (-1 where another rank owns the expert), then w[K] once the softmax
+// weights are formed (a receiver needs them only for its sums); a token t >= ep_tokens has
+// n_owned 0, ids -1 and w 0. The other warps, spread over the CTAs, quantise the
+// tokens' x block by block to GGUF q8_1 (9 words per 32 values) and store each block into
+// every rank's window (only the owners of one of the token's experts read it).
 __device__ void ep2_dispatch(const MoeParams &p, uint32_t e, int K, int H, float *s_logits,
-                             int32_t *s_ids, float *s_w, uint8_t *row) {
+                             int32_t *s_ids, float *s_w, uint8_t *blkbuf) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
-    const int row_words = H / 32 * 9;
-    for (int t = blockIdx.x; t < tmax; t += gridDim.x) {
-        if (t >= p.ep_tokens) {
-            if (tid < G) st_tagged(ep2_tslot(p, tid, e, me, t), 0u, e);
-            continue;
-        }
-        if (warp == 0) {
-            route(p, p.logits + (size_t)t * p.n_experts, s_logits, s_ids, s_w, lane, true);
-            if (lane < K) p.ep_src_ids[t * K + lane] = s_ids[lane];
-        } else {
-            const float *x = p.x + (size_t)t * H;
-            for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1)
-                quant_block_q8(__ldg(x + 32 * g + lane), lane, nullptr, nullptr, nullptr, nullptr,
-                               row + 36 * g);
-        }
-        __syncthreads();
-        const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
-        for (int d = 0; d < G; ++d) {
-            uint64_t *slot = ep2_tslot(p, d, e, me, t);
-            int n = 0;
-            for (int k = 0; k < K; ++k) n += s_ids[k] / per == d;
-            if (tid < K) {
-                const int id = s_ids[tid];
-                st_tagged(slot + EPT_IDS + tid, (uint32_t)(id / per == d ? id : -1), e);
-                st_tagged(slot + EPT_W + tid, __float_as_uint(s_w[tid]), e);
+    uint64_t *route_rec = reinterpret_cast<uint64_t *>(p.ep_src_ids);  // [tmax][K] tagged ids
+    if (warp == 0) {
+        for (int t = blockIdx.x; t < tmax; t += gridDim.x) {
+            const bool live = t < p.ep_tokens;
+            const float *L = p.logits + (size_t)t * p.n_experts;
+            float lv[8];
+            const bool regs = p.n_experts <= 256;  // weights formed after the ids are out
+            if (live) {
+                if (regs) route_regs(p, L, lane, s_ids, s_w, false, lv);
+                else route_smem(p, L, s_logits, s_ids, s_w, lane, true);
             }
-            if (tid == 0) st_tagged(slot, (uint32_t)n, e);
-            if (n > 0)
-                for (int i = tid; i < row_words; i += MOE_THREADS) st_tagged(slot + EPT_ROW + i, rw[i], e);
+            __syncwarp();
+            trace(p, 20);
+            const int id = live && lane < K ? s_ids[lane] : -1;
+            if (lane < K) st_tagged(route_rec + (size_t)t * K + lane, (uint32_t)id, e);
+            for (int d = 0; d < G; ++d) {
+                uint64_t *slot = ep2_tslot(p, d, e, me, t);
+                const bool mine = id >= 0 && id / per == d;
+                const int n = __popc(__ballot_sync(KQ_FULL, lane < K && mine));
+                if (lane < K) st_tagged(slot + EPT_IDS + lane, (uint32_t)(mine ? id : -1), e);
+                if (lane == 0) st_tagged(slot, (uint32_t)n, e);
+            }
+            if (live && regs) route_weights_regs(p, lane, lv, s_ids, s_w);
+            __syncwarp();
+            const float w = live && lane < K ? s_w[lane] : 0.0f;
+            if (lane < K)
+                for (int d = 0; d < G; ++d) st_tagged(ep2_tslot(p, d, e, me, t) + EPT_W + lane, __float_as_uint(w), e);
+            __syncwarp();
         }
-        trace(p, 16);
-        __syncthreads();  // row and routing reused by the next token
+    } else {
+        const int nblk = H / 32, items = p.ep_tokens * nblk;
+        uint8_t *b = blkbuf + 36 * (warp - 1);
+        for (int i = (warp - 1) * (int)gridDim.x + (int)blockIdx.x; i < items;
+             i += (MOE_WARPS - 1) * (int)gridDim.x) {
+            const int t = i / nblk, g = i - t * nblk;
+            quant_block_q8(__ldg(p.x + (size_t)t * H + 32 * g + lane), lane, nullptr, nullptr, nullptr,
+                           nullptr, b);
+            __syncwarp();
+            if (lane < 9) {
+                const uint32_t wv = reinterpret_cast<const uint32_t *>(b)[lane];
+                for (int d = 0; d < G; ++d) st_tagged(ep2_tslot(p, d, e, me, t) + EPT_ROW + 9 * g + lane, wv, e);
+            }
+            __syncwarp();
+        }
     }
 }
-// Combine: y[t][r] = sum over ranks d owning one of t's experts (rank order) of the sum
-// rank d stored for slot (this rank, t), two tagged words per double in this rank's window.
-__device__ void ep2_combine(const MoeParams &p, uint32_t e, int K, int H) {
-    const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
+// Word i of the received slot headers of call e (this rank's window): slot s = i / (1 + K),
+// then n_owned, ids[K] (the weights are read later, per round).
+__device__ __forceinline__ const uint64_t *ep2_hdr_word(const MoeParams &p, uint32_t e, int K, int i) {
+    const int s = i / (1 + K), j = i - s * (1 + K);
+    return ep2_tslot(p, p.ep_rank, e, s / p.ep_tmax, s % p.ep_tmax) + (j == 0 ? 0 : EPT_IDS + j - 1);
+}
+// Every thread of the CTA polls its words of the received headers (all loads issued before
+// any wait) into hw[nslots][1 + K].
+__device__ void ep2_headers(const MoeParams &p, uint32_t e, int nslots, int K, uint32_t *hw) {
+    const int n = nslots * (1 + K);
+    for (int i0 = threadIdx.x; i0 < n; i0 += 2 * MOE_THREADS) {
+        const int i1 = i0 + MOE_THREADS;
+        const uint64_t *a0 = ep2_hdr_word(p, e, K, i0);
+        const uint64_t *a1 = i1 < n ? ep2_hdr_word(p, e, K, i1) : a0;
+        const uint64_t v0 = ld_tagged(a0), v1 = ld_tagged(a1);
+        hw[i0] = tagged_value(a0, v0, e, p.status);
+        if (i1 < n) hw[i1] = tagged_value(a1, v1, e, p.status);
+    }
+}
+// x of a phase-A block's token (warps 1..15): slot sl's q8_1 row from this rank's window of
+// call e, polled in parallel into raw (9 words per 32 values: d | sum, then 32 int8 four to a
+// word), then unpacked into the activation area.
+__device__ void ep2_stage_x(const MoeParams &p, uint32_t e, int H, int sl, uint32_t *raw, int8_t *xq,
+                            float *xd, int *xs32, int *xs16) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint64_t *trow = ep2_tslot(p, p.ep_rank, e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_ROW;
+    const int nw = H / 32 * 9, nt = MOE_THREADS - 32;
+    for (int i0 = tid - 32; i0 < nw; i0 += 2 * nt) {
+        const int i1 = i0 + nt;
+        const uint64_t v0 = ld_tagged(trow + i0), v1 = ld_tagged(trow + (i1 < nw ? i1 : i0));
+        raw[i0] = tagged_value(trow + i0, v0, e, p.status);
+        if (i1 < nw) raw[i1] = tagged_value(trow + i1, v1, e, p.status);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(MOE_THREADS - 32) : "memory");
+    for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
+        const int qi = (int)(signed char)(raw[9 * g + 1 + (lane >> 2)] >> (8 * (lane & 3)));
+        const int sum = __reduce_add_sync(KQ_FULL, qi);
+        const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+        xq[32 * g + lane] = (int8_t)qi;
+        if (lane == 0) {
+            xd[g] = h2f(raw[9 * g] & 0xFFFFu);
+            xs32[g] = sum;
+            xs16[2 * g] = sum_lo;
+            xs16[2 * g + 1] = sum - sum_lo;
+        }
+    }
+}
+// Combine: y[t][r] = sum over ranks d owning one of t's experts (rank order) of the sum rank d
+// stored for slot (this rank, t), two tagged words per double in this rank's window. s_own:
+// the owner ranks of each token (from the tagged routing record); a token whose experts are
+// all on this rank was written by phase B and is skipped.
+__device__ void ep2_combine(const MoeParams &p, uint32_t e, int H, const uint32_t *s_own) {
+    const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax;
     const uint64_t *back = p.ep_peer_tback[me] + (size_t)(e & 1u) * G * tmax * H * 2;
     const size_t n = (size_t)p.ep_tokens * H;
     for (size_t i = (size_t)blockIdx.x * MOE_THREADS + threadIdx.x; i < n;
          i += (size_t)gridDim.x * MOE_THREADS) {
         const int t = (int)(i / H), r = (int)(i % H);
-        uint32_t owners = 0;  // ranks owning one of t's experts
-        for (int k = 0; k < K; ++k) owners |= 1u << (__ldcg(p.ep_src_ids + t * K + k) / per);
+        const uint32_t owners = s_own[t];
+        if (owners == (1u << me)) continue;
         double acc = 0.0;
-        for (int d = 0; d < G; ++d) {
-            if (!((owners >> d) & 1u)) continue;
-            const uint64_t *w = back + (((size_t)d * tmax + t) * H + r) * 2;
-            const uint32_t hi = poll_tagged(w, e, p.status), lo = poll_tagged(w + 1, e, p.status);
-            acc += __hiloint2double((int)hi, (int)lo);
+        for (int d0 = 0; d0 < G; d0 += 4) {  // four owners' words in flight at a time
+            uint64_t v[4][2];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (d0 + j < G && ((owners >> (d0 + j)) & 1u))
+                    ld_tagged2(back + (((size_t)(d0 + j) * tmax + t) * H + r) * 2, v[j][0], v[j][1]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (d0 + j < G && ((owners >> (d0 + j)) & 1u)) {
+                    const uint64_t *w = back + (((size_t)(d0 + j) * tmax + t) * H + r) * 2;
+                    const uint32_t hi = tagged_value(w, v[j][0], e, p.status);
+                    const uint32_t lo = tagged_value(w + 1, v[j][1], e, p.status);
+                    acc += __hiloint2double((int)hi, (int)lo);
+                }
         }
         p.y[i] = p.accum ? __fadd_rn(p.y[i], (float)acc) : (float)acc;
     }
 }
-// Expert-parallel pairs of the received slots, in slot then k order (warp 0): a slot
-// header holds n_owned, t, pad[2], ids[K] (global expert id, or -1 when another rank
-// owns it), w[K]; slots with n_owned == 0 carry no pairs.
-template <int EP>
-__device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, uint32_t e, int nslots, int K,
-                         int lane, int *pslot, int *pid, float *pw, int *np) {
+// EP 2 pairs from the polled headers hw (warp 0): in slot then k order; pw holds each pair's
+// k (as int bits) until its round reads the weight; s_nown[s] = n_owned.
+__device__ void ep2_pairs(const uint32_t *hw, int nslots, int K, int lane, int *pslot, int *pid,
+                          float *pw, int *np, int *s_nown) {
+    int base = 0;
+    for (int s0 = 0; s0 < nslots; s0 += 32) {
+        const int s = s0 + lane;
+        const uint32_t *h = hw + (size_t)s * (1 + K);
+        const int n = s < nslots ? (int)h[0] : 0;
+        if (s < nslots) s_nown[s] = n;
+        int cnt = 0;
+        if (n > 0)
+            for (int k = 0; k < K; ++k) cnt += (int)h[1 + k] >= 0;
+        int incl = cnt;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(KQ_FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int off = base + incl - cnt;
+        if (n > 0)
+            for (int k = 0; k < K; ++k)
+                if ((int)h[1 + k] >= 0) {
+                    pslot[off] = s;
+                    pid[off] = (int)h[1 + k];
+                    pw[off] = __int_as_float(k);
+                    ++off;
+                }
+        base += __shfl_sync(KQ_FULL, incl, 31);
+    }
+    if (lane == 0) *np = base;
+    __syncwarp();
+}
+// Expert-parallel pairs of the received slots (EP 1), in slot then k order (warp 0): a slot
+// header holds n_owned, t, pad[2], ids[K] (global expert id, or -1 when another rank owns
+// it), w[K]; slots with n_owned == 0 carry no pairs.
+__device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, int nslots, int K, int lane,
+                         int *pslot, int *pid, float *pw, int *np) {
     int base = 0;
     for (int s0 = 0; s0 < nslots; s0 += 32) {
         const int s = s0 + lane;
         int idv[MOE_MAX_K];
         float wv[MOE_MAX_K];
         bool live = false;
-        if (EP == 2 && s < nslots) {  // this rank's window: tagged words of call e
-            const uint64_t *slot = ep2_tslot(p, p.ep_rank, e, s / p.ep_tmax, s % p.ep_tmax);
-            const int n = (int)poll_tagged(slot, e, p.status);
-            live = n > 0;
-            if (live)
-#pragma unroll
-                for (int k = 0; k < MOE_MAX_K; ++k)
-                    if (k < K) {
-                        idv[k] = (int)poll_tagged(slot + EPT_IDS + k, e, p.status);
-                        wv[k] = __uint_as_float(poll_tagged(slot + EPT_W + k, e, p.status));
-                    }
-        } else if (EP != 2 && s < nslots) {  // every header word loaded before any is used
+        if (s < nslots) {  // every header word loaded before any is used
             const uint8_t *slot = recv + (size_t)s * p.ep_slot_bytes;
             const int *ids = reinterpret_cast<const int *>(slot + 16);
             const float *ws = reinterpret_cast<const float *>(slot + 16 + 4 * K);
@@ -288,18 +410,23 @@ __device__ void ep_pairs(const MoeParams &p, const uint8_t *recv, uint32_t e, in
     __syncwarp();
 }
 // A slot's sum for one row: in ep_ret (a run of the slot's pairs continues from it in the
-// next round) and, EP 2, once the sum is final, into the source rank's window as two tagged
-// words (the source takes the first value that carries the call number).
+// next round; EP 2 keeps only such partial sums there) and, EP 2, once the sum is final: into the source rank's window as two tagged
+// words (the source takes the first value that carries the call number), or, for a token of
+// this rank whose experts are all here (local), straight into y as the combine would.
 template <int EP>
 __device__ __forceinline__ void ep_store_t(const MoeParams &p, uint32_t e, int slot, int H, uint32_t row,
-                                           double v, bool final_sum) {
-    p.ep_ret[(size_t)slot * H + row] = v;
+                                           double v, bool final_sum, bool local) {
+    if (EP != 2 || !final_sum) p.ep_ret[(size_t)slot * H + row] = v;
     if (EP == 2 && final_sum) {  // tback[e & 1][this rank][t][row], slot = src * tmax + t
         const int src = slot / p.ep_tmax, t = slot % p.ep_tmax;
+        if (local) {
+            float *y = p.y + (size_t)t * H + row;
+            *y = p.accum ? __fadd_rn(*y, (float)v) : (float)v;
+            return;
+        }
         uint64_t *w = p.ep_peer_tback[src] +
                       ((((size_t)(e & 1u) * p.ep_ranks + p.ep_rank) * p.ep_tmax + t) * H + row) * 2;
-        st_tagged(w, (uint32_t)__double2hiint(v), e);
-        st_tagged(w + 1, (uint32_t)__double2loint(v), e);
+        st_tagged2(w, (uint32_t)__double2hiint(v), (uint32_t)__double2loint(v), e);
     }
 }
 
@@ -331,12 +458,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *s_h = s_w + MOE_MAX_K;                                   // MAX_ABLK * HB floats
     uint8_t *s_rec = reinterpret_cast<uint8_t *>(s_h + MAX_ABLK * HB);  // MAX_ABLK * REC_BYTES
     float *s_logits = reinterpret_cast<float *>(s_rec + MAX_ABLK * REC_BYTES);
-    // expert-parallel pairs: slot, expert, weight of each owned pair; the round's slots
+    // expert-parallel pairs: slot, expert, weight of each owned pair; their count; n_owned of
+    // each received slot; owner ranks of each of this rank's tokens
     int *s_pslot = reinterpret_cast<int *>(s_logits + p.n_experts);
     int *s_pid = s_pslot + MOE_EP_MAX_PAIRS;
     float *s_pw = reinterpret_cast<float *>(s_pid + MOE_EP_MAX_PAIRS);
-    int *s_slotr = reinterpret_cast<int *>(s_pw + MOE_EP_MAX_PAIRS);
-    int *s_np = s_slotr + MOE_MAX_K;
+    int *s_np = reinterpret_cast<int *>(s_pw + MOE_EP_MAX_PAIRS);
+    int *s_nown = s_np + 4;
+    uint32_t *s_own = reinterpret_cast<uint32_t *>(s_nown + MOE_EP_MAX_SLOTS);
 
     const uint32_t Q = (uint32_t)H / p.rg;  // phase-B row groups (16-byte aligned copies)
     const uint32_t q0 = Q * c / G, q1 = Q * (c + 1) / G;
@@ -374,28 +503,49 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     int *xs16 = xs32 + H / 32;
     float *xfs = reinterpret_cast<float *>(act + 4 * H);  // fp32 mode: per-32 sums
     int npairs = K, nrounds = 1;
-    int nbar = 0;  // grid barriers passed
+    int nbar = 0;        // grid barriers passed
+    uint32_t sbase = 0;  // thread 0: the barrier counter at launch (sync_base)
     const uint8_t *ep_recv = p.ep_recv;
     int ep_nslots = (int)p.ep_slots;
     uint32_t ep_e = 0;
     if constexpr (EP == 2) {
         pdl_wait();
+        if (tid == 0) sbase = sync_base(p);
         ep_e = *p.ep_epoch + 1;
         ep_nslots = p.ep_ranks * p.ep_tmax;  // slot s = source rank * tmax + token
         ep2_dispatch(p, ep_e, K, H, s_logits, s_ids, s_w, act);
         if (c < (uint32_t)p.ep_tmax) trace(p, 1);
-        __syncthreads();  // s_ids / s_w / act reused below
-    }
-    if constexpr (EP != 0) {
+        // the expert pointer table, then every header word of the call in parallel, and the
+        // owner ranks of this rank's tokens from the routing record (for the combine)
+        const int npair = (3 * p.n_experts + 1) / 2;  // 2 pointers per 16 B
+        for (int i = tid; i < npair; i += MOE_THREADS)
+            reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
+        if (tid < MOE_EP_MAX_SLOTS) s_own[tid] = 0u;
+        __syncthreads();  // the dispatch's staging in act is free again
+        uint32_t *hw = reinterpret_cast<uint32_t *>(act);
+        ep2_headers(p, ep_e, ep_nslots, K, hw);
+        {
+            const uint64_t *route_rec = reinterpret_cast<const uint64_t *>(p.ep_src_ids);
+            const int per = p.n_experts / p.ep_ranks;
+            for (int i = tid; i < p.ep_tokens * K; i += MOE_THREADS)
+                atomicOr(&s_own[i / K], 1u << ((int)poll_tagged(route_rec + i, ep_e, p.status) / per));
+        }
+        __syncthreads();
+        if (warp == 0) ep2_pairs(hw, ep_nslots, K, lane, s_pslot, s_pid, s_pw, s_np, s_nown);
+        __syncthreads();
+    } else if constexpr (EP == 1) {
         pdl_wait();
+        if (tid == 0) sbase = sync_base(p);
         if (warp == 0) {
-            ep_pairs<EP>(p, ep_recv, ep_e, ep_nslots, K, lane, s_pslot, s_pid, s_pw, s_np);
+            ep_pairs(p, ep_recv, ep_nslots, K, lane, s_pslot, s_pid, s_pw, s_np);
         } else {
             const int npair = (3 * p.n_experts + 1) / 2;  // expert pointer table, 2 per 16 B
             for (int i = tid - 32; i < npair; i += MOE_THREADS - 32)
                 reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
         }
         __syncthreads();
+    }
+    if constexpr (EP != 0) {
         npairs = *s_np;
         nrounds = (npairs + K - 1) / K;
         trace(p, 11);
@@ -418,6 +568,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         const float4 nw = xl ? __ldg(reinterpret_cast<const float4 *>(p.rt_norm) + tid)
                              : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         pdl_wait();
+        if (tid == 0) sbase = sync_base(p);
         double *red = reinterpret_cast<double *>(s_h);  // MOE_WARPS doubles, free until phase A
         auto block_sum = [&](double v) {
             v = warp_sum_d(v);
@@ -453,7 +604,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 if (tid == 0) const_cast<float *>(p.logits)[r0 + i] = (float)d;
             }
         }
-        grid_barrier(p, nbar);  // every CTA's logits published
+        grid_barrier(p, nbar, sbase);  // every CTA's logits published
         if (warp == 0) {
             if (route_in_regs) route_regs<RT>(p, p.logits, lane, s_ids, s_w, false, route_lv);
             else route<RT>(p, p.logits, s_logits, s_ids, s_w, lane, false);  // weights after the copies are issued
@@ -461,6 +612,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     } else if (warp == 0) {
         pdl_wait();  // under a programmatic launch: x, logits / ids, scratch only after this
+        if (lane == 0) sbase = sync_base(p);
         if (p.ids) {
             if (lane < K) {
                 s_ids[lane] = p.ids[lane];
@@ -486,11 +638,93 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     if constexpr (!EP) __syncthreads();
     trace(p, 2);
 
+    // Expert-parallel rounds overlap when the decoded down rows have their own area: round
+    // rd + 1's gate/up rows are requested (and its x rows staged) once round rd's phase A is
+    // done, its down rows once round rd's rows are decoded.
+    const bool pipe = EP && MODE == 0 && DT == T_Q6_K && p.dec_enabled && p.dec_off != 0 && nrB != 0;
+    const uint32_t per = nrB * rbd;  // down-row bytes of one expert for this CTA
+    // Request round r's bytes (warp 0, one copy per lane): gate/up chunks (what & 1), then
+    // each selected expert's down rows on its own barrier (what & 2), decoded as they arrive.
+    // One warp keeps that order (copies issued from every warp interleave and delay the
+    // first gate/up chunk).
+    auto issue_round = [&](int r, int what) {
+        const int KRr = EP ? min(K, npairs - r * K) : K;
+        const int32_t *rids = EP ? s_pid + r * K : s_ids;
+        const uint32_t BAr = (uint32_t)KRr * F / HB, b0r = BAr * c / G;
+        const int nchunk = (int)(BAr * (c + 1) / G - b0r) * NCH;
+        if ((what & 1) && lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
+        if ((what & 2) && nrB && lane < KRr) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
+        __syncwarp();
+        const uint64_t pol = l2_evict_first_policy();
+        const int q0 = (what & 1) ? 0 : 2 * nchunk;
+        const int ncopy = (what & 2) ? 2 * nchunk + (nrB ? KRr : 0) : 2 * nchunk;
+        for (int q = q0 + lane; q < ncopy; q += 32) {
+            if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
+                const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
+                const uint32_t blk = b0r + a;
+                const int k = (int)(blk / (F / HB));
+                const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
+                const uint32_t rb = up ? rbu : rbg;
+                const uint8_t *base = s_tab[3 * rids[k] + up];
+                const uint8_t *src = base ? base + (size_t)j0 * rb : nullptr;
+                uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
+                bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol, p.status);
+            } else {  // down rows [rB0, rB0 + nrB) of selected expert k
+                const int k = q - 2 * nchunk;
+                const uint8_t *base = s_tab[3 * rids[k] + 2];
+                bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
+                               per, &bars[DBAR + k], pol, p.status);
+            }
+        }
+    };
+    // x of round r's phase-A block of this CTA (warps 1..15): its pair's token, from the
+    // slot's q8_1 row (EP 2: tagged words in this rank's window; EP 1: the received bytes)
+    auto stage_x = [&](int r) {
+        const int KRr = min(K, npairs - r * K);
+        const uint32_t BAr = (uint32_t)KRr * F / HB, b0r = BAr * c / G;
+        if (BAr * (c + 1) / G == b0r) return;  // no phase-A block
+        const int sl = s_pslot[r * K + (int)(b0r / (F / HB))];
+        if constexpr (EP == 2) {
+            ep2_stage_x(p, ep_e, H, sl, reinterpret_cast<uint32_t *>(act), xq, xd, xs32, xs16);
+        } else {
+            const uint8_t *row = ep_recv + (size_t)sl * p.ep_slot_bytes + p.ep_hdr_bytes;
+            for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
+                const uint8_t *blk = row + 36 * g;
+                const int qi = (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
+                const int sum = __reduce_add_sync(KQ_FULL, qi);
+                const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
+                xq[32 * g + lane] = (int8_t)qi;
+                if (lane == 0) {
+                    xd[g] = h2f(__ldcg(reinterpret_cast<const unsigned short *>(blk)));
+                    xs32[g] = sum;
+                    xs16[2 * g] = sum_lo;
+                    xs16[2 * g + 1] = sum - sum_lo;
+                }
+            }
+        }
+    };
+
+    // EP 2: after the call's last grid barrier no CTA reads this rank's window of the call any
+    // more; CTA 0 then writes this rank's done word into every rank's window (a rank with no
+    // pairs passes one barrier for it)
+    auto ep2_done = [&]() {
+        if (EP == 2 && c == 0 && tid < p.ep_ranks)
+            st_tagged(p.ep_peer_tdone[tid] + (size_t)(ep_e & 1u) * p.ep_ranks + p.ep_rank, 1u, ep_e);
+    };
+    if (EP == 2 && nrounds == 0) {
+        grid_barrier(p, nbar, sbase);
+        ep2_done();
+    }
+    // a slot of this rank whose token's experts are all here: its sum goes straight to y
+    auto local_slot = [&](int sl) { return EP == 2 && sl / p.ep_tmax == p.ep_rank && s_nown[sl] == K; };
+
     for (int rd = 0; rd < nrounds; ++rd) {
     // pairs of this round: K (one token's experts), or expert-parallel pairs [rd K, rd K + KR)
     const int KR = EP ? min(K, npairs - rd * K) : K;
+    const float *rw = EP ? s_pw + rd * K : s_w;  // the round's weights
+    const int *rslot = s_pslot + rd * K;         // and slots (EP)
     if constexpr (EP) {
-        if (rd > 0) {  // every wait of the previous round has returned: re-arm the barriers
+        if (rd > 0 && !pipe) {  // every wait of the previous round has returned: re-arm the barriers
             __syncthreads();
             if (tid == 32) {
                 for (int i = 0; i < NBARS; ++i) {
@@ -499,94 +733,39 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 }
                 fence_mbar_init();
             }
+            __syncthreads();
         }
-        if (tid < KR) {
-            s_ids[tid] = s_pid[rd * K + tid];
-            s_w[tid] = s_pw[rd * K + tid];
-            s_slotr[tid] = s_pslot[rd * K + tid];
-        }
-        __syncthreads();
     }
     const uint32_t BA = (uint32_t)KR * F / HB;  // phase-A blocks of this round
     const uint32_t b0 = BA * c / G, b1 = BA * (c + 1) / G;  // 32-bit: BA * G < 2^32
     const int nbA = (int)(b1 - b0);
     const uint32_t hb0 = EP ? (uint32_t)(rd * K) * (F / HB) : 0u;  // first h record of the round
 
-    // ---- 2. request every expert byte this CTA needs (warp 0, one copy per lane) ----
-    // Copy q: gate/up rows first (phase A waits for them), then each selected expert's
-    // down rows on its own barrier, decoded as they arrive. One warp keeps that order
-    // (copies issued from every warp interleave and delay the first gate/up chunk).
-    const int nchunk = nbA * NCH;
-    const uint32_t per = nrB * rbd;
-    const int ncopy = 2 * nchunk + (nrB ? KR : 0);
-    auto issue = [&](int q) {
-        const uint64_t pol = l2_evict_first_policy();
-        if (q < 2 * nchunk) {  // gate (even) or up (odd) rows of one chunk
-            const int ci = q >> 1, a = ci / NCH, ch = ci % NCH, up = q & 1;
-            const uint32_t blk = b0 + a;
-            const int k = (int)(blk / (F / HB));
-            const uint32_t j0 = (blk % (F / HB)) * HB + ch * HCH;
-            const uint32_t rb = up ? rbu : rbg;
-            const uint8_t *base = s_tab[3 * s_ids[k] + up];
-            const uint8_t *src = base ? base + (size_t)j0 * rb : nullptr;
-            uint8_t *dst = sa + (size_t)a * blk_bytes + (up ? HB * rbg : 0) + ch * HCH * rb;
-            bulk_g2s_split(dst, src, HCH * rb, &bars[ci], pol, p.status);
-        } else {  // down rows [rB0, rB0 + nrB) of selected expert k
-            const int k = q - 2 * nchunk;
-            const uint8_t *base = s_tab[3 * s_ids[k] + 2];
-            bulk_g2s_split(sb + (size_t)k * (per + 16), base ? base + (size_t)rB0 * rbd : nullptr,
-                           per, &bars[DBAR + k], pol, p.status);
-        }
-    };
-    if (warp == 0) {
-        if (lane < nchunk) mbar_arrive_expect_tx(&bars[lane], HCH * (rbg + rbu));
-        if (nrB && lane < KR) mbar_arrive_expect_tx(&bars[DBAR + lane], per);
-        __syncwarp();
-        for (int q = lane; q < ncopy; q += 32) issue(q);
-        trace(p, 3);
-        if (!EP && !p.ids) {
-            if (route_in_regs) route_weights_regs(p, lane, route_lv, s_ids, s_w);
-            else route_weights<RT>(p, p.logits, nullptr, 0, lane, s_ids, s_w);
-        }
-    } else if (EP) {
-        // x of this CTA's phase-A block: its pair's token, from the slot's q8_1 row
-        if (nbA > 0) {
-            const int kb = (int)(b0 / (F / HB));
-            const int sl = s_slotr[kb];
-            // EP 2: the row's tagged words in this rank's window (9 per block: d | sum, then
-            // 32 int8 four to a word); EP 1: the received bytes
-            const uint64_t *trow = EP == 2 ? ep2_tslot(p, p.ep_rank, ep_e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_ROW
-                                           : nullptr;
-            const uint8_t *row = EP == 2 ? nullptr : ep_recv + (size_t)sl * p.ep_slot_bytes + p.ep_hdr_bytes;
+    // ---- 2. request every expert byte this CTA needs; stage x ---------------------------
+    if (!(pipe && rd > 0)) {  // (an overlapped round's bytes were requested in the previous one)
+        if (warp == 0) {
+            issue_round(rd, 3);
+            trace(p, 3);
+            if (!EP && !p.ids) {
+                if (route_in_regs) route_weights_regs(p, lane, route_lv, s_ids, s_w);
+                else route_weights<RT>(p, p.logits, nullptr, 0, lane, s_ids, s_w);
+            }
+        } else if (EP) {
+            stage_x(rd);
+        } else if (warp > 0) {
             for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
-                const uint8_t *blk = EP == 2 ? nullptr : row + 36 * g;
-                const int qi = EP == 2
-                    ? (int)(signed char)(poll_tagged(trow + 9 * g + 1 + (lane >> 2), ep_e, p.status) >> (8 * (lane & 3)))
-                    : (int)__ldcg(reinterpret_cast<const signed char *>(blk) + 4 + lane);
-                const int sum = __reduce_add_sync(KQ_FULL, qi);
-                const int sum_lo = __reduce_add_sync(KQ_FULL, lane < 16 ? qi : 0);
-                xq[32 * g + lane] = (int8_t)qi;
-                if (lane == 0) {
-                    xd[g] = h2f(EP == 2 ? poll_tagged(trow + 9 * g, ep_e, p.status) & 0xFFFFu
-                                        : __ldcg(reinterpret_cast<const unsigned short *>(blk)));
-                    xs32[g] = sum;
-                    xs16[2 * g] = sum_lo;
-                    xs16[2 * g + 1] = sum - sum_lo;
+                const float v = xf[32 * g + lane];
+                if (MODE == 0) {
+                    quant_block_q8(v, lane, xq + 32 * g, xd + g, xs32 + g, xs16 + 2 * g, nullptr);
+                } else {
+                    const float s = warp_sum_f(v);
+                    if (lane == 0) xfs[g] = s;
                 }
             }
         }
-    } else if (warp > 0) {
-        for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
-            const float v = xf[32 * g + lane];
-            if (MODE == 0) {
-                quant_block_q8(v, lane, xq + 32 * g, xd + g, xs32 + g, xs16 + 2 * g, nullptr);
-            } else {
-                const float s = warp_sum_f(v);
-                if (lane == 0) xfs[g] = s;
-            }
-        }
+        __syncthreads();
     }
-    __syncthreads();
+    if (EP) trace(p, 21);
 
     // ---- 3. phase A: gate/up row pairs -> h = silu(g) * u, quantised per block --
     bool ok = true;
@@ -663,6 +842,25 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     // The CTA barrier orders every thread's h stores before thread 0's release.
     __syncthreads();
     if (tid == 0) red_release_gpu_add(&p.sync[0], 1u);
+    // Overlap: round rd + 1's gate/up rows into the phase-A staging (every read of it is done:
+    // the decoded rows have their own area) and its x rows into the activation area.
+    const bool pre = pipe && rd + 1 < nrounds;
+    if (pre) {
+        if (warp == 0) {
+            if (lane == 0) {
+                for (int i = 0; i < DBAR; ++i) {
+                    mbar_inval(&bars[i]);
+                    mbar_init(&bars[i], 1);
+                }
+                fence_mbar_init();
+            }
+            __syncwarp();
+            issue_round(rd + 1, 1);
+            trace(p, 23);
+        } else {
+            stage_x(rd + 1);
+        }
+    }
     const bool predecode = MODE == 0 && DT == T_Q6_K && p.dec_enabled && nrB != 0;
     // Phase B's expert-major path (F a power of two from 256 to 2048) reads h and the
     // decoded down rows in chunk-major order; the row-major path in element order.
@@ -695,19 +893,30 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     }
     trace(p, 14);
-    if (tid == 0) {
-        uint32_t it = 0;
-        while (ld_acquire_gpu(&p.sync[0]) < (uint32_t)(nbar + 1) * G) {
-            if (++it > SPIN_LIMIT) {
-                *p.status |= ERR_TIMEOUT_GRID;
-                break;
-            }
-            if (it > 32) __nanosleep(20);
-        }
-    }
+    if (tid == 0) grid_wait(p, sbase + (uint32_t)(nbar + 1) * G);
     ++nbar;
     __syncthreads();
     trace(p, 6);
+    if constexpr (EP == 2) {
+        if (rd == nrounds - 1) ep2_done();
+        // the round's weights: the sources store them after the ids, so they are read only now
+        if (warp == 1 && lane < KR) {
+            const int i = rd * K + lane, sl = s_pslot[i], k = __float_as_int(s_pw[i]);
+            const uint64_t *wa = ep2_tslot(p, p.ep_rank, ep_e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_W + k;
+            s_pw[i] = __uint_as_float(poll_tagged(wa, ep_e, p.status));
+        }
+    }
+    if (pre && warp == 0) {  // round rd + 1's down rows: every thread has decoded round rd's
+        if (lane == 0) {
+            for (int i = DBAR; i < NBARS; ++i) {
+                mbar_inval(&bars[i]);
+                mbar_init(&bars[i], 1);
+            }
+            fence_mbar_init();
+        }
+        __syncwarp();
+        issue_round(rd + 1, 2);
+    }
 
     // ---- 5. load h for phase B ------------------------------------------------
     int8_t *hq = reinterpret_cast<int8_t *>(hact);  // expert stride F + 16 (bank spread)
@@ -811,21 +1020,23 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                     int cur = -1;
                     double acc = 0.0;
                     for (int kk = 0; kk < KR; ++kk) {
-                        const int sl = s_slotr[kk];
+                        const int sl = rslot[kk];
                         if (sl != cur) {  // the previous slot's run ends here: its sum is final
-                            if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, true);
+                            if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, true, local_slot(cur));
                             const bool cont = kk == 0 && rd > 0 && s_pslot[rd * K - 1] == sl;
                             acc = cont ? p.ep_ret[(size_t)sl * H + rB0 + r] : 0.0;
                             cur = sl;
                         }
-                        acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
+                        acc += (double)rw[kk] * (double)s_dot[(size_t)kk * nrB + r];
                     }
                     // final unless the slot's run continues in the next round
                     const int nx = rd * K + KR;
-                    if (cur >= 0) ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, nx >= npairs || s_pslot[nx] != cur);
+                    if (cur >= 0)
+                        ep_store_t<EP>(p, ep_e, cur, H, rB0 + r, acc, nx >= npairs || s_pslot[nx] != cur,
+                                       local_slot(cur));
                 } else {
                     double acc = 0.0;
-                    for (int kk = 0; kk < K; ++kk) acc += (double)s_w[kk] * (double)s_dot[(size_t)kk * nrB + r];
+                    for (int kk = 0; kk < K; ++kk) acc += (double)rw[kk] * (double)s_dot[(size_t)kk * nrB + r];
                     p.y[rB0 + r] = p.accum ? __fadd_rn(p.y[rB0 + r], (float)acc) : (float)acc;
                 }
             }
@@ -839,7 +1050,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             const uint32_t per = nrB * rbd;
             const ActQ8 ah{hq + (size_t)k * (F + 16), hd + (size_t)k * F / 32,
                            hs32 + (size_t)k * F / 32, hs16 + (size_t)k * F / 16, 0};
-            const double wk = k < K ? (double)s_w[k] : 0.0;
+            const double wk = k < KR ? (double)rw[k] : 0.0;
             for (uint32_t rr = warp; rr < nrB; rr += MOE_WARPS) {
                 double part = 0.0;
                 if (k < K) {
@@ -863,41 +1074,28 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             }
         }
     }
+    if (EP && rd == 0) trace(p, 22);
     }  // rounds
     if constexpr (EP == 2) {
-        // no CTA reads this rank's window of call e any more: the last one to count itself
-        // writes this rank's done word into every rank's window
-        __syncthreads();
-        if (tid == 0) {
-            const uint32_t prev = atomicAdd(&p.ep_done[1], 1u);
-            if (prev == G - 1) {
-                p.ep_done[1] = 0u;
-                for (int d = 0; d < p.ep_ranks; ++d)
-                    st_tagged(p.ep_peer_tdone[d] + (size_t)(ep_e & 1u) * p.ep_ranks + p.ep_rank, 1u, ep_e);
-            }
-        }
-        trace(p, 2);
-        ep2_combine(p, ep_e, K, H);
+        trace(p, 18);
+        ep2_combine(p, ep_e, H, s_own);
         trace(p, 19);
     }
     trace(p, 8);
 
-    // ---- 7. the last CTA out re-arms the barrier counters --------------------
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.sync[1], 1u);
-        if (prev == G - 1) {
-            atomicExch(&p.sync[0], 0u);
-            atomicExch(&p.sync[1], 0u);
-            if (EP == 2) {
-                // every rank has finished reading its window of call e, so call e + 2 may
-                // rewrite this parity; the next call uses the other one
-                for (int d = 0; d < p.ep_ranks; ++d)
-                    poll_tagged(p.ep_peer_tdone[p.ep_rank] + (size_t)(ep_e & 1u) * p.ep_ranks + d, ep_e, p.status);
-                __threadfence();
-                *p.ep_epoch = ep_e;
-            }
+    // ---- 7. CTA 0 leaves the barrier counter's value for the next launch; EP 2: it waits for
+    // every rank's done word of this call (no rank reads its window of the call any more, so
+    // call e + 2 may rewrite this parity) and advances the call number
+    if (c == 0 && warp == 0) {
+        if constexpr (EP == 2) {
+            if (lane < p.ep_ranks)
+                poll_tagged(p.ep_peer_tdone[p.ep_rank] + (size_t)(ep_e & 1u) * p.ep_ranks + lane, ep_e, p.status);
+            __syncwarp();
+            if (lane == 0) *p.ep_epoch = ep_e;
         }
+        if (lane == 0 && nbar > 0)
+            asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p.sync + 3), "r"(sbase + (uint32_t)nbar * G)
+                         : "memory");
     }
 }
 
@@ -928,16 +1126,18 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     p.misc_off = al128(p.hact_off + hact);
     const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * BAR_SLOTS +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
-                          4 * (uint32_t)p.n_experts + 12 * MOE_EP_MAX_PAIRS + 4 * MOE_MAX_K + 16;
+                          4 * (uint32_t)p.n_experts + 12 * MOE_EP_MAX_PAIRS + 16 + 8 * MOE_EP_MAX_SLOTS + 16;
     p.sdot_off = al128(p.misc_off + misc);
     p.smem_bytes = al128(p.sdot_off + 4 * (uint32_t)p.K * rg * qpc);
     // Decoded int8 down rows (Q6_K, q8_1 mode): reuse the phase-A staging area
     // when it is large enough (phase A is finished by then), else append.
     p.dec_off = 0;
     p.dec_enabled = 0;
+    p.dec_bytes = 0;
     p.dec_row_bytes = (uint32_t)((p.F + p.F / 16 + 4 * (p.F / 256) + 15) & ~15);
     if (p.mode == 0 && p.down_type == T_Q6_K) {
         const uint32_t need = (uint32_t)p.K * (rg * qpc * p.dec_row_bytes + 16);
+        p.dec_bytes = need;
         if (need <= p.sa_bytes) {
             p.dec_off = 0;  // the phase-A staging area
             p.dec_enabled = 1;
@@ -948,6 +1148,14 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
         }
     }
     return p.smem_bytes <= (uint32_t)max_smem ? 0 : -1;
+}
+
+int moe_plan_dec_apart(MoeParams &p, int max_smem) {
+    if (!p.dec_enabled || p.dec_off != 0) return p.dec_enabled && p.dec_off != 0;
+    if (al128(p.smem_bytes) + p.dec_bytes > (uint32_t)max_smem) return 0;
+    p.dec_off = al128(p.smem_bytes);
+    p.smem_bytes = al128(p.dec_off + p.dec_bytes);
+    return 1;
 }
 
 template <int MODE, uint32_t DT, int SHAPE, int EP = 0, int RT = 0>

@@ -45,7 +45,7 @@ int fail_cuda(const char *what, cudaError_t e) {
 
 constexpr size_t TABLE_BYTES = 3u * KATALI_MOE_STATIC_MAX_EXPERTS * sizeof(void *) + 256;
 constexpr size_t H_BYTES = (size_t)KATALI_MOE_STATIC_MAX_TOPK_FFN * sizeof(float);
-constexpr size_t SYNC_OFF = TABLE_BYTES + H_BYTES;  // 2 barrier counters + status word
+constexpr size_t SYNC_OFF = TABLE_BYTES + H_BYTES;  // barrier counter, unused, status word, counter base
 constexpr size_t SCRATCH_BYTES = SYNC_OFF + 256;
 
 static __device__ __align__(256) unsigned char g_moe_scratch[SCRATCH_BYTES];
