@@ -439,7 +439,7 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
-TRACE_SLOTS = 24  # per CTA, as the plugin writes them
+TRACE_SLOTS = 32  # per CTA, as the plugin writes them
 TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first chunk in",
                5: "gate/up done", 6: "barrier passed", 7: "phase B start", 8: "end",
                9: "route: logits in", 10: "route: sorted", 11: "route: top-k done",
@@ -449,7 +449,10 @@ TRACE_NAMES = {1: "routed", 2: "x/table staged", 3: "loads issued", 4: "first ch
 
 EP_TRACE_NAMES = {**TRACE_NAMES, 1: "slots stored", 11: "pairs received", 18: "rounds done",
                   19: "combine done", 20: "dispatch: routed", 21: "x rows staged",
-                  22: "round 0 done", 23: "next round requested"}
+                  22: "round 0 done", 23: "next round requested", 24: "round 0: first chunk in",
+                  25: "round 0: gate/up done", 26: "round 0: barrier passed",
+                  27: "round 0: phase B start", 28: "dispatch: ids stored",
+                  29: "dispatch: weights formed", 30: "dispatch: weights stored"}
 
 
 def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False, call=None, names=TRACE_NAMES,

@@ -446,11 +446,11 @@ int katali_cuda_debug_row_isums(uint32_t type, const void *w, uint64_t rows,
                                 uint64_t cols, const void *xq, int32_t *isum,
                                 int32_t *xsum);
 /* Phase timeline of subsequent katali_cuda_moe_layer calls: when trace is a
- * device buffer of (*grid) * 24 uint64, every CTA writes %globaltimer (ns) at
+ * device buffer of (*grid) * 32 uint64, every CTA writes %globaltimer (ns) at
  * start, routed, x staged, loads issued, first gate/up chunk landed, gate/up
  * done, barrier passed, down rows landed, end (slots 0-8), phase details in
- * slots 9-15 and 18-23 (the expert-parallel layer's exchange steps), and the
- * SM cycle counter at start and end (slots 16, 17).
+ * slots 9-15 and 18-31 (the expert-parallel layer's exchange steps and its
+ * first round), and the SM cycle counter at start and end (slots 16, 17).
  * NULL switches tracing off. *grid receives the launch's CTA count. */
 int katali_cuda_debug_moe_trace(KataliMoe *m, uint64_t *trace, int *grid);
 /* The MoE kernel's routing decision for router_logits: ids/w of top_k. */

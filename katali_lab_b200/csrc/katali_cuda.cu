@@ -161,8 +161,10 @@ struct KataliMoe {
     // Ragged-batch scratch, grown on demand (katali_cuda_moe_batch, the EP stages).
     unsigned char *bscratch;
     size_t bscratch_bytes;
-    int32_t *ep_src_ids;  // routing of the last dispatch (8 bytes per id: tagged in the fused layer)
+    int32_t *ep_src_ids;  // routing of the last katali_cuda_moe_ep_dispatch
     uint32_t ep_src_cap;  // tokens
+    uint64_t *ep_route;   // the single-launch layer's tagged routing record (zeroed when made)
+    uint32_t ep_route_cap;
     KataliExpertCache *cache;  // the residency cache this layer's experts are bound to
 };
 
@@ -514,6 +516,7 @@ int katali_cuda_moe_destroy(KataliMoe *m) {
     cudaFree(m->dbg_w);
     cudaFree(m->bscratch);
     cudaFree(m->ep_src_ids);
+    cudaFree(m->ep_route);
     delete m;
     return KATALI_OK;
 }
@@ -701,7 +704,7 @@ int moe_ep_dispatch(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uint32_
         if (e != cudaSuccess) return cuda_fail(e);
         cudaFree(m->ep_src_ids);
         m->ep_src_cap = 0;
-        e = cudaMalloc((void **)&m->ep_src_ids, 8ull * K * max_tokens);  // tagged in the fused layer
+        e = cudaMalloc((void **)&m->ep_src_ids, 4ull * K * max_tokens);
         if (e != cudaSuccess) {
             m->ep_src_ids = nullptr;
             return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
@@ -773,17 +776,20 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
     if (n_tokens > max_tokens) return KATALI_ERR_BAD_ARG;
     if (n_tokens && (!x || !router_logits || !y || !aligned16(x))) return KATALI_ERR_BAD_ARG;
     const uint32_t K = (uint32_t)m->plan[0].K;
-    if (max_tokens > m->ep_src_cap) {
+    if (max_tokens > m->ep_route_cap) {
+        // Zeroed: a word of it counts only once it carries the current call number (>= 1).
         cudaError_t e = cudaStreamSynchronize(g_stream);
         if (e != cudaSuccess) return cuda_fail(e);
-        cudaFree(m->ep_src_ids);
-        m->ep_src_cap = 0;
-        e = cudaMalloc((void **)&m->ep_src_ids, 8ull * K * max_tokens);  // tagged in the fused layer
+        cudaFree(m->ep_route);
+        m->ep_route_cap = 0;
+        e = cudaMalloc((void **)&m->ep_route, 8ull * K * max_tokens);
+        if (e == cudaSuccess) e = cudaMemsetAsync(m->ep_route, 0, 8ull * K * max_tokens, g_stream);
         if (e != cudaSuccess) {
-            m->ep_src_ids = nullptr;
+            cudaFree(m->ep_route);
+            m->ep_route = nullptr;
             return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : cuda_fail(e);
         }
-        m->ep_src_cap = max_tokens;
+        m->ep_route_cap = max_tokens;
     }
     kq::MoeParams p = m->plan[KATALI_MOE_Q8_1];
     kq::moe_plan_dec_apart(p, g_max_smem);  // rounds overlap when shared memory allows
@@ -809,7 +815,7 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
     p.ep_ranks = (int)n_ranks;
     p.ep_tmax = (int)max_tokens;
     p.ep_tokens = (int)n_tokens;
-    p.ep_src_ids = m->ep_src_ids;
+    p.ep_route_rec = m->ep_route;
     p.ep_peer_recv = pp->recv;
     p.ep_peer_back = pp->back;
     p.ep_peer_flags = pp->flags;

@@ -109,8 +109,8 @@ constexpr int MOE_EP_MAX_SLOTS = 16;
 constexpr int MOE_EP_MAX_PAIRS = MOE_EP_MAX_SLOTS * MOE_MAX_K;
 constexpr int MOE_MAX_CHUNKS = 64;
 constexpr int MOE_RT_ROWS = 4;   // router rows per CTA when the router is folded into the launch
-// Per CTA when tracing: %globaltimer slots 0-15 and 18-23, clock64 at start and end in 16, 17.
-constexpr int TRACE_SLOTS = 24;
+// Per CTA when tracing: %globaltimer slots 0-15 and 18-31, clock64 at start and end in 16, 17.
+constexpr int TRACE_SLOTS = 32;
 
 struct MoeParams {
     const uint8_t *const *experts;  // device table: gate_e, up_e, down_e per expert
@@ -159,7 +159,7 @@ struct MoeParams {
     // ep_slots are then derived on the device (this rank's window of the call's parity)
     // and ep_ret is local scratch for the per-slot sums. Windows as in EpPeer.
     int ep_rank, ep_ranks, ep_tmax, ep_tokens;
-    int32_t *ep_src_ids;
+    uint64_t *ep_route_rec;  // [tmax][K] this rank's routing, tagged words (read by the combine)
     uint8_t *const *ep_peer_recv;
     double *const *ep_peer_back;
     uint32_t *const *ep_peer_flags;

@@ -203,7 +203,7 @@ __device__ void ep2_dispatch(const MoeParams &p, uint32_t e, int K, int H, float
                              int32_t *s_ids, float *s_w, uint8_t *blkbuf) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = p.ep_ranks, me = p.ep_rank, tmax = p.ep_tmax, per = p.n_experts / G;
-    uint64_t *route_rec = reinterpret_cast<uint64_t *>(p.ep_src_ids);  // [tmax][K] tagged ids
+    uint64_t *route_rec = p.ep_route_rec;
     if (warp == 0) {
         for (int t = blockIdx.x; t < tmax; t += gridDim.x) {
             const bool live = t < p.ep_tokens;
@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         uint32_t *hw = reinterpret_cast<uint32_t *>(act);
         ep2_headers(p, ep_e, ep_nslots, K, hw);
         {
-            const uint64_t *route_rec = reinterpret_cast<const uint64_t *>(p.ep_src_ids);
+            const uint64_t *route_rec = p.ep_route_rec;
             const int per = p.n_experts / p.ep_ranks;
             for (int i = tid; i < p.ep_tokens * K; i += MOE_THREADS)
                 atomicOr(&s_own[i / K], 1u << ((int)poll_tagged(route_rec + i, ep_e, p.status) / per));
@@ -782,7 +782,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         double pg0, pu0, pg1, pu1;
         // pair p0 (first chunk) is computed while the second chunk is still arriving
         ok &= mbar_wait_warp(&bars[a * NCH + p0 / HCH], 0);
-        if (a == 0) trace(p, 4);
+        if (a == 0) {
+            trace(p, 4);
+            if (EP && rd == 0) trace(p, 24);
+        }
         if (MODE == 0 && nbh == 8) {
             pg0 = q4k_q8_unit_r(g0, lane, xr);
             pu0 = q4k_q8_unit_r(u0, lane, xr);
@@ -819,6 +822,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     }
     if (!ok && lane == 0) *p.status |= ERR_TIMEOUT_TMA;
     trace(p, 5);
+    if (EP && rd == 0) trace(p, 25);
     __syncthreads();
     if (warp < nbA) {  // one warp per block: publish h as a q8_1 record (fp32 in mode 1)
         const int a = warp;
@@ -897,6 +901,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     ++nbar;
     __syncthreads();
     trace(p, 6);
+    if (EP && rd == 0) trace(p, 26);
     if constexpr (EP == 2) {
         if (rd == nrounds - 1) ep2_done();
         // the round's weights: the sources store them after the ids, so they are read only now
@@ -963,6 +968,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             if (lane == 0) *p.status |= ERR_TIMEOUT_TMA;
         } else if (xmaj) {
             trace(p, 7);
+            if (EP && rd == 0) trace(p, 27);
             // Expert-major: warp -> (expert k, row subset); lane -> (row slot, 64-element
             // unit u). The lane keeps unit u of expert k's h in registers and dots it
             // with the same unit of several rows; dots meet in shared memory and the
@@ -1042,6 +1048,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             }
         } else {
             trace(p, 7);
+            if (EP && rd == 0) trace(p, 27);
             // lanes per expert: 32 / next_pow2(K); lane = (expert k, slot g)
             int kp2 = 1;
             while (kp2 < K) kp2 <<= 1;

@@ -276,7 +276,7 @@ class MoeLayer:
         self.p.check(self.p.L.katali_cuda_debug_route(self.h, _ptr(logits), _ptr(ids), _ptr(w)))
 
     def set_trace(self, buf) -> int:
-        """Record per-CTA phase timestamps into `buf` (uint64 CUDA tensor, >= grid*24
+        """Record per-CTA phase timestamps into `buf` (uint64 CUDA tensor, >= grid*32
         entries, zeroed) on later calls; None switches it off. Returns the grid size."""
         g = _i32()
         self.p.check(self.p.L.katali_cuda_debug_moe_trace(self.h, _ptr(buf), C.byref(g)))
