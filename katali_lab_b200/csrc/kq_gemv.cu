@@ -375,15 +375,21 @@ namespace kq {
 static int num_sms() { return device_sms(); }
 
 cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
-    // Rows per tile: ~16 KB stages; Q6_K tiles in row multiples that keep every
-    // stage start 16-byte aligned.
+    // Rows per tile: ~16 KB stages, ~48 KB for launches that stream GEMV_BIG_BYTES or more
+    // (every consumer warp passes through every tile of its CTA, so fewer, larger tiles cost
+    // less per row: 2.9 -> 3.6 TB/s on a 113 MB Q4_K matrix with q8_1 activations); Q6_K
+    // tiles in row multiples that keep every stage start 16-byte aligned.
+    uint64_t bytes = 0;
+    for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
+    const bool big = bytes >= GEMV_BIG_BYTES;
+    const uint32_t tile_bytes = big ? 49152u : 16384u;
     uint32_t stage = 0;
     uint32_t tiles = 0;
     for (int j = 0; j < p.njobs; ++j) {
         GemvJob &J = p.job[j];
         uint32_t m = 16;
         for (uint32_t g = J.rb; g % 2 == 0 && m > 1; g /= 2) m /= 2;  // 16 / gcd(rb, 16)
-        uint32_t tr = J.rb >= 16384 ? 1 : 16384 / J.rb;
+        uint32_t tr = J.rb >= tile_bytes ? 1 : tile_bytes / J.rb;
         tr = tr < m ? m : tr / m * m;
         J.tr = tr;
         J.tile0 = tiles;
@@ -397,15 +403,12 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
     const uint32_t act_bytes =
         mode == 2 ? (cols + cols / 16) * 4 + cols / 32 * 4 : cols + cols / 4 + cols / 32 * 16;
-    uint64_t bytes = 0;
-    for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
-    const bool big = bytes >= GEMV_BIG_BYTES;
     // A standalone small launch (not a programmatic dependent inside a decode step) runs up
     // to 3 CTAs per SM with 64 KB rings; the others 2 CTAs per SM with 96 KB rings.
     const bool three = !p.pdl && !big;
     p.stage_bytes = stage + 16;
     p.use_tma = 1;
-    int ns = (int)((three ? 65536 : 98304) / p.stage_bytes);
+    int ns = (int)((three ? 65536 : (big ? 98400 : 98304)) / p.stage_bytes);
     if (ns > 8) ns = 8;
     if (ns < 2) {
         ns = 2;
