@@ -341,6 +341,10 @@ typedef struct KataliHybridLayerW {
     const void *wq, *wk, *wv, *wo;
     uint32_t wq_type, wk_type, wv_type, wo_type;
     const float *q_norm, *k_norm;  /* device fp32 [head_dim], or NULL */
+    /* GDN, optional: device fp32 [nv] decay rates A = -exp(A_log) as GGUF files store them
+     * (tensor ssm_a); when set the recurrence uses -A in place of exp(ssm_a_log), which
+     * may then be NULL. */
+    const float *ssm_decay;
 } KataliHybridLayerW;
 
 typedef struct KataliHybridDesc {
@@ -368,7 +372,11 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *desc, KataliHybrid **out);
 int katali_cuda_hybrid_destroy(KataliHybrid *m);
 /* Empties the KV cache and zeroes the recurrent (GDN) and conv states. */
 int katali_cuda_hybrid_reset(KataliHybrid *m);
-/* Greedy decode as katali_cuda_dense_generate (one graph replay per step). */
+/* Greedy decode as katali_cuda_dense_generate (one graph replay per step). A decoder whose
+ * experts are fed by a residency cache (katali_cuda_hybrid_create_from_gguf with a cache)
+ * runs each step layer by layer instead: after a layer's router the routing decision is read
+ * back, the selected experts are bound through the cache (uploading the ones not on the
+ * device from the file's mapping on the cache's stream), then the MoE block runs. */
 int katali_cuda_hybrid_generate(KataliHybrid *m, const int32_t *prompt, uint32_t n_prompt,
                                 uint32_t n_gen, int32_t *out_tokens);
 int katali_cuda_hybrid_logits(KataliHybrid *m, const float **logits_dev, int32_t *position);
@@ -435,6 +443,29 @@ int katali_cuda_gguf_upload(KataliGguf *g, uint64_t index, void *dev);
  * KATALI_ERR_UNSUPPORTED_TYPE. flags as KataliDenseDesc.flags. */
 int katali_cuda_dense_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t flags,
                                        KataliDense **out);
+/* The on-device hybrid MoE decoder (section 9) of a qwen35moe-architecture file (Gated
+ * DeltaNet and gated-attention layers, each followed by a routed-expert block; the names
+ * and layout of llama.cpp's conversion of that family). Metadata (prefix qwen35moe.):
+ * block_count, embedding_length, attention.head_count[_kv], attention.key_length,
+ * rope.dimension_count, rope.freq_base, attention.layer_norm_rms_epsilon, expert_count,
+ * expert_used_count, expert_feed_forward_length, ssm.conv_kernel, ssm.state_size,
+ * ssm.group_count, ssm.time_step_rank, ssm.inner_size, expert_weights_norm (default 1).
+ * Tensors: token_embd, output_norm, output (the embedding when absent); per layer
+ * blk.N.attn_norm, post_attention_norm, ffn_gate_inp (fp32 router, [hidden, experts]),
+ * the stacked experts ffn_gate_exps / ffn_up_exps ([hidden, ffn, experts]) and
+ * ffn_down_exps ([ffn, hidden, experts]); a GDN layer attn_qkv, attn_gate (z),
+ * ssm_beta, ssm_alpha, ssm_out, ssm_conv1d (fp32 [conv, channels]), ssm_a (fp32 A =
+ * -exp(A_log)), ssm_dt.bias, ssm_norm; an attention layer attn_q (query and gate rows per
+ * head), attn_k, attn_v, attn_output, attn_q_norm, attn_k_norm. Shared-expert tensors
+ * (ffn_*_shexp) are not supported (KATALI_ERR_UNSUPPORTED_SHAPE).
+ * cache NULL: every tensor, experts included, is uploaded unchanged into device memory the
+ * decoder owns. cache non-NULL: the experts stay in the file's read-only mapping, registered
+ * with the cache under key = layer * expert_count + e (slot_bytes must hold one expert), and
+ * are uploaded on demand by katali_cuda_hybrid_generate; the file and the cache must outlive
+ * the decoder. The decoder owns the MoE objects it creates (freed by
+ * katali_cuda_hybrid_destroy). Errors as katali_cuda_dense_create_from_gguf. */
+int katali_cuda_hybrid_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t flags,
+                                        KataliExpertCache *cache, KataliHybrid **out);
 
 /* ------------------------------------------------------------------------ */
 /* 5. Checks (the cuda-check / cuda-dp4a-selftest family, README.md:99-102)  */

@@ -32,6 +32,8 @@ int ensure_runtime();
 void set_status_message(const char *msg);
 cudaStream_t current_stream();
 void dense_adopt_weights(KataliDense *m, void *mem);
+void hybrid_adopt(KataliHybrid *m, std::vector<void *> allocs, std::vector<KataliMoe *> moes,
+                  std::vector<void *> pinned, KataliExpertCache *cache);
 }  // namespace kq
 
 namespace {
@@ -562,6 +564,306 @@ int katali_cuda_dense_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t 
         return s;
     }
     kq::dense_adopt_weights(*out, mem);
+    return KATALI_OK;
+}
+
+
+// The hybrid MoE decoder of a qwen35moe file. Non-expert tensors go into one device
+// allocation; each layer's stacked experts (expert e's gate rows at e * ffn * row bytes of
+// ffn_gate_exps, and so on) either into one allocation per layer (no cache) or, with a cache,
+// stay in the mapping and are registered per expert (the stacked tensors page-locked).
+int katali_cuda_hybrid_create_from_gguf(KataliGguf *g, uint32_t kv_cap, uint32_t flags,
+                                        KataliExpertCache *cache, KataliHybrid **out) {
+    if (!g || !out || !kv_cap) return KATALI_ERR_BAD_ARG;
+    *out = nullptr;
+    const char *arch = nullptr;
+    uint64_t alen = 0;
+    if (katali_cuda_gguf_get_str(g, "general.architecture", &arch, &alen) != KATALI_OK)
+        return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: no general.architecture");
+    const std::string A(arch, (size_t)alen);
+    if (A != "qwen35moe") {
+        kq::set_status_message("katali_cuda_hybrid_create_from_gguf: architecture is not qwen35moe");
+        return KATALI_ERR_UNSUPPORTED_SHAPE;
+    }
+    auto meta = [&](const char *key, int64_t def) {
+        int64_t v = def;
+        if (katali_cuda_gguf_get_int(g, (A + "." + key).c_str(), &v) != KATALI_OK) v = def;
+        return v;
+    };
+    auto metaf = [&](const char *key, double def) {
+        double v = def;
+        if (katali_cuda_gguf_get_float(g, (A + "." + key).c_str(), &v) != KATALI_OK) v = def;
+        return v;
+    };
+    const int64_t NL = meta("block_count", 0), H = meta("embedding_length", 0);
+    const int64_t NH = meta("attention.head_count", 0), NKV = meta("attention.head_count_kv", NH);
+    const int64_t HD = meta("attention.key_length", 0), RD = meta("rope.dimension_count", 0);
+    const int64_t E = meta("expert_count", 0), K = meta("expert_used_count", 0);
+    const int64_t F = meta("expert_feed_forward_length", 0), CK = meta("ssm.conv_kernel", 0);
+    const int64_t DK = meta("ssm.state_size", 0), NK = meta("ssm.group_count", 0);
+    const int64_t NV = meta("ssm.time_step_rank", 0), VD = meta("ssm.inner_size", 0);
+    const bool norm_topk = meta("expert_weights_norm", 1) != 0;
+    if (NL <= 0 || NL > 4096 || H <= 0 || E <= 0 || K <= 0 || K > E || F <= 0)
+        return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: missing or bad qwen35moe dimensions");
+    const int64_t C = 2 * NK * DK + VD;  // GDN in-projection channels (q, k, v)
+
+    struct Want {
+        uint64_t idx, off;
+    };
+    std::vector<Want> wants;
+    uint64_t total = 0;
+    const std::string who = "katali_cuda_hybrid_create_from_gguf: ";
+    auto find = [&](const std::string &name, uint64_t *i) {
+        return katali_cuda_gguf_find(g, name.c_str(), i) == KATALI_OK;
+    };
+    // a tensor of exact shape (d1 = 0: one dimension; matrix: a GGUF block type), queued for
+    // upload into the decoder's allocation
+    auto take = [&](const std::string &name, bool matrix, uint64_t d0, uint64_t d1, uint64_t *slot,
+                    uint32_t *type, bool optional = false) -> int {
+        uint64_t i = 0;
+        if (!find(name, &i)) {
+            if (optional) {
+                *slot = UINT64_MAX;
+                return KATALI_OK;
+            }
+            kq::set_status_message((who + "missing tensor " + name).c_str());
+            return KATALI_ERR_BAD_ARG;
+        }
+        const Tensor &t = g->t[(size_t)i];
+        const bool shape_ok = matrix ? (t.n_dims == 2 && t.dims[0] == d0 && t.dims[1] == d1)
+                                     : (d1 ? (t.n_dims == 2 && t.dims[0] == d0 && t.dims[1] == d1)
+                                           : (t.n_dims == 1 && t.dims[0] == d0)) && t.type == 0;
+        if (!shape_ok || !t.nbytes) {
+            kq::set_status_message((who + "unexpected shape or type of " + name).c_str());
+            return matrix ? KATALI_ERR_UNSUPPORTED_TYPE : KATALI_ERR_BAD_ARG;
+        }
+        if (type) *type = t.type;
+        *slot = wants.size();
+        wants.push_back(Want{i, total});
+        total += (t.nbytes + 255) & ~(uint64_t)255;
+        return KATALI_OK;
+    };
+    int s;
+    uint64_t emb_i, on_i, lm_i, vocab = 0;
+    uint32_t emb_t = 0, lm_t = 0;
+    {
+        uint64_t i = 0;
+        if (!find("token_embd.weight", &i) || g->t[(size_t)i].n_dims != 2)
+            return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: missing tensor token_embd.weight");
+        vocab = g->t[(size_t)i].dims[1];
+    }
+    if ((s = take("token_embd.weight", true, (uint64_t)H, vocab, &emb_i, &emb_t))) return s;
+    if ((s = take("output_norm.weight", false, (uint64_t)H, 0, &on_i, nullptr))) return s;
+    if ((s = take("output.weight", true, (uint64_t)H, vocab, &lm_i, &lm_t, true))) return s;
+    if (lm_i == UINT64_MAX) {  // tied embeddings
+        lm_i = emb_i;
+        lm_t = emb_t;
+    }
+    struct LayerSlots {
+        uint32_t kind;
+        uint64_t an, fn, rt, w[5], conv, adec, dtb, snorm, qn, kn;
+        uint32_t t[5];
+        uint64_t exps[3];  // gate, up, down stacked tensors (file indices)
+    };
+    std::vector<LayerSlots> ls((size_t)NL);
+    uint32_t etype[3] = {0, 0, 0};
+    for (int64_t l = 0; l < NL; ++l) {
+        const std::string pfx = "blk." + std::to_string(l) + ".";
+        LayerSlots &L = ls[(size_t)l];
+        uint64_t dummy = 0;
+        if (find(pfx + "ffn_gate_shexp.weight", &dummy) || find(pfx + "ffn_up_shexp.weight", &dummy)) {
+            kq::set_status_message((who + "shared experts (ffn_*_shexp) are not supported").c_str());
+            return KATALI_ERR_UNSUPPORTED_SHAPE;
+        }
+        if ((s = take(pfx + "attn_norm.weight", false, (uint64_t)H, 0, &L.an, nullptr))) return s;
+        if ((s = take(pfx + "post_attention_norm.weight", false, (uint64_t)H, 0, &L.fn, nullptr))) return s;
+        if ((s = take(pfx + "ffn_gate_inp.weight", false, (uint64_t)H, (uint64_t)E, &L.rt, nullptr))) return s;
+        L.kind = find(pfx + "attn_qkv.weight", &dummy) ? KATALI_HYBRID_GDN : KATALI_HYBRID_ATTN;
+        if (L.kind == KATALI_HYBRID_GDN) {
+            if (C <= 0 || VD <= 0 || NV <= 0 || CK <= 0)
+                return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: missing or bad ssm dimensions");
+            const char *mats[5] = {"attn_qkv", "attn_gate", "ssm_beta", "ssm_alpha", "ssm_out"};
+            const uint64_t cols[5] = {(uint64_t)H, (uint64_t)H, (uint64_t)H, (uint64_t)H, (uint64_t)VD};
+            const uint64_t rows[5] = {(uint64_t)C, (uint64_t)VD, (uint64_t)NV, (uint64_t)NV, (uint64_t)H};
+            for (int j = 0; j < 5; ++j)
+                if ((s = take(pfx + mats[j] + ".weight", true, cols[j], rows[j], &L.w[j], &L.t[j]))) return s;
+            if ((s = take(pfx + "ssm_conv1d.weight", false, (uint64_t)CK, (uint64_t)C, &L.conv, nullptr))) return s;
+            if ((s = take(pfx + "ssm_a", false, (uint64_t)NV, 0, &L.adec, nullptr))) return s;
+            if ((s = take(pfx + "ssm_dt.bias", false, (uint64_t)NV, 0, &L.dtb, nullptr))) return s;
+            if ((s = take(pfx + "ssm_norm.weight", false, (uint64_t)DK, 0, &L.snorm, nullptr))) return s;
+        } else {
+            if (NH <= 0 || NKV <= 0 || HD <= 0)
+                return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: missing or bad attention dimensions");
+            const char *mats[4] = {"attn_q", "attn_k", "attn_v", "attn_output"};
+            const uint64_t cols[4] = {(uint64_t)H, (uint64_t)H, (uint64_t)H, (uint64_t)(NH * HD)};
+            const uint64_t rows[4] = {(uint64_t)(2 * NH * HD), (uint64_t)(NKV * HD), (uint64_t)(NKV * HD),
+                                      (uint64_t)H};
+            for (int j = 0; j < 4; ++j)
+                if ((s = take(pfx + mats[j] + ".weight", true, cols[j], rows[j], &L.w[j], &L.t[j]))) return s;
+            if ((s = take(pfx + "attn_q_norm.weight", false, (uint64_t)HD, 0, &L.qn, nullptr, true))) return s;
+            if ((s = take(pfx + "attn_k_norm.weight", false, (uint64_t)HD, 0, &L.kn, nullptr, true))) return s;
+        }
+        const char *ex[3] = {"ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"};
+        const uint64_t d0[3] = {(uint64_t)H, (uint64_t)H, (uint64_t)F}, d1[3] = {(uint64_t)F, (uint64_t)F, (uint64_t)H};
+        for (int j = 0; j < 3; ++j) {
+            uint64_t i = 0;
+            if (!find(pfx + ex[j] + ".weight", &i)) {
+                kq::set_status_message((who + "missing tensor " + pfx + ex[j] + ".weight").c_str());
+                return KATALI_ERR_BAD_ARG;
+            }
+            const Tensor &t = g->t[(size_t)i];
+            if (t.n_dims != 3 || t.dims[0] != d0[j] || t.dims[1] != d1[j] || t.dims[2] != (uint64_t)E ||
+                !t.nbytes || t.nbytes % (uint64_t)E || (t.nbytes / (uint64_t)E) % 16) {
+                kq::set_status_message((who + "unexpected shape or type of " + pfx + ex[j] + ".weight").c_str());
+                return KATALI_ERR_UNSUPPORTED_TYPE;
+            }
+            if (l == 0) etype[j] = t.type;
+            else if (t.type != etype[j]) return fail(nullptr, "katali_cuda_hybrid_create_from_gguf: expert types differ between layers");
+            L.exps[j] = i;
+        }
+    }
+    if (const int rs = kq::ensure_runtime()) return rs;
+    std::vector<void *> allocs;
+    std::vector<KataliMoe *> moes;
+    std::vector<void *> pinned;
+    auto cleanup = [&](int status) {
+        for (KataliMoe *m : moes) katali_cuda_moe_destroy(m);
+        for (void *a : allocs) cudaFree(a);
+        for (void *h : pinned) cudaHostUnregister(h);
+        return status;
+    };
+    auto dev_alloc = [&](uint64_t bytes, unsigned char **p) -> int {
+        cudaError_t e = cudaMalloc((void **)p, bytes);
+        if (e != cudaSuccess) {
+            kq::set_status_message(cudaGetErrorString(e));
+            return e == cudaErrorMemoryAllocation ? KATALI_ERR_OOM : KATALI_ERR_CUDA;
+        }
+        allocs.push_back(*p);
+        return KATALI_OK;
+    };
+    unsigned char *mem = nullptr;
+    if ((s = dev_alloc(total, &mem))) return cleanup(s);
+    for (const Want &w : wants)
+        if ((s = katali_cuda_gguf_upload(g, w.idx, mem + w.off)) != KATALI_OK) return cleanup(s);
+    auto ptr = [&](uint64_t slot) -> const void * {
+        return slot == UINT64_MAX ? nullptr : mem + wants[(size_t)slot].off;
+    };
+    // experts: one MoE object per layer, its table on the device copy or left empty for the cache
+    std::vector<const void *> table(3 * (size_t)E);
+    for (int64_t l = 0; l < NL; ++l) {
+        const LayerSlots &L = ls[(size_t)l];
+        uint64_t slice[3];
+        const uint8_t *host[3];
+        for (int j = 0; j < 3; ++j) {
+            const Tensor &t = g->t[(size_t)L.exps[j]];
+            slice[j] = t.nbytes / (uint64_t)E;
+            host[j] = g->map + t.abs;
+        }
+        if (!cache) {
+            unsigned char *ex = nullptr;
+            uint64_t off[3], sum = 0;
+            for (int j = 0; j < 3; ++j) {
+                off[j] = sum;
+                sum += (g->t[(size_t)L.exps[j]].nbytes + 255) & ~(uint64_t)255;
+            }
+            if ((s = dev_alloc(sum, &ex))) return cleanup(s);
+            for (int j = 0; j < 3; ++j)
+                if ((s = katali_cuda_gguf_upload(g, L.exps[j], ex + off[j])) != KATALI_OK) return cleanup(s);
+            for (int64_t e = 0; e < E; ++e)
+                for (int j = 0; j < 3; ++j) table[3 * (size_t)e + j] = ex + off[j] + (uint64_t)e * slice[j];
+        } else {
+            for (int j = 0; j < 3; ++j) {  // page-lock the stacked tensor once (async uploads)
+                const uintptr_t pg = 4096, a = (uintptr_t)host[j] & ~(pg - 1);
+                const uintptr_t b = ((uintptr_t)host[j] + g->t[(size_t)L.exps[j]].nbytes + pg - 1) & ~(pg - 1);
+                if (cudaHostRegister((void *)a, b - a, cudaHostRegisterReadOnly) == cudaSuccess)
+                    pinned.push_back((void *)a);
+                else
+                    cudaGetLastError();
+            }
+            for (int64_t e = 0; e < E; ++e) {
+                s = katali_cuda_expert_register(cache, (uint64_t)l * (uint64_t)E + (uint64_t)e,
+                                                host[0] + (uint64_t)e * slice[0], slice[0],
+                                                host[1] + (uint64_t)e * slice[1], slice[1],
+                                                host[2] + (uint64_t)e * slice[2], slice[2]);
+                if (s) return cleanup(s);
+            }
+            for (auto &p : table) p = nullptr;
+        }
+        KataliMoeDesc md = {};
+        md.n_experts = (uint32_t)E;
+        md.hidden = (uint32_t)H;
+        md.ffn = (uint32_t)F;
+        md.top_k = (uint32_t)K;
+        md.gate_type = etype[0];
+        md.up_type = etype[1];
+        md.down_type = etype[2];
+        md.flags = norm_topk ? KATALI_MOE_NORM_TOPK : 0u;
+        md.experts = table.data();
+        KataliMoe *moe = nullptr;
+        if ((s = katali_cuda_moe_create(&md, &moe)) != KATALI_OK) return cleanup(s);
+        moes.push_back(moe);
+    }
+    std::vector<KataliHybridLayerW> lw((size_t)NL);
+    for (int64_t l = 0; l < NL; ++l) {
+        const LayerSlots &L = ls[(size_t)l];
+        KataliHybridLayerW &w = lw[(size_t)l];
+        w.kind = L.kind;
+        w.attn_norm = (const float *)ptr(L.an);
+        w.ffn_norm = (const float *)ptr(L.fn);
+        w.router = (const float *)ptr(L.rt);
+        w.moe = moes[(size_t)l];
+        if (L.kind == KATALI_HYBRID_GDN) {
+            w.ssm_qkv = ptr(L.w[0]);
+            w.ssm_z = ptr(L.w[1]);
+            w.ssm_b = ptr(L.w[2]);
+            w.ssm_a = ptr(L.w[3]);
+            w.ssm_out = ptr(L.w[4]);
+            w.ssm_qkv_type = L.t[0];
+            w.ssm_z_type = L.t[1];
+            w.ssm_b_type = L.t[2];
+            w.ssm_a_type = L.t[3];
+            w.ssm_out_type = L.t[4];
+            w.ssm_conv = (const float *)ptr(L.conv);
+            w.ssm_decay = (const float *)ptr(L.adec);
+            w.ssm_dt_bias = (const float *)ptr(L.dtb);
+            w.ssm_norm = (const float *)ptr(L.snorm);
+        } else {
+            w.wq = ptr(L.w[0]);
+            w.wk = ptr(L.w[1]);
+            w.wv = ptr(L.w[2]);
+            w.wo = ptr(L.w[3]);
+            w.wq_type = L.t[0];
+            w.wk_type = L.t[1];
+            w.wv_type = L.t[2];
+            w.wo_type = L.t[3];
+            w.q_norm = (const float *)ptr(L.qn);
+            w.k_norm = (const float *)ptr(L.kn);
+        }
+    }
+    KataliHybridDesc d = {};
+    d.n_layers = (uint32_t)NL;
+    d.hidden = (uint32_t)H;
+    d.vocab = (uint32_t)vocab;
+    d.kv_cap = kv_cap;
+    d.n_heads = (uint32_t)(NH > 0 ? NH : 0);
+    d.n_kv_heads = (uint32_t)(NKV > 0 ? NKV : 0);
+    d.head_dim = (uint32_t)(HD > 0 ? HD : 0);
+    d.rope_dim = (uint32_t)(RD > 0 ? RD : 0);
+    d.rms_eps = (float)metaf("attention.layer_norm_rms_epsilon", 1e-6);
+    d.rope_theta = (float)metaf("rope.freq_base", 1e7);
+    d.ssm_k_heads = (uint32_t)(NK > 0 ? NK : 0);
+    d.ssm_v_heads = (uint32_t)(NV > 0 ? NV : 0);
+    d.ssm_head_dim = (uint32_t)(DK > 0 ? DK : 0);
+    d.ssm_conv = (uint32_t)(CK > 0 ? CK : 0);
+    d.embed = ptr(emb_i);
+    d.embed_type = emb_t;
+    d.out_norm = (const float *)ptr(on_i);
+    d.lm_head = ptr(lm_i);
+    d.lm_head_type = lm_t;
+    d.layers = lw.data();
+    d.flags = flags;
+    if ((s = katali_cuda_hybrid_create(&d, out)) != KATALI_OK) return cleanup(s);
+    kq::hybrid_adopt(*out, std::move(allocs), std::move(moes), std::move(pinned), cache);
     return KATALI_OK;
 }
 

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(GDN_THREADS) k_gdn(HybridParams p, HybridLayer
         pre[q] = acc;
         wl[q] = w[K - 1];
     }
-    const float ea = kq_expf(L.a_log[vh]), dtb = L.dt_bias[vh];
+    const float ea = L.a_neg ? -L.a_neg[vh] : kq_expf(L.a_log[vh]), dtb = L.dt_bias[vh];
     pdl_trigger();
     pdl_wait();
 #pragma unroll
@@ -358,7 +358,8 @@ cudaError_t launch_gdn(HybridParams &p, const HybridLayer &L, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams *g,
-                               MoeParams *moe, const int *moe_grid, cudaStream_t st) {
+                               MoeParams *moe, const int *moe_grid, cudaStream_t st,
+                               HybridHook before_moe, void *ctx, int *hook_status) {
     // Every launch but the first (the embedding) and the cooperative MoE kernels is a
     // programmatic dependent of the one before it (the GEMVs carry it in GemvParams.pdl).
     cudaError_t e = launch_dense_embed(p.d, st);
@@ -380,6 +381,13 @@ cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams
         if ((p.moe_ep || !moe[l].rt_w) &&  // else the router runs inside the MoE launch
             (e = launch_k(router, rgrid, dim3(RW * 32), rt_smem, st, 1, p, L[l])) != cudaSuccess)
             return e;
+        if (before_moe) {
+            const int hs = before_moe(ctx, l);
+            if (hs) {
+                if (hook_status) *hook_status = hs;
+                return cudaSuccess;
+            }
+        }
         e = p.moe_ep ? launch_moe_ep_layer(moe[l], moe_grid[l], st) : launch_moe(moe[l], moe_grid[l], st);
         if (e != cudaSuccess) return e;
     }

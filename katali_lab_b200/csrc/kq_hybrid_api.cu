@@ -23,6 +23,10 @@ int moe_ep_fused_params(KataliMoe *m, uint32_t n_ranks, uint32_t max_tokens, uin
                         double *ret_scratch, MoeParams *out, int *grid);
 int ep_peer_prepare(KataliEp *ep, KataliMoe *m, uint32_t max_tokens, uint32_t *n_ranks,
                     const EpPeer **pp, double **ret);
+// Resources a decoder made from a file owns: device allocations, the MoE objects, page-locked
+// host ranges; with a cache, its experts are fed through it (keys layer * n_experts + e).
+void hybrid_adopt(KataliHybrid *m, std::vector<void *> allocs, std::vector<KataliMoe *> moes,
+                  std::vector<void *> pinned, KataliExpertCache *cache);
 }  // namespace kq
 
 namespace {
@@ -68,6 +72,11 @@ kq::GemvParams gemv_jobs(const float *x, uint64_t cols, int n, const void *const
 
 }  // namespace
 
+struct KataliHybrid;
+namespace {
+int bind_routed(void *ctx, int layer);
+}
+
 struct KataliHybrid {
     KataliHybridDesc d;
     std::vector<KataliHybridLayerW> lw;
@@ -77,6 +86,13 @@ struct KataliHybrid {
     std::vector<int> moe_grid;
     std::vector<kq::MoeParams> moe_local;  // single-GPU launches (kept while expert-parallel)
     std::vector<int> grid_local;
+    std::vector<kq::MoeParams> moe_sep;    // the same with the router as its own kernel
+    // owned when made from a file (katali_cuda_hybrid_create_from_gguf)
+    std::vector<void *> own_allocs, own_pinned;
+    std::vector<KataliMoe *> own_moe;
+    KataliExpertCache *cache = nullptr;    // residency mode: experts bound per step
+    int32_t *route_dev = nullptr;          // [2 * top_k]: one routing decision (ids, weights)
+    uint32_t n_experts = 0, top_k = 0;
     kq::HybridParams p;
     void *mem = nullptr;
     size_t state_off = 0, state_bytes = 0;  // GDN states + conv rings (zeroed by reset)
@@ -85,6 +101,45 @@ struct KataliHybrid {
     cudaGraphExec_t exec = nullptr;
     cudaStream_t graph_stream = nullptr;
 };
+
+namespace {
+// Residency mode, after layer l's router: the routing decision of the MoE kernel itself
+// (its route-only launch on the router logits), read back, then every selected expert bound
+// through the cache (uploaded from the host mapping when not on the device; the MoE launch
+// that follows waits for the upload).
+int bind_routed(void *ctx, int layer) {
+    KataliHybrid *m = (KataliHybrid *)ctx;
+    KataliMoe *moe = m->lw[(size_t)layer].moe;
+    const uint32_t K = m->top_k;
+    int s = katali_cuda_debug_route(moe, m->p.rlogits, m->route_dev, (float *)(m->route_dev + K));
+    if (s) return s;
+    int32_t ids[kq::MOE_MAX_K];
+    cudaStream_t st = kq::current_stream();
+    cudaError_t e = cudaMemcpyAsync(ids, m->route_dev, 4ull * K, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        kq::set_status_message(cudaGetErrorString(e));
+        return KATALI_ERR_CUDA;
+    }
+    for (uint32_t k = 0; k < K; ++k) {
+        if (ids[k] < 0 || (uint32_t)ids[k] >= m->n_experts) return KATALI_ERR_CUDA;
+        s = katali_cuda_expert_bind(m->cache, (uint64_t)layer * m->n_experts + (uint64_t)ids[k], moe,
+                                    (uint32_t)ids[k]);
+        if (s) return s;
+    }
+    return KATALI_OK;
+}
+}  // namespace
+
+namespace kq {
+void hybrid_adopt(KataliHybrid *m, std::vector<void *> allocs, std::vector<KataliMoe *> moes,
+                  std::vector<void *> pinned, KataliExpertCache *cache) {
+    m->own_allocs = std::move(allocs);
+    m->own_moe = std::move(moes);
+    m->own_pinned = std::move(pinned);
+    m->cache = cache;
+}
+}  // namespace kq
 
 extern "C" {
 
@@ -124,7 +179,7 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
         if (!w.attn_norm || !w.ffn_norm || !a16(w.router) || !w.moe)
             return bad("katali_cuda_hybrid_create: layer norms / router / MoE");
         if (w.kind == KATALI_HYBRID_GDN) {
-            if (!w.ssm_conv || !w.ssm_a_log || !w.ssm_dt_bias || !w.ssm_norm)
+            if (!w.ssm_conv || (!w.ssm_a_log && !w.ssm_decay) || !w.ssm_dt_bias || !w.ssm_norm)
                 return bad("katali_cuda_hybrid_create: GDN parameters");
             const void *m[5] = {w.ssm_qkv, w.ssm_z, w.ssm_b, w.ssm_a, w.ssm_out};
             const uint32_t t[5] = {w.ssm_qkv_type, w.ssm_z_type, w.ssm_b_type, w.ssm_a_type, w.ssm_out_type};
@@ -282,6 +337,7 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
             hl.kind = 0;
             hl.conv_w = w.ssm_conv;
             hl.a_log = w.ssm_a_log;
+            hl.a_neg = w.ssm_decay;
             hl.dt_bias = w.ssm_dt_bias;
             hl.ssm_norm = w.ssm_norm;
             hl.ring = (float *)(st_base + (size_t)gi * (ring_bytes + state_bytes));
@@ -321,6 +377,8 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
         mp.y = p.x;
         mp.accum = 1;
         mp.pdl = 1;
+        mp.x = p.xb;  // RMSNorm and router logits from the router kernel
+        m->moe_sep.push_back(mp);
         const int grid = m->moe_grid[l];
         if (H <= 4u * 512u && (n_experts + grid - 1) / grid <= (uint32_t)kq::MOE_RT_ROWS) {
             // the router runs inside the MoE launch: x is the residual stream itself (read by
@@ -342,6 +400,8 @@ int katali_cuda_hybrid_create(const KataliHybridDesc *d, KataliHybrid **out) {
     }
     m->moe_local = m->moe;
     m->grid_local = m->moe_grid;
+    m->n_experts = n_experts;
+    m->top_k = (uint32_t)m->moe[0].K;
     *out = m;
     return KATALI_OK;
 }
@@ -394,6 +454,10 @@ int katali_cuda_hybrid_destroy(KataliHybrid *m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->graph) cudaGraphDestroy(m->graph);
     cudaFree(m->mem);
+    cudaFree(m->route_dev);
+    for (KataliMoe *moe : m->own_moe) katali_cuda_moe_destroy(moe);
+    for (void *a : m->own_allocs) cudaFree(a);
+    for (void *h : m->own_pinned) cudaHostUnregister(h);
     delete m;
     return KATALI_OK;
 }
@@ -423,7 +487,20 @@ int katali_cuda_hybrid_generate(KataliHybrid *m, const int32_t *prompt, uint32_t
                                     cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->p.d.tok, ctl, sizeof ctl, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return KATALI_ERR_CUDA;
-    for (uint64_t s = 0; s < steps; ++s) {
+    if (m->cache) {  // residency mode: each step layer by layer, experts bound after the router
+        if (!m->route_dev && (e = cudaMalloc((void **)&m->route_dev, 8ull * kq::MOE_MAX_K)) != cudaSuccess) {
+            m->route_dev = nullptr;
+            return KATALI_ERR_OOM;
+        }
+        for (uint64_t s = 0; s < steps; ++s) {
+            int hs = 0;
+            e = kq::launch_hybrid_step(m->p, m->L.data(), m->g.data(), m->moe_sep.data(),
+                                       m->grid_local.data(), st, bind_routed, m, &hs);
+            if (hs) return hs;
+            if (e != cudaSuccess) break;
+        }
+    }
+    for (uint64_t s = 0; s < steps && !m->cache; ++s) {
         if (!m->exec || m->graph_stream != st) {
             // First step on this stream: run it eagerly (sets kernel attributes), then
             // capture the same launch sequence once for the following steps.

@@ -296,6 +296,7 @@ struct HybridLayer {
     int kind;                        // 0: Gated DeltaNet, 1: gated full attention
     const float *conv_w;             // GDN: [C][conv_k] depthwise causal conv, C = 2 nk dk + nv dv
     const float *a_log, *dt_bias;    // GDN: [nv]
+    const float *a_neg;              // GDN, optional: [nv] A = -exp(A_log), used instead of a_log
     const float *ssm_norm;           // GDN: [dv] weight of the gated RMSNorm
     float *ring;                     // GDN: [conv_k][C] last conv_k inputs (slot pos % conv_k)
     float *state;                    // GDN: [nv][dv][dk] recurrent state, column j of head h contiguous
@@ -317,8 +318,13 @@ struct HybridParams {
 };
 // One decode step: g[2 l], g[2 l + 1] are layer l's input and output projections, g[2 NL]
 // the LM head; moe[l] / moe_grid[l] the layer's fused MoE launch (x = xb, y = x, accum).
+// before_moe (optional): called after layer l's router launch and before its MoE launch
+// (the residency mode binds the layer's selected experts there); nonzero stops the step.
+typedef int (*HybridHook)(void *ctx, int layer);
 cudaError_t launch_hybrid_step(HybridParams &p, const HybridLayer *L, GemvParams *g,
-                               MoeParams *moe, const int *moe_grid, cudaStream_t st);
+                               MoeParams *moe, const int *moe_grid, cudaStream_t st,
+                               HybridHook before_moe = nullptr, void *ctx = nullptr,
+                               int *hook_status = nullptr);
 cudaError_t hybrid_set_attention_smem(int kv_cap);
 
 }  // namespace kq

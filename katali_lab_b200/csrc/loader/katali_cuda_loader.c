@@ -130,6 +130,9 @@
     X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
     X(int, katali_cuda_dense_create_from_gguf,                                                \
       (KataliGguf * g, uint32_t c, uint32_t f, KataliDense **o), (g, c, f, o))                \
+    X(int, katali_cuda_hybrid_create_from_gguf,                                               \
+      (KataliGguf * g, uint32_t c, uint32_t f, KataliExpertCache *x, KataliHybrid **o),       \
+      (g, c, f, x, o))                                                                        \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \
@@ -312,6 +315,9 @@ const char *katali_cuda_strerror(int s) {
     X(int, katali_cuda_gguf_upload, (KataliGguf * g, uint64_t i, void *d), (g, i, d))        \
     X(int, katali_cuda_dense_create_from_gguf,                                                \
       (KataliGguf * g, uint32_t c, uint32_t f, KataliDense **o), (g, c, f, o))                \
+    X(int, katali_cuda_hybrid_create_from_gguf,                                               \
+      (KataliGguf * g, uint32_t c, uint32_t f, KataliExpertCache *x, KataliHybrid **o),       \
+      (g, c, f, x, o))                                                                        \
     X(int, katali_cuda_ep_unique_id, (void *id), (id))                                        \
     X(int, katali_cuda_ep_create, (uint32_t g, uint32_t r, const void *id, KataliEp **o),     \
       (g, r, id, o))                                                                          \

@@ -53,7 +53,7 @@ class KataliHybridLayerW(C.Structure):
                 ("ssm_a_type", _u32), ("ssm_out_type", _u32), ("ssm_conv", _vp), ("ssm_a_log", _vp),
                 ("ssm_dt_bias", _vp), ("ssm_norm", _vp), ("wq", _vp), ("wk", _vp), ("wv", _vp),
                 ("wo", _vp), ("wq_type", _u32), ("wk_type", _u32), ("wv_type", _u32),
-                ("wo_type", _u32), ("q_norm", _vp), ("k_norm", _vp)]
+                ("wo_type", _u32), ("q_norm", _vp), ("k_norm", _vp), ("ssm_decay", _vp)]
 
 
 class KataliHybridDesc(C.Structure):
@@ -166,6 +166,7 @@ class Plugin:
             "katali_cuda_gguf_array_int": ([_vp, C.c_char_p, _u64, C.POINTER(C.c_int64)], _i32),
             "katali_cuda_gguf_upload": ([_vp, _u64, _vp], _i32),
             "katali_cuda_dense_create_from_gguf": ([_vp, _u32, _u32, C.POINTER(_vp)], _i32),
+            "katali_cuda_hybrid_create_from_gguf": ([_vp, _u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_unique_id": ([_vp], _i32),
             "katali_cuda_ep_create": ([_u32, _u32, _vp, C.POINTER(_vp)], _i32),
             "katali_cuda_ep_destroy": ([_vp], _i32),
@@ -435,8 +436,9 @@ class HybridModel:
                 for k in ("ssm_qkv", "ssm_z", "ssm_b", "ssm_a", "ssm_out"):
                     setattr(e, k, _ptr(w[k]))
                     setattr(e, k + "_type", T[k])
-                for k in ("ssm_conv", "ssm_a_log", "ssm_dt_bias", "ssm_norm"):
-                    setattr(e, k, _ptr(w[k]))
+                for k in ("ssm_conv", "ssm_a_log", "ssm_dt_bias", "ssm_norm", "ssm_decay"):
+                    if w.get(k) is not None:
+                        setattr(e, k, _ptr(w[k]))
             else:
                 for k in ("wq", "wk", "wv", "wo"):
                     setattr(e, k, _ptr(w[k]))
@@ -458,6 +460,23 @@ class HybridModel:
             plugin.check(rc)
         self.h = h
         self.vocab = cfg.vocab
+
+    @classmethod
+    def from_gguf(cls, plugin: Plugin, gguf, kv_cap: int, q8: bool = False,
+                  cache=None) -> "HybridModel":
+        """The decoder of a qwen35moe-architecture GGUF file
+        (katali_cuda_hybrid_create_from_gguf); gguf: an open katali_lab_b200.Gguf; cache: an
+        ExpertCache feeding the experts from the file's mapping on demand (None: all resident).
+        The decoder owns its MoE objects; the file and the cache must outlive it."""
+        self = cls.__new__(cls)
+        self.p = plugin
+        self.moes = []
+        h = _vp()
+        plugin.check(plugin.L.katali_cuda_hybrid_create_from_gguf(
+            gguf.h, kv_cap, 1 if q8 else 0, cache.h if cache is not None else None, C.byref(h)))
+        self.h = h
+        self.vocab = gguf.tensor(gguf.find("token_embd.weight"))["dims"][1]
+        return self
 
     def reset(self) -> None:
         self.p.check(self.p.L.katali_cuda_hybrid_reset(self.h))

@@ -136,3 +136,72 @@ def dense_model_file(port, cfg, seed=0, std=0.02, byte_vocab=False):
     if byte_vocab:
         kvs.append(("tokenizer.ggml.model", STR, "gpt2"))
     return build(kvs, [(n, t, d, b) for n, t, d, b in ts])
+
+
+def hybrid_model_file(port, cfg, seed=0, std=0.02):
+    """A qwen35moe-architecture hybrid MoE model (llama.cpp tensor names and layout) for a
+    katali_lab_b200.synth.HybridConfig: Gated DeltaNet layers (attn_qkv, attn_gate, ssm_beta,
+    ssm_alpha, ssm_out, ssm_conv1d, ssm_a = -exp(A_log), ssm_dt.bias, ssm_norm) and gated
+    attention layers (attn_q with query and gate rows per head, attn_k, attn_v, attn_output,
+    attn_q_norm, attn_k_norm), each followed by the routed experts (ffn_gate_inp fp32 router,
+    ffn_gate_exps / ffn_up_exps [hidden, ffn, experts] Q4_K, ffn_down_exps [ffn, hidden,
+    experts] Q6_K). Matrices ~ N(0, std) encoded by the oracle's encoder (the types of
+    synth.HYBRID_TYPES); norms 1 + 0.1 N(0, 1), conv taps N(0, 0.3), A_log = log U(1, 16),
+    dt_bias U(-4, -2)."""
+    from oracle.oracle import Q4_K, Q6_K
+    rng = np.random.default_rng(seed)
+    H, E, F = cfg.hidden, cfg.n_experts, cfg.ffn
+    nk, nv, dh, ck = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim, cfg.ssm_conv
+    Cc, VD = (2 * nk + nv) * dh, nv * dh
+    QD, KD = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+
+    def enc(qt, rows, cols):
+        return port.quantize(qt, rng.normal(0, std, (rows, cols)).astype(np.float32)).tobytes()
+
+    def mat(qt, rows, cols):
+        return (qt, (cols, rows), enc(qt, rows, cols))
+
+    def f32(dims, a):
+        return (0, dims, np.ascontiguousarray(a, dtype=np.float32).tobytes())
+
+    def norm(n):
+        return f32((n,), 1.0 + 0.1 * rng.normal(0, 1, n))
+
+    ts = [("token_embd.weight",) + mat(Q4_K, cfg.vocab, H)]
+    for l in range(cfg.n_layers):
+        p = f"blk.{l}."
+        ts += [(p + "attn_norm.weight",) + norm(H)]
+        if cfg.kind(l) == 0:
+            a_log = np.log(rng.uniform(1.0, 16.0, nv)).astype(np.float32)
+            ts += [(p + "attn_qkv.weight",) + mat(Q4_K, Cc, H), (p + "attn_gate.weight",) + mat(Q4_K, VD, H),
+                   (p + "ssm_beta.weight",) + mat(Q4_K, nv, H), (p + "ssm_alpha.weight",) + mat(Q4_K, nv, H),
+                   (p + "ssm_out.weight",) + mat(Q4_K, H, VD),
+                   (p + "ssm_conv1d.weight",) + f32((ck, Cc), rng.normal(0, 0.3, (Cc, ck))),
+                   (p + "ssm_a",) + f32((nv,), -np.exp(a_log)),
+                   (p + "ssm_dt.bias",) + f32((nv,), rng.uniform(-4.0, -2.0, nv)),
+                   (p + "ssm_norm.weight",) + norm(dh)]
+        else:
+            ts += [(p + "attn_q.weight",) + mat(Q4_K, 2 * QD, H), (p + "attn_k.weight",) + mat(Q4_K, KD, H),
+                   (p + "attn_v.weight",) + mat(Q6_K, KD, H), (p + "attn_output.weight",) + mat(Q4_K, H, QD),
+                   (p + "attn_q_norm.weight",) + norm(cfg.head_dim),
+                   (p + "attn_k_norm.weight",) + norm(cfg.head_dim)]
+        ts += [(p + "post_attention_norm.weight",) + norm(H),
+               (p + "ffn_gate_inp.weight",) + f32((H, E), rng.normal(0, std, (E, H))),
+               (p + "ffn_gate_exps.weight", Q4_K, (H, F, E), b"".join(enc(Q4_K, F, H) for _ in range(E))),
+               (p + "ffn_up_exps.weight", Q4_K, (H, F, E), b"".join(enc(Q4_K, F, H) for _ in range(E))),
+               (p + "ffn_down_exps.weight", Q6_K, (F, H, E), b"".join(enc(Q6_K, H, F) for _ in range(E)))]
+    ts += [("output_norm.weight",) + norm(H), ("output.weight",) + mat(Q6_K, cfg.vocab, H)]
+    A = "qwen35moe"
+    kvs = [("general.architecture", STR, A), (A + ".block_count", U32, cfg.n_layers),
+           (A + ".embedding_length", U32, H), (A + ".attention.head_count", U32, cfg.n_heads),
+           (A + ".attention.head_count_kv", U32, cfg.n_kv_heads),
+           (A + ".attention.key_length", U32, cfg.head_dim), (A + ".rope.dimension_count", U32, cfg.rope_dim),
+           (A + ".rope.freq_base", F32, cfg.rope_theta),
+           (A + ".attention.layer_norm_rms_epsilon", F32, cfg.rms_eps),
+           (A + ".expert_count", U32, E), (A + ".expert_used_count", U32, cfg.top_k),
+           (A + ".expert_feed_forward_length", U32, F), (A + ".ssm.conv_kernel", U32, ck),
+           (A + ".ssm.state_size", U32, dh), (A + ".ssm.group_count", U32, nk),
+           (A + ".ssm.time_step_rank", U32, nv), (A + ".ssm.inner_size", U32, VD),
+           (A + ".full_attention_interval", U32, cfg.attn_every), (A + ".context_length", U32, cfg.kv_cap),
+           ("tokenizer.ggml.tokens", ARR, (STR, [f"t{i}" for i in range(cfg.vocab)]))]
+    return build(kvs, [(n, t, d, b) for n, t, d, b in ts])
