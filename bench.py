@@ -106,10 +106,10 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def committed_traffic():
-    """Per-launch DRAM bytes of the MoE kernel from the committed ncu summary."""
+def committed_traffic(name="moe_kernel_traffic.json"):
+    """Per-launch DRAM bytes of a kernel from its committed ncu summary (profiles/)."""
     try:
-        with open(os.path.join(ROOT, "profiles", "moe_kernel_traffic.json")) as f:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
             return json.load(f)
     except Exception:
         return None
@@ -609,7 +609,9 @@ def _run_c1(args, rank, world, local_rank, Q4_K, Plugin, make_dense):
                        "us_per_call": round(us_call, 3)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} hbm_gbs",
-                         "traffic": None, "algorithmic_bytes_per_launch": C1_BYTES},
+                         "traffic": (committed_traffic("gemv_c1_traffic.json") or {}).get("dram_bytes_per_launch")
+                         if not args.dp4a else None,
+                         "algorithmic_bytes_per_launch": C1_BYTES},
             "clocks": clk.summary(),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": C1_COLS * 4,
                     "d2h_bytes_per_step": C1_ROWS * 4},
