@@ -382,7 +382,19 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     uint64_t bytes = 0;
     for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
     const bool big = bytes >= GEMV_BIG_BYTES;
-    const uint32_t tile_bytes = big ? 49152u : 16384u;
+    const uint32_t cols = p.cols;
+    // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
+    const uint32_t act_bytes =
+        mode == 2 ? (cols + cols / 16) * 4 + cols / 32 * 4 : cols + cols / 4 + cols / 32 * 16;
+    // Big launches run two CTAs per SM with two-stage rings: the stages shrink for wide rows
+    // (a long activation area) so that both CTAs still fit the SM's 228 KB.
+    uint32_t tile_bytes = 16384u;
+    if (big) {
+        const uint32_t budget = 233472u / 2u - 1024u - act_bytes - 512u;  // per CTA
+        tile_bytes = budget / 2u - 32u;
+        if (tile_bytes > 49152u) tile_bytes = 49152u;
+        if (tile_bytes < 16384u) tile_bytes = 16384u;
+    }
     uint32_t stage = 0;
     uint32_t tiles = 0;
     for (int j = 0; j < p.njobs; ++j) {
@@ -399,16 +411,12 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     }
     p.total_tiles = tiles;
     if (tiles == 0) return cudaSuccess;
-    const uint32_t cols = p.cols;
-    // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
-    const uint32_t act_bytes =
-        mode == 2 ? (cols + cols / 16) * 4 + cols / 32 * 4 : cols + cols / 4 + cols / 32 * 16;
     // A standalone small launch (not a programmatic dependent inside a decode step) runs up
     // to 3 CTAs per SM with 64 KB rings; the others 2 CTAs per SM with 96 KB rings.
     const bool three = !p.pdl && !big;
     p.stage_bytes = stage + 16;
     p.use_tma = 1;
-    int ns = (int)((three ? 65536 : (big ? 98400 : 98304)) / p.stage_bytes);
+    int ns = (int)((three ? 65536 : (big ? 2 * p.stage_bytes : 98304)) / p.stage_bytes);
     if (ns > 8) ns = 8;
     if (ns < 2) {
         ns = 2;
