@@ -381,7 +381,10 @@ cudaError_t launch_gemv(GemvParams &p, int mode, cudaStream_t st) {
     // tiles in row multiples that keep every stage start 16-byte aligned.
     uint64_t bytes = 0;
     for (int j = 0; j < p.njobs; ++j) bytes += p.job[j].rows * p.job[j].rb;
-    const bool big = bytes >= GEMV_BIG_BYTES;
+    // A programmatic dependent inside a decode step with rows of 4096 columns or more streams
+    // its tiles as a big launch from 8 MB (C4's q/k/v and output projections: +6 % tokens/s;
+    // C5's 2048-column projections were 3 % slower that way).
+    const bool big = bytes >= (p.pdl && p.cols >= 4096 ? (8ull << 20) : GEMV_BIG_BYTES);
     const uint32_t cols = p.cols;
     // activation area (bank-spread): fp32 x + per-32 sums, or q8 values + d + 32-sums + 16-sums
     const uint32_t act_bytes =
