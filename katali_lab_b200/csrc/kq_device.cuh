@@ -522,6 +522,35 @@ __device__ __forceinline__ float byte_as_float(uint32_t w, int k, float bias2p23
 constexpr float TWO23 = 8388608.0f;         // 2^23
 constexpr float TWO23_P32 = 8388640.0f;     // 2^23 + 32 (Q6_K values are stored + 32)
 
+// Two fp32 values in one 64-bit register, for sm_100's packed f32x2 instructions: each element
+// of fma.rn.f32x2 / sub.rn.f32x2 is exactly fmaf / __fsub_rn on that element, so two independent
+// accumulation chains advance in one instruction with the same results.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2_pack(float a, float b) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(f32x2 v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ f32x2 f2_sub(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// byte_as_float of byte k of wa and of wb, as one pair.
+__device__ __forceinline__ f32x2 bytes_as_f2(uint32_t wa, uint32_t wb, int k, f32x2 bias2) {
+    return f2_sub(f2_pack(__int_as_float((int)__byte_perm(wa, 0x4B000000u, 0x7440u | (uint32_t)k)),
+                          __int_as_float((int)__byte_perm(wb, 0x4B000000u, 0x7440u | (uint32_t)k))),
+                  bias2);
+}
+
 __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const float *x,
                                                const float *xs, int pad = 0) {
     const int b = u >> 2, c = u & 3;
@@ -531,21 +560,21 @@ __device__ __forceinline__ double q4k_f32_unit(const uint8_t *row, int u, const 
     const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
     const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     const float *xl = x + fpos(pad, 256 * b + 64 * c);
-    float lo = 0.0f, hi = 0.0f;
+    // lo (low nibbles, first 32 elements) and hi (high nibbles, next 32) as one pair
+    const f32x2 bias = f2_pack(TWO23, TWO23);
+    f32x2 acc = f2_pack(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 xa = *reinterpret_cast<const float4 *>(xl + 4 * i);
         const float4 xb = *reinterpret_cast<const float4 *>(xl + 32 + 4 * i);
         const uint32_t wl = ww[i] & 0x0F0F0F0Fu, wh = (ww[i] >> 4) & 0x0F0F0F0Fu;
-        lo = fmaf(byte_as_float(wl, 0, TWO23), xa.x, lo);
-        hi = fmaf(byte_as_float(wh, 0, TWO23), xb.x, hi);
-        lo = fmaf(byte_as_float(wl, 1, TWO23), xa.y, lo);
-        hi = fmaf(byte_as_float(wh, 1, TWO23), xb.y, hi);
-        lo = fmaf(byte_as_float(wl, 2, TWO23), xa.z, lo);
-        hi = fmaf(byte_as_float(wh, 2, TWO23), xb.z, hi);
-        lo = fmaf(byte_as_float(wl, 3, TWO23), xa.w, lo);
-        hi = fmaf(byte_as_float(wh, 3, TWO23), xb.w, hi);
+        acc = f2_fma(bytes_as_f2(wl, wh, 0, bias), f2_pack(xa.x, xb.x), acc);
+        acc = f2_fma(bytes_as_f2(wl, wh, 1, bias), f2_pack(xa.y, xb.y), acc);
+        acc = f2_fma(bytes_as_f2(wl, wh, 2, bias), f2_pack(xa.z, xb.z), acc);
+        acc = f2_fma(bytes_as_f2(wl, wh, 3, bias), f2_pack(xa.w, xb.w), acc);
     }
+    float lo, hi;
+    f2_unpack(acc, lo, hi);
     int sc0, m0, sc1, m1;
     q4k_scales(h, c, sc0, m0, sc1, m1);
     const float d = h2f(h.x), dmin = h2f(h.x >> 16);
@@ -566,23 +595,25 @@ __device__ __forceinline__ double q6k_f32_unit(const uint8_t *row, int u, const 
     const float *xA = x + fpos(pad, 256 * b + 128 * h + 32 * qo);
     const float *xB = x + fpos(pad, 256 * b + 128 * h + 32 * qo + 64);
     const int shA = 2 * qo, shB = 2 * qo + 4;
-    float fA[2] = {0.0f, 0.0f}, fB[2] = {0.0f, 0.0f};
+    // quarter qo (A) and quarter qo + 2 (B) as one pair, per 16-element half: acc[0] over
+    // elements 0-15 of each quarter, acc[1] over 16-31
+    const f32x2 bias = f2_pack(TWO23_P32, TWO23_P32);
+    f32x2 acc[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const uint32_t vA = (ql[i] & 0x0F0F0F0Fu) | (((qh[i] >> shA) & 0x03030303u) << 4);
         const uint32_t vB = ((ql[i] >> 4) & 0x0F0F0F0Fu) | (((qh[i] >> shB) & 0x03030303u) << 4);
         const float4 a4 = *reinterpret_cast<const float4 *>(xA + 4 * i);
         const float4 b4 = *reinterpret_cast<const float4 *>(xB + 4 * i);
-        float &fa = fA[i >> 2], &fb = fB[i >> 2];
-        fa = fmaf(byte_as_float(vA, 0, TWO23_P32), a4.x, fa);
-        fa = fmaf(byte_as_float(vA, 1, TWO23_P32), a4.y, fa);
-        fa = fmaf(byte_as_float(vA, 2, TWO23_P32), a4.z, fa);
-        fa = fmaf(byte_as_float(vA, 3, TWO23_P32), a4.w, fa);
-        fb = fmaf(byte_as_float(vB, 0, TWO23_P32), b4.x, fb);
-        fb = fmaf(byte_as_float(vB, 1, TWO23_P32), b4.y, fb);
-        fb = fmaf(byte_as_float(vB, 2, TWO23_P32), b4.z, fb);
-        fb = fmaf(byte_as_float(vB, 3, TWO23_P32), b4.w, fb);
+        f32x2 &ab = acc[i >> 2];
+        ab = f2_fma(bytes_as_f2(vA, vB, 0, bias), f2_pack(a4.x, b4.x), ab);
+        ab = f2_fma(bytes_as_f2(vA, vB, 1, bias), f2_pack(a4.y, b4.y), ab);
+        ab = f2_fma(bytes_as_f2(vA, vB, 2, bias), f2_pack(a4.z, b4.z), ab);
+        ab = f2_fma(bytes_as_f2(vA, vB, 3, bias), f2_pack(a4.w, b4.w), ab);
     }
+    float fA[2], fB[2];
+    f2_unpack(acc[0], fA[0], fB[0]);
+    f2_unpack(acc[1], fA[1], fB[1]);
     const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
     const float d = h2f(ld_u16(blk + 208));
     return ((double)(d * (float)sc[2 * qo]) * (double)fA[0] +
