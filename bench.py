@@ -355,7 +355,7 @@ def run_ours(args, rank, world, local_rank):
     us_per_call = 1e3 * ms / (args.steps * reps * T)
 
     if args.trace and rank == 0:
-        print_trace(plugin, layers, xs, lgs, ys, T, L, args.warm)
+        print_trace(plugin, layers, xs, lgs, ys, T, L, args.warm, mode=mode)
 
     # ---- e2e through the C ABI with host buffers --------------------------
     import ctypes as C
@@ -456,7 +456,7 @@ EP_TRACE_NAMES = {**TRACE_NAMES, 1: "slots stored", 11: "pairs received", 18: "r
 
 
 def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False, call=None, names=TRACE_NAMES,
-                tag="[trace]"):
+                tag="[trace]", mode=None):
     """Phase timeline of the fused MoE kernel from its %globaltimer trace (ns). `call(i)`
     runs layer call i (default: the single-GPU layer on token i)."""
     import torch
@@ -470,7 +470,7 @@ def print_trace(plugin, layers, xs, lgs, ys, T, L, warm=False, call=None, names=
         lay = layers[i % L]
         grid = lay.set_trace(buf)
         if call is None:
-            lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1)
+            lay.forward(xs[i], lgs[i], ys[i], MOE_Q8_1 if mode is None else mode)
         else:
             call(i)
         plugin.sync()

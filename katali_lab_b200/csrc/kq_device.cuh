@@ -628,8 +628,8 @@ __device__ __forceinline__ double unit_q8(const uint8_t *row, int u, const ActQ8
 }
 template <uint32_t T>
 __device__ __forceinline__ double unit_f32(const uint8_t *row, int u, const float *x,
-                                           const float *xs) {
-    return T == T_Q4_K ? q4k_f32_unit(row, u, x, xs) : q6k_f32_unit(row, u, x);
+                                           const float *xs, int pad = 0) {
+    return T == T_Q4_K ? q4k_f32_unit(row, u, x, xs, pad) : q6k_f32_unit(row, u, x, pad);
 }
 
 // One warp per row: this lane's double partial over units lane, lane+32, ...

@@ -501,7 +501,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *xd = reinterpret_cast<float *>(act + 5 * H);
     int *xs32 = reinterpret_cast<int *>(xd + H / 32);
     int *xs16 = xs32 + H / 32;
-    float *xfs = reinterpret_cast<float *>(act + 4 * H);  // fp32 mode: per-32 sums
+    // fp32 mode: x bank-spread (element i at fpos(1, i): 16 bytes of padding after every 64
+    // floats, so the lanes' 64-element units fall on distinct banks), then the per-32 sums
+    float *xfs = reinterpret_cast<float *>(act + (MODE == 1 ? 4 * (H + H / 16) : 4 * H));
+    auto xfi = [&](int i) { return MODE == 1 ? fpos(1, i) : i; };
     int npairs = K, nrounds = 1;
     int nbar = 0;        // grid barriers passed
     uint32_t sbase = 0;  // thread 0: the barrier counter at launch (sync_base)
@@ -591,7 +594,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             xv.y = __fmul_rn(__fmul_rn(xv.y, inv), nw.y);
             xv.z = __fmul_rn(__fmul_rn(xv.z, inv), nw.z);
             xv.w = __fmul_rn(__fmul_rn(xv.w, inv), nw.w);
-            reinterpret_cast<float4 *>(xf)[tid] = xv;
+            *reinterpret_cast<float4 *>(xf + xfi(4 * tid)) = xv;
         }
 #pragma unroll
         for (int i = 0; i < MOE_RT_ROWS; ++i) {
@@ -633,7 +636,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             reinterpret_cast<uint4 *>(s_tab)[i] = __ldg(reinterpret_cast<const uint4 *>(p.experts) + i);
         pdl_wait();
         for (int i = tid - 32; i < H / 4; i += MOE_THREADS - 32)
-            reinterpret_cast<float4 *>(xf)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
+            *reinterpret_cast<float4 *>(xf + xfi(4 * i)) = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
     }
     if constexpr (!EP) __syncthreads();
     trace(p, 2);
@@ -754,7 +757,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             stage_x(rd);
         } else if (warp > 0) {
             for (int g = warp - 1; g < H / 32; g += MOE_WARPS - 1) {
-                const float v = xf[32 * g + lane];
+                const float v = xf[xfi(32 * g + lane)];
                 if (MODE == 0) {
                     quant_block_q8(v, lane, xq + 32 * g, xd + g, xs32 + g, xs16 + 2 * g, nullptr);
                 } else {
@@ -793,8 +796,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             pg0 = q4k_q8_partial(g0, nbh, ax, lane);
             pu0 = q4k_q8_partial(u0, nbh, ax, lane);
         } else {
-            pg0 = q4k_f32_partial(g0, nbh, xf, xfs, lane);
-            pu0 = q4k_f32_partial(u0, nbh, xf, xfs, lane);
+            pg0 = q4k_f32_partial(g0, nbh, xf, xfs, lane, 1);
+            pu0 = q4k_f32_partial(u0, nbh, xf, xfs, lane, 1);
         }
         ok &= mbar_wait_warp(&bars[a * NCH + p1 / HCH], 0);
         if (a == 0) trace(p, 12);
@@ -805,8 +808,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             pg1 = q4k_q8_partial(g1, nbh, ax, lane);
             pu1 = q4k_q8_partial(u1, nbh, ax, lane);
         } else {
-            pg1 = q4k_f32_partial(g1, nbh, xf, xfs, lane);
-            pu1 = q4k_f32_partial(u1, nbh, xf, xfs, lane);
+            pg1 = q4k_f32_partial(g1, nbh, xf, xfs, lane, 1);
+            pu1 = q4k_f32_partial(u1, nbh, xf, xfs, lane, 1);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -928,8 +931,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *hd = reinterpret_cast<float *>(hact + (size_t)K * (F + 16));
     int *hs32 = reinterpret_cast<int *>(hd + (size_t)K * F / 32);
     int *hs16 = hs32 + (size_t)K * F / 32;
-    float *hf = reinterpret_cast<float *>(hact);
-    float *hfs = hf + (size_t)K * F;
+    float *hf = reinterpret_cast<float *>(hact);  // fp32 mode: bank-spread as x
+    float *hfs = hf + (size_t)K * F + (size_t)K * F / 16;
     if (MODE == 0) {
         const int nrec = (int)BA;
         const int nun = F / 64;
@@ -950,10 +953,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     } else {
         for (int t = tid; t < K * F / 4; t += MOE_THREADS)
-            reinterpret_cast<float4 *>(hf)[t] = __ldcg(reinterpret_cast<const float4 *>(p.hbuf) + t);
+            *reinterpret_cast<float4 *>(hf + fpos(1, 4 * t)) = __ldcg(reinterpret_cast<const float4 *>(p.hbuf) + t);
         __syncthreads();
         for (int g = warp; g < K * F / 32; g += MOE_WARPS) {
-            const float s = warp_sum_f(hf[32 * g + lane]);
+            const float s = warp_sum_f(hf[fpos(1, 32 * g + lane)]);
             if (lane == 0) hfs[g] = s;
         }
     }
@@ -1068,7 +1071,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                         const uint8_t *row = sb + (size_t)k * (per + 16) + (size_t)rr * rbd;
                         for (int u = g; u < nunits; u += lpe) {
                             if (MODE == 0) part += unit_q8<DT>(row, u, ah);
-                            else part += unit_f32<DT>(row, u, hf + (size_t)k * F, hfs + (size_t)k * F / 32);
+                            else part += unit_f32<DT>(row, u, hf + fpos(1, k * F), hfs + (size_t)k * F / 32, 1);
                         }
                     }
                 }
@@ -1126,10 +1129,10 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     const uint32_t qpc = (Q + grid - 1) / grid;
     p.sb_bytes = (uint32_t)p.K * (rg * qpc * p.rbd + 16);
     p.act_off = al128(p.sb_off + p.sb_bytes);
-    const uint32_t act = p.mode == 0 ? 5 * p.H + p.H / 32 * 16 : 4 * p.H + p.H / 32 * 4;
+    const uint32_t act = p.mode == 0 ? 5 * p.H + p.H / 32 * 16 : 4 * (p.H + p.H / 16) + p.H / 32 * 4;
     p.hact_off = al128(p.act_off + act);
     const uint32_t KF = (uint32_t)p.K * p.F;
-    const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16 : KF * 4 + KF / 32 * 4;
+    const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16 : 4 * (KF + KF / 16) + KF / 32 * 4;
     p.misc_off = al128(p.hact_off + hact);
     const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * BAR_SLOTS +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
