@@ -144,7 +144,7 @@ struct MoeParams {
     uint32_t sa_bytes;     // phase-A staging capacity
     uint32_t sb_off, sb_bytes;
     uint32_t act_off, hact_off, misc_off, smem_bytes;
-    uint32_t dec_off, dec_row_bytes;  // decoded int8 down rows (q8_1 mode, Q6_K)
+    uint32_t dec_off, dec_row_bytes;  // decoded 6-bit down rows (Q6_K), read by phase B
     uint32_t dec_bytes;               // their area (dec_off == 0: inside the phase-A staging)
     uint32_t sdot_off;                // phase-B per-expert row dots [K][rows]
     int dec_enabled;

@@ -103,6 +103,49 @@ __device__ __forceinline__ double dec_q8_unit(const uint8_t *drow, int F, int u,
            ((double)d * (double)a.d[2 * u + 1]) * (double)I1;
 }
 
+// fp32-activation phase B: the lanes of one expert take a row's units in the order 0, 2, 4, ...
+// then 1, 3, 5, ... (i-th unit -> this unit), so that lanes reading x at the same time start on
+// different banks (units 2j and 2j + 1 are 32 floats apart: the same bank).
+__device__ __forceinline__ int f32_unit(int i, int nunits) {
+    const int half = nunits >> 1;
+    return (i % half) * 2 + i / half;
+}
+// The fp32-activation Q6_K unit u (block b = u/4, half h, quarter pair {qo, qo+2}: the unit
+// of q6k_f32_unit) from an element-order decoded row (16-byte aligned 6-bit values, sub-scales,
+// d per block): the same terms in the same order, so the same result.
+__device__ __forceinline__ double dec_f32_unit(const uint8_t *drow, int F, int u, const float *x) {
+    const int b = u >> 2, h = (u >> 1) & 1, qo = u & 1;
+    const int eA = 256 * b + 128 * h + 32 * qo, eB = eA + 64;
+    const uint4 a0 = *reinterpret_cast<const uint4 *>(drow + eA);
+    const uint4 a1 = *reinterpret_cast<const uint4 *>(drow + eA + 16);
+    const uint4 b0 = *reinterpret_cast<const uint4 *>(drow + eB);
+    const uint4 b1 = *reinterpret_cast<const uint4 *>(drow + eB + 16);
+    const uint32_t vA[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t vB[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float *xA = x + fpos(1, eA), *xB = x + fpos(1, eB);
+    const f32x2 bias = f2_pack(TWO23_P32, TWO23_P32);
+    f32x2 acc[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 a4 = *reinterpret_cast<const float4 *>(xA + 4 * i);
+        const float4 b4 = *reinterpret_cast<const float4 *>(xB + 4 * i);
+        f32x2 &ab = acc[i >> 2];
+        ab = f2_fma(bytes_as_f2(vA[i], vB[i], 0, bias), f2_pack(a4.x, b4.x), ab);
+        ab = f2_fma(bytes_as_f2(vA[i], vB[i], 1, bias), f2_pack(a4.y, b4.y), ab);
+        ab = f2_fma(bytes_as_f2(vA[i], vB[i], 2, bias), f2_pack(a4.z, b4.z), ab);
+        ab = f2_fma(bytes_as_f2(vA[i], vB[i], 3, bias), f2_pack(a4.w, b4.w), ab);
+    }
+    float fA[2], fB[2];
+    f2_unpack(acc[0], fA[0], fB[0]);
+    f2_unpack(acc[1], fA[1], fB[1]);
+    const int8_t *sc = reinterpret_cast<const int8_t *>(drow + F) + 16 * b + 8 * h;
+    const float d = reinterpret_cast<const float *>(drow + F + F / 16)[b];
+    return ((double)(d * (float)sc[2 * qo]) * (double)fA[0] +
+            (double)(d * (float)sc[2 * qo + 1]) * (double)fA[1]) +
+           ((double)(d * (float)sc[2 * qo + 4]) * (double)fB[0] +
+            (double)(d * (float)sc[2 * qo + 5]) * (double)fB[1]);
+}
+
 __device__ __forceinline__ void mbar_inval(uint64_t *bar) {
     asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -868,10 +911,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
             stage_x(rd + 1);
         }
     }
-    const bool predecode = MODE == 0 && DT == T_Q6_K && p.dec_enabled && nrB != 0;
+    const bool predecode = DT == T_Q6_K && p.dec_enabled && nrB != 0;
     // Phase B's expert-major path (F a power of two from 256 to 2048) reads h and the
     // decoded down rows in chunk-major order; the row-major path in element order.
-    const bool xmaj = predecode && (F == 256 || F == 512 || F == 1024 || F == 2048);
+    const bool xmaj = predecode && MODE == 0 && (F == 256 || F == 512 || F == 1024 || F == 2048);
     uint8_t *sdec = smem + p.dec_off;
     const uint32_t drb = p.dec_row_bytes;
     const uint32_t dstride = nrB * drb + 16;  // padded decoded expert stride
@@ -931,8 +974,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     float *hd = reinterpret_cast<float *>(hact + (size_t)K * (F + 16));
     int *hs32 = reinterpret_cast<int *>(hd + (size_t)K * F / 32);
     int *hs16 = hs32 + (size_t)K * F / 32;
-    float *hf = reinterpret_cast<float *>(hact);  // fp32 mode: bank-spread as x
-    float *hfs = hf + (size_t)K * F + (size_t)K * F / 16;
+    // fp32 mode: h bank-spread as x, each expert's part skewed by a further 4 floats per expert
+    float *hf = reinterpret_cast<float *>(hact);
+    float *hfs = hf + (size_t)K * F + (size_t)K * F / 16 + 4 * (size_t)K;
+    auto hfi = [&](int e) { return fpos(1, e) + 4 * (e / F); };
     if (MODE == 0) {
         const int nrec = (int)BA;
         const int nun = F / 64;
@@ -953,10 +998,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     } else {
         for (int t = tid; t < K * F / 4; t += MOE_THREADS)
-            *reinterpret_cast<float4 *>(hf + fpos(1, 4 * t)) = __ldcg(reinterpret_cast<const float4 *>(p.hbuf) + t);
+            *reinterpret_cast<float4 *>(hf + hfi(4 * t)) = __ldcg(reinterpret_cast<const float4 *>(p.hbuf) + t);
         __syncthreads();
         for (int g = warp; g < K * F / 32; g += MOE_WARPS) {
-            const float s = warp_sum_f(hf[fpos(1, 32 * g + lane)]);
+            const float s = warp_sum_f(hf[hfi(32 * g + lane)]);
             if (lane == 0) hfs[g] = s;
         }
     }
@@ -1066,12 +1111,15 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
                 if (k < K) {
                     if (predecode) {
                         const uint8_t *drow = sdec + (size_t)k * dstride + (size_t)rr * drb;
-                        for (int u = g; u < nunits; u += lpe) part += dec_q8_unit(drow, F, u, ah);
+                        for (int i = g; i < nunits; i += lpe)
+                            part += MODE == 0 ? dec_q8_unit(drow, F, i, ah)
+                                              : dec_f32_unit(drow, F, f32_unit(i, nunits), hf + hfi(k * F));
                     } else {
                         const uint8_t *row = sb + (size_t)k * (per + 16) + (size_t)rr * rbd;
                         for (int u = g; u < nunits; u += lpe) {
                             if (MODE == 0) part += unit_q8<DT>(row, u, ah);
-                            else part += unit_f32<DT>(row, u, hf + fpos(1, k * F), hfs + (size_t)k * F / 32, 1);
+                            else part += unit_f32<DT>(row, f32_unit(u, nunits), hf + hfi(k * F),
+                                                      hfs + (size_t)k * F / 32, 1);
                         }
                     }
                 }
@@ -1132,20 +1180,21 @@ int moe_plan(MoeParams &p, int grid, int max_smem) {
     const uint32_t act = p.mode == 0 ? 5 * p.H + p.H / 32 * 16 : 4 * (p.H + p.H / 16) + p.H / 32 * 4;
     p.hact_off = al128(p.act_off + act);
     const uint32_t KF = (uint32_t)p.K * p.F;
-    const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16 : 4 * (KF + KF / 16) + KF / 32 * 4;
+    const uint32_t hact = p.mode == 0 ? KF + 16 * (uint32_t)p.K + KF / 32 * 16
+                                      : 4 * (KF + KF / 16 + 4 * (uint32_t)p.K) + KF / 32 * 4;
     p.misc_off = al128(p.hact_off + hact);
     const uint32_t misc = 24 * (((uint32_t)p.n_experts + 1) & ~1u) + 8 * BAR_SLOTS +
                           8 * MOE_MAX_K + 4 * MAX_ABLK * HB + MAX_ABLK * REC_BYTES +
                           4 * (uint32_t)p.n_experts + 12 * MOE_EP_MAX_PAIRS + 16 + 8 * MOE_EP_MAX_SLOTS + 16;
     p.sdot_off = al128(p.misc_off + misc);
     p.smem_bytes = al128(p.sdot_off + 4 * (uint32_t)p.K * rg * qpc);
-    // Decoded int8 down rows (Q6_K, q8_1 mode): reuse the phase-A staging area
+    // Decoded down rows (Q6_K, both activation modes): reuse the phase-A staging area
     // when it is large enough (phase A is finished by then), else append.
     p.dec_off = 0;
     p.dec_enabled = 0;
     p.dec_bytes = 0;
     p.dec_row_bytes = (uint32_t)((p.F + p.F / 16 + 4 * (p.F / 256) + 15) & ~15);
-    if (p.mode == 0 && p.down_type == T_Q6_K) {
+    if (p.down_type == T_Q6_K) {
         const uint32_t need = (uint32_t)p.K * (rg * qpc * p.dec_row_bytes + 16);
         p.dec_bytes = need;
         if (need <= p.sa_bytes) {
