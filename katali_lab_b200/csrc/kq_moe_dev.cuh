@@ -158,14 +158,17 @@ __device__ __forceinline__ void route_weights_regs(const MoeParams &p, int lane,
                                                    const int32_t *s_ids, float *s_w) {
     const int n = p.n_experts, K = p.K;
     const int npl = (n + 31) >> 5;
-    float mine = 0.0f;  // lane t < K: the t-th chosen logit
-    for (int t = 0; t < K; ++t) {
-        const int id = s_ids[t], slot = id % npl;
-        float f = lv[0];
+    // lane t < K: the t-th chosen logit, fetched from its owner lane by eight independent
+    // shuffles (one per register slot) and a select
+    float mine = 0.0f;
+    {
+        const int id = lane < K ? s_ids[lane] : 0, src = id / npl, slot = id % npl;
 #pragma unroll
-        for (int j = 1; j < 8; ++j) f = slot == j ? lv[j] : f;
-        f = __shfl_sync(KQ_FULL, f, id / npl);
-        if (lane == t) mine = f;
+        for (int j = 0; j < 8; ++j) {
+            const float v = __shfl_sync(KQ_FULL, lv[j], src);
+            mine = slot == j ? v : mine;
+        }
+        if (lane >= K) mine = 0.0f;
     }
     const float m = __shfl_sync(KQ_FULL, mine, 0);
     double S = 0.0;
