@@ -943,6 +943,15 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
         }
     }
     trace(p, 14);
+    if constexpr (EP == 2) {
+        // the round's weights (the sources store them after the ids), read while thread 0
+        // waits at the barrier
+        if (warp == 1 && lane < KR) {
+            const int i = rd * K + lane, sl = s_pslot[i], k = __float_as_int(s_pw[i]);
+            const uint64_t *wa = ep2_tslot(p, p.ep_rank, ep_e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_W + k;
+            s_pw[i] = __uint_as_float(poll_tagged(wa, ep_e, p.status));
+        }
+    }
     if (tid == 0) grid_wait(p, sbase + (uint32_t)(nbar + 1) * G);
     ++nbar;
     __syncthreads();
@@ -950,12 +959,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_kernel(const __grid_consta
     if (EP && rd == 0) trace(p, 26);
     if constexpr (EP == 2) {
         if (rd == nrounds - 1) ep2_done();
-        // the round's weights: the sources store them after the ids, so they are read only now
-        if (warp == 1 && lane < KR) {
-            const int i = rd * K + lane, sl = s_pslot[i], k = __float_as_int(s_pw[i]);
-            const uint64_t *wa = ep2_tslot(p, p.ep_rank, ep_e, sl / p.ep_tmax, sl % p.ep_tmax) + EPT_W + k;
-            s_pw[i] = __uint_as_float(poll_tagged(wa, ep_e, p.status));
-        }
     }
     if (pre && warp == 0) {  // round rd + 1's down rows: every thread has decoded round rd's
         if (lane == 0) {
