@@ -1359,15 +1359,6 @@ def main():
             line = run_c5(args, rank, world, local_rank)
         elif world > 1 and not args.replicas:
             line = run_ep(args, rank, world, local_rank)
-            if args.config == "c2" and not args.nccl and not args.trace and not args.no_secondary:
-                # the same job as independent replicas (every GPU holds all experts), beside it
-                rep = run_ours(args, rank, world, local_rank)
-                if rank == 0 and line is not None and rep is not None:
-                    line["replicas"] = {
-                        "value": rep["value"], "unit": rep["unit"],
-                        "us_per_layer": rep["config"].get("us_per_layer"),
-                        "what": "the same job with all experts on every GPU: independent single-GPU "
-                                "layers, no exchange (bench.py --replicas)"}
         elif args.config == "c3":
             line = run_c3(args, rank, world, local_rank)
         else:
