@@ -207,7 +207,7 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
     unsigned char *xq = take(T * H), *xd = take(4 * T * H / 32), *xs32 = take(4 * T * H / 32),
                   *xs16 = take(4 * T * H / 16);
     unsigned char *ge = take(4 * E), *go = take(4 * (E + 1)), *ps = take(4 * P),
-                  *po = take(4 * P);
+                  *po = take(4 * P), *tcg = take(4 * E);
     unsigned char *h = take(4 * P * F), *hq = take(P * F), *hd = take(4 * P * F / 32),
                   *hs32 = take(4 * P * F / 32), *hs16 = take(4 * P * F / 16);
     unsigned char *part = take(4 * P * H);
@@ -220,6 +220,7 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
         b->xs16 = (int *)xs16;
         b->grp_expert = (int *)ge;
         b->grp_off = (int *)go;
+        b->tc_groups = (int *)tcg;
         b->n_groups = (int *)ng;
         b->work = (uint32_t *)(ng + 4);
         b->pair_src = (int *)ps;
@@ -608,13 +609,18 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
     b.rbd = pl.rbd;
     b.status = g_status_dev;
     b.sms = g_num_sms;
-    // Groups of >= 16 tokens run gate/up on the tensor cores (Q4_K gate and up only);
-    // KATALI_CUDA_NO_TC=1 keeps every group on the DP4A kernels.
+    // Groups of >= 16 tokens run gate/up on the tensor cores (Q4_K gate and up only) and
+    // the down projection there too (Q6_K down whose 128-row tile fits the kernel's
+    // staging); KATALI_CUDA_NO_TC=1 keeps every group on the DP4A kernels.
     const char *no_tc = getenv("KATALI_CUDA_NO_TC");
-    b.tc_min = (pl.gate_type == KATALI_TYPE_Q4_K && pl.up_type == KATALI_TYPE_Q4_K && pl.F % 128 == 0 &&
-                !(no_tc && no_tc[0] == '1'))
+    const bool tc = !(no_tc && no_tc[0] == '1');
+    b.tc_min = (pl.gate_type == KATALI_TYPE_Q4_K && pl.up_type == KATALI_TYPE_Q4_K && pl.F % 128 == 0 && tc)
                    ? 16
                    : 0;
+    b.tc_down_min = (pl.down_type == KATALI_TYPE_Q6_K && pl.H % 128 == 0 &&
+                     128ull * pl.rbd <= kq::TC_DOWN_RAW_MAX && tc)
+                        ? 16
+                        : 0;
     return b;
 }
 

@@ -197,7 +197,8 @@ struct MoeBatchParams {
     float *xd;
     int *xs32, *xs16;
     int *grp_expert, *grp_off, *n_groups, *pair_src, *pos_of;
-    uint32_t *work;  // item counters of the gate/up and down kernels, zeroed by the group kernel
+    uint32_t *work;  // item counters of the gate/up and down kernels, zeroed by the group kernel;
+                     // work[2]: the number of listed tensor-core groups
     float *h;
     int8_t *hq;
     float *hd;
@@ -225,6 +226,8 @@ struct MoeBatchParams {
     uint32_t *ep_epoch;  // calls completed by this rank (the next call is *ep_epoch + 1)
     uint32_t *ep_done;   // last-CTA counters of the three peer kernels
     int tc_min;          // groups with >= tc_min tokens: gate/up on the tensor cores (0: never)
+    int tc_down_min;     // groups with >= tc_down_min tokens: down on the tensor cores (0: never)
+    int *tc_groups;      // indices of the groups with >= min(positive tc thresholds) tokens; count in work[2]
     const int32_t *ids_in;  // routing given (ids / weights [T][K]) instead of logits
     const float *w_in;
 };
@@ -254,6 +257,9 @@ constexpr int EPT_ROW = 1 + 2 * MOE_MAX_K;
 inline uint32_t ep_tslot_words(uint32_t H) { return EPT_ROW + H / 32 * 9; }
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st);
 void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st);
+void launch_down_tc(MoeBatchParams &p, int max_groups, cudaStream_t st);
+// Largest raw row tile (128 rows of the down matrix) the tensor-core down kernel stages.
+constexpr uint32_t TC_DOWN_RAW_MAX = 96 * 1024;
 cudaError_t launch_moe_ep_dispatch(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_experts(MoeBatchParams &p, cudaStream_t st);
 cudaError_t launch_moe_ep_combine(MoeBatchParams &p, cudaStream_t st);

@@ -156,20 +156,27 @@ __device__ void group_body(const MoeBatchParams &p, int *cnt, int *off, int *wsu
     for (int i = threadIdx.x; i < P; i += blockDim.x)
         if (p.ids[i] >= 0) atomicAdd(&cnt[p.ids[i]], 1);
     __syncthreads();
-    int c = 0, nz = 0;
+    // Groups the tensor-core kernels take (n >= the smaller of their positive thresholds)
+    // are also listed, in group order, so those kernels size their work to them.
+    const int thr = p.tc_min > 0 && (p.tc_down_min <= 0 || p.tc_min <= p.tc_down_min) ? p.tc_min
+                                                                                      : p.tc_down_min;
+    int c = 0, nz = 0, ntc = 0;
     for (int e = e0; e < e0 + epT && e < E; ++e) {
         c += cnt[e];
         nz += cnt[e] > 0;
+        ntc += thr > 0 && cnt[e] >= thr;
     }
-    int total, ngroups;
+    int total, ngroups, ntcg;
     int o = block_exscan(c, wsum, total);
     int gi = block_exscan(nz, wsum, ngroups);
+    int ti = block_exscan(ntc, wsum, ntcg);
     for (int e = e0; e < e0 + epT && e < E; ++e) {
         const int ce = cnt[e];
         off[e] = o;
         if (ce > 0) {
             p.grp_expert[gi] = e;
             p.grp_off[gi] = o;
+            if (thr > 0 && ce >= thr) p.tc_groups[ti++] = gi;
             ++gi;
         }
         o += ce;
@@ -181,6 +188,7 @@ __device__ void group_body(const MoeBatchParams &p, int *cnt, int *off, int *wsu
         *p.n_groups = ngroups;
         p.work[0] = 0u;  // the item counters of this call's gate/up and down kernels
         p.work[1] = 0u;
+        p.work[2] = (uint32_t)ntcg;  // listed tensor-core groups
     }
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {
@@ -468,10 +476,11 @@ __device__ bool down_items(const MoeBatchParams &p, const ItemSmem &S, int *s_ne
         const uint32_t next = next_item_async(&p.work[1]);
         const int g = it / nrb, rb = it % nrb;
         const int e = p.grp_expert[g], p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+        const bool tc = p.tc_down_min > 0 && p1 - p0 >= p.tc_down_min;  // the tensor-core kernel takes it
         const bool resident = p.experts[3 * e + 2] != nullptr;
         if (!resident && threadIdx.x == 0 && p.status)  // not resident: report, skip
             atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
-        if (p1 <= p0 || !resident) {
+        if (p1 <= p0 || tc || !resident) {
             it = hand_over_item(next, s_next, st.slot);
             continue;
         }
@@ -821,7 +830,7 @@ static void plan_tiles(MoeBatchParams &p) {
 
 // group -> gate/up -> h quantisation -> down for the pairs in p.ids (T = tokens or slots).
 // pdl: every launch a programmatic dependent of the one before (each kernel waits for its
-// predecessor before its first statement); the tensor-core gate/up launch stays ordinary.
+// predecessor before its first statement); the tensor-core gate/up and down launches stay ordinary.
 static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st, int pdl = 0) {
     plan_tiles(p);
     launch_k(moe_batch_group, dim3(1), dim3((p.n_experts + 31) / 32 * 32), 0, st, pdl, p);
@@ -844,6 +853,7 @@ static void launch_experts(MoeBatchParams &p, int max_groups, cudaStream_t st, i
         launch_items(moe_batch_down<T_Q6_K>, ditems, dsm, p.sms, p, st, pdl);
     else
         launch_items(moe_batch_down<T_Q4_K>, ditems, dsm, p.sms, p, st, pdl);
+    if (p.tc_down_min > 0) launch_down_tc(p, max_groups, st);
 }
 
 cudaError_t launch_moe_batch(MoeBatchParams &p, cudaStream_t st) {

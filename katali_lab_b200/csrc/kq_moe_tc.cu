@@ -11,14 +11,22 @@
 // in fp32 per block (the DP4A kernels use exact double terms; this path rounds
 // each block term to fp32, within the layer tolerance).
 //
-// CTA = (group, 128-row tile), 4 warps; per token tile of 32 and per super-block
-// of 256 columns: cp.async the 128 raw gate and up rows (144 B each) -> unpack to
-// int8 in the canonical no-swizzle K-major layout (core matrices of 8 rows x
-// 16 B: LBO 128 B between the two K halves, SBO 256 B between 8-row groups) with
-// the per-row block scales -> stage the tokens' q8_1 values the same way ->
-// thread 0 issues 16 MMAs (8 chunks x gate/up) into separate TMEM columns and
-// commits to an mbarrier -> each warp reads its 32 TMEM lanes (= rows) and
-// accumulates. TMEM: 16 chunks x 32 columns = 512 columns, allocated once per CTA.
+// CTA = (group, 128-row tile), 16 warps. Warp w serves TMEM lanes 32*(w%4)..+31
+// (the rows of its quadrant) in role w/4: gate or up, tokens 0..15 or 16..31 of
+// the token tile. Per token tile of 32 and per super-block b of 256 columns:
+//   * the copies of super-block b+1 (raw gate and up rows, 144 B each; the tokens'
+//     q8_1 values in the canonical no-swizzle K-major layout of the B operand; their
+//     block scales and sums) go out with cp.async into the other half of a double
+//     buffer before b is unpacked, so they land while b is computed;
+//   * unpack row r of one matrix (two of its four chunk pairs) to int8 in the
+//     canonical no-swizzle K-major layout (core matrices of 8 rows x 16 B: LBO 128 B
+//     between the two K halves, SBO 256 B between 8-row groups) with its block scales;
+//   * thread 0 issues 16 MMAs (8 chunks x gate/up) into separate TMEM columns and
+//     commits to an mbarrier;
+//   * each thread reads its row's 16 tokens of its matrix (tcgen05.ld) and accumulates.
+// The up sums meet the gate sums in shared memory for h = silu(g) * u. TMEM: 16 chunks
+// x 32 columns = 512 columns, allocated once per CTA. Each token's arithmetic is the
+// same sequence of fp32 operations for any warp split.
 #include <cuda_runtime.h>
 
 #include "kq_device.cuh"
@@ -28,21 +36,27 @@ namespace kq {
 
 namespace {
 
-constexpr int TC_THREADS = 128;
+constexpr int TC_THREADS = 512;
 constexpr int TC_NT = 32;  // tokens per tile (MMA N)
 constexpr int TC_ROWS = 128;  // rows per tile (MMA M)
 constexpr int TC_COLS = 512;  // TMEM columns: 2 matrices x 8 chunks x 32
 constexpr uint32_t A_CHUNK = TC_ROWS * 32;  // 4096 B: one 128 x 32 int8 operand
 constexpr uint32_t B_CHUNK = TC_NT * 32;    // 1024 B
+constexpr uint32_t RAW_BYTES = 2 * TC_ROWS * 144;  // one super-block of 128 gate + 128 up rows
+constexpr uint32_t XR_BYTES = 2 * TC_NT * 8 * 4;   // d [32][8] f32, then block sums [32][8] s32
 
 // Shared-memory plan (bytes from the dynamic base, 1024-aligned).
-constexpr uint32_t OFF_AG = 0;                        // 8 chunks of gate A
-constexpr uint32_t OFF_AU = OFF_AG + 8 * A_CHUNK;     // 8 chunks of up A
-constexpr uint32_t OFF_B = OFF_AU + 8 * A_CHUNK;      // 8 chunks of B
-constexpr uint32_t OFF_RAW = OFF_B + 8 * B_CHUNK;     // raw rows: 128 gate + 128 up, 144 B each
-constexpr uint32_t OFF_SC = OFF_RAW + 2 * TC_ROWS * 144;  // S_g, M_g, S_u, M_u: [8][128] floats each
-constexpr uint32_t OFF_TOK = OFF_SC + 4 * 8 * TC_ROWS * 4;  // DX[32][8], XS[32][8] floats
-constexpr uint32_t TC_SMEM = OFF_TOK + 2 * TC_NT * 8 * 4;
+constexpr uint32_t OFF_AG = 0;                          // 8 chunks of gate A
+constexpr uint32_t OFF_AU = OFF_AG + 8 * A_CHUNK;       // 8 chunks of up A
+constexpr uint32_t OFF_B = OFF_AU + 8 * A_CHUNK;        // 2 buffers x 8 chunks of B
+constexpr uint32_t OFF_RAW = OFF_B + 2 * 8 * B_CHUNK;   // 2 buffers of raw rows
+constexpr uint32_t OFF_XR = OFF_RAW + 2 * RAW_BYTES;    // 2 buffers of token scales as copied
+constexpr uint32_t OFF_SC = OFF_XR + 2 * XR_BYTES;      // S_g, M_g, S_u, M_u: [8][128] floats each
+constexpr uint32_t OFF_DX = OFF_SC + 4 * 8 * TC_ROWS * 4;  // DX[8][32], XS[8][32] floats
+constexpr uint32_t OFF_UP = OFF_DX + 2 * 8 * TC_NT * 4;  // up sums [32][128] floats
+constexpr uint32_t OFF_TOK = OFF_UP + TC_NT * TC_ROWS * 4;  // the tile's token indices
+constexpr uint32_t TC_SMEM = OFF_TOK + TC_NT * 4;
+static_assert(TC_SMEM <= 227 * 1024, "shared-memory plan");
 
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr) {
     // start address >> 4, LBO 128 B, SBO 256 B, version 1, no swizzle
@@ -67,9 +81,47 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
           "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(addr));
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_pending() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // Canonical offset of the 16-byte piece (row r, K half h) inside one operand chunk.
 __device__ __forceinline__ uint32_t canon(int r, int h) { return (r >> 3) * 256 + h * 128 + (r & 7) * 16; }
+
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7])
+                 : "r"(addr));
+}
+// 32 bytes of shared memory at a 2-byte aligned address as 8 words: nine aligned word
+// loads, funnel-shifted into place.
+__device__ __forceinline__ void ld32_unaligned(const uint8_t *src, uint32_t (&out)[8]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(src);
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+    const uint32_t sh = (uint32_t)(a & 3) * 8;
+    uint32_t x[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) x[i] = w[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = __funnelshift_r(x[i], x[i + 1], sh);
+}
+
+// Down projection plan (bytes from the dynamic base): A holds, per 32-wide chunk c of a
+// Q6_K super-block, two operands: 2c with the chunk's first 16 values and zeros in its
+// second K half, 2c + 1 with zeros in its first K half and the last 16 values (each
+// half has its own 16-element scale). The zero halves are written once per CTA.
+constexpr uint32_t OFF_DA = 0;                           // 16 operands of 128 x 32 int8
+constexpr uint32_t OFF_DB = OFF_DA + 16 * A_CHUNK;       // 2 buffers x 8 chunks of B
+constexpr uint32_t OFF_DXR = OFF_DB + 2 * 8 * B_CHUNK;   // 2 buffers of h block scales [32][8]
+constexpr uint32_t OFF_DDX = OFF_DXR + 2 * TC_NT * 8 * 4;  // DX [8][32]
+constexpr uint32_t OFF_DRAW = OFF_DDX + 8 * TC_NT * 4;   // the raw 128-row tile
+constexpr uint32_t TC_DOWN_SMEM = OFF_DRAW + TC_DOWN_RAW_MAX + 16;
+static_assert(TC_DOWN_SMEM <= 227 * 1024, "shared-memory plan");
+static_assert(OFF_DRAW % 16 == 0, "bulk-copy destination");
 
 }  // namespace
 
@@ -77,23 +129,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ __align__(8) uint64_t bar;
     __shared__ uint32_t taddr_s;
-    const int ntile = p.F / TC_ROWS;
-    const int g = blockIdx.x / ntile, rt = blockIdx.x % ntile;
-    if (g >= *p.n_groups) return;
-    const int p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
-    if (p1 - p0 < p.tc_min) return;  // small groups: the DP4A kernel
-    const int e = p.grp_expert[g];
-    const uint8_t *G = p.experts[3 * e], *U = p.experts[3 * e + 1];
-    if (!G || !U) {
-        if (threadIdx.x == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
-        return;
-    }
+    // Work items (listed group, 128-row tile), CTA i taking items i, i + gridDim.x, ...
+    const int ntile = p.F / TC_ROWS, items = (int)p.work[2] * ntile;
+    if ((int)blockIdx.x >= items) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int r = tid;  // the row this thread unpacks and accumulates (TMEM lane)
-    const int j0 = rt * TC_ROWS, K = p.K, H = p.H, nb = H / 256;
+    const int quad = warp & 3, m = (warp >> 2) & 1, th = warp >> 3;  // lane quadrant, matrix, token half
+    const int r = 32 * quad + lane;  // the row this thread unpacks and accumulates (TMEM lane)
+    const int K = p.K, H = p.H, nb = H / 256;
     float *S_g = reinterpret_cast<float *>(sm + OFF_SC), *M_g = S_g + 8 * TC_ROWS;
     float *S_u = M_g + 8 * TC_ROWS, *M_u = S_u + 8 * TC_ROWS;
-    float *DX = reinterpret_cast<float *>(sm + OFF_TOK), *XS = DX + TC_NT * 8;
+    float *DX = reinterpret_cast<float *>(sm + OFF_DX), *XS = DX + 8 * TC_NT;  // [chunk][token]
+    float *UP = reinterpret_cast<float *>(sm + OFF_UP);
+    int *tok = reinterpret_cast<int *>(sm + OFF_TOK);
 
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)));
@@ -111,142 +158,408 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
     uint32_t phase = 0;
     bool ok = true;
 
-    for (int t0 = p0; t0 < p1; t0 += TC_NT) {
-        const int nt = min(TC_NT, p1 - t0);
-        float ag[TC_NT], au[TC_NT];
-#pragma unroll
-        for (int t = 0; t < TC_NT; ++t) ag[t] = au[t] = 0.0f;
-        for (int b = 0; b < nb; ++b) {
-            // raw rows of super-block b: 128 gate + 128 up rows x 144 B (9 x 16 B each)
-            uint8_t *raw = sm + OFF_RAW;
-            for (int i = tid; i < 2 * TC_ROWS * 9; i += TC_THREADS) {
-                const int m = i / (TC_ROWS * 9), rr = (i / 9) % TC_ROWS, q = i % 9;
-                const uint8_t *src = (m ? U + (size_t)(j0 + rr) * p.rbu : G + (size_t)(j0 + rr) * p.rbg) +
-                                     (size_t)b * Q4K_BYTES + 16 * q;
-                cp_async16(raw + (size_t)(m * TC_ROWS + rr) * 144 + 16 * q, src);
-            }
-            // B: the tile's tokens' q8_1 values of the 8 blocks of super-block b
-            for (int i = tid; i < TC_NT * 8 * 2; i += TC_THREADS) {
-                const int t = i / 16, c = (i / 2) % 8, h = i % 2;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (t < nt) {
-                    const int tok = p.pair_src[t0 + t] / K;
-                    v = *reinterpret_cast<const uint4 *>(p.xq + (size_t)tok * H + 256 * b + 32 * c + 16 * h);
-                }
-                *reinterpret_cast<uint4 *>(sm + OFF_B + c * B_CHUNK + canon(t, h)) = v;
-            }
-            for (int i = tid; i < TC_NT * 8; i += TC_THREADS) {
-                const int t = i / 8, c = i % 8;
-                float dx = 0.0f, xs = 0.0f;
-                if (t < nt) {
-                    const int tok = p.pair_src[t0 + t] / K, blk = 8 * b + c;
-                    dx = p.xd[(size_t)tok * (H / 32) + blk];
-                    xs = __fmul_rn(dx, (float)p.xs32[(size_t)tok * (H / 32) + blk]);
-                }
-                DX[t * 8 + c] = dx;
-                XS[t * 8 + c] = xs;
-            }
-            cp_async_wait_all();
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const int g = p.tc_groups[it / ntile], j0 = (it % ntile) * TC_ROWS;
+        const int p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+        if (p.tc_min <= 0 || p1 - p0 < p.tc_min) continue;  // small groups: the DP4A kernel
+        const int e = p.grp_expert[g];
+        const uint8_t *G = p.experts[3 * e], *U = p.experts[3 * e + 1];
+        if (!G || !U) {
+            if (tid == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+            continue;
+        }
+        for (int t0 = p0; t0 < p1 && ok; t0 += TC_NT) {
+            const int nt = min(TC_NT, p1 - t0);
+            if (tid < nt) tok[tid] = p.pair_src[t0 + tid] / K;
             __syncthreads();
-            // unpack row r of gate and up: nibbles -> int8 chunks, block scales
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-                const uint8_t *blk = raw + (size_t)(m * TC_ROWS + r) * 144;
-                const uint4 h = *reinterpret_cast<const uint4 *>(blk);
-                uint8_t *A = sm + (m ? OFF_AU : OFF_AG);
-                float *S = m ? S_u : S_g, *M = m ? M_u : M_g;
-                const float d = h2f(h.x), dmin = h2f(h.x >> 16);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
-                    const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
-                    const uint32_t MK = 0x0F0F0F0Fu;
-                    *reinterpret_cast<uint4 *>(A + (2 * c) * A_CHUNK + canon(r, 0)) =
-                        make_uint4(w0.x & MK, w0.y & MK, w0.z & MK, w0.w & MK);
-                    *reinterpret_cast<uint4 *>(A + (2 * c) * A_CHUNK + canon(r, 1)) =
-                        make_uint4(w1.x & MK, w1.y & MK, w1.z & MK, w1.w & MK);
-                    *reinterpret_cast<uint4 *>(A + (2 * c + 1) * A_CHUNK + canon(r, 0)) =
-                        make_uint4((w0.x >> 4) & MK, (w0.y >> 4) & MK, (w0.z >> 4) & MK, (w0.w >> 4) & MK);
-                    *reinterpret_cast<uint4 *>(A + (2 * c + 1) * A_CHUNK + canon(r, 1)) =
-                        make_uint4((w1.x >> 4) & MK, (w1.y >> 4) & MK, (w1.z >> 4) & MK, (w1.w >> 4) & MK);
-                    int sc0, m0, sc1, m1;
-                    q4k_scales(h, c, sc0, m0, sc1, m1);
-                    S[(2 * c) * TC_ROWS + r] = __fmul_rn(d, (float)sc0);
-                    M[(2 * c) * TC_ROWS + r] = __fmul_rn(dmin, (float)m0);
-                    S[(2 * c + 1) * TC_ROWS + r] = __fmul_rn(d, (float)sc1);
-                    M[(2 * c + 1) * TC_ROWS + r] = __fmul_rn(dmin, (float)m1);
+            // The copies of super-block b into buffer buf: raw rows, the B operand (tokens
+            // >= nt keep stale values; their columns are never read back) and the tokens'
+            // block scales and sums of the 8 blocks.
+            auto issue = [&](int b, int buf) {
+                uint8_t *raw = sm + OFF_RAW + buf * RAW_BYTES;
+                for (int i = tid; i < 2 * TC_ROWS * 9; i += TC_THREADS) {
+                    const int mm = i / (TC_ROWS * 9), rr = (i / 9) % TC_ROWS, q = i % 9;
+                    const uint8_t *src = (mm ? U + (size_t)(j0 + rr) * p.rbu : G + (size_t)(j0 + rr) * p.rbg) +
+                                         (size_t)b * Q4K_BYTES + 16 * q;
+                    cp_async16(raw + (size_t)(mm * TC_ROWS + rr) * 144 + 16 * q, src);
                 }
-            }
-            // make the generic-proxy shared-memory writes visible to the tensor cores
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncthreads();
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            if (tid == 0) {
-                const uint32_t sa_g = smem_u32(sm + OFF_AG), sa_u = smem_u32(sm + OFF_AU);
-                const uint32_t sb = smem_u32(sm + OFF_B);
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint64_t db = umma_sdesc(sb + c * B_CHUNK);
-                    umma_i8(taddr + c * TC_NT, umma_sdesc(sa_g + c * A_CHUNK), db);
-                    umma_i8(taddr + 256 + c * TC_NT, umma_sdesc(sa_u + c * A_CHUNK), db);
+                uint8_t *B = sm + OFF_B + buf * 8 * B_CHUNK;
+                for (int i = tid; i < nt * 16; i += TC_THREADS) {
+                    const int t = i / 16, c = (i / 2) % 8, h = i % 2;
+                    cp_async16(B + c * B_CHUNK + canon(t, h), p.xq + (size_t)tok[t] * H + 256 * b + 32 * c + 16 * h);
                 }
-                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 smem_u32(&bar))
-                             : "memory");
-            }
-            // bounded wait for this super-block's MMAs; the verdict is the CTA's, not a thread's
-            uint32_t done = 0;
-            for (uint32_t it = 0; it < SPIN_LIMIT && !done; ++it) {
-                done = mbar_try_wait(&bar, phase) ? 1u : 0u;
-                if (!done && it > 64) __nanosleep(64);
-            }
-            phase ^= 1u;
-            if (!__syncthreads_and(done)) {
-                ok = false;
-                break;
-            }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            // accumulate: this warp's 32 TMEM lanes are rows 32*warp .. +31
-            const uint32_t lane_base = taddr + ((uint32_t)(32 * warp) << 16);
-#pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
-                const float sg = S_g[c * TC_ROWS + r], mg = M_g[c * TC_ROWS + r];
-                const float su = S_u[c * TC_ROWS + r], mu = M_u[c * TC_ROWS + r];
+                uint8_t *xr = sm + OFF_XR + buf * XR_BYTES;
+                for (int i = tid; i < nt * 4; i += TC_THREADS) {
+                    const int t = i / 4, k = i % 4;  // k 0, 1: halves of the 8 scales; 2, 3: of the 8 sums
+                    const size_t at = (size_t)tok[t] * (H / 32) + 8 * b + 4 * (k & 1);
+                    const void *src = k < 2 ? static_cast<const void *>(p.xd + at) : static_cast<const void *>(p.xs32 + at);
+                    cp_async16(xr + (k >> 1) * (XR_BYTES / 2) + t * 32 + 16 * (k & 1), src);
+                }
+                cp_async_commit();
+            };
+            float acc[16];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t vg[16], vu[16];
-                    tmem_ld16(lane_base + c * TC_NT + 16 * half, vg);
-                    tmem_ld16(lane_base + 256 + c * TC_NT + 16 * half, vu);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int q = 0; q < 16; ++q) acc[q] = 0.0f;
+            issue(0, 0);
+            for (int b = 0; b < nb; ++b) {
+                const int buf = b & 1;
+                if (b + 1 < nb) {
+                    issue(b + 1, buf ^ 1);
+                    cp_async_wait_pending<1>();
+                } else {
+                    cp_async_wait_pending<0>();
+                }
+                __syncthreads();  // super-block b's copies from every thread are in
+                if (tid < 8 * TC_NT) {  // token scales as [chunk][token]; xsum terms dx * s32
+                    const int c = tid / TC_NT, t = tid % TC_NT;
+                    const float *xd = reinterpret_cast<const float *>(sm + OFF_XR + buf * XR_BYTES);
+                    const int *xs = reinterpret_cast<const int *>(sm + OFF_XR + buf * XR_BYTES + XR_BYTES / 2);
+                    float dx = 0.0f, sx = 0.0f;
+                    if (t < nt) {
+                        dx = xd[t * 8 + c];
+                        sx = __fmul_rn(dx, (float)xs[t * 8 + c]);
+                    }
+                    DX[c * TC_NT + t] = dx;
+                    XS[c * TC_NT + t] = sx;
+                }
+                // unpack row r of matrix m, chunk pairs 2*th and 2*th + 1: nibbles -> int8, block scales
+                {
+                    const uint8_t *blk = sm + OFF_RAW + buf * RAW_BYTES + (size_t)(m * TC_ROWS + r) * 144;
+                    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+                    uint8_t *A = sm + (m ? OFF_AU : OFF_AG);
+                    float *S = m ? S_u : S_g, *M = m ? M_u : M_g;
+                    const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) {
-                        const int t = 16 * half + q;
-                        const float dx = DX[t * 8 + c], xs = XS[t * 8 + c];
-                        ag[t] = fmaf(__fmul_rn(sg, dx), (float)(int)vg[q], fmaf(-mg, xs, ag[t]));
-                        au[t] = fmaf(__fmul_rn(su, dx), (float)(int)vu[q], fmaf(-mu, xs, au[t]));
+                    for (int cc = 0; cc < 2; ++cc) {
+                        const int c = 2 * th + cc;
+                        const uint4 w0 = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * c);
+                        const uint4 w1 = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * c);
+                        const uint32_t MK = 0x0F0F0F0Fu;
+                        *reinterpret_cast<uint4 *>(A + (2 * c) * A_CHUNK + canon(r, 0)) =
+                            make_uint4(w0.x & MK, w0.y & MK, w0.z & MK, w0.w & MK);
+                        *reinterpret_cast<uint4 *>(A + (2 * c) * A_CHUNK + canon(r, 1)) =
+                            make_uint4(w1.x & MK, w1.y & MK, w1.z & MK, w1.w & MK);
+                        *reinterpret_cast<uint4 *>(A + (2 * c + 1) * A_CHUNK + canon(r, 0)) =
+                            make_uint4((w0.x >> 4) & MK, (w0.y >> 4) & MK, (w0.z >> 4) & MK, (w0.w >> 4) & MK);
+                        *reinterpret_cast<uint4 *>(A + (2 * c + 1) * A_CHUNK + canon(r, 1)) =
+                            make_uint4((w1.x >> 4) & MK, (w1.y >> 4) & MK, (w1.z >> 4) & MK, (w1.w >> 4) & MK);
+                        int sc0, m0, sc1, m1;
+                        q4k_scales(hd, c, sc0, m0, sc1, m1);
+                        S[(2 * c) * TC_ROWS + r] = __fmul_rn(d, (float)sc0);
+                        M[(2 * c) * TC_ROWS + r] = __fmul_rn(dmin, (float)m0);
+                        S[(2 * c + 1) * TC_ROWS + r] = __fmul_rn(d, (float)sc1);
+                        M[(2 * c + 1) * TC_ROWS + r] = __fmul_rn(dmin, (float)m1);
                     }
                 }
-            }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            __syncthreads();  // shared memory and TMEM are reused by the next super-block
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        }
-        if (!ok) break;
+                // make the generic-proxy shared-memory writes visible to the tensor cores
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncthreads();
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                if (tid == 0) {
+                    const uint32_t sa_g = smem_u32(sm + OFF_AG), sa_u = smem_u32(sm + OFF_AU);
+                    const uint32_t sb = smem_u32(sm + OFF_B + buf * 8 * B_CHUNK);
 #pragma unroll
-        for (int t = 0; t < TC_NT; ++t)
-            if (t < nt) p.h[(size_t)(t0 + t) * p.F + j0 + r] = __fmul_rn(kq_silu(ag[t]), au[t]);
+                    for (int c = 0; c < 8; ++c) {
+                        const uint64_t db = umma_sdesc(sb + c * B_CHUNK);
+                        umma_i8(taddr + c * TC_NT, umma_sdesc(sa_g + c * A_CHUNK), db);
+                        umma_i8(taddr + 256 + c * TC_NT, umma_sdesc(sa_u + c * A_CHUNK), db);
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(&bar))
+                                 : "memory");
+                }
+                // bounded wait for this super-block's MMAs; the verdict is the CTA's, not a thread's
+                uint32_t done = 0;
+                for (uint32_t it = 0; it < SPIN_LIMIT && !done; ++it) {
+                    done = mbar_try_wait(&bar, phase) ? 1u : 0u;
+                    if (!done && it > 64) __nanosleep(64);
+                }
+                phase ^= 1u;
+                if (!__syncthreads_and(done)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                // accumulate tokens 16*th .. +15 of matrix m for row r (TMEM lane r)
+                {
+                    const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 256 * m + 16 * th;
+                    const float *S = m ? S_u : S_g, *M = m ? M_u : M_g;
+#pragma unroll 1
+                    for (int c = 0; c < 8; c += 2) {
+                        uint32_t v0[16], v1[16];
+                        tmem_ld16(col + c * TC_NT, v0);
+                        tmem_ld16(col + (c + 1) * TC_NT, v1);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const float sc = S[(c + cc) * TC_ROWS + r], mn = M[(c + cc) * TC_ROWS + r];
+                            const float4 *dx4 = reinterpret_cast<const float4 *>(DX + (c + cc) * TC_NT + 16 * th);
+                            const float4 *xs4 = reinterpret_cast<const float4 *>(XS + (c + cc) * TC_NT + 16 * th);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const float4 dx = dx4[k], xs = xs4[k];
+                                const float dv[4] = {dx.x, dx.y, dx.z, dx.w}, xv[4] = {xs.x, xs.y, xs.z, xs.w};
+#pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    const int i = 4 * k + q;
+                                    const uint32_t iv = cc ? v1[i] : v0[i];
+                                    acc[i] = fmaf(__fmul_rn(sc, dv[q]), (float)(int)iv, fmaf(-mn, xv[q], acc[i]));
+                                }
+                            }
+                        }
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncthreads();  // A, the scales and TMEM are reused by the next super-block
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            }
+            if (!ok) break;
+            if (m == 1) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) UP[(16 * th + q) * TC_ROWS + r] = acc[q];
+            }
+            __syncthreads();
+            if (m == 0) {
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                    const int t = 16 * th + q;
+                    if (t < nt) p.h[(size_t)(t0 + t) * p.F + j0 + r] = __fmul_rn(kq_silu(acc[q]), UP[t * TC_ROWS + r]);
+                }
+            }
+        }
     }
+    cp_async_wait_all();  // a stopped CTA leaves no copy in flight
     if (!ok && tid == 0 && p.status) atomicOr((uint32_t *)p.status, 4u);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(TC_COLS));
 }
 
+// ---------------------------------------------------------------------------
+// Down projection on the tensor cores: part[pair][row] for the pairs of groups with
+// n >= p.tc_down_min tokens, Q6_K rows (values q - 32 in -32..31 are int8) against
+// the pairs' q8_1 h. One q8_1 block (32 values) spans two Q6_K scale groups, so each
+// chunk takes two M=128 x N=32 x K=32 MMAs over half-zeroed operands, giving the exact
+// per-group sums I_lo, I_hi; the CUDA cores form I = sc_lo*I_lo + sc_hi*I_hi (exact:
+// |I| < 2^24) and accumulate (d*dx) * I in double. Each term is exact there (d*dx, a
+// product of two fp16, has 22 significant bits), the terms are added in the order of
+// the reference's Q6_K x q8_1 dot (super-block, then block) and the row rounds once to
+// fp32, so a row equals that dot for the same q8_1 h.
+// CTA = (group, 128-row tile of H) items, 16 warps: warp w serves TMEM lanes
+// 32*(w%4)..+31 for tokens 8*(w/4)..+7 and unpacks chunks 2*(w/4), 2*(w/4)+1. The raw
+// 128-row tile arrives in one bulk copy; the B operand and h scales of super-block b+1
+// are copied (cp.async, double buffer) while b is computed.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParams p) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    __shared__ __align__(8) uint64_t bar, tbar;
+    __shared__ uint32_t taddr_s;
+    const int nrt = p.H / TC_ROWS, items = (int)p.work[2] * nrt;  // (listed group, 128-row tile)
+    if ((int)blockIdx.x >= items) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, role = warp >> 2;
+    const int r = 32 * quad + lane;
+    const int F = p.F, nb = F / 256;
+    const uint32_t rbd = p.rbd;
+    uint8_t *raw = sm + OFF_DRAW;
+    float *DX = reinterpret_cast<float *>(sm + OFF_DDX);  // [chunk][token]
+
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&tbar)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // the zero K halves of the 16 operands
+    for (int i = tid; i < 8 * 2 * TC_ROWS; i += TC_THREADS) {
+        const int c = i / (2 * TC_ROWS), hi = (i / TC_ROWS) & 1, rr = i % TC_ROWS;
+        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c + hi) * A_CHUNK + canon(rr, hi ? 0 : 1)) =
+            make_uint4(0, 0, 0, 0);
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
+                     "r"(TC_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t taddr = taddr_s;
+    uint32_t phase = 0, tphase = 0;
+    bool ok = true;
+
+    for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const int g = p.tc_groups[it / nrt], j0 = (it % nrt) * TC_ROWS;
+        const int p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
+        if (p.tc_down_min <= 0 || p1 - p0 < p.tc_down_min) continue;  // small groups: the DP4A kernel
+        const uint8_t *D = p.experts[3 * p.grp_expert[g] + 2];
+        if (!D) {
+            if (tid == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
+            continue;
+        }
+        __syncthreads();  // the previous item's raw tile is no longer read
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t bytes = TC_ROWS * rbd;
+            mbar_arrive_expect_tx(&tbar, bytes);
+            bulk_g2s_hint(raw, D + (size_t)j0 * rbd, bytes, &tbar, l2_evict_first_policy());
+        }
+        bool tile_in = false;
+        for (int t0 = p0; t0 < p1 && ok; t0 += TC_NT) {
+            const int nt = min(TC_NT, p1 - t0);
+            auto issue = [&](int b, int buf) {
+                uint8_t *B = sm + OFF_DB + buf * 8 * B_CHUNK;
+                for (int i = tid; i < nt * 16; i += TC_THREADS) {
+                    const int t = i / 16, c = (i / 2) % 8, h = i % 2;
+                    cp_async16(B + c * B_CHUNK + canon(t, h), p.hq + (size_t)(t0 + t) * F + 256 * b + 32 * c + 16 * h);
+                }
+                uint8_t *xr = sm + OFF_DXR + buf * (TC_NT * 8 * 4);
+                for (int i = tid; i < nt * 2; i += TC_THREADS) {
+                    const int t = i / 2, k = i % 2;
+                    cp_async16(xr + t * 32 + 16 * k, p.hd + (size_t)(t0 + t) * (F / 32) + 8 * b + 4 * k);
+                }
+                cp_async_commit();
+            };
+            double acc[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[q] = 0.0;
+            issue(0, 0);
+            for (int b = 0; b < nb; ++b) {
+                const int buf = b & 1;
+                if (b + 1 < nb) {
+                    issue(b + 1, buf ^ 1);
+                    cp_async_wait_pending<1>();
+                } else {
+                    cp_async_wait_pending<0>();
+                }
+                __syncthreads();  // super-block b's copies from every thread are in
+                if (!tile_in) {
+                    const bool in = mbar_wait(&tbar, tphase);
+                    if (__syncthreads_or(!in)) {
+                        ok = false;
+                        break;
+                    }
+                    tphase ^= 1u;
+                    tile_in = true;
+                }
+                if (tid < 8 * TC_NT) {
+                    const int c = tid / TC_NT, t = tid % TC_NT;
+                    const float *xr = reinterpret_cast<const float *>(sm + OFF_DXR + buf * (TC_NT * 8 * 4));
+                    DX[c * TC_NT + t] = t < nt ? xr[t * 8 + c] : 0.0f;
+                }
+                // unpack row r, chunks 2*role and 2*role + 1 of super-block b: 6-bit values - 32
+                {
+                    const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
+#pragma unroll
+                    for (int cc = 0; cc < 2; ++cc) {
+                        const int c = 2 * role + cc, n = c >> 2, j = c & 3;
+                        uint32_t lo[8], hi[8], q[8];
+                        ld32_unaligned(blk + 64 * n + 32 * (j & 1), lo);
+                        ld32_unaligned(blk + 128 + 32 * n, hi);
+                        const int ns = 4 * (j >> 1), hs = 2 * j;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            q[i] = __vsub4(((lo[i] >> ns) & 0x0F0F0F0Fu) | (((hi[i] >> hs) & 0x03030303u) << 4),
+                                           0x20202020u);
+                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c) * A_CHUNK + canon(r, 0)) =
+                            make_uint4(q[0], q[1], q[2], q[3]);
+                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c + 1) * A_CHUNK + canon(r, 1)) =
+                            make_uint4(q[4], q[5], q[6], q[7]);
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncthreads();
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                if (tid == 0) {
+                    const uint32_t sa = smem_u32(sm + OFF_DA), sb = smem_u32(sm + OFF_DB + buf * 8 * B_CHUNK);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint64_t db = umma_sdesc(sb + c * B_CHUNK);
+                        umma_i8(taddr + (2 * c) * TC_NT, umma_sdesc(sa + (2 * c) * A_CHUNK), db);
+                        umma_i8(taddr + (2 * c + 1) * TC_NT, umma_sdesc(sa + (2 * c + 1) * A_CHUNK), db);
+                    }
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(&bar))
+                                 : "memory");
+                }
+                uint32_t done = 0;
+                for (uint32_t sp = 0; sp < SPIN_LIMIT && !done; ++sp) {
+                    done = mbar_try_wait(&bar, phase) ? 1u : 0u;
+                    if (!done && sp > 64) __nanosleep(64);
+                }
+                phase ^= 1u;
+                if (!__syncthreads_and(done)) {
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                // accumulate tokens 8*role .. +7 of row r
+                {
+                    const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
+                    const float d = h2f((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
+                    const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 8 * role;
+#pragma unroll 1
+                    for (int c = 0; c < 8; c += 2) {
+                        uint32_t l0[8], h0[8], l1[8], h1[8];
+                        tmem_ld8(col + (2 * c) * TC_NT, l0);
+                        tmem_ld8(col + (2 * c + 1) * TC_NT, h0);
+                        tmem_ld8(col + (2 * c + 2) * TC_NT, l1);
+                        tmem_ld8(col + (2 * c + 3) * TC_NT, h1);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int cc = 0; cc < 2; ++cc) {
+                            const int sl = (int)(int8_t)blk[192 + 2 * (c + cc)];
+                            const int sh = (int)(int8_t)blk[193 + 2 * (c + cc)];
+                            const float4 *dx4 = reinterpret_cast<const float4 *>(DX + (c + cc) * TC_NT + 8 * role);
+                            const float4 da = dx4[0], db = dx4[1];
+                            const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                const int I = sl * (int)(cc ? l1[q] : l0[q]) + sh * (int)(cc ? h1[q] : h0[q]);
+                                acc[q] = fma((double)__fmul_rn(d, dv[q]), (double)I, acc[q]);
+                            }
+                        }
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncthreads();  // A, B, the scales and TMEM are reused by the next super-block
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int t = 8 * role + q;
+                if (t < nt) p.part[(size_t)(t0 + t) * p.H + j0 + r] = (float)acc[q];
+            }
+        }
+    }
+    cp_async_wait_all();  // a stopped CTA leaves no copy in flight
+    if (!ok && tid == 0 && p.status) atomicOr((uint32_t *)p.status, 4u);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(TC_COLS));
+}
+
+// Persistent grids: one CTA per SM at most (each holds all 512 TMEM columns), never more
+// than the worst-case item count.
+static int tc_grid(const MoeBatchParams &p, int max_items) {
+    const int sms = p.sms > 0 ? p.sms : 1;
+    return max_items < sms ? max_items : sms;
+}
+
 void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
     static size_t set_bytes[KQ_MAX_DEVICES];
     ensure_smem_limit(moe_batch_gateup_tc, TC_SMEM, set_bytes);
-    moe_batch_gateup_tc<<<max_groups * (p.F / TC_ROWS), TC_THREADS, TC_SMEM, st>>>(p);
+    const int grid = tc_grid(p, max_groups * (p.F / TC_ROWS));
+    if (grid > 0) moe_batch_gateup_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(p);
+}
+
+void launch_down_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
+    static size_t set_bytes[KQ_MAX_DEVICES];
+    ensure_smem_limit(moe_batch_down_tc, TC_DOWN_SMEM, set_bytes);
+    const int grid = tc_grid(p, max_groups * (p.H / TC_ROWS));
+    if (grid > 0) moe_batch_down_tc<<<grid, TC_THREADS, TC_DOWN_SMEM, st>>>(p);
 }
 
 }  // namespace kq
