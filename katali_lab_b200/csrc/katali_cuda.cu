@@ -211,6 +211,7 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
     unsigned char *h = take(4 * P * F), *hq = take(P * F), *hd = take(4 * P * F / 32),
                   *hs32 = take(4 * P * F / 32), *hs16 = take(4 * P * F / 16);
     unsigned char *part = take(4 * P * H);
+    unsigned char *hu = take(4 * P * F), *ptc = take(P);
     if (b) {
         b->ids = (int32_t *)ids;
         b->w = (float *)w;
@@ -221,6 +222,8 @@ size_t moe_batch_layout(const kq::MoeParams &pl, int T, unsigned char *base, kq:
         b->grp_expert = (int *)ge;
         b->grp_off = (int *)go;
         b->tc_groups = (int *)tcg;
+        b->hu = (float *)hu;
+        b->pair_tc = (uint8_t *)ptc;
         b->n_groups = (int *)ng;
         b->work = (uint32_t *)(ng + 4);
         b->pair_src = (int *)ps;

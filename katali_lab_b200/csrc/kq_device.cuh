@@ -544,6 +544,11 @@ __device__ __forceinline__ f32x2 f2_sub(f32x2 a, f32x2 b) {
     asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
 // byte_as_float of byte k of wa and of wb, as one pair.
 __device__ __forceinline__ f32x2 bytes_as_f2(uint32_t wa, uint32_t wb, int k, f32x2 bias2) {
     return f2_sub(f2_pack(__int_as_float((int)__byte_perm(wa, 0x4B000000u, 0x7440u | (uint32_t)k)),

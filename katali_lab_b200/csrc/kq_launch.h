@@ -228,6 +228,8 @@ struct MoeBatchParams {
     int tc_min;          // groups with >= tc_min tokens: gate/up on the tensor cores (0: never)
     int tc_down_min;     // groups with >= tc_down_min tokens: down on the tensor cores (0: never)
     int *tc_groups;      // indices of the groups with >= min(positive tc thresholds) tokens; count in work[2]
+    float *hu;           // up sums of the pairs whose gate/up ran on the tensor cores (their gate sums in h)
+    uint8_t *pair_tc;    // per grouped pair: 1 when its gate/up ran on the tensor cores
     const int32_t *ids_in;  // routing given (ids / weights [T][K]) instead of logits
     const float *w_in;
 };

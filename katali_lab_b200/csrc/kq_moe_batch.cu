@@ -197,6 +197,8 @@ __device__ void group_body(const MoeBatchParams &p, int *cnt, int *off, int *wsu
         const int pos = off[ex] + atomicAdd(&cnt[ex], 1);
         p.pair_src[pos] = i;  // i = t * K + k
         p.pos_of[i] = pos;
+        const int n_ex = (ex + 1 < E ? off[ex + 1] : total) - off[ex];  // the expert's group size
+        p.pair_tc[pos] = p.tc_min > 0 && n_ex >= p.tc_min;
     }
 }
 
@@ -450,7 +452,9 @@ __device__ __forceinline__ void hquant_range(const MoeBatchParams &p, int w0, in
     const int P = p.grp_off[*p.n_groups];  // grouped pairs (<= T * K)
     for (int wg = w0; wg < P * nblk; wg += ws) {
         const int q = wg / nblk, b = wg % nblk;
-        const float v = p.h[(size_t)q * p.F + 32 * b + lane];
+        const size_t i = (size_t)q * p.F + 32 * b + lane;
+        // pairs whose gate/up ran on the tensor cores: h holds the gate sums, hu the up sums
+        const float v = p.pair_tc[q] ? __fmul_rn(kq_silu(p.h[i]), p.hu[i]) : p.h[i];
         quant_block_q8(v, lane, p.hq + (size_t)q * p.F + 32 * b, p.hd + (size_t)q * nblk + b,
                        p.hs32 + (size_t)q * nblk + b, p.hs16 + ((size_t)q * nblk + b) * 2, nullptr);
     }

@@ -36,27 +36,27 @@ namespace kq {
 
 namespace {
 
-constexpr int TC_THREADS = 512;
+constexpr int TC_THREADS = 512;    // down kernel: 16 warps, one CTA per SM
+constexpr int GU_THREADS = 256;    // gate/up kernel: 8 warps, two CTAs per SM
 constexpr int TC_NT = 32;  // tokens per tile (MMA N)
 constexpr int TC_ROWS = 128;  // rows per tile (MMA M)
-constexpr int TC_COLS = 512;  // TMEM columns: 2 matrices x 8 chunks x 32
+constexpr int TC_COLS = 512;  // down TMEM columns: 16 operands x 32
+constexpr int GU_COLS = 256;  // gate/up TMEM columns: 8 chunks x 32
 constexpr uint32_t A_CHUNK = TC_ROWS * 32;  // 4096 B: one 128 x 32 int8 operand
 constexpr uint32_t B_CHUNK = TC_NT * 32;    // 1024 B
-constexpr uint32_t RAW_BYTES = 2 * TC_ROWS * 144;  // one super-block of 128 gate + 128 up rows
-constexpr uint32_t XR_BYTES = 2 * TC_NT * 8 * 4;   // d [32][8] f32, then block sums [32][8] s32
+constexpr uint32_t RAW_BYTES = TC_ROWS * 144;     // one super-block of 128 rows of one matrix
+constexpr uint32_t XR_BYTES = 2 * TC_NT * 8 * 4;  // d [32][8] f32, then block sums [32][8] s32
 
-// Shared-memory plan (bytes from the dynamic base, 1024-aligned).
-constexpr uint32_t OFF_AG = 0;                          // 8 chunks of gate A
-constexpr uint32_t OFF_AU = OFF_AG + 8 * A_CHUNK;       // 8 chunks of up A
-constexpr uint32_t OFF_B = OFF_AU + 8 * A_CHUNK;        // 2 buffers x 8 chunks of B
-constexpr uint32_t OFF_RAW = OFF_B + 2 * 8 * B_CHUNK;   // 2 buffers of raw rows
-constexpr uint32_t OFF_XR = OFF_RAW + 2 * RAW_BYTES;    // 2 buffers of token scales as copied
-constexpr uint32_t OFF_SC = OFF_XR + 2 * XR_BYTES;      // S_g, M_g, S_u, M_u: [8][128] floats each
-constexpr uint32_t OFF_DX = OFF_SC + 4 * 8 * TC_ROWS * 4;  // DX[8][32], XS[8][32] floats
-constexpr uint32_t OFF_UP = OFF_DX + 2 * 8 * TC_NT * 4;  // up sums [32][128] floats
-constexpr uint32_t OFF_TOK = OFF_UP + TC_NT * TC_ROWS * 4;  // the tile's token indices
+// Gate/up shared-memory plan (bytes from the dynamic base, 1024-aligned).
+constexpr uint32_t OFF_A = 0;                             // 8 chunks of A
+constexpr uint32_t OFF_B = OFF_A + 8 * A_CHUNK;           // 2 buffers x 8 chunks of B
+constexpr uint32_t OFF_RAW = OFF_B + 2 * 8 * B_CHUNK;     // 2 buffers of raw rows
+constexpr uint32_t OFF_XR = OFF_RAW + 2 * RAW_BYTES;      // 2 buffers of token scales as copied
+constexpr uint32_t OFF_SC = OFF_XR + 2 * XR_BYTES;        // S, M: [8][128] floats each
+constexpr uint32_t OFF_DX = OFF_SC + 2 * 8 * TC_ROWS * 4;  // DX[8][32], XS[8][32] floats
+constexpr uint32_t OFF_TOK = OFF_DX + 2 * 8 * TC_NT * 4;  // the tile's token indices
 constexpr uint32_t TC_SMEM = OFF_TOK + TC_NT * 4;
-static_assert(TC_SMEM <= 227 * 1024, "shared-memory plan");
+static_assert(2 * (TC_SMEM + 2048) <= 228 * 1024, "two gate/up CTAs per SM");
 
 __device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr) {
     // start address >> 4, LBO 128 B, SBO 256 B, version 1, no swizzle
@@ -117,29 +117,28 @@ __device__ __forceinline__ void ld32_unaligned(const uint8_t *src, uint32_t (&ou
 constexpr uint32_t OFF_DA = 0;                           // 16 operands of 128 x 32 int8
 constexpr uint32_t OFF_DB = OFF_DA + 16 * A_CHUNK;       // 2 buffers x 8 chunks of B
 constexpr uint32_t OFF_DXR = OFF_DB + 2 * 8 * B_CHUNK;   // 2 buffers of h block scales [32][8]
-constexpr uint32_t OFF_DDX = OFF_DXR + 2 * TC_NT * 8 * 4;  // DX [8][32]
-constexpr uint32_t OFF_DRAW = OFF_DDX + 8 * TC_NT * 4;   // the raw 128-row tile
+constexpr uint32_t OFF_DDX = OFF_DXR + 2 * TC_NT * 8 * 4;  // DX [8][32] as doubles
+constexpr uint32_t OFF_DRAW = OFF_DDX + 8 * TC_NT * 8;   // the raw 128-row tile
 constexpr uint32_t TC_DOWN_SMEM = OFF_DRAW + TC_DOWN_RAW_MAX + 16;
 static_assert(TC_DOWN_SMEM <= 227 * 1024, "shared-memory plan");
 static_assert(OFF_DRAW % 16 == 0, "bulk-copy destination");
 
 }  // namespace
 
-__global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchParams p) {
+__global__ void __launch_bounds__(GU_THREADS, 2) moe_batch_gateup_tc(MoeBatchParams p) {
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ __align__(8) uint64_t bar;
     __shared__ uint32_t taddr_s;
-    // Work items (listed group, 128-row tile), CTA i taking items i, i + gridDim.x, ...
-    const int ntile = p.F / TC_ROWS, items = (int)p.work[2] * ntile;
+    // Work items (listed group, 128-row tile, matrix): gate and up of one tile are items
+    // 2i and 2i + 1; CTA j takes items j, j + gridDim.x, ...
+    const int ntile = p.F / TC_ROWS, items = (int)p.work[2] * ntile * 2;
     if ((int)blockIdx.x >= items) return;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, m = (warp >> 2) & 1, th = warp >> 3;  // lane quadrant, matrix, token half
+    const int quad = warp & 3, th = warp >> 2;  // lane quadrant, token half
     const int r = 32 * quad + lane;  // the row this thread unpacks and accumulates (TMEM lane)
     const int K = p.K, H = p.H, nb = H / 256;
-    float *S_g = reinterpret_cast<float *>(sm + OFF_SC), *M_g = S_g + 8 * TC_ROWS;
-    float *S_u = M_g + 8 * TC_ROWS, *M_u = S_u + 8 * TC_ROWS;
+    float *S = reinterpret_cast<float *>(sm + OFF_SC), *M = S + 8 * TC_ROWS;  // [chunk][row]
     float *DX = reinterpret_cast<float *>(sm + OFF_DX), *XS = DX + 8 * TC_NT;  // [chunk][token]
-    float *UP = reinterpret_cast<float *>(sm + OFF_UP);
     int *tok = reinterpret_cast<int *>(sm + OFF_TOK);
 
     if (tid == 0) {
@@ -148,7 +147,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
-                     "r"(TC_COLS));
+                     "r"(GU_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -159,15 +158,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
     bool ok = true;
 
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
-        const int g = p.tc_groups[it / ntile], j0 = (it % ntile) * TC_ROWS;
+        const int m = it & 1, ti = it >> 1;  // m: 0 gate, 1 up
+        const int g = p.tc_groups[ti / ntile], j0 = (ti % ntile) * TC_ROWS;
         const int p0 = p.grp_off[g], p1 = p.grp_off[g + 1];
         if (p.tc_min <= 0 || p1 - p0 < p.tc_min) continue;  // small groups: the DP4A kernel
-        const int e = p.grp_expert[g];
-        const uint8_t *G = p.experts[3 * e], *U = p.experts[3 * e + 1];
-        if (!G || !U) {
+        const uint8_t *W = p.experts[3 * p.grp_expert[g] + m];
+        const size_t rb = m ? p.rbu : p.rbg;
+        if (!W) {
             if (tid == 0 && p.status) atomicOr((uint32_t *)p.status, KQ_STATUS_NOT_RESIDENT);
             continue;
         }
+        float *out = m ? p.hu : p.h;  // pre-activation sums; the h quantiser forms silu(g) * u
         for (int t0 = p0; t0 < p1 && ok; t0 += TC_NT) {
             const int nt = min(TC_NT, p1 - t0);
             if (tid < nt) tok[tid] = p.pair_src[t0 + tid] / K;
@@ -177,19 +178,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
             // block scales and sums of the 8 blocks.
             auto issue = [&](int b, int buf) {
                 uint8_t *raw = sm + OFF_RAW + buf * RAW_BYTES;
-                for (int i = tid; i < 2 * TC_ROWS * 9; i += TC_THREADS) {
-                    const int mm = i / (TC_ROWS * 9), rr = (i / 9) % TC_ROWS, q = i % 9;
-                    const uint8_t *src = (mm ? U + (size_t)(j0 + rr) * p.rbu : G + (size_t)(j0 + rr) * p.rbg) +
-                                         (size_t)b * Q4K_BYTES + 16 * q;
-                    cp_async16(raw + (size_t)(mm * TC_ROWS + rr) * 144 + 16 * q, src);
+                for (int i = tid; i < TC_ROWS * 9; i += GU_THREADS) {
+                    const int rr = i / 9, q = i % 9;
+                    cp_async16(raw + (size_t)rr * 144 + 16 * q, W + (size_t)(j0 + rr) * rb + (size_t)b * Q4K_BYTES + 16 * q);
                 }
                 uint8_t *B = sm + OFF_B + buf * 8 * B_CHUNK;
-                for (int i = tid; i < nt * 16; i += TC_THREADS) {
+                for (int i = tid; i < nt * 16; i += GU_THREADS) {
                     const int t = i / 16, c = (i / 2) % 8, h = i % 2;
                     cp_async16(B + c * B_CHUNK + canon(t, h), p.xq + (size_t)tok[t] * H + 256 * b + 32 * c + 16 * h);
                 }
                 uint8_t *xr = sm + OFF_XR + buf * XR_BYTES;
-                for (int i = tid; i < nt * 4; i += TC_THREADS) {
+                for (int i = tid; i < nt * 4; i += GU_THREADS) {
                     const int t = i / 4, k = i % 4;  // k 0, 1: halves of the 8 scales; 2, 3: of the 8 sums
                     const size_t at = (size_t)tok[t] * (H / 32) + 8 * b + 4 * (k & 1);
                     const void *src = k < 2 ? static_cast<const void *>(p.xd + at) : static_cast<const void *>(p.xs32 + at);
@@ -197,9 +196,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                 }
                 cp_async_commit();
             };
-            float acc[16];
+            f32x2 acc[8];  // tokens 16*th + 2i, 16*th + 2i + 1
 #pragma unroll
-            for (int q = 0; q < 16; ++q) acc[q] = 0.0f;
+            for (int q = 0; q < 8; ++q) acc[q] = f2_pack(0.0f, 0.0f);
             issue(0, 0);
             for (int b = 0; b < nb; ++b) {
                 const int buf = b & 1;
@@ -210,7 +209,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                     cp_async_wait_pending<0>();
                 }
                 __syncthreads();  // super-block b's copies from every thread are in
-                if (tid < 8 * TC_NT) {  // token scales as [chunk][token]; xsum terms dx * s32
+                {  // token scales as [chunk][token]; xsum terms dx * s32
                     const int c = tid / TC_NT, t = tid % TC_NT;
                     const float *xd = reinterpret_cast<const float *>(sm + OFF_XR + buf * XR_BYTES);
                     const int *xs = reinterpret_cast<const int *>(sm + OFF_XR + buf * XR_BYTES + XR_BYTES / 2);
@@ -222,12 +221,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                     DX[c * TC_NT + t] = dx;
                     XS[c * TC_NT + t] = sx;
                 }
-                // unpack row r of matrix m, chunk pairs 2*th and 2*th + 1: nibbles -> int8, block scales
+                // unpack row r, chunk pairs 2*th and 2*th + 1: nibbles -> int8, block scales
                 {
-                    const uint8_t *blk = sm + OFF_RAW + buf * RAW_BYTES + (size_t)(m * TC_ROWS + r) * 144;
+                    const uint8_t *blk = sm + OFF_RAW + buf * RAW_BYTES + (size_t)r * 144;
                     const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-                    uint8_t *A = sm + (m ? OFF_AU : OFF_AG);
-                    float *S = m ? S_u : S_g, *M = m ? M_u : M_g;
+                    uint8_t *A = sm + OFF_A;
                     const float d = h2f(hd.x), dmin = h2f(hd.x >> 16);
 #pragma unroll
                     for (int cc = 0; cc < 2; ++cc) {
@@ -257,23 +255,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                 __syncthreads();
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 if (tid == 0) {
-                    const uint32_t sa_g = smem_u32(sm + OFF_AG), sa_u = smem_u32(sm + OFF_AU);
-                    const uint32_t sb = smem_u32(sm + OFF_B + buf * 8 * B_CHUNK);
+                    const uint32_t sa = smem_u32(sm + OFF_A), sb = smem_u32(sm + OFF_B + buf * 8 * B_CHUNK);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint64_t db = umma_sdesc(sb + c * B_CHUNK);
-                        umma_i8(taddr + c * TC_NT, umma_sdesc(sa_g + c * A_CHUNK), db);
-                        umma_i8(taddr + 256 + c * TC_NT, umma_sdesc(sa_u + c * A_CHUNK), db);
-                    }
+                    for (int c = 0; c < 8; ++c)
+                        umma_i8(taddr + c * TC_NT, umma_sdesc(sa + c * A_CHUNK), umma_sdesc(sb + c * B_CHUNK));
                     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                                      smem_u32(&bar))
                                  : "memory");
                 }
                 // bounded wait for this super-block's MMAs; the verdict is the CTA's, not a thread's
                 uint32_t done = 0;
-                for (uint32_t it = 0; it < SPIN_LIMIT && !done; ++it) {
+                for (uint32_t sp = 0; sp < SPIN_LIMIT && !done; ++sp) {
                     done = mbar_try_wait(&bar, phase) ? 1u : 0u;
-                    if (!done && it > 64) __nanosleep(64);
+                    if (!done && sp > 64) __nanosleep(64);
                 }
                 phase ^= 1u;
                 if (!__syncthreads_and(done)) {
@@ -281,10 +275,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                // accumulate tokens 16*th .. +15 of matrix m for row r (TMEM lane r)
+                // accumulate tokens 16*th .. +15 for row r (TMEM lane r); token pairs in packed
+                // f32x2 registers (each element the same fmaf / __fmul_rn sequence), the integer
+                // sums (|isum| < 2^22) converted exactly by an integer add under the exponent of
+                // 1.5 * 2^23 and one float subtraction
                 {
-                    const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 256 * m + 16 * th;
-                    const float *S = m ? S_u : S_g, *M = m ? M_u : M_g;
+                    const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 16 * th;
+                    const f32x2 magic = f2_pack(12582912.0f, 12582912.0f);
 #pragma unroll 1
                     for (int c = 0; c < 8; c += 2) {
                         uint32_t v0[16], v1[16];
@@ -294,17 +291,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
 #pragma unroll
                         for (int cc = 0; cc < 2; ++cc) {
                             const float sc = S[(c + cc) * TC_ROWS + r], mn = M[(c + cc) * TC_ROWS + r];
+                            const f32x2 sc2 = f2_pack(sc, sc), nm2 = f2_pack(-mn, -mn);
                             const float4 *dx4 = reinterpret_cast<const float4 *>(DX + (c + cc) * TC_NT + 16 * th);
                             const float4 *xs4 = reinterpret_cast<const float4 *>(XS + (c + cc) * TC_NT + 16 * th);
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
                                 const float4 dx = dx4[k], xs = xs4[k];
-                                const float dv[4] = {dx.x, dx.y, dx.z, dx.w}, xv[4] = {xs.x, xs.y, xs.z, xs.w};
 #pragma unroll
-                                for (int q = 0; q < 4; ++q) {
-                                    const int i = 4 * k + q;
-                                    const uint32_t iv = cc ? v1[i] : v0[i];
-                                    acc[i] = fmaf(__fmul_rn(sc, dv[q]), (float)(int)iv, fmaf(-mn, xv[q], acc[i]));
+                                for (int hp = 0; hp < 2; ++hp) {
+                                    const int i = 4 * k + 2 * hp;
+                                    const uint32_t ia = cc ? v1[i] : v0[i], ib = cc ? v1[i + 1] : v0[i + 1];
+                                    const f32x2 isf = f2_sub(f2_pack(__int_as_float((int)(ia + 0x4B400000u)),
+                                                                     __int_as_float((int)(ib + 0x4B400000u))),
+                                                             magic);
+                                    const f32x2 d2 = hp ? f2_pack(dx.z, dx.w) : f2_pack(dx.x, dx.y);
+                                    const f32x2 x2 = hp ? f2_pack(xs.z, xs.w) : f2_pack(xs.x, xs.y);
+                                    acc[i / 2] = f2_fma(f2_mul(sc2, d2), isf, f2_fma(nm2, x2, acc[i / 2]));
                                 }
                             }
                         }
@@ -315,16 +317,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
             if (!ok) break;
-            if (m == 1) {
 #pragma unroll
-                for (int q = 0; q < 16; ++q) UP[(16 * th + q) * TC_ROWS + r] = acc[q];
-            }
-            __syncthreads();
-            if (m == 0) {
+            for (int q = 0; q < 8; ++q) {
+                float a[2];
+                f2_unpack(acc[q], a[0], a[1]);
 #pragma unroll
-                for (int q = 0; q < 16; ++q) {
-                    const int t = 16 * th + q;
-                    if (t < nt) p.h[(size_t)(t0 + t) * p.F + j0 + r] = __fmul_rn(kq_silu(acc[q]), UP[t * TC_ROWS + r]);
+                for (int k = 0; k < 2; ++k) {
+                    const int t = 16 * th + 2 * q + k;
+                    if (t < nt) out[(size_t)(t0 + t) * p.F + j0 + r] = a[k];
                 }
             }
         }
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_gateup_tc(MoeBatchPar
     if (!ok && tid == 0 && p.status) atomicOr((uint32_t *)p.status, 4u);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(TC_COLS));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(GU_COLS));
 }
 
 // ---------------------------------------------------------------------------
@@ -363,7 +363,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
     const int F = p.F, nb = F / 256;
     const uint32_t rbd = p.rbd;
     uint8_t *raw = sm + OFF_DRAW;
-    float *DX = reinterpret_cast<float *>(sm + OFF_DDX);  // [chunk][token]
+    double *DX = reinterpret_cast<double *>(sm + OFF_DDX);  // [chunk][token]
 
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)));
@@ -445,7 +445,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
                 if (tid < 8 * TC_NT) {
                     const int c = tid / TC_NT, t = tid % TC_NT;
                     const float *xr = reinterpret_cast<const float *>(sm + OFF_DXR + buf * (TC_NT * 8 * 4));
-                    DX[c * TC_NT + t] = t < nt ? xr[t * 8 + c] : 0.0f;
+                    DX[c * TC_NT + t] = t < nt ? (double)xr[t * 8 + c] : 0.0;
                 }
                 // unpack row r, chunks 2*role and 2*role + 1 of super-block b: 6-bit values - 32
                 {
@@ -494,10 +494,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                // accumulate tokens 8*role .. +7 of row r
+                // accumulate tokens 8*role .. +7 of row r. I (|I| < 2^24) becomes a double
+                // exactly: the word pair {0x43380000, I ^ 2^31} is 1.5 * 2^52 + 2^31 + I.
                 {
                     const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
-                    const float d = h2f((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
+                    const double dd = (double)h2f((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
                     const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 8 * role;
 #pragma unroll 1
                     for (int c = 0; c < 8; c += 2) {
@@ -511,13 +512,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
                         for (int cc = 0; cc < 2; ++cc) {
                             const int sl = (int)(int8_t)blk[192 + 2 * (c + cc)];
                             const int sh = (int)(int8_t)blk[193 + 2 * (c + cc)];
-                            const float4 *dx4 = reinterpret_cast<const float4 *>(DX + (c + cc) * TC_NT + 8 * role);
-                            const float4 da = dx4[0], db = dx4[1];
-                            const float dv[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+                            const double2 *dx2 = reinterpret_cast<const double2 *>(DX + (c + cc) * TC_NT + 8 * role);
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                const int I = sl * (int)(cc ? l1[q] : l0[q]) + sh * (int)(cc ? h1[q] : h0[q]);
-                                acc[q] = fma((double)__fmul_rn(d, dv[q]), (double)I, acc[q]);
+                            for (int k = 0; k < 4; ++k) {
+                                const double2 dx = dx2[k];
+#pragma unroll
+                                for (int e = 0; e < 2; ++e) {
+                                    const int q = 2 * k + e;
+                                    const int I = sl * (int)(cc ? l1[q] : l0[q]) + sh * (int)(cc ? h1[q] : h0[q]);
+                                    const double fI =
+                                        __hiloint2double(0x43380000, I ^ (int)0x80000000) - 6755401588539392.0;
+                                    acc[q] = fma(dd * (e ? dx.y : dx.x), fI, acc[q]);
+                                }
                             }
                         }
                     }
@@ -541,7 +547,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(TC_COLS));
 }
 
-// Persistent grids: one CTA per SM at most (each holds all 512 TMEM columns), never more
+// Persistent grids: the SM count at most (the down kernel holds all 512 TMEM columns of
+// an SM; the gate/up kernel, 256 columns, runs two CTAs per SM on twice this), never more
 // than the worst-case item count.
 static int tc_grid(const MoeBatchParams &p, int max_items) {
     const int sms = p.sms > 0 ? p.sms : 1;
@@ -551,8 +558,9 @@ static int tc_grid(const MoeBatchParams &p, int max_items) {
 void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
     static size_t set_bytes[KQ_MAX_DEVICES];
     ensure_smem_limit(moe_batch_gateup_tc, TC_SMEM, set_bytes);
-    const int grid = tc_grid(p, max_groups * (p.F / TC_ROWS));
-    if (grid > 0) moe_batch_gateup_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(p);
+    const int max_items = 2 * max_groups * (p.F / TC_ROWS);
+    const int grid = 2 * tc_grid(p, max_items) < max_items ? 2 * tc_grid(p, max_items) : max_items;
+    if (grid > 0) moe_batch_gateup_tc<<<grid, GU_THREADS, TC_SMEM, st>>>(p);
 }
 
 void launch_down_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {

@@ -45,7 +45,8 @@ class DevLayer:
         ptrs = [(g.data_ptr() + e * g.shape[1], u.data_ptr() + e * u.shape[1],
                  d.data_ptr() + e * d.shape[1]) for e in range(E)]
         self.ptrs = ptrs
-        self.layer = MoeLayer(plugin, E, H, F, K, ptrs, norm_topk=norm)
+        self.layer = MoeLayer(plugin, E, H, F, K, ptrs, norm_topk=norm, gate_type=self.host.gate_type,
+                              up_type=self.host.up_type, down_type=self.host.down_type)
         self.H, self.E, self.K = H, E, K
 
     def run(self, x, logits, mode=MOE_Q8_1):

@@ -4,15 +4,18 @@ Bars, per token of a batch: routing identical to the batch-1 kernel, output with
 rel_L2 <= 1e-5 of the q8_1 restatement (port.moe_layer, mode 0) and at least 99.9 %
 of elements bit-equal to it; the same bars against the batch-1 kernel's output for
 the same token. Groups of >= 16 tokens run gate/up on the tensor cores (tcgen05
-int8 MMA) with fp32 block terms; their bar is TC_TOL below. Edge cases: one token,
+int8 MMA) with fp32 block terms; their bar is TC_TOL below. Their Q6_K down projection
+also runs there, with exact integer block sums and double accumulation in the
+restatement's order, so a layer whose gate/up stay on the DP4A kernels (Q6_K gate and
+up) keeps the strict bars with its down projection on the tensor cores. Edge cases: one token,
 every token on the same experts, groups of 16 / 33 / 100 tokens, batch sizes that
 grow and shrink between calls, no-norm routing, 1024 experts with top-16, and the
 argument checks."""
 import numpy as np
 import pytest
 
-from katali_lab_b200 import MOE_F32, MOE_Q8_1, KataliError
-from oracle.oracle import rel_l2
+from katali_lab_b200 import MOE_F32, MOE_Q8_1, Q6_K, KataliError
+from oracle.oracle import MoeWeights, rel_l2
 from tests.test_gpu_moe import DevLayer, dev, empty, host
 
 pytestmark = pytest.mark.gpu
@@ -100,6 +103,36 @@ def test_batch_tensor_core_groups(c3_layer, port, T, hot):
     Y = run_batch(c3_layer, X, L)
     idx = sorted({0, T // 3, T // 2, T - 1})
     check_tokens_tc(c3_layer, port, X[idx], L[idx], Y[idx])
+
+
+@pytest.fixture(scope="module")
+def q6_layer(plugin, port):
+    """Q6_K gate, up and down (16 experts, H 2048, F 512, top-4; Q6_K gate/up rows are
+    16-byte multiples from H 2048): gate/up stay on the DP4A kernels, the down projection
+    of groups of >= 16 tokens runs on the tensor cores."""
+    E, H, F, K = 16, 2048, 512, 4
+    rng = np.random.default_rng(41)
+
+    def store(rows, cols):
+        return np.stack([port.quantize(Q6_K, rng.normal(0, 0.02, rows * cols).astype(np.float32))
+                         for _ in range(E)])
+
+    mw = MoeWeights(store(F, H), store(F, H), store(H, F), H, F, K, True,
+                    gate_type=Q6_K, up_type=Q6_K, down_type=Q6_K)
+    return DevLayer(plugin, E, H, F, K, seed=0, from_host=mw)
+
+
+@pytest.mark.parametrize("T", [20, 64])
+def test_batch_tensor_core_down_strict(q6_layer, port, monkeypatch, T):
+    """Every token on the same 4 experts: groups of T tokens (one partial token tile at
+    T = 20, two full tiles at 64) whose down projection runs on the tensor cores; the
+    strict bars against the restatement, and bit-equality with the all-DP4A run."""
+    X, L = batch_inputs(950 + T, T, 2048, 16, bias=[2, 5, 11, 13])
+    Y = run_batch(q6_layer, X, L)
+    check_tokens(q6_layer, port, X, L, Y, against_batch1=False)
+    monkeypatch.setenv("KATALI_CUDA_NO_TC", "1")
+    Y2 = run_batch(q6_layer, X, L)
+    assert np.mean(Y == Y2) >= 0.999
 
 
 def test_batch_ragged_sequence(c3_layer, port):
