@@ -36,11 +36,9 @@ namespace kq {
 
 namespace {
 
-constexpr int TC_THREADS = 512;    // down kernel: 16 warps, one CTA per SM
 constexpr int GU_THREADS = 256;    // gate/up kernel: 8 warps, two CTAs per SM
 constexpr int TC_NT = 32;  // tokens per tile (MMA N)
 constexpr int TC_ROWS = 128;  // rows per tile (MMA M)
-constexpr int TC_COLS = 512;  // down TMEM columns: 16 operands x 32
 constexpr int GU_COLS = 256;  // gate/up TMEM columns: 8 chunks x 32
 constexpr uint32_t A_CHUNK = TC_ROWS * 32;  // 4096 B: one 128 x 32 int8 operand
 constexpr uint32_t B_CHUNK = TC_NT * 32;    // 1024 B
@@ -110,15 +108,17 @@ __device__ __forceinline__ void ld32_unaligned(const uint8_t *src, uint32_t (&ou
     for (int i = 0; i < 8; ++i) out[i] = __funnelshift_r(x[i], x[i + 1], sh);
 }
 
-// Down projection plan (bytes from the dynamic base): A holds, per 32-wide chunk c of a
-// Q6_K super-block, two operands: 2c with the chunk's first 16 values and zeros in its
-// second K half, 2c + 1 with zeros in its first K half and the last 16 values (each
-// half has its own 16-element scale). The zero halves are written once per CTA.
-constexpr uint32_t OFF_DA = 0;                           // 16 operands of 128 x 32 int8
-constexpr uint32_t OFF_DB = OFF_DA + 16 * A_CHUNK;       // 2 buffers x 8 chunks of B
+// Down projection plan (bytes from the dynamic base): per half of a Q6_K super-block
+// (4 chunks of 32), A holds two operands per chunk k: 2k with the chunk's first 16 values
+// and zeros in its second K half, 2k + 1 with zeros in its first K half and the last 16
+// values (each half has its own 16-element scale). The zero halves are written once per CTA.
+constexpr int DN_THREADS = 256;                          // 8 warps
+constexpr int DN_COLS = 256;                             // TMEM: 8 operands x 32 columns
+constexpr uint32_t OFF_DA = 0;                           // 8 operands of 128 x 32 int8
+constexpr uint32_t OFF_DB = OFF_DA + 8 * A_CHUNK;        // 2 buffers x 8 chunks of B
 constexpr uint32_t OFF_DXR = OFF_DB + 2 * 8 * B_CHUNK;   // 2 buffers of h block scales [32][8]
 constexpr uint32_t OFF_DDX = OFF_DXR + 2 * TC_NT * 8 * 4;  // DX [8][32] as doubles
-constexpr uint32_t OFF_DRAW = OFF_DDX + 8 * TC_NT * 8;   // the raw 128-row tile
+constexpr uint32_t OFF_DRAW = OFF_DDX + 8 * TC_NT * 8;   // the raw 128-row tile (+16 B of slack)
 constexpr uint32_t TC_DOWN_SMEM = OFF_DRAW + TC_DOWN_RAW_MAX + 16;
 static_assert(TC_DOWN_SMEM <= 227 * 1024, "shared-memory plan");
 static_assert(OFF_DRAW % 16 == 0, "bulk-copy destination");
@@ -346,12 +346,14 @@ __global__ void __launch_bounds__(GU_THREADS, 2) moe_batch_gateup_tc(MoeBatchPar
 // product of two fp16, has 22 significant bits), the terms are added in the order of
 // the reference's Q6_K x q8_1 dot (super-block, then block) and the row rounds once to
 // fp32, so a row equals that dot for the same q8_1 h.
-// CTA = (group, 128-row tile of H) items, 16 warps: warp w serves TMEM lanes
-// 32*(w%4)..+31 for tokens 8*(w/4)..+7 and unpacks chunks 2*(w/4), 2*(w/4)+1. The raw
-// 128-row tile arrives in one bulk copy; the B operand and h scales of super-block b+1
-// are copied (cp.async, double buffer) while b is computed.
+// CTA = (group, 128-row tile of H) items, 8 warps: warp w serves TMEM lanes
+// 32*(w%4)..+31 for tokens 16*(w/4)..+15; each half of a super-block (4 chunks, 8 MMAs,
+// 256 TMEM columns) is unpacked, multiplied and accumulated in turn, w unpacking chunks
+// 2*(w/4) and 2*(w/4)+1 of the half. The raw 128-row tile arrives in one bulk copy and
+// its size sets the shared memory (two CTAs per SM up to ~60 KB of tile); the B operand
+// and h scales of super-block b+1 are copied (cp.async, double buffer) while b is computed.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParams p) {
+__global__ void __launch_bounds__(DN_THREADS, 2) moe_batch_down_tc(MoeBatchParams p) {
     extern __shared__ __align__(1024) uint8_t sm[];
     __shared__ __align__(8) uint64_t bar, tbar;
     __shared__ uint32_t taddr_s;
@@ -370,15 +372,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&tbar)));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // the zero K halves of the 16 operands
-    for (int i = tid; i < 8 * 2 * TC_ROWS; i += TC_THREADS) {
-        const int c = i / (2 * TC_ROWS), hi = (i / TC_ROWS) & 1, rr = i % TC_ROWS;
-        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c + hi) * A_CHUNK + canon(rr, hi ? 0 : 1)) =
+    // the zero K halves of the 8 operands
+    for (int i = tid; i < 4 * 2 * TC_ROWS; i += DN_THREADS) {
+        const int k = i / (2 * TC_ROWS), hi = (i / TC_ROWS) & 1, rr = i % TC_ROWS;
+        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * k + hi) * A_CHUNK + canon(rr, hi ? 0 : 1)) =
             make_uint4(0, 0, 0, 0);
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&taddr_s)),
-                     "r"(TC_COLS));
+                     "r"(DN_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -409,22 +411,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
             const int nt = min(TC_NT, p1 - t0);
             auto issue = [&](int b, int buf) {
                 uint8_t *B = sm + OFF_DB + buf * 8 * B_CHUNK;
-                for (int i = tid; i < nt * 16; i += TC_THREADS) {
+                for (int i = tid; i < nt * 16; i += DN_THREADS) {
                     const int t = i / 16, c = (i / 2) % 8, h = i % 2;
                     cp_async16(B + c * B_CHUNK + canon(t, h), p.hq + (size_t)(t0 + t) * F + 256 * b + 32 * c + 16 * h);
                 }
                 uint8_t *xr = sm + OFF_DXR + buf * (TC_NT * 8 * 4);
-                for (int i = tid; i < nt * 2; i += TC_THREADS) {
+                for (int i = tid; i < nt * 2; i += DN_THREADS) {
                     const int t = i / 2, k = i % 2;
                     cp_async16(xr + t * 32 + 16 * k, p.hd + (size_t)(t0 + t) * (F / 32) + 8 * b + 4 * k);
                 }
                 cp_async_commit();
             };
-            double acc[8];
+            double acc[16];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc[q] = 0.0;
+            for (int q = 0; q < 16; ++q) acc[q] = 0.0;
             issue(0, 0);
-            for (int b = 0; b < nb; ++b) {
+            for (int b = 0; b < nb && ok; ++b) {
                 const int buf = b & 1;
                 if (b + 1 < nb) {
                     issue(b + 1, buf ^ 1);
@@ -442,17 +444,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
                     tphase ^= 1u;
                     tile_in = true;
                 }
-                if (tid < 8 * TC_NT) {
+                {
                     const int c = tid / TC_NT, t = tid % TC_NT;
                     const float *xr = reinterpret_cast<const float *>(sm + OFF_DXR + buf * (TC_NT * 8 * 4));
                     DX[c * TC_NT + t] = t < nt ? (double)xr[t * 8 + c] : 0.0;
                 }
-                // unpack row r, chunks 2*role and 2*role + 1 of super-block b: 6-bit values - 32
-                {
-                    const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
+                const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
+                for (int half = 0; half < 2; ++half) {
+                    // unpack row r, chunks 4*half + 2*role + {0, 1}: 6-bit values - 32
 #pragma unroll
                     for (int cc = 0; cc < 2; ++cc) {
-                        const int c = 2 * role + cc, n = c >> 2, j = c & 3;
+                        const int k = 2 * role + cc, c = 4 * half + k, n = c >> 2, j = c & 3;
                         uint32_t lo[8], hi[8], q[8];
                         ld32_unaligned(blk + 64 * n + 32 * (j & 1), lo);
                         ld32_unaligned(blk + 128 + 32 * n, hi);
@@ -461,81 +463,77 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
                         for (int i = 0; i < 8; ++i)
                             q[i] = __vsub4(((lo[i] >> ns) & 0x0F0F0F0Fu) | (((hi[i] >> hs) & 0x03030303u) << 4),
                                            0x20202020u);
-                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c) * A_CHUNK + canon(r, 0)) =
+                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * k) * A_CHUNK + canon(r, 0)) =
                             make_uint4(q[0], q[1], q[2], q[3]);
-                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * c + 1) * A_CHUNK + canon(r, 1)) =
+                        *reinterpret_cast<uint4 *>(sm + OFF_DA + (2 * k + 1) * A_CHUNK + canon(r, 1)) =
                             make_uint4(q[4], q[5], q[6], q[7]);
                     }
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncthreads();
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                if (tid == 0) {
-                    const uint32_t sa = smem_u32(sm + OFF_DA), sb = smem_u32(sm + OFF_DB + buf * 8 * B_CHUNK);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncthreads();
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    if (tid == 0) {
+                        const uint32_t sa = smem_u32(sm + OFF_DA), sb = smem_u32(sm + OFF_DB + buf * 8 * B_CHUNK);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint64_t db = umma_sdesc(sb + c * B_CHUNK);
-                        umma_i8(taddr + (2 * c) * TC_NT, umma_sdesc(sa + (2 * c) * A_CHUNK), db);
-                        umma_i8(taddr + (2 * c + 1) * TC_NT, umma_sdesc(sa + (2 * c + 1) * A_CHUNK), db);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint64_t db = umma_sdesc(sb + (4 * half + k) * B_CHUNK);
+                            umma_i8(taddr + (2 * k) * TC_NT, umma_sdesc(sa + (2 * k) * A_CHUNK), db);
+                            umma_i8(taddr + (2 * k + 1) * TC_NT, umma_sdesc(sa + (2 * k + 1) * A_CHUNK), db);
+                        }
+                        asm volatile(
+                            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                smem_u32(&bar))
+                            : "memory");
                     }
-                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                     smem_u32(&bar))
-                                 : "memory");
-                }
-                uint32_t done = 0;
-                for (uint32_t sp = 0; sp < SPIN_LIMIT && !done; ++sp) {
-                    done = mbar_try_wait(&bar, phase) ? 1u : 0u;
-                    if (!done && sp > 64) __nanosleep(64);
-                }
-                phase ^= 1u;
-                if (!__syncthreads_and(done)) {
-                    ok = false;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                // accumulate tokens 8*role .. +7 of row r. I (|I| < 2^24) becomes a double
-                // exactly: the word pair {0x43380000, I ^ 2^31} is 1.5 * 2^52 + 2^31 + I.
-                {
-                    const uint8_t *blk = raw + (size_t)r * rbd + (size_t)b * Q6K_BYTES;
-                    const double dd = (double)h2f((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
-                    const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 8 * role;
+                    uint32_t done = 0;
+                    for (uint32_t sp = 0; sp < SPIN_LIMIT && !done; ++sp) {
+                        done = mbar_try_wait(&bar, phase) ? 1u : 0u;
+                        if (!done && sp > 64) __nanosleep(64);
+                    }
+                    phase ^= 1u;
+                    if (!__syncthreads_and(done)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    // accumulate tokens 16*role .. +15 of row r over the half's 4 chunks. I
+                    // (|I| < 2^24) becomes a double exactly: the word pair {0x43380000,
+                    // I ^ 2^31} is 1.5 * 2^52 + 2^31 + I.
+                    {
+                        const double dd = (double)h2f((uint32_t)blk[208] | ((uint32_t)blk[209] << 8));
+                        const uint32_t col = taddr + ((uint32_t)(32 * quad) << 16) + 16 * role;
 #pragma unroll 1
-                    for (int c = 0; c < 8; c += 2) {
-                        uint32_t l0[8], h0[8], l1[8], h1[8];
-                        tmem_ld8(col + (2 * c) * TC_NT, l0);
-                        tmem_ld8(col + (2 * c + 1) * TC_NT, h0);
-                        tmem_ld8(col + (2 * c + 2) * TC_NT, l1);
-                        tmem_ld8(col + (2 * c + 3) * TC_NT, h1);
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        for (int k = 0; k < 4; ++k) {
+                            const int c = 4 * half + k;
+                            uint32_t lo[16], hi[16];
+                            tmem_ld16(col + (2 * k) * TC_NT, lo);
+                            tmem_ld16(col + (2 * k + 1) * TC_NT, hi);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                            const int sl = (int)(int8_t)blk[192 + 2 * c], sh = (int)(int8_t)blk[193 + 2 * c];
+                            const double2 *dx2 = reinterpret_cast<const double2 *>(DX + c * TC_NT + 16 * role);
 #pragma unroll
-                        for (int cc = 0; cc < 2; ++cc) {
-                            const int sl = (int)(int8_t)blk[192 + 2 * (c + cc)];
-                            const int sh = (int)(int8_t)blk[193 + 2 * (c + cc)];
-                            const double2 *dx2 = reinterpret_cast<const double2 *>(DX + (c + cc) * TC_NT + 8 * role);
+                            for (int e = 0; e < 8; ++e) {
+                                const double2 dx = dx2[e];
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const double2 dx = dx2[k];
-#pragma unroll
-                                for (int e = 0; e < 2; ++e) {
-                                    const int q = 2 * k + e;
-                                    const int I = sl * (int)(cc ? l1[q] : l0[q]) + sh * (int)(cc ? h1[q] : h0[q]);
+                                for (int f = 0; f < 2; ++f) {
+                                    const int q = 2 * e + f;
+                                    const int I = sl * (int)lo[q] + sh * (int)hi[q];
                                     const double fI =
                                         __hiloint2double(0x43380000, I ^ (int)0x80000000) - 6755401588539392.0;
-                                    acc[q] = fma(dd * (e ? dx.y : dx.x), fI, acc[q]);
+                                    acc[q] = fma(dd * (f ? dx.y : dx.x), fI, acc[q]);
                                 }
                             }
                         }
                     }
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    __syncthreads();  // A and TMEM are reused by the next half
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 }
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncthreads();  // A, B, the scales and TMEM are reused by the next super-block
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             }
             if (!ok) break;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const int t = 8 * role + q;
+            for (int q = 0; q < 16; ++q) {
+                const int t = 16 * role + q;
                 if (t < nt) p.part[(size_t)(t0 + t) * p.H + j0 + r] = (float)acc[q];
             }
         }
@@ -544,12 +542,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) moe_batch_down_tc(MoeBatchParam
     if (!ok && tid == 0 && p.status) atomicOr((uint32_t *)p.status, 4u);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(TC_COLS));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(DN_COLS));
 }
 
-// Persistent grids: the SM count at most (the down kernel holds all 512 TMEM columns of
-// an SM; the gate/up kernel, 256 columns, runs two CTAs per SM on twice this), never more
-// than the worst-case item count.
+// Persistent grids: the SM count at most, twice that where two CTAs fit an SM (each holds
+// 256 TMEM columns), never more than the worst-case item count.
 static int tc_grid(const MoeBatchParams &p, int max_items) {
     const int sms = p.sms > 0 ? p.sms : 1;
     return max_items < sms ? max_items : sms;
@@ -566,8 +563,10 @@ void launch_gateup_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
 void launch_down_tc(MoeBatchParams &p, int max_groups, cudaStream_t st) {
     static size_t set_bytes[KQ_MAX_DEVICES];
     ensure_smem_limit(moe_batch_down_tc, TC_DOWN_SMEM, set_bytes);
-    const int grid = tc_grid(p, max_groups * (p.H / TC_ROWS));
-    if (grid > 0) moe_batch_down_tc<<<grid, TC_THREADS, TC_DOWN_SMEM, st>>>(p);
+    const uint32_t smem = OFF_DRAW + TC_ROWS * p.rbd + 16;
+    const int max_items = max_groups * (p.H / TC_ROWS), per_sm = 2 * (smem + 2048) <= 228 * 1024 ? 2 : 1;
+    const int grid = per_sm * tc_grid(p, max_items) < max_items ? per_sm * tc_grid(p, max_items) : max_items;
+    if (grid > 0) moe_batch_down_tc<<<grid, DN_THREADS, smem, st>>>(p);
 }
 
 }  // namespace kq
