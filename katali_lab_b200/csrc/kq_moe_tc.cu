@@ -1,5 +1,5 @@
-// kq_moe_tc.cu — gate/up of the ragged-batch MoE on the 5th-generation tensor cores
-// (tcgen05.mma kind::i8) for expert groups with many tokens.
+// kq_moe_tc.cu — the ragged-batch MoE's expert groups with many tokens on the
+// 5th-generation tensor cores (tcgen05.mma kind::i8): Q4_K gate/up and Q6_K down.
 //
 // For one selected expert with n >= p.tc_min tokens, gate and up are dense
 // [F x H] x [H x n] products of int4 weights (Q4_K nibbles 0..15) and int8
@@ -9,24 +9,27 @@
 // 128 rows x 32 tokens; the CUDA cores then apply
 //   acc += (d*sc) * dx * isum - (dmin*m) * (dx * xsum)
 // in fp32 per block (the DP4A kernels use exact double terms; this path rounds
-// each block term to fp32, within the layer tolerance).
+// each block term to fp32, within the layer tolerance). The down projection
+// (below moe_batch_gateup_tc) keeps exact terms in double.
 //
-// CTA = (group, 128-row tile), 16 warps. Warp w serves TMEM lanes 32*(w%4)..+31
-// (the rows of its quadrant) in role w/4: gate or up, tokens 0..15 or 16..31 of
-// the token tile. Per token tile of 32 and per super-block b of 256 columns:
-//   * the copies of super-block b+1 (raw gate and up rows, 144 B each; the tokens'
-//     q8_1 values in the canonical no-swizzle K-major layout of the B operand; their
-//     block scales and sums) go out with cp.async into the other half of a double
-//     buffer before b is unpacked, so they land while b is computed;
-//   * unpack row r of one matrix (two of its four chunk pairs) to int8 in the
-//     canonical no-swizzle K-major layout (core matrices of 8 rows x 16 B: LBO 128 B
-//     between the two K halves, SBO 256 B between 8-row groups) with its block scales;
-//   * thread 0 issues 16 MMAs (8 chunks x gate/up) into separate TMEM columns and
-//     commits to an mbarrier;
-//   * each thread reads its row's 16 tokens of its matrix (tcgen05.ld) and accumulates.
-// The up sums meet the gate sums in shared memory for h = silu(g) * u. TMEM: 16 chunks
-// x 32 columns = 512 columns, allocated once per CTA. Each token's arithmetic is the
-// same sequence of fp32 operations for any warp split.
+// Gate/up items are (listed group, 128-row tile, matrix): the gate and the up rows
+// of a tile are separate CTAs (8 warps, 256 TMEM columns, two CTAs per SM). Warp w
+// serves TMEM lanes 32*(w%4)..+31 (the rows of its quadrant) for tokens 0..15 or
+// 16..31 of the token tile (w/4). Per token tile of 32 and per super-block b of 256
+// columns:
+//   * the copies of super-block b+1 (raw rows, 144 B each; the tokens' q8_1 values
+//     in the canonical no-swizzle K-major layout of the B operand; their block scales
+//     and sums) go out with cp.async into the other half of a double buffer before b
+//     is unpacked, so they land while b is computed;
+//   * unpack row r (two of its four chunk pairs) to int8 in the canonical no-swizzle
+//     K-major layout (core matrices of 8 rows x 16 B: LBO 128 B between the two K
+//     halves, SBO 256 B between 8-row groups) with its block scales;
+//   * thread 0 issues 8 MMAs (one per chunk) into separate TMEM columns and commits
+//     to an mbarrier;
+//   * each thread reads its row's 16 tokens (tcgen05.ld) and accumulates.
+// The gate item writes its sums into h, the up item into hu; the h quantiser forms
+// h = silu(g) * u for the pairs the group kernel flagged. Each token's arithmetic is
+// the same sequence of fp32 operations for any warp split.
 #include <cuda_runtime.h>
 
 #include "kq_device.cuh"
