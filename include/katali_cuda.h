@@ -150,11 +150,11 @@ int katali_cuda_moe_layer_routed(KataliMoe *m, const float *x, const int32_t *id
  * y[n_tokens][H], row-major device buffers. Each token is routed as in
  * katali_cuda_moe_layer; the (token, expert) pairs are grouped by expert so
  * every selected expert's rows are read once per call. Row t of y equals
- * katali_cuda_moe_layer on row t up to the order of double additions, except
- * that an expert with 16 or more of the batch's pairs runs on the tensor cores:
- * its Q4_K gate/up with fp32 block terms (the layer output then within a
- * relative L2 of 5e-4), its Q6_K down projection with exact integer block sums
- * accumulated in double (each row equal to the reference's Q6_K x q8_1 dot).
+ * katali_cuda_moe_layer on row t up to the order of double additions. Experts
+ * with many of the batch's pairs run on the tensor cores: from 8 pairs the Q6_K
+ * down projection (exact integer block sums accumulated in double, each row
+ * equal to the reference's Q6_K x q8_1 dot), from 16 pairs also the Q4_K
+ * gate/up (fp32 block terms: the layer output then within a relative L2 of 5e-4).
  * The environment variable KATALI_CUDA_NO_TC=1 keeps every expert on the
  * other kernels.
  * mode: KATALI_MOE_Q8_1 only (else KATALI_ERR_UNSUPPORTED_TYPE). Scratch is

@@ -612,9 +612,12 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
     b.rbd = pl.rbd;
     b.status = g_status_dev;
     b.sms = g_num_sms;
-    // Groups of >= 16 tokens run gate/up on the tensor cores (Q4_K gate and up only) and
-    // the down projection there too (Q6_K down whose 128-row tile fits the kernel's
-    // staging); KATALI_CUDA_NO_TC=1 keeps every group on the DP4A kernels.
+    // Groups of >= 16 tokens run gate/up on the tensor cores (Q4_K gate and up only; fp32
+    // block terms, so its bar against the restatement is looser), groups of >= 8 tokens the
+    // down projection (Q6_K down whose 128-row tile fits the kernel's staging; rows equal to
+    // the restatement's dot): a tensor-core item costs the same for 1 to 32 tokens, and from
+    // about 8 tokens it is shorter than the DP4A items of the same group.
+    // KATALI_CUDA_NO_TC=1 keeps every group on the DP4A kernels.
     const char *no_tc = getenv("KATALI_CUDA_NO_TC");
     const bool tc = !(no_tc && no_tc[0] == '1');
     b.tc_min = (pl.gate_type == KATALI_TYPE_Q4_K && pl.up_type == KATALI_TYPE_Q4_K && pl.F % 128 == 0 && tc)
@@ -622,7 +625,7 @@ static kq::MoeBatchParams batch_params(KataliMoe *m, int T) {
                    : 0;
     b.tc_down_min = (pl.down_type == KATALI_TYPE_Q6_K && pl.H % 128 == 0 &&
                      128ull * pl.rbd <= kq::TC_DOWN_RAW_MAX && tc)
-                        ? 16
+                        ? 8
                         : 0;
     return b;
 }

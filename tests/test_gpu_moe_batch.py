@@ -4,7 +4,9 @@ Bars, per token of a batch: routing identical to the batch-1 kernel, output with
 rel_L2 <= 1e-5 of the q8_1 restatement (port.moe_layer, mode 0) and at least 99.9 %
 of elements bit-equal to it; the same bars against the batch-1 kernel's output for
 the same token. Groups of >= 16 tokens run gate/up on the tensor cores (tcgen05
-int8 MMA) with fp32 block terms; their bar is TC_TOL below. Their Q6_K down projection
+int8 MMA) with fp32 block terms; their bar is TC_TOL below. Groups of >= 8 tokens run
+the Q6_K down projection there, at the strict bars; the strict bars are also checked
+with every group on the DP4A kernels (KATALI_CUDA_NO_TC=1). Their Q6_K down projection
 also runs there, with exact integer block sums and double accumulation in the
 restatement's order, so a layer whose gate/up stay on the DP4A kernels (Q6_K gate and
 up) keeps the strict bars with its down projection on the tensor cores. Edge cases: one token,
@@ -54,8 +56,13 @@ def c3_layer(plugin):
 
 
 @pytest.mark.parametrize("T", [1, 5, 17, 64])
-def test_batch_vs_restatement(c3_layer, port, T):
+def test_batch_vs_restatement(c3_layer, port, monkeypatch, T):
+    """As run (at T = 64 groups of 8 to 15 tokens take the tensor-core down projection),
+    then with every group on the DP4A kernels; the strict bars both times."""
     X, L = batch_inputs(300 + T, T, 2048, 64)
+    Y = run_batch(c3_layer, X, L)
+    check_tokens(c3_layer, port, X, L, Y, against_batch1=T <= 17)
+    monkeypatch.setenv("KATALI_CUDA_NO_TC", "1")
     Y = run_batch(c3_layer, X, L)
     check_tokens(c3_layer, port, X, L, Y, against_batch1=T <= 17)
 
@@ -135,13 +142,16 @@ def test_batch_tensor_core_down_strict(q6_layer, port, monkeypatch, T):
     assert np.mean(Y == Y2) >= 0.999
 
 
-def test_batch_ragged_sequence(c3_layer, port):
-    """Scratch grows and shrinks: T = 3, 40, 7, 64, 2 on one layer object."""
-    for i, T in enumerate([3, 40, 7, 64, 2]):
-        X, L = batch_inputs(600 + i, T, 2048, 64)
-        Y = run_batch(c3_layer, X, L)
-        idx = sorted({0, T // 2, T - 1})
-        check_tokens(c3_layer, port, X[idx], L[idx], Y[idx], against_batch1=False)
+def test_batch_ragged_sequence(c3_layer, port, monkeypatch):
+    """Scratch grows and shrinks: T = 3, 40, 7, 64, 2 on one layer object, as run and with
+    every group on the DP4A kernels; the strict bars both times."""
+    for no_tc in ("0", "1"):
+        monkeypatch.setenv("KATALI_CUDA_NO_TC", no_tc)
+        for i, T in enumerate([3, 40, 7, 64, 2]):
+            X, L = batch_inputs(600 + i, T, 2048, 64)
+            Y = run_batch(c3_layer, X, L)
+            idx = sorted({0, T // 2, T - 1})
+            check_tokens(c3_layer, port, X[idx], L[idx], Y[idx], against_batch1=False)
 
 
 def test_batch_deterministic(c3_layer):
