@@ -92,12 +92,6 @@ __device__ __forceinline__ void cp_async_wait_pending() {
 // Canonical offset of the 16-byte piece (row r, K half h) inside one operand chunk.
 __device__ __forceinline__ uint32_t canon(int r, int h) { return (r >> 3) * 256 + h * 128 + (r & 7) * 16; }
 
-__device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                   "=r"(v[7])
-                 : "r"(addr));
-}
 // 32 bytes of shared memory at a 2-byte aligned address as 8 words: nine aligned word
 // loads, funnel-shifted into place.
 __device__ __forceinline__ void ld32_unaligned(const uint8_t *src, uint32_t (&out)[8]) {
