@@ -5,7 +5,8 @@ of experts, exchange their slot buffers by device copies. Bars: dispatch slots
 equal the oracle's restatement (headers, owned ids, weights bit-identical, q8_1 rows
 byte-identical); the experts stage's per-slot partial sums within rel_L2 <= 1e-5 of
 the oracle's on the same received bytes; every token's output within rel_L2 <= 1e-5
-of katali_cuda_moe_batch on the full layer with >= 99.9 % of elements bit-equal."""
+of katali_cuda_moe_batch on the full layer with >= 99.9 % of elements bit-equal, also with
+every token on the same experts (tensor-core groups in the experts stage)."""
 import numpy as np
 import pytest
 import torch
@@ -63,6 +64,41 @@ def test_ep_virtual_ranks_vs_batch(plugin, full, G, Ts):
         for t in range(Ts[r]):
             assert rel_l2(y[t], want[t]) <= 1e-5, (r, t)
             assert np.mean(y[t] == want[t]) >= 0.999, (r, t)
+    for e in eps:
+        e.close()
+    plugin.set_stream(None)
+
+
+def test_ep_virtual_ranks_tensor_core_groups(plugin, full):
+    """Every token on the same 8 experts (4 on each of 2 virtual ranks): each rank's experts
+    stage sees groups of 48 received slots, so gate/up and down run on the tensor cores.
+    A token's arithmetic there does not depend on its place in the group, so each rank's
+    outputs equal katali_cuda_moe_batch of all ranks' tokens on the full layer (the same
+    groups) at the expert-parallel bars."""
+    plugin.set_stream(torch.cuda.current_stream())
+    G, T = 2, 24
+    eps = ep_layers(plugin, full, G, T)
+    hot = [3, 9, 20, 30, 35, 41, 50, 60]
+    ins = []
+    for r in range(G):
+        X, L = inputs(90 + r, T)
+        L[:, hot] += 8.0
+        ins.append((X, L))
+    sends = [eps[r].dispatch(T, dev(ins[r][0]), dev(ins[r][1])).clone() for r in range(G)]
+    recvs = exchange(sends, G)
+    rets = [eps[r].experts(recvs[r]).clone() for r in range(G)]
+    backs = exchange(rets, G)
+    want = empty(G * T * H).view(G * T, H)
+    full.layer.forward_batch(dev(np.concatenate([x for x, _ in ins])),
+                             dev(np.concatenate([l for _, l in ins])), want)
+    want = host(want)
+    for r in range(G):
+        y = empty(T * H).view(T, H)
+        eps[r].combine(T, backs[r], y)
+        y = host(y)
+        for t in range(T):
+            assert rel_l2(y[t], want[r * T + t]) <= 1e-5, (r, t)
+            assert np.mean(y[t] == want[r * T + t]) >= 0.999, (r, t)
     for e in eps:
         e.close()
     plugin.set_stream(None)
